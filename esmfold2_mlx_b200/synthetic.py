@@ -1,0 +1,170 @@
+"""Seeded synthetic trunks and pair tensors with the shapes the reference's benchmarks use.
+
+Biohub's checkpoints and the ``esm`` package are not available here, so benchmarks and tests
+build a module tree with the attribute names the reference reads when it copies a trunk's
+weights (``src/esmfold2_mlx/mlx_trunk.py:40-67``; ``fast_trunk.py:52-56``):
+
+    folding_trunk.blocks[i].tri_mul_out._engine.{latent_channels, norm_start, proj_bundle,
+                                                norm_mix, proj_emit, proj_gate}
+    folding_trunk.blocks[i].tri_mul_in._engine.{...}
+    folding_trunk.blocks[i].pair_transition.{norm, ffn.w12, ffn.w3, ffn.hidden_features}
+
+Weights are N(0, 1/fan_in); LayerNorm gamma=1, beta=0 unless ``ln_noise`` is set; Linear
+layers have no bias, as in the reference (``fast_trunk.py:53,59``).  Optional tri-mul biases
+(N(0, 0.02), one benchmark configuration adds them) are returned separately because the
+reference module tree has no place for them.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+from torch import nn
+
+
+def _linear(out_f: int, in_f: int, g: torch.Generator) -> nn.Linear:
+    lin = nn.Linear(in_f, out_f, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(out_f, in_f, generator=g) / in_f**0.5)
+    return lin
+
+
+def _ln(ch: int, g: torch.Generator, noise: float) -> nn.LayerNorm:
+    ln = nn.LayerNorm(ch)
+    if noise:
+        with torch.no_grad():
+            ln.weight.copy_(1.0 + noise * torch.randn(ch, generator=g))
+            ln.bias.copy_(noise * torch.randn(ch, generator=g))
+    return ln
+
+
+class TriangleMultiplicativeBlock(nn.Module):
+    """Holds the weights of one triangle update under the names the reference reads."""
+
+    def __init__(self, c_z: int, c: int, g: torch.Generator, ln_noise: float = 0.0):
+        super().__init__()
+        self.latent_channels = c
+        self.norm_start = _ln(c_z, g, ln_noise)
+        self.proj_bundle = _linear(4 * c, c_z, g)  # rows [signal_a | signal_b | gate_a | gate_b]
+        self.norm_mix = _ln(c, g, ln_noise)
+        self.proj_emit = _linear(c_z, c, g)
+        self.proj_gate = _linear(c_z, c_z, g)
+
+
+class TriangleMultiplicativeUpdate(nn.Module):
+    def __init__(self, c_z: int, c: int, g: torch.Generator, ln_noise: float = 0.0):
+        super().__init__()
+        self._engine = TriangleMultiplicativeBlock(c_z, c, g, ln_noise)
+
+
+class _FFN(nn.Module):
+    def __init__(self, c_z: int, hidden: int, g: torch.Generator, activation: str):
+        super().__init__()
+        self.hidden_features = hidden
+        self.activation = activation
+        width = 2 * hidden if activation == "swiglu" else hidden
+        self.w12 = _linear(width, c_z, g)
+        self.w3 = _linear(c_z, hidden, g)
+
+
+class Transition(nn.Module):
+    def __init__(self, c_z: int, hidden: int, g: torch.Generator, activation: str = "swiglu",
+                 ln_noise: float = 0.0):
+        super().__init__()
+        self.norm = _ln(c_z, g, ln_noise)
+        self.ffn = _FFN(c_z, hidden, g, activation)
+
+
+class PairUpdateBlock(nn.Module):
+    def __init__(self, c_z: int, c: int, hidden: int, g: torch.Generator, activation: str, ln_noise: float):
+        super().__init__()
+        self.tri_mul_out = TriangleMultiplicativeUpdate(c_z, c, g, ln_noise)
+        self.tri_mul_in = TriangleMultiplicativeUpdate(c_z, c, g, ln_noise)
+        self.pair_transition = Transition(c_z, hidden, g, activation, ln_noise)
+
+
+class FoldingTrunk(nn.Module):
+    """A trunk-shaped module tree; its own forward is never used (the swap replaces it)."""
+
+    def __init__(self, n_blocks: int, c_z: int = 128, c: int = 128, hidden: int | None = None,
+                 seed: int = 0, activation: str = "swiglu", ln_noise: float = 0.0):
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        hidden = hidden if hidden is not None else 4 * c_z
+        self.blocks = nn.ModuleList(
+            PairUpdateBlock(c_z, c, hidden, g, activation, ln_noise) for _ in range(n_blocks))
+        self.chunk_size = None
+        self.kernel_backend = None
+
+    def set_chunk_size(self, chunk_size):
+        self.chunk_size = chunk_size
+
+    def set_kernel_backend(self, backend):
+        self.kernel_backend = backend
+
+
+class FoldModel(nn.Module):
+    """Minimal model object with a ``folding_trunk`` attribute, for the variant registry."""
+
+    def __init__(self, folding_trunk: nn.Module):
+        super().__init__()
+        self.folding_trunk = folding_trunk
+
+
+def trimul_biases(c_z: int, c: int, seed: int, std: float = 0.02) -> dict:
+    """Biases for one tri-mul: proj (4c, reference column order), emit (c_z), gate (c_z)."""
+    g = torch.Generator().manual_seed(seed)
+    return {
+        "b_in": std * torch.randn(4 * c, generator=g),
+        "b_emit": std * torch.randn(c_z, generator=g),
+        "b_gate": std * torch.randn(c_z, generator=g),
+    }
+
+
+def pair_tensor(B: int, L: int, c_z: int, seed: int) -> torch.Tensor:
+    """z ~ N(0, 1), fp32, generated on the CPU so every consumer sees identical values."""
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(B, L, L, c_z, generator=g)
+
+
+def pair_mask(B: int, L: int, n_pad: int = 0) -> torch.Tensor:
+    """Pair mask m_i * m_j with the last ``n_pad`` residues masked out (padding)."""
+    m = torch.ones(B, L)
+    if n_pad:
+        m[:, L - n_pad:] = 0.0
+    return m[:, :, None] * m[:, None, :]
+
+
+@dataclass(frozen=True)
+class Config:
+    """One synthetic workload (the five benchmark configurations)."""
+
+    name: str
+    L: int
+    B: int = 1
+    c_z: int = 128
+    c: int = 128
+    seed: int = 0
+    n_pad: int = 0
+    biases: bool = False
+    directions: tuple = ("out",)
+    blocks: int = 0
+    recycles: int = 0
+    transition: str = "swiglu"
+
+    @property
+    def pair_cells_per_step(self) -> int:
+        """L^2 x tri-mul blocks in one step (all folds)."""
+        n_tm = len(self.directions) if not self.blocks else 2 * self.blocks * max(1, self.recycles)
+        return self.B * self.L * self.L * n_tm
+
+
+CONFIGS = {
+    "c1": Config("c1_L76_out", L=76, seed=0, directions=("out",)),
+    "c2": Config("c2_L238_out_in_mask_bias", L=238, seed=1, n_pad=24, biases=True, directions=("out", "in")),
+    "c3": Config("c3_L384_16blk_3rec_relu", L=384, seed=2, blocks=16, recycles=3, transition="relu"),
+    "c4": Config("c4_64x_L146_out_in", L=146, B=64, seed=100, directions=("out", "in")),
+    "c5": Config("c5_L3072_out_in", L=3072, seed=3, directions=("out", "in")),
+    "L2048": Config("L2048_out_in", L=2048, seed=4, directions=("out", "in")),
+}
