@@ -1,0 +1,289 @@
+// K1: input LayerNorm + the four c_z -> c projections of the contraction operands, sigmoid
+// gating and the pair mask, written channel-major for the contraction (no transpose pass).
+//
+// Reference (src/esmfold2_mlx/): mlx_trunk.py:81-83 and :72-76 (_gated_cf);
+// mlx_trunk_kernels.py:214-216 and the Metal kernel trunk_gate_cf (:47-80):
+//   n     = fp16(LN(z; norm_start, eps=1e-5))                    fp32 statistics
+//   proj  = fp16(n @ w_in [+ b_in])                                fp32 accumulation
+//   a     = fp16(proj[:, 0:c]  * sigmoid(proj[:, 2c:3c]) * mask)   fp32 math, one rounding
+//   b     = fp16(proj[:, c:2c] * sigmoid(proj[:, 3c:4c]) * mask)
+// a, b stored [B*c, L, Lpad] (channel d, row i, column j).  The fp16 pre-scale of w_in[:, :c]
+// by 1/256 (mlx_trunk.py:47-48) lives in the packed weights.
+//
+// One tile = 128 pair positions, an ih x jw block of the L x L grid (ih * jw = 128), chosen by
+// the host to minimise padding at ragged L.  CTA = 14 warps, one per SM, persistent:
+//   warp 0      TMA: packed weights once (resident, 4c x c_z fp16), then z tiles (2 stages)
+//   warp 1      TMEM allocation (512 columns = 4 slots of 128) and the single MMA thread:
+//               per tile, NCH chunks of N = 128 columns ([signal 64 | gate 64] of one 64-channel
+//               block of a or b), K = c_z, each chunk into the next free TMEM slot
+//   warps 2-5   LayerNorm of the z tile in shared memory, in place (row = position)
+//   warps 6-13  epilogue: two warps per TMEM lane quadrant split the 64 channels of a chunk;
+//               gate, mask, fp16, transpose through shared memory, TMA store of a 64 x ih x jw box
+#pragma once
+
+#include "tmu_common.cuh"
+
+namespace tmu {
+namespace k1 {
+
+constexpr int CZ = 128;  // c_z
+constexpr int CC = 128;  // c (latent channels)
+constexpr int TILE = 128;
+constexpr int NCH = 4 * CC / 128;       // 128-column chunks per tile
+constexpr int KATOMS = CZ / 64;         // 64-channel swizzle atoms along K
+constexpr int ATOM_BYTES = TILE * 128;  // 128 rows x 128 B
+constexpr int WCHUNK_BYTES = 128 * CZ * 2;
+constexpr int A_BYTES = TILE * CZ * 2;
+constexpr int STG_BYTES = 64 * TILE * 2;
+constexpr int NSTAGE = 2;
+constexpr int NSLOT = 4;
+constexpr int OFF_W = 0;
+constexpr int OFF_A = OFF_W + NCH * WCHUNK_BYTES;
+constexpr int OFF_STG = OFF_A + NSTAGE * A_BYTES;
+constexpr int SMEM_BYTES = OFF_STG + 2 * STG_BYTES + 1024;
+constexpr int kThreads = 448;
+constexpr int TMEM_COLS = 512;
+
+struct Params {
+  CUtensorMap tm_z;  // z [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle
+  CUtensorMap tm_w;  // packed proj weights [4c, c_z]: box {64, 128}, 128B swizzle
+  CUtensorMap tm_a;  // a [B*c, L, Lpad]: box {jw, ih, 64}, no swizzle (store)
+  CUtensorMap tm_b;  // b, same
+  const __half* ln_w;
+  const __half* ln_b;
+  const float* bias;  // [4c] in packed-row order, or null
+  const __half* mask;  // [B, L, L] or null
+  int L, ih, jw, tiles_i, tiles_j, num_tiles;
+  DeviceStatus* status;
+  unsigned long long timeout_ns;
+};
+
+enum Site : unsigned int {
+  kSiteProducer = 0x101, kSiteLn = 0x102, kSiteMmaW = 0x103, kSiteMmaLn = 0x104, kSiteMmaSlot = 0x105,
+  kSiteEpilogue = 0x106
+};
+
+__device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, int& i0, int& j0) {
+  const int per_b = p.tiles_i * p.tiles_j;
+  bb = tile / per_b;
+  const int r = tile - bb * per_b;
+  i0 = (r / p.tiles_j) * p.ih;
+  j0 = (r % p.tiles_j) * p.jw;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_constant__ Params p) {
+  constexpr uint32_t IDESC = idesc_f16_f32(128, 128, false, false);
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t w_bar, zfull[NSTAGE], zempty[NSTAGE], lnfull[NSTAGE];
+  __shared__ __align__(8) uint64_t tfull[NSLOT], tempty[NSLOT], drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_sh;
+  __shared__ volatile int ep_ok_sh;
+
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const WaitCtx ctx{p.status, &abort_sh, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    mbar_init(&w_bar, 1);
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&zfull[s], 1);
+      mbar_init(&zempty[s], 1);
+      mbar_init(&lnfull[s], 128);
+    }
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 256);
+    }
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tm_z);
+    tma_prefetch_desc(&p.tm_w);
+    tma_prefetch_desc(&p.tm_a);
+    tma_prefetch_desc(&p.tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&w_bar, NCH * WCHUNK_BYTES);
+      for (int q = 0; q < NCH; ++q)
+        for (int a = 0; a < KATOMS; ++a)
+          tma_load_2d(smem + OFF_W + q * WCHUNK_BYTES + a * ATOM_BYTES, &p.tm_w, &w_bar, a * 64, q * 128);
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+        int bb, i0, j0;
+        decode_tile(p, tile, bb, i0, j0);
+        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        if (!mbar_wait(&zempty[s], ph ^ 1, ctx, kSiteProducer)) break;
+        mbar_arrive_expect_tx(&zfull[s], A_BYTES);
+        for (int a = 0; a < KATOMS; ++a)
+          tma_load_4d(smem + OFF_A + s * A_BYTES + a * ATOM_BYTES, &p.tm_z, &zfull[s], a * 64, j0, i0, bb);
+      }
+      if (abort_sh) {
+        mbar_drain(&w_bar, 0, 200000000ull);
+        for (uint32_t s = 0; s < NSTAGE; ++s) {
+          const uint32_t n_armed = it > s ? (it - s + 1) / 2 : 0;
+          if (n_armed) mbar_drain(&zfull[s], (n_armed - 1) & 1, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      bool ok = mbar_wait(&w_bar, 0, ctx, kSiteMmaW);
+      uint32_t it = 0, cit = 0;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
+        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        if (!mbar_wait(&lnfull[s], ph, ctx, kSiteMmaLn)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_base = smem_u32(smem + OFF_A + s * A_BYTES);
+        for (int q = 0; q < NCH; ++q, ++cit) {
+          const uint32_t slot = cit % NSLOT, sph = (cit / NSLOT) & 1;
+          if (!mbar_wait(&tempty[slot], sph ^ 1, ctx, kSiteMmaSlot)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t w_base = smem_u32(smem + OFF_W + q * WCHUNK_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < CZ / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
+            umma_f16(tmem_base + slot * 128, sdesc_sw128(a_base + off, 16, 1024), sdesc_sw128(w_base + off, 16, 1024),
+                     IDESC, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&tfull[slot]);
+        }
+        umma_commit(&zempty[s]);  // the z/n tile may be refilled once these MMAs have read it
+      }
+      umma_commit(&drain_bar);
+      mbar_drain(&drain_bar, 0, 200000000ull);
+    }
+  } else if (warp < 6) {
+    // ---------------- LayerNorm of the z tile, in place ----------------
+    const int row = threadIdx.x - 64;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+      const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      if (!mbar_wait(&zfull[s], ph, ctx, kSiteLn)) break;
+      uint8_t* A = smem + OFF_A + s * A_BYTES;
+      uint4 v[KATOMS * 8];
+      float sum = 0.f;
+#pragma unroll
+      for (int c16 = 0; c16 < KATOMS * 8; ++c16) {
+        v[c16] = *reinterpret_cast<const uint4*>(A + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7));
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[c16]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_half2(w[e]);
+          sum += f.x + f.y;
+        }
+      }
+      const float mean = sum * (1.0f / CZ);
+      float sq = 0.f;
+#pragma unroll
+      for (int c16 = 0; c16 < KATOMS * 8; ++c16) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[c16]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_half2(w[e]);
+          const float d0 = f.x - mean, d1 = f.y - mean;
+          sq += d0 * d0 + d1 * d1;
+        }
+      }
+      const float rstd = rsqrtf(sq * (1.0f / CZ) + 1e-5f);
+      const __half2* lw = reinterpret_cast<const __half2*>(p.ln_w);
+      const __half2* lb = reinterpret_cast<const __half2*>(p.ln_b);
+#pragma unroll
+      for (int c16 = 0; c16 < KATOMS * 8; ++c16) {
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v[c16]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_half2(w[e]);
+          const float2 g = __half22float2(__ldg(lw + c16 * 4 + e));
+          const float2 bb = __half22float2(__ldg(lb + c16 * 4 + e));
+          w[e] = pack_half2((f.x - mean) * rstd * g.x + bb.x, (f.y - mean) * rstd * g.y + bb.y);
+        }
+        *reinterpret_cast<uint4*>(A + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7)) = v[c16];
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
+      mbar_arrive(&lnfull[s]);
+    }
+  } else {
+    // ---------------- epilogue: gate, mask, channel-major store ----------------
+    const int e = threadIdx.x - 192;  // 0..255
+    const int q = warp & 3;
+    const int h = (warp - 6) >> 2;   // which 32 of the chunk's 64 channels
+    const int row = q * 32 + lane;   // position within the tile
+    uint8_t* stg = smem + OFF_STG;
+    uint32_t it = 0, cit = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
+      int bb, i0, j0;
+      decode_tile(p, tile, bb, i0, j0);
+      const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
+      float mval = 1.0f;
+      if (p.mask != nullptr && gi < p.L && gj < p.L)
+        mval = __half2float(p.mask[(static_cast<size_t>(bb) * p.L + gi) * p.L + gj]);
+      for (int qc = 0; qc < NCH; ++qc, ++cit) {
+        const uint32_t slot = cit % NSLOT, sph = (cit / NSLOT) & 1;
+        if (e == 0) {
+          ep_ok_sh = mbar_wait(&tfull[slot], sph, ctx, kSiteEpilogue) ? 1 : 0;
+          bulk_wait_read<1>();  // the store that last used this staging buffer has read it
+        }
+        named_bar_sync(2, 256);
+        if (!ep_ok_sh) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 128 + h * 32;
+        uint32_t sg[32], gt[32];
+        tmem_ld32(taddr, sg);
+        tmem_ld32(taddr + 64, gt);
+        tmem_wait_ld2(sg, gt);
+        tc_fence_before();
+        mbar_arrive(&tempty[slot]);
+        __half* st = reinterpret_cast<__half*>(stg + (cit & 1) * STG_BYTES);
+        const int col0 = qc * 128 + h * 32;  // packed-row index of this thread's first signal column
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float s = __uint_as_float(sg[i]);
+          float g = __uint_as_float(gt[i]);
+          if (p.bias != nullptr) {
+            s += __ldg(p.bias + col0 + i);
+            g += __ldg(p.bias + col0 + 64 + i);
+          }
+          s = round_f16(s);  // proj is an fp16 tensor in the reference
+          g = round_f16(g);
+          st[(h * 32 + i) * TILE + row] = __float2half_rn(s * sigmoid_f32(g) * mval);
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(2, 256);
+        if (e == 0) {
+          const bool is_a = qc < NCH / 2;
+          const int ch0 = (qc % (NCH / 2)) * 64;
+          tma_store_3d(is_a ? &p.tm_a : &p.tm_b, st, j0, i0, bb * CC + ch0);
+          bulk_commit();
+        }
+      }
+    }
+    if (e == 0) bulk_wait<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace k1
+}  // namespace tmu

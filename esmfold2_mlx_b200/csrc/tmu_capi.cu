@@ -1,0 +1,456 @@
+// Host side of the C ABI declared in include/tmu.h: argument checks, TMA tensor maps, tile
+// shapes, launches and the device status word.  Nothing here allocates device memory or
+// synchronises a stream (except tmu_read_status, whose job is to).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "k1_project.cuh"
+#include "k2_contract.cuh"
+#include "k3_emit.cuh"
+#include "tmu.h"
+
+using namespace tmu;
+
+namespace {
+
+thread_local std::string g_last_error;
+unsigned long long g_timeout_ns = 2000000000ull;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+constexpr int kMaxDevices = 64;
+int g_num_sms[kMaxDevices] = {0};
+unsigned g_attr_done[kMaxDevices] = {0};
+
+int fail(int code, const char* what) {
+  g_last_error = what;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return TMU_ERR_CUDA;
+}
+
+int get_encoder() {
+  static std::once_flag once;
+  static int st = TMU_OK;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      st = TMU_ERR_DRIVER;
+      g_last_error = "cuTensorMapEncodeTiled entry point not available";
+    } else {
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  });
+  return st;
+}
+
+int encode_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+               const uint32_t* box, CUtensorMapSwizzle sw) {
+  int st = get_encoder();
+  if (st != TMU_OK) return st;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) s[i] = strides[i];
+  }
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<cuuint32_t>(rank), const_cast<void*>(base),
+                        d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d), rank %d", static_cast<int>(r), rank);
+    return fail(TMU_ERR_DRIVER, buf);
+  }
+  return TMU_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int row_pitch(int L) { return (L + 7) & ~7; }
+
+// 128-position tile as an ih x jw block of the pair grid, minimising padding at ragged L.
+void choose_tile(int L, int& ih, int& jw) {
+  static const int opts[5][2] = {{1, 128}, {2, 64}, {4, 32}, {8, 16}, {16, 8}};
+  long long best = -1;
+  for (auto& o : opts) {
+    const long long area = static_cast<long long>((L + o[0] - 1) / o[0]) * o[0] * ((L + o[1] - 1) / o[1]) * o[1];
+    if (best < 0 || area < best) {
+      best = area;
+      ih = o[0];
+      jw = o[1];
+    }
+  }
+}
+
+struct Dev {
+  int id;
+  int sms;
+};
+
+int current_device(Dev& d, unsigned attr_bit, const void* kernel, int smem) {
+  cudaError_t e = cudaGetDevice(&d.id);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (d.id < 0 || d.id >= kMaxDevices) return fail(TMU_ERR_INVALID_ARGUMENT, "device id out of range");
+  if (g_num_sms[d.id] == 0) {
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d.id);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    g_num_sms[d.id] = n;
+  }
+  d.sms = g_num_sms[d.id];
+  if (!(g_attr_done[d.id] & attr_bit)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    g_attr_done[d.id] |= attr_bit;
+  }
+  return TMU_OK;
+}
+
+int check_sizes(int B, int L, int c_z, int c) {
+  if (B < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "B and L must be positive");
+  if (c_z != 128 || c != 128) return fail(TMU_ERR_UNSUPPORTED, "only c_z == c == 128 is built");
+  if (L > 8192) return fail(TMU_ERR_UNSUPPORTED, "L > 8192");
+  if (static_cast<long long>(B) * c > 65535) return fail(TMU_ERR_UNSUPPORTED, "B*c > 65535");
+  return TMU_OK;
+}
+
+int check_weights(const tmu_trimul_weights* w, bool k1, bool k3) {
+  if (w == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "weights is NULL");
+  if (k1 && (!w->ln_in_w || !w->ln_in_b || !w->w_proj)) return fail(TMU_ERR_INVALID_ARGUMENT, "K1 weights missing");
+  if (k3 && (!w->ln_in_w || !w->ln_in_b || !w->ln_mix_w || !w->ln_mix_b || !w->w_emit || !w->w_gate))
+    return fail(TMU_ERR_INVALID_ARGUMENT, "K3 weights missing");
+  const void* al[] = {w->ln_in_w, w->ln_in_b, w->w_proj, w->ln_mix_w, w->ln_mix_b, w->w_emit, w->w_gate};
+  for (const void* p : al)
+    if (p != nullptr && !aligned16(p)) return fail(TMU_ERR_MISALIGNED, "weight pointer not 16-byte aligned");
+  return TMU_OK;
+}
+
+int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int B, int L, void* a, void* b,
+              DeviceStatus* status, cudaStream_t stream) {
+  Dev dev;
+  int st = current_device(dev, 1u << 0, reinterpret_cast<const void*>(&k1::project_gate_kernel), k1::SMEM_BYTES);
+  if (st) return st;
+  k1::Params p;
+  memset(&p, 0, sizeof(p));
+  int ih = 1, jw = 128;
+  choose_tile(L, ih, jw);
+  const uint64_t Lp = row_pitch(L);
+  {
+    const uint64_t dims[4] = {128, (uint64_t)L, (uint64_t)L, (uint64_t)B};
+    const uint64_t str[3] = {256, 256ull * L, 256ull * L * L};
+    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[2] = {128, 512};
+    const uint64_t str[1] = {256};
+    const uint32_t box[2] = {64, 128};
+    if ((st = encode_map(&p.tm_w, w->w_proj, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)B * 128};
+    const uint64_t str[2] = {Lp * 2, Lp * 2 * L};
+    const uint32_t box[3] = {(uint32_t)jw, (uint32_t)ih, 64};
+    if ((st = encode_map(&p.tm_a, a, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+    if ((st = encode_map(&p.tm_b, b, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+  }
+  p.ln_w = static_cast<const __half*>(w->ln_in_w);
+  p.ln_b = static_cast<const __half*>(w->ln_in_b);
+  p.bias = w->b_proj;
+  p.mask = static_cast<const __half*>(mask);
+  p.L = L;
+  p.ih = ih;
+  p.jw = jw;
+  p.tiles_i = (L + ih - 1) / ih;
+  p.tiles_j = (L + jw - 1) / jw;
+  p.num_tiles = B * p.tiles_i * p.tiles_j;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms);
+  k1::project_gate_kernel<<<grid, k1::kThreads, k1::SMEM_BYTES, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch project_gate_kernel");
+}
+
+template <int BN, bool MN>
+int launch_k2_t(const void* a, const void* b, void* x, int Bc, int L, DeviceStatus* status, cudaStream_t stream,
+                unsigned attr_bit) {
+  using C = k2::Cfg<BN>;
+  auto kern = &k2::contract_kernel<BN, MN>;
+  Dev dev;
+  int st = current_device(dev, attr_bit, reinterpret_cast<const void*>(kern), C::SMEM_BYTES);
+  if (st) return st;
+  k2::Params p;
+  memset(&p, 0, sizeof(p));
+  const uint64_t Lp = row_pitch(L);
+  const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)Bc};
+  const uint64_t str[2] = {Lp * 2, Lp * 2 * L};
+  if (!MN) {
+    const uint32_t boxa[3] = {64, 128, 1};
+    const uint32_t boxb[3] = {64, (uint32_t)BN, 1};
+    if ((st = encode_map(&p.tm_a, a, 3, dims, str, boxa, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_map(&p.tm_b, b, 3, dims, str, boxb, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  } else {
+    const uint32_t box[3] = {64, 64, 1};
+    if ((st = encode_map(&p.tm_a, a, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_map(&p.tm_b, b, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint32_t box[3] = {64, 128, 1};
+    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  p.L = L;
+  p.tiles_m = (L + k2::BM - 1) / k2::BM;
+  p.tiles_n = (L + BN - 1) / BN;
+  p.num_tiles = Bc * p.tiles_m * p.tiles_n;
+  p.num_kb = (L + k2::BK - 1) / k2::BK;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms);
+  kern<<<grid, k2::kThreads, C::SMEM_BYTES, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch contract_kernel");
+}
+
+int launch_k2(const void* a, const void* b, void* x, int Bc, int L, bool outgoing, DeviceStatus* status,
+              cudaStream_t stream) {
+  if (L <= 128) {
+    return outgoing ? launch_k2_t<128, false>(a, b, x, Bc, L, status, stream, 1u << 1)
+                    : launch_k2_t<128, true>(a, b, x, Bc, L, status, stream, 1u << 2);
+  }
+  return outgoing ? launch_k2_t<256, false>(a, b, x, Bc, L, status, stream, 1u << 3)
+                  : launch_k2_t<256, true>(a, b, x, Bc, L, status, stream, 1u << 4);
+}
+
+int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int L, float mix_eps,
+              DeviceStatus* status, cudaStream_t stream) {
+  Dev dev;
+  int st = current_device(dev, 1u << 5, reinterpret_cast<const void*>(&k3::emit_residual_kernel), k3::SMEM_BYTES);
+  if (st) return st;
+  k3::Params p;
+  memset(&p, 0, sizeof(p));
+  int ih = 1, jw = 128;
+  choose_tile(L, ih, jw);
+  const uint64_t Lp = row_pitch(L);
+  {
+    const uint64_t dims[4] = {128, (uint64_t)L, (uint64_t)L, (uint64_t)B};
+    const uint64_t str[3] = {256, 256ull * L, 256ull * L * L};
+    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)B * 128};
+    const uint64_t str[2] = {Lp * 2, Lp * 2 * L};
+    const uint32_t box[3] = {(uint32_t)jw, (uint32_t)ih, 128};
+    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+  }
+  {
+    const uint64_t dims[2] = {128, 128};
+    const uint64_t str[1] = {256};
+    const uint32_t box[2] = {64, 128};
+    if ((st = encode_map(&p.tm_we, w->w_emit, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_map(&p.tm_wg, w->w_gate, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  p.ln_in_w = static_cast<const __half*>(w->ln_in_w);
+  p.ln_in_b = static_cast<const __half*>(w->ln_in_b);
+  p.ln_mix_w = static_cast<const __half*>(w->ln_mix_w);
+  p.ln_mix_b = static_cast<const __half*>(w->ln_mix_b);
+  p.b_emit = w->b_emit;
+  p.b_gate = w->b_gate;
+  p.mix_eps = mix_eps;
+  p.L = L;
+  p.ih = ih;
+  p.jw = jw;
+  p.tiles_i = (L + ih - 1) / ih;
+  p.tiles_j = (L + jw - 1) / jw;
+  p.num_tiles = B * p.tiles_i * p.tiles_j;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms);
+  k3::emit_residual_kernel<<<grid, k3::kThreads, k3::SMEM_BYTES, stream>>>(p);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_kernel");
+}
+
+size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+size_t cm_bytes(int B, int L, int c) { return align256(static_cast<size_t>(B) * c * L * row_pitch(L) * 2); }
+
+__global__ void wait_timeout_kernel(DeviceStatus* status, unsigned long long timeout_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ volatile int abort_sh;
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const WaitCtx ctx{status, &abort_sh, timeout_ns};
+    mbar_wait(&bar, 0, ctx, 0x901u);  // nothing arrives: must give up and record the timeout
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* tmu_version(void) { return "tmu-b200 0.1 (sm_100a)"; }
+
+const char* tmu_status_name(int s) {
+  switch (s) {
+    case TMU_OK: return "TMU_OK";
+    case TMU_ERR_INVALID_ARGUMENT: return "TMU_ERR_INVALID_ARGUMENT";
+    case TMU_ERR_MISALIGNED: return "TMU_ERR_MISALIGNED";
+    case TMU_ERR_WORKSPACE_TOO_SMALL: return "TMU_ERR_WORKSPACE_TOO_SMALL";
+    case TMU_ERR_UNSUPPORTED: return "TMU_ERR_UNSUPPORTED";
+    case TMU_ERR_CUDA: return "TMU_ERR_CUDA";
+    case TMU_ERR_DEVICE_TIMEOUT: return "TMU_ERR_DEVICE_TIMEOUT";
+    case TMU_ERR_ARCH: return "TMU_ERR_ARCH";
+    case TMU_ERR_DRIVER: return "TMU_ERR_DRIVER";
+    default: return "TMU_ERR_UNKNOWN";
+  }
+}
+
+const char* tmu_last_error(void) { return g_last_error.c_str(); }
+
+int tmu_device_check(void) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (major != 10 || minor != 0) {
+    char buf[96];
+    snprintf(buf, sizeof(buf), "device %d is sm_%d%d; kernels are built for sm_100a", dev, major, minor);
+    return fail(TMU_ERR_ARCH, buf);
+  }
+  return TMU_OK;
+}
+
+int tmu_row_pitch(int L) { return row_pitch(L); }
+
+int tmu_proj_row_order(int c, int* order) {
+  if (order == nullptr || c <= 0 || c % 64 != 0) return fail(TMU_ERR_INVALID_ARGUMENT, "c must be a multiple of 64");
+  // chunk q covers 64 channels of a (q < c/64) or b; rows [signal 64 | gate 64]
+  const int per = c / 64;
+  for (int q = 0; q < 2 * per; ++q) {
+    const int which = q < per ? 0 : 1;  // 0 = a, 1 = b
+    const int ch0 = (q % per) * 64;
+    for (int r = 0; r < 64; ++r) {
+      order[q * 128 + r] = which * c + ch0 + r;               // signal rows: [0, c) a, [c, 2c) b
+      order[q * 128 + 64 + r] = 2 * c + which * c + ch0 + r;  // gate rows:   [2c, 3c) a, [3c, 4c) b
+    }
+  }
+  return TMU_OK;
+}
+
+size_t tmu_workspace_bytes(int B, int L, int c_z, int c) {
+  (void)c_z;
+  if (B < 1 || L < 1 || c < 1) return 0;
+  return TMU_STATUS_BYTES + 3 * cm_bytes(B, L, c);
+}
+
+unsigned long long tmu_set_wait_timeout_ns(unsigned long long ns) {
+  const unsigned long long old = g_timeout_ns;
+  g_timeout_ns = ns;
+  return old;
+}
+
+int tmu_reset_status(void* status, void* stream) {
+  if (status == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "status is NULL");
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(DeviceStatus), static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "cudaMemsetAsync(status)");
+}
+
+int tmu_read_status(const void* status, void* stream, int* code, int* site) {
+  if (status == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "status is NULL");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  DeviceStatus h;
+  e = cudaMemcpy(&h, status, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  if (code) *code = static_cast<int>(h.code);
+  if (site) *site = static_cast<int>(h.site);
+  return TMU_OK;
+}
+
+int tmu_project_gate(const void* z, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z, int c,
+                     void* a, void* b, void* status, void* stream) {
+  int st = check_sizes(B, L, c_z, c);
+  if (st) return st;
+  if ((st = check_weights(w, true, false))) return st;
+  if (!z || !a || !b || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!aligned16(z) || !aligned16(a) || !aligned16(b)) return fail(TMU_ERR_MISALIGNED, "z/a/b not 16-byte aligned");
+  return launch_k1(z, mask, w, B, L, a, b, static_cast<DeviceStatus*>(status), static_cast<cudaStream_t>(stream));
+}
+
+int tmu_contract(const void* a, const void* b, void* x, int Bc, int L, int outgoing, void* status, void* stream) {
+  if (Bc < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "Bc and L must be positive");
+  if (L > 8192 || Bc > 65535) return fail(TMU_ERR_UNSUPPORTED, "L > 8192 or Bc > 65535");
+  if (!a || !b || !x || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(x)) return fail(TMU_ERR_MISALIGNED, "a/b/x not 16-byte aligned");
+  return launch_k2(a, b, x, Bc, L, outgoing != 0, static_cast<DeviceStatus*>(status),
+                   static_cast<cudaStream_t>(stream));
+}
+
+int tmu_emit_residual(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int L, int c_z,
+                      int c, float mix_eps, void* status, void* stream) {
+  int st = check_sizes(B, L, c_z, c);
+  if (st) return st;
+  if ((st = check_weights(w, false, true))) return st;
+  if (!x || !z || !z_out || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!aligned16(x) || !aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "x/z not 16-byte aligned");
+  if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
+  return launch_k3(x, z, z_out, w, B, L, mix_eps, static_cast<DeviceStatus*>(status),
+                   static_cast<cudaStream_t>(stream));
+}
+
+int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z,
+               int c, int outgoing, float mix_eps, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_sizes(B, L, c_z, c);
+  if (st) return st;
+  if ((st = check_weights(w, true, true))) return st;
+  if (!z || !z_out || !workspace) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail(TMU_ERR_MISALIGNED, "workspace not 256-byte aligned");
+  if (!aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "z not 16-byte aligned");
+  if (workspace_bytes < tmu_workspace_bytes(B, L, c_z, c)) return fail(TMU_ERR_WORKSPACE_TOO_SMALL, "workspace too small");
+  if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  DeviceStatus* status = reinterpret_cast<DeviceStatus*>(ws);
+  const size_t cm = cm_bytes(B, L, c);
+  void* a = ws + TMU_STATUS_BYTES;
+  void* b = ws + TMU_STATUS_BYTES + cm;
+  void* x = ws + TMU_STATUS_BYTES + 2 * cm;
+  if ((st = tmu_reset_status(status, stream))) return st;
+  if ((st = launch_k1(z, mask, w, B, L, a, b, status, s))) return st;
+  if ((st = launch_k2(a, b, x, B * c, L, outgoing != 0, status, s))) return st;
+  return launch_k3(x, z, z_out, w, B, L, mix_eps, status, s);
+}
+
+int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream) {
+  if (status == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "status is NULL");
+  wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<DeviceStatus*>(status),
+                                                                       timeout_ns);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch wait_timeout_kernel");
+}
+
+}  // extern "C"

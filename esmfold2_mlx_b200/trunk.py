@@ -1,0 +1,136 @@
+"""The folding trunk on B200: a drop-in for the reference's MLX trunk module.
+
+Mirrors ``src/esmfold2_mlx/mlx_trunk.py`` / ``mlx_trunk_kernels.py`` / ``var_mlx_trunk.py``:
+
+* :func:`trunk_params` (``mlx_trunk.py:58-69``) copies every block's weights once into
+  device-resident fp16 buffers in the kernels' layouts (fp16 scheme with the 1/256 pre-scale);
+* :func:`block_forward` / :func:`trunk_forward` / :func:`make_trunk`
+  (``mlx_trunk_kernels.py:232-255``) run tri-mul out, tri-mul in and the pair transition;
+* :class:`CUDAFoldingTrunk` (``var_mlx_trunk.py:24-46``) is an ``nn.Module`` with the same
+  surface as ``MLXFoldingTrunk``: ``params``, ``_fn(params, z, mask)``, ``set_chunk_size``,
+  ``set_kernel_backend`` and ``forward(pair, pair_attention_mask=None)`` -> fp32 on
+  ``pair.device``.
+
+Each triangle update is one C-ABI call (three sm_100a kernels).  The pair transition between
+them is torch on the GPU (cuBLAS GEMMs + element-wise ops with the reference's fp16 rounding
+points); it is not part of the accelerated tri-mul path.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import ops
+
+EPS = ops.EPS
+
+
+def _transition_params(tr, device) -> dict:
+    h16 = lambda t: t.detach().float().cpu().to(torch.float16).to(device).contiguous()  # noqa: E731
+    act = getattr(tr.ffn, "activation", "swiglu")
+    return {
+        "ln_w": h16(tr.norm.weight), "ln_b": h16(tr.norm.bias),
+        "w12": h16(tr.ffn.w12.weight),  # nn.Linear layout [2h or h, c_z]
+        "w3t": h16(tr.ffn.w3.weight.T),  # [h, c_z] so that z + s @ w3t is one addmm
+        "activation": act,
+    }
+
+
+def trunk_params(folding_trunk, dtype=torch.float16, device="cuda", biases: list | None = None) -> list:
+    """Copy every block's weights out of a trunk-shaped module (``mlx_trunk.py:58-69``).
+
+    ``biases``: optional per-block ``{"out": {...}, "in": {...}}`` tri-mul biases (not part of
+    the reference module tree; see :func:`esmfold2_mlx_b200.synthetic.trimul_biases`)."""
+    if dtype != torch.float16:
+        raise ValueError("the B200 trunk implements the reference's fp16 scheme only")
+    blocks = []
+    for i, blk in enumerate(folding_trunk.blocks):
+        bb = biases[i] if biases is not None else {}
+        blocks.append({
+            "out": ops.TrimulWeights.from_module(blk.tri_mul_out, device, bb.get("out")),
+            "in": ops.TrimulWeights.from_module(blk.tri_mul_in, device, bb.get("in")),
+            **_transition_params(blk.pair_transition, device),
+        })
+    return blocks
+
+
+def transition_(p: dict, z: torch.Tensor) -> torch.Tensor:
+    """``z + ffn(LN(z))`` in place (``mlx_trunk_kernels.py:236-239``): fp16 LayerNorm output,
+    fp16 GEMM output, three fp16 element-wise ops for SwiGLU, one-rounding ``addmm`` residual."""
+    c_z = z.shape[-1]
+    h = F.layer_norm(z, (c_z,), p["ln_w"], p["ln_b"], EPS)
+    x = F.linear(h, p["w12"])
+    if p["activation"] == "swiglu":
+        x1, x2 = x.chunk(2, dim=-1)
+        s = x1 * torch.sigmoid(x1) * x2
+    else:
+        s = torch.relu(x)
+    z2 = z.view(-1, c_z)
+    torch.addmm(z2, s.reshape(-1, s.shape[-1]), p["w3t"], out=z2)
+    return z
+
+
+def block_forward(p: dict, z: torch.Tensor, mask, mix_eps: float = ops.MIX_EPS_FP16,
+                  workspace: ops.Workspace | None = None) -> torch.Tensor:
+    """One PairUpdateBlock, updating fp16 ``z`` [B, L, L, c_z] in place."""
+    ops.trimul(z, mask, p["out"], True, mix_eps, out=z, workspace=workspace)
+    ops.trimul(z, mask, p["in"], False, mix_eps, out=z, workspace=workspace)
+    return transition_(p, z)
+
+
+def trunk_forward(params: list, z: torch.Tensor, mask=None, mix_eps: float = ops.MIX_EPS_FP16,
+                  workspace: ops.Workspace | None = None) -> torch.Tensor:
+    """z in any float dtype on any device; computed in fp16 on the params' device; returns fp32
+    there (``mlx_trunk_kernels.py:242-249``)."""
+    device = params[0]["out"].device
+    z = z.to(device=device, dtype=torch.float16).contiguous().clone()
+    if mask is not None:
+        mask = mask.to(device=device, dtype=torch.float16).contiguous()
+    ws = workspace if workspace is not None else ops.Workspace()
+    for p in params:
+        block_forward(p, z, mask, mix_eps, ws)
+    return z.float()
+
+
+class _Trunk:
+    """The compiled-trunk callable ``fn(params, z, mask)`` (``make_trunk``'s return value)."""
+
+    def __init__(self, mix_eps: float):
+        self.mix_eps = mix_eps
+        self.workspace = ops.Workspace()
+
+    def __call__(self, params, z, mask=None):
+        return trunk_forward(params, z, mask, self.mix_eps, self.workspace)
+
+
+def make_trunk(dtype=torch.float16):
+    """Trunk function for params from :func:`trunk_params` (``mlx_trunk_kernels.py:252-255``)."""
+    if dtype != torch.float16:
+        raise ValueError("the B200 trunk implements the reference's fp16 scheme only")
+    return _Trunk(ops.MIX_EPS_FP16)
+
+
+class CUDAFoldingTrunk(nn.Module):
+    """Drop-in replacement for ``model.folding_trunk`` (``var_mlx_trunk.py:24-46``)."""
+
+    def __init__(self, folding_trunk, dtype=torch.float16, device="cuda", biases: list | None = None):
+        super().__init__()
+        self.params = trunk_params(folding_trunk, dtype, device, biases)
+        self._fn = make_trunk(dtype)
+
+    # FoldingTrunk API the model calls on its trunk; the fused kernels ignore both.
+    def set_chunk_size(self, chunk_size):
+        pass
+
+    def set_kernel_backend(self, backend):
+        pass
+
+    def forward(self, pair, pair_attention_mask=None):
+        # A single-chain fold has an all-ones mask; skipping it saves a multiply per tri-mul.
+        mask = None
+        if pair_attention_mask is not None and not bool(pair_attention_mask.all()):
+            mask = pair_attention_mask
+        out = self._fn(self.params, pair, mask)
+        return out.to(pair.device)

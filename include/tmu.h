@@ -1,0 +1,125 @@
+/*
+ * tmu.h -- C ABI of the B200 (sm_100a) triangle multiplicative update.
+ *
+ * This is the drop-in boundary for the hot path of abhi0raj/esmfold2-mlx's folding trunk
+ * (paths below are relative to the reference's src/esmfold2_mlx/).  The reference runs the
+ * tri-mul as MLX ops plus three Metal kernels compiled through mx.fast.metal_kernel; each entry
+ * point here replaces one or more of those calls:
+ *
+ *   tmu_project_gate   <- proj = n @ w_in; gate_cf(proj, mask, c)        mlx_trunk_kernels.py:214-216, :85-97
+ *                         (and the input LayerNorm: mlx_trunk_kernels.py:233 / mlx_trunk.py:81)
+ *   tmu_contract       <- a @ b.swapaxes(2,3) | a.swapaxes(2,3) @ b       mlx_trunk_kernels.py:219, mlx_trunk.py:84-88
+ *   tmu_emit_residual  <- ln_cf_to_cl; @ w_emit; n @ w_out_gate; resgate  mlx_trunk_kernels.py:221-227, :152-160, :195-203
+ *   tmu_trimul         <- one whole triangle update z + _trimul(z)        mlx_trunk_kernels.py:210-229, mlx_trunk.py:79-90,94-95
+ *
+ * Conventions
+ *   - All tensors are device pointers to fp16 (IEEE binary16) unless stated; biases are fp32.
+ *   - z, z_out: [B, L, L, c_z] channels-last, contiguous, 16-byte aligned.  z_out may equal z.
+ *   - mask: [B, L, L] fp16 pair mask (reference: pair_attention_mask cast to fp16), or NULL for
+ *     an all-ones mask (var_mlx_trunk.py:40-43 skips the multiply in that case).
+ *   - a, b, x: [B*c, L, Lpad] channel-major, Lpad = tmu_row_pitch(L) (= L rounded up to 8);
+ *     the pad columns are never read.
+ *   - stream: a cudaStream_t passed as void*; every launch goes on it, nothing synchronises.
+ *   - status: device memory of at least TMU_STATUS_BYTES holding the device-side status word;
+ *     kernels record a bounded-wait timeout there (read it with tmu_read_status).
+ *   - Supported now: c_z == c == 128, 1 <= L <= 8192, B*c <= 65535.  Other sizes return
+ *     TMU_ERR_UNSUPPORTED.
+ *   - Return value: TMU_OK or a TMU_ERR_* code (never aborts the process).
+ */
+#ifndef TMU_H_
+#define TMU_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TMU_OK 0
+#define TMU_ERR_INVALID_ARGUMENT 1
+#define TMU_ERR_MISALIGNED 2
+#define TMU_ERR_WORKSPACE_TOO_SMALL 3
+#define TMU_ERR_UNSUPPORTED 4
+#define TMU_ERR_CUDA 5
+#define TMU_ERR_DEVICE_TIMEOUT 6
+#define TMU_ERR_ARCH 7
+#define TMU_ERR_DRIVER 8
+
+#define TMU_STATUS_BYTES 256
+
+/* Weights of one triangle update, device pointers (mlx_trunk.py:40-55 `_trimul_params`).
+ * w_proj rows follow tmu_proj_row_order(); the signal-a rows already carry the fp16 scheme's
+ * 1/256 pre-scale (mlx_trunk.py:47-48).  Biases are optional (NULL = the reference's form). */
+typedef struct tmu_trimul_weights {
+  const void* ln_in_w;  /* [c_z]       norm_start.weight */
+  const void* ln_in_b;  /* [c_z]       norm_start.bias */
+  const void* w_proj;   /* [4c, c_z]   proj_bundle.weight rows, packed order */
+  const float* b_proj;  /* [4c]        fp32, packed order, or NULL */
+  const void* ln_mix_w; /* [c]         norm_mix.weight */
+  const void* ln_mix_b; /* [c]         norm_mix.bias */
+  const void* w_emit;   /* [c_z, c]    proj_emit.weight */
+  const float* b_emit;  /* [c_z]       fp32 or NULL */
+  const void* w_gate;   /* [c_z, c_z]  proj_gate.weight */
+  const float* b_gate;  /* [c_z]       fp32 or NULL */
+} tmu_trimul_weights;
+
+/* Library version string. */
+const char* tmu_version(void);
+
+/* Name of a status code ("TMU_OK", "TMU_ERR_UNSUPPORTED", ...). */
+const char* tmu_status_name(int status);
+
+/* Last CUDA error string seen by the library on this thread (for TMU_ERR_CUDA / _DRIVER). */
+const char* tmu_last_error(void);
+
+/* Checks that the current device is a Blackwell sm_100 part the kernels were built for. */
+int tmu_device_check(void);
+
+/* Row pitch (elements) of the channel-major a, b, x buffers for sequence length L. */
+int tmu_row_pitch(int L);
+
+/* Packed-row order of proj_bundle.weight: order[r] is the proj_bundle row that becomes packed
+ * row r (chunks of 128 rows = 64 signal rows then the 64 matching gate rows, a before b).
+ * `order` must hold 4*c ints. */
+int tmu_proj_row_order(int c, int* order);
+
+/* Bytes of workspace tmu_trimul needs: status word + a + b + x. */
+size_t tmu_workspace_bytes(int B, int L, int c_z, int c);
+
+/* Default bound for every device-side wait, in nanoseconds (initially 2e9).  Returns the old value. */
+unsigned long long tmu_set_wait_timeout_ns(unsigned long long ns);
+
+/* Zero the status word (async on `stream`). */
+int tmu_reset_status(void* status, void* stream);
+
+/* Synchronise `stream`, then copy the status word to the host.  *code is TMU_OK or
+ * TMU_ERR_DEVICE_TIMEOUT; *site identifies the wait that gave up (0 if none). */
+int tmu_read_status(const void* status, void* stream, int* code, int* site);
+
+/* K1: n = LN(z); a, b = gated projections of n, channel-major.  outputs a, b: [B*c, L, Lpad]. */
+int tmu_project_gate(const void* z, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z,
+                     int c, void* a, void* b, void* status, void* stream);
+
+/* K2: x[d] = a[d] b[d]^T (outgoing != 0) or a[d]^T b[d] (incoming), d in [0, Bc). fp32 accumulate. */
+int tmu_contract(const void* a, const void* b, void* x, int Bc, int L, int outgoing, void* status, void* stream);
+
+/* K3: z_out = z + fp16(LN_mix(x) @ w_emit) * sigmoid(fp16(LN(z) @ w_gate)). */
+int tmu_emit_residual(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int L,
+                      int c_z, int c, float mix_eps, void* status, void* stream);
+
+/* K1 -> K2 -> K3: z_out = z + tri-mul(z).  `workspace` of tmu_workspace_bytes() bytes, 256-byte
+ * aligned; its first TMU_STATUS_BYTES are the status word (zeroed by this call). */
+int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z,
+               int c, int outgoing, float mix_eps, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Self-test of the bounded-wait machinery: launches one CTA that waits on an mbarrier nothing
+ * ever arrives at, with a limit of `timeout_ns`; the kernel must give up, record
+ * TMU_ERR_DEVICE_TIMEOUT in `status` and exit.  Returns the launch status. */
+int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TMU_H_ */

@@ -1,0 +1,66 @@
+"""CPU checks of the C-ABI library: it loads without a GPU, exports every symbol include/tmu.h
+declares, and its host-only helpers agree with the Python side.  No kernel is launched."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from esmfold2_mlx_b200 import _lib, build, ops
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build.build()  # no-op when up to date; nvcc cross-compiles sm_100a without a GPU
+    return _lib.load()
+
+
+def _declared_symbols():
+    src = open(os.path.join(ROOT, "include", "tmu.h")).read()
+    return sorted(set(re.findall(r"\b(tmu_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    declared = _declared_symbols()
+    assert len(declared) >= 14
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert set(declared) == set(_lib.SIGNATURES), "ctypes signatures out of sync with tmu.h"
+
+
+def test_host_helpers(lib):
+    assert lib.tmu_version().startswith(b"tmu-b200")
+    assert lib.tmu_status_name(0) == b"TMU_OK"
+    assert lib.tmu_status_name(6) == b"TMU_ERR_DEVICE_TIMEOUT"
+    for code, name in _lib.STATUS_NAMES.items():
+        assert lib.tmu_status_name(code).decode() == name
+    for L in (1, 7, 8, 76, 146, 238, 3072):
+        assert lib.tmu_row_pitch(L) == ops.row_pitch(L) and ops.row_pitch(L) % 8 == 0
+    assert ops.proj_row_order(128) == ops.proj_row_order_py(128)
+    assert sorted(ops.proj_row_order_py(128)) == list(range(512))
+    assert lib.tmu_proj_row_order(100, (ctypes.c_int * 400)()) == 1
+
+
+def test_workspace_size(lib):
+    for B, L in ((1, 76), (64, 146), (1, 3072)):
+        cm = B * 128 * L * ops.row_pitch(L) * 2
+        cm = (cm + 255) // 256 * 256
+        assert lib.tmu_workspace_bytes(B, L, 128, 128) == 256 + 3 * cm
+    assert lib.tmu_workspace_bytes(0, 10, 128, 128) == 0
+
+
+def test_argument_checks_need_no_gpu(lib):
+    # shape / null checks run before any CUDA call
+    W = ctypes.POINTER(_lib.TmuTrimulWeights)
+    assert lib.tmu_trimul(None, None, None, W(), 1, 64, 256, 256, 1, 1e-5, None, 0, None) == 4  # unsupported c
+    assert lib.tmu_trimul(None, None, None, W(), 0, 64, 128, 128, 1, 1e-5, None, 0, None) == 1
+    assert lib.tmu_contract(None, None, None, 0, 64, 1, None, None) == 1
+    assert lib.tmu_contract(None, None, None, 1, 9000, 1, None, None) == 4
+    assert lib.tmu_reset_status(None, None) == 1
+    old = lib.tmu_set_wait_timeout_ns(123)
+    assert lib.tmu_set_wait_timeout_ns(old) == 123
