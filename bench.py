@@ -1,0 +1,448 @@
+#!/usr/bin/env python
+"""Benchmark: triangle-multiplicative-update pair-cells/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {b200,reference}]
+
+Workload: one fold, L = 238, c_z = c = 128, fp16 storage, outgoing then
+incoming tri-mul back to back, the last 24 residues masked out (pair mask m_i*m_j), Linear
+weights N(0, 1/fan_in) plus N(0, 0.02) biases, z ~ N(0, 1).  One step = tri-mul out + tri-mul in
+= 2 * 238^2 pair-cells.  Inputs are seeded synthetic tensors with the reference's shapes
+(Biohub checkpoints are not available); weights are random-init with the reference architecture.
+
+* value      device throughput: inputs resident in HBM, each step one CUDA-graph replay of the
+             two C-ABI tri-mul calls, timed with CUDA events on the launching stream; L2 is
+             flushed (256 MiB write) between steps, outside the timed intervals.
+* e2e        the same metric through the public API (``ops.trimul``) with the step's input
+             copied from pinned host memory and the result copied back, inside the interval.
+* roofline   the kernel with the largest time share, from per-kernel CUDA events captured in a
+             second graph (K1 project+gate, K2 contraction, K3 emit+residual, each launched
+             through its own C-ABI entry point); algorithmic bytes / FLOPs per launch as stated
+             in DESIGN.md; peaks from MEASURED_PEAKS.json.
+* N > 1      one process per GPU (torchrun), each rank runs its own fold (seed + rank): weak
+             scaling, no collective on the data path; times are the max over ranks.
+* --impl reference   the reference's CPU path (the PyTorch restatement in oracle/, all host
+             threads) on the same workload; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "tri-mul pair-cells/s (L^2 x tri-mul blocks / s)"
+UNIT = "pair-cells/s"
+C_Z = C = 128
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _init_pg(ws, local, backend):
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local) if backend == "nccl" else None)
+
+
+def _max_over_ranks(x: float, ws: int, device) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.lines: list[str] = []
+        self.proc = None
+        self.device_index = device_index
+
+    def start(self):
+        ident = str(self.device_index)
+        try:
+            uuid = str(torch.cuda.get_device_properties(self.device_index).uuid)
+            if uuid:
+                ident = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            pass
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+WORKLOADS = ("c2", "c1", "c4", "L2048")
+
+
+def _workload(rank: int, device, name: str = "c2"):
+    """Seeded weights and one step's input for a named configuration (``synthetic.CONFIGS``);
+    ``device=None`` keeps everything on the CPU (reference arm)."""
+    from esmfold2_mlx_b200.synthetic import CONFIGS, FoldingTrunk, pair_mask, pair_tensor, trimul_biases
+
+    cfg = CONFIGS[name]
+    trunk = FoldingTrunk(1, C_Z, C, seed=cfg.seed)
+    biases = {d: (trimul_biases(C_Z, C, cfg.seed + 31 + i) if cfg.biases else None)
+              for i, d in enumerate(("out", "in"))}
+    w = None
+    if device is not None:
+        from esmfold2_mlx_b200 import ops
+
+        w = {d: ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + d), device, biases[d])
+             for d in ("out", "in")}
+    z = pair_tensor(cfg.B, cfg.L, C_Z, cfg.seed + rank).half()
+    mask = pair_mask(cfg.B, cfg.L, cfg.n_pad).half() if cfg.n_pad else None
+    return cfg, trunk, biases, w, z, mask
+
+
+def _cpu_sample(trunk, biases, z, mask, min_seconds: float):
+    """Oracle (CPU) out+in tri-muls on the first fold of the workload, repeated until
+    ``min_seconds`` have elapsed.  Returns (pair-cells processed, seconds)."""
+    from oracle import trimul_oracle as orc
+
+    p = {d: orc.trimul_params(getattr(trunk.blocks[0], "tri_mul_" + d), True, biases[d]) for d in ("out", "in")}
+    zf = z[:1].float()
+    mf = None if mask is None else mask[:1].float()
+    L = zf.shape[1]
+    n, t0 = 0, time.perf_counter()
+    while True:
+        z1 = orc.trimul_fp16(p["out"], zf, mf, True)
+        orc.trimul_fp16(p["in"], z1, mf, False)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            return n * 2 * L * L, el
+
+
+def run_reference(args, ws, rank, local):
+    """The reference arm: the reference's CPU path (the oracle port, all host threads) on the
+    same workload; one step = out+in tri-mul of one fold (a bounded sample for batched configs)."""
+    if rank != 0:
+        return
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    cfg, trunk, biases, _, z, mask = _workload(0, None, args.workload)
+    L = cfg.L
+    from oracle import trimul_oracle as orc
+
+    p = {d: orc.trimul_params(getattr(trunk.blocks[0], "tri_mul_" + d), True, biases[d]) for d in ("out", "in")}
+    zf = z[:1].float()
+    mf = None if mask is None else mask[:1].float()
+    for _ in range(args.warmup):
+        orc.trimul_fp16(p["in"], orc.trimul_fp16(p["out"], zf, mf, True), mf, False)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        orc.trimul_fp16(p["in"], orc.trimul_fp16(p["out"], zf, mf, True), mf, False)
+    el = time.perf_counter() - t0
+    cells = 2 * L * L
+    value = cells * args.steps / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": _config_dict(cfg, 1),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps, each out+in tri-mul of one fold at L={L}; "
+                                   "oracle/trimul_oracle.py on torch CPU (fp32 math, fp16 rounding points)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def _config_dict(cfg, ws):
+    return {"workload": cfg.name, "L": cfg.L, "B": cfg.B, "c_z": C_Z, "c": C, "directions": ["out", "in"],
+            "mask_pad": cfg.n_pad, "biases": cfg.biases, "parallelism": f"folds x{ws} (one fold group per GPU)",
+            "l2": "flushed between steps (256 MiB write, outside the timed intervals)",
+            "launch": "one CUDA graph per step"}
+
+
+def _kernel_costs(L: int, B: int, masked: bool):
+    """Algorithmic bytes and FLOPs per launch of each kernel (one tri-mul)."""
+    cells = B * L * L
+    return {
+        "K1_project_gate": {"bytes": cells * (2 * C_Z + (2 if masked else 0) + 2 * 2 * C),
+                            "flops": cells * 2 * C_Z * 4 * C},
+        "K2_contract": {"bytes": cells * (2 * 2 * C + 2 * C), "flops": cells * 2 * C * L},
+        "K3_emit_residual": {"bytes": cells * (2 * C + 2 * C_Z + 2 * C_Z), "flops": cells * 2 * (C * C_Z + C_Z * C_Z)},
+    }
+
+
+def run_b200(args, ws, rank, local):
+    from esmfold2_mlx_b200 import _lib, ops
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
+    cfg, trunk, biases, w, z_host, mask_host = _workload(rank, device, args.workload)
+    L, B = cfg.L, cfg.B
+    cells_per_step = 2 * B * L * L
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+
+    z0 = z_host.to(device)
+    mask = None if mask_host is None else mask_host.to(device)
+    z1 = torch.empty_like(z0)
+    z2 = torch.empty_like(z0)
+    wsp = ops.Workspace()
+    wsp.get(B, L, C_Z, C, device)
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
+
+    def step():
+        ops.trimul(z0, mask, w["out"], True, out=z1, workspace=wsp)
+        ops.trimul(z1, mask, w["in"], False, out=z2, workspace=wsp)
+
+    # per-kernel instrumented step: the same work through the per-kernel entry points
+    Lp = ops.row_pitch(L)
+    a = torch.empty(B * C, L, Lp, dtype=torch.float16, device=device)
+    b = torch.empty_like(a)
+    x = torch.empty_like(a)
+    status = ops.new_status(device)
+    lib = _lib.load()
+    sp = ops._stream_ptr(device)
+    kev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(7)]
+
+    def step_kernels():
+        zin = z0
+        for k, (d, outgoing, zout) in enumerate((("out", True, z1), ("in", False, z2))):
+            wt = w[d]
+            kev[3 * k].record()
+            _lib.check(lib.tmu_project_gate(ops._ptr(zin), ops._ptr(mask), ops.ctypes.byref(wt.struct), B, L, C_Z, C,
+                                            ops._ptr(a), ops._ptr(b), ops._ptr(status), sp), "K1")
+            kev[3 * k + 1].record()
+            _lib.check(lib.tmu_contract(ops._ptr(a), ops._ptr(b), ops._ptr(x), B * C, L, 1 if outgoing else 0,
+                                        ops._ptr(status), sp), "K2")
+            kev[3 * k + 2].record()
+            _lib.check(lib.tmu_emit_residual(ops._ptr(x), ops._ptr(zin), ops._ptr(zout), ops.ctypes.byref(wt.struct),
+                                             B, L, C_Z, C, ops.MIX_EPS_FP16, ops._ptr(status), sp), "K3")
+            zin = zout
+        kev[6].record()
+
+    # eager warm-up (first-call host setup), then capture both steps as CUDA graphs
+    step()
+    step_kernels()
+    torch.cuda.synchronize()
+    g_step, g_kern = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step, stream=stream):
+        step()
+    with torch.cuda.graph(g_kern, stream=stream):
+        step_kernels()
+    torch.cuda.synchronize()
+
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        g_step.replay()
+    torch.cuda.synchronize()
+    _barrier(ws)
+
+    # ---------------- timed region: K steps ----------------
+    sampler = ClockSampler(local)
+    sampler.start()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    _barrier(ws)
+    for e0, e1 in evs:
+        flush.zero_()
+        e0.record()
+        g_step.replay()
+        e1.record()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    step_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
+    clocks = sampler.stop()
+    step_ms_max = _max_over_ranks(step_ms, ws, device)
+    ms_per_step = step_ms_max / args.steps
+    value = ws * cells_per_step / (ms_per_step * 1e-3)
+    code, site = ops.read_status(wsp.status)
+    if code != 0:
+        raise RuntimeError(f"device status {code} at site {site:#x}")
+
+    # ---------------- per-kernel times (instrumented graph) ----------------
+    names = ["K1_project_gate", "K2_contract", "K3_emit_residual"]
+    ktime = {n: 0.0 for n in names}
+    for _ in range(args.steps):
+        flush.zero_()
+        g_kern.replay()
+        torch.cuda.synchronize()
+        for k in range(2):
+            for j, n in enumerate(names):
+                ktime[n] += kev[3 * k + j].elapsed_time(kev[3 * k + j + 1])
+    n_launch = 2 * args.steps
+    kavg = {n: ktime[n] / n_launch for n in names}  # ms per launch
+    share = {n: ktime[n] / sum(ktime.values()) for n in names}
+    dom = max(names, key=lambda n: ktime[n])
+    hbm, tflops, peak_kind = _peaks()
+    costs = _kernel_costs(L, B, mask is not None)
+    kernels = {}
+    for n in names:
+        t = kavg[n] * 1e-3
+        byt, fl = costs[n]["bytes"], costs[n]["flops"]
+        bound = "tensor" if fl / (tflops * 1e12) > byt / (hbm * 1e9) else "hbm"
+        ach = (fl / t / 1e12) if bound == "tensor" else (byt / t / 1e9)
+        pk = tflops if bound == "tensor" else hbm
+        kernels[n] = {"us_per_launch": round(kavg[n] * 1e3, 3), "share": round(share[n], 4), "bound": bound,
+                      "achieved": round(ach, 2), "frac": round(ach / pk, 4)}
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        tj = json.load(open(tpath))
+        per_cell = tj.get(dom, {}).get("dram_bytes_per_cell")
+        if per_cell is not None:
+            traffic = per_cell * B * L * L
+    d = kernels[dom]
+    roofline = {"kernel": dom, "bound": d["bound"], "achieved": d["achieved"],
+                "peak": tflops if d["bound"] == "tensor" else hbm,
+                "unit": "TFLOP/s" if d["bound"] == "tensor" else "GB/s", "frac": d["frac"], "traffic": traffic,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)" if peak_kind == "measured" else "fallback",
+                "algorithmic_per_launch": costs[dom], "kernels": kernels}
+
+    # ---------------- end to end through the public API, host buffers ----------------
+    zh = z_host.pin_memory()
+    mh = None if mask_host is None else mask_host.pin_memory()
+    outh = torch.empty_like(z_host).pin_memory()
+    z_in = torch.empty_like(z0)
+    m_in = None if mask is None else torch.empty_like(mask)
+    e2e_ms = 0.0
+    for i in range(args.steps + 2):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        z_in.copy_(zh, non_blocking=True)
+        if m_in is not None:
+            m_in.copy_(mh, non_blocking=True)
+        ops.trimul(z_in, m_in, w["out"], True, out=z1, workspace=wsp)
+        ops.trimul(z1, m_in, w["in"], False, out=z2, workspace=wsp)
+        outh.copy_(z2, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        if i >= 2:
+            e2e_ms += e0.elapsed_time(e1)
+    e2e_ms = _max_over_ranks(e2e_ms, ws, device) / args.steps
+    h2d = zh.numel() * zh.element_size() + (0 if mh is None else mh.numel() * mh.element_size())
+    d2h = outh.numel() * outh.element_size()
+    e2e = {"value": ws * cells_per_step / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
+
+    # ---------------- CPU baseline (rank 0, N = 1) ----------------
+    cpu = None
+    if ws == 1 and not args.no_cpu_baseline and L <= 512:
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        ncells, el = _cpu_sample(trunk, biases, z_host, mask_host, args.cpu_seconds)
+        cpu = {"value": ncells / el, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{ncells // (2 * L * L)} x (out+in tri-mul of one fold at L={L}) in {el:.1f} s; "
+                         "oracle/trimul_oracle.py on torch CPU (fp32 math, fp16 rounding points)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": _config_dict(cfg, ws),
+            "e2e": e2e, "gpu_launches": 6 * args.steps, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del g_step, g_kern
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", choices=WORKLOADS, default="c2",
+                    help="c2 (default: the metric's configuration), c1, c4 (64 folds x L=146), L2048")
+    args = ap.parse_args()
+    ws, rank, local = _dist()
+    if args.impl == "reference":
+        run_reference(args, ws, rank, local)
+        return
+    _init_pg(ws, local, "nccl")
+    try:
+        run_b200(args, ws, rank, local)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
