@@ -15,10 +15,12 @@
 //   warp 0      TMA: packed weights once (resident, 4c x c_z fp16), then z tiles (2 stages)
 //   warp 1      TMEM allocation (512 columns = 4 slots of 128) and the single MMA thread:
 //               per tile, NCH chunks of N = 128 columns ([signal 64 | gate 64] of one 64-channel
-//               block of a or b), K = c_z, each chunk into the next free TMEM slot
-//   warps 2-5   LayerNorm of the z tile in shared memory, in place (row = position)
-//   warps 6-13  epilogue: two warps per TMEM lane quadrant split the 64 channels of a chunk;
-//               gate, mask, fp16, transpose through shared memory, TMA store of a 64 x ih x jw box
+//               block of a or b), K = c_z, each chunk into the next TMEM slot
+//   warps 2-5   LayerNorm of the z tile in shared memory, in place (thread = position)
+//   warps 6-13  epilogue, two groups of four warps (one per TMEM lane quadrant); group g takes
+//               the chunks with (chunk index % 2 == g), so two chunks drain at once.  Each warp
+//               owns 32 positions: gate, mask, fp16, then a 16-channel x 32-position block is
+//               staged in shared memory and stored with its own TMA store (no CTA-wide barrier).
 #pragma once
 
 #include "tmu_common.cuh"
@@ -34,24 +36,27 @@ constexpr int KATOMS = CZ / 64;         // 64-channel swizzle atoms along K
 constexpr int ATOM_BYTES = TILE * 128;  // 128 rows x 128 B
 constexpr int WCHUNK_BYTES = 128 * CZ * 2;
 constexpr int A_BYTES = TILE * CZ * 2;
-constexpr int STG_BYTES = 64 * TILE * 2;
 constexpr int NSTAGE = 2;
 constexpr int NSLOT = 4;
+constexpr int SUB = 16;                      // channels per epilogue store
+constexpr int WSTG_BYTES = SUB * 32 * 2;     // one warp's staging buffer (16 ch x 32 positions)
 constexpr int OFF_W = 0;
 constexpr int OFF_A = OFF_W + NCH * WCHUNK_BYTES;
 constexpr int OFF_STG = OFF_A + NSTAGE * A_BYTES;
-constexpr int SMEM_BYTES = OFF_STG + 2 * STG_BYTES + 1024;
+constexpr int OFF_PAR = OFF_STG + 8 * 2 * WSTG_BYTES;  // fp32 LN gamma, beta, bias
+constexpr int PAR_FLOATS = 2 * CZ + 4 * CC;
+constexpr int SMEM_BYTES = OFF_PAR + PAR_FLOATS * 4 + 1024;
 constexpr int kThreads = 448;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
   CUtensorMap tm_z;  // z [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle
   CUtensorMap tm_w;  // packed proj weights [4c, c_z]: box {64, 128}, 128B swizzle
-  CUtensorMap tm_a;  // a [B*c, L, Lpad]: box {jw, ih, 64}, no swizzle (store)
+  CUtensorMap tm_a;  // a [B*c, L, Lpad]: box {min(jw,32), 32/min(jw,32), 16}, no swizzle (store)
   CUtensorMap tm_b;  // b, same
   const __half* ln_w;
   const __half* ln_b;
-  const float* bias;  // [4c] in packed-row order, or null
+  const float* bias;   // [4c] in packed-row order, or null
   const __half* mask;  // [B, L, L] or null
   int L, ih, jw, tiles_i, tiles_j, num_tiles;
   DeviceStatus* status;
@@ -78,9 +83,9 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   __shared__ __align__(8) uint64_t tfull[NSLOT], tempty[NSLOT], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
-  __shared__ volatile int ep_ok_sh;
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  float* par = reinterpret_cast<float*>(smem + OFF_PAR);  // [gamma 128 | beta 128 | bias 512]
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtx ctx{p.status, &abort_sh, p.timeout_ns};
@@ -95,10 +100,17 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     }
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 256);
+      mbar_init(&tempty[s], 4);  // one arrival per epilogue warp of the group that owns the slot
     }
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < PAR_FLOATS; i += blockDim.x) {
+    float v;
+    if (i < CZ) v = __half2float(p.ln_w[i]);
+    else if (i < 2 * CZ) v = __half2float(p.ln_b[i - CZ]);
+    else v = p.bias ? p.bias[i - 2 * CZ] : 0.0f;
+    par[i] = v;
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.tm_z);
@@ -176,105 +188,78 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
       if (!mbar_wait(&zfull[s], ph, ctx, kSiteLn)) break;
       uint8_t* A = smem + OFF_A + s * A_BYTES;
-      uint4 v[KATOMS * 8];
-      float sum = 0.f;
-#pragma unroll
-      for (int c16 = 0; c16 < KATOMS * 8; ++c16) {
-        v[c16] = *reinterpret_cast<const uint4*>(A + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7));
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[c16]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_half2(w[e]);
-          sum += f.x + f.y;
-        }
-      }
-      const float mean = sum * (1.0f / CZ);
-      float sq = 0.f;
-#pragma unroll
-      for (int c16 = 0; c16 < KATOMS * 8; ++c16) {
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(&v[c16]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_half2(w[e]);
-          const float d0 = f.x - mean, d1 = f.y - mean;
-          sq += d0 * d0 + d1 * d1;
-        }
-      }
-      const float rstd = rsqrtf(sq * (1.0f / CZ) + 1e-5f);
-      const __half2* lw = reinterpret_cast<const __half2*>(p.ln_w);
-      const __half2* lb = reinterpret_cast<const __half2*>(p.ln_b);
-#pragma unroll
-      for (int c16 = 0; c16 < KATOMS * 8; ++c16) {
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v[c16]);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_half2(w[e]);
-          const float2 g = __half22float2(__ldg(lw + c16 * 4 + e));
-          const float2 bb = __half22float2(__ldg(lb + c16 * 4 + e));
-          w[e] = pack_half2((f.x - mean) * rstd * g.x + bb.x, (f.y - mean) * rstd * g.y + bb.y);
-        }
-        *reinterpret_cast<uint4*>(A + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7)) = v[c16];
-      }
+      ln_row128_sw128(A, A, ATOM_BYTES, row, 1e-5f, LnParSmem{par, par + CZ});
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
       mbar_arrive(&lnfull[s]);
     }
   } else {
     // ---------------- epilogue: gate, mask, channel-major store ----------------
-    const int e = threadIdx.x - 192;  // 0..255
-    const int q = warp & 3;
-    const int h = (warp - 6) >> 2;   // which 32 of the chunk's 64 channels
+    const int ew = warp - 6;         // 0..7
+    const int q = warp & 3;          // TMEM lane quadrant
+    const int grp = ew >> 2;         // chunk parity this warp drains
     const int row = q * 32 + lane;   // position within the tile
-    uint8_t* stg = smem + OFF_STG;
-    uint32_t it = 0, cit = 0;
+    const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
+    __half* stg = reinterpret_cast<__half*>(smem + OFF_STG + ew * 2 * WSTG_BYTES);
+    const bool has_bias = p.bias != nullptr;
+    const float* bias = par + 2 * CZ;
+    uint32_t cit = 0, sit = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
       float mval = 1.0f;
       if (p.mask != nullptr && gi < p.L && gj < p.L)
         mval = __half2float(p.mask[(static_cast<size_t>(bb) * p.L + gi) * p.L + gj]);
+      const float2 m2 = make_float2(mval, mval);
       for (int qc = 0; qc < NCH; ++qc, ++cit) {
+        if ((cit & 1) != static_cast<uint32_t>(grp)) continue;
         const uint32_t slot = cit % NSLOT, sph = (cit / NSLOT) & 1;
-        if (e == 0) {
-          ep_ok_sh = mbar_wait(&tfull[slot], sph, ctx, kSiteEpilogue) ? 1 : 0;
-          bulk_wait_read<1>();  // the store that last used this staging buffer has read it
-        }
-        named_bar_sync(2, 256);
-        if (!ep_ok_sh) { ok = false; break; }
+        if (!warp_wait(&tfull[slot], sph, ctx, kSiteEpilogue)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 128 + h * 32;
-        uint32_t sg[32], gt[32];
-        tmem_ld32(taddr, sg);
-        tmem_ld32(taddr + 64, gt);
-        tmem_wait_ld2(sg, gt);
-        tc_fence_before();
-        mbar_arrive(&tempty[slot]);
-        __half* st = reinterpret_cast<__half*>(stg + (cit & 1) * STG_BYTES);
-        const int col0 = qc * 128 + h * 32;  // packed-row index of this thread's first signal column
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float s = __uint_as_float(sg[i]);
-          float g = __uint_as_float(gt[i]);
-          if (p.bias != nullptr) {
-            s += __ldg(p.bias + col0 + i);
-            g += __ldg(p.bias + col0 + 64 + i);
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 128;
+        const int col0 = qc * 128;  // packed-row index of the chunk's first signal column
+        const bool is_a = qc < NCH / 2;
+        const int ch0 = (qc % (NCH / 2)) * 64;
+#pragma unroll 1
+        for (int sub = 0; sub < 64 / SUB; ++sub, ++sit) {
+          uint32_t sg[16], gt[16];
+          tmem_ld16(taddr + sub * SUB, sg);
+          tmem_ld16(taddr + 64 + sub * SUB, gt);
+          tmem_wait_ld16x2(sg, gt);
+          if (sub == 64 / SUB - 1) {  // the whole slot has been read: hand it back to the MMA
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[slot]);
           }
-          s = round_f16(s);  // proj is an fp16 tensor in the reference
-          g = round_f16(g);
-          st[(h * 32 + i) * TILE + row] = __float2half_rn(s * sigmoid_f32(g) * mval);
-        }
-        fence_proxy_async_smem();
-        named_bar_sync(2, 256);
-        if (e == 0) {
-          const bool is_a = qc < NCH / 2;
-          const int ch0 = (qc % (NCH / 2)) * 64;
-          tma_store_3d(is_a ? &p.tm_a : &p.tm_b, st, j0, i0, bb * CC + ch0);
-          bulk_commit();
+          __half* st = stg + (sit & 1) * (WSTG_BYTES / 2);
+          if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < SUB; i += 2) {
+            float2 s = make_float2(__uint_as_float(sg[i]), __uint_as_float(sg[i + 1]));
+            float2 g = make_float2(__uint_as_float(gt[i]), __uint_as_float(gt[i + 1]));
+            if (has_bias) {
+              const int c = col0 + sub * SUB + i;
+              s = __fadd2_rn(s, make_float2(bias[c], bias[c + 1]));
+              g = __fadd2_rn(g, make_float2(bias[c + 64], bias[c + 65]));
+            }
+            s = round_f16x2(s);  // proj is an fp16 tensor in the reference
+            g = round_f16x2(g);
+            const float2 y = __fmul2_rn(__fmul2_rn(s, sigmoid_f32x2(g)), m2);
+            st[i * 32 + lane] = __float2half_rn(y.x);
+            st[(i + 1) * 32 + lane] = __float2half_rn(y.y);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(is_a ? &p.tm_a : &p.tm_b, st, j0 + jo, i0 + io, bb * CC + ch0 + sub * SUB);
+            bulk_commit();
+          }
         }
       }
     }
-    if (e == 0) bulk_wait<0>();
+    if (lane == 0) bulk_wait<0>();
   }
 
   tc_fence_before();

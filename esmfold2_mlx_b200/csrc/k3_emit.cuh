@@ -12,13 +12,15 @@
 // The LayerNorm that the reference fuses after the residual (resgate_ln's second output) is
 // the next kernel's prologue (K1 of the next tri-mul normalises the z' it loads).
 //
-// One tile = 128 positions (ih x jw block).  CTA = 10 warps, one per SM, persistent:
+// One tile = 128 positions (ih x jw block).  CTA = 14 warps, one per SM, persistent:
 //   warp 0     TMA: w_emit and w_gate once (resident), then per tile the z tile (2 stages,
 //              128B swizzle, position-major) and the x tile (channel-major, unswizzled)
 //   warp 1     TMEM (2 x 256 columns) + MMA thread: emit (A1 x W_e) and gate (A2 x W_g)
 //   warps 2-5  transforms: A1 = fp16(LN_mix(x column)), A2 = fp16(LN_in(z row)), both written
 //              as K-major 128B-swizzled UMMA operands
-//   warps 6-9  epilogue: TMEM -> gate/residual in fp32 -> z' written over the z tile -> TMA store
+//   warps 6-13 epilogue, two groups of four warps (one per TMEM lane quadrant); group h owns
+//              output channels [64h, 64h+64): TMEM -> gate/residual in fp32 -> z' written over
+//              the z tile -> each warp TMA-stores its own 32 positions x 64 channels
 #pragma once
 
 #include "tmu_common.cuh"
@@ -38,12 +40,12 @@ constexpr int OFF_X = OFF_Z + 2 * TILE_BYTES;
 constexpr int OFF_A1 = OFF_X + TILE * CC * 2;
 constexpr int OFF_A2 = OFF_A1 + TILE_BYTES;
 constexpr int SMEM_BYTES = OFF_A2 + TILE_BYTES + 1024;
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
   CUtensorMap tm_z;   // z [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle (load)
-  CUtensorMap tm_zo;  // z_out, same geometry (store)
+  CUtensorMap tm_zo;  // z_out: box {64, min(jw,32), 32/min(jw,32), 1}, 128B swizzle (per-warp store)
   CUtensorMap tm_x;   // x [B*c, L, Lpad]: box {jw, ih, c}, no swizzle (load)
   CUtensorMap tm_we;  // w_emit [c_z, c]: box {64, 128}
   CUtensorMap tm_wg;  // w_gate [c_z, c_z]: box {64, 128}
@@ -72,50 +74,6 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
-// LayerNorm of 128 fp16 values held as 16 uint4, written as fp16 to a K-major SW128 row.
-__device__ __forceinline__ void ln_row_store(uint4 (&v)[16], const __half* w, const __half* b, float eps,
-                                             uint8_t* dst, int row) {
-  float sum = 0.f;
-#pragma unroll
-  for (int c16 = 0; c16 < 16; ++c16) {
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[c16]);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_half2(u[e]);
-      sum += f.x + f.y;
-    }
-  }
-  const float mean = sum * (1.0f / 128);
-  float sq = 0.f;
-#pragma unroll
-  for (int c16 = 0; c16 < 16; ++c16) {
-    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v[c16]);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_half2(u[e]);
-      const float d0 = f.x - mean, d1 = f.y - mean;
-      sq += d0 * d0 + d1 * d1;
-    }
-  }
-  const float rstd = rsqrtf(sq * (1.0f / 128) + eps);
-  const __half2* lw = reinterpret_cast<const __half2*>(w);
-  const __half2* lb = reinterpret_cast<const __half2*>(b);
-#pragma unroll
-  for (int c16 = 0; c16 < 16; ++c16) {
-    uint32_t* u = reinterpret_cast<uint32_t*>(&v[c16]);
-    uint4 o;
-    uint32_t* ou = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_half2(u[e]);
-      const float2 g = __half22float2(__ldg(lw + c16 * 4 + e));
-      const float2 bb = __half22float2(__ldg(lb + c16 * 4 + e));
-      ou[e] = pack_half2((f.x - mean) * rstd * g.x + bb.x, (f.y - mean) * rstd * g.y + bb.y);
-    }
-    *reinterpret_cast<uint4*>(dst + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7)) = o;
-  }
-}
-
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid_constant__ Params p) {
   constexpr uint32_t IDESC = idesc_f16_f32(128, CZ, false, false);
   extern __shared__ uint8_t smem_raw[];
@@ -123,7 +81,6 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   __shared__ __align__(8) uint64_t tfull[2], tempty[2], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
-  __shared__ volatile int ep_ok_sh;
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5;
@@ -135,9 +92,9 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     mbar_init(&w_bar, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&zfull[s], 1);
-      mbar_init(&zempty[s], 1);
+      mbar_init(&zempty[s], 8);   // each epilogue warp, once its store has read the tile
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 128);
+      mbar_init(&tempty[s], 8);   // one arrival per epilogue warp
     }
     mbar_init(&xfull, 1);
     mbar_init(&xempty, 128);
@@ -231,102 +188,91 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       if (!mbar_wait(&aempty, (it & 1) ^ 1, ctx, kSiteTrA)) break;
       if (!mbar_wait(&xfull, it & 1, ctx, kSiteTrX)) break;
       {
-        // x tile is [channel][position]: gather this position's column
+        // x tile is [channel][position]: gather this position's column into row `row` of A1
+        // (raw fp16), release the x buffer, then normalise the row in place.
         const __half* X = reinterpret_cast<const __half*>(smem + OFF_X);
-        uint4 v[16];
-#pragma unroll
+        uint8_t* A1 = smem + OFF_A1;
+#pragma unroll 4
         for (int c16 = 0; c16 < 16; ++c16) {
-          uint32_t* u = reinterpret_cast<uint32_t*>(&v[c16]);
+          uint32_t u[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int ch = c16 * 8 + e * 2;
             __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
             u[e] = *reinterpret_cast<uint32_t*>(&h2);
           }
+          *reinterpret_cast<uint4*>(A1 + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7)) =
+              make_uint4(u[0], u[1], u[2], u[3]);
         }
         mbar_arrive(&xempty);
-        ln_row_store(v, p.ln_mix_w, p.ln_mix_b, p.mix_eps, smem + OFF_A1, row);
+        ln_row128_sw128(A1, A1, ATOM_BYTES, row, p.mix_eps, LnParHalf{p.ln_mix_w, p.ln_mix_b});
       }
       if (!mbar_wait(&zfull[s], ph, ctx, kSiteTrZ)) break;
-      {
-        const uint8_t* Z = smem + OFF_Z + s * TILE_BYTES;
-        uint4 v[16];
-#pragma unroll
-        for (int c16 = 0; c16 < 16; ++c16)
-          v[c16] = *reinterpret_cast<const uint4*>(Z + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7));
-        ln_row_store(v, p.ln_in_w, p.ln_in_b, 1e-5f, smem + OFF_A2, row);
-      }
+      ln_row128_sw128(smem + OFF_Z + s * TILE_BYTES, smem + OFF_A2, ATOM_BYTES, row, 1e-5f,
+                      LnParHalf{p.ln_in_w, p.ln_in_b});
       fence_proxy_async_smem();
       mbar_arrive(&afull);
     }
   } else {
     // ---------------- epilogue ----------------
-    const int e = threadIdx.x - 192;  // 0..127
-    const int q = warp & 3;
+    const int q = warp & 3;          // TMEM lane quadrant
+    const int h = (warp - 6) >> 2;   // output channels [64h, 64h+64)
     const int row = q * 32 + lane;
+    const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
+    const bool has_be = p.b_emit != nullptr, has_bg = p.b_gate != nullptr;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
       const uint32_t acc = it & 1, aph = (it >> 1) & 1;
-      if (e == 0) {
-        ep_ok_sh = (mbar_wait(&tfull[acc], aph, ctx, kSiteEpilogue) && mbar_wait(&zfull[s], ph, ctx, kSiteEpilogue))
-                       ? 1 : 0;
-      }
-      named_bar_sync(2, 128);
-      if (!ep_ok_sh) break;
+      if (!warp_wait(&tfull[acc], aph, ctx, kSiteEpilogue)) break;
+      if (!warp_wait(&zfull[s], ph, ctx, kSiteEpilogue)) break;
       tc_fence_after();
-      uint8_t* Z = smem + OFF_Z + s * TILE_BYTES;
-      const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256;
+      uint8_t* Zh = smem + OFF_Z + s * TILE_BYTES + h * ATOM_BYTES;
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256 + h * 64;
 #pragma unroll 1
-      for (int cc = 0; cc < CZ / 32; ++cc) {
-        uint32_t em[32], gt[32];
-        tmem_ld32(trow + cc * 32, em);
-        tmem_ld32(trow + CZ + cc * 32, gt);
-        tmem_wait_ld2(em, gt);
+      for (int cc = 0; cc < 4; ++cc) {  // 16 output channels at a time
+        uint32_t em[16], gt[16];
+        tmem_ld16(trow + cc * 16, em);
+        tmem_ld16(trow + CZ + cc * 16, gt);
+        tmem_wait_ld16x2(em, gt);
+        if (cc == 3) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c16 = (cc & 1) * 4 + j;
-          uint8_t* zp = Z + (cc >> 1) * ATOM_BYTES + sw128_off(row, c16);
+        for (int j = 0; j < 2; ++j) {
+          uint8_t* zp = Zh + sw128_off(row, cc * 2 + j);
           uint4 zv = *reinterpret_cast<const uint4*>(zp);
           uint32_t* zu = reinterpret_cast<uint32_t*>(&zv);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int i = j * 8 + k * 2;
-            const int n = cc * 32 + i;
-            float m0 = __uint_as_float(em[i]), m1 = __uint_as_float(em[i + 1]);
-            float g0 = __uint_as_float(gt[i]), g1 = __uint_as_float(gt[i + 1]);
-            if (p.b_emit != nullptr) {
-              m0 += __ldg(p.b_emit + n);
-              m1 += __ldg(p.b_emit + n + 1);
-            }
-            if (p.b_gate != nullptr) {
-              g0 += __ldg(p.b_gate + n);
-              g1 += __ldg(p.b_gate + n + 1);
-            }
-            m0 = round_f16(m0);
-            m1 = round_f16(m1);
-            g0 = round_f16(g0);
-            g1 = round_f16(g1);
-            const float2 zf = unpack_half2(zu[k]);
-            zu[k] = pack_half2(zf.x + m0 * sigmoid_f32(g0), zf.y + m1 * sigmoid_f32(g1));
+            const int n = h * 64 + cc * 16 + i;
+            float2 m = make_float2(__uint_as_float(em[i]), __uint_as_float(em[i + 1]));
+            float2 g = make_float2(__uint_as_float(gt[i]), __uint_as_float(gt[i + 1]));
+            if (has_be) m = __fadd2_rn(m, __ldg(reinterpret_cast<const float2*>(p.b_emit + n)));
+            if (has_bg) g = __fadd2_rn(g, __ldg(reinterpret_cast<const float2*>(p.b_gate + n)));
+            m = round_f16x2(m);  // mixed and g are fp16 tensors in the reference
+            g = round_f16x2(g);
+            const float2 zn = __ffma2_rn(m, sigmoid_f32x2(g), unpack_half2(zu[k]));
+            zu[k] = pack_half2(zn.x, zn.y);
           }
           *reinterpret_cast<uint4*>(zp) = zv;
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty[acc]);
       fence_proxy_async_smem();
-      named_bar_sync(2, 128);
-      if (e == 0) {
-        for (int a = 0; a < CZ / 64; ++a) tma_store_4d(&p.tm_zo, Z + a * ATOM_BYTES, a * 64, j0, i0, bb);
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_4d(&p.tm_zo, Zh + q * 32 * 128, h * 64, j0 + jo, i0 + io, bb);
         bulk_commit();
         bulk_wait_read<0>();
         mbar_arrive(&zempty[s]);
       }
     }
-    if (e == 0) bulk_wait<0>();
+    if (lane == 0) bulk_wait<0>();
   }
 
   tc_fence_before();

@@ -164,7 +164,8 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int 
   {
     const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)B * 128};
     const uint64_t str[2] = {Lp * 2, Lp * 2 * L};
-    const uint32_t box[3] = {(uint32_t)jw, (uint32_t)ih, 64};
+    const uint32_t jwp = jw < 32 ? jw : 32;  // one epilogue warp's 32 positions
+    const uint32_t box[3] = {jwp, 32 / jwp, (uint32_t)k1::SUB};
     if ((st = encode_map(&p.tm_a, a, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
     if ((st = encode_map(&p.tm_b, b, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
   }
@@ -251,7 +252,9 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
     const uint64_t str[3] = {256, 256ull * L, 256ull * L * L};
     const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
     if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
-    if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    const uint32_t jwp = jw < 32 ? jw : 32;  // one epilogue warp's 32 positions
+    const uint32_t boxo[4] = {64, jwp, 32 / jwp, 1};
+    if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, boxo, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
     const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)B * 128};

@@ -248,6 +248,34 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
                : "memory");
 }
 
+// 32 lanes x 16 columns of 32-bit.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld16x2(uint32_t (&r)[16], uint32_t (&s)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(s[0]), "+r"(s[1]), "+r"(s[2]), "+r"(s[3]), "+r"(s[4]), "+r"(s[5]), "+r"(s[6]),
+                 "+r"(s[7]), "+r"(s[8]), "+r"(s[9]), "+r"(s[10]), "+r"(s[11]), "+r"(s[12]), "+r"(s[13]),
+                 "+r"(s[14]), "+r"(s[15])
+               :
+               : "memory");
+}
+
+// One thread of a warp waits (bounded) and the whole warp gets its verdict.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const WaitCtx& ctx, unsigned int site) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, ctx, site) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 __device__ __forceinline__ void tmem_wait_ld2(uint32_t (&r)[32], uint32_t (&s)[32]) {
   tmem_wait_ld(r);
   asm volatile(""
@@ -299,9 +327,33 @@ __device__ __forceinline__ uint32_t sw128_off(uint32_t row, uint32_t chunk) {
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
 
-// Sigmoid in fp32: 1 / (1 + e^-x) with the hardware exponential and a correctly rounded
-// reciprocal-divide.  Saturates cleanly: e^-x = inf gives 0, e^-x = 0 gives 1.
-__device__ __forceinline__ float sigmoid_f32(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Sigmoid in fp32: 1 / (1 + 2^(-x log2 e)) with the hardware base-2 exponential and reciprocal
+// (both ~1 ulp of fp32, far below the fp16 rounding that follows).  Saturates cleanly:
+// 2^(+big) = inf gives 0, 2^(-big) = 0 gives 1.
+__device__ __forceinline__ float sigmoid_f32(float x) {
+  return rcp_approx(1.0f + ex2_approx(x * -1.4426950408889634f));
+}
+
+__device__ __forceinline__ float2 sigmoid_f32x2(float2 x) {
+  const float2 t = __fmul2_rn(x, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 d = __fadd2_rn(make_float2(ex2_approx(t.x), ex2_approx(t.y)), make_float2(1.0f, 1.0f));
+  return make_float2(rcp_approx(d.x), rcp_approx(d.y));
+}
+
+// Round a pair of fp32 values to fp16 and back (the value an fp16 tensor would hold).
+__device__ __forceinline__ float2 round_f16x2(float2 v) { return __half22float2(__floats2half2_rn(v.x, v.y)); }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
@@ -312,5 +364,85 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t v) {
   __half2 h = *reinterpret_cast<__half2*>(&v);
   return __half22float2(h);
 }
+
+// ------------------------------------------------------------------------------------------
+// LayerNorm of one 128-channel fp16 row held in a K-major 128B-swizzled tile (two 64-channel
+// atoms `atom_bytes` apart): fp32 statistics, two-pass (mean, then centred variance, as the
+// reference's Metal kernels), y = (x - mean) * rstd * gamma + beta rounded once to fp16 and
+// written to the same row of `dst` (which may be `src`).  Each pass re-reads shared memory so
+// the row is never held in registers.  `par(k, g, b)` returns gamma/beta for channels 8k..8k+7.
+// ------------------------------------------------------------------------------------------
+template <typename Par>
+__device__ __forceinline__ void ln_row128_sw128(const uint8_t* src, uint8_t* dst, int atom_bytes, int row, float eps,
+                                                Par par) {
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c16 = 0; c16 < 16; ++c16) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7));
+    acc = __fadd2_rn(acc, __fadd2_rn(__fadd2_rn(unpack_half2(v.x), unpack_half2(v.y)),
+                                     __fadd2_rn(unpack_half2(v.z), unpack_half2(v.w))));
+  }
+  const float mean = (acc.x + acc.y) * (1.0f / 128);
+  const float2 m2 = make_float2(-mean, -mean);
+  asm volatile("" ::: "memory");
+  float2 sq = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c16 = 0; c16 < 16; ++c16) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7));
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 d = __fadd2_rn(unpack_half2(u[e]), m2);
+      sq = __ffma2_rn(d, d, sq);
+    }
+  }
+  const float rstd = rsqrtf((sq.x + sq.y) * (1.0f / 128) + eps);
+  const float2 r2 = make_float2(rstd, rstd);
+  asm volatile("" ::: "memory");
+#pragma unroll 4
+  for (int c16 = 0; c16 < 16; ++c16) {
+    const int off = (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    float g[8], b[8];
+    par(c16, g, b);
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 d = __fmul2_rn(__fadd2_rn(unpack_half2(u[e]), m2), r2);
+      const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
+      o[e] = pack_half2(y.x, y.y);
+    }
+    *reinterpret_cast<uint4*>(dst + off) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// gamma/beta from fp32 arrays in shared memory
+struct LnParSmem {
+  const float* g;
+  const float* b;
+  __device__ __forceinline__ void operator()(int k, float (&gg)[8], float (&bb)[8]) const {
+    const float4 g0 = reinterpret_cast<const float4*>(g)[2 * k], g1 = reinterpret_cast<const float4*>(g)[2 * k + 1];
+    const float4 b0 = reinterpret_cast<const float4*>(b)[2 * k], b1 = reinterpret_cast<const float4*>(b)[2 * k + 1];
+    gg[0] = g0.x; gg[1] = g0.y; gg[2] = g0.z; gg[3] = g0.w; gg[4] = g1.x; gg[5] = g1.y; gg[6] = g1.z; gg[7] = g1.w;
+    bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w; bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
+  }
+};
+
+// gamma/beta from fp16 arrays in global memory (L1-cached broadcast loads)
+struct LnParHalf {
+  const __half* g;
+  const __half* b;
+  __device__ __forceinline__ void operator()(int k, float (&gg)[8], float (&bb)[8]) const {
+    const uint4 gw = __ldg(reinterpret_cast<const uint4*>(g) + k), bw = __ldg(reinterpret_cast<const uint4*>(b) + k);
+    const uint32_t gu[4] = {gw.x, gw.y, gw.z, gw.w}, bu[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = unpack_half2(gu[e]), y = unpack_half2(bu[e]);
+      gg[2 * e] = x.x; gg[2 * e + 1] = x.y;
+      bb[2 * e] = y.x; bb[2 * e + 1] = y.y;
+    }
+  }
+};
 
 }  // namespace tmu
