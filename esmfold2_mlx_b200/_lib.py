@@ -58,6 +58,7 @@ SIGNATURES = {
     "tmu_contract": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "tmu_emit_residual": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_trimul": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp]),
+    "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_selftest_wait_timeout": (_i, [_vp, _ull, _vp]),
 }
 

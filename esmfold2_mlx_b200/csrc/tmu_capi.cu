@@ -309,6 +309,35 @@ __global__ void wait_timeout_kernel(DeviceStatus* status, unsigned long long tim
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// Scratch for tmu_trimul_noalloc: a fixed, statically sized device array, so that entry point
+// never allocates.  It lives in this library's module on every GPU that loads the library, for
+// the life of the process.  Host code must not hand the symbol itself to a kernel (on the host it
+// is only a stand-in); the device address is looked up once per device with
+// cudaGetSymbolAddress, with that device current, and cached.
+// ------------------------------------------------------------------------------------------
+constexpr size_t kNoAllocBufBytes = TMU_NOALLOC_MAX_BUFFER_BYTES;
+constexpr size_t kNoAllocBytes = TMU_STATUS_BYTES + 3 * kNoAllocBufBytes;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+void* g_noalloc_addr[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(TMU_ERR_INVALID_ARGUMENT, "device id out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return TMU_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -446,6 +475,38 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
   if ((st = launch_k1(z, mask, w, B, L, a, b, status, s))) return st;
   if ((st = launch_k2(a, b, x, B * c, L, outgoing != 0, status, s))) return st;
   return launch_k3(x, z, z_out, w, B, L, mix_eps, status, s);
+}
+
+int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L,
+                       int c_z, int c, int outgoing, float mix_eps, void* status, void* stream) {
+  int st = check_sizes(B, L, c_z, c);
+  if (st) return st;
+  if ((st = check_weights(w, true, true))) return st;
+  if (!z || !z_out) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "z not 16-byte aligned");
+  if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
+  const size_t cm = cm_bytes(B, L, c);
+  if (cm > kNoAllocBufBytes) {
+    char buf[200];
+    snprintf(buf, sizeof(buf),
+             "tmu_trimul_noalloc: B*c*L*row_pitch(L)*2 = %zu bytes exceeds the static scratch of %zu bytes per "
+             "buffer; use tmu_trimul with a caller-provided workspace",
+             static_cast<size_t>(B) * c * L * row_pitch(L) * 2, kNoAllocBufBytes);
+    return fail(TMU_ERR_UNSUPPORTED, buf);
+  }
+  void* scratch = nullptr;
+  if ((st = noalloc_scratch_address(&scratch))) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  DeviceStatus* dstat = reinterpret_cast<DeviceStatus*>(status != nullptr ? status : base);
+  void* a = base + TMU_STATUS_BYTES;
+  void* b = base + TMU_STATUS_BYTES + kNoAllocBufBytes;
+  void* x = base + TMU_STATUS_BYTES + 2 * kNoAllocBufBytes;
+  // the status word must start at zero; a, b and x are fully rewritten before they are read
+  if ((st = tmu_reset_status(dstat, stream))) return st;
+  if ((st = launch_k1(z, mask, w, B, L, a, b, dstat, s))) return st;
+  if ((st = launch_k2(a, b, x, B * c, L, outgoing != 0, dstat, s))) return st;
+  return launch_k3(x, z, z_out, w, B, L, mix_eps, dstat, s);
 }
 
 int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream) {

@@ -113,6 +113,34 @@ int tmu_emit_residual(const void* x, const void* z, void* z_out, const tmu_trimu
 int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z,
                int c, int outgoing, float mix_eps, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size cap of tmu_trimul_noalloc: each of its three channel-major buffers (a, b, x) must fit in
+ * this many bytes, i.e. B * c * L * tmu_row_pitch(L) * 2 <= 8 MiB (B = 1, c = 128: L <= 178). */
+#define TMU_NOALLOC_MAX_BUFFER_BYTES (8u << 20)
+
+/* One triangle update, z_out = z + tri-mul(z), like tmu_trimul but without a workspace argument
+ * and without allocating anything.  This entry point has no counterpart in the reference.
+ *
+ * It is meant for callers that are not allowed to allocate device memory at the moment they
+ * run the update: for example a host framework that reserves all device memory up front and
+ * forbids allocation inside its execute callback, or a caller that cannot accept the implicit
+ * device-wide synchronisation that cudaMalloc/cudaFree bring.  Instead of a caller-provided
+ * workspace it uses one fixed scratch array built into this library (3 x 8 MiB plus a 256-byte
+ * status word, TMU_NOALLOC_MAX_BUFFER_BYTES per buffer), which every GPU that loads the library
+ * holds until the process exits.  Sizes beyond the cap return TMU_ERR_UNSUPPORTED with a message
+ * (tmu_last_error); use tmu_trimul for them.  The call itself issues no cudaMalloc or cudaFree.
+ *
+ * - The first call on each device looks up that device's address of the scratch array
+ *   (cudaGetSymbolAddress, with the device current) and caches it: make that first call before
+ *   any stream capture on the device.
+ * - All calls on a device share the one scratch array, which keeps the previous call's
+ *   contents.  The call clears the status word it uses; everything else is rewritten before it
+ *   is read.  Calls that can overlap on the GPU (different streams without ordering, or several
+ *   host threads) race on the scratch and give wrong results: serialise them.
+ * - `status`: device memory of TMU_STATUS_BYTES for the bounded-wait status word (read it with
+ *   tmu_read_status), or NULL to use the scratch's own word, which the caller cannot read. */
+int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L,
+                       int c_z, int c, int outgoing, float mix_eps, void* status, void* stream);
+
 /* Self-test of the bounded-wait machinery: launches one CTA that waits on an mbarrier nothing
  * ever arrives at, with a limit of `timeout_ns`; the kernel must give up, record
  * TMU_ERR_DEVICE_TIMEOUT in `status` and exit.  Returns the launch status. */
