@@ -356,13 +356,10 @@ def run_b200(args, ws, rank, local):
         pk = tflops if bound == "tensor" else hbm
         kernels[n] = {"us_per_launch": round(kavg[n] * 1e3, 3), "share": round(share[n], 4), "bound": bound,
                       "achieved": round(ach, 2), "frac": round(ach / pk, 4)}
-    traffic = None
+    traffic = None  # DRAM bytes per launch of the dominant kernel, from a committed ncu capture
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
-        tj = json.load(open(tpath))
-        per_cell = tj.get(dom, {}).get("dram_bytes_per_cell")
-        if per_cell is not None:
-            traffic = per_cell * B * L * L
+        traffic = json.load(open(tpath)).get(cfg.name, {}).get(dom, {}).get("dram_bytes_per_launch")
     d = kernels[dom]
     roofline = {"kernel": dom, "bound": d["bound"], "achieved": d["achieved"],
                 "peak": tflops if d["bound"] == "tensor" else hbm,

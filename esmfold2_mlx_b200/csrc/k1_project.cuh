@@ -11,14 +11,14 @@
 // by 1/256 (mlx_trunk.py:47-48) lives in the packed weights.
 //
 // One tile = 128 pair positions, an ih x jw block of the L x L grid (ih * jw = 128), chosen by
-// the host to minimise padding at ragged L.  CTA = 14 warps, one per SM, persistent:
+// the host to minimise padding at ragged L.  CTA = 18 warps, one per SM, persistent:
 //   warp 0      TMA: packed weights once (resident, 4c x c_z fp16), then z tiles (2 stages)
 //   warp 1      TMEM allocation (512 columns = 4 slots of 128) and the single MMA thread:
 //               per tile, NCH chunks of N = 128 columns ([signal 64 | gate 64] of one 64-channel
 //               block of a or b), K = c_z, each chunk into the next TMEM slot
 //   warps 2-5   LayerNorm of the z tile in shared memory, in place (thread = position)
-//   warps 6-13  epilogue, two groups of four warps (one per TMEM lane quadrant); group g takes
-//               the chunks with (chunk index % 2 == g), so two chunks drain at once.  Each warp
+//   warps 6-17  epilogue, three groups of four warps (one per TMEM lane quadrant); group g takes
+//               the chunks with (chunk index % 3 == g), so three chunks drain at once.  Each warp
 //               owns 32 positions: gate, mask, fp16, then a 16-channel x 32-position block is
 //               staged in shared memory and stored with its own TMA store (no CTA-wide barrier).
 #pragma once
@@ -43,10 +43,11 @@ constexpr int WSTG_BYTES = SUB * 32 * 2;     // one warp's staging buffer (16 ch
 constexpr int OFF_W = 0;
 constexpr int OFF_A = OFF_W + NCH * WCHUNK_BYTES;
 constexpr int OFF_STG = OFF_A + NSTAGE * A_BYTES;
-constexpr int OFF_PAR = OFF_STG + 8 * 2 * WSTG_BYTES;  // fp32 LN gamma, beta, bias
+constexpr int NEPI = 12;                                 // epilogue warps (3 groups of 4)
+constexpr int OFF_PAR = OFF_STG + NEPI * 2 * WSTG_BYTES;  // fp32 LN gamma, beta, bias
 constexpr int PAR_FLOATS = 2 * CZ + 4 * CC;
 constexpr int SMEM_BYTES = OFF_PAR + PAR_FLOATS * 4 + 1024;
-constexpr int kThreads = 448;
+constexpr int kThreads = 576;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
@@ -59,6 +60,7 @@ struct Params {
   const float* bias;   // [4c] in packed-row order, or null
   const __half* mask;  // [B, L, L] or null
   int L, ih, jw, tiles_i, tiles_j, num_tiles;
+  int reset_status;  // block 0 zeroes the status word (after the dependency wait)
   DeviceStatus* status;
   unsigned long long timeout_ns;
 };
@@ -76,6 +78,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
+template <bool HAS_BIAS, bool HAS_MASK>
 __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_constant__ Params p) {
   constexpr uint32_t IDESC = idesc_f16_f32(128, 128, false, false);
   extern __shared__ uint8_t smem_raw[];
@@ -96,7 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&zfull[s], 1);
       mbar_init(&zempty[s], 1);
-      mbar_init(&lnfull[s], 128);
+      mbar_init(&lnfull[s], 4);  // one arrival per LayerNorm warp
     }
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(&tfull[s], 1);
@@ -105,11 +108,14 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
   }
+  // Prologue (overlaps the previous kernel when launched with programmatic serialisation):
+  // weights and parameters are never written by the kernels of this library, so they are
+  // fetched before the dependency wait; z, mask, a, b and the status word only after it.
   for (int i = threadIdx.x; i < PAR_FLOATS; i += blockDim.x) {
     float v;
     if (i < CZ) v = __half2float(p.ln_w[i]);
     else if (i < 2 * CZ) v = __half2float(p.ln_b[i - CZ]);
-    else v = p.bias ? p.bias[i - 2 * CZ] : 0.0f;
+    else v = HAS_BIAS ? p.bias[i - 2 * CZ] : 0.0f;
     par[i] = v;
   }
   if (warp == 0 && lane == 0) {
@@ -126,14 +132,23 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  if (warp == 0 && lane == 0) {
+    mbar_arrive_expect_tx(&w_bar, NCH * WCHUNK_BYTES);
+    for (int q = 0; q < NCH; ++q)
+      for (int a = 0; a < KATOMS; ++a)
+        tma_load_2d(smem + OFF_W + q * WCHUNK_BYTES + a * ATOM_BYTES, &p.tm_w, &w_bar, a * 64, q * 128);
+  }
+  griddep_trigger();
+  griddep_wait();
+  if (p.reset_status && blockIdx.x == 0 && threadIdx.x == 0) {
+    p.status->code = 0;
+    p.status->site = 0;
+    p.status->block = 0;
+  }
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      mbar_arrive_expect_tx(&w_bar, NCH * WCHUNK_BYTES);
-      for (int q = 0; q < NCH; ++q)
-        for (int a = 0; a < KATOMS; ++a)
-          tma_load_2d(smem + OFF_W + q * WCHUNK_BYTES + a * ATOM_BYTES, &p.tm_w, &w_bar, a * 64, q * 128);
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         int bb, i0, j0;
@@ -186,21 +201,23 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
-      if (!mbar_wait(&zfull[s], ph, ctx, kSiteLn)) break;
+      if (!warp_wait(&zfull[s], ph, ctx, kSiteLn)) break;
       uint8_t* A = smem + OFF_A + s * A_BYTES;
       ln_row128_sw128(A, A, ATOM_BYTES, row, 1e-5f, LnParSmem{par, par + CZ});
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
-      mbar_arrive(&lnfull[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&lnfull[s]);
     }
   } else {
     // ---------------- epilogue: gate, mask, channel-major store ----------------
-    const int ew = warp - 6;         // 0..7
+    const int ew = warp - 6;         // 0..11
     const int q = warp & 3;          // TMEM lane quadrant
-    const int grp = ew >> 2;         // chunk parity this warp drains
+    const int grp = ew >> 2;         // this warp drains the chunks with index % 3 == grp
     const int row = q * 32 + lane;   // position within the tile
     const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
     __half* stg = reinterpret_cast<__half*>(smem + OFF_STG + ew * 2 * WSTG_BYTES);
-    const bool has_bias = p.bias != nullptr;
+    constexpr bool has_bias = HAS_BIAS;
+    constexpr bool has_mask = HAS_MASK;
     const float* bias = par + 2 * CZ;
     uint32_t cit = 0, sit = 0;
     bool ok = true;
@@ -209,11 +226,11 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
       decode_tile(p, tile, bb, i0, j0);
       const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
       float mval = 1.0f;
-      if (p.mask != nullptr && gi < p.L && gj < p.L)
+      if (HAS_MASK && gi < p.L && gj < p.L)
         mval = __half2float(p.mask[(static_cast<size_t>(bb) * p.L + gi) * p.L + gj]);
       const float2 m2 = make_float2(mval, mval);
       for (int qc = 0; qc < NCH; ++qc, ++cit) {
-        if ((cit & 1) != static_cast<uint32_t>(grp)) continue;
+        if (cit % 3 != static_cast<uint32_t>(grp)) continue;
         const uint32_t slot = cit % NSLOT, sph = (cit / NSLOT) & 1;
         if (!warp_wait(&tfull[slot], sph, ctx, kSiteEpilogue)) { ok = false; break; }
         tc_fence_after();
@@ -246,7 +263,8 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
             }
             s = round_f16x2(s);  // proj is an fp16 tensor in the reference
             g = round_f16x2(g);
-            const float2 y = __fmul2_rn(__fmul2_rn(s, sigmoid_f32x2(g)), m2);
+            float2 y = __fmul2_rn(s, sigmoid_f32x2(g));
+            if (has_mask) y = __fmul2_rn(y, m2);
             st[i * 32 + lane] = __float2half_rn(y.x);
             st[(i + 1) * 32 + lane] = __float2half_rn(y.y);
           }

@@ -93,6 +93,8 @@ __global__ void __launch_bounds__(kThreads, 1) contract_kernel(const __grid_cons
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
   const int tiles_per_d = p.tiles_m * p.tiles_n;
+  griddep_trigger();
+  griddep_wait();  // a, b come from the previous kernel; x may still be read by it
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------

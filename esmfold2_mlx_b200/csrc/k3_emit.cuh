@@ -12,13 +12,14 @@
 // The LayerNorm that the reference fuses after the residual (resgate_ln's second output) is
 // the next kernel's prologue (K1 of the next tri-mul normalises the z' it loads).
 //
-// One tile = 128 positions (ih x jw block).  CTA = 14 warps, one per SM, persistent:
-//   warp 0     TMA: w_emit and w_gate once (resident), then per tile the z tile (2 stages,
-//              128B swizzle, position-major) and the x tile (channel-major, unswizzled)
+// One tile = 128 positions (ih x jw block).  CTA = 18 warps, one per SM, persistent:
+//   warp 0     TMA: w_emit and w_gate once (resident), then per tile the z tile and the x tile
+//              (2 stages each; z 128B-swizzled position-major, x channel-major unswizzled)
 //   warp 1     TMEM (2 x 256 columns) + MMA thread: emit (A1 x W_e) and gate (A2 x W_g)
-//   warps 2-5  transforms: A1 = fp16(LN_mix(x column)), A2 = fp16(LN_in(z row)), both written
-//              as K-major 128B-swizzled UMMA operands
-//   warps 6-13 epilogue, two groups of four warps (one per TMEM lane quadrant); group h owns
+//   warps 2-5  A1 = fp16(LN_mix(x column)), written over the x tile it was gathered from once all
+//              four warps hold their columns in registers; warps 6-9  A2 = fp16(LN_in(z row));
+//              both concurrently, both K-major 128B-swizzled UMMA operands
+//   warps 10-17 epilogue, two groups of four warps (one per TMEM lane quadrant); group h owns
 //              output channels [64h, 64h+64): TMEM -> gate/residual in fp32 -> z' written over
 //              the z tile -> each warp TMA-stores its own 32 positions x 64 channels
 #pragma once
@@ -36,11 +37,10 @@ constexpr int TILE_BYTES = TILE * 128 * 2;  // 128 positions x 128 channels fp16
 constexpr int OFF_WE = 0;
 constexpr int OFF_WG = OFF_WE + CZ * CC * 2;
 constexpr int OFF_Z = OFF_WG + CZ * CZ * 2;
-constexpr int OFF_X = OFF_Z + 2 * TILE_BYTES;
-constexpr int OFF_A1 = OFF_X + TILE * CC * 2;
-constexpr int OFF_A2 = OFF_A1 + TILE_BYTES;
+constexpr int OFF_X = OFF_Z + 2 * TILE_BYTES;  // 2 stages; stage s holds the x tile, then A1 in place
+constexpr int OFF_A2 = OFF_X + 2 * TILE_BYTES;
 constexpr int SMEM_BYTES = OFF_A2 + TILE_BYTES + 1024;
-constexpr int kThreads = 448;
+constexpr int kThreads = 576;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
@@ -74,13 +74,15 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
+template <bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid_constant__ Params p) {
   constexpr uint32_t IDESC = idesc_f16_f32(128, CZ, false, false);
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t w_bar, zfull[2], zempty[2], xfull, xempty, afull, aempty;
+  __shared__ __align__(8) uint64_t w_bar, zfull[2], zempty[2], xfull[2], xempty[2], afull, a2empty;
   __shared__ __align__(8) uint64_t tfull[2], tempty[2], drain_bar;
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_sh;
+  __shared__ volatile int x_ok_sh;
 
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   const int warp = threadIdx.x >> 5;
@@ -96,10 +98,12 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       mbar_init(&tfull[s], 1);
       mbar_init(&tempty[s], 8);   // one arrival per epilogue warp
     }
-    mbar_init(&xfull, 1);
-    mbar_init(&xempty, 128);
-    mbar_init(&afull, 128);
-    mbar_init(&aempty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);  // committed by the MMA that read A1 from this stage
+    }
+    mbar_init(&afull, 8);  // one arrival per LN_mix / LN_in warp
+    mbar_init(&a2empty, 1);
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
   }
@@ -118,13 +122,18 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  // weights are never written by this library's kernels: fetch them before the dependency wait
+  if (warp == 0 && lane == 0) {
+    mbar_arrive_expect_tx(&w_bar, (CZ * CC + CZ * CZ) * 2);
+    for (int a = 0; a < CC / 64; ++a) tma_load_2d(smem + OFF_WE + a * ATOM_BYTES, &p.tm_we, &w_bar, a * 64, 0);
+    for (int a = 0; a < CZ / 64; ++a) tma_load_2d(smem + OFF_WG + a * ATOM_BYTES, &p.tm_wg, &w_bar, a * 64, 0);
+  }
+  griddep_trigger();
+  griddep_wait();  // x, z come from previous kernels; z_out may alias what they read
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      mbar_arrive_expect_tx(&w_bar, (CZ * CC + CZ * CZ) * 2);
-      for (int a = 0; a < CC / 64; ++a) tma_load_2d(smem + OFF_WE + a * ATOM_BYTES, &p.tm_we, &w_bar, a * 64, 0);
-      for (int a = 0; a < CZ / 64; ++a) tma_load_2d(smem + OFF_WG + a * ATOM_BYTES, &p.tm_wg, &w_bar, a * 64, 0);
       uint32_t it = 0, nz = 0, nx = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         int bb, i0, j0;
@@ -135,18 +144,19 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
         for (int a = 0; a < CZ / 64; ++a)
           tma_load_4d(smem + OFF_Z + s * TILE_BYTES + a * ATOM_BYTES, &p.tm_z, &zfull[s], a * 64, j0, i0, bb);
         ++nz;
-        if (!mbar_wait(&xempty, (it & 1) ^ 1, ctx, kSiteProdX)) break;
-        mbar_arrive_expect_tx(&xfull, TILE * CC * 2);
-        tma_load_3d(smem + OFF_X, &p.tm_x, &xfull, j0, i0, bb * CC);
+        if (!mbar_wait(&xempty[s], ph ^ 1, ctx, kSiteProdX)) break;
+        mbar_arrive_expect_tx(&xfull[s], TILE * CC * 2);
+        tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
         ++nx;
       }
       if (abort_sh) {
         mbar_drain(&w_bar, 0, 200000000ull);
         for (uint32_t s = 0; s < 2; ++s) {
-          const uint32_t n_armed = nz > s ? (nz - s + 1) / 2 : 0;
-          if (n_armed) mbar_drain(&zfull[s], (n_armed - 1) & 1, 200000000ull);
+          const uint32_t nza = nz > s ? (nz - s + 1) / 2 : 0;
+          if (nza) mbar_drain(&zfull[s], (nza - 1) & 1, 200000000ull);
+          const uint32_t nxa = nx > s ? (nx - s + 1) / 2 : 0;
+          if (nxa) mbar_drain(&xfull[s], (nxa - 1) & 1, 200000000ull);
         }
-        if (nx) mbar_drain(&xfull, (nx - 1) & 1, 200000000ull);
       }
     }
   } else if (warp == 1) {
@@ -154,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     if (lane == 0) {
       bool ok = mbar_wait(&w_bar, 0, ctx, kSiteMmaW);
       uint32_t it = 0;
-      const uint32_t a1 = smem_u32(smem + OFF_A1), a2 = smem_u32(smem + OFF_A2);
+      const uint32_t a2 = smem_u32(smem + OFF_A2);
       const uint32_t we = smem_u32(smem + OFF_WE), wg = smem_u32(smem + OFF_WG);
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t acc = it & 1, aph = (it >> 1) & 1;
@@ -162,6 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
         if (!mbar_wait(&tempty[acc], aph ^ 1, ctx, kSiteMmaT)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * 256;
+        const uint32_t a1 = smem_u32(smem + OFF_X + (it & 1) * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < CC / 16; ++kk) {
           const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
@@ -173,53 +184,71 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
           umma_f16(d + CZ, sdesc_sw128(a2 + off, 16, 1024), sdesc_sw128(wg + off, 16, 1024), IDESC,
                    kk > 0 ? 1u : 0u);
         }
-        umma_commit(&aempty);
+        umma_commit(&xempty[it & 1]);  // A1 (over the x tile) and A2 have been read
+        umma_commit(&a2empty);
         umma_commit(&tfull[acc]);
       }
       umma_commit(&drain_bar);
       mbar_drain(&drain_bar, 0, 200000000ull);
     }
   } else if (warp < 6) {
-    // ---------------- operand transforms ----------------
+    // ---------------- A1 = LN_mix of each position's x column ----------------
     const int row = threadIdx.x - 64;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
-      if (!mbar_wait(&aempty, (it & 1) ^ 1, ctx, kSiteTrA)) break;
-      if (!mbar_wait(&xfull, it & 1, ctx, kSiteTrX)) break;
-      {
-        // x tile is [channel][position]: gather this position's column into row `row` of A1
-        // (raw fp16), release the x buffer, then normalise the row in place.
-        const __half* X = reinterpret_cast<const __half*>(smem + OFF_X);
-        uint8_t* A1 = smem + OFF_A1;
-#pragma unroll 4
-        for (int c16 = 0; c16 < 16; ++c16) {
-          uint32_t u[4];
+      // one thread waits (bounded) and shares the verdict, so the four warps always meet at
+      // the named barriers below together
+      if (row == 0) x_ok_sh = mbar_wait(&xfull[s], ph, ctx, kSiteTrX) ? 1 : 0;
+      named_bar_sync(1, 128);
+      if (!x_ok_sh) break;
+      // The x tile is [channel][position] (256 B per channel).  A1's 64-channel atom h occupies
+      // exactly the bytes of x channels [64h, 64h+64), so each half of this position's column
+      // is gathered into registers, the 128 threads meet, and the half is written back as row
+      // `row` of atom h of the K-major swizzled A1 operand; then the row is normalised in place.
+      const __half* X = reinterpret_cast<const __half*>(smem + OFF_X + s * TILE_BYTES);
+      uint8_t* A1 = smem + OFF_X + s * TILE_BYTES;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t u[32];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int ch = c16 * 8 + e * 2;
-            __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
-            u[e] = *reinterpret_cast<uint32_t*>(&h2);
-          }
-          *reinterpret_cast<uint4*>(A1 + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7)) =
-              make_uint4(u[0], u[1], u[2], u[3]);
+        for (int k = 0; k < 32; ++k) {
+          const int ch = 64 * h + 2 * k;
+          __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
+          u[k] = *reinterpret_cast<uint32_t*>(&h2);
         }
-        mbar_arrive(&xempty);
-        ln_row128_sw128(A1, A1, ATOM_BYTES, row, p.mix_eps, LnParHalf{p.ln_mix_w, p.ln_mix_b});
+        named_bar_sync(1, 128);  // these 64 channels are in registers everywhere: overwrite them
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16)
+          *reinterpret_cast<uint4*>(A1 + h * ATOM_BYTES + sw128_off(row, c16)) =
+              make_uint4(u[4 * c16], u[4 * c16 + 1], u[4 * c16 + 2], u[4 * c16 + 3]);
       }
-      if (!mbar_wait(&zfull[s], ph, ctx, kSiteTrZ)) break;
+      ln_row128_sw128(A1, A1, ATOM_BYTES, row, p.mix_eps, LnParHalf{p.ln_mix_w, p.ln_mix_b});
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull);
+    }
+  } else if (warp < 10) {
+    // ---------------- A2 = LN_in of each position's z row ----------------
+    const int row = threadIdx.x - 192;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+      const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      if (!warp_wait(&a2empty, (it & 1) ^ 1, ctx, kSiteTrA)) break;
+      if (!warp_wait(&zfull[s], ph, ctx, kSiteTrZ)) break;
       ln_row128_sw128(smem + OFF_Z + s * TILE_BYTES, smem + OFF_A2, ATOM_BYTES, row, 1e-5f,
                       LnParHalf{p.ln_in_w, p.ln_in_b});
       fence_proxy_async_smem();
-      mbar_arrive(&afull);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull);
     }
   } else {
     // ---------------- epilogue ----------------
     const int q = warp & 3;          // TMEM lane quadrant
-    const int h = (warp - 6) >> 2;   // output channels [64h, 64h+64)
+    const int h = (warp - 10) >> 2;  // output channels [64h, 64h+64)
     const int row = q * 32 + lane;
     const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
-    const bool has_be = p.b_emit != nullptr, has_bg = p.b_gate != nullptr;
+    constexpr bool has_be = HAS_BIAS, has_bg = HAS_BIAS;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;

@@ -139,10 +139,32 @@ int check_weights(const tmu_trimul_weights* w, bool k1, bool k3) {
   return TMU_OK;
 }
 
+// Launch with programmatic stream serialisation: the kernel may begin (prologue: barriers,
+// TMEM, weight loads) while the previous kernel in the stream drains; each kernel waits with
+// griddepcontrol.wait before touching data another kernel produces or consumes.
+template <typename P>
+cudaError_t launch_pdl(void (*kern)(P), int grid, int block, int smem, cudaStream_t stream, const P& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
 int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int B, int L, void* a, void* b,
-              DeviceStatus* status, cudaStream_t stream) {
+              DeviceStatus* status, cudaStream_t stream, bool reset_status = false) {
+  const bool hb = w->b_proj != nullptr, hm = mask != nullptr;
+  void (*kern)(k1::Params) = hb ? (hm ? k1::project_gate_kernel<true, true> : k1::project_gate_kernel<true, false>)
+                                : (hm ? k1::project_gate_kernel<false, true> : k1::project_gate_kernel<false, false>);
   Dev dev;
-  int st = current_device(dev, 1u << 0, reinterpret_cast<const void*>(&k1::project_gate_kernel), k1::SMEM_BYTES);
+  int st = current_device(dev, 1u << (8 + (hb ? 2 : 0) + (hm ? 1 : 0)), reinterpret_cast<const void*>(kern),
+                          k1::SMEM_BYTES);
   if (st) return st;
   k1::Params p;
   memset(&p, 0, sizeof(p));
@@ -179,11 +201,12 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int 
   p.tiles_i = (L + ih - 1) / ih;
   p.tiles_j = (L + jw - 1) / jw;
   p.num_tiles = B * p.tiles_i * p.tiles_j;
+  p.reset_status = reset_status ? 1 : 0;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
   const int grid = std::min(p.num_tiles, dev.sms);
-  k1::project_gate_kernel<<<grid, k1::kThreads, k1::SMEM_BYTES, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, grid, k1::kThreads, k1::SMEM_BYTES, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch project_gate_kernel");
 }
 
@@ -222,8 +245,8 @@ int launch_k2_t(const void* a, const void* b, void* x, int Bc, int L, DeviceStat
   p.status = status;
   p.timeout_ns = g_timeout_ns;
   const int grid = std::min(p.num_tiles, dev.sms);
-  kern<<<grid, k2::kThreads, C::SMEM_BYTES, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, grid, k2::kThreads, C::SMEM_BYTES, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch contract_kernel");
 }
 
@@ -239,8 +262,13 @@ int launch_k2(const void* a, const void* b, void* x, int Bc, int L, bool outgoin
 
 int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int L, float mix_eps,
               DeviceStatus* status, cudaStream_t stream) {
+  // the emit and gate biases come together (both present, or neither: the reference's form)
+  if ((w->b_emit == nullptr) != (w->b_gate == nullptr))
+    return fail(TMU_ERR_INVALID_ARGUMENT, "b_emit and b_gate must both be set or both be NULL");
+  const bool hb = w->b_emit != nullptr;
+  void (*kern)(k3::Params) = hb ? k3::emit_residual_kernel<true> : k3::emit_residual_kernel<false>;
   Dev dev;
-  int st = current_device(dev, 1u << 5, reinterpret_cast<const void*>(&k3::emit_residual_kernel), k3::SMEM_BYTES);
+  int st = current_device(dev, 1u << (12 + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern), k3::SMEM_BYTES);
   if (st) return st;
   k3::Params p;
   memset(&p, 0, sizeof(p));
@@ -285,8 +313,8 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   p.status = status;
   p.timeout_ns = g_timeout_ns;
   const int grid = std::min(p.num_tiles, dev.sms);
-  k3::emit_residual_kernel<<<grid, k3::kThreads, k3::SMEM_BYTES, stream>>>(p);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, grid, k3::kThreads, k3::SMEM_BYTES, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_kernel");
 }
 
@@ -471,8 +499,9 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
   void* a = ws + TMU_STATUS_BYTES;
   void* b = ws + TMU_STATUS_BYTES + cm;
   void* x = ws + TMU_STATUS_BYTES + 2 * cm;
-  if ((st = tmu_reset_status(status, stream))) return st;
-  if ((st = launch_k1(z, mask, w, B, L, a, b, status, s))) return st;
+  // K1 zeroes the status word after its dependency wait (no memset node between the kernels,
+  // so the three launches chain with programmatic dependent launch)
+  if ((st = launch_k1(z, mask, w, B, L, a, b, status, s, true))) return st;
   if ((st = launch_k2(a, b, x, B * c, L, outgoing != 0, status, s))) return st;
   return launch_k3(x, z, z_out, w, B, L, mix_eps, status, s);
 }

@@ -112,6 +112,14 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint6
   }
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic-serialisation
+// attribute may start while the previous kernel in the stream is still running; it must execute
+// griddep_wait() before it touches anything that kernel writes or reads.  griddep_trigger() lets
+// the next kernel start launching (its own griddep_wait still waits for this grid to finish).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void griddep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
@@ -367,39 +375,38 @@ __device__ __forceinline__ float2 unpack_half2(uint32_t v) {
 
 // ------------------------------------------------------------------------------------------
 // LayerNorm of one 128-channel fp16 row held in a K-major 128B-swizzled tile (two 64-channel
-// atoms `atom_bytes` apart): fp32 statistics, two-pass (mean, then centred variance, as the
-// reference's Metal kernels), y = (x - mean) * rstd * gamma + beta rounded once to fp16 and
-// written to the same row of `dst` (which may be `src`).  Each pass re-reads shared memory so
-// the row is never held in registers.  `par(k, g, b)` returns gamma/beta for channels 8k..8k+7.
+// atoms `atom_bytes` apart): fp32 statistics, y = (x - mean) * rstd * gamma + beta rounded once
+// to fp16 and written to the same row of `dst` (which may be `src`).
+// Statistics take one pass over the row as sums of (x - k) and (x - k)^2 around k = the row's
+// first value (shifted data keeps the cancellation in E[d^2] - E[d]^2 to O(eps * ((mean - k)/std)^2)
+// of fp32); the normalising pass re-reads shared memory, so the row is never held in registers.
+// `par(k, g, b)` returns gamma/beta for channels 8k..8k+7.
 // ------------------------------------------------------------------------------------------
 template <typename Par>
 __device__ __forceinline__ void ln_row128_sw128(const uint8_t* src, uint8_t* dst, int atom_bytes, int row, float eps,
                                                 Par par) {
-  float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-  for (int c16 = 0; c16 < 16; ++c16) {
-    const uint4 v = *reinterpret_cast<const uint4*>(src + (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7));
-    acc = __fadd2_rn(acc, __fadd2_rn(__fadd2_rn(unpack_half2(v.x), unpack_half2(v.y)),
-                                     __fadd2_rn(unpack_half2(v.z), unpack_half2(v.w))));
-  }
-  const float mean = (acc.x + acc.y) * (1.0f / 128);
-  const float2 m2 = make_float2(-mean, -mean);
-  asm volatile("" ::: "memory");
-  float2 sq = make_float2(0.f, 0.f);
+  const float k = __half2float(*reinterpret_cast<const __half*>(src + sw128_off(row, 0)));
+  const float2 nk = make_float2(-k, -k);
+  float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c16 = 0; c16 < 16; ++c16) {
     const uint4 v = *reinterpret_cast<const uint4*>(src + (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7));
     const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float2 d = __fadd2_rn(unpack_half2(u[e]), m2);
-      sq = __ffma2_rn(d, d, sq);
+      const float2 d = __fadd2_rn(unpack_half2(u[e]), nk);
+      s1 = __fadd2_rn(s1, d);
+      s2 = __ffma2_rn(d, d, s2);
     }
   }
-  const float rstd = rsqrtf((sq.x + sq.y) * (1.0f / 128) + eps);
+  const float m1 = (s1.x + s1.y) * (1.0f / 128);
+  const float var = fmaxf((s2.x + s2.y) * (1.0f / 128) - m1 * m1, 0.0f);
+  const float mean = k + m1;
+  const float rstd = rsqrtf(var + eps);
+  const float2 m2 = make_float2(-mean, -mean);
   const float2 r2 = make_float2(rstd, rstd);
   asm volatile("" ::: "memory");
-#pragma unroll 4
+#pragma unroll
   for (int c16 = 0; c16 < 16; ++c16) {
     const int off = (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7);
     const uint4 v = *reinterpret_cast<const uint4*>(src + off);

@@ -50,7 +50,8 @@ extern "C" {
 
 /* Weights of one triangle update, device pointers (mlx_trunk.py:40-55 `_trimul_params`).
  * w_proj rows follow tmu_proj_row_order(); the signal-a rows already carry the fp16 scheme's
- * 1/256 pre-scale (mlx_trunk.py:47-48).  Biases are optional (NULL = the reference's form). */
+ * 1/256 pre-scale (mlx_trunk.py:47-48).  Biases are optional (NULL = the reference's form);
+ * b_emit and b_gate must be both set or both NULL. */
 typedef struct tmu_trimul_weights {
   const void* ln_in_w;  /* [c_z]       norm_start.weight */
   const void* ln_in_b;  /* [c_z]       norm_start.bias */
@@ -109,7 +110,9 @@ int tmu_emit_residual(const void* x, const void* z, void* z_out, const tmu_trimu
                       int c_z, int c, float mix_eps, void* status, void* stream);
 
 /* K1 -> K2 -> K3: z_out = z + tri-mul(z).  `workspace` of tmu_workspace_bytes() bytes, 256-byte
- * aligned; its first TMU_STATUS_BYTES are the status word (zeroed by this call). */
+ * aligned; its first TMU_STATUS_BYTES are the status word (zeroed by this call's first kernel).
+ * The kernels are launched with programmatic dependent launch, so each one's set-up overlaps
+ * the end of the kernel before it. */
 int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z,
                int c, int outgoing, float mix_eps, void* workspace, size_t workspace_bytes, void* stream);
 
