@@ -26,6 +26,7 @@ STATUS_NAMES = {
     6: "TMU_ERR_DEVICE_TIMEOUT",
     7: "TMU_ERR_ARCH",
     8: "TMU_ERR_DRIVER",
+    9: "TMU_ERR_SMEM_LAYOUT",
 }
 
 # Every symbol include/tmu.h declares, with its ctypes signature.

@@ -39,7 +39,9 @@ constexpr int OFF_WG = OFF_WE + CZ * CC * 2;
 constexpr int OFF_Z = OFF_WG + CZ * CZ * 2;
 constexpr int OFF_X = OFF_Z + 2 * TILE_BYTES;  // 2 stages; stage s holds the x tile, then A1 in place
 constexpr int OFF_A2 = OFF_X + 2 * TILE_BYTES;
-constexpr int SMEM_BYTES = OFF_A2 + TILE_BYTES + 1024;
+constexpr int OFF_PAR = OFF_A2 + TILE_BYTES;     // fp32 LN params: in gamma, in beta, mix gamma, mix beta
+constexpr int OFF_BAR = OFF_PAR + 4 * 128 * 4;   // mbarriers and flags
+constexpr int SMEM_BYTES = OFF_BAR + 256;        // no alignment slack: the kernel checks the base instead
 constexpr int kThreads = 576;
 constexpr int TMEM_COLS = 512;
 
@@ -77,14 +79,28 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 template <bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid_constant__ Params p) {
   constexpr uint32_t IDESC = idesc_f16_f32(128, CZ, false, false);
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t w_bar, zfull[2], zempty[2], xfull[2], xempty[2], afull, a2empty;
-  __shared__ __align__(8) uint64_t tfull[2], tempty[2], drain_bar;
-  __shared__ uint32_t tmem_base_sh;
-  __shared__ volatile int abort_sh;
-  __shared__ volatile int x_ok_sh;
-
-  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  // All shared state lives in the dynamic buffer (no static __shared__), whose base the 128B
+  // swizzle needs 1024-byte aligned; a misaligned base is reported, never computed on.
+  extern __shared__ uint8_t smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x3ff;
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t& w_bar = bars[0];
+  uint64_t* zfull = bars + 1;
+  uint64_t* zempty = bars + 3;
+  uint64_t* xfull = bars + 5;
+  uint64_t* xempty = bars + 7;
+  uint64_t& afull = bars[9];
+  uint64_t& a2empty = bars[10];
+  uint64_t* tfull = bars + 11;
+  uint64_t* tempty = bars + 13;
+  uint64_t& drain_bar = bars[15];
+  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 16) + 4);
+  volatile int& x_ok_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 16) + 8);
+  float* par = reinterpret_cast<float*>(smem + OFF_PAR);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtx ctx{p.status, &abort_sh, p.timeout_ns};
@@ -113,6 +129,10 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     tma_prefetch_desc(&p.tm_x);
     tma_prefetch_desc(&p.tm_we);
     tma_prefetch_desc(&p.tm_wg);
+  }
+  for (int i = threadIdx.x; i < 4 * 128; i += blockDim.x) {
+    const __half* src = i < 128 ? p.ln_in_w : i < 256 ? p.ln_in_b : i < 384 ? p.ln_mix_w : p.ln_mix_b;
+    par[i] = __half2float(src[i & 127]);
   }
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, TMEM_COLS);
@@ -223,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
           *reinterpret_cast<uint4*>(A1 + h * ATOM_BYTES + sw128_off(row, c16)) =
               make_uint4(u[4 * c16], u[4 * c16 + 1], u[4 * c16 + 2], u[4 * c16 + 3]);
       }
-      ln_row128_sw128(A1, A1, ATOM_BYTES, row, p.mix_eps, LnParHalf{p.ln_mix_w, p.ln_mix_b});
+      ln_row128_sw128(A1, A1, ATOM_BYTES, row, p.mix_eps, LnParSmem{par + 256, par + 384});
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull);
@@ -237,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       if (!warp_wait(&a2empty, (it & 1) ^ 1, ctx, kSiteTrA)) break;
       if (!warp_wait(&zfull[s], ph, ctx, kSiteTrZ)) break;
       ln_row128_sw128(smem + OFF_Z + s * TILE_BYTES, smem + OFF_A2, ATOM_BYTES, row, 1e-5f,
-                      LnParHalf{p.ln_in_w, p.ln_in_b});
+                      LnParSmem{par, par + 128});
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull);

@@ -383,6 +383,7 @@ const char* tmu_status_name(int s) {
     case TMU_ERR_DEVICE_TIMEOUT: return "TMU_ERR_DEVICE_TIMEOUT";
     case TMU_ERR_ARCH: return "TMU_ERR_ARCH";
     case TMU_ERR_DRIVER: return "TMU_ERR_DRIVER";
+    case TMU_ERR_SMEM_LAYOUT: return "TMU_ERR_SMEM_LAYOUT";
     default: return "TMU_ERR_UNKNOWN";
   }
 }

@@ -30,6 +30,7 @@ struct DeviceStatus {
 };
 
 constexpr unsigned int kStatusDeviceTimeout = 6;  // TMU_ERR_DEVICE_TIMEOUT in tmu.h
+constexpr unsigned int kStatusLayout = 9;         // TMU_ERR_SMEM_LAYOUT in tmu.h
 
 struct WaitCtx {
   DeviceStatus* status;   // global
@@ -88,6 +89,22 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes
+// or about `hint_ns` pass, instead of re-polling and taking issue slots from working warps.
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 200000;  // 0.2 ms: one timer/abort check per sleep
+
 // Wait until the phase with parity `parity` of `bar` has completed.  Bounded: returns false
 // (after raising the abort) when `ctx.timeout_ns` elapses or another role already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const WaitCtx& ctx,
@@ -95,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
-    if (mbar_test(bar, parity)) return true;
+    if (mbar_test_sleep(bar, parity, kSuspendHintNs)) return true;
     if (*ctx.abort) return false;
     if (globaltimer_ns() - t0 > ctx.timeout_ns) {
       raise_abort(ctx, site);
@@ -107,7 +124,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
 // Bounded wait used while winding down after an abort: never raises, gives up silently.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_test(bar, parity)) {
+  while (!mbar_test_sleep(bar, parity, kSuspendHintNs)) {
     if (globaltimer_ns() - t0 > limit_ns) return;
   }
 }
@@ -360,6 +377,18 @@ __device__ __forceinline__ float2 sigmoid_f32x2(float2 x) {
   return make_float2(rcp_approx(d.x), rcp_approx(d.y));
 }
 
+// cvt(h) + c with one rounding (the fp16 -> fp32 conversion is exact): sm_100's mixed-precision
+// add, which saves the separate conversion instruction.
+__device__ __forceinline__ float add_f16_f32(unsigned short h, float c) {
+  float d;
+  asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(d) : "h"(h), "f"(c));
+  return d;
+}
+
+__device__ __forceinline__ void split_half2(uint32_t u, unsigned short& lo, unsigned short& hi) {
+  asm("mov.b32 {%0, %1}, %2;" : "=h"(lo), "=h"(hi) : "r"(u));
+}
+
 // Round a pair of fp32 values to fp16 and back (the value an fp16 tensor would hold).
 __device__ __forceinline__ float2 round_f16x2(float2 v) { return __half22float2(__floats2half2_rn(v.x, v.y)); }
 
@@ -386,7 +415,6 @@ template <typename Par>
 __device__ __forceinline__ void ln_row128_sw128(const uint8_t* src, uint8_t* dst, int atom_bytes, int row, float eps,
                                                 Par par) {
   const float k = __half2float(*reinterpret_cast<const __half*>(src + sw128_off(row, 0)));
-  const float2 nk = make_float2(-k, -k);
   float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c16 = 0; c16 < 16; ++c16) {
@@ -394,7 +422,9 @@ __device__ __forceinline__ void ln_row128_sw128(const uint8_t* src, uint8_t* dst
     const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float2 d = __fadd2_rn(unpack_half2(u[e]), nk);
+      unsigned short lo, hi;
+      split_half2(u[e], lo, hi);
+      const float2 d = make_float2(add_f16_f32(lo, -k), add_f16_f32(hi, -k));
       s1 = __fadd2_rn(s1, d);
       s2 = __ffma2_rn(d, d, s2);
     }
@@ -403,7 +433,6 @@ __device__ __forceinline__ void ln_row128_sw128(const uint8_t* src, uint8_t* dst
   const float var = fmaxf((s2.x + s2.y) * (1.0f / 128) - m1 * m1, 0.0f);
   const float mean = k + m1;
   const float rstd = rsqrtf(var + eps);
-  const float2 m2 = make_float2(-mean, -mean);
   const float2 r2 = make_float2(rstd, rstd);
   asm volatile("" ::: "memory");
 #pragma unroll
@@ -416,7 +445,9 @@ __device__ __forceinline__ void ln_row128_sw128(const uint8_t* src, uint8_t* dst
     uint32_t o[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float2 d = __fmul2_rn(__fadd2_rn(unpack_half2(u[e]), m2), r2);
+      unsigned short lo, hi;
+      split_half2(u[e], lo, hi);
+      const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
       const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
       o[e] = pack_half2(y.x, y.y);
     }

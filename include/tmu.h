@@ -24,7 +24,8 @@
  *     kernels record a bounded-wait timeout there (read it with tmu_read_status).
  *   - Supported now: c_z == c == 128, 1 <= L <= 8192, B*c <= 65535.  Other sizes return
  *     TMU_ERR_UNSUPPORTED.
- *   - Return value: TMU_OK or a TMU_ERR_* code (never aborts the process).
+ *   - Return value: TMU_OK or a TMU_ERR_* code (never aborts the process).  Device-side
+ *     conditions (TMU_ERR_DEVICE_TIMEOUT, TMU_ERR_SMEM_LAYOUT) land in the status word.
  */
 #ifndef TMU_H_
 #define TMU_H_
@@ -45,6 +46,7 @@ extern "C" {
 #define TMU_ERR_DEVICE_TIMEOUT 6
 #define TMU_ERR_ARCH 7
 #define TMU_ERR_DRIVER 8
+#define TMU_ERR_SMEM_LAYOUT 9 /* device status: a kernel found its shared memory misaligned and did nothing */
 
 #define TMU_STATUS_BYTES 256
 
