@@ -10,17 +10,23 @@
 // a, b stored [B*c, L, Lpad] (channel d, row i, column j).  The fp16 pre-scale of w_in[:, :c]
 // by 1/256 (mlx_trunk.py:47-48) lives in the packed weights.
 //
+// The projection is computed transposed, D = W n^T (M = 128 output channels, N = 64 positions,
+// K = c_z), so TMEM lane = channel and column = position: an epilogue thread owns one channel
+// and reads 16 consecutive positions at a time, which are contiguous in the channel-major
+// output.  The signal and gate rows of the same channels go through two MMAs into the same
+// TMEM lanes (columns [0,64) and [64,128) of a slot), so the gate pairs up in registers.
+//
 // One tile = 128 pair positions, an ih x jw block of the L x L grid (ih * jw = 128), chosen by
-// the host to minimise padding at ragged L.  CTA = 18 warps, one per SM, persistent:
+// the host to minimise padding at ragged L.  CTA = 22 warps, one per SM, persistent:
 //   warp 0      TMA: packed weights once (resident, 4c x c_z fp16), then z tiles (2 stages)
-//   warp 1      TMEM allocation (512 columns = 4 slots of 128) and the single MMA thread:
-//               per tile, NCH chunks of N = 128 columns ([signal 64 | gate 64] of one 64-channel
-//               block of a or b), K = c_z, each chunk into the next TMEM slot
-//   warps 2-5   LayerNorm of the z tile in shared memory, in place (thread = position)
-//   warps 6-17  epilogue, three groups of four warps (one per TMEM lane quadrant); group g takes
-//               the chunks with (chunk index % 3 == g), so three chunks drain at once.  Each warp
-//               owns 32 positions: gate, mask, fp16, then a 16-channel x 32-position block is
-//               staged in shared memory and stored with its own TMA store (no CTA-wide barrier).
+//   warp 1      TMEM allocation (512 columns = 4 slots of 128: {a, b} x {positions 0-63,
+//               64-127}) and the MMA thread, which refills a slot as soon as it is drained
+//   warps 2-5   LayerNorm of the z tile in place (thread = position) + the tile's mask as fp32
+//   warps 6-21  epilogue: four warps (one per TMEM lane quadrant) per slot; per 16 positions:
+//               gate, mask, fp16, 32 B per thread into a 2 KB staging block; every 32 positions
+//               a per-warp TMA store of the 32-channel x 32-position box (64-byte rows when
+//               jw >= 32), staged with the swizzle that keeps a warp's 32 row writes free of
+//               bank conflicts.
 #pragma once
 
 #include "tmu_common.cuh"
@@ -31,35 +37,37 @@ namespace k1 {
 constexpr int CZ = 128;  // c_z
 constexpr int CC = 128;  // c (latent channels)
 constexpr int TILE = 128;
-constexpr int NCH = 4 * CC / 128;       // 128-column chunks per tile
-constexpr int KATOMS = CZ / 64;         // 64-channel swizzle atoms along K
-constexpr int ATOM_BYTES = TILE * 128;  // 128 rows x 128 B
-constexpr int WCHUNK_BYTES = 128 * CZ * 2;
+constexpr int KATOMS = CZ / 64;              // 64-channel swizzle atoms along K
+constexpr int ATOM_BYTES = TILE * 128;       // 128 rows x 128 B
+constexpr int WBLOCK_BYTES = 128 * CZ * 2;   // 128 weight rows
 constexpr int A_BYTES = TILE * CZ * 2;
 constexpr int NSTAGE = 2;
+constexpr int POS = 16;                      // positions per epilogue step (one TMEM load)
+constexpr int SPOS = 32;                     // positions per TMA store (two steps)
+constexpr int WSTG_BYTES = 32 * SPOS * 2;    // one warp's staging block (32 channels x 32 positions)
+constexpr int NEPI = 16;
 constexpr int NSLOT = 4;
-constexpr int SUB = 16;                      // channels per epilogue store
-constexpr int WSTG_BYTES = SUB * 32 * 2;     // one warp's staging buffer (16 ch x 32 positions)
-constexpr int OFF_W = 0;
-constexpr int OFF_A = OFF_W + NCH * WCHUNK_BYTES;
+constexpr int NMASK = 3;                     // mask stages (a tile's mask outlives its z stage)
+constexpr int OFF_W = 0;                     // [sig_a | gate_a | sig_b | gate_b], 128 rows each
+constexpr int OFF_A = OFF_W + 4 * WBLOCK_BYTES;
 constexpr int OFF_STG = OFF_A + NSTAGE * A_BYTES;
-constexpr int NEPI = 12;                                 // epilogue warps (3 groups of 4)
-constexpr int OFF_PAR = OFF_STG + NEPI * 2 * WSTG_BYTES;  // fp32 LN gamma, beta, bias
-constexpr int PAR_FLOATS = 2 * CZ + 4 * CC;
-constexpr int SMEM_BYTES = OFF_PAR + PAR_FLOATS * 4 + 1024;
-constexpr int kThreads = 576;
+constexpr int OFF_PAR = OFF_STG + NEPI * WSTG_BYTES;      // fp32 LN gamma, beta
+constexpr int OFF_MASK = OFF_PAR + 2 * CZ * 4;            // fp32 mask per tile position
+constexpr int OFF_BAR = OFF_MASK + NMASK * TILE * 4;     // mbarriers and flags
+constexpr int SMEM_BYTES = OFF_BAR + 256;                 // no alignment slack: the kernel checks the base
+constexpr int kThreads = 704;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
   CUtensorMap tm_z;  // z [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle
   CUtensorMap tm_w;  // packed proj weights [4c, c_z]: box {64, 128}, 128B swizzle
-  CUtensorMap tm_a;  // a [B*c, L, Lpad]: box {min(jw,32), 32/min(jw,32), 16}, no swizzle (store)
+  CUtensorMap tm_a;  // a [B*c, L, Lpad]: box {min(jw,32), 32/min(jw,32), 32}, swizzle by jw (store)
   CUtensorMap tm_b;  // b, same
   const __half* ln_w;
   const __half* ln_b;
   const float* bias;   // [4c] in packed-row order, or null
   const __half* mask;  // [B, L, L] or null
-  int L, ih, jw, tiles_i, tiles_j, num_tiles;
+  int L, ih, jw, log2_jw, tiles_i, tiles_j, num_tiles;
   int reset_status;  // block 0 zeroes the status word (after the dependency wait)
   DeviceStatus* status;
   unsigned long long timeout_ns;
@@ -80,15 +88,28 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 
 template <bool HAS_BIAS, bool HAS_MASK>
 __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_constant__ Params p) {
-  constexpr uint32_t IDESC = idesc_f16_f32(128, 128, false, false);
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t w_bar, zfull[NSTAGE], zempty[NSTAGE], lnfull[NSTAGE];
-  __shared__ __align__(8) uint64_t tfull[NSLOT], tempty[NSLOT], drain_bar;
-  __shared__ uint32_t tmem_base_sh;
-  __shared__ volatile int abort_sh;
-
-  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  float* par = reinterpret_cast<float*>(smem + OFF_PAR);  // [gamma 128 | beta 128 | bias 512]
+  constexpr uint32_t IDESC = idesc_f16_f32(128, 64, false, false);
+  // All shared state lives in the dynamic buffer (no static __shared__), whose base the 128B
+  // swizzle needs 1024-byte aligned; a misaligned base is reported, never computed on.
+  extern __shared__ uint8_t smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x1ff;
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t& w_bar = bars[0];
+  uint64_t* zfull = bars + 1;
+  uint64_t* zempty = bars + 3;
+  uint64_t* lnfull = bars + 5;
+  uint64_t* tfull = bars + 7;
+  uint64_t* tempty = bars + 11;
+  uint64_t* mfull = bars + 15;
+  uint64_t* mempty = bars + 18;
+  uint64_t& drain_bar = bars[21];
+  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 22);
+  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 22) + 4);
+  float* par = reinterpret_cast<float*>(smem + OFF_PAR);    // [gamma 128 | beta 128]
+  float* maskf = reinterpret_cast<float*>(smem + OFF_MASK);  // [NMASK][128]
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtx ctx{p.status, &abort_sh, p.timeout_ns};
@@ -103,7 +124,11 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     }
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 4);  // one arrival per epilogue warp of the group that owns the slot
+      mbar_init(&tempty[s], 4);  // one arrival per epilogue warp draining the slot
+    }
+    for (int k = 0; k < NMASK; ++k) {
+      mbar_init(&mfull[k], 4);      // LayerNorm warps wrote the tile's mask
+      mbar_init(&mempty[k], NEPI);  // every epilogue warp is done with it
     }
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
@@ -111,13 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   // Prologue (overlaps the previous kernel when launched with programmatic serialisation):
   // weights and parameters are never written by the kernels of this library, so they are
   // fetched before the dependency wait; z, mask, a, b and the status word only after it.
-  for (int i = threadIdx.x; i < PAR_FLOATS; i += blockDim.x) {
-    float v;
-    if (i < CZ) v = __half2float(p.ln_w[i]);
-    else if (i < 2 * CZ) v = __half2float(p.ln_b[i - CZ]);
-    else v = HAS_BIAS ? p.bias[i - 2 * CZ] : 0.0f;
-    par[i] = v;
-  }
+  for (int i = threadIdx.x; i < 2 * CZ; i += blockDim.x) par[i] = __half2float(i < CZ ? p.ln_w[i] : p.ln_b[i - CZ]);
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.tm_z);
     tma_prefetch_desc(&p.tm_w);
@@ -133,10 +152,10 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
   if (warp == 0 && lane == 0) {
-    mbar_arrive_expect_tx(&w_bar, NCH * WCHUNK_BYTES);
-    for (int q = 0; q < NCH; ++q)
+    mbar_arrive_expect_tx(&w_bar, 4 * WBLOCK_BYTES);
+    for (int q = 0; q < 4; ++q)
       for (int a = 0; a < KATOMS; ++a)
-        tma_load_2d(smem + OFF_W + q * WCHUNK_BYTES + a * ATOM_BYTES, &p.tm_w, &w_bar, a * 64, q * 128);
+        tma_load_2d(smem + OFF_W + q * WBLOCK_BYTES + a * ATOM_BYTES, &p.tm_w, &w_bar, a * 64, q * 128);
   }
   griddep_trigger();
   griddep_wait();
@@ -168,39 +187,54 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: D[slot] = W_slot n^T ----------------
     if (lane == 0) {
       bool ok = mbar_wait(&w_bar, 0, ctx, kSiteMmaW);
-      uint32_t it = 0, cit = 0;
+      uint32_t it = 0;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t s = it & 1, ph = (it >> 1) & 1;
         if (!mbar_wait(&lnfull[s], ph, ctx, kSiteMmaLn)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t a_base = smem_u32(smem + OFF_A + s * A_BYTES);
-        for (int q = 0; q < NCH; ++q, ++cit) {
-          const uint32_t slot = cit % NSLOT, sph = (cit / NSLOT) & 1;
-          if (!mbar_wait(&tempty[slot], sph ^ 1, ctx, kSiteMmaSlot)) { ok = false; break; }
+        const uint32_t n_base = smem_u32(smem + OFF_A + s * A_BYTES);
+        for (int slot = 0; slot < NSLOT; ++slot) {  // slot = 2 * (a: 0, b: 1) + position half
+          const int x = slot >> 1, hpos = slot & 1;
+          if (!mbar_wait(&tempty[slot], (it & 1) ^ 1, ctx, kSiteMmaSlot)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t w_base = smem_u32(smem + OFF_W + q * WCHUNK_BYTES);
+          const uint32_t b_base = n_base + hpos * 64 * 128;  // positions [64 hpos, 64 hpos + 64)
+          for (int h = 0; h < 2; ++h) {  // h = 0 signal rows, h = 1 gate rows
+            const uint32_t w_base = smem_u32(smem + OFF_W + (2 * x + h) * WBLOCK_BYTES);
 #pragma unroll
-          for (int kk = 0; kk < CZ / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-            umma_f16(tmem_base + slot * 128, sdesc_sw128(a_base + off, 16, 1024), sdesc_sw128(w_base + off, 16, 1024),
-                     IDESC, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < CZ / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
+              umma_f16(tmem_base + slot * 128 + h * 64, sdesc_sw128(w_base + off, 16, 1024),
+                       sdesc_sw128(b_base + off, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+            }
           }
           umma_commit(&tfull[slot]);
         }
-        umma_commit(&zempty[s]);  // the z/n tile may be refilled once these MMAs have read it
+        if (ok) umma_commit(&zempty[s]);  // the z/n tile may be refilled once these MMAs have read it
       }
       umma_commit(&drain_bar);
       mbar_drain(&drain_bar, 0, 200000000ull);
     }
   } else if (warp < 6) {
-    // ---------------- LayerNorm of the z tile, in place ----------------
+    // ---------------- LayerNorm of the z tile in place; the tile's mask as fp32 ----------------
     const int row = threadIdx.x - 64;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      if (HAS_MASK) {  // stage k of the mask ring holds tiles k, k + NMASK, ...
+        const uint32_t k = it % NMASK, mph = (it / NMASK) & 1;
+        if (!warp_wait(&mempty[k], mph ^ 1, ctx, kSiteLn)) break;
+        int bb, i0, j0;
+        decode_tile(p, tile, bb, i0, j0);
+        const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
+        float m = 0.0f;
+        if (gi < p.L && gj < p.L) m = __half2float(p.mask[(static_cast<size_t>(bb) * p.L + gi) * p.L + gj]);
+        maskf[k * TILE + row] = m;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&mfull[k]);
+      }
       if (!warp_wait(&zfull[s], ph, ctx, kSiteLn)) break;
       uint8_t* A = smem + OFF_A + s * A_BYTES;
       ln_row128_sw128(A, A, ATOM_BYTES, row, 1e-5f, LnParSmem{par, par + CZ});
@@ -210,71 +244,94 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     }
   } else {
     // ---------------- epilogue: gate, mask, channel-major store ----------------
-    const int ew = warp - 6;         // 0..11
-    const int q = warp & 3;          // TMEM lane quadrant
-    const int grp = ew >> 2;         // this warp drains the chunks with index % 3 == grp
-    const int row = q * 32 + lane;   // position within the tile
-    const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
-    __half* stg = reinterpret_cast<__half*>(smem + OFF_STG + ew * 2 * WSTG_BYTES);
-    constexpr bool has_bias = HAS_BIAS;
-    constexpr bool has_mask = HAS_MASK;
-    const float* bias = par + 2 * CZ;
-    uint32_t cit = 0, sit = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+    const int slot = (warp - 6) >> 2;  // 2 * (a: 0, b: 1) + position half
+    const int x = slot >> 1, hpos = slot & 1;
+    const int q = warp & 3;            // TMEM lane quadrant = channels [32q, 32q+32)
+    const int ch = q * 32 + lane;      // this thread's output channel
+    uint8_t* stg = smem + OFF_STG + (warp - 6) * WSTG_BYTES;
+    // Byte offsets in the staging block of this thread's two 16-byte chunks c of compute step
+    // st (positions 16 st + 8 c ..), matching the store box and its swizzle:
+    //   jw >= 32: box {32, 1, 32}, 64 B rows (row = channel), 64B swizzle
+    //   jw == 16: box {16, 2, 32}, 32 B rows (row = 2 channel + st), 32B swizzle
+    //   jw == 8:  box {8, 4, 32},  16 B rows (row = 4 channel + 2 st + c), no swizzle
+    uint32_t soff[2][2];
+#pragma unroll
+    for (int st = 0; st < 2; ++st)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        if (p.jw >= 32) {
+          const uint32_t r = lane, cc = 2 * st + c;
+          soff[st][c] = r * 64 + 16 * (cc ^ ((r >> 1) & 3));
+        } else if (p.jw == 16) {
+          const uint32_t r = 2 * lane + st;
+          soff[st][c] = r * 32 + 16 * (c ^ ((r >> 2) & 1));
+        } else {
+          soff[st][c] = (4 * lane + 2 * st + c) * 16;
+        }
+      }
+    float bs = 0.0f, bg = 0.0f;
+    if (HAS_BIAS) {
+      bs = __ldg(p.bias + (2 * x) * 128 + ch);
+      bg = __ldg(p.bias + (2 * x + 1) * 128 + ch);
+    }
+    const float2 bs2 = make_float2(bs, bs), bg2 = make_float2(bg, bg);
+    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 128;
+    const CUtensorMap* tm = x == 0 ? &p.tm_a : &p.tm_b;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
-      const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
-      float mval = 1.0f;
-      if (HAS_MASK && gi < p.L && gj < p.L)
-        mval = __half2float(p.mask[(static_cast<size_t>(bb) * p.L + gi) * p.L + gj]);
-      const float2 m2 = make_float2(mval, mval);
-      for (int qc = 0; qc < NCH; ++qc, ++cit) {
-        if (cit % 3 != static_cast<uint32_t>(grp)) continue;
-        const uint32_t slot = cit % NSLOT, sph = (cit / NSLOT) & 1;
-        if (!warp_wait(&tfull[slot], sph, ctx, kSiteEpilogue)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 128;
-        const int col0 = qc * 128;  // packed-row index of the chunk's first signal column
-        const bool is_a = qc < NCH / 2;
-        const int ch0 = (qc % (NCH / 2)) * 64;
+      if (!warp_wait(&tfull[slot], it & 1, ctx, kSiteEpilogue)) break;
+      if (HAS_MASK && !warp_wait(&mfull[it % NMASK], (it / NMASK) & 1, ctx, kSiteEpilogue)) break;
+      tc_fence_after();
+      const float* mrow = maskf + (it % NMASK) * TILE + hpos * 64;
 #pragma unroll 1
-        for (int sub = 0; sub < 64 / SUB; ++sub, ++sit) {
-          uint32_t sg[16], gt[16];
-          tmem_ld16(taddr + sub * SUB, sg);
-          tmem_ld16(taddr + 64 + sub * SUB, gt);
-          tmem_wait_ld16x2(sg, gt);
-          if (sub == 64 / SUB - 1) {  // the whole slot has been read: hand it back to the MMA
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[slot]);
-          }
-          __half* st = stg + (sit & 1) * (WSTG_BYTES / 2);
-          if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+      for (int pb = 0; pb < 64; pb += POS) {
+        uint32_t sg[16], gt[16];
+        tmem_ld16(taddr + pb, sg);
+        tmem_ld16(taddr + 64 + pb, gt);
+        tmem_wait_ld16x2(sg, gt);
+        if (pb == 64 - POS) {  // the whole slot has been read: hand it back to the MMA
+          tc_fence_before();
           __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[slot]);
+        }
+        uint32_t o[8];
 #pragma unroll
-          for (int i = 0; i < SUB; i += 2) {
-            float2 s = make_float2(__uint_as_float(sg[i]), __uint_as_float(sg[i + 1]));
-            float2 g = make_float2(__uint_as_float(gt[i]), __uint_as_float(gt[i + 1]));
-            if (has_bias) {
-              const int c = col0 + sub * SUB + i;
-              s = __fadd2_rn(s, make_float2(bias[c], bias[c + 1]));
-              g = __fadd2_rn(g, make_float2(bias[c + 64], bias[c + 65]));
-            }
-            s = round_f16x2(s);  // proj is an fp16 tensor in the reference
-            g = round_f16x2(g);
-            float2 y = __fmul2_rn(s, sigmoid_f32x2(g));
-            if (has_mask) y = __fmul2_rn(y, m2);
-            st[i * 32 + lane] = __float2half_rn(y.x);
-            st[(i + 1) * 32 + lane] = __float2half_rn(y.y);
+        for (int i = 0; i < POS; i += 2) {
+          float2 s = make_float2(__uint_as_float(sg[i]), __uint_as_float(sg[i + 1]));
+          float2 g = make_float2(__uint_as_float(gt[i]), __uint_as_float(gt[i + 1]));
+          if (HAS_BIAS) {
+            s = __fadd2_rn(s, bs2);
+            g = __fadd2_rn(g, bg2);
           }
+          s = round_f16x2(s);  // proj is an fp16 tensor in the reference
+          g = round_f16x2(g);
+          float2 y = __fmul2_rn(s, sigmoid_f32x2(g));
+          if (HAS_MASK) y = __fmul2_rn(y, *reinterpret_cast<const float2*>(mrow + pb + i));
+          o[i / 2] = pack_half2(y.x, y.y);
+        }
+        const int step = (pb / POS) & 1;
+        if (step == 0) {  // first half of a store box: the previous store must have read the block
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+        }
+        const uint32_t off0 = step ? soff[1][0] : soff[0][0], off1 = step ? soff[1][1] : soff[0][1];
+        *reinterpret_cast<uint4*>(stg + off0) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(stg + off1) = make_uint4(o[4], o[5], o[6], o[7]);
+        if (step == 1) {
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(is_a ? &p.tm_a : &p.tm_b, st, j0 + jo, i0 + io, bb * CC + ch0 + sub * SUB);
+            const int tp = hpos * 64 + pb - POS;  // tile position of the first of these 32
+            tma_store_3d(tm, stg, j0 + (tp & (p.jw - 1)), i0 + (tp >> p.log2_jw), bb * CC + q * 32);
             bulk_commit();
           }
         }
+      }
+      if (HAS_MASK) {  // this warp no longer reads the tile's mask
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&mempty[it % NMASK]);
       }
     }
     if (lane == 0) bulk_wait<0>();

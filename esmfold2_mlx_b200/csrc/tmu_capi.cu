@@ -186,10 +186,13 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int 
   {
     const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)B * 128};
     const uint64_t str[2] = {Lp * 2, Lp * 2 * L};
-    const uint32_t jwp = jw < 32 ? jw : 32;  // one epilogue warp's 32 positions
-    const uint32_t box[3] = {jwp, 32 / jwp, (uint32_t)k1::SUB};
-    if ((st = encode_map(&p.tm_a, a, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
-    if ((st = encode_map(&p.tm_b, b, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+    // one epilogue store: 32 positions x 32 channels, staged with the swizzle matching its row width
+    const uint32_t w32 = jw < k1::SPOS ? jw : k1::SPOS;
+    const uint32_t box[3] = {w32, k1::SPOS / w32, 32};
+    const CUtensorMapSwizzle sw = w32 == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : w32 == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    if ((st = encode_map(&p.tm_a, a, 3, dims, str, box, sw))) return st;
+    if ((st = encode_map(&p.tm_b, b, 3, dims, str, box, sw))) return st;
   }
   p.ln_w = static_cast<const __half*>(w->ln_in_w);
   p.ln_b = static_cast<const __half*>(w->ln_in_b);
@@ -198,6 +201,7 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int 
   p.L = L;
   p.ih = ih;
   p.jw = jw;
+  p.log2_jw = 31 - __builtin_clz(static_cast<unsigned>(jw));
   p.tiles_i = (L + ih - 1) / ih;
   p.tiles_j = (L + jw - 1) / jw;
   p.num_tiles = B * p.tiles_i * p.tiles_j;
@@ -409,15 +413,13 @@ int tmu_row_pitch(int L) { return row_pitch(L); }
 
 int tmu_proj_row_order(int c, int* order) {
   if (order == nullptr || c <= 0 || c % 64 != 0) return fail(TMU_ERR_INVALID_ARGUMENT, "c must be a multiple of 64");
-  // chunk q covers 64 channels of a (q < c/64) or b; rows [signal 64 | gate 64]
-  const int per = c / 64;
-  for (int q = 0; q < 2 * per; ++q) {
-    const int which = q < per ? 0 : 1;  // 0 = a, 1 = b
-    const int ch0 = (q % per) * 64;
-    for (int r = 0; r < 64; ++r) {
-      order[q * 128 + r] = which * c + ch0 + r;               // signal rows: [0, c) a, [c, 2c) b
-      order[q * 128 + 64 + r] = 2 * c + which * c + ch0 + r;  // gate rows:   [2c, 3c) a, [3c, 4c) b
-    }
+  // blocks of c rows: [signal a | gate a | signal b | gate b]; proj_bundle rows are
+  // [signal a | signal b | gate a | gate b] (mlx_trunk.py:44)
+  for (int r = 0; r < c; ++r) {
+    order[r] = r;                // signal a
+    order[c + r] = 2 * c + r;    // gate a
+    order[2 * c + r] = c + r;    // signal b
+    order[3 * c + r] = 3 * c + r;  // gate b
   }
   return TMU_OK;
 }

@@ -294,11 +294,14 @@ __device__ __forceinline__ void tmem_wait_ld16x2(uint32_t (&r)[16], uint32_t (&s
                : "memory");
 }
 
-// One thread of a warp waits (bounded) and the whole warp gets its verdict.
+// One thread of a warp waits (bounded) and the whole warp gets its verdict; the __syncwarp
+// orders the other lanes' later reads after lane 0's acquiring wait.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const WaitCtx& ctx, unsigned int site) {
   int ok = 0;
   if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, ctx, site) ? 1 : 0;
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  return ok != 0;
 }
 
 __device__ __forceinline__ void tmem_wait_ld2(uint32_t (&r)[32], uint32_t (&s)[32]) {

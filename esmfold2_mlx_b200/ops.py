@@ -44,15 +44,10 @@ def proj_row_order(c: int) -> list[int]:
 
 
 def proj_row_order_py(c: int) -> list[int]:
-    """The same order computed in Python (no library needed): chunks of 128 packed rows, each
-    64 signal rows then the 64 matching gate rows, channel blocks of a before those of b."""
-    order = []
-    per = c // 64
-    for q in range(2 * per):
-        which, ch0 = (0, q * 64) if q < per else (1, (q - per) * 64)
-        order += [which * c + ch0 + r for r in range(64)]
-        order += [2 * c + which * c + ch0 + r for r in range(64)]
-    return order
+    """The same order computed in Python (no library needed): blocks of c packed rows,
+    [signal a | gate a | signal b | gate b], from proj_bundle's [signal a | signal b | gate a |
+    gate b] (mlx_trunk.py:44)."""
+    return list(range(c)) + list(range(2 * c, 3 * c)) + list(range(c, 2 * c)) + list(range(3 * c, 4 * c))
 
 
 @dataclass

@@ -83,8 +83,7 @@ int tmu_device_check(void);
 int tmu_row_pitch(int L);
 
 /* Packed-row order of proj_bundle.weight: order[r] is the proj_bundle row that becomes packed
- * row r (chunks of 128 rows = 64 signal rows then the 64 matching gate rows, a before b).
- * `order` must hold 4*c ints. */
+ * row r (blocks of c rows: signal a, gate a, signal b, gate b).  `order` must hold 4*c ints. */
 int tmu_proj_row_order(int c, int* order);
 
 /* Bytes of workspace tmu_trimul needs: status word + a + b + x. */
