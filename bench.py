@@ -242,6 +242,54 @@ def _kernel_costs(L: int, B: int, masked: bool):
     }
 
 
+def _trunk_recycle(device, flush, reps: int = 3):
+    """ms per trunk recycle on BASELINE config 3: a 16-block pair stack (tri-mul out, tri-mul in,
+    ReLU transition 128 -> 512 -> 128), L = 384, run for 3 recycles with z fed back; random
+    N(0, 1/fan_in) weights (seed 2), z0 ~ N(0, 1).  The whole 3-recycle forward is one CUDA graph
+    through the public module (CUDAFoldingTrunk); L2 flushed before each timed replay."""
+    from esmfold2_mlx_b200.synthetic import CONFIGS, FoldingTrunk, pair_tensor
+    from esmfold2_mlx_b200.trunk import CUDAFoldingTrunk
+
+    cfg = CONFIGS["c3"]
+    trunk = FoldingTrunk(cfg.blocks, C_Z, C, hidden=512, seed=cfg.seed, activation="relu")
+    mod = CUDAFoldingTrunk(trunk, device=device)
+    z0 = pair_tensor(1, cfg.L, C_Z, cfg.seed).to(device)
+
+    def forward():
+        z = z0
+        for _ in range(cfg.recycles):
+            z = mod(z)
+        return z
+
+    out = forward()  # eager warm-up (first-call host setup, workspace)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = forward()
+    for _ in range(2):
+        flush.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        e1.synchronize()
+        ms.append(e0.elapsed_time(e1))
+    finite = bool(torch.isfinite(out).all())
+    per_recycle = statistics.median(ms) / cfg.recycles
+    L = cfg.L
+    cells = 2 * cfg.blocks * L * L  # tri-mul pair cells per recycle
+    del g
+    return {"workload": cfg.name, "L": L, "blocks": cfg.blocks, "recycles": cfg.recycles,
+            "ms_per_recycle": round(per_recycle, 4), "trimul_pair_cells_per_s": cells / (per_recycle * 1e-3),
+            "roofline_ms_per_recycle": 2.4, "transition": "ReLU 128->512->128, torch on the GPU (cuBLAS)",
+            "output_finite": finite}
+
+
 def run_b200(args, ws, rank, local):
     from esmfold2_mlx_b200 import _lib, ops
 
@@ -394,6 +442,11 @@ def run_b200(args, ws, rank, local):
     e2e = {"value": ws * cells_per_step / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4)}
 
+    # ---------------- trunk recycle, N = 1 only ----------------
+    recycle = None
+    if ws == 1 and not args.no_trunk:
+        recycle = _trunk_recycle(device, flush)
+
     # ---------------- CPU baseline (rank 0, N = 1) ----------------
     cpu = None
     if ws == 1 and not args.no_cpu_baseline and L <= 512:
@@ -411,6 +464,7 @@ def run_b200(args, ws, rank, local):
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": _config_dict(cfg, ws),
             "e2e": e2e, "gpu_launches": 6 * args.steps, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
+            "trunk_recycle": recycle,
         }
         print(json.dumps(line), flush=True)
     del g_step, g_kern
@@ -423,6 +477,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-trunk", action="store_true", help="skip the trunk-recycle (config 3) measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--workload", choices=WORKLOADS, default="c2",
                     help="c2 (default: the metric's configuration), c1, c4 (64 folds x L=146), L2048")

@@ -43,7 +43,19 @@ class TmuTrimulWeights(ctypes.Structure):
     ]
 
 
+class TmuPairLayout(ctypes.Structure):
+    """Mirror of ``tmu_pair_layout``."""
+
+    _fields_ = [
+        ("B", ctypes.c_int), ("rows", ctypes.c_int), ("cols", ctypes.c_int),
+        ("stride_b", ctypes.c_longlong), ("stride_row", ctypes.c_longlong), ("stride_col", ctypes.c_longlong),
+        ("mask_stride_b", ctypes.c_longlong), ("mask_stride_row", ctypes.c_longlong),
+        ("mask_stride_col", ctypes.c_longlong),
+    ]
+
+
 _W = ctypes.POINTER(TmuTrimulWeights)
+_G = ctypes.POINTER(TmuPairLayout)
 SIGNATURES = {
     "tmu_version": (ctypes.c_char_p, []),
     "tmu_status_name": (ctypes.c_char_p, [_i]),
@@ -58,6 +70,9 @@ SIGNATURES = {
     "tmu_project_gate": (_i, [_vp, _vp, _W, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tmu_contract": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "tmu_emit_residual": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _f, _vp, _vp]),
+    "tmu_project_gate_ex": (_i, [_vp, _vp, _G, _W, _i, _i, _vp, _vp, _vp, _vp]),
+    "tmu_contract_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+    "tmu_emit_residual_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _W, _i, _i, _f, _vp, _vp]),
     "tmu_trimul": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp]),
     "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_selftest_wait_timeout": (_i, [_vp, _ull, _vp]),

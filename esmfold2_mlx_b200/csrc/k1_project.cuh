@@ -59,15 +59,16 @@ constexpr int kThreads = 704;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
-  CUtensorMap tm_z;  // z [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle
+  CUtensorMap tm_z;  // z [B, rows, cols, c_z] (any element strides): box {64, jw, ih, 1}, 128B swizzle
   CUtensorMap tm_w;  // packed proj weights [4c, c_z]: box {64, 128}, 128B swizzle
   CUtensorMap tm_a;  // a [B*c, L, Lpad]: box {min(jw,32), 32/min(jw,32), 32}, swizzle by jw (store)
   CUtensorMap tm_b;  // b, same
   const __half* ln_w;
   const __half* ln_b;
   const float* bias;   // [4c] in packed-row order, or null
-  const __half* mask;  // [B, L, L] or null
-  int L, ih, jw, log2_jw, tiles_i, tiles_j, num_tiles;
+  const __half* mask;  // [B, rows, cols] with element strides mask_s*, or null
+  long long mask_sb, mask_si, mask_sj;
+  int rows, cols, ih, jw, log2_jw, tiles_i, tiles_j, num_tiles;
   int reset_status;  // block 0 zeroes the status word (after the dependency wait)
   DeviceStatus* status;
   unsigned long long timeout_ns;
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
         decode_tile(p, tile, bb, i0, j0);
         const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
         float m = 0.0f;
-        if (gi < p.L && gj < p.L) m = __half2float(p.mask[(static_cast<size_t>(bb) * p.L + gi) * p.L + gj]);
+        if (gi < p.rows && gj < p.cols) m = __half2float(p.mask[bb * p.mask_sb + gi * p.mask_si + gj * p.mask_sj]);
         maskf[k * TILE + row] = m;
         __syncwarp();
         if (lane == 0) mbar_arrive(&mfull[k]);

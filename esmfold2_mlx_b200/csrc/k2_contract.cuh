@@ -36,10 +36,12 @@ struct Cfg {
 };
 
 struct Params {
-  CUtensorMap tm_a;  // loads of a: K-major box {64, 128, 1} or MN-major box {64, 64, 1}
-  CUtensorMap tm_b;  // loads of b: K-major box {64, BN, 1}  or MN-major box {64, 64, 1}
-  CUtensorMap tm_x;  // store of x: box {64, 128, 1}, 128B swizzle
-  int L;
+  CUtensorMap tm_a;  // loads of a: K-major {K, M, Bc} box {64, 128, 1}, or MN-major box {64, 64, 1}
+  CUtensorMap tm_b;  // loads of b: K-major {K, rows_per_part, Bc, parts} box {64, BN, 1, 1},
+                     //             or MN-major box {64, 64, 1}
+  CUtensorMap tm_x;  // store of x: {N, M, Bc}, box {64, 128, 1}, 128B swizzle
+  int N;                 // columns of x = rows of the (possibly gathered) B operand
+  int rows_per_part;     // K-major B: rows held by each part of a gathered buffer (BN divides it)
   int tiles_m, tiles_n, num_tiles, num_kb;
   DeviceStatus* status;
   unsigned long long timeout_ns;
@@ -115,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1) contract_kernel(const __grid_cons
           const int k0 = kb * BK;
           if (!MN_MAJOR) {
             tma_load_3d(sa, &p.tm_a, &full_bar[s], k0, m0, d);
-            tma_load_3d(sb, &p.tm_b, &full_bar[s], k0, n0, d);
+            tma_load_4d(sb, &p.tm_b, &full_bar[s], k0, n0 % p.rows_per_part, d, n0 / p.rows_per_part);
           } else {
 #pragma unroll
             for (int h = 0; h < BM / 64; ++h) tma_load_3d(sa + h * 8192, &p.tm_a, &full_bar[s], m0 + 64 * h, k0, d);
@@ -210,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1) contract_kernel(const __grid_cons
         fence_proxy_async_smem();
         named_bar_sync(1, 128);
         if (ep == 0) {
-          if (n0 + ch * 64 < p.L) tma_store_3d(&p.tm_x, st, n0 + ch * 64, m0, d);
+          if (n0 + ch * 64 < p.N) tma_store_3d(&p.tm_x, st, n0 + ch * 64, m0, d);
           bulk_commit();
         }
       }

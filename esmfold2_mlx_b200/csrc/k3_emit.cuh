@@ -46,7 +46,7 @@ constexpr int kThreads = 576;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
-  CUtensorMap tm_z;   // z [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle (load)
+  CUtensorMap tm_z;   // z [B, rows, cols, c_z]: box {64, jw, ih, 1}, 128B swizzle (load)
   CUtensorMap tm_zo;  // z_out: box {64, min(jw,32), 32/min(jw,32), 1}, 128B swizzle (per-warp store)
   CUtensorMap tm_x;   // x [B*c, L, Lpad]: box {jw, ih, c}, no swizzle (load)
   CUtensorMap tm_we;  // w_emit [c_z, c]: box {64, 128}
@@ -58,7 +58,7 @@ struct Params {
   const float* b_emit;  // [c_z] or null
   const float* b_gate;  // [c_z] or null
   float mix_eps;
-  int L, ih, jw, tiles_i, tiles_j, num_tiles;
+  int rows, cols, ih, jw, tiles_i, tiles_j, num_tiles;
   DeviceStatus* status;
   unsigned long long timeout_ns;
 };

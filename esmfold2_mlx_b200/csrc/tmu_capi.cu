@@ -82,12 +82,13 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int row_pitch(int L) { return (L + 7) & ~7; }
 
-// 128-position tile as an ih x jw block of the pair grid, minimising padding at ragged L.
-void choose_tile(int L, int& ih, int& jw) {
+// 128-position tile as an ih x jw block of a rows x cols pair grid, minimising padding.
+void choose_tile(int rows, int cols, int& ih, int& jw) {
   static const int opts[5][2] = {{1, 128}, {2, 64}, {4, 32}, {8, 16}, {16, 8}};
   long long best = -1;
   for (auto& o : opts) {
-    const long long area = static_cast<long long>((L + o[0] - 1) / o[0]) * o[0] * ((L + o[1] - 1) / o[1]) * o[1];
+    const long long area =
+        static_cast<long long>((rows + o[0] - 1) / o[0]) * o[0] * ((cols + o[1] - 1) / o[1]) * o[1];
     if (best < 0 || area < best) {
       best = area;
       ih = o[0];
@@ -157,7 +158,20 @@ cudaError_t launch_pdl(void (*kern)(P), int grid, int block, int smem, cudaStrea
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int B, int L, void* a, void* b,
+// A pair tensor [B, rows, cols, c_z] with contiguous channels and arbitrary element strides
+// (z, or a transposed view of a received slab), plus the element strides of its mask.
+struct PairGeom {
+  int B, rows, cols;
+  long long sb, sr, sc;
+  long long msb, msr, msc;
+};
+
+PairGeom square_geom(int B, int L) {
+  const long long cz = 128;
+  return PairGeom{B, L, L, cz * L * L, cz * L, cz, 1LL * L * L, L, 1};
+}
+
+int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
               DeviceStatus* status, cudaStream_t stream, bool reset_status = false) {
   const bool hb = w->b_proj != nullptr, hm = mask != nullptr;
   void (*kern)(k1::Params) = hb ? (hm ? k1::project_gate_kernel<true, true> : k1::project_gate_kernel<true, false>)
@@ -169,11 +183,11 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int 
   k1::Params p;
   memset(&p, 0, sizeof(p));
   int ih = 1, jw = 128;
-  choose_tile(L, ih, jw);
-  const uint64_t Lp = row_pitch(L);
+  choose_tile(g.rows, g.cols, ih, jw);
+  const uint64_t cp = row_pitch(g.cols);
   {
-    const uint64_t dims[4] = {128, (uint64_t)L, (uint64_t)L, (uint64_t)B};
-    const uint64_t str[3] = {256, 256ull * L, 256ull * L * L};
+    const uint64_t dims[4] = {128, (uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B};
+    const uint64_t str[3] = {2ull * g.sc, 2ull * g.sr, 2ull * g.sb};
     const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
     if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
@@ -184,8 +198,8 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int 
     if ((st = encode_map(&p.tm_w, w->w_proj, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
-    const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)B * 128};
-    const uint64_t str[2] = {Lp * 2, Lp * 2 * L};
+    const uint64_t dims[3] = {(uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B * 128};
+    const uint64_t str[2] = {cp * 2, cp * 2 * g.rows};
     // one epilogue store: 32 positions x 32 channels, staged with the swizzle matching its row width
     const uint32_t w32 = jw < k1::SPOS ? jw : k1::SPOS;
     const uint32_t box[3] = {w32, k1::SPOS / w32, 32};
@@ -198,13 +212,17 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int 
   p.ln_b = static_cast<const __half*>(w->ln_in_b);
   p.bias = w->b_proj;
   p.mask = static_cast<const __half*>(mask);
-  p.L = L;
+  p.mask_sb = g.msb;
+  p.mask_si = g.msr;
+  p.mask_sj = g.msc;
+  p.rows = g.rows;
+  p.cols = g.cols;
   p.ih = ih;
   p.jw = jw;
   p.log2_jw = 31 - __builtin_clz(static_cast<unsigned>(jw));
-  p.tiles_i = (L + ih - 1) / ih;
-  p.tiles_j = (L + jw - 1) / jw;
-  p.num_tiles = B * p.tiles_i * p.tiles_j;
+  p.tiles_i = (g.rows + ih - 1) / ih;
+  p.tiles_j = (g.cols + jw - 1) / jw;
+  p.num_tiles = g.B * p.tiles_i * p.tiles_j;
   p.reset_status = reset_status ? 1 : 0;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
@@ -214,9 +232,13 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, int 
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch project_gate_kernel");
 }
 
+// x[d] (M x N) = A[d] B[d]^T with K-deep rows.  K-major (outgoing form): a is [Bc, M, pitch(K)];
+// b is `parts` consecutive blocks [Bc, rows_per_part, pitch(K)] (N = parts * rows_per_part), the
+// layout an all-gather of row slabs produces.  MN-major (incoming form): a, b are [Bc, K, pitch(M)]
+// with M = N = K (square only).  x is [Bc, M, pitch(N)].
 template <int BN, bool MN>
-int launch_k2_t(const void* a, const void* b, void* x, int Bc, int L, DeviceStatus* status, cudaStream_t stream,
-                unsigned attr_bit) {
+int launch_k2_t(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int rows_per_part,
+                DeviceStatus* status, cudaStream_t stream, unsigned attr_bit) {
   using C = k2::Cfg<BN>;
   auto kern = &k2::contract_kernel<BN, MN>;
   Dev dev;
@@ -224,28 +246,36 @@ int launch_k2_t(const void* a, const void* b, void* x, int Bc, int L, DeviceStat
   if (st) return st;
   k2::Params p;
   memset(&p, 0, sizeof(p));
-  const uint64_t Lp = row_pitch(L);
-  const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)Bc};
-  const uint64_t str[2] = {Lp * 2, Lp * 2 * L};
+  const uint64_t kp = row_pitch(K), np = row_pitch(N);
   if (!MN) {
+    const int parts = N / rows_per_part;
+    const uint64_t da[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)Bc};
+    const uint64_t sa[2] = {kp * 2, kp * 2 * M};
     const uint32_t boxa[3] = {64, 128, 1};
-    const uint32_t boxb[3] = {64, (uint32_t)BN, 1};
-    if ((st = encode_map(&p.tm_a, a, 3, dims, str, boxa, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
-    if ((st = encode_map(&p.tm_b, b, 3, dims, str, boxb, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_map(&p.tm_a, a, 3, da, sa, boxa, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    const uint64_t db[4] = {(uint64_t)K, (uint64_t)rows_per_part, (uint64_t)Bc, (uint64_t)parts};
+    const uint64_t sb[3] = {kp * 2, kp * 2 * rows_per_part, kp * 2 * rows_per_part * Bc};
+    const uint32_t boxb[4] = {64, (uint32_t)BN, 1, 1};
+    if ((st = encode_map(&p.tm_b, b, 4, db, sb, boxb, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   } else {
+    const uint64_t dims[3] = {(uint64_t)M, (uint64_t)K, (uint64_t)Bc};
+    const uint64_t str[2] = {row_pitch(M) * 2ull, row_pitch(M) * 2ull * K};
     const uint32_t box[3] = {64, 64, 1};
     if ((st = encode_map(&p.tm_a, a, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
     if ((st = encode_map(&p.tm_b, b, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
+    const uint64_t dims[3] = {(uint64_t)N, (uint64_t)M, (uint64_t)Bc};
+    const uint64_t str[2] = {np * 2, np * 2 * M};
     const uint32_t box[3] = {64, 128, 1};
     if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
-  p.L = L;
-  p.tiles_m = (L + k2::BM - 1) / k2::BM;
-  p.tiles_n = (L + BN - 1) / BN;
+  p.N = N;
+  p.rows_per_part = rows_per_part;
+  p.tiles_m = (M + k2::BM - 1) / k2::BM;
+  p.tiles_n = (N + BN - 1) / BN;
   p.num_tiles = Bc * p.tiles_m * p.tiles_n;
-  p.num_kb = (L + k2::BK - 1) / k2::BK;
+  p.num_kb = (K + k2::BK - 1) / k2::BK;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
   const int grid = std::min(p.num_tiles, dev.sms);
@@ -254,18 +284,27 @@ int launch_k2_t(const void* a, const void* b, void* x, int Bc, int L, DeviceStat
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch contract_kernel");
 }
 
-int launch_k2(const void* a, const void* b, void* x, int Bc, int L, bool outgoing, DeviceStatus* status,
-              cudaStream_t stream) {
-  if (L <= 128) {
-    return outgoing ? launch_k2_t<128, false>(a, b, x, Bc, L, status, stream, 1u << 1)
-                    : launch_k2_t<128, true>(a, b, x, Bc, L, status, stream, 1u << 2);
+int launch_k2(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int rows_per_part, bool outgoing,
+              DeviceStatus* status, cudaStream_t stream) {
+  if (!outgoing) {
+    if (M != N || M != K || rows_per_part != N) return fail(TMU_ERR_UNSUPPORTED, "incoming form is square only");
+    return N <= 128 ? launch_k2_t<128, true>(a, b, x, Bc, M, N, K, N, status, stream, 1u << 2)
+                    : launch_k2_t<256, true>(a, b, x, Bc, M, N, K, N, status, stream, 1u << 4);
   }
-  return outgoing ? launch_k2_t<256, false>(a, b, x, Bc, L, status, stream, 1u << 3)
-                  : launch_k2_t<256, true>(a, b, x, Bc, L, status, stream, 1u << 4);
+  const int parts = N / rows_per_part;
+  if (parts * rows_per_part != N) return fail(TMU_ERR_INVALID_ARGUMENT, "N must be a multiple of rows_per_part");
+  if (parts == 1) {
+    return N <= 128 ? launch_k2_t<128, false>(a, b, x, Bc, M, N, K, N, status, stream, 1u << 1)
+                    : launch_k2_t<256, false>(a, b, x, Bc, M, N, K, N, status, stream, 1u << 3);
+  }
+  // a gathered B operand: a tile of BN rows must not straddle two parts
+  if (rows_per_part % 256 == 0) return launch_k2_t<256, false>(a, b, x, Bc, M, N, K, rows_per_part, status, stream, 1u << 3);
+  if (rows_per_part % 128 == 0) return launch_k2_t<128, false>(a, b, x, Bc, M, N, K, rows_per_part, status, stream, 1u << 1);
+  return fail(TMU_ERR_UNSUPPORTED, "rows_per_part of a gathered operand must be a multiple of 128");
 }
 
-int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int L, float mix_eps,
-              DeviceStatus* status, cudaStream_t stream) {
+int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
+              float mix_eps, DeviceStatus* status, cudaStream_t stream) {
   // the emit and gate biases come together (both present, or neither: the reference's form)
   if ((w->b_emit == nullptr) != (w->b_gate == nullptr))
     return fail(TMU_ERR_INVALID_ARGUMENT, "b_emit and b_gate must both be set or both be NULL");
@@ -277,11 +316,11 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   k3::Params p;
   memset(&p, 0, sizeof(p));
   int ih = 1, jw = 128;
-  choose_tile(L, ih, jw);
-  const uint64_t Lp = row_pitch(L);
+  choose_tile(rows, cols, ih, jw);
+  const uint64_t cp = row_pitch(cols);
   {
-    const uint64_t dims[4] = {128, (uint64_t)L, (uint64_t)L, (uint64_t)B};
-    const uint64_t str[3] = {256, 256ull * L, 256ull * L * L};
+    const uint64_t dims[4] = {128, (uint64_t)cols, (uint64_t)rows, (uint64_t)B};
+    const uint64_t str[3] = {256, 256ull * cols, 256ull * cols * rows};
     const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
     if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
     const uint32_t jwp = jw < 32 ? jw : 32;  // one epilogue warp's 32 positions
@@ -289,8 +328,8 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
     if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, boxo, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
-    const uint64_t dims[3] = {(uint64_t)L, (uint64_t)L, (uint64_t)B * 128};
-    const uint64_t str[2] = {Lp * 2, Lp * 2 * L};
+    const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, (uint64_t)B * 128};
+    const uint64_t str[2] = {cp * 2, cp * 2 * rows};
     const uint32_t box[3] = {(uint32_t)jw, (uint32_t)ih, 128};
     if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
   }
@@ -308,11 +347,12 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   p.b_emit = w->b_emit;
   p.b_gate = w->b_gate;
   p.mix_eps = mix_eps;
-  p.L = L;
+  p.rows = rows;
+  p.cols = cols;
   p.ih = ih;
   p.jw = jw;
-  p.tiles_i = (L + ih - 1) / ih;
-  p.tiles_j = (L + jw - 1) / jw;
+  p.tiles_i = (rows + ih - 1) / ih;
+  p.tiles_j = (cols + jw - 1) / jw;
   p.num_tiles = B * p.tiles_i * p.tiles_j;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
@@ -461,7 +501,8 @@ int tmu_project_gate(const void* z, const void* mask, const tmu_trimul_weights* 
   if ((st = check_weights(w, true, false))) return st;
   if (!z || !a || !b || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   if (!aligned16(z) || !aligned16(a) || !aligned16(b)) return fail(TMU_ERR_MISALIGNED, "z/a/b not 16-byte aligned");
-  return launch_k1(z, mask, w, B, L, a, b, static_cast<DeviceStatus*>(status), static_cast<cudaStream_t>(stream));
+  return launch_k1(z, mask, w, square_geom(B, L), a, b, static_cast<DeviceStatus*>(status),
+                   static_cast<cudaStream_t>(stream));
 }
 
 int tmu_contract(const void* a, const void* b, void* x, int Bc, int L, int outgoing, void* status, void* stream) {
@@ -469,7 +510,7 @@ int tmu_contract(const void* a, const void* b, void* x, int Bc, int L, int outgo
   if (L > 8192 || Bc > 65535) return fail(TMU_ERR_UNSUPPORTED, "L > 8192 or Bc > 65535");
   if (!a || !b || !x || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   if (!aligned16(a) || !aligned16(b) || !aligned16(x)) return fail(TMU_ERR_MISALIGNED, "a/b/x not 16-byte aligned");
-  return launch_k2(a, b, x, Bc, L, outgoing != 0, static_cast<DeviceStatus*>(status),
+  return launch_k2(a, b, x, Bc, L, L, L, L, outgoing != 0, static_cast<DeviceStatus*>(status),
                    static_cast<cudaStream_t>(stream));
 }
 
@@ -481,7 +522,47 @@ int tmu_emit_residual(const void* x, const void* z, void* z_out, const tmu_trimu
   if (!x || !z || !z_out || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   if (!aligned16(x) || !aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "x/z not 16-byte aligned");
   if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
-  return launch_k3(x, z, z_out, w, B, L, mix_eps, static_cast<DeviceStatus*>(status),
+  return launch_k3(x, z, z_out, w, B, L, L, mix_eps, static_cast<DeviceStatus*>(status),
+                   static_cast<cudaStream_t>(stream));
+}
+
+int tmu_project_gate_ex(const void* z, const void* mask, const tmu_pair_layout* g, const tmu_trimul_weights* w,
+                        int c_z, int c, void* a, void* b, void* status, void* stream) {
+  if (g == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "layout is NULL");
+  if (g->rows < 1 || g->cols < 1 || g->B < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "empty pair grid");
+  int st = check_sizes(g->B, std::max(g->rows, g->cols), c_z, c);
+  if (st) return st;
+  if ((st = check_weights(w, true, false))) return st;
+  if (!z || !a || !b || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!aligned16(z) || !aligned16(a) || !aligned16(b)) return fail(TMU_ERR_MISALIGNED, "z/a/b not 16-byte aligned");
+  if (g->stride_col % 8 || g->stride_row % 8 || g->stride_b % 8)
+    return fail(TMU_ERR_MISALIGNED, "z strides must be multiples of 8 elements (16 bytes)");
+  const PairGeom pg{g->B, g->rows, g->cols, g->stride_b, g->stride_row, g->stride_col,
+                    g->mask_stride_b, g->mask_stride_row, g->mask_stride_col};
+  return launch_k1(z, mask, w, pg, a, b, static_cast<DeviceStatus*>(status), static_cast<cudaStream_t>(stream));
+}
+
+int tmu_contract_ex(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int b_rows_per_part,
+                    void* status, void* stream) {
+  if (Bc < 1 || M < 1 || N < 1 || K < 1 || b_rows_per_part < 1)
+    return fail(TMU_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  if (M > 8192 || N > 8192 || K > 8192 || Bc > 65535) return fail(TMU_ERR_UNSUPPORTED, "size too large");
+  if (!a || !b || !x || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(x)) return fail(TMU_ERR_MISALIGNED, "a/b/x not 16-byte aligned");
+  return launch_k2(a, b, x, Bc, M, N, K, b_rows_per_part, true, static_cast<DeviceStatus*>(status),
+                   static_cast<cudaStream_t>(stream));
+}
+
+int tmu_emit_residual_ex(const void* x, const void* z, void* z_out, int B, int rows, int cols,
+                         const tmu_trimul_weights* w, int c_z, int c, float mix_eps, void* status, void* stream) {
+  if (rows < 1 || cols < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "empty pair grid");
+  int st = check_sizes(B, std::max(rows, cols), c_z, c);
+  if (st) return st;
+  if ((st = check_weights(w, false, true))) return st;
+  if (!x || !z || !z_out || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!aligned16(x) || !aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "x/z not 16-byte aligned");
+  if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
+  return launch_k3(x, z, z_out, w, B, rows, cols, mix_eps, static_cast<DeviceStatus*>(status),
                    static_cast<cudaStream_t>(stream));
 }
 
@@ -504,9 +585,9 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
   void* x = ws + TMU_STATUS_BYTES + 2 * cm;
   // K1 zeroes the status word after its dependency wait (no memset node between the kernels,
   // so the three launches chain with programmatic dependent launch)
-  if ((st = launch_k1(z, mask, w, B, L, a, b, status, s, true))) return st;
-  if ((st = launch_k2(a, b, x, B * c, L, outgoing != 0, status, s))) return st;
-  return launch_k3(x, z, z_out, w, B, L, mix_eps, status, s);
+  if ((st = launch_k1(z, mask, w, square_geom(B, L), a, b, status, s, true))) return st;
+  if ((st = launch_k2(a, b, x, B * c, L, L, L, L, outgoing != 0, status, s))) return st;
+  return launch_k3(x, z, z_out, w, B, L, L, mix_eps, status, s);
 }
 
 int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L,
@@ -536,9 +617,9 @@ int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_t
   void* x = base + TMU_STATUS_BYTES + 2 * kNoAllocBufBytes;
   // the status word must start at zero; a, b and x are fully rewritten before they are read
   if ((st = tmu_reset_status(dstat, stream))) return st;
-  if ((st = launch_k1(z, mask, w, B, L, a, b, dstat, s))) return st;
-  if ((st = launch_k2(a, b, x, B * c, L, outgoing != 0, dstat, s))) return st;
-  return launch_k3(x, z, z_out, w, B, L, mix_eps, dstat, s);
+  if ((st = launch_k1(z, mask, w, square_geom(B, L), a, b, dstat, s))) return st;
+  if ((st = launch_k2(a, b, x, B * c, L, L, L, L, outgoing != 0, dstat, s))) return st;
+  return launch_k3(x, z, z_out, w, B, L, L, mix_eps, dstat, s);
 }
 
 int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream) {

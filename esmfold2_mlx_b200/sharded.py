@@ -1,0 +1,142 @@
+"""One long sequence's triangle update row-sharded over the GPUs of a process group.
+
+The reference runs one fold on one device; this path (L = 3072 over 2/4/8
+B200s) has no counterpart there.  Rank r holds rows [r*Lr, (r+1)*Lr) of the pair tensor
+z [1, L, L, c_z] (Lr = L / P) and returns the same rows of z + update.
+
+Outgoing, x[d,i,j] = sum_k a[d,i,k] b[d,j,k]: a and b are projected on the local rows (K1); the
+ranks' b slabs are all-gathered into [P, B*c, Lr, pitch] -- exactly the block layout the
+contraction kernel reads through a 4-D tensor map, so no reorder copy -- and each rank contracts
+its rows of a against all rows of b (K2) and finishes its rows (K3).
+
+Incoming, x[d,i,j] = sum_k a[d,k,i] b[d,k,j]: with a'[d,i,k] = a[d,k,i] (the projection of
+z^T[i,k] = z[k,i]) it is the outgoing form of the transposed grid.  An all-to-all sends each
+rank's [Lr, Lr] blocks to the rank owning those columns, which then holds z[:, its columns] as a
+[P, Lr, Lr, c_z] buffer; K1 reads that buffer as the transposed slab z^T[its columns, :] through
+strides alone (element (i, k) sits at k*Lr*c_z + i*c_z), the b' slabs are all-gathered, K2
+contracts, and K3 finishes the local rows of z in their original orientation.
+
+The collectives are NCCL through torch.distributed on the current stream (the stages only ever
+launch on it, so collective and kernels are stream-ordered).  The three stages are injectable
+(``stages=``) so the data movement can be exercised on CPU ranks with gloo.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib, ops
+
+
+class CudaStages:
+    """The three sm_100a kernels through the slab entry points of the C ABI."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.status = ops.new_status(self.device)
+
+    def project_gate(self, z, layout, mask, w):
+        """z: storage holding a [B, rows, cols, c_z] view with element strides
+        (stride_b, stride_row, stride_col); mask likewise with mask strides (or None).
+        Returns a, b: [B*c, rows, pitch(cols)]."""
+        B, rows, cols, sb, sr, sc, msb, msr, msc = layout
+        lib = _lib.load()
+        g = _lib.TmuPairLayout(B, rows, cols, sb, sr, sc, msb, msr, msc)
+        a = torch.empty(B * w.c, rows, ops.row_pitch(cols), dtype=torch.float16, device=self.device)
+        b = torch.empty_like(a)
+        _lib.check(lib.tmu_project_gate_ex(ops._ptr(z), ops._ptr(mask), ctypes.byref(g), ctypes.byref(w.struct),
+                                           w.c_z, w.c, ops._ptr(a), ops._ptr(b), ops._ptr(self.status),
+                                           ops._stream_ptr(self.device)), "tmu_project_gate_ex")
+        return a, b
+
+    def contract(self, a, b_parts, M, N, K, rows_per_part):
+        """a [Bc, M, pitch(K)], b_parts [P, Bc, rows_per_part, pitch(K)] -> x [Bc, M, pitch(N)]."""
+        lib = _lib.load()
+        Bc = a.shape[0]
+        x = torch.empty(Bc, M, ops.row_pitch(N), dtype=torch.float16, device=self.device)
+        _lib.check(lib.tmu_contract_ex(ops._ptr(a), ops._ptr(b_parts), ops._ptr(x), Bc, M, N, K, rows_per_part,
+                                       ops._ptr(self.status), ops._stream_ptr(self.device)), "tmu_contract_ex")
+        return x
+
+    def emit_residual(self, x, z, w, mix_eps, out):
+        lib = _lib.load()
+        B, rows, cols = z.shape[0], z.shape[1], z.shape[2]
+        _lib.check(lib.tmu_emit_residual_ex(ops._ptr(x), ops._ptr(z), ops._ptr(out), B, rows, cols,
+                                            ctypes.byref(w.struct), w.c_z, w.c, float(mix_eps),
+                                            ops._ptr(self.status), ops._stream_ptr(self.device)),
+                   "tmu_emit_residual_ex")
+        return out
+
+
+class DistExchange:
+    """The two collectives of the sharded update over a torch.distributed process group."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def all_gather(self, local):
+        """Every rank's ``local`` stacked along a new leading dim: [P, *local.shape]."""
+        out = torch.empty((self.size * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+        dist.all_gather_into_tensor(out, local.contiguous(), group=self.group)
+        return out.view((self.size,) + tuple(local.shape))
+
+    def all_to_all(self, send):
+        """send[q] goes to rank q; returns recv with recv[q] from rank q (same shape as send)."""
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send.contiguous(), group=self.group)
+        return recv
+
+
+class RowShardedTrimul:
+    """Triangle update of a pair tensor row-sharded over the ranks of ``group`` (B = 1).
+
+    ``exchange`` replaces the process-group collectives (an object with ``size``, ``rank``,
+    ``all_gather`` and ``all_to_all`` as in :class:`DistExchange`)."""
+
+    def __init__(self, L: int, group=None, device=None, stages=None, exchange=None):
+        self.exchange = exchange if exchange is not None else DistExchange(group)
+        self.P = self.exchange.size
+        self.rank = self.exchange.rank
+        if L % self.P:
+            raise ValueError(f"L={L} is not divisible by the {self.P} ranks")
+        self.L = L
+        self.Lr = L // self.P
+        if self.P > 1 and self.Lr % 128:
+            raise ValueError("rows per rank must be a multiple of 128 (the contraction's B-operand tiles)")
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.stages = stages if stages is not None else CudaStages(self.device)
+
+    def _to_columns(self, t):
+        """[Lr(my rows), L, ...] -> [P(source), Lr(source rows), Lr(my columns), ...]."""
+        P, Lr = self.P, self.Lr
+        send = torch.stack([t[:, q * Lr:(q + 1) * Lr] for q in range(P)])  # [P(dest), Lr, Lr, ...]
+        return self.exchange.all_to_all(send)
+
+    def __call__(self, z_local: torch.Tensor, mask_local, w: ops.TrimulWeights, outgoing: bool,
+                 mix_eps: float = ops.MIX_EPS_FP16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """z_local: [1, Lr, L, c_z] fp16 (this rank's rows); mask_local: [1, Lr, L] fp16 or None."""
+        L, Lr, P = self.L, self.Lr, self.P
+        cz = w.c_z
+        if tuple(z_local.shape) != (1, Lr, L, cz):
+            raise ValueError(f"z_local must be [1, {Lr}, {L}, {cz}], got {tuple(z_local.shape)}")
+        z_local = z_local.contiguous()
+        out = torch.empty_like(z_local) if out is None else out
+        if outgoing:
+            layout = (1, Lr, L, Lr * L * cz, L * cz, cz, Lr * L, L, 1)
+            a, b = self.stages.project_gate(z_local, layout, None if mask_local is None else mask_local.contiguous(), w)
+        else:
+            zt = self._to_columns(z_local[0])  # [P, Lr(k within source), Lr(i), cz]: z[k, i] at k*Lr*cz + i*cz
+            mt = None
+            if mask_local is not None:
+                mt = self._to_columns(mask_local[0])  # [P, Lr(k), Lr(i)]: mask[k, i] at k*Lr + i
+            layout = (1, Lr, L, L * Lr * cz, cz, Lr * cz, L * Lr, 1, Lr)
+            a, b = self.stages.project_gate(zt, layout, mt, w)
+        b_parts = self.exchange.all_gather(b)  # [P, Bc, Lr, pitch(L)]
+        x = self.stages.contract(a, b_parts, Lr, L, L, Lr)
+        return self.stages.emit_residual(x, z_local, w, mix_eps, out)

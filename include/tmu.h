@@ -110,6 +110,34 @@ int tmu_contract(const void* a, const void* b, void* x, int Bc, int L, int outgo
 int tmu_emit_residual(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int L,
                       int c_z, int c, float mix_eps, void* status, void* stream);
 
+/* ---- Row slabs (one long sequence sharded over devices; no counterpart in the reference, which
+ * runs one device).  A slab is a rows x cols block of the pair grid.  These entry points let a
+ * caller run the three stages on slabs and do the exchange between them itself (NCCL):
+ *   outgoing: project_gate_ex on the local rows -> all-gather b -> contract_ex -> emit_residual_ex
+ *   incoming: all-to-all the local rows into local columns (z^T), project_gate_ex on that
+ *             transposed view -> all-gather b' -> contract_ex -> emit_residual_ex on the local rows.
+ */
+typedef struct tmu_pair_layout {
+  int B, rows, cols;                       /* B folds of rows x cols positions */
+  long long stride_b, stride_row, stride_col;                 /* z element strides (channels contiguous) */
+  long long mask_stride_b, mask_stride_row, mask_stride_col;  /* mask element strides (ignored if no mask) */
+} tmu_pair_layout;
+
+/* K1 on a strided rows x cols view: a, b are [B*c, rows, tmu_row_pitch(cols)]. */
+int tmu_project_gate_ex(const void* z, const void* mask, const tmu_pair_layout* layout, const tmu_trimul_weights* w,
+                        int c_z, int c, void* a, void* b, void* status, void* stream);
+
+/* K2 in the outgoing form on slabs: x[d] (M x N) = a[d] (M x K) b[d]^T, a is [Bc, M, pitch(K)],
+ * x is [Bc, M, pitch(N)], and b is N / b_rows_per_part consecutive blocks [Bc, b_rows_per_part,
+ * pitch(K)] (what an all-gather of the ranks' [Bc, rows, pitch(K)] slabs produces).  With more
+ * than one block, b_rows_per_part must be a multiple of 128. */
+int tmu_contract_ex(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int b_rows_per_part,
+                    void* status, void* stream);
+
+/* K3 on a contiguous [B, rows, cols, c_z] slab with x [B*c, rows, pitch(cols)]. */
+int tmu_emit_residual_ex(const void* x, const void* z, void* z_out, int B, int rows, int cols,
+                         const tmu_trimul_weights* w, int c_z, int c, float mix_eps, void* status, void* stream);
+
 /* K1 -> K2 -> K3: z_out = z + tri-mul(z).  `workspace` of tmu_workspace_bytes() bytes, 256-byte
  * aligned; its first TMU_STATUS_BYTES are the status word (zeroed by this call's first kernel).
  * The kernels are launched with programmatic dependent launch, so each one's set-up overlaps

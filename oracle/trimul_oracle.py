@@ -151,14 +151,11 @@ def _contract(a: torch.Tensor, b: torch.Tensor, outgoing: bool) -> torch.Tensor:
     return x.reshape(B, c, L, L)
 
 
-def trimul_fp16(p: dict, z: torch.Tensor, mask, outgoing: bool, mix_eps: float = MIX_EPS_FP16,
-                return_intermediates: bool = False):
-    """One fused fp16 triangle update, returning ``z + update`` rounded to fp16 (as fp32).
-
-    z: [B, L, L, c_z] (values representable in fp16); mask: [B, L, L] or None.
-    Follows mlx_trunk_kernels.py:210-229 with ``use=ALL`` (the default stack's path)."""
-    z = r16(z.float())
+def project_gate_fp16(p: dict, z: torch.Tensor, mask):
+    """The first fused step (mlx_trunk_kernels.py:214-216, gate_cf :47-80) on a [B, rows, cols,
+    c_z] grid: returns n and channel-major a, b [B, c, rows, cols] (fp16 values as fp32)."""
     c = p["c"]
+    z = r16(z.float())
     n = r16(layer_norm(z, p["ln_in_w"], p["ln_in_b"], EPS))
     proj = n @ p["w_in"]
     if p.get("b_in") is not None:
@@ -170,11 +167,17 @@ def trimul_fp16(p: dict, z: torch.Tensor, mask, outgoing: bool, mix_eps: float =
         v = proj[..., lo:lo + c] / (1.0 + torch.exp(-proj[..., 2 * c + lo:3 * c + lo]))  # gate_cf :62
         if m is not None:
             v = v * m[..., None]
-        return r16(v).permute(0, 3, 1, 2).contiguous()  # [B, c, L, L]
+        return r16(v).permute(0, 3, 1, 2).contiguous()
 
-    a, b = gated(0), gated(c)
-    x = r16(_contract(a, b, outgoing))
-    mixn = r16(layer_norm(x.permute(0, 2, 3, 1), p["ln_mix_w"], p["ln_mix_b"], mix_eps))
+    return n, gated(0), gated(c)
+
+
+def emit_residual_fp16(p: dict, z: torch.Tensor, x: torch.Tensor, mix_eps: float = MIX_EPS_FP16):
+    """The last fused step (ln_cf_to_cl, @ w_emit, n @ w_out_gate, resgate_ln:
+    mlx_trunk_kernels.py:221-227) on a [B, rows, cols, c_z] grid with x [B, c, rows, cols]."""
+    z = r16(z.float())
+    n = r16(layer_norm(z, p["ln_in_w"], p["ln_in_b"], EPS))
+    mixn = r16(layer_norm(r16(x.float()).permute(0, 2, 3, 1), p["ln_mix_w"], p["ln_mix_b"], mix_eps))
     mixed = mixn @ p["w_emit"]
     if p.get("b_emit") is not None:
         mixed = mixed + p["b_emit"]
@@ -183,9 +186,20 @@ def trimul_fp16(p: dict, z: torch.Tensor, mask, outgoing: bool, mix_eps: float =
     if p.get("b_gate") is not None:
         g = g + p["b_gate"]
     g = r16(g)
-    z_new = r16(z + mixed / (1.0 + torch.exp(-g)))  # resgate_ln :176-177
+    return r16(z + mixed / (1.0 + torch.exp(-g))), {"mixn": mixn, "mixed": mixed, "g": g}  # resgate_ln :176-177
+
+
+def trimul_fp16(p: dict, z: torch.Tensor, mask, outgoing: bool, mix_eps: float = MIX_EPS_FP16,
+                return_intermediates: bool = False):
+    """One fused fp16 triangle update, returning ``z + update`` rounded to fp16 (as fp32).
+
+    z: [B, L, L, c_z] (values representable in fp16); mask: [B, L, L] or None.
+    Follows mlx_trunk_kernels.py:210-229 with ``use=ALL`` (the default stack's path)."""
+    n, a, b = project_gate_fp16(p, z, mask)
+    x = r16(_contract(a, b, outgoing))
+    z_new, it = emit_residual_fp16(p, z, x, mix_eps)
     if return_intermediates:
-        return z_new, {"n": n, "proj": proj, "a": a, "b": b, "x": x, "mixn": mixn, "mixed": mixed, "g": g}
+        return z_new, {"n": n, "a": a, "b": b, "x": x, **it}
     return z_new
 
 
