@@ -2,7 +2,7 @@
 //
 // Everything here is hand-written inline PTX for Blackwell (sm_100a):
 //   * mbarrier init / arrive / expect-tx / bounded parity wait,
-//   * TMA tiled loads and stores (cp.async.bulk.tensor, no multicast anywhere),
+//   * TMA tiled loads and stores (cp.async.bulk.tensor; every load fills only its own CTA),
 //   * tcgen05: TMEM alloc/dealloc, kind::f16 MMA with fp32 accumulation in TMEM, commit to an
 //     mbarrier, and 32x32b TMEM loads for the epilogues,
 //   * shared-memory matrix descriptors for 128-byte-swizzled K-major and MN-major operands.
@@ -147,7 +147,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // ------------------------------------------------------------------------------------------
 // TMA (tiled tensor copies).  Loads signal an mbarrier with complete_tx; stores use bulk groups.
-// No .multicast::cluster form is used anywhere in this library.
+// Every load fills only the issuing CTA's shared memory (no cluster-wide broadcast form).
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
