@@ -12,8 +12,10 @@
 #include <string>
 
 #include "k1_project.cuh"
+#include "k1w_project.cuh"
 #include "k2_contract.cuh"
 #include "k3_emit.cuh"
+#include "k3w_emit.cuh"
 #include "tmu.h"
 
 using namespace tmu;
@@ -82,17 +84,19 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int row_pitch(int L) { return (L + 7) & ~7; }
 
-// 128-position tile as an ih x jw block of a rows x cols pair grid, minimising padding.
-void choose_tile(int rows, int cols, int& ih, int& jw) {
-  static const int opts[5][2] = {{1, 128}, {2, 64}, {4, 32}, {8, 16}, {16, 8}};
+// A tile of `tile` (128 or 64) positions as an ih x jw block of a rows x cols pair grid, jw >= 8,
+// minimising padding.
+void choose_tile(int rows, int cols, int& ih, int& jw, int tile = 128) {
+  static const int widths[5] = {128, 64, 32, 16, 8};
   long long best = -1;
-  for (auto& o : opts) {
-    const long long area =
-        static_cast<long long>((rows + o[0] - 1) / o[0]) * o[0] * ((cols + o[1] - 1) / o[1]) * o[1];
+  for (int wi : widths) {
+    if (wi > tile || tile / wi > 16) continue;  // 128: 1x128 .. 16x8; 64: 1x64 .. 8x8
+    const int hi = tile / wi;
+    const long long area = static_cast<long long>((rows + hi - 1) / hi) * hi * ((cols + wi - 1) / wi) * wi;
     if (best < 0 || area < best) {
       best = area;
-      ih = o[0];
-      jw = o[1];
+      ih = hi;
+      jw = wi;
     }
   }
 }
@@ -123,9 +127,20 @@ int current_device(Dev& d, unsigned attr_bit, const void* kernel, int smem) {
 
 int check_sizes(int B, int L, int c_z, int c) {
   if (B < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "B and L must be positive");
-  if (c_z != 128 || c != 128) return fail(TMU_ERR_UNSUPPORTED, "only c_z == c == 128 is built");
+  if (c_z != c || (c != 128 && c != 256)) return fail(TMU_ERR_UNSUPPORTED, "c_z == c, 128 or 256, is built");
   if (L > 8192) return fail(TMU_ERR_UNSUPPORTED, "L > 8192");
   if (static_cast<long long>(B) * c > 65535) return fail(TMU_ERR_UNSUPPORTED, "B*c > 65535");
+  return TMU_OK;
+}
+
+// The c_z = 256 emit kernel splits each tile's output channels over two CTAs, so one CTA may write
+// z' while the other still reads z: an in-place (or overlapping) update is rejected up front.
+int check_wide_alias(const void* z, const void* z_out, int B, int L, int c_z) {
+  if (c_z != 256) return TMU_OK;
+  const uintptr_t bytes = static_cast<uintptr_t>(B) * L * L * 256 * 2;
+  const uintptr_t zi = reinterpret_cast<uintptr_t>(z), zo = reinterpret_cast<uintptr_t>(z_out);
+  if (zi < zo + bytes && zo < zi + bytes)
+    return fail(TMU_ERR_INVALID_ARGUMENT, "c_z = 256: z_out must not overlap z (no in-place update)");
   return TMU_OK;
 }
 
@@ -158,21 +173,25 @@ cudaError_t launch_pdl(void (*kern)(P), int grid, int block, int smem, cudaStrea
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-// A pair tensor [B, rows, cols, c_z] with contiguous channels and arbitrary element strides
+// A pair tensor [B, rows, cols, cz] with contiguous channels and arbitrary element strides
 // (z, or a transposed view of a received slab), plus the element strides of its mask.
 struct PairGeom {
   int B, rows, cols;
   long long sb, sr, sc;
   long long msb, msr, msc;
+  int cz;
 };
 
-PairGeom square_geom(int B, int L) {
-  const long long cz = 128;
-  return PairGeom{B, L, L, cz * L * L, cz * L, cz, 1LL * L * L, L, 1};
+PairGeom square_geom(int B, int L, int cz) {
+  return PairGeom{B, L, L, 1LL * cz * L * L, 1LL * cz * L, cz, 1LL * L * L, L, 1, cz};
 }
+
+int launch_k1w(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
+               DeviceStatus* status, cudaStream_t stream, bool reset_status);
 
 int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
               DeviceStatus* status, cudaStream_t stream, bool reset_status = false) {
+  if (g.cz == 256) return launch_k1w(z, mask, w, g, a, b, status, stream, reset_status);
   const bool hb = w->b_proj != nullptr, hm = mask != nullptr;
   void (*kern)(k1::Params) = hb ? (hm ? k1::project_gate_kernel<true, true> : k1::project_gate_kernel<true, false>)
                                 : (hm ? k1::project_gate_kernel<false, true> : k1::project_gate_kernel<false, false>);
@@ -303,11 +322,15 @@ int launch_k2(const void* a, const void* b, void* x, int Bc, int M, int N, int K
   return fail(TMU_ERR_UNSUPPORTED, "rows_per_part of a gathered operand must be a multiple of 128");
 }
 
+int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
+               float mix_eps, DeviceStatus* status, cudaStream_t stream);
+
 int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
-              float mix_eps, DeviceStatus* status, cudaStream_t stream) {
+              float mix_eps, DeviceStatus* status, cudaStream_t stream, int cz) {
   // the emit and gate biases come together (both present, or neither: the reference's form)
   if ((w->b_emit == nullptr) != (w->b_gate == nullptr))
     return fail(TMU_ERR_INVALID_ARGUMENT, "b_emit and b_gate must both be set or both be NULL");
+  if (cz == 256) return launch_k3w(x, z, z_out, w, B, rows, cols, mix_eps, status, stream);
   const bool hb = w->b_emit != nullptr;
   void (*kern)(k3::Params) = hb ? k3::emit_residual_kernel<true> : k3::emit_residual_kernel<false>;
   Dev dev;
@@ -360,6 +383,128 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   cudaError_t e = launch_pdl(kern, grid, k3::kThreads, k3::SMEM_BYTES, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_kernel");
+}
+
+int launch_k1w(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
+               DeviceStatus* status, cudaStream_t stream, bool reset_status) {
+  const bool hb = w->b_proj != nullptr, hm = mask != nullptr;
+  void (*kern)(k1w::Params) = hb ? (hm ? k1w::project_gate_w_kernel<true, true> : k1w::project_gate_w_kernel<true, false>)
+                                 : (hm ? k1w::project_gate_w_kernel<false, true> : k1w::project_gate_w_kernel<false, false>);
+  Dev dev;
+  int st = current_device(dev, 1u << (16 + (hb ? 2 : 0) + (hm ? 1 : 0)), reinterpret_cast<const void*>(kern),
+                          k1w::SMEM_BYTES);
+  if (st) return st;
+  if (dev.sms < 4) return fail(TMU_ERR_UNSUPPORTED, "fewer than 4 SMs");
+  k1w::Params p;
+  memset(&p, 0, sizeof(p));
+  int ih = 1, jw = 64;
+  choose_tile(g.rows, g.cols, ih, jw, k1w::TILE);
+  const uint64_t cp = row_pitch(g.cols);
+  {
+    const uint64_t dims[4] = {256, (uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B};
+    const uint64_t str[3] = {2ull * g.sc, 2ull * g.sr, 2ull * g.sb};
+    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[2] = {256, 1024};
+    const uint64_t str[1] = {512};
+    const uint32_t box[2] = {64, 128};
+    if ((st = encode_map(&p.tm_w, w->w_proj, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B * 256};
+    const uint64_t str[2] = {cp * 2, cp * 2 * g.rows};
+    const uint32_t w32 = jw < k1w::SPOS ? jw : k1w::SPOS;
+    const uint32_t box[3] = {w32, k1w::SPOS / w32, 32};
+    const CUtensorMapSwizzle sw = w32 == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                            : w32 == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    if ((st = encode_map(&p.tm_a, a, 3, dims, str, box, sw))) return st;
+    if ((st = encode_map(&p.tm_b, b, 3, dims, str, box, sw))) return st;
+  }
+  p.ln_w = static_cast<const __half*>(w->ln_in_w);
+  p.ln_b = static_cast<const __half*>(w->ln_in_b);
+  p.bias = w->b_proj;
+  p.mask = static_cast<const __half*>(mask);
+  p.mask_sb = g.msb;
+  p.mask_si = g.msr;
+  p.mask_sj = g.msc;
+  p.rows = g.rows;
+  p.cols = g.cols;
+  p.ih = ih;
+  p.jw = jw;
+  p.log2_jw = 31 - __builtin_clz(static_cast<unsigned>(jw));
+  p.tiles_i = (g.rows + ih - 1) / ih;
+  p.tiles_j = (g.cols + jw - 1) / jw;
+  p.num_tiles = 4 * g.B * p.tiles_i * p.tiles_j;
+  p.reset_status = reset_status ? 1 : 0;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms & ~3);  // a multiple of 4: a CTA keeps one weight set
+  cudaError_t e = launch_pdl(kern, grid, k1w::kThreads, k1w::SMEM_BYTES, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch project_gate_w_kernel");
+}
+
+int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
+               float mix_eps, DeviceStatus* status, cudaStream_t stream) {
+  const uintptr_t bytes = static_cast<uintptr_t>(B) * rows * cols * 256 * 2;
+  const uintptr_t zi = reinterpret_cast<uintptr_t>(z), zo = reinterpret_cast<uintptr_t>(z_out);
+  if (zi < zo + bytes && zo < zi + bytes)
+    return fail(TMU_ERR_INVALID_ARGUMENT, "c_z = 256: z_out must not overlap z (two CTAs share each tile's z)");
+  const bool hb = w->b_emit != nullptr;
+  void (*kern)(k3w::Params) = hb ? k3w::emit_residual_w_kernel<true> : k3w::emit_residual_w_kernel<false>;
+  Dev dev;
+  int st = current_device(dev, 1u << (20 + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern), k3w::SMEM_BYTES);
+  if (st) return st;
+  if (dev.sms < 2) return fail(TMU_ERR_UNSUPPORTED, "fewer than 2 SMs");
+  k3w::Params p;
+  memset(&p, 0, sizeof(p));
+  int ih = 1, jw = 64;
+  choose_tile(rows, cols, ih, jw, k3w::TILE);
+  const uint64_t cp = row_pitch(cols);
+  {
+    const uint64_t dims[4] = {256, (uint64_t)cols, (uint64_t)rows, (uint64_t)B};
+    const uint64_t str[3] = {512, 512ull * cols, 512ull * cols * rows};
+    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, (uint64_t)B * 256};
+    const uint64_t str[2] = {cp * 2, cp * 2 * rows};
+    const uint32_t box[3] = {(uint32_t)jw, (uint32_t)ih, 256};
+    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+  }
+  {
+    const uint64_t dims[2] = {256, 256};
+    const uint64_t str[1] = {512};
+    const uint32_t box[2] = {64, 128};
+    if ((st = encode_map(&p.tm_we, w->w_emit, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_map(&p.tm_wg, w->w_gate, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  p.z = static_cast<const __half*>(z);
+  p.z_out = static_cast<__half*>(z_out);
+  p.ln_in_w = static_cast<const __half*>(w->ln_in_w);
+  p.ln_in_b = static_cast<const __half*>(w->ln_in_b);
+  p.ln_mix_w = static_cast<const __half*>(w->ln_mix_w);
+  p.ln_mix_b = static_cast<const __half*>(w->ln_mix_b);
+  p.b_emit = w->b_emit;
+  p.b_gate = w->b_gate;
+  p.mix_eps = mix_eps;
+  p.rows = rows;
+  p.cols = cols;
+  p.ih = ih;
+  p.jw = jw;
+  p.log2_jw = 31 - __builtin_clz(static_cast<unsigned>(jw));
+  p.tiles_i = (rows + ih - 1) / ih;
+  p.tiles_j = (cols + jw - 1) / jw;
+  p.num_tiles = 2 * B * p.tiles_i * p.tiles_j;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms & ~1);  // even: a CTA keeps one output half
+  cudaError_t e = launch_pdl(kern, grid, k3w::kThreads, k3w::SMEM_BYTES, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_w_kernel");
 }
 
 size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
@@ -501,7 +646,7 @@ int tmu_project_gate(const void* z, const void* mask, const tmu_trimul_weights* 
   if ((st = check_weights(w, true, false))) return st;
   if (!z || !a || !b || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   if (!aligned16(z) || !aligned16(a) || !aligned16(b)) return fail(TMU_ERR_MISALIGNED, "z/a/b not 16-byte aligned");
-  return launch_k1(z, mask, w, square_geom(B, L), a, b, static_cast<DeviceStatus*>(status),
+  return launch_k1(z, mask, w, square_geom(B, L, c_z), a, b, static_cast<DeviceStatus*>(status),
                    static_cast<cudaStream_t>(stream));
 }
 
@@ -523,7 +668,7 @@ int tmu_emit_residual(const void* x, const void* z, void* z_out, const tmu_trimu
   if (!aligned16(x) || !aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "x/z not 16-byte aligned");
   if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
   return launch_k3(x, z, z_out, w, B, L, L, mix_eps, static_cast<DeviceStatus*>(status),
-                   static_cast<cudaStream_t>(stream));
+                   static_cast<cudaStream_t>(stream), c_z);
 }
 
 int tmu_project_gate_ex(const void* z, const void* mask, const tmu_pair_layout* g, const tmu_trimul_weights* w,
@@ -538,7 +683,7 @@ int tmu_project_gate_ex(const void* z, const void* mask, const tmu_pair_layout* 
   if (g->stride_col % 8 || g->stride_row % 8 || g->stride_b % 8)
     return fail(TMU_ERR_MISALIGNED, "z strides must be multiples of 8 elements (16 bytes)");
   const PairGeom pg{g->B, g->rows, g->cols, g->stride_b, g->stride_row, g->stride_col,
-                    g->mask_stride_b, g->mask_stride_row, g->mask_stride_col};
+                    g->mask_stride_b, g->mask_stride_row, g->mask_stride_col, c_z};
   return launch_k1(z, mask, w, pg, a, b, static_cast<DeviceStatus*>(status), static_cast<cudaStream_t>(stream));
 }
 
@@ -563,7 +708,7 @@ int tmu_emit_residual_ex(const void* x, const void* z, void* z_out, int B, int r
   if (!aligned16(x) || !aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "x/z not 16-byte aligned");
   if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
   return launch_k3(x, z, z_out, w, B, rows, cols, mix_eps, static_cast<DeviceStatus*>(status),
-                   static_cast<cudaStream_t>(stream));
+                   static_cast<cudaStream_t>(stream), c_z);
 }
 
 int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z,
@@ -576,6 +721,7 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
   if (!aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "z not 16-byte aligned");
   if (workspace_bytes < tmu_workspace_bytes(B, L, c_z, c)) return fail(TMU_ERR_WORKSPACE_TOO_SMALL, "workspace too small");
   if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
+  if ((st = check_wide_alias(z, z_out, B, L, c_z))) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   DeviceStatus* status = reinterpret_cast<DeviceStatus*>(ws);
@@ -585,9 +731,9 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
   void* x = ws + TMU_STATUS_BYTES + 2 * cm;
   // K1 zeroes the status word after its dependency wait (no memset node between the kernels,
   // so the three launches chain with programmatic dependent launch)
-  if ((st = launch_k1(z, mask, w, square_geom(B, L), a, b, status, s, true))) return st;
+  if ((st = launch_k1(z, mask, w, square_geom(B, L, c_z), a, b, status, s, true))) return st;
   if ((st = launch_k2(a, b, x, B * c, L, L, L, L, outgoing != 0, status, s))) return st;
-  return launch_k3(x, z, z_out, w, B, L, L, mix_eps, status, s);
+  return launch_k3(x, z, z_out, w, B, L, L, mix_eps, status, s, c_z);
 }
 
 int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L,
@@ -598,6 +744,7 @@ int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_t
   if (!z || !z_out) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   if (!aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "z not 16-byte aligned");
   if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
+  if ((st = check_wide_alias(z, z_out, B, L, c_z))) return st;
   const size_t cm = cm_bytes(B, L, c);
   if (cm > kNoAllocBufBytes) {
     char buf[200];
@@ -617,9 +764,9 @@ int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_t
   void* x = base + TMU_STATUS_BYTES + 2 * kNoAllocBufBytes;
   // the status word must start at zero; a, b and x are fully rewritten before they are read
   if ((st = tmu_reset_status(dstat, stream))) return st;
-  if ((st = launch_k1(z, mask, w, square_geom(B, L), a, b, dstat, s))) return st;
+  if ((st = launch_k1(z, mask, w, square_geom(B, L, c_z), a, b, dstat, s))) return st;
   if ((st = launch_k2(a, b, x, B * c, L, L, L, L, outgoing != 0, dstat, s))) return st;
-  return launch_k3(x, z, z_out, w, B, L, L, mix_eps, dstat, s);
+  return launch_k3(x, z, z_out, w, B, L, L, mix_eps, dstat, s, c_z);
 }
 
 int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream) {

@@ -458,6 +458,82 @@ __device__ __forceinline__ void ln_row128_sw128(const uint8_t* src, uint8_t* dst
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// LayerNorm of a 256-channel row (four 128B-swizzled atoms of `atom_bytes` each), split over two
+// threads: thread `half` owns channels [128 half, 128 half + 128) = atoms 2 half, 2 half + 1.
+// Each computes the shifted partial sums of its half (shift k = the row's channel 0, read by
+// both), the caller adds the two halves, and each normalises its own half in place or to dst.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ float ln_row_shift(const uint8_t* src, int row) {
+  return __half2float(*reinterpret_cast<const __half*>(src + sw128_off(row, 0)));
+}
+
+__device__ __forceinline__ float2 ln_half_sums(const uint8_t* src, int atom_bytes, int row, int half, float k) {
+  const uint8_t* base = src + 2 * half * atom_bytes;
+  float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c16 = 0; c16 < 16; ++c16) {
+    const uint4 v = *reinterpret_cast<const uint4*>(base + (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7));
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      unsigned short lo, hi;
+      split_half2(u[e], lo, hi);
+      const float2 d = make_float2(add_f16_f32(lo, -k), add_f16_f32(hi, -k));
+      s1 = __fadd2_rn(s1, d);
+      s2 = __ffma2_rn(d, d, s2);
+    }
+  }
+  return make_float2(s1.x + s1.y, s2.x + s2.y);
+}
+
+// mean and 1/sqrt(var + eps) of a 256-channel row from the two halves' shifted sums
+__device__ __forceinline__ float2 ln256_moments(float2 a, float2 b, float k, float eps) {
+  const float m1 = (a.x + b.x) * (1.0f / 256);
+  const float var = fmaxf((a.y + b.y) * (1.0f / 256) - m1 * m1, 0.0f);
+  return make_float2(k + m1, rsqrtf(var + eps));
+}
+
+template <typename Par>
+__device__ __forceinline__ void ln_half_apply(const uint8_t* src, uint8_t* dst, int atom_bytes, int row, int half,
+                                              float mean, float rstd, Par par) {
+  const float2 r2 = make_float2(rstd, rstd);
+#pragma unroll
+  for (int c16 = 0; c16 < 16; ++c16) {
+    const int off = (2 * half + (c16 >> 3)) * atom_bytes + sw128_off(row, c16 & 7);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    float g[8], b[8];
+    par(16 * half + c16, g, b);
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      unsigned short lo, hi;
+      split_half2(u[e], lo, hi);
+      const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
+      const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
+      o[e] = pack_half2(y.x, y.y);
+    }
+    *reinterpret_cast<uint4*>(dst + off) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// gamma/beta from fp16 arrays in shared memory
+struct LnParSmemHalf {
+  const __half* g;
+  const __half* b;
+  __device__ __forceinline__ void operator()(int k, float (&gg)[8], float (&bb)[8]) const {
+    const uint4 gw = reinterpret_cast<const uint4*>(g)[k], bw = reinterpret_cast<const uint4*>(b)[k];
+    const uint32_t gu[4] = {gw.x, gw.y, gw.z, gw.w}, bu[4] = {bw.x, bw.y, bw.z, bw.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = unpack_half2(gu[e]), y = unpack_half2(bu[e]);
+      gg[2 * e] = x.x; gg[2 * e + 1] = x.y;
+      bb[2 * e] = y.x; bb[2 * e + 1] = y.y;
+    }
+  }
+};
+
 // gamma/beta from fp32 arrays in shared memory
 struct LnParSmem {
   const float* g;

@@ -171,13 +171,17 @@ def contract(a: torch.Tensor, b: torch.Tensor, L: int, outgoing: bool, status: t
 
 def emit_residual(x: torch.Tensor, z: torch.Tensor, w: TrimulWeights, mix_eps: float = MIX_EPS_FP16,
                   out: torch.Tensor | None = None, status: torch.Tensor | None = None):
-    """K3: z + fp16(LN_mix(x) @ w_emit) * sigmoid(fp16(LN(z) @ w_gate)); ``out`` may be ``z``."""
+    """K3: z + fp16(LN_mix(x) @ w_emit) * sigmoid(fp16(LN(z) @ w_gate)); ``out`` may be ``z``
+    (through a temporary when c_z = 256)."""
     lib = _lib.load()
     B, L = _check_pair(z, w.c_z)
     out = torch.empty_like(z) if out is None else out
+    dst = torch.empty_like(z) if w.c_z == 256 and _overlaps(z, out) else out
     status = new_status(z.device) if status is None else status
-    _lib.check(lib.tmu_emit_residual(_ptr(x), _ptr(z), _ptr(out), ctypes.byref(w.struct), B, L, w.c_z, w.c,
+    _lib.check(lib.tmu_emit_residual(_ptr(x), _ptr(z), _ptr(dst), ctypes.byref(w.struct), B, L, w.c_z, w.c,
                                      float(mix_eps), _ptr(status), _stream_ptr(z.device)), "tmu_emit_residual")
+    if dst is not out:
+        out.copy_(dst)
     return out
 
 
@@ -186,6 +190,7 @@ class Workspace:
 
     def __init__(self):
         self.buf: torch.Tensor | None = None
+        self.pair: torch.Tensor | None = None
 
     def get(self, B: int, L: int, c_z: int, c: int, device) -> torch.Tensor:
         need = int(_lib.load().tmu_workspace_bytes(B, L, c_z, c))
@@ -193,20 +198,38 @@ class Workspace:
             self.buf = torch.empty(need + 256, dtype=torch.uint8, device=device)
         return self.buf
 
+    def pair_like(self, z: torch.Tensor) -> torch.Tensor:
+        """A second pair buffer shaped like ``z`` (for updates that cannot run in place)."""
+        if self.pair is None or self.pair.shape != z.shape or self.pair.device != z.device:
+            self.pair = torch.empty_like(z)
+        return self.pair
+
     @property
     def status(self) -> torch.Tensor | None:
         return None if self.buf is None else self.buf[:_lib.TMU_STATUS_BYTES]
 
 
+def _overlaps(a: torch.Tensor, b: torch.Tensor) -> bool:
+    a0, b0 = a.data_ptr(), b.data_ptr()
+    return a0 < b0 + b.numel() * b.element_size() and b0 < a0 + a.numel() * a.element_size()
+
+
 def trimul(z: torch.Tensor, mask: torch.Tensor | None, w: TrimulWeights, outgoing: bool,
            mix_eps: float = MIX_EPS_FP16, out: torch.Tensor | None = None, workspace: Workspace | None = None):
-    """One triangle update: ``z + trimul(z)`` in fp16 (``out`` may be ``z`` for in-place)."""
+    """One triangle update: ``z + trimul(z)`` in fp16 (``out`` may be ``z`` for in-place).
+
+    The c_z = 256 kernels cannot write over their input (two CTAs share each tile's z), so an
+    in-place call there goes through the workspace's second pair buffer and a copy back."""
     lib = _lib.load()
     B, L = _check_pair(z, w.c_z)
     mask = _check_mask(mask, B, L)
     out = torch.empty_like(z) if out is None else out
-    ws = (workspace if workspace is not None else Workspace()).get(B, L, w.c_z, w.c, z.device)
-    _lib.check(lib.tmu_trimul(_ptr(z), _ptr(out), _ptr(mask), ctypes.byref(w.struct), B, L, w.c_z, w.c,
+    workspace = workspace if workspace is not None else Workspace()
+    ws = workspace.get(B, L, w.c_z, w.c, z.device)
+    dst = workspace.pair_like(z) if w.c_z == 256 and _overlaps(z, out) else out
+    _lib.check(lib.tmu_trimul(_ptr(z), _ptr(dst), _ptr(mask), ctypes.byref(w.struct), B, L, w.c_z, w.c,
                               1 if outgoing else 0, float(mix_eps), _ptr(ws), ws.numel(), _stream_ptr(z.device)),
                "tmu_trimul")
+    if dst is not out:
+        out.copy_(dst)
     return out

@@ -93,6 +93,18 @@ class DistExchange:
         return recv
 
 
+class LocalExchange:
+    """The exchange of a single rank (P = 1): the collectives are identities."""
+
+    size, rank = 1, 0
+
+    def all_gather(self, local):
+        return local.unsqueeze(0)
+
+    def all_to_all(self, send):
+        return send
+
+
 class RowShardedTrimul:
     """Triangle update of a pair tensor row-sharded over the ranks of ``group`` (B = 1).
 

@@ -75,8 +75,14 @@ def transition_(p: dict, z: torch.Tensor) -> torch.Tensor:
 def block_forward(p: dict, z: torch.Tensor, mask, mix_eps: float = ops.MIX_EPS_FP16,
                   workspace: ops.Workspace | None = None) -> torch.Tensor:
     """One PairUpdateBlock, updating fp16 ``z`` [B, L, L, c_z] in place."""
-    ops.trimul(z, mask, p["out"], True, mix_eps, out=z, workspace=workspace)
-    ops.trimul(z, mask, p["in"], False, mix_eps, out=z, workspace=workspace)
+    if z.shape[-1] == 256:  # the wide kernels write a second buffer: out z -> t, in t -> z
+        workspace = workspace if workspace is not None else ops.Workspace()
+        t = workspace.pair_like(z)
+        ops.trimul(z, mask, p["out"], True, mix_eps, out=t, workspace=workspace)
+        ops.trimul(t, mask, p["in"], False, mix_eps, out=z, workspace=workspace)
+    else:
+        ops.trimul(z, mask, p["out"], True, mix_eps, out=z, workspace=workspace)
+        ops.trimul(z, mask, p["in"], False, mix_eps, out=z, workspace=workspace)
     return transition_(p, z)
 
 

@@ -57,7 +57,8 @@ def test_workspace_size(lib):
 def test_argument_checks_need_no_gpu(lib):
     # shape / null checks run before any CUDA call
     W = ctypes.POINTER(_lib.TmuTrimulWeights)
-    assert lib.tmu_trimul(None, None, None, W(), 1, 64, 256, 256, 1, 1e-5, None, 0, None) == 4  # unsupported c
+    assert lib.tmu_trimul(None, None, None, W(), 1, 64, 192, 192, 1, 1e-5, None, 0, None) == 4  # unsupported c
+    assert lib.tmu_trimul(None, None, None, W(), 1, 64, 256, 128, 1, 1e-5, None, 0, None) == 4  # c != c_z
     assert lib.tmu_trimul(None, None, None, W(), 0, 64, 128, 128, 1, 1e-5, None, 0, None) == 1
     assert lib.tmu_contract(None, None, None, 0, 64, 1, None, None) == 1
     assert lib.tmu_contract(None, None, None, 1, 9000, 1, None, None) == 4

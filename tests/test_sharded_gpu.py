@@ -273,3 +273,19 @@ def test_row_sharded_two_nccl_ranks_match_oracle():
         assert "error" not in out[r], out[r]["error"]
     for d, (err, ulp) in out[0].items():
         assert err <= 4 * ulp, f"{d}: {err} vs ulp {ulp}"
+
+
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_row_sharded_emulated_ranks_wide_pair(outgoing):
+    """c_z = c = 256 through the same sharded driver (P = 2, L = 256)."""
+    P, L, cz = 2, 256, 256
+    direction = "out" if outgoing else "in"
+    trunk = FoldingTrunk(1, cz, cz, hidden=512, seed=41, ln_noise=0.1)
+    z = pair_tensor(1, L, cz, 40).half().float()
+    mask = pair_mask(1, L, 13)
+    tri = getattr(trunk.blocks[0], "tri_mul_" + direction)
+    w, p = ops.TrimulWeights.from_module(tri, DEV), orc.trimul_params(tri, True)
+    zd, md = z.half().to(DEV), mask.half().to(DEV)
+    got = _emulate(P, L, zd, md, w, outgoing).float().cpu()
+    ref16 = orc.trimul_fp16(p, z, mask, outgoing)
+    assert float((got - ref16).abs().max()) <= 4 * _ulp16(float(ref16.abs().max()))
