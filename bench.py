@@ -147,7 +147,8 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-WORKLOADS = ("c2", "c1", "c4", "L2048")
+WORKLOADS = ("c2", "c1", "c4", "L2048", "c5", "c2w", "L2048w")
+SHARDED_WORKLOADS = ("c5",)
 
 
 def _workload(rank: int, device, name: str = "c2"):
@@ -156,8 +157,8 @@ def _workload(rank: int, device, name: str = "c2"):
     from esmfold2_mlx_b200.synthetic import CONFIGS, FoldingTrunk, pair_mask, pair_tensor, trimul_biases
 
     cfg = CONFIGS[name]
-    trunk = FoldingTrunk(1, C_Z, C, seed=cfg.seed)
-    biases = {d: (trimul_biases(C_Z, C, cfg.seed + 31 + i) if cfg.biases else None)
+    trunk = FoldingTrunk(1, cfg.c_z, cfg.c, seed=cfg.seed)
+    biases = {d: (trimul_biases(cfg.c_z, cfg.c, cfg.seed + 31 + i) if cfg.biases else None)
               for i, d in enumerate(("out", "in"))}
     w = None
     if device is not None:
@@ -165,7 +166,7 @@ def _workload(rank: int, device, name: str = "c2"):
 
         w = {d: ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + d), device, biases[d])
              for d in ("out", "in")}
-    z = pair_tensor(cfg.B, cfg.L, C_Z, cfg.seed + rank).half()
+    z = pair_tensor(cfg.B, cfg.L, cfg.c_z, cfg.seed + rank).half()
     mask = pair_mask(cfg.B, cfg.L, cfg.n_pad).half() if cfg.n_pad else None
     return cfg, trunk, biases, w, z, mask
 
@@ -225,13 +226,13 @@ def run_reference(args, ws, rank, local):
 
 
 def _config_dict(cfg, ws):
-    return {"workload": cfg.name, "L": cfg.L, "B": cfg.B, "c_z": C_Z, "c": C, "directions": ["out", "in"],
+    return {"workload": cfg.name, "L": cfg.L, "B": cfg.B, "c_z": cfg.c_z, "c": cfg.c, "directions": ["out", "in"],
             "mask_pad": cfg.n_pad, "biases": cfg.biases, "parallelism": f"folds x{ws} (one fold group per GPU)",
             "l2": "flushed between steps (256 MiB write, outside the timed intervals)",
             "launch": "one CUDA graph per step"}
 
 
-def _kernel_costs(L: int, B: int, masked: bool):
+def _kernel_costs(L: int, B: int, masked: bool, C_Z: int = 128, C: int = 128):
     """Algorithmic bytes and FLOPs per launch of each kernel (one tri-mul)."""
     cells = B * L * L
     return {
@@ -290,6 +291,124 @@ def _trunk_recycle(device, flush, reps: int = 3):
             "output_finite": finite}
 
 
+def run_sharded(args, ws, rank, local):
+    """one fold of L = 3072, outgoing then incoming tri-mul, its rows split over
+    the N ranks (strong scaling: the total work is fixed).  Each rank projects its rows, the b
+    slabs are all-gathered (and, for the incoming form, z's column blocks exchanged all-to-all
+    first) over NCCL, and each rank contracts and finishes its rows.  Eager launches (no graph);
+    inputs per rank (>= 302 MB at N = 8) exceed L2, so no flush is needed between steps."""
+    from esmfold2_mlx_b200 import _lib, ops
+    from esmfold2_mlx_b200.sharded import DistExchange, LocalExchange, RowShardedTrimul
+    from esmfold2_mlx_b200.synthetic import CONFIGS, FoldingTrunk, pair_tensor
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
+    cfg = CONFIGS[args.workload]
+    L = cfg.L
+    trunk = FoldingTrunk(1, C_Z, C, seed=cfg.seed)
+    w = {d: ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + d), device) for d in ("out", "in")}
+
+    class TimedExchange(DistExchange if ws > 1 else LocalExchange):
+        """Records CUDA events around each collective so the step can be split into parts."""
+
+        marks: list = []
+
+        def all_gather(self, local_):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = super().all_gather(local_)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            self.marks.append((e0, e1))
+            return r
+
+        def all_to_all(self, send):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = super().all_to_all(send)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e1.record()
+            self.marks.append((e0, e1))
+            return r
+
+    ex = TimedExchange() if ws == 1 else TimedExchange(None)
+    sh = RowShardedTrimul(L, device=device, exchange=ex)
+    Lr = sh.Lr
+    z_host = pair_tensor(1, L, C_Z, cfg.seed).half()[:, rank * Lr:(rank + 1) * Lr].contiguous()
+    z0 = z_host.to(device)
+    z1 = torch.empty_like(z0)
+    z2 = torch.empty_like(z0)
+
+    def step(zin):
+        sh(zin, None, w["out"], True, out=z1)
+        return sh(z1, None, w["in"], False, out=z2)
+
+    for _ in range(max(3, args.warmup)):
+        step(z0)
+    torch.cuda.synchronize()
+    _barrier(ws)
+    ex.marks.clear()
+    sampler = ClockSampler(local)
+    sampler.start()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    _barrier(ws)
+    for e0, e1 in evs:
+        e0.record()
+        step(z0)
+        e1.record()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    clocks = sampler.stop()
+    step_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
+    comm_ms = sum(e0.elapsed_time(e1) for e0, e1 in ex.marks)
+    step_ms_max = _max_over_ranks(step_ms, ws, device)
+    comm_ms_max = _max_over_ranks(comm_ms, ws, device)
+    ms_per_step = step_ms_max / args.steps
+    cells = 2 * L * L
+    code, site = ops.read_status(sh.stages.status)
+    if code != 0:
+        raise RuntimeError(f"device status {code} at site {site:#x}")
+
+    # end to end: this rank's rows from pinned host memory and back, inside the interval
+    zh = z_host.pin_memory()
+    outh = torch.empty_like(z_host).pin_memory()
+    z_in = torch.empty_like(z0)
+    e2e_ms = 0.0
+    for i in range(args.steps + 1):
+        _barrier(ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        z_in.copy_(zh, non_blocking=True)
+        outh.copy_(step(z_in), non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        if i >= 1:
+            e2e_ms += e0.elapsed_time(e1)
+    e2e_ms = _max_over_ranks(e2e_ms, ws, device) / args.steps
+    pitch = ops.row_pitch(L)
+    # bytes each rank receives per step: (P-1)/P of b for both directions, plus z's column blocks
+    recv = (ws - 1) * (2 * C * Lr * pitch * 2 + Lr * Lr * C_Z * 2)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": cells / (ms_per_step * 1e-3), "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": cfg.name, "L": L, "B": 1, "c_z": C_Z, "c": C, "directions": ["out", "in"],
+                       "parallelism": f"rows x{ws} (row-sharded fold; NCCL all-gather of b, all-to-all of z blocks)",
+                       "l2": "inputs larger than L2 (no flush)", "launch": "eager"},
+            "e2e": {"value": cells / (e2e_ms * 1e-3), "unit": UNIT,
+                    "h2d_bytes_per_step": zh.numel() * 2, "d2h_bytes_per_step": outh.numel() * 2,
+                    "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": 6 * args.steps,
+            "collectives": {"ms_per_step": round(comm_ms_max / args.steps, 4), "recv_bytes_per_rank_per_step": recv,
+                            "note": "CUDA-event span of each collective on the compute stream, max over ranks"},
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_b200(args, ws, rank, local):
     from esmfold2_mlx_b200 import _lib, ops
 
@@ -298,6 +417,7 @@ def run_b200(args, ws, rank, local):
     _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
     cfg, trunk, biases, w, z_host, mask_host = _workload(rank, device, args.workload)
     L, B = cfg.L, cfg.B
+    C_Z, C = cfg.c_z, cfg.c  # noqa: N806 - the pair and latent widths of this workload
     cells_per_step = 2 * B * L * L
     stream = torch.cuda.Stream(device)
     torch.cuda.set_stream(stream)
@@ -394,7 +514,7 @@ def run_b200(args, ws, rank, local):
     share = {n: ktime[n] / sum(ktime.values()) for n in names}
     dom = max(names, key=lambda n: ktime[n])
     hbm, tflops, peak_kind = _peaks()
-    costs = _kernel_costs(L, B, mask is not None)
+    costs = _kernel_costs(L, B, mask is not None, C_Z, C)
     kernels = {}
     for n in names:
         t = kavg[n] * 1e-3
@@ -480,7 +600,8 @@ def main():
     ap.add_argument("--no-trunk", action="store_true", help="skip the trunk-recycle (config 3) measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--workload", choices=WORKLOADS, default="c2",
-                    help="c2 (default: the metric's configuration), c1, c4 (64 folds x L=146), L2048")
+                    help="c2 (default: the metric's configuration), c1, c4 (64 folds x L=146), L2048, "
+                         "c5 (one L=3072 fold row-sharded over the N ranks), c2w / L2048w (c_z = c = 256)")
     args = ap.parse_args()
     ws, rank, local = _dist()
     if args.impl == "reference":
@@ -488,7 +609,10 @@ def main():
         return
     _init_pg(ws, local, "nccl")
     try:
-        run_b200(args, ws, rank, local)
+        if args.workload in SHARDED_WORKLOADS:
+            run_sharded(args, ws, rank, local)
+        else:
+            run_b200(args, ws, rank, local)
     finally:
         if ws > 1:
             import torch.distributed as dist

@@ -9,17 +9,19 @@
 // x column and z row (the LayerNorms are computed twice).  Because the sibling CTA reads all of
 // z's channels while this one writes its half of z', z_out must not alias z (the host rejects it).
 //
-// One tile = 64 positions; D = W X^T with M = 128 output channels (TMEM lane = channel),
-// N = 64 positions, K = 256: emit into columns [0, 64) of a slot, gate into [64, 128).
+// One tile = 32 positions (small enough that every buffer is double-buffered next to the
+// resident weights); D = W X^T with M = 128 output channels (TMEM lane = channel), N = 32
+// positions, K = 256: emit into columns [0, 32) of a 64-column slot, gate into [32, 64).
 // CTA = 14 warps, persistent:
-//   warp 0      TMA: weights once; per tile the x tile (channel-major, 32 KB, one stage) and the
-//               z tile (position-major 128B-swizzled, 2 stages)
-//   warp 1      TMEM (2 slots x 128 columns) + MMA thread
-//   warps 2-5   A1 = fp16(LN_mix(x column)) written over the x tile (transposed in registers)
-//   warps 6-9   A2 = fp16(LN_in(z row)) in place over the z tile (the MMA's operand)
-//   warps 10-13 epilogue, one TMEM lane quadrant (warp mod 4: 32 channels) each: z' = z + m * sigmoid(g) with
-//               z re-read from global memory (L2-resident: the tile was just loaded) and z'
-//               stored from registers (64 contiguous bytes per warp and position).
+//   warp 0      TMA: weights once; per tile the x tile (channel-major, 16 KB) and the z tile
+//               (position-major, 128B-swizzled, 16 KB), 2 stages each
+//   warp 1      TMEM (4 slots x 64 columns) + MMA thread
+//   warps 2-5   A1 = fp16(LN_mix(x column)) over the x tile, one 64-channel atom per warp:
+//               each thread gathers its row's 64 channels, the group meets, the rows are written
+//               back K-major swizzled, the four partial sums are combined through shared memory
+//   warps 6-9   A2 = fp16(LN_in(z row)) into its own 2-stage buffer (z stays for the residual)
+//   warps 10-13 epilogue, TMEM lane quadrant warp mod 4 (32 channels each): z' = z + m*sigmoid(g)
+//               computed over the z tile's half-h atoms in shared memory, then TMA-stored.
 #pragma once
 
 #include "tmu_common.cuh"
@@ -29,17 +31,19 @@ namespace k3w {
 
 constexpr int CZ = 256;
 constexpr int CC = 256;
-constexpr int TILE = 64;
-constexpr int ATOM_BYTES = TILE * 128;          // activation atoms: 64 rows x 128 B
+constexpr int TILE = 32;
+constexpr int ATOM_BYTES = TILE * 128;          // activation atoms: 32 rows x 128 B
 constexpr int WATOM_BYTES = 128 * 128;          // weight atoms: 128 rows x 128 B
 constexpr int WBLOCK_BYTES = 128 * 256 * 2;     // 128 rows x K = 256
-constexpr int TILE_BYTES = TILE * 256 * 2;      // 64 positions x 256 channels
+constexpr int TILE_BYTES = TILE * 256 * 2;      // 32 positions x 256 channels
+constexpr int NSLOT = 4;
 constexpr int OFF_WE = 0;
 constexpr int OFF_WG = OFF_WE + WBLOCK_BYTES;
-constexpr int OFF_X = OFF_WG + WBLOCK_BYTES;    // one stage: the x tile, then A1 in place
-constexpr int OFF_Z = OFF_X + TILE_BYTES;       // two stages: the z tile, then A2 in place
-constexpr int OFF_RED = OFF_Z + 2 * TILE_BYTES; // float2 [2][64]: half-row exchange (mix, in)
-constexpr int OFF_BAR = OFF_RED + 2 * TILE * 8;
+constexpr int OFF_X = OFF_WG + WBLOCK_BYTES;     // 2 stages: the x tile, then A1 in place
+constexpr int OFF_Z = OFF_X + 2 * TILE_BYTES;    // 2 stages: the z tile, then z' (half h) in place
+constexpr int OFF_A2 = OFF_Z + 2 * TILE_BYTES;   // 2 stages: LN_in(z)
+constexpr int OFF_RED = OFF_A2 + 2 * TILE_BYTES; // float2 [2 groups][4 parts][32 rows]
+constexpr int OFF_BAR = OFF_RED + 2 * 4 * TILE * 8;
 constexpr int SMEM_BYTES = OFF_BAR + 256;
 constexpr int kThreads = 448;
 constexpr int TMEM_COLS = 256;
@@ -47,11 +51,10 @@ static_assert(SMEM_BYTES <= 232448, "K3W shared memory exceeds the per-block lim
 
 struct Params {
   CUtensorMap tm_z;   // z [B, rows, cols, 256]: box {64, jw, ih, 1}, 128B swizzle (load)
+  CUtensorMap tm_zo;  // z_out, same geometry (store)
   CUtensorMap tm_x;   // x [B*256, rows, pitch]: box {jw, ih, 256}, no swizzle (load)
   CUtensorMap tm_we;  // w_emit [256, 256]: box {64, 128}
   CUtensorMap tm_wg;  // w_gate [256, 256]: box {64, 128}
-  const __half* z;    // [B, rows, cols, 256] contiguous (residual)
-  __half* z_out;      // same shape; must not alias z
   const __half* ln_in_w;
   const __half* ln_in_b;
   const __half* ln_mix_w;
@@ -59,7 +62,7 @@ struct Params {
   const float* b_emit;  // [256] or null
   const float* b_gate;  // [256] or null
   float mix_eps;
-  int rows, cols, ih, jw, log2_jw, tiles_i, tiles_j, num_tiles;  // num_tiles = 2 x position tiles
+  int rows, cols, ih, jw, tiles_i, tiles_j, num_tiles;  // num_tiles = 2 x position tiles
   DeviceStatus* status;
   unsigned long long timeout_ns;
 };
@@ -80,7 +83,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 
 template <bool HAS_BIAS>
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __grid_constant__ Params p) {
-  constexpr uint32_t IDESC = idesc_f16_f32(128, 64, false, false);
+  constexpr uint32_t IDESC = idesc_f16_f32(128, TILE, false, false);
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x31f;
@@ -88,18 +91,19 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t& w_bar = bars[0];
-  uint64_t& xfull = bars[1];
-  uint64_t& xempty = bars[2];
-  uint64_t& a1full = bars[3];
-  uint64_t* zfull = bars + 4;
-  uint64_t* zempty = bars + 6;
-  uint64_t* a2full = bars + 8;
-  uint64_t* tfull = bars + 10;
-  uint64_t* tempty = bars + 12;
-  uint64_t& drain_bar = bars[14];
-  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 15);
-  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 15) + 4);
-  volatile int* ok_sh = reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 16));  // [2]
+  uint64_t* xfull = bars + 1;
+  uint64_t* xempty = bars + 3;
+  uint64_t* zfull = bars + 5;
+  uint64_t* zempty = bars + 7;
+  uint64_t* a1full = bars + 9;
+  uint64_t* a2full = bars + 11;
+  uint64_t* a2empty = bars + 13;
+  uint64_t* tfull = bars + 15;
+  uint64_t* tempty = bars + 19;
+  uint64_t& drain_bar = bars[23];
+  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 24);
+  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 24) + 4);
+  volatile int* ok_sh = reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 25));  // [3]
   float2* red = reinterpret_cast<float2*>(smem + OFF_RED);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -109,13 +113,16 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
   if (threadIdx.x == 0) {
     abort_sh = 0;
     mbar_init(&w_bar, 1);
-    mbar_init(&xfull, 1);
-    mbar_init(&xempty, 1);
-    mbar_init(&a1full, 4);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);   // the MMA that read A1
       mbar_init(&zfull[s], 1);
-      mbar_init(&zempty[s], 1);
-      mbar_init(&a2full[s], 4);
+      mbar_init(&zempty[s], 1);   // the epilogue's store of z' has read the stage
+      mbar_init(&a1full[s], 4);   // the four LN_mix warps
+      mbar_init(&a2full[s], 4);   // the four LN_in warps
+      mbar_init(&a2empty[s], 1);  // the MMA that read A2
+    }
+    for (int s = 0; s < NSLOT; ++s) {
       mbar_init(&tfull[s], 1);
       mbar_init(&tempty[s], 4);
     }
@@ -124,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&p.tm_z);
+    tma_prefetch_desc(&p.tm_zo);
     tma_prefetch_desc(&p.tm_x);
     tma_prefetch_desc(&p.tm_we);
     tma_prefetch_desc(&p.tm_wg);
@@ -159,9 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
         for (int a = 0; a < 4; ++a)
           tma_load_4d(smem + OFF_Z + s * TILE_BYTES + a * ATOM_BYTES, &p.tm_z, &zfull[s], a * 64, j0, i0, bb);
         ++nz;
-        if (!mbar_wait(&xempty, (it & 1) ^ 1, ctx, kSiteProdX)) break;
-        mbar_arrive_expect_tx(&xfull, TILE_BYTES);
-        tma_load_3d(smem + OFF_X, &p.tm_x, &xfull, j0, i0, bb * CC);
+        if (!mbar_wait(&xempty[s], ph ^ 1, ctx, kSiteProdX)) break;
+        mbar_arrive_expect_tx(&xfull[s], TILE_BYTES);
+        tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
         ++nx;
       }
       if (abort_sh) {
@@ -169,8 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
         for (uint32_t s = 0; s < 2; ++s) {
           const uint32_t nza = nz > s ? (nz - s + 1) / 2 : 0;
           if (nza) mbar_drain(&zfull[s], (nza - 1) & 1, 200000000ull);
+          const uint32_t nxa = nx > s ? (nx - s + 1) / 2 : 0;
+          if (nxa) mbar_drain(&xfull[s], (nxa - 1) & 1, 200000000ull);
         }
-        if (nx) mbar_drain(&xfull, (nx - 1) & 1, 200000000ull);
       }
     }
   } else if (warp == 1) {
@@ -178,16 +187,17 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
     if (lane == 0) {
       bool ok = mbar_wait(&w_bar, 0, ctx, kSiteMmaW);
       uint32_t it = 0;
-      const uint32_t a1 = smem_u32(smem + OFF_X);
       const uint32_t we = smem_u32(smem + OFF_WE), wg = smem_u32(smem + OFF_WG);
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t s = it & 1, ph = (it >> 1) & 1;
-        if (!mbar_wait(&a1full, it & 1, ctx, kSiteMmaA)) break;
+        const uint32_t slot = it & 3, sph = (it >> 2) & 1;
+        if (!mbar_wait(&a1full[s], ph, ctx, kSiteMmaA)) break;
         if (!mbar_wait(&a2full[s], ph, ctx, kSiteMmaA)) break;
-        if (!mbar_wait(&tempty[s], ph ^ 1, ctx, kSiteMmaT)) break;
+        if (!mbar_wait(&tempty[slot], sph ^ 1, ctx, kSiteMmaT)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + s * 128;
-        const uint32_t a2 = smem_u32(smem + OFF_Z + s * TILE_BYTES);
+        const uint32_t d = tmem_base + slot * 64;
+        const uint32_t a1 = smem_u32(smem + OFF_X + s * TILE_BYTES);
+        const uint32_t a2 = smem_u32(smem + OFF_A2 + s * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
           const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
@@ -197,12 +207,12 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
           const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
-          umma_f16(d + 64, sdesc_sw128(wg + ka * WATOM_BYTES + kb, 16, 1024),
+          umma_f16(d + TILE, sdesc_sw128(wg + ka * WATOM_BYTES + kb, 16, 1024),
                    sdesc_sw128(a2 + ka * ATOM_BYTES + kb, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&xempty);     // A1 has been read
-        umma_commit(&zempty[s]);  // A2 has been read (the epilogue takes z from global memory)
-        umma_commit(&tfull[s]);
+        umma_commit(&xempty[s]);   // A1 has been read
+        umma_commit(&a2empty[s]);  // A2 has been read
+        umma_commit(&tfull[slot]);
       }
       umma_commit(&drain_bar);
       mbar_drain(&drain_bar, 0, 200000000ull);
@@ -212,102 +222,133 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
     const bool mix = warp < 6;
     const int grp = mix ? 0 : 1;
     const int t = threadIdx.x - (mix ? 64 : 192);
-    const int row = t & 63, half = t >> 6;
+    const int row = t & 31, part = t >> 5;  // part = this warp's 64-channel atom
     const uint32_t bar_id = 1 + grp;
-    float2* rd = red + grp * TILE;
+    float2* rd = red + grp * 4 * TILE;
     const LnParHalf par = mix ? LnParHalf{p.ln_mix_w, p.ln_mix_b} : LnParHalf{p.ln_in_w, p.ln_in_b};
     const float eps = mix ? p.mix_eps : 1e-5f;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
       // one thread waits (bounded) and shares the verdict, so the group meets at every barrier
-      if (t == 0) ok_sh[grp] = (mix ? mbar_wait(&xfull, it & 1, ctx, kSiteMix) : mbar_wait(&zfull[s], ph, ctx, kSiteIn)) ? 1 : 0;
+      if (t == 0) {
+        bool ok;
+        if (mix) {
+          ok = mbar_wait(&xfull[s], ph, ctx, kSiteMix);
+        } else {
+          ok = mbar_wait(&a2empty[s], ph ^ 1, ctx, kSiteIn);
+          ok = ok && mbar_wait(&zfull[s], ph, ctx, kSiteIn);
+        }
+        ok_sh[grp] = ok ? 1 : 0;
+      }
       named_bar_sync(bar_id, 128);
       if (!ok_sh[grp]) break;
-      uint8_t* A = mix ? smem + OFF_X : smem + OFF_Z + s * TILE_BYTES;
+      uint8_t* src;
+      uint8_t* dst;
       if (mix) {
-        // The x tile is [channel][position] (128 B per channel).  A1's atom a occupies exactly
-        // the bytes of x channels [64a, 64a+64): gather this row's 64 channels of atom a into
-        // registers, meet, write them back as the swizzled K-major row (two rounds, atoms
-        // {r, r + 2}, so a round never overwrites what the other round still reads).
+        // The x tile is [channel][position] (64 B per channel).  A1's atom a occupies exactly
+        // the bytes of x channels [64a, 64a+64): gather this row's 64 channels of this warp's
+        // atom, meet, and write them back as the swizzled K-major row.
+        uint8_t* A = smem + OFF_X + s * TILE_BYTES;
         const __half* X = reinterpret_cast<const __half*>(A);
-#pragma unroll 1
-        for (int r2 = 0; r2 < 2; ++r2) {
-          const int a = 2 * half + r2;
-          uint32_t u[32];
+        uint32_t u[32];
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int ch = 64 * a + 2 * k;
-            __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
-            u[k] = *reinterpret_cast<uint32_t*>(&h2);
-          }
-          named_bar_sync(bar_id, 128);
-#pragma unroll
-          for (int c16 = 0; c16 < 8; ++c16)
-            *reinterpret_cast<uint4*>(A + a * ATOM_BYTES + sw128_off(row, c16)) =
-                make_uint4(u[4 * c16], u[4 * c16 + 1], u[4 * c16 + 2], u[4 * c16 + 3]);
+        for (int k = 0; k < 32; ++k) {
+          const int ch = 64 * part + 2 * k;
+          __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
+          u[k] = *reinterpret_cast<uint32_t*>(&h2);
         }
+        named_bar_sync(bar_id, 128);
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16)
+          *reinterpret_cast<uint4*>(A + part * ATOM_BYTES + sw128_off(row, c16)) =
+              make_uint4(u[4 * c16], u[4 * c16 + 1], u[4 * c16 + 2], u[4 * c16 + 3]);
         named_bar_sync(bar_id, 128);  // every row's channel 0 (the shift) is in place
+        src = dst = A;
+      } else {
+        src = smem + OFF_Z + s * TILE_BYTES;
+        dst = smem + OFF_A2 + s * TILE_BYTES;
       }
-      const float shift = ln_row_shift(A, row);
-      const float2 sums = ln_half_sums(A, ATOM_BYTES, row, half, shift);
-      if (half) rd[row] = sums;
+      const float shift = ln_row_shift(src, row);
+      rd[part * TILE + row] = ln_atom_sums(src, ATOM_BYTES, row, part, shift);
       named_bar_sync(bar_id, 128);
-      if (!half) rd[row] = ln256_moments(sums, rd[row], shift, eps);
-      named_bar_sync(bar_id, 128);
-      const float2 mr = rd[row];
-      ln_half_apply(A, A, ATOM_BYTES, row, half, mr.x, mr.y, par);
+      const float2 s0 = rd[row], s1 = rd[TILE + row], s2 = rd[2 * TILE + row], s3 = rd[3 * TILE + row];
+      const float2 mr = ln256_moments(make_float2(s0.x + s1.x, s0.y + s1.y), make_float2(s2.x + s3.x, s2.y + s3.y),
+                                      shift, eps);
+      ln_atom_apply(src, dst, ATOM_BYTES, row, part, mr.x, mr.y, par);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(mix ? &a1full : &a2full[s]);
+      if (lane == 0) mbar_arrive(mix ? &a1full[s] : &a2full[s]);
     }
   } else {
     // ---------------- epilogue ----------------
-    const int q = warp & 3;                   // TMEM lane quadrant this warp may access
-    const int ch = hsel * 128 + q * 32 + lane;  // this thread's output channel
+    const int q = warp & 3;                       // TMEM lane quadrant this warp may access
+    const int ch = hsel * 128 + q * 32 + lane;    // this thread's output channel
+    const uint32_t zoff = (ch >> 6) * ATOM_BYTES + (ch & 7) * 2;  // + sw128_off(position, chunk)
+    const uint32_t chunk = (ch & 63) >> 3;
     float be = 0.f, bgv = 0.f;
     if (HAS_BIAS) {
       be = __ldg(p.b_emit + ch);
       bgv = __ldg(p.b_gate + ch);
     }
+    const float2 be2 = make_float2(be, be), bg2 = make_float2(bgv, bgv);
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
-      if (!warp_wait(&tfull[s], ph, ctx, kSiteEpilogue)) break;
+      const uint32_t slot = it & 3, sph = (it >> 2) & 1;
+      if (warp == 10 && lane == 0) {
+        bool ok = mbar_wait(&tfull[slot], sph, ctx, kSiteEpilogue);
+        ok = ok && mbar_wait(&zfull[s], ph, ctx, kSiteEpilogue);
+        ok_sh[2] = ok ? 1 : 0;
+      }
+      named_bar_sync(3, 128);
+      if (!ok_sh[2]) break;
       tc_fence_after();
-      const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + s * 128;
+      uint8_t* Zs = smem + OFF_Z + s * TILE_BYTES;
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 64;
 #pragma unroll 1
       for (int pb = 0; pb < TILE; pb += 16) {
         uint32_t em[16], gt[16];
         tmem_ld16(trow + pb, em);
-        tmem_ld16(trow + 64 + pb, gt);
+        tmem_ld16(trow + TILE + pb, gt);
         tmem_wait_ld16x2(em, gt);
-        if (pb == TILE - 16) {
+        if (pb == TILE - 16) {  // the slot has been read: hand it back to the MMA
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[s]);
+          if (lane == 0) mbar_arrive(&tempty[slot]);
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int tp = pb + i;
-          const int gi = i0 + (tp >> p.log2_jw), gj = j0 + (tp & (p.jw - 1));
-          if (gi < p.rows && gj < p.cols) {
-            const size_t idx = ((static_cast<size_t>(bb) * p.rows + gi) * p.cols + gj) * CZ + ch;
-            float m = __uint_as_float(em[i]), g = __uint_as_float(gt[i]);
-            if (HAS_BIAS) {
-              m += be;
-              g += bgv;
-            }
-            m = round_f16(m);  // mixed and g are fp16 tensors in the reference
-            g = round_f16(g);
-            const float zn = fmaf(m, sigmoid_f32(g), __half2float(p.z[idx]));
-            p.z_out[idx] = __float2half_rn(zn);
+        for (int i = 0; i < 16; i += 2) {
+          __half* z0 = reinterpret_cast<__half*>(Zs + zoff + sw128_off(pb + i, chunk));
+          __half* z1 = reinterpret_cast<__half*>(Zs + zoff + sw128_off(pb + i + 1, chunk));
+          float2 m = make_float2(__uint_as_float(em[i]), __uint_as_float(em[i + 1]));
+          float2 g = make_float2(__uint_as_float(gt[i]), __uint_as_float(gt[i + 1]));
+          if (HAS_BIAS) {
+            m = __fadd2_rn(m, be2);
+            g = __fadd2_rn(g, bg2);
           }
+          m = round_f16x2(m);  // mixed and g are fp16 tensors in the reference
+          g = round_f16x2(g);
+          const float2 zn = __ffma2_rn(m, sigmoid_f32x2(g), make_float2(__half2float(*z0), __half2float(*z1)));
+          *z0 = __float2half_rn(zn.x);
+          *z1 = __float2half_rn(zn.y);
         }
       }
+      fence_proxy_async_smem();  // z' (generic-proxy writes) -> visible to the TMA store
+      named_bar_sync(3, 128);
+      if (warp == 10 && lane == 0) {
+        for (int k = 0; k < 2; ++k) {
+          const int a = 2 * hsel + k;
+          tma_store_4d(&p.tm_zo, Zs + a * ATOM_BYTES, a * 64, j0, i0, bb);
+        }
+        bulk_commit();
+        bulk_wait_read<0>();
+        mbar_arrive(&zempty[s]);
+      }
     }
+    if (warp == 10 && lane == 0) bulk_wait<0>();
   }
 
   tc_fence_before();

@@ -460,7 +460,7 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
   if (dev.sms < 2) return fail(TMU_ERR_UNSUPPORTED, "fewer than 2 SMs");
   k3w::Params p;
   memset(&p, 0, sizeof(p));
-  int ih = 1, jw = 64;
+  int ih = 1, jw = 32;
   choose_tile(rows, cols, ih, jw, k3w::TILE);
   const uint64_t cp = row_pitch(cols);
   {
@@ -468,6 +468,7 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
     const uint64_t str[3] = {512, 512ull * cols, 512ull * cols * rows};
     const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
     if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
     const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, (uint64_t)B * 256};
@@ -482,8 +483,6 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
     if ((st = encode_map(&p.tm_we, w->w_emit, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
     if ((st = encode_map(&p.tm_wg, w->w_gate, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
-  p.z = static_cast<const __half*>(z);
-  p.z_out = static_cast<__half*>(z_out);
   p.ln_in_w = static_cast<const __half*>(w->ln_in_w);
   p.ln_in_b = static_cast<const __half*>(w->ln_in_b);
   p.ln_mix_w = static_cast<const __half*>(w->ln_mix_w);
@@ -495,7 +494,6 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
   p.cols = cols;
   p.ih = ih;
   p.jw = jw;
-  p.log2_jw = 31 - __builtin_clz(static_cast<unsigned>(jw));
   p.tiles_i = (rows + ih - 1) / ih;
   p.tiles_j = (cols + jw - 1) / jw;
   p.num_tiles = 2 * B * p.tiles_i * p.tiles_j;

@@ -518,6 +518,51 @@ __device__ __forceinline__ void ln_half_apply(const uint8_t* src, uint8_t* dst, 
   }
 }
 
+// The same split four ways: thread `part` owns the single atom `part` (channels [64 part,
+// 64 part + 64)) of a 256-channel row; the caller adds the four partial sums.
+__device__ __forceinline__ float2 ln_atom_sums(const uint8_t* src, int atom_bytes, int row, int part, float k) {
+  const uint8_t* base = src + part * atom_bytes;
+  float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int c16 = 0; c16 < 8; ++c16) {
+    const uint4 v = *reinterpret_cast<const uint4*>(base + sw128_off(row, c16));
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      unsigned short lo, hi;
+      split_half2(u[e], lo, hi);
+      const float2 d = make_float2(add_f16_f32(lo, -k), add_f16_f32(hi, -k));
+      s1 = __fadd2_rn(s1, d);
+      s2 = __ffma2_rn(d, d, s2);
+    }
+  }
+  return make_float2(s1.x + s1.y, s2.x + s2.y);
+}
+
+template <typename Par>
+__device__ __forceinline__ void ln_atom_apply(const uint8_t* src, uint8_t* dst, int atom_bytes, int row, int part,
+                                              float mean, float rstd, Par par) {
+  const float2 r2 = make_float2(rstd, rstd);
+#pragma unroll
+  for (int c16 = 0; c16 < 8; ++c16) {
+    const int off = part * atom_bytes + sw128_off(row, c16);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    float g[8], b[8];
+    par(8 * part + c16, g, b);
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      unsigned short lo, hi;
+      split_half2(u[e], lo, hi);
+      const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
+      const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
+      o[e] = pack_half2(y.x, y.y);
+    }
+    *reinterpret_cast<uint4*>(dst + off) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // gamma/beta from fp16 arrays in shared memory
 struct LnParSmemHalf {
   const __half* g;

@@ -1,10 +1,10 @@
 """Run one triangle update (or one of its kernels) at a chosen size, for profilers.
 
     python -m esmfold2_mlx_b200.profile_case --L 1024 [--B 1] [--direction out|in]
-           [--stage all|k1|k2|k3] [--reps 3] [--mask-pad 0]
+           [--stage all|k1|k2|k3] [--reps 3] [--mask-pad 0] [--cz 128|256]
 
 Inputs are seeded synthetic tensors (``synthetic``); weights are random-init.  The chosen stage
-is launched ``--reps`` times after one untimed launch of every stage, then the script checks the
+is launched ``--reps`` times after one untimed launch of every stage (and one more of itself), then the script checks the
 device status word and prints the mean CUDA-event time per launch.  Use ``ncu -k regex:<name>``
 with ``project_gate``, ``contract`` or ``emit_residual`` to select a kernel.
 """
@@ -27,14 +27,15 @@ def main():
     ap.add_argument("--stage", choices=["all", "k1", "k2", "k3"], default="all")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--mask-pad", type=int, default=0)
+    ap.add_argument("--cz", type=int, choices=[128, 256], default=128, help="c_z = c")
     args = ap.parse_args()
 
     dev = torch.device("cuda", 0)
     _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
     L, B = args.L, args.B
-    trunk = FoldingTrunk(1, 128, 128, seed=0)
+    trunk = FoldingTrunk(1, args.cz, args.cz, seed=0)
     w = ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + args.direction), dev)
-    z = pair_tensor(B, L, 128, 0).half().to(dev)
+    z = pair_tensor(B, L, args.cz, 0).half().to(dev)
     mask = pair_mask(B, L, args.mask_pad).half().to(dev) if args.mask_pad else None
     outgoing = args.direction == "out"
     status = ops.new_status(dev)
@@ -51,6 +52,8 @@ def main():
         "all": lambda: ops.trimul(z, mask, w, outgoing, out=out),
     }
     fn = stages[args.stage]
+    fn()  # warm-up: the stage's own output allocations happen here, outside the timed launches
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.reps):
@@ -61,7 +64,7 @@ def main():
     if code != 0:
         raise SystemExit(f"device status {code} at site {site:#x}")
     ms = e0.elapsed_time(e1) / max(1, args.reps)
-    print(f"L={L} B={B} {args.direction} stage={args.stage}: {ms * 1e3:.1f} us per launch")
+    print(f"L={L} B={B} c_z={args.cz} {args.direction} stage={args.stage}: {ms * 1e3:.1f} us per launch")
 
 
 if __name__ == "__main__":

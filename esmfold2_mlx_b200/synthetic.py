@@ -167,4 +167,8 @@ CONFIGS = {
     "c4": Config("c4_64x_L146_out_in", L=146, B=64, seed=100, directions=("out", "in")),
     "c5": Config("c5_L3072_out_in", L=3072, seed=3, directions=("out", "in")),
     "L2048": Config("L2048_out_in", L=2048, seed=4, directions=("out", "in")),
+    # c_z = c = 256, the width of ESMFold2's released trunk, on config 2's and L2048's shapes
+    "c2w": Config("c2w_L238_cz256_out_in_mask_bias", L=238, c_z=256, c=256, seed=1, n_pad=24, biases=True,
+                  directions=("out", "in")),
+    "L2048w": Config("L2048w_cz256_out_in", L=2048, c_z=256, c=256, seed=4, directions=("out", "in")),
 }
