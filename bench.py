@@ -285,9 +285,37 @@ def _trunk_recycle(device, flush, reps: int = 3):
     L = cfg.L
     cells = 2 * cfg.blocks * L * L  # tri-mul pair cells per recycle
     del g
+
+    # K4 alone: the fused transition of block 0, 20 launches in one graph on an L2-flushed z
+    from esmfold2_mlx_b200 import ops
+
+    tw = mod.params[0]["tw"]
+    zt = z0.half().contiguous()
+    st = ops.new_status(device)
+    ops.transition(zt, tw, out=zt, status=st)
+    gk = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gk):
+        for _ in range(20):
+            ops.transition(zt, tw, out=zt, status=st)
+    flush.zero_()
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record()
+    gk.replay()
+    k1.record()
+    k1.synchronize()
+    k4_us = k0.elapsed_time(k1) * 1e3 / 20
+    del gk
+    hbm, tflops, _ = _peaks()
+    k4_flops = L * L * 2 * 2 * C_Z * tw.hidden * (1.5 if tw.activation == "swiglu" else 1.0)
+    k4_bytes = L * L * 2 * 2 * C_Z
     return {"workload": cfg.name, "L": L, "blocks": cfg.blocks, "recycles": cfg.recycles,
             "ms_per_recycle": round(per_recycle, 4), "trimul_pair_cells_per_s": cells / (per_recycle * 1e-3),
-            "roofline_ms_per_recycle": 2.4, "transition": "ReLU 128->512->128, torch on the GPU (cuBLAS)",
+            "roofline_ms_per_recycle": 2.4,
+            "transition": "ReLU 128->512->128, fused kernel K4 (tmu_transition)",
+            "k4_us_per_launch": round(k4_us, 2),
+            "k4_roofline": {"bound": "tensor", "achieved": round(k4_flops / (k4_us * 1e-6) / 1e12, 1),
+                            "peak": tflops, "unit": "TFLOP/s", "frac": round(k4_flops / (k4_us * 1e-6) / 1e12 / tflops, 4),
+                            "hbm_gbs": round(k4_bytes / (k4_us * 1e-6) / 1e9, 1)},
             "output_finite": finite}
 
 

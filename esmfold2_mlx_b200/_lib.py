@@ -54,8 +54,17 @@ class TmuPairLayout(ctypes.Structure):
     ]
 
 
+class TmuTransitionWeights(ctypes.Structure):
+    """Mirror of ``tmu_transition_weights``."""
+
+    _fields_ = [("ln_w", _vp), ("ln_b", _vp), ("w12", _vp), ("w3", _vp)]
+
+
+TMU_ACT_SWIGLU, TMU_ACT_RELU = 0, 1
+
 _W = ctypes.POINTER(TmuTrimulWeights)
 _G = ctypes.POINTER(TmuPairLayout)
+_TW = ctypes.POINTER(TmuTransitionWeights)
 SIGNATURES = {
     "tmu_version": (ctypes.c_char_p, []),
     "tmu_status_name": (ctypes.c_char_p, [_i]),
@@ -75,6 +84,7 @@ SIGNATURES = {
     "tmu_emit_residual_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _W, _i, _i, _f, _vp, _vp]),
     "tmu_trimul": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp]),
     "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),
+    "tmu_transition": (_i, [_vp, _vp, _TW, _i, _i, _i, _i, _i, _vp, _vp]),
     "tmu_selftest_wait_timeout": (_i, [_vp, _ull, _vp]),
 }
 

@@ -1,0 +1,388 @@
+// K4: the pair transition of a PairUpdateBlock, z' = z + ffn(LN(z)), in one pass over the pair
+// grid (c_z = 128, hidden h a multiple of 64).
+//
+// Reference (src/esmfold2_mlx/): mlx_trunk.py:96-99, fused path mlx_trunk_kernels.py:236-239
+// (module form fast_trunk.py:35-42), in the fp16 scheme:
+//   h  = fp16(LN(z; norm, eps=1e-5))
+//   x  = fp16(h @ w12^T)                       w12 [2h, c_z] (SwiGLU) or [h, c_z] (ReLU)
+//   SwiGLU: s = fp16(fp16(x1 * fp16(sigmoid(x1))) * x2),  x1 = x[:, :h], x2 = x[:, h:]
+//   ReLU (synthetic configurations only): s = relu(x)
+//   z' = fp16(z + s @ w3^T)                    w3 [c_z, h]; one rounding (mx.addmm)
+//
+// Tile = 128 positions (ih x jw block of the grid); TMEM lane = position.  The hidden dimension
+// is processed in chunks of 64: GEMM1 of chunk k (D1 = h W12_k^T, N = 64, or 2 x 64 for SwiGLU's
+// x1 and x2 halves) lands in one of two TMEM chunk buffers, the activation warps turn it into
+// the fp16 A operand s_k in shared memory, and GEMM2 accumulates D2 += s_k W3_k^T (N = c_z,
+// K = 64) in one of two per-tile TMEM accumulators.  The MMA thread issues G1(0), G1(1), G2(0),
+// G1(2), G2(1), ... so the tensor core computes the next chunk while the current one is being
+// activated.  The weights (256-384 KB) do not fit beside the tiles, so they stream from L2
+// through a 4-stage ring of 16 KB items in exactly that order.
+// CTA = 15 warps, one per SM, persistent:
+//   warp 0      TMA: the weight ring
+//   warp 1      TMEM (512 columns: D2 x 2 at [0, 256), D1 x 2 at [256, 512)) + MMA thread
+//   warp 2      TMA: z tiles (2 stages)
+//   warps 3-6   LayerNorm z tile -> h (K-major swizzled A operand, 2 stages)
+//   warps 7-10  activation: D1 -> s (per chunk, one TMEM lane quadrant each)
+//   warps 11-14 epilogue: D2 + z -> z' over the z tile, per-warp TMA store of 32 positions
+// Each tile is read and written by exactly one CTA, so z_out may alias z.
+#pragma once
+
+#include "tmu_common.cuh"
+
+namespace tmu {
+namespace k4 {
+
+constexpr int CZ = 128;
+constexpr int TILE = 128;
+constexpr int CHUNK = 64;                        // hidden units per chunk
+constexpr int ATOM_BYTES = TILE * 128;           // 128 rows x 128 B
+constexpr int TILE_BYTES = TILE * CZ * 2;        // 32 KB
+constexpr int S_BYTES = TILE * CHUNK * 2;        // 16 KB: one chunk of s
+constexpr int W_BYTES = 16384;                   // one ring item
+constexpr int NW = 4;
+constexpr int OFF_Z = 0;                         // 2 stages
+constexpr int OFF_H = OFF_Z + 2 * TILE_BYTES;    // 2 stages
+constexpr int OFF_S = OFF_H + 2 * TILE_BYTES;    // 2 buffers
+constexpr int OFF_W = OFF_S + 2 * S_BYTES;       // NW ring items
+constexpr int OFF_PAR = OFF_W + NW * W_BYTES;    // fp32 LN gamma[128], beta[128]
+constexpr int OFF_BAR = OFF_PAR + 2 * CZ * 4;
+constexpr int SMEM_BYTES = OFF_BAR + 256;
+constexpr int kThreads = 480;
+constexpr int TMEM_COLS = 512;
+static_assert(SMEM_BYTES <= 232448, "K4 shared memory exceeds the per-block limit");
+
+struct Params {
+  CUtensorMap tm_z;    // z [B, L, L, 128]: box {64, jw, ih, 1}, 128B swizzle (load)
+  CUtensorMap tm_zo;   // z_out: box {64, min(jw,32), 32/min(jw,32), 1}, 128B swizzle (per-warp store)
+  CUtensorMap tm_w12;  // w12 [W, 128]: box {64, 64}, 128B swizzle
+  CUtensorMap tm_w3;   // w3 [128, h]: box {64, 128}, 128B swizzle
+  const __half* ln_w;
+  const __half* ln_b;
+  int hidden;          // h
+  int nchunk;          // h / 64
+  int L, ih, jw, tiles_i, tiles_j, num_tiles;
+  DeviceStatus* status;
+  unsigned long long timeout_ns;
+};
+
+enum Site : unsigned int {
+  kSiteProdW = 0x401, kSiteProdZ = 0x402, kSiteLn = 0x403, kSiteMmaH = 0x404, kSiteMmaW = 0x405,
+  kSiteMmaD1 = 0x406, kSiteMmaS = 0x407, kSiteMmaAcc = 0x408, kSiteAct = 0x409, kSiteEpi = 0x40a
+};
+
+__device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, int& i0, int& j0) {
+  const int per_b = p.tiles_i * p.tiles_j;
+  bb = tile / per_b;
+  const int r = tile - bb * per_b;
+  i0 = (r / p.tiles_j) * p.ih;
+  j0 = (r % p.tiles_j) * p.jw;
+}
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_constant__ Params p) {
+  constexpr uint32_t IDESC1 = idesc_f16_f32(128, CHUNK, false, false);
+  constexpr uint32_t IDESC2 = idesc_f16_f32(128, CZ, false, false);
+  constexpr int W1_ITEMS = SWIGLU ? 2 : 1;  // ring items per GEMM1 chunk
+  extern __shared__ uint8_t smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x4ff;
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* wfull = bars;           // [NW]
+  uint64_t* wempty = bars + 4;      // [NW]
+  uint64_t* zfull = bars + 8;       // [2]
+  uint64_t* zempty = bars + 10;     // [2]
+  uint64_t* hfull = bars + 12;      // [2]
+  uint64_t* hempty = bars + 14;     // [2]
+  uint64_t* d1full = bars + 16;     // [2]
+  uint64_t* d1empty = bars + 18;    // [2]
+  uint64_t* sfull = bars + 20;      // [2]
+  uint64_t* sempty = bars + 22;     // [2]
+  uint64_t* accfull = bars + 24;    // [2]
+  uint64_t* accempty = bars + 26;   // [2]
+  uint64_t& drain_bar = bars[28];
+  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 29);
+  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 29) + 4);
+  float* par = reinterpret_cast<float*>(smem + OFF_PAR);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const WaitCtx ctx{p.status, &abort_sh, p.timeout_ns};
+  const int n = p.nchunk;
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    for (int s = 0; s < NW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&zfull[s], 1);
+      mbar_init(&zempty[s], 4);    // the four epilogue warps, after their stores read the tile
+      mbar_init(&hfull[s], 4);     // the four LayerNorm warps
+      mbar_init(&hempty[s], 1);    // the MMA, after the tile's last GEMM1
+      mbar_init(&d1full[s], 1);
+      mbar_init(&d1empty[s], 4);   // the four activation warps
+      mbar_init(&sfull[s], 4);
+      mbar_init(&sempty[s], 1);
+      mbar_init(&accfull[s], 1);
+      mbar_init(&accempty[s], 4);  // the four epilogue warps
+    }
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < 2 * CZ; i += blockDim.x) par[i] = __half2float(i < CZ ? p.ln_w[i] : p.ln_b[i - CZ]);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&p.tm_z);
+    tma_prefetch_desc(&p.tm_zo);
+    tma_prefetch_desc(&p.tm_w12);
+    tma_prefetch_desc(&p.tm_w3);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+  griddep_trigger();
+  griddep_wait();
+
+  if (warp == 0) {
+    // ---------------- weight ring producer: G1(0), then G1(k), G2(k-1) for k = 1..n-1, G2(n-1) ----------------
+    if (lane == 0) {
+      uint32_t r = 0;
+      bool ok = true;
+      auto put = [&](const CUtensorMap* m, int c0, int c1, int nloads, int c0_step) -> bool {
+        const uint32_t s = r % NW, ph = (r / NW) & 1;
+        if (!mbar_wait(&wempty[s], ph ^ 1, ctx, kSiteProdW)) return false;
+        mbar_arrive_expect_tx(&wfull[s], W_BYTES);
+        for (int q = 0; q < nloads; ++q)
+          tma_load_2d(smem + OFF_W + s * W_BYTES + q * (W_BYTES / nloads), m, &wfull[s], c0 + q * c0_step, c1);
+        ++r;
+        return true;
+      };
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
+        for (int k = 0; ok && k <= n; ++k) {
+          if (k < n) {  // w12 rows of chunk k (x1), and of x2 for SwiGLU: two 64 x 64 boxes each
+            ok = put(&p.tm_w12, 0, k * CHUNK, 2, 64);
+            if (ok && SWIGLU) ok = put(&p.tm_w12, 0, p.hidden + k * CHUNK, 2, 64);
+          }
+          if (ok && k >= 1) ok = put(&p.tm_w3, (k - 1) * CHUNK, 0, 1, 0);  // w3[:, chunk k-1]
+        }
+      }
+      if (abort_sh) {  // drain the loads still in flight before the CTA exits
+        for (uint32_t s = 0; s < NW; ++s) {
+          const uint32_t armed = r > s ? (r - s + NW - 1) / NW : 0;
+          if (armed) mbar_drain(&wfull[s], (armed - 1) & 1, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 2) {
+    // ---------------- z tile producer ----------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+        int bb, i0, j0;
+        decode_tile(p, tile, bb, i0, j0);
+        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        if (!mbar_wait(&zempty[s], ph ^ 1, ctx, kSiteProdZ)) break;
+        mbar_arrive_expect_tx(&zfull[s], TILE_BYTES);
+        for (int a = 0; a < 2; ++a)
+          tma_load_4d(smem + OFF_Z + s * TILE_BYTES + a * ATOM_BYTES, &p.tm_z, &zfull[s], a * 64, j0, i0, bb);
+      }
+      if (abort_sh) {
+        for (uint32_t s = 0; s < 2; ++s) {
+          const uint32_t armed = it > s ? (it - s + 1) / 2 : 0;
+          if (armed) mbar_drain(&zfull[s], (armed - 1) & 1, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t r = 0, it = 0, gc = 0;  // ring item, tile, global chunk counters
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
+        const uint32_t tb = it & 1, tph = (it >> 1) & 1;
+        if (!(ok = mbar_wait(&hfull[tb], tph, ctx, kSiteMmaH))) break;
+        const uint32_t hbase = smem_u32(smem + OFF_H + tb * TILE_BYTES);
+        const uint32_t acc = tmem_base + tb * CZ;
+        for (int k = 0; ok && k <= n; ++k) {
+          if (k < n) {  // GEMM1 of chunk gc + k
+            const uint32_t c = gc + k, b = c & 1, cph = (c >> 1) & 1;
+            if (!(ok = mbar_wait(&d1empty[b], cph ^ 1, ctx, kSiteMmaD1))) break;
+            for (int half = 0; half < W1_ITEMS; ++half) {
+              const uint32_t s = r % NW, ph = (r / NW) & 1;
+              if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
+              tc_fence_after();
+              const uint32_t wb = smem_u32(smem + OFF_W + s * W_BYTES);
+              const uint32_t d = tmem_base + 256 + b * 128 + half * CHUNK;
+#pragma unroll
+              for (int kk = 0; kk < CZ / 16; ++kk) {
+                const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
+                umma_f16(d, sdesc_sw128(hbase + ka * ATOM_BYTES + kb, 16, 1024),
+                         sdesc_sw128(wb + ka * (W_BYTES / 2) + kb, 16, 1024), IDESC1, kk > 0 ? 1u : 0u);
+              }
+              umma_commit(&wempty[s]);
+              ++r;
+            }
+            if (!ok) break;
+            umma_commit(&d1full[b]);
+            if (k == n - 1) umma_commit(&hempty[tb]);  // the tile's last read of h
+          }
+          if (k >= 1) {  // GEMM2 of chunk gc + k - 1
+            const uint32_t c = gc + k - 1, b = c & 1, cph = (c >> 1) & 1;
+            if (k == 1 && !(ok = mbar_wait(&accempty[tb], tph ^ 1, ctx, kSiteMmaAcc))) break;
+            if (!(ok = mbar_wait(&sfull[b], cph, ctx, kSiteMmaS))) break;
+            const uint32_t s = r % NW, ph = (r / NW) & 1;
+            if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
+            tc_fence_after();
+            const uint32_t sb = smem_u32(smem + OFF_S + b * S_BYTES);
+            const uint32_t wb = smem_u32(smem + OFF_W + s * W_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < CHUNK / 16; ++kk)
+              umma_f16(acc, sdesc_sw128(sb + kk * 32, 16, 1024), sdesc_sw128(wb + kk * 32, 16, 1024), IDESC2,
+                       (k > 1 || kk > 0) ? 1u : 0u);
+            umma_commit(&wempty[s]);
+            umma_commit(&sempty[b]);
+            ++r;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&accfull[tb]);
+        gc += n;
+      }
+      umma_commit(&drain_bar);
+      mbar_drain(&drain_bar, 0, 200000000ull);
+    }
+  } else if (warp < 7) {
+    // ---------------- LayerNorm: z tile -> h ----------------
+    const int row = threadIdx.x - 96;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+      const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      if (!warp_wait(&hempty[s], ph ^ 1, ctx, kSiteLn)) break;
+      if (!warp_wait(&zfull[s], ph, ctx, kSiteLn)) break;
+      ln_row128_sw128(smem + OFF_Z + s * TILE_BYTES, smem + OFF_H + s * TILE_BYTES, ATOM_BYTES, row, 1e-5f,
+                      LnParSmem{par, par + CZ});
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&hfull[s]);
+    }
+  } else if (warp < 11) {
+    // ---------------- activation: D1 chunk -> s chunk (fp16, K-major swizzled) ----------------
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t tl = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t gc = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      bool ok = true;
+      for (int k = 0; k < n; ++k, ++gc) {
+        const uint32_t b = gc & 1, cph = (gc >> 1) & 1;
+        if (!(ok = warp_wait(&d1full[b], cph, ctx, kSiteAct))) break;
+        if (!(ok = warp_wait(&sempty[b], cph ^ 1, ctx, kSiteAct))) break;
+        tc_fence_after();
+        uint8_t* S = smem + OFF_S + b * S_BYTES;
+        const uint32_t d = tmem_base + tl + 256 + b * 128;
+#pragma unroll 1
+        for (int j = 0; j < CHUNK / 16; ++j) {  // 16 hidden units at a time
+          uint32_t x1[16], x2[16];
+          tmem_ld16(d + j * 16, x1);
+          if (SWIGLU) {
+            tmem_ld16(d + CHUNK + j * 16, x2);
+            tmem_wait_ld16x2(x1, x2);
+          } else {
+            tmem_wait_ld16x2(x1, x1);
+          }
+          if (j == CHUNK / 16 - 1) {  // the chunk buffer has been read: hand it back
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d1empty[b]);
+          }
+          uint32_t o[8];
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            float2 a = round_f16x2(make_float2(__uint_as_float(x1[e]), __uint_as_float(x1[e + 1])));  // x is fp16
+            if (SWIGLU) {
+              const float2 c = round_f16x2(make_float2(__uint_as_float(x2[e]), __uint_as_float(x2[e + 1])));
+              const float2 sg = round_f16x2(sigmoid_f32x2(a));
+              a = __fmul2_rn(round_f16x2(__fmul2_rn(a, sg)), c);
+            } else {
+              a = make_float2(fmaxf(a.x, 0.0f), fmaxf(a.y, 0.0f));
+            }
+            o[e / 2] = pack_half2(a.x, a.y);
+          }
+          *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * j)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * j + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sfull[b]);
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ---------------- epilogue: z' = fp16(z + D2) over the z tile, per-warp TMA store ----------------
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
+    const uint32_t tl = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t it = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+      int bb, i0, j0;
+      decode_tile(p, tile, bb, i0, j0);
+      const uint32_t tb = it & 1, tph = (it >> 1) & 1;
+      if (!warp_wait(&accfull[tb], tph, ctx, kSiteEpi)) break;
+      if (!warp_wait(&zfull[tb], tph, ctx, kSiteEpi)) break;
+      tc_fence_after();
+      uint8_t* Z = smem + OFF_Z + tb * TILE_BYTES;
+#pragma unroll 1
+      for (int c16 = 0; c16 < CZ / 16; ++c16) {  // 16 channels at a time
+        uint32_t v[16];
+        tmem_ld16(tmem_base + tl + tb * CZ + c16 * 16, v);
+        tmem_wait_ld16x2(v, v);
+        if (c16 == CZ / 16 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&accempty[tb]);
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // two 8-channel chunks of the z row
+          const int chunk = 2 * c16 + h;
+          uint8_t* zp = Z + (chunk >> 3) * ATOM_BYTES + sw128_off(row, chunk & 7);
+          uint4 zv = *reinterpret_cast<const uint4*>(zp);
+          uint32_t* zu = reinterpret_cast<uint32_t*>(&zv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 zz = unpack_half2(zu[e]);
+            const float2 y = __fadd2_rn(zz, make_float2(__uint_as_float(v[8 * h + 2 * e]),
+                                                        __uint_as_float(v[8 * h + 2 * e + 1])));
+            zu[e] = pack_half2(y.x, y.y);
+          }
+          *reinterpret_cast<uint4*>(zp) = zv;
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        for (int a = 0; a < 2; ++a) tma_store_4d(&p.tm_zo, Z + a * ATOM_BYTES + q * 32 * 128, a * 64, j0 + jo, i0 + io, bb);
+        bulk_commit();
+        bulk_wait_read<0>();
+        mbar_arrive(&zempty[tb]);
+      }
+    }
+    if (lane == 0) bulk_wait<0>();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace k4
+}  // namespace tmu

@@ -16,6 +16,7 @@
 #include "k2_contract.cuh"
 #include "k3_emit.cuh"
 #include "k3w_emit.cuh"
+#include "k4_transition.cuh"
 #include "tmu.h"
 
 using namespace tmu;
@@ -505,6 +506,55 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_w_kernel");
 }
 
+int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int hidden, bool swiglu,
+              DeviceStatus* status, cudaStream_t stream) {
+  void (*kern)(k4::Params) = swiglu ? k4::transition_kernel<true> : k4::transition_kernel<false>;
+  Dev dev;
+  int st = current_device(dev, 1u << (24 + (swiglu ? 1 : 0)), reinterpret_cast<const void*>(kern), k4::SMEM_BYTES);
+  if (st) return st;
+  k4::Params p;
+  memset(&p, 0, sizeof(p));
+  int ih = 1, jw = 128;
+  choose_tile(L, L, ih, jw, k4::TILE);
+  {
+    const uint64_t dims[4] = {128, (uint64_t)L, (uint64_t)L, (uint64_t)B};
+    const uint64_t str[3] = {256, 256ull * L, 256ull * L * L};
+    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    const uint32_t jwp = jw < 32 ? jw : 32;  // one epilogue warp's 32 positions
+    const uint32_t boxo[4] = {64, jwp, 32 / jwp, 1};
+    if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, boxo, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[2] = {128, (uint64_t)(swiglu ? 2 * hidden : hidden)};
+    const uint64_t str[1] = {256};
+    const uint32_t box[2] = {64, 64};
+    if ((st = encode_map(&p.tm_w12, w->w12, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)hidden, 128};
+    const uint64_t str[1] = {2ull * hidden};
+    const uint32_t box[2] = {64, 128};
+    if ((st = encode_map(&p.tm_w3, w->w3, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  p.ln_w = static_cast<const __half*>(w->ln_w);
+  p.ln_b = static_cast<const __half*>(w->ln_b);
+  p.hidden = hidden;
+  p.nchunk = hidden / k4::CHUNK;
+  p.L = L;
+  p.ih = ih;
+  p.jw = jw;
+  p.tiles_i = (L + ih - 1) / ih;
+  p.tiles_j = (L + jw - 1) / jw;
+  p.num_tiles = B * p.tiles_i * p.tiles_j;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms);
+  cudaError_t e = launch_pdl(kern, grid, k4::kThreads, k4::SMEM_BYTES, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel");
+}
+
 size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
 size_t cm_bytes(int B, int L, int c) { return align256(static_cast<size_t>(B) * c * L * row_pitch(L) * 2); }
@@ -765,6 +815,22 @@ int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_t
   if ((st = launch_k1(z, mask, w, square_geom(B, L, c_z), a, b, dstat, s))) return st;
   if ((st = launch_k2(a, b, x, B * c, L, L, L, L, outgoing != 0, dstat, s))) return st;
   return launch_k3(x, z, z_out, w, B, L, L, mix_eps, dstat, s, c_z);
+}
+
+int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int c_z, int hidden,
+                   int activation, void* status, void* stream) {
+  if (B < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "B and L must be positive");
+  if (c_z != 128) return fail(TMU_ERR_UNSUPPORTED, "the fused transition is built for c_z = 128");
+  if (hidden < 64 || hidden > 4096 || hidden % 64) return fail(TMU_ERR_UNSUPPORTED, "hidden must be a multiple of 64 in [64, 4096]");
+  if (L > 8192 || B > 65535) return fail(TMU_ERR_UNSUPPORTED, "L > 8192");
+  if (activation != TMU_ACT_SWIGLU && activation != TMU_ACT_RELU) return fail(TMU_ERR_INVALID_ARGUMENT, "unknown activation");
+  if (w == nullptr || !w->ln_w || !w->ln_b || !w->w12 || !w->w3) return fail(TMU_ERR_INVALID_ARGUMENT, "transition weights missing");
+  if (!z || !z_out || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  const void* al[] = {z, z_out, w->ln_w, w->ln_b, w->w12, w->w3};
+  for (const void* q : al)
+    if (!aligned16(q)) return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");
+  return launch_k4(z, z_out, w, B, L, hidden, activation == TMU_ACT_SWIGLU, static_cast<DeviceStatus*>(status),
+                   static_cast<cudaStream_t>(stream));
 }
 
 int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream) {

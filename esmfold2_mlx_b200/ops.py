@@ -198,6 +198,12 @@ class Workspace:
             self.buf = torch.empty(need + 256, dtype=torch.uint8, device=device)
         return self.buf
 
+    def aux_status(self, device) -> torch.Tensor:
+        """A status word for kernels outside the tri-mul (the transition)."""
+        if getattr(self, "_aux", None) is None or self._aux.device != torch.device(device):
+            self._aux = new_status(device)
+        return self._aux
+
     def pair_like(self, z: torch.Tensor) -> torch.Tensor:
         """A second pair buffer shaped like ``z`` (for updates that cannot run in place)."""
         if self.pair is None or self.pair.shape != z.shape or self.pair.device != z.device:
@@ -232,4 +238,52 @@ def trimul(z: torch.Tensor, mask: torch.Tensor | None, w: TrimulWeights, outgoin
                "tmu_trimul")
     if dst is not out:
         out.copy_(dst)
+    return out
+
+
+@dataclass
+class TransitionWeights:
+    """Device-resident weights of one pair transition (``norm``, ``ffn.w12``, ``ffn.w3``) in the
+    layouts of ``tmu_transition``: LayerNorm fp16, w12 [2h or h, c_z] and w3 [c_z, h] as
+    ``nn.Linear`` stores them (mlx_trunk.py:65-66 keeps the same matrices transposed)."""
+
+    c_z: int
+    hidden: int
+    activation: str
+    ln_w: torch.Tensor
+    ln_b: torch.Tensor
+    w12: torch.Tensor
+    w3: torch.Tensor
+    _struct: _lib.TmuTransitionWeights | None = field(default=None, repr=False)
+
+    @classmethod
+    def from_module(cls, tr, device="cuda") -> "TransitionWeights":
+        h16 = lambda t: t.detach().float().cpu().to(torch.float16).to(device).contiguous()  # noqa: E731
+        act = getattr(tr.ffn, "activation", "swiglu")
+        w3 = tr.ffn.w3.weight
+        return cls(c_z=int(w3.shape[0]), hidden=int(w3.shape[1]), activation=act,
+                   ln_w=h16(tr.norm.weight), ln_b=h16(tr.norm.bias), w12=h16(tr.ffn.w12.weight), w3=h16(w3))
+
+    @property
+    def struct(self) -> _lib.TmuTransitionWeights:
+        if self._struct is None:
+            self._struct = _lib.TmuTransitionWeights(_ptr(self.ln_w), _ptr(self.ln_b), _ptr(self.w12), _ptr(self.w3))
+        return self._struct
+
+    @property
+    def fused(self) -> bool:
+        """Whether ``tmu_transition`` covers this shape (c_z = 128, hidden a multiple of 64)."""
+        return self.c_z == 128 and self.hidden % 64 == 0 and 64 <= self.hidden <= 4096
+
+
+def transition(z: torch.Tensor, w: TransitionWeights, out: torch.Tensor | None = None,
+               status: torch.Tensor | None = None) -> torch.Tensor:
+    """K4: ``z + ffn(LN(z))`` in fp16 (``out`` may be ``z``)."""
+    lib = _lib.load()
+    B, L = _check_pair(z, w.c_z)
+    out = torch.empty_like(z) if out is None else out
+    status = new_status(z.device) if status is None else status
+    act = _lib.TMU_ACT_SWIGLU if w.activation == "swiglu" else _lib.TMU_ACT_RELU
+    _lib.check(lib.tmu_transition(_ptr(z), _ptr(out), ctypes.byref(w.struct), B, L, w.c_z, w.hidden, act,
+                                  _ptr(status), _stream_ptr(z.device)), "tmu_transition")
     return out

@@ -11,9 +11,9 @@ Mirrors ``src/esmfold2_mlx/mlx_trunk.py`` / ``mlx_trunk_kernels.py`` / ``var_mlx
   ``set_kernel_backend`` and ``forward(pair, pair_attention_mask=None)`` -> fp32 on
   ``pair.device``.
 
-Each triangle update is one C-ABI call (three sm_100a kernels).  The pair transition between
-them is torch on the GPU (cuBLAS GEMMs + element-wise ops with the reference's fp16 rounding
-points); it is not part of the accelerated tri-mul path.
+Each triangle update is one C-ABI call (three sm_100a kernels) and, at c_z = 128, the pair
+transition is one more (K4, ``tmu_transition``).  At other widths the transition runs as torch
+ops on the GPU (cuBLAS GEMMs + element-wise ops with the reference's fp16 rounding points).
 """
 
 from __future__ import annotations
@@ -30,12 +30,15 @@ EPS = ops.EPS
 def _transition_params(tr, device) -> dict:
     h16 = lambda t: t.detach().float().cpu().to(torch.float16).to(device).contiguous()  # noqa: E731
     act = getattr(tr.ffn, "activation", "swiglu")
-    return {
-        "ln_w": h16(tr.norm.weight), "ln_b": h16(tr.norm.bias),
-        "w12": h16(tr.ffn.w12.weight),  # nn.Linear layout [2h or h, c_z]
-        "w3t": h16(tr.ffn.w3.weight.T),  # [h, c_z] so that z + s @ w3t is one addmm
-        "activation": act,
-    }
+    tw = ops.TransitionWeights.from_module(tr, device)
+    p = {"tw": tw, "activation": act}
+    if not tw.fused:  # shapes K4 does not cover run as torch ops on the GPU
+        p.update({
+            "ln_w": h16(tr.norm.weight), "ln_b": h16(tr.norm.bias),
+            "w12": h16(tr.ffn.w12.weight),  # nn.Linear layout [2h or h, c_z]
+            "w3t": h16(tr.ffn.w3.weight.T),  # [h, c_z] so that z + s @ w3t is one addmm
+        })
+    return p
 
 
 def trunk_params(folding_trunk, dtype=torch.float16, device="cuda", biases: list | None = None) -> list:
@@ -56,9 +59,13 @@ def trunk_params(folding_trunk, dtype=torch.float16, device="cuda", biases: list
     return blocks
 
 
-def transition_(p: dict, z: torch.Tensor) -> torch.Tensor:
+def transition_(p: dict, z: torch.Tensor, workspace: ops.Workspace | None = None) -> torch.Tensor:
     """``z + ffn(LN(z))`` in place (``mlx_trunk_kernels.py:236-239``): fp16 LayerNorm output,
-    fp16 GEMM output, three fp16 element-wise ops for SwiGLU, one-rounding ``addmm`` residual."""
+    fp16 GEMM output, three fp16 element-wise ops for SwiGLU, one-rounding ``addmm`` residual.
+    c_z = 128 runs the fused kernel K4 (``tmu_transition``); other widths run torch ops."""
+    if p["tw"].fused:
+        status = workspace.aux_status(z.device) if workspace is not None else None
+        return ops.transition(z, p["tw"], out=z, status=status)
     c_z = z.shape[-1]
     h = F.layer_norm(z, (c_z,), p["ln_w"], p["ln_b"], EPS)
     x = F.linear(h, p["w12"])
@@ -83,7 +90,7 @@ def block_forward(p: dict, z: torch.Tensor, mask, mix_eps: float = ops.MIX_EPS_F
     else:
         ops.trimul(z, mask, p["out"], True, mix_eps, out=z, workspace=workspace)
         ops.trimul(z, mask, p["in"], False, mix_eps, out=z, workspace=workspace)
-    return transition_(p, z)
+    return transition_(p, z, workspace)
 
 
 def trunk_forward(params: list, z: torch.Tensor, mask=None, mix_eps: float = ops.MIX_EPS_FP16,

@@ -173,6 +173,25 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
 int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L,
                        int c_z, int c, int outgoing, float mix_eps, void* status, void* stream);
 
+/* ---- Pair transition (K4), the third op of a PairUpdateBlock: z_out = z + ffn(LN(z)).
+ * Replaces the reference's transition (mlx_trunk.py:96-99; fused path mlx_trunk_kernels.py:236-239):
+ * h = fp16(LN(z)), x = fp16(h @ w12^T), SwiGLU s = fp16(fp16(x1 * fp16(sigmoid(x1))) * x2) with
+ * x1, x2 the two halves of x (TMU_ACT_RELU: s = relu(x), for synthetic configurations), and
+ * z_out = fp16(z + s @ w3^T) with one rounding.  z_out may alias z. */
+#define TMU_ACT_SWIGLU 0
+#define TMU_ACT_RELU 1
+
+typedef struct tmu_transition_weights {
+  const void* ln_w;  /* fp16 [c_z]: norm.weight */
+  const void* ln_b;  /* fp16 [c_z]: norm.bias */
+  const void* w12;   /* fp16 [2*hidden, c_z] (SwiGLU) or [hidden, c_z] (ReLU): ffn.w12.weight */
+  const void* w3;    /* fp16 [c_z, hidden]: ffn.w3.weight */
+} tmu_transition_weights;
+
+/* c_z = 128, hidden a multiple of 64 in [64, 4096]; z [B, L, L, c_z] fp16. */
+int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int c_z, int hidden,
+                   int activation, void* status, void* stream);
+
 /* Self-test of the bounded-wait machinery: launches one CTA that waits on an mbarrier nothing
  * ever arrives at, with a limit of `timeout_ns`; the kernel must give up, record
  * TMU_ERR_DEVICE_TIMEOUT in `status` and exit.  Returns the launch status. */
