@@ -17,13 +17,14 @@
 // G1(2), G2(1), ... so the tensor core computes the next chunk while the current one is being
 // activated.  The weights (256-384 KB) do not fit beside the tiles, so they stream from L2
 // through a 4-stage ring of 16 KB items in exactly that order.
-// CTA = 15 warps, one per SM, persistent:
+// CTA = 19 warps, one per SM, persistent:
 //   warp 0      TMA: the weight ring
 //   warp 1      TMEM (512 columns: D2 x 2 at [0, 256), D1 x 2 at [256, 512)) + MMA thread
 //   warp 2      TMA: z tiles (2 stages)
 //   warps 3-6   LayerNorm z tile -> h (K-major swizzled A operand, 2 stages)
-//   warps 7-10  activation: D1 -> s (per chunk, one TMEM lane quadrant each)
-//   warps 11-14 epilogue: D2 + z -> z' over the z tile, per-warp TMA store of 32 positions
+//   warps 7-14  activation: D1 -> s, two groups of four (one TMEM lane quadrant per warp),
+//               group g on the chunks that use buffer g
+//   warps 15-18 epilogue: D2 + z -> z' over the z tile, per-warp TMA store of 32 positions
 // Each tile is read and written by exactly one CTA, so z_out may alias z.
 #pragma once
 
@@ -47,7 +48,7 @@ constexpr int OFF_W = OFF_S + 2 * S_BYTES;       // NW ring items
 constexpr int OFF_PAR = OFF_W + NW * W_BYTES;    // fp32 LN gamma[128], beta[128]
 constexpr int OFF_BAR = OFF_PAR + 2 * CZ * 4;
 constexpr int SMEM_BYTES = OFF_BAR + 256;
-constexpr int kThreads = 480;
+constexpr int kThreads = 608;
 constexpr int TMEM_COLS = 512;
 static_assert(SMEM_BYTES <= 232448, "K4 shared memory exceeds the per-block limit");
 
@@ -271,57 +272,74 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(&hfull[s]);
     }
-  } else if (warp < 11) {
+  } else if (warp < 15) {
     // ---------------- activation: D1 chunk -> s chunk (fp16, K-major swizzled) ----------------
+    // Two groups of four warps; group g takes the chunks that use D1 / s buffer g (every other
+    // chunk), so one group's TMEM-load latency hides behind the other's arithmetic.
+    const int g = (warp - 7) >> 2;
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t tl = static_cast<uint32_t>(q * 32) << 16;
     uint32_t gc = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      bool ok = true;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
       for (int k = 0; k < n; ++k, ++gc) {
-        const uint32_t b = gc & 1, cph = (gc >> 1) & 1;
+        if (static_cast<int>(gc & 1) != g) continue;
+        const uint32_t b = g, cph = (gc >> 1) & 1;
         if (!(ok = warp_wait(&d1full[b], cph, ctx, kSiteAct))) break;
         if (!(ok = warp_wait(&sempty[b], cph ^ 1, ctx, kSiteAct))) break;
         tc_fence_after();
         uint8_t* S = smem + OFF_S + b * S_BYTES;
         const uint32_t d = tmem_base + tl + 256 + b * 128;
-#pragma unroll 1
-        for (int j = 0; j < CHUNK / 16; ++j) {  // 16 hidden units at a time
-          uint32_t x1[16], x2[16];
-          tmem_ld16(d + j * 16, x1);
-          if (SWIGLU) {
-            tmem_ld16(d + CHUNK + j * 16, x2);
-            tmem_wait_ld16x2(x1, x2);
-          } else {
-            tmem_wait_ld16x2(x1, x1);
-          }
-          if (j == CHUNK / 16 - 1) {  // the chunk buffer has been read: hand it back
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&d1empty[b]);
-          }
-          uint32_t o[8];
+        if (!SWIGLU) {
+          uint32_t x[32], y[32];  // hidden units [0, 32) and [32, 64) of the chunk
+          tmem_ld32(d, x);
+          tmem_ld32(d + 32, y);
+          tmem_wait_ld2(x, y);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&d1empty[b]);
 #pragma unroll
-          for (int e = 0; e < 16; e += 2) {
-            float2 a = round_f16x2(make_float2(__uint_as_float(x1[e]), __uint_as_float(x1[e + 1])));  // x is fp16
-            if (SWIGLU) {
-              const float2 c = round_f16x2(make_float2(__uint_as_float(x2[e]), __uint_as_float(x2[e + 1])));
-              const float2 sg = round_f16x2(sigmoid_f32x2(a));
-              a = __fmul2_rn(round_f16x2(__fmul2_rn(a, sg)), c);
-            } else {
-              a = make_float2(fmaxf(a.x, 0.0f), fmaxf(a.y, 0.0f));
-            }
-            o[e / 2] = pack_half2(a.x, a.y);
+          for (int c8 = 0; c8 < 8; ++c8) {  // relu(fp16(v)) == fp16(relu(v)): one rounding
+            const uint32_t* v = c8 < 4 ? x + 8 * c8 : y + 8 * (c8 - 4);
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              o[e] = pack_half2(fmaxf(__uint_as_float(v[2 * e]), 0.0f), fmaxf(__uint_as_float(v[2 * e + 1]), 0.0f));
+            *reinterpret_cast<uint4*>(S + sw128_off(row, c8)) = make_uint4(o[0], o[1], o[2], o[3]);
           }
-          *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * j)) = make_uint4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * j + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+        } else {
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {  // 32 hidden units at a time: x1 and x2 columns
+            uint32_t x[32], y[32];
+            tmem_ld32(d + hh * 32, x);
+            tmem_ld32(d + CHUNK + hh * 32, y);
+            tmem_wait_ld2(x, y);
+            if (hh == 1) {  // the chunk buffer has been read: hand it back
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&d1empty[b]);
+            }
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+              uint32_t o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int i = 8 * c8 + 2 * e;
+                const float2 a = round_f16x2(make_float2(__uint_as_float(x[i]), __uint_as_float(x[i + 1])));
+                const float2 c = round_f16x2(make_float2(__uint_as_float(y[i]), __uint_as_float(y[i + 1])));
+                const float2 sg = round_f16x2(sigmoid_f32x2(a));
+                const float2 r = __fmul2_rn(round_f16x2(__fmul2_rn(a, sg)), c);
+                o[e] = pack_half2(r.x, r.y);
+              }
+              *reinterpret_cast<uint4*>(S + sw128_off(row, hh * 4 + c8)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sfull[b]);
       }
-      if (!ok) break;
     }
   } else {
     // ---------------- epilogue: z' = fp16(z + D2) over the z tile, per-warp TMA store ----------------
@@ -339,26 +357,26 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
       tc_fence_after();
       uint8_t* Z = smem + OFF_Z + tb * TILE_BYTES;
 #pragma unroll 1
-      for (int c16 = 0; c16 < CZ / 16; ++c16) {  // 16 channels at a time
-        uint32_t v[16];
-        tmem_ld16(tmem_base + tl + tb * CZ + c16 * 16, v);
-        tmem_wait_ld16x2(v, v);
-        if (c16 == CZ / 16 - 1) {
+      for (int a = 0; a < 2; ++a) {  // channels [64a, 64a + 64) = z atom a
+        uint32_t v[32], u[32];
+        tmem_ld32(tmem_base + tl + tb * CZ + a * 64, v);
+        tmem_ld32(tmem_base + tl + tb * CZ + a * 64 + 32, u);
+        tmem_wait_ld2(v, u);
+        if (a == 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&accempty[tb]);
         }
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // two 8-channel chunks of the z row
-          const int chunk = 2 * c16 + h;
-          uint8_t* zp = Z + (chunk >> 3) * ATOM_BYTES + sw128_off(row, chunk & 7);
+        for (int c8 = 0; c8 < 8; ++c8) {  // 8-channel chunks of the z row
+          const uint32_t* acc = c8 < 4 ? v + 8 * c8 : u + 8 * (c8 - 4);
+          uint8_t* zp = Z + a * ATOM_BYTES + sw128_off(row, c8);
           uint4 zv = *reinterpret_cast<const uint4*>(zp);
           uint32_t* zu = reinterpret_cast<uint32_t*>(&zv);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 zz = unpack_half2(zu[e]);
-            const float2 y = __fadd2_rn(zz, make_float2(__uint_as_float(v[8 * h + 2 * e]),
-                                                        __uint_as_float(v[8 * h + 2 * e + 1])));
+            const float2 y = __fadd2_rn(unpack_half2(zu[e]),
+                                        make_float2(__uint_as_float(acc[2 * e]), __uint_as_float(acc[2 * e + 1])));
             zu[e] = pack_half2(y.x, y.y);
           }
           *reinterpret_cast<uint4*>(zp) = zv;

@@ -1,12 +1,14 @@
 """Run one triangle update (or one of its kernels) at a chosen size, for profilers.
 
     python -m esmfold2_mlx_b200.profile_case --L 1024 [--B 1] [--direction out|in]
-           [--stage all|k1|k2|k3] [--reps 3] [--mask-pad 0] [--cz 128|256]
+           [--stage all|k1|k2|k3|k4] [--reps 3] [--mask-pad 0] [--cz 128|256]
+           [--hidden 512] [--activation swiglu|relu]
 
 Inputs are seeded synthetic tensors (``synthetic``); weights are random-init.  The chosen stage
 is launched ``--reps`` times after one untimed launch of every stage (and one more of itself), then the script checks the
 device status word and prints the mean CUDA-event time per launch.  Use ``ncu -k regex:<name>``
-with ``project_gate``, ``contract`` or ``emit_residual`` to select a kernel.
+with ``project_gate``, ``contract``, ``emit_residual`` or ``transition`` to select a kernel
+(k4 is the fused pair transition, c_z = 128).
 """
 
 from __future__ import annotations
@@ -24,16 +26,18 @@ def main():
     ap.add_argument("--L", type=int, default=1024)
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--direction", choices=["out", "in"], default="out")
-    ap.add_argument("--stage", choices=["all", "k1", "k2", "k3"], default="all")
+    ap.add_argument("--stage", choices=["all", "k1", "k2", "k3", "k4"], default="all")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--mask-pad", type=int, default=0)
     ap.add_argument("--cz", type=int, choices=[128, 256], default=128, help="c_z = c")
+    ap.add_argument("--hidden", type=int, default=512, help="transition hidden width (k4)")
+    ap.add_argument("--activation", choices=["swiglu", "relu"], default="swiglu", help="transition activation (k4)")
     args = ap.parse_args()
 
     dev = torch.device("cuda", 0)
     _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
     L, B = args.L, args.B
-    trunk = FoldingTrunk(1, args.cz, args.cz, seed=0)
+    trunk = FoldingTrunk(1, args.cz, args.cz, hidden=args.hidden, seed=0, activation=args.activation)
     w = ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + args.direction), dev)
     z = pair_tensor(B, L, args.cz, 0).half().to(dev)
     mask = pair_mask(B, L, args.mask_pad).half().to(dev) if args.mask_pad else None
@@ -51,6 +55,9 @@ def main():
         "k3": lambda: ops.emit_residual(x, z, w, out=out, status=status),
         "all": lambda: ops.trimul(z, mask, w, outgoing, out=out),
     }
+    if args.stage == "k4":
+        tw = ops.TransitionWeights.from_module(trunk.blocks[0].pair_transition, dev)
+        stages["k4"] = lambda: ops.transition(z, tw, out=out, status=status)
     fn = stages[args.stage]
     fn()  # warm-up: the stage's own output allocations happen here, outside the timed launches
     torch.cuda.synchronize()
