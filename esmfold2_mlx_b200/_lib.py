@@ -80,7 +80,7 @@ SIGNATURES = {
     "tmu_contract": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "tmu_emit_residual": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_project_gate_ex": (_i, [_vp, _vp, _G, _W, _i, _i, _vp, _vp, _vp, _vp]),
-    "tmu_contract_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp]),
+    "tmu_contract_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp]),
     "tmu_emit_residual_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _W, _i, _i, _f, _vp, _vp]),
     "tmu_trimul": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp]),
     "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),

@@ -257,8 +257,8 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, cons
 // layout an all-gather of row slabs produces.  MN-major (incoming form): a, b are [Bc, K, pitch(M)]
 // with M = N = K (square only).  x is [Bc, M, pitch(N)].
 template <int BN, bool MN>
-int launch_k2_t(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int rows_per_part,
-                DeviceStatus* status, cudaStream_t stream, unsigned attr_bit) {
+int launch_k2_t(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int rows_per_part, int ldx,
+                DeviceStatus* status, cudaStream_t stream, unsigned attr_bit, int max_ctas) {
   using C = k2::Cfg<BN>;
   auto kern = &k2::contract_kernel<BN, MN>;
   Dev dev;
@@ -266,7 +266,7 @@ int launch_k2_t(const void* a, const void* b, void* x, int Bc, int M, int N, int
   if (st) return st;
   k2::Params p;
   memset(&p, 0, sizeof(p));
-  const uint64_t kp = row_pitch(K), np = row_pitch(N);
+  const uint64_t kp = row_pitch(K), np = ldx > 0 ? ldx : row_pitch(N);
   if (!MN) {
     const int parts = N / rows_per_part;
     const uint64_t da[3] = {(uint64_t)K, (uint64_t)M, (uint64_t)Bc};
@@ -298,28 +298,31 @@ int launch_k2_t(const void* a, const void* b, void* x, int Bc, int M, int N, int
   p.num_kb = (K + k2::BK - 1) / k2::BK;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
-  const int grid = std::min(p.num_tiles, dev.sms);
+  int grid = std::min(p.num_tiles, dev.sms);
+  if (max_ctas > 0) grid = std::min(grid, max_ctas);
   cudaError_t e = launch_pdl(kern, grid, k2::kThreads, C::SMEM_BYTES, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch contract_kernel");
 }
 
+// ldx: row pitch of x in elements (0: row_pitch(N)); x may be a column block of a wider matrix.
+// max_ctas > 0 caps the persistent grid (leaving SMs to kernels that run alongside, e.g. NCCL's).
 int launch_k2(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int rows_per_part, bool outgoing,
-              DeviceStatus* status, cudaStream_t stream) {
+              DeviceStatus* status, cudaStream_t stream, int ldx = 0, int max_ctas = 0) {
   if (!outgoing) {
     if (M != N || M != K || rows_per_part != N) return fail(TMU_ERR_UNSUPPORTED, "incoming form is square only");
-    return N <= 128 ? launch_k2_t<128, true>(a, b, x, Bc, M, N, K, N, status, stream, 1u << 2)
-                    : launch_k2_t<256, true>(a, b, x, Bc, M, N, K, N, status, stream, 1u << 4);
+    return N <= 128 ? launch_k2_t<128, true>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 2, max_ctas)
+                    : launch_k2_t<256, true>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 4, max_ctas);
   }
   const int parts = N / rows_per_part;
   if (parts * rows_per_part != N) return fail(TMU_ERR_INVALID_ARGUMENT, "N must be a multiple of rows_per_part");
   if (parts == 1) {
-    return N <= 128 ? launch_k2_t<128, false>(a, b, x, Bc, M, N, K, N, status, stream, 1u << 1)
-                    : launch_k2_t<256, false>(a, b, x, Bc, M, N, K, N, status, stream, 1u << 3);
+    return N <= 128 ? launch_k2_t<128, false>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 1, max_ctas)
+                    : launch_k2_t<256, false>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 3, max_ctas);
   }
   // a gathered B operand: a tile of BN rows must not straddle two parts
-  if (rows_per_part % 256 == 0) return launch_k2_t<256, false>(a, b, x, Bc, M, N, K, rows_per_part, status, stream, 1u << 3);
-  if (rows_per_part % 128 == 0) return launch_k2_t<128, false>(a, b, x, Bc, M, N, K, rows_per_part, status, stream, 1u << 1);
+  if (rows_per_part % 256 == 0) return launch_k2_t<256, false>(a, b, x, Bc, M, N, K, rows_per_part, ldx, status, stream, 1u << 3, max_ctas);
+  if (rows_per_part % 128 == 0) return launch_k2_t<128, false>(a, b, x, Bc, M, N, K, rows_per_part, ldx, status, stream, 1u << 1, max_ctas);
   return fail(TMU_ERR_UNSUPPORTED, "rows_per_part of a gathered operand must be a multiple of 128");
 }
 
@@ -736,14 +739,17 @@ int tmu_project_gate_ex(const void* z, const void* mask, const tmu_pair_layout* 
 }
 
 int tmu_contract_ex(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int b_rows_per_part,
-                    void* status, void* stream) {
+                    int ldx, int max_ctas, void* status, void* stream) {
   if (Bc < 1 || M < 1 || N < 1 || K < 1 || b_rows_per_part < 1)
     return fail(TMU_ERR_INVALID_ARGUMENT, "sizes must be positive");
+  if (ldx != 0 && (ldx < N || ldx % 8 != 0))
+    return fail(TMU_ERR_INVALID_ARGUMENT, "ldx must be 0 or a multiple of 8 that is >= N");
   if (M > 8192 || N > 8192 || K > 8192 || Bc > 65535) return fail(TMU_ERR_UNSUPPORTED, "size too large");
   if (!a || !b || !x || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   if (!aligned16(a) || !aligned16(b) || !aligned16(x)) return fail(TMU_ERR_MISALIGNED, "a/b/x not 16-byte aligned");
+  if (max_ctas < 0) return fail(TMU_ERR_INVALID_ARGUMENT, "max_ctas must be >= 0");
   return launch_k2(a, b, x, Bc, M, N, K, b_rows_per_part, true, static_cast<DeviceStatus*>(status),
-                   static_cast<cudaStream_t>(stream));
+                   static_cast<cudaStream_t>(stream), ldx, max_ctas);
 }
 
 int tmu_emit_residual_ex(const void* x, const void* z, void* z_out, int B, int rows, int cols,

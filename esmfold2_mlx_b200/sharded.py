@@ -5,20 +5,23 @@ B200s) has no counterpart there.  Rank r holds rows [r*Lr, (r+1)*Lr) of the pair
 z [1, L, L, c_z] (Lr = L / P) and returns the same rows of z + update.
 
 Outgoing, x[d,i,j] = sum_k a[d,i,k] b[d,j,k]: a and b are projected on the local rows (K1); the
-ranks' b slabs are all-gathered into [P, B*c, Lr, pitch] -- exactly the block layout the
-contraction kernel reads through a 4-D tensor map, so no reorder copy -- and each rank contracts
-its rows of a against all rows of b (K2) and finishes its rows (K3).
+ranks' b slabs are all-gathered by NCCL on its own stream into [P, B*c, Lr, pitch] -- the block
+layout the contraction kernel reads through a 4-D tensor map -- while the local block of b is
+contracted into its column block of x (K2 writes a column block through its row pitch, on a
+grid that leaves SMs to NCCL); then the remote blocks are contracted and each rank finishes its
+rows (K3).
 
 Incoming, x[d,i,j] = sum_k a[d,k,i] b[d,k,j]: with a'[d,i,k] = a[d,k,i] (the projection of
 z^T[i,k] = z[k,i]) it is the outgoing form of the transposed grid.  An all-to-all sends each
 rank's [Lr, Lr] blocks to the rank owning those columns, which then holds z[:, its columns] as a
 [P, Lr, Lr, c_z] buffer; K1 reads that buffer as the transposed slab z^T[its columns, :] through
-strides alone (element (i, k) sits at k*Lr*c_z + i*c_z), the b' slabs are all-gathered, K2
-contracts, and K3 finishes the local rows of z in their original orientation.
+strides alone (element (i, k) sits at k*Lr*c_z + i*c_z), b' is gathered and contracted as above,
+and K3 finishes the local rows of z in their original orientation.
 
-The collectives are NCCL through torch.distributed on the current stream (the stages only ever
-launch on it, so collective and kernels are stream-ordered).  The three stages are injectable
-(``stages=``) so the data movement can be exercised on CPU ranks with gloo.
+The collectives are NCCL through torch.distributed (the all-gather asynchronous, joined to the
+current stream before the remote blocks are read).  The three stages and the exchange are
+injectable (``stages=``, ``exchange=``) so the data movement can be exercised on CPU ranks
+with gloo, or by threads standing in for ranks on one GPU.
 """
 
 from __future__ import annotations
@@ -52,13 +55,20 @@ class CudaStages:
                                            ops._stream_ptr(self.device)), "tmu_project_gate_ex")
         return a, b
 
-    def contract(self, a, b_parts, M, N, K, rows_per_part):
-        """a [Bc, M, pitch(K)], b_parts [P, Bc, rows_per_part, pitch(K)] -> x [Bc, M, pitch(N)]."""
+    def contract(self, a, b_parts, M, N, K, rows_per_part, x=None, max_ctas=0):
+        """a [Bc, M, pitch(K)], b_parts [P, Bc, rows_per_part, pitch(K)] -> x [Bc, M, >= N].
+
+        ``x`` may be a column block x_full[:, :, c0:] of a wider row-major matrix (its row pitch is
+        taken from its stride); by default a new [Bc, M, pitch(N)] tensor.  ``max_ctas`` > 0 caps
+        the kernel's grid so that SMs stay free for a transfer running alongside."""
         lib = _lib.load()
         Bc = a.shape[0]
-        x = torch.empty(Bc, M, ops.row_pitch(N), dtype=torch.float16, device=self.device)
+        if x is None:
+            x = torch.empty(Bc, M, ops.row_pitch(N), dtype=torch.float16, device=self.device)
         _lib.check(lib.tmu_contract_ex(ops._ptr(a), ops._ptr(b_parts), ops._ptr(x), Bc, M, N, K, rows_per_part,
-                                       ops._ptr(self.status), ops._stream_ptr(self.device)), "tmu_contract_ex")
+                                       x.stride(1), int(max_ctas), ops._ptr(self.status),
+                                       ops._stream_ptr(self.device)),
+                   "tmu_contract_ex")
         return x
 
     def emit_residual(self, x, z, w, mix_eps, out):
@@ -92,6 +102,18 @@ class DistExchange:
         dist.all_to_all_single(recv, send.contiguous(), group=self.group)
         return recv
 
+    def all_gather_start(self, local):
+        """Start an all-gather of ``local``; returns ([P, *local.shape] buffer, handle).  NCCL runs it
+        on its own stream, so kernels enqueued before ``wait(handle)`` overlap the transfer."""
+        out = torch.empty((self.size * local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+        work = dist.all_gather_into_tensor(out, local.contiguous(), group=self.group, async_op=True)
+        return out.view((self.size,) + tuple(local.shape)), work
+
+    def wait(self, handle):
+        """Order the current stream (CPU: block) after an ``all_gather_start``."""
+        handle.wait()
+
 
 class LocalExchange:
     """The exchange of a single rank (P = 1): the collectives are identities."""
@@ -101,6 +123,12 @@ class LocalExchange:
     def all_gather(self, local):
         return local.unsqueeze(0)
 
+    def all_gather_start(self, local):
+        return local.unsqueeze(0), None
+
+    def wait(self, handle):
+        pass
+
     def all_to_all(self, send):
         return send
 
@@ -108,8 +136,12 @@ class LocalExchange:
 class RowShardedTrimul:
     """Triangle update of a pair tensor row-sharded over the ranks of ``group`` (B = 1).
 
+    ``NCCL_SMS``: SMs left free during the overlapped contraction steps.
+
     ``exchange`` replaces the process-group collectives (an object with ``size``, ``rank``,
-    ``all_gather`` and ``all_to_all`` as in :class:`DistExchange`)."""
+    ``all_to_all``, ``all_gather_start`` and ``wait`` as in :class:`DistExchange`)."""
+
+    NCCL_SMS = 16
 
     def __init__(self, L: int, group=None, device=None, stages=None, exchange=None):
         self.exchange = exchange if exchange is not None else DistExchange(group)
@@ -123,11 +155,17 @@ class RowShardedTrimul:
             raise ValueError("rows per rank must be a multiple of 128 (the contraction's B-operand tiles)")
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.stages = stages if stages is not None else CudaStages(self.device)
+        # SMs the contraction may use while a block of b is in flight (the rest run NCCL's copy)
+        self.contract_ctas = 0
+        if self.P > 1 and self.device.type == "cuda":
+            self.contract_ctas = max(1, torch.cuda.get_device_properties(self.device).multi_processor_count
+                                     - self.NCCL_SMS)
 
     def _to_columns(self, t):
         """[Lr(my rows), L, ...] -> [P(source), Lr(source rows), Lr(my columns), ...]."""
         P, Lr = self.P, self.Lr
-        send = torch.stack([t[:, q * Lr:(q + 1) * Lr] for q in range(P)])  # [P(dest), Lr, Lr, ...]
+        # [Lr, P, Lr, ...] -> [P(dest), Lr, Lr, ...]: one copy with Lr*c contiguous elements per run
+        send = t.reshape((Lr, P, Lr) + tuple(t.shape[2:])).transpose(0, 1).contiguous()
         return self.exchange.all_to_all(send)
 
     def __call__(self, z_local: torch.Tensor, mask_local, w: ops.TrimulWeights, outgoing: bool,
@@ -149,6 +187,22 @@ class RowShardedTrimul:
                 mt = self._to_columns(mask_local[0])  # [P, Lr(k), Lr(i)]: mask[k, i] at k*Lr + i
             layout = (1, Lr, L, L * Lr * cz, cz, Lr * cz, L * Lr, 1, Lr)
             a, b = self.stages.project_gate(zt, layout, mt, w)
-        b_parts = self.exchange.all_gather(b)  # [P, Bc, Lr, pitch(L)]
-        x = self.stages.contract(a, b_parts, Lr, L, L, Lr)
+        x = self._contract_ring(a, b)
         return self.stages.emit_residual(x, z_local, w, mix_eps, out)
+
+    def _contract_ring(self, a, b_local):
+        """x = a [all ranks' b]^T, [Bc, Lr, pitch(L)].  The all-gather of b runs on NCCL's stream
+        while the local block is contracted into its column block of x on a grid that leaves
+        SMs to NCCL; then the other blocks are contracted (one call per contiguous run of them)."""
+        P, r, Lr, L = self.P, self.rank, self.Lr, self.L
+        if P == 1:
+            return self.stages.contract(a, b_local.unsqueeze(0), Lr, L, L, Lr)
+        Bc = a.shape[0]
+        x = torch.empty(Bc, Lr, ops.row_pitch(L), dtype=a.dtype, device=a.device)
+        parts, handle = self.exchange.all_gather_start(b_local)  # [P, Bc, Lr, pitch(L)]
+        self.stages.contract(a, b_local.unsqueeze(0), Lr, Lr, L, Lr, x=x[:, :, r * Lr:], max_ctas=self.contract_ctas)
+        self.exchange.wait(handle)
+        for q0, q1 in ((0, r), (r + 1, P)):  # the remote blocks before and after this rank's
+            if q1 > q0:
+                self.stages.contract(a, parts[q0:q1], Lr, (q1 - q0) * Lr, L, Lr, x=x[:, :, q0 * Lr:])
+        return x

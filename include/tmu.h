@@ -128,11 +128,15 @@ int tmu_project_gate_ex(const void* z, const void* mask, const tmu_pair_layout* 
                         int c_z, int c, void* a, void* b, void* status, void* stream);
 
 /* K2 in the outgoing form on slabs: x[d] (M x N) = a[d] (M x K) b[d]^T, a is [Bc, M, pitch(K)],
- * x is [Bc, M, pitch(N)], and b is N / b_rows_per_part consecutive blocks [Bc, b_rows_per_part,
- * pitch(K)] (what an all-gather of the ranks' [Bc, rows, pitch(K)] slabs produces).  With more
- * than one block, b_rows_per_part must be a multiple of 128. */
+ * and b is N / b_rows_per_part consecutive blocks [Bc, b_rows_per_part, pitch(K)] (what an
+ * all-gather of the ranks' [Bc, rows, pitch(K)] slabs produces).  With more than one block,
+ * b_rows_per_part must be a multiple of 128.  x is [Bc, M, ldx] with rows of ldx elements
+ * (ldx = 0: tmu_row_pitch(N)); with ldx > N, x may point at a column block of a wider matrix
+ * (16-byte aligned), so the blocks of b can be contracted one at a time as they arrive.
+ * max_ctas > 0 caps the kernel's persistent grid (one CTA per SM otherwise), leaving SMs free
+ * for kernels that must run alongside it, such as the NCCL transfer of the next block. */
 int tmu_contract_ex(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int b_rows_per_part,
-                    void* status, void* stream);
+                    int ldx, int max_ctas, void* status, void* stream);
 
 /* K3 on a contiguous [B, rows, cols, c_z] slab with x [B*c, rows, pitch(cols)]. */
 int tmu_emit_residual_ex(const void* x, const void* z, void* z_out, int B, int rows, int cols,

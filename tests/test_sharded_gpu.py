@@ -109,6 +109,27 @@ def test_contract_ex_gathered_parts_matches_fp64(P, R, K, Bc):
     assert bool((err <= 2 * ref.abs().clamp_min(1.0) * 2.0**-11 + 1e-2).all()), float(err.max())
 
 
+def test_contract_ex_column_blocks_through_row_pitch():
+    """Each block of b contracted on its own into its column block of one wide x (ldx > N)."""
+    g = torch.Generator().manual_seed(11)
+    P, R, K, Bc, M = 3, 128, 384, 2, 128
+    kp = ops.row_pitch(K)
+    a = torch.randn(Bc, M, kp, generator=g).half()
+    bp = torch.randn(P, Bc, R, kp, generator=g).half()
+    a[:, :, K:] = 0
+    bp[..., K:] = 0
+    st = CudaStages(DEV)
+    ad, bd = a.to(DEV), bp.to(DEV)
+    full = st.contract(ad, bd, M, P * R, K, R)
+    x = torch.full((Bc, M, ops.row_pitch(P * R) + 8), float("nan"), dtype=torch.float16, device=DEV)
+    for q in (2, 0, 1):  # one block on a capped grid (fewer CTAs than tiles)
+        st.contract(ad, bd[q:q + 1], M, R, K, R, x=x[:, :, q * R:], max_ctas=7 if q == 0 else 0)
+    torch.cuda.synchronize()
+    assert ops.read_status(st.status)[0] == 0
+    assert torch.equal(x[:, :, :P * R], full[:, :, :P * R])
+    assert bool(torch.isnan(x[:, :, P * R:]).all())  # nothing written past N
+
+
 @pytest.mark.parametrize("rows,cols,outgoing", [(128, 300, True), (56, 256, False)])
 def test_emit_residual_ex_row_slab_matches_oracle(rows, cols, outgoing):
     direction = "out" if outgoing else "in"
@@ -149,6 +170,12 @@ class _ThreadExchange:
         slots = self._swap(send)
         return torch.stack([slots[q][self.rank] for q in range(self.size)])
 
+    def all_gather_start(self, local):
+        return torch.stack(self._swap(local)), None
+
+    def wait(self, handle):
+        pass
+
 
 class _SerialStages(CudaStages):
     """One launch at a time across the emulating threads."""
@@ -159,9 +186,9 @@ class _SerialStages(CudaStages):
         with self.lock:
             return super().project_gate(*a)
 
-    def contract(self, *a):
+    def contract(self, *a, **kw):
         with self.lock:
-            return super().contract(*a)
+            return super().contract(*a, **kw)
 
     def emit_residual(self, *a):
         with self.lock:
