@@ -85,6 +85,7 @@ SIGNATURES = {
     "tmu_trimul": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp]),
     "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_transition": (_i, [_vp, _vp, _TW, _i, _i, _i, _i, _i, _vp, _vp]),
+    "tmu_disto_expected": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "tmu_selftest_wait_timeout": (_i, [_vp, _ull, _vp]),
 }
 

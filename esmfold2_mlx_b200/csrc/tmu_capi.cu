@@ -17,6 +17,7 @@
 #include "k3_emit.cuh"
 #include "k3w_emit.cuh"
 #include "k4_transition.cuh"
+#include "k5_disto.cuh"
 #include "tmu.h"
 
 using namespace tmu;
@@ -558,6 +559,50 @@ int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel");
 }
 
+template <int CZ>
+int launch_k5(const void* z, const void* w, const float* bias, const float* centres, float* out, int B, int L,
+              DeviceStatus* status, cudaStream_t stream) {
+  using C = k5::Cfg<CZ>;
+  auto kern = &k5::disto_kernel<CZ>;
+  Dev dev;
+  int st = current_device(dev, 1u << (26 + (CZ == 256 ? 1 : 0)), reinterpret_cast<const void*>(kern), C::SMEM_BYTES);
+  if (st) return st;
+  k5::Params p;
+  memset(&p, 0, sizeof(p));
+  int ih = 1, jw = 128;
+  choose_tile(L, L, ih, jw, k5::TILE);
+  const uint64_t e = 2ull * CZ;  // bytes per position
+  {
+    const uint64_t dims[4] = {(uint64_t)CZ, (uint64_t)L, (uint64_t)L, (uint64_t)B};
+    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    const uint64_t str[3] = {e, e * L, e * L * L};     // (c, j, i, b) -> z[b, i, j, c]
+    if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    const uint64_t strt[3] = {e * L, e, e * L * L};    // (c, j, i, b) -> z[b, j, i, c]
+    if ((st = encode_map(&p.tm_zt, z, 4, dims, strt, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)CZ, (uint64_t)k5::NBINS};
+    const uint64_t str[1] = {e};
+    const uint32_t box[2] = {64, 128};
+    if ((st = encode_map(&p.tm_w, w, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  p.bias = bias;
+  p.centres = centres;
+  p.out = out;
+  p.L = L;
+  p.ih = ih;
+  p.jw = jw;
+  p.tiles_i = (L + ih - 1) / ih;
+  p.tiles_j = (L + jw - 1) / jw;
+  p.num_tiles = B * p.tiles_i * p.tiles_j;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms);
+  cudaError_t err = launch_pdl(kern, grid, k5::kThreads, C::SMEM_BYTES, stream, p);
+  if (err == cudaSuccess) err = cudaGetLastError();
+  return err == cudaSuccess ? TMU_OK : cuda_fail(err, "launch disto_kernel");
+}
+
 size_t align256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
 size_t cm_bytes(int B, int L, int c) { return align256(static_cast<size_t>(B) * c * L * row_pitch(L) * 2); }
@@ -837,6 +882,20 @@ int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, 
     if (!aligned16(q)) return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");
   return launch_k4(z, z_out, w, B, L, hidden, activation == TMU_ACT_SWIGLU, static_cast<DeviceStatus*>(status),
                    static_cast<cudaStream_t>(stream));
+}
+
+int tmu_disto_expected(const void* z, const void* w, const float* bias, const float* centres, float* out, int B,
+                       int L, int c_z, int n_bins, void* status, void* stream) {
+  if (B < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "B and L must be positive");
+  if (c_z != 128 && c_z != 256) return fail(TMU_ERR_UNSUPPORTED, "c_z must be 128 or 256");
+  if (n_bins != k5::NBINS) return fail(TMU_ERR_UNSUPPORTED, "the distogram head must have 128 bins");
+  if (L > 8192 || B > 65535) return fail(TMU_ERR_UNSUPPORTED, "L > 8192");
+  if (!z || !w || !centres || !out || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!aligned16(z) || !aligned16(w)) return fail(TMU_ERR_MISALIGNED, "z/w not 16-byte aligned");
+  DeviceStatus* st = static_cast<DeviceStatus*>(status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return c_z == 128 ? launch_k5<128>(z, w, bias, centres, out, B, L, st, s)
+                    : launch_k5<256>(z, w, bias, centres, out, B, L, st, s);
 }
 
 int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream) {

@@ -196,6 +196,14 @@ typedef struct tmu_transition_weights {
 int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int c_z, int hidden,
                    int activation, void* status, void* stream);
 
+/* ---- Distogram expected distance (K5), the convergence signal of adaptive recycling
+ * (var_adaptive_loops.py:43-46): out[b,i,j] = sum_k softmax((z[b,i,j] + z[b,j,i]) @ w^T + bias)_k
+ * * centres[k].  z [B, L, L, c_z] fp16 (c_z = 128 or 256), w fp16 [n_bins, c_z] (the head's
+ * weight rounded to fp16), bias fp32 [n_bins] or NULL, centres fp32 [n_bins], out fp32
+ * [B, L, L]; n_bins = 128. */
+int tmu_disto_expected(const void* z, const void* w, const float* bias, const float* centres, float* out, int B,
+                       int L, int c_z, int n_bins, void* status, void* stream);
+
 /* Self-test of the bounded-wait machinery: launches one CTA that waits on an mbarrier nothing
  * ever arrives at, with a limit of `timeout_ns`; the kernel must give up, record
  * TMU_ERR_DEVICE_TIMEOUT in `status` and exit.  Returns the launch status. */
