@@ -13,9 +13,9 @@
 // is processed in chunks of 64: GEMM1 of chunk k (D1 = h W12_k^T, N = 64, or 2 x 64 for SwiGLU's
 // x1 and x2 halves) lands in one of two TMEM chunk buffers, the activation warps turn it into
 // the fp16 A operand s_k in shared memory, and GEMM2 accumulates D2 += s_k W3_k^T (N = c_z,
-// K = 64) in one of two per-tile TMEM accumulators.  The MMA thread issues G1(0), G1(1), G2(0),
-// G1(2), G2(1), ... so the tensor core computes the next chunk while the current one is being
-// activated.  The weights (256-384 KB) do not fit beside the tiles, so they stream from L2
+// K = 64) in one of two per-tile TMEM accumulators.  The MMA thread issues G1(0), G1(1), G1(2),
+// G2(0), G1(3), G2(1), ... (GEMM1 two chunks ahead), so the tensor core computes the next chunks
+// while the current ones are being activated.  The weights (256-384 KB) do not fit beside the tiles, so they stream from L2
 // through a 4-stage ring of 16 KB items in exactly that order.
 // CTA = 19 warps, one per SM, persistent:
 //   warp 0      TMA: the weight ring
@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
   griddep_wait();
 
   if (warp == 0) {
-    // ---------------- weight ring producer: G1(0), then G1(k), G2(k-1) for k = 1..n-1, G2(n-1) ----------------
+    // ---------------- weight ring producer, in the MMA's order: G1(j), then G2(j-2) ----------------
     if (lane == 0) {
       uint32_t r = 0;
       bool ok = true;
@@ -165,12 +165,12 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
         return true;
       };
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        for (int k = 0; ok && k <= n; ++k) {
-          if (k < n) {  // w12 rows of chunk k (x1), and of x2 for SwiGLU: two 64 x 64 boxes each
-            ok = put(&p.tm_w12, 0, k * CHUNK, 2, 64);
-            if (ok && SWIGLU) ok = put(&p.tm_w12, 0, p.hidden + k * CHUNK, 2, 64);
+        for (int j = 0; ok && j <= n + 1; ++j) {
+          if (j < n) {  // w12 rows of chunk j (x1), and of x2 for SwiGLU: two 64 x 64 boxes each
+            ok = put(&p.tm_w12, 0, j * CHUNK, 2, 64);
+            if (ok && SWIGLU) ok = put(&p.tm_w12, 0, p.hidden + j * CHUNK, 2, 64);
           }
-          if (ok && k >= 1) ok = put(&p.tm_w3, (k - 1) * CHUNK, 0, 1, 0);  // w3[:, chunk k-1]
+          if (ok && j >= 2) ok = put(&p.tm_w3, (j - 2) * CHUNK, 0, 1, 0);  // w3[:, chunk j-2]
         }
       }
       if (abort_sh) {  // drain the loads still in flight before the CTA exits
@@ -210,9 +210,12 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
         if (!(ok = mbar_wait(&hfull[tb], tph, ctx, kSiteMmaH))) break;
         const uint32_t hbase = smem_u32(smem + OFF_H + tb * TILE_BYTES);
         const uint32_t acc = tmem_base + tb * CZ;
-        for (int k = 0; ok && k <= n; ++k) {
-          if (k < n) {  // GEMM1 of chunk gc + k
-            const uint32_t c = gc + k, b = c & 1, cph = (c >> 1) & 1;
+        // GEMM1 runs two chunks ahead of GEMM2: G1(j) needs only that its TMEM buffer has been
+        // read (by the activation of chunk j-2), so the tensor core computes chunk j while
+        // chunks j-1 and j-2 are still being activated.
+        for (int j = 0; ok && j <= n + 1; ++j) {
+          if (j < n) {  // GEMM1 of chunk gc + j
+            const uint32_t c = gc + j, b = c & 1, cph = (c >> 1) & 1;
             if (!(ok = mbar_wait(&d1empty[b], cph ^ 1, ctx, kSiteMmaD1))) break;
             for (int half = 0; half < W1_ITEMS; ++half) {
               const uint32_t s = r % NW, ph = (r / NW) & 1;
@@ -231,11 +234,11 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
             }
             if (!ok) break;
             umma_commit(&d1full[b]);
-            if (k == n - 1) umma_commit(&hempty[tb]);  // the tile's last read of h
+            if (j == n - 1) umma_commit(&hempty[tb]);  // the tile's last read of h
           }
-          if (k >= 1) {  // GEMM2 of chunk gc + k - 1
-            const uint32_t c = gc + k - 1, b = c & 1, cph = (c >> 1) & 1;
-            if (k == 1 && !(ok = mbar_wait(&accempty[tb], tph ^ 1, ctx, kSiteMmaAcc))) break;
+          if (j >= 2) {  // GEMM2 of chunk gc + j - 2
+            const uint32_t c = gc + j - 2, b = c & 1, cph = (c >> 1) & 1;
+            if (j == 2 && !(ok = mbar_wait(&accempty[tb], tph ^ 1, ctx, kSiteMmaAcc))) break;
             if (!(ok = mbar_wait(&sfull[b], cph, ctx, kSiteMmaS))) break;
             const uint32_t s = r % NW, ph = (r / NW) & 1;
             if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
 #pragma unroll
             for (int kk = 0; kk < CHUNK / 16; ++kk)
               umma_f16(acc, sdesc_sw128(sb + kk * 32, 16, 1024), sdesc_sw128(wb + kk * 32, 16, 1024), IDESC2,
-                       (k > 1 || kk > 0) ? 1u : 0u);
+                       (j > 2 || kk > 0) ? 1u : 0u);
             umma_commit(&wempty[s]);
             umma_commit(&sempty[b]);
             ++r;
@@ -287,11 +290,12 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
         if (static_cast<int>(gc & 1) != g) continue;
         const uint32_t b = g, cph = (gc >> 1) & 1;
         if (!(ok = warp_wait(&d1full[b], cph, ctx, kSiteAct))) break;
-        if (!(ok = warp_wait(&sempty[b], cph ^ 1, ctx, kSiteAct))) break;
         tc_fence_after();
-        uint8_t* S = smem + OFF_S + b * S_BYTES;
         const uint32_t d = tmem_base + tl + 256 + b * 128;
+        uint8_t* S = smem + OFF_S + b * S_BYTES;
         if (!SWIGLU) {
+          // ReLU: load and activate the whole chunk, and only then wait for the s buffer (GEMM2 of
+          // chunk gc - 2 done reading it), so that wait overlaps this warp's own work.
           uint32_t x[32], y[32];  // hidden units [0, 32) and [32, 64) of the chunk
           tmem_ld32(d, x);
           tmem_ld32(d + 32, y);
@@ -299,41 +303,42 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&d1empty[b]);
+          uint32_t o[32];
 #pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {  // relu(fp16(v)) == fp16(relu(v)): one rounding
-            const uint32_t* v = c8 < 4 ? x + 8 * c8 : y + 8 * (c8 - 4);
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              o[e] = pack_half2(fmaxf(__uint_as_float(v[2 * e]), 0.0f), fmaxf(__uint_as_float(v[2 * e + 1]), 0.0f));
-            *reinterpret_cast<uint4*>(S + sw128_off(row, c8)) = make_uint4(o[0], o[1], o[2], o[3]);
+          for (int e = 0; e < 16; ++e) {  // relu(fp16(v)) == fp16(relu(v)): one rounding
+            o[e] = pack_half2(fmaxf(__uint_as_float(x[2 * e]), 0.0f), fmaxf(__uint_as_float(x[2 * e + 1]), 0.0f));
+            o[16 + e] = pack_half2(fmaxf(__uint_as_float(y[2 * e]), 0.0f), fmaxf(__uint_as_float(y[2 * e + 1]), 0.0f));
           }
+          if (!(ok = warp_wait(&sempty[b], cph ^ 1, ctx, kSiteAct))) break;
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8)
+            *reinterpret_cast<uint4*>(S + sw128_off(row, c8)) = make_uint4(o[4 * c8], o[4 * c8 + 1], o[4 * c8 + 2], o[4 * c8 + 3]);
         } else {
+          // SwiGLU: the sigmoid makes this the longer computation; holding all 64 results would
+          // spill, so wait for the s buffer first and store 16 hidden units at a time.
+          if (!(ok = warp_wait(&sempty[b], cph ^ 1, ctx, kSiteAct))) break;
 #pragma unroll 1
-          for (int hh = 0; hh < 2; ++hh) {  // 32 hidden units at a time: x1 and x2 columns
-            uint32_t x[32], y[32];
-            tmem_ld32(d + hh * 32, x);
-            tmem_ld32(d + CHUNK + hh * 32, y);
-            tmem_wait_ld2(x, y);
-            if (hh == 1) {  // the chunk buffer has been read: hand it back
+          for (int hq = 0; hq < 4; ++hq) {
+            uint32_t x[16], y[16];
+            tmem_ld16(d + hq * 16, x);
+            tmem_ld16(d + CHUNK + hq * 16, y);
+            tmem_wait_ld16x2(x, y);
+            if (hq == 3) {  // the chunk buffer has been read: hand it back
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(&d1empty[b]);
             }
+            uint32_t o[8];
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-              uint32_t o[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int i = 8 * c8 + 2 * e;
-                const float2 a = round_f16x2(make_float2(__uint_as_float(x[i]), __uint_as_float(x[i + 1])));
-                const float2 c = round_f16x2(make_float2(__uint_as_float(y[i]), __uint_as_float(y[i + 1])));
-                const float2 sg = round_f16x2(sigmoid_f32x2(a));
-                const float2 r = __fmul2_rn(round_f16x2(__fmul2_rn(a, sg)), c);
-                o[e] = pack_half2(r.x, r.y);
-              }
-              *reinterpret_cast<uint4*>(S + sw128_off(row, hh * 4 + c8)) = make_uint4(o[0], o[1], o[2], o[3]);
+            for (int e = 0; e < 8; ++e) {
+              const float2 a = round_f16x2(make_float2(__uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1])));
+              const float2 c = round_f16x2(make_float2(__uint_as_float(y[2 * e]), __uint_as_float(y[2 * e + 1])));
+              const float2 sg = round_f16x2(sigmoid_f32x2(a));
+              const float2 r = __fmul2_rn(round_f16x2(__fmul2_rn(a, sg)), c);
+              o[e] = pack_half2(r.x, r.y);
             }
+            *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * hq)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * hq + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
           }
         }
         fence_proxy_async_smem();
