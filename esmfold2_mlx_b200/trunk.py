@@ -125,13 +125,29 @@ def make_trunk(dtype=torch.float16):
     return _Trunk(ops.MIX_EPS_FP16)
 
 
-class CUDAFoldingTrunk(nn.Module):
-    """Drop-in replacement for ``model.folding_trunk`` (``var_mlx_trunk.py:24-46``)."""
+class _GraphEntry:
+    """One captured trunk pass: static input / mask / output buffers and the CUDA graph."""
 
-    def __init__(self, folding_trunk, dtype=torch.float16, device="cuda", biases: list | None = None):
+    def __init__(self, graph, z_in, mask_in, out):
+        self.graph, self.z_in, self.mask_in, self.out = graph, z_in, mask_in, out
+
+
+class CUDAFoldingTrunk(nn.Module):
+    """Drop-in replacement for ``model.folding_trunk`` (``var_mlx_trunk.py:24-46``).
+
+    With ``graphs=True`` (default) each pass on CUDA input is replayed from a CUDA graph captured
+    once per (B, L, mask present, device) -- the reference recompiles its MLX trunk per new L in
+    the same way (``var_mlx_trunk.py:28-30``) -- so a 24-block pass is one launch instead of
+    ~170; up to ``max_graphs`` shapes are kept (least recently used evicted), each holding its
+    own static buffers.  The graph's output buffer is reused, so the returned tensor is a copy."""
+
+    def __init__(self, folding_trunk, dtype=torch.float16, device="cuda", biases: list | None = None,
+                 graphs: bool = True, max_graphs: int = 4):
         super().__init__()
         self.params = trunk_params(folding_trunk, dtype, device, biases)
         self._fn = make_trunk(dtype)
+        self.graphs, self.max_graphs = graphs, max_graphs
+        self._graph_cache: dict = {}
 
     # FoldingTrunk API the model calls on its trunk; the fused kernels ignore both.
     def set_chunk_size(self, chunk_size):
@@ -140,10 +156,42 @@ class CUDAFoldingTrunk(nn.Module):
     def set_kernel_backend(self, backend):
         pass
 
+    def _graph_pass(self, pair, mask):
+        dev = self.params[0]["out"].device
+        key = (tuple(pair.shape), mask is not None, dev)
+        entry = self._graph_cache.pop(key, None)
+        if entry is None:
+            z_in = torch.empty(pair.shape, dtype=torch.float16, device=dev)
+            mask_in = None if mask is None else torch.empty(mask.shape, dtype=torch.float16, device=dev)
+            z_in.copy_(pair)
+            if mask_in is not None:
+                mask_in.copy_(mask)
+            fn = make_trunk()  # its own workspace, owned by this graph
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):  # eager pass first: sizes every allocation before capture
+                fn(self.params, z_in, mask_in)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                out = fn(self.params, z_in, mask_in)
+            entry = _GraphEntry(graph, z_in, mask_in, out)
+            while len(self._graph_cache) >= self.max_graphs:
+                self._graph_cache.pop(next(iter(self._graph_cache)))
+        self._graph_cache[key] = entry  # most recently used last
+        entry.z_in.copy_(pair)
+        if entry.mask_in is not None:
+            entry.mask_in.copy_(mask)
+        entry.graph.replay()
+        return entry.out.clone()
+
     def forward(self, pair, pair_attention_mask=None):
         # A single-chain fold has an all-ones mask; skipping it saves a multiply per tri-mul.
         mask = None
         if pair_attention_mask is not None and not bool(pair_attention_mask.all()):
             mask = pair_attention_mask
-        out = self._fn(self.params, pair, mask)
+        if self.graphs and pair.is_cuda and not torch.cuda.is_current_stream_capturing():
+            out = self._graph_pass(pair, mask)
+        else:
+            out = self._fn(self.params, pair, mask)
         return out.to(pair.device)

@@ -203,3 +203,22 @@ def test_invalid_arguments_raise():
     assert ops._lib.STATUS_NAMES[code] == "TMU_ERR_INVALID_ARGUMENT"
     code = lib.tmu_contract(None, None, None, 1, 40, 1, None, None)
     assert code == 1
+
+
+def test_trunk_graph_replay_equals_eager_and_is_cached():
+    from esmfold2_mlx_b200.trunk import CUDAFoldingTrunk
+
+    trunk = FoldingTrunk(2, 128, 128, hidden=256, seed=4, ln_noise=0.1)
+    eager = CUDAFoldingTrunk(trunk, graphs=False)
+    graphed = CUDAFoldingTrunk(trunk, graphs=True, max_graphs=2)
+    for L, n_pad in ((40, 0), (57, 5), (40, 0), (57, 5)):
+        z = pair_tensor(1, L, 128, L).to(DEV)
+        mask = pair_mask(1, L, n_pad).to(DEV) if n_pad else None
+        a = eager(z, pair_attention_mask=mask)
+        b = graphed(z, pair_attention_mask=mask)
+        assert torch.equal(a, b)
+    assert len(graphed._graph_cache) == 2  # one graph per (shape, mask) seen, reused on repeat
+    # a third shape evicts the least recently used one
+    z = pair_tensor(1, 33, 128, 1).to(DEV)
+    assert torch.equal(eager(z), graphed(z))
+    assert len(graphed._graph_cache) == 2
