@@ -1,14 +1,14 @@
 """Run one triangle update (or one of its kernels) at a chosen size, for profilers.
 
     python -m esmfold2_mlx_b200.profile_case --L 1024 [--B 1] [--direction out|in]
-           [--stage all|k1|k2|k3|k4] [--reps 3] [--mask-pad 0] [--cz 128|256]
+           [--stage all|k1|k2|k3|k4|k5] [--reps 3] [--mask-pad 0] [--cz 128|256]
            [--hidden 512] [--activation swiglu|relu]
 
 Inputs are seeded synthetic tensors (``synthetic``); weights are random-init.  The chosen stage
 is launched ``--reps`` times after one untimed launch of every stage (and one more of itself), then the script checks the
 device status word and prints the mean CUDA-event time per launch.  Use ``ncu -k regex:<name>``
 with ``project_gate``, ``contract``, ``emit_residual`` or ``transition`` to select a kernel
-(k4 is the fused pair transition, c_z = 128).
+(k4 is the fused pair transition, c_z = 128; k5 the distogram expected distance, ``disto``).
 """
 
 from __future__ import annotations
@@ -26,7 +26,7 @@ def main():
     ap.add_argument("--L", type=int, default=1024)
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--direction", choices=["out", "in"], default="out")
-    ap.add_argument("--stage", choices=["all", "k1", "k2", "k3", "k4"], default="all")
+    ap.add_argument("--stage", choices=["all", "k1", "k2", "k3", "k4", "k5"], default="all")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--mask-pad", type=int, default=0)
     ap.add_argument("--cz", type=int, choices=[128, 256], default=128, help="c_z = c")
@@ -55,6 +55,12 @@ def main():
         "k3": lambda: ops.emit_residual(x, z, w, out=out, status=status),
         "all": lambda: ops.trimul(z, mask, w, outgoing, out=out),
     }
+    if args.stage == "k5":
+        from torch import nn
+
+        from .adaptive import DistoHead, expected_distance
+        head = DistoHead(nn.Linear(args.cz, 128), dev)
+        stages["k5"] = lambda: expected_distance(z, head)
     if args.stage == "k4":
         tw = ops.TransitionWeights.from_module(trunk.blocks[0].pair_transition, dev)
         stages["k4"] = lambda: ops.transition(z, tw, out=out, status=status)
