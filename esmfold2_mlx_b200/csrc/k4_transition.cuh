@@ -47,7 +47,7 @@ constexpr int OFF_S = OFF_H + 2 * TILE_BYTES;    // 2 buffers
 constexpr int OFF_W = OFF_S + 2 * S_BYTES;       // NW ring items
 constexpr int OFF_PAR = OFF_W + NW * W_BYTES;    // fp32 LN gamma[128], beta[128]
 constexpr int OFF_BAR = OFF_PAR + 2 * CZ * 4;
-constexpr int SMEM_BYTES = OFF_BAR + 256;
+constexpr int SMEM_BYTES = OFF_BAR + 512;
 constexpr int kThreads = 608;
 constexpr int TMEM_COLS = 512;
 static_assert(SMEM_BYTES <= 232448, "K4 shared memory exceeds the per-block limit");
@@ -105,6 +105,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
   uint64_t& drain_bar = bars[28];
   uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 29);
   volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 29) + 4);
+  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 30);  // [4 groups][2] group_wait verdicts
   float* par = reinterpret_cast<float*>(smem + OFF_PAR);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -264,11 +265,10 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
   } else if (warp < 7) {
     // ---------------- LayerNorm: z tile -> h ----------------
     const int row = threadIdx.x - 96;
-    uint32_t it = 0;
+    uint32_t it = 0, gcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
-      if (!warp_wait(&hempty[s], ph ^ 1, ctx, kSiteLn)) break;
-      if (!warp_wait(&zfull[s], ph, ctx, kSiteLn)) break;
+      if (!group_wait(&hempty[s], ph ^ 1, &zfull[s], ph, ctx, kSiteLn, row == 0, 4, 128, gflags + 6, gcount)) break;
       ln_row128_sw128(smem + OFF_Z + s * TILE_BYTES, smem + OFF_H + s * TILE_BYTES, ATOM_BYTES, row, 1e-5f,
                       LnParSmem{par, par + CZ});
       fence_proxy_async_smem();
@@ -283,13 +283,15 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const uint32_t tl = static_cast<uint32_t>(q * 32) << 16;
-    uint32_t gc = 0;
+    const bool leader = (warp - 7) % 4 == 0 && lane == 0;
+    uint32_t gc = 0, gcount = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
       for (int k = 0; k < n; ++k, ++gc) {
         if (static_cast<int>(gc & 1) != g) continue;
         const uint32_t b = g, cph = (gc >> 1) & 1;
-        if (!(ok = warp_wait(&d1full[b], cph, ctx, kSiteAct))) break;
+        if (!(ok = group_wait(&d1full[b], cph, nullptr, 0, ctx, kSiteAct, leader, 1 + g, 128, gflags + 2 * g, gcount)))
+          break;
         tc_fence_after();
         const uint32_t d = tmem_base + tl + 256 + b * 128;
         uint8_t* S = smem + OFF_S + b * S_BYTES;
@@ -309,14 +311,18 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
             o[e] = pack_half2(fmaxf(__uint_as_float(x[2 * e]), 0.0f), fmaxf(__uint_as_float(x[2 * e + 1]), 0.0f));
             o[16 + e] = pack_half2(fmaxf(__uint_as_float(y[2 * e]), 0.0f), fmaxf(__uint_as_float(y[2 * e + 1]), 0.0f));
           }
-          if (!(ok = warp_wait(&sempty[b], cph ^ 1, ctx, kSiteAct))) break;
+          if (!(ok = group_wait(&sempty[b], cph ^ 1, nullptr, 0, ctx, kSiteAct, leader, 1 + g, 128, gflags + 2 * g,
+                                gcount)))
+            break;
 #pragma unroll
           for (int c8 = 0; c8 < 8; ++c8)
             *reinterpret_cast<uint4*>(S + sw128_off(row, c8)) = make_uint4(o[4 * c8], o[4 * c8 + 1], o[4 * c8 + 2], o[4 * c8 + 3]);
         } else {
           // SwiGLU: the sigmoid makes this the longer computation; holding all 64 results would
           // spill, so wait for the s buffer first and store 16 hidden units at a time.
-          if (!(ok = warp_wait(&sempty[b], cph ^ 1, ctx, kSiteAct))) break;
+          if (!(ok = group_wait(&sempty[b], cph ^ 1, nullptr, 0, ctx, kSiteAct, leader, 1 + g, 128, gflags + 2 * g,
+                                gcount)))
+            break;
 #pragma unroll 1
           for (int hq = 0; hq < 4; ++hq) {
             uint32_t x[16], y[16];
@@ -352,13 +358,14 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     const int row = q * 32 + lane;
     const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
     const uint32_t tl = static_cast<uint32_t>(q * 32) << 16;
-    uint32_t it = 0;
+    uint32_t it = 0, gcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const uint32_t tb = it & 1, tph = (it >> 1) & 1;
-      if (!warp_wait(&accfull[tb], tph, ctx, kSiteEpi)) break;
-      if (!warp_wait(&zfull[tb], tph, ctx, kSiteEpi)) break;
+      if (!group_wait(&accfull[tb], tph, &zfull[tb], tph, ctx, kSiteEpi, warp == 15 && lane == 0, 3, 128, gflags + 4,
+                      gcount))
+        break;
       tc_fence_after();
       uint8_t* Z = smem + OFF_Z + tb * TILE_BYTES;
 #pragma unroll 1

@@ -121,6 +121,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// A group of warps waits for one or two mbarrier phases: one thread (`leader`) waits (bounded)
+// and the group meets at named barrier `bar_id`, where the other warps park without issuing
+// instructions.  The verdict goes through flags[count & 1] (count = this group's wait counter,
+// advanced identically by every thread): a slow reader of wait k still finds wait k's verdict,
+// because the leader writes that slot again only after every thread has reached wait k+1.
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, uint64_t* bar2, uint32_t parity2,
+                                           const WaitCtx& ctx, unsigned int site, bool leader, uint32_t bar_id,
+                                           uint32_t nthreads, volatile int* flags, uint32_t& count) {
+  volatile int* flag = flags + (count & 1);
+  ++count;
+  if (leader) {
+    bool ok = mbar_wait(bar, parity, ctx, site);
+    if (ok && bar2 != nullptr) ok = mbar_wait(bar2, parity2, ctx, site);
+    *flag = ok ? 1 : 0;
+  }
+  named_bar_sync(bar_id, nthreads);
+  return *flag != 0;
+}
+
 // Bounded wait used while winding down after an abort: never raises, gives up silently.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
