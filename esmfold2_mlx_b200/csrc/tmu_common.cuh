@@ -121,25 +121,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
-// A group of warps waits for one or two mbarrier phases: one thread (`leader`) waits (bounded)
-// and the group meets at named barrier `bar_id`, where the other warps park without issuing
-// instructions.  The verdict goes through flags[count & 1] (count = this group's wait counter,
-// advanced identically by every thread): a slow reader of wait k still finds wait k's verdict,
-// because the leader writes that slot again only after every thread has reached wait k+1.
-__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, uint64_t* bar2, uint32_t parity2,
-                                           const WaitCtx& ctx, unsigned int site, bool leader, uint32_t bar_id,
-                                           uint32_t nthreads, volatile int* flags, uint32_t& count) {
-  volatile int* flag = flags + (count & 1);
-  ++count;
-  if (leader) {
-    bool ok = mbar_wait(bar, parity, ctx, site);
-    if (ok && bar2 != nullptr) ok = mbar_wait(bar2, parity2, ctx, site);
-    *flag = ok ? 1 : 0;
-  }
-  named_bar_sync(bar_id, nthreads);
-  return *flag != 0;
-}
-
 // Bounded wait used while winding down after an abort: never raises, gives up silently.
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
@@ -158,6 +139,25 @@ __device__ __forceinline__ void griddep_trigger() { asm volatile("griddepcontrol
 
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// A group of warps waits for one or two mbarrier phases: one thread (`leader`) waits (bounded)
+// and the group meets at named barrier `bar_id`, where the other warps park without issuing
+// instructions.  The verdict goes through flags[count & 1] (count = this group's wait counter,
+// advanced identically by every thread): a slow reader of wait k still finds wait k's verdict,
+// because the leader writes that slot again only after every thread has reached wait k+1.
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, uint64_t* bar2, uint32_t parity2,
+                                           const WaitCtx& ctx, unsigned int site, bool leader, uint32_t bar_id,
+                                           uint32_t nthreads, volatile int* flags, uint32_t& count) {
+  volatile int* flag = flags + (count & 1);
+  ++count;
+  if (leader) {
+    bool ok = mbar_wait(bar, parity, ctx, site);
+    if (ok && bar2 != nullptr) ok = mbar_wait(bar2, parity2, ctx, site);
+    *flag = ok ? 1 : 0;
+  }
+  named_bar_sync(bar_id, nthreads);
+  return *flag != 0;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -569,6 +569,58 @@ __device__ __forceinline__ void ln_atom_apply(const uint8_t* src, uint8_t* dst, 
     const uint32_t u[4] = {v.x, v.y, v.z, v.w};
     float g[8], b[8];
     par(8 * part + c16, g, b);
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      unsigned short lo, hi;
+      split_half2(u[e], lo, hi);
+      const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
+      const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
+      o[e] = pack_half2(y.x, y.y);
+    }
+    *reinterpret_cast<uint4*>(dst + off) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// LayerNorm of a 128-channel row (two 128B-swizzled atoms) by a lane pair (lanes 2r, 2r+1 of a
+// warp): lane parity `half` owns the 16-byte chunks of that parity in both atoms (channels
+// 8c..8c+7 for c = half, half+2, ..); the partial sums meet through one shuffle.  Interleaving
+// by chunk keeps the pair's two accesses in different banks of the same 128-byte row.
+template <typename Par>
+__device__ __forceinline__ void ln_row128_pair_sw128(const uint8_t* src, uint8_t* dst, int atom_bytes, int row,
+                                                     int half, float eps, Par par) {
+  const float k = __half2float(*reinterpret_cast<const __half*>(src + sw128_off(row, 0)));
+  float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c16 = 2 * i + half;  // chunk index over both atoms
+    const uint4 v = *reinterpret_cast<const uint4*>(src + (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7));
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      unsigned short lo, hi;
+      split_half2(u[e], lo, hi);
+      const float2 d = make_float2(add_f16_f32(lo, -k), add_f16_f32(hi, -k));
+      s1 = __fadd2_rn(s1, d);
+      s2 = __ffma2_rn(d, d, s2);
+    }
+  }
+  float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+  t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
+  t2 += __shfl_xor_sync(0xffffffffu, t2, 1);
+  const float m1 = t1 * (1.0f / 128);
+  const float var = fmaxf(t2 * (1.0f / 128) - m1 * m1, 0.0f);
+  const float mean = k + m1;
+  const float2 r2 = make_float2(rsqrtf(var + eps), rsqrtf(var + eps));
+  asm volatile("" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c16 = 2 * i + half;
+    const int off = (c16 >> 3) * atom_bytes + sw128_off(row, c16 & 7);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    float g[8], b[8];
+    par(c16, g, b);
     uint32_t o[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
