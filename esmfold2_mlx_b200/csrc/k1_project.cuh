@@ -17,12 +17,13 @@
 // TMEM lanes (columns [0,64) and [64,128) of a slot), so the gate pairs up in registers.
 //
 // One tile = 128 pair positions, an ih x jw block of the L x L grid (ih * jw = 128), chosen by
-// the host to minimise padding at ragged L.  CTA = 22 warps, one per SM, persistent:
+// the host to minimise padding at ragged L.  CTA = 26 warps, one per SM, persistent:
 //   warp 0      TMA: packed weights once (resident, 4c x c_z fp16), then z tiles (2 stages)
 //   warp 1      TMEM allocation (512 columns = 4 slots of 128: {a, b} x {positions 0-63,
 //               64-127}) and the MMA thread, which refills a slot as soon as it is drained
-//   warps 2-5   LayerNorm of the z tile in place (thread = position) + the tile's mask as fp32
-//   warps 6-21  epilogue: four warps (one per TMEM lane quadrant) per slot; per 16 positions:
+//   warps 2-9   LayerNorm of the z tile in place (a lane pair per position, each lane one half of
+//               the channels, interleaved by 16-byte chunk) + the tile's mask as fp32
+//   warps 10-25 epilogue: four warps (one per TMEM lane quadrant) per slot; per 16 positions:
 //               gate, mask, fp16, 32 B per thread into a 2 KB staging block; every 32 positions
 //               a per-warp TMA store of the 32-channel x 32-position box (64-byte rows when
 //               jw >= 32), staged with the swizzle that keeps a warp's 32 row writes free of
@@ -55,7 +56,7 @@ constexpr int OFF_PAR = OFF_STG + NEPI * WSTG_BYTES;      // fp32 LN gamma, beta
 constexpr int OFF_MASK = OFF_PAR + 2 * CZ * 4;            // fp32 mask per tile position
 constexpr int OFF_BAR = OFF_MASK + NMASK * TILE * 4;     // mbarriers and flags
 constexpr int SMEM_BYTES = OFF_BAR + 256;                 // no alignment slack: the kernel checks the base
-constexpr int kThreads = 704;
+constexpr int kThreads = 832;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
@@ -121,14 +122,14 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&zfull[s], 1);
       mbar_init(&zempty[s], 1);
-      mbar_init(&lnfull[s], 4);  // one arrival per LayerNorm warp
+      mbar_init(&lnfull[s], 8);  // one arrival per LayerNorm warp
     }
     for (int s = 0; s < NSLOT; ++s) {
       mbar_init(&tfull[s], 1);
       mbar_init(&tempty[s], 4);  // one arrival per epilogue warp draining the slot
     }
     for (int k = 0; k < NMASK; ++k) {
-      mbar_init(&mfull[k], 4);      // LayerNorm warps wrote the tile's mask
+      mbar_init(&mfull[k], 8);      // LayerNorm warps wrote the tile's mask
       mbar_init(&mempty[k], NEPI);  // every epilogue warp is done with it
     }
     mbar_init(&drain_bar, 1);
@@ -218,9 +219,9 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
       umma_commit(&drain_bar);
       mbar_drain(&drain_bar, 0, 200000000ull);
     }
-  } else if (warp < 6) {
-    // ---------------- LayerNorm of the z tile in place; the tile's mask as fp32 ----------------
-    const int row = threadIdx.x - 64;
+  } else if (warp < 10) {
+    // ---------------- LayerNorm of the z tile in place (a lane pair per row); the tile's mask ----------------
+    const int row = (threadIdx.x - 64) >> 1, half = threadIdx.x & 1;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
@@ -230,26 +231,28 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
         int bb, i0, j0;
         decode_tile(p, tile, bb, i0, j0);
         const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
-        float m = 0.0f;
-        if (gi < p.rows && gj < p.cols) m = __half2float(p.mask[bb * p.mask_sb + gi * p.mask_si + gj * p.mask_sj]);
-        maskf[k * TILE + row] = m;
+        if (half == 0) {
+          float m = 0.0f;
+          if (gi < p.rows && gj < p.cols) m = __half2float(p.mask[bb * p.mask_sb + gi * p.mask_si + gj * p.mask_sj]);
+          maskf[k * TILE + row] = m;
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&mfull[k]);
       }
       if (!warp_wait(&zfull[s], ph, ctx, kSiteLn)) break;
       uint8_t* A = smem + OFF_A + s * A_BYTES;
-      ln_row128_sw128(A, A, ATOM_BYTES, row, 1e-5f, LnParSmem{par, par + CZ});
+      ln_row128_pair_sw128(A, A, ATOM_BYTES, row, half, 1e-5f, LnParSmem{par, par + CZ});
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
       __syncwarp();
       if (lane == 0) mbar_arrive(&lnfull[s]);
     }
   } else {
     // ---------------- epilogue: gate, mask, channel-major store ----------------
-    const int slot = (warp - 6) >> 2;  // 2 * (a: 0, b: 1) + position half
+    const int slot = (warp - 10) >> 2;  // 2 * (a: 0, b: 1) + position half
     const int x = slot >> 1, hpos = slot & 1;
     const int q = warp & 3;            // TMEM lane quadrant = channels [32q, 32q+32)
     const int ch = q * 32 + lane;      // this thread's output channel
-    uint8_t* stg = smem + OFF_STG + (warp - 6) * WSTG_BYTES;
+    uint8_t* stg = smem + OFF_STG + (warp - 10) * WSTG_BYTES;
     // Byte offsets in the staging block of this thread's two 16-byte chunks c of compute step
     // st (positions 16 st + 8 c ..), matching the store box and its swizzle:
     //   jw >= 32: box {32, 1, 32}, 64 B rows (row = channel), 64B swizzle
