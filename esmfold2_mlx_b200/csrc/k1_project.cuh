@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   uint64_t& drain_bar = bars[21];
   uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 22);
   volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 22) + 4);
+  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 23);  // [5 groups][2] group_wait verdicts
   float* par = reinterpret_cast<float*>(smem + OFF_PAR);    // [gamma 128 | beta 128]
   float* maskf = reinterpret_cast<float*>(smem + OFF_MASK);  // [NMASK][128]
   const int warp = threadIdx.x >> 5;
@@ -222,12 +223,15 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   } else if (warp < 10) {
     // ---------------- LayerNorm of the z tile in place (a lane pair per row); the tile's mask ----------------
     const int row = (threadIdx.x - 64) >> 1, half = threadIdx.x & 1;
-    uint32_t it = 0;
+    uint32_t it = 0, gcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      // one thread waits for the z tile (and the mask stage), the other warps park on barrier 1
+      const uint32_t k = it % NMASK, mph = (it / NMASK) & 1;
+      if (!group_wait(&zfull[s], ph, HAS_MASK ? &mempty[k] : nullptr, mph ^ 1, ctx, kSiteLn, threadIdx.x == 64, 1,
+                      256, gflags, gcount))
+        break;
       if (HAS_MASK) {  // stage k of the mask ring holds tiles k, k + NMASK, ...
-        const uint32_t k = it % NMASK, mph = (it / NMASK) & 1;
-        if (!warp_wait(&mempty[k], mph ^ 1, ctx, kSiteLn)) break;
         int bb, i0, j0;
         decode_tile(p, tile, bb, i0, j0);
         const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
@@ -239,7 +243,6 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
         __syncwarp();
         if (lane == 0) mbar_arrive(&mfull[k]);
       }
-      if (!warp_wait(&zfull[s], ph, ctx, kSiteLn)) break;
       uint8_t* A = smem + OFF_A + s * A_BYTES;
       ln_row128_pair_sw128(A, A, ATOM_BYTES, row, half, 1e-5f, LnParSmem{par, par + CZ});
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
@@ -281,12 +284,15 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     const float2 bs2 = make_float2(bs, bs), bg2 = make_float2(bg, bg);
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 128;
     const CUtensorMap* tm = x == 0 ? &p.tm_a : &p.tm_b;
-    uint32_t it = 0;
+    uint32_t it = 0, gcount = 0;
+    const bool leader = ((warp - 10) & 3) == 0 && lane == 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
-      if (!warp_wait(&tfull[slot], it & 1, ctx, kSiteEpilogue)) break;
-      if (HAS_MASK && !warp_wait(&mfull[it % NMASK], (it / NMASK) & 1, ctx, kSiteEpilogue)) break;
+      // one thread of the slot's four warps waits, the others park on barrier 2 + slot
+      if (!group_wait(&tfull[slot], it & 1, HAS_MASK ? &mfull[it % NMASK] : nullptr, (it / NMASK) & 1, ctx,
+                      kSiteEpilogue, leader, 2 + slot, 128, gflags + 2 + 2 * slot, gcount))
+        break;
       tc_fence_after();
       const float* mrow = maskf + (it % NMASK) * TILE + hpos * 64;
 #pragma unroll 1

@@ -99,6 +99,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   uint64_t& drain_bar = bars[15];
   uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 16);
   volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 16) + 4);
+  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 18);  // [3 groups][2] group_wait verdicts
   volatile int& x_ok_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 16) + 8);
   float* par = reinterpret_cast<float*>(smem + OFF_PAR);
   const int warp = threadIdx.x >> 5;
@@ -251,11 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   } else if (warp < 10) {
     // ---------------- A2 = LN_in of each position's z row ----------------
     const int row = threadIdx.x - 192;
-    uint32_t it = 0;
+    uint32_t it = 0, gcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
-      if (!warp_wait(&a2empty, (it & 1) ^ 1, ctx, kSiteTrA)) break;
-      if (!warp_wait(&zfull[s], ph, ctx, kSiteTrZ)) break;
+      if (!group_wait(&a2empty, (it & 1) ^ 1, &zfull[s], ph, ctx, kSiteTrZ, row == 0, 2, 128, gflags, gcount)) break;
       ln_row128_sw128(smem + OFF_Z + s * TILE_BYTES, smem + OFF_A2, ATOM_BYTES, row, 1e-5f,
                       LnParSmem{par, par + 128});
       fence_proxy_async_smem();
@@ -269,14 +269,17 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     const int row = q * 32 + lane;
     const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
     constexpr bool has_be = HAS_BIAS, has_bg = HAS_BIAS;
-    uint32_t it = 0;
+    uint32_t it = 0, gcount = 0;
+    const bool leader = ((warp - 10) & 3) == 0 && lane == 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
       const uint32_t acc = it & 1, aph = (it >> 1) & 1;
-      if (!warp_wait(&tfull[acc], aph, ctx, kSiteEpilogue)) break;
-      if (!warp_wait(&zfull[s], ph, ctx, kSiteEpilogue)) break;
+      // one thread of each channel half's four warps waits, the others park on barrier 3 + h
+      if (!group_wait(&tfull[acc], aph, &zfull[s], ph, ctx, kSiteEpilogue, leader, 3 + h, 128, gflags + 2 + 2 * h,
+                      gcount))
+        break;
       tc_fence_after();
       uint8_t* Zh = smem + OFF_Z + s * TILE_BYTES + h * ATOM_BYTES;
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256 + h * 64;
