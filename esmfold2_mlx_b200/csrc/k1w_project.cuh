@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_w_kernel(const __gri
   uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 24);
   volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 24) + 4);
   volatile int& ln_ok_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 24) + 8);
+  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 26);  // [4 groups][2] group_wait verdicts
   __half* par = reinterpret_cast<__half*>(smem + OFF_PAR);     // [gamma 256 | beta 256]
   __half* maskh = reinterpret_cast<__half*>(smem + OFF_MASK);  // [NSLOT][64]
   float2* red = reinterpret_cast<float2*>(smem + OFF_RED);
@@ -280,13 +281,16 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_w_kernel(const __gri
     const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + g * 128;
     const CUtensorMap* tm = xsel == 0 ? &p.tm_a : &p.tm_b;
     const __half* mrow = maskh + g * TILE;
-    uint32_t it = g;
+    uint32_t it = g, gcount = 0;
+    const bool leader = ((warp - 6) & 3) == 0 && lane == 0;
     for (int tile = blockIdx.x + g * gridDim.x; tile < p.num_tiles; tile += 4 * gridDim.x, it += 4) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const uint32_t sph = (it >> 2) & 1;
-      if (!warp_wait(&tfull[g], sph, ctx, kSiteEpilogue)) break;
-      if (HAS_MASK && !warp_wait(&mfull[g], sph, ctx, kSiteEpilogue)) break;
+      // one thread of the group waits, the other warps park on barrier 2 + g
+      if (!group_wait(&tfull[g], sph, HAS_MASK ? &mfull[g] : nullptr, sph, ctx, kSiteEpilogue, leader, 2 + g, 128,
+                      gflags + 2 * g, gcount))
+        break;
       tc_fence_after();
 #pragma unroll 1
       for (int pb = 0; pb < TILE; pb += POS) {

@@ -79,6 +79,7 @@ __global__ void __launch_bounds__(kThreads, 1) disto_kernel(const __grid_constan
   uint64_t& drain_bar = bars[9];
   uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 10);
   volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 10) + 4);
+  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 11);  // [2] group_wait verdicts
   float* bias = reinterpret_cast<float*>(smem + C::OFF_PAR);
   float* centres = bias + NBINS;
   const int warp = threadIdx.x >> 5;
@@ -180,12 +181,13 @@ __global__ void __launch_bounds__(kThreads, 1) disto_kernel(const __grid_constan
     const int row = q * 32 + lane;  // tile position
     const uint32_t tl = static_cast<uint32_t>(q * 32) << 16;
     constexpr float kLog2e = 1.4426950408889634f;
-    uint32_t it = 0;
+    uint32_t it = 0, gcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const uint32_t b = it & 1, bph = (it >> 1) & 1;
-      if (!warp_wait(&accfull[b], bph, ctx, kSiteEpi)) break;
+      if (!group_wait(&accfull[b], bph, nullptr, 0, ctx, kSiteEpi, warp == 2 && lane == 0, 1, 128, gflags, gcount))
+        break;
       tc_fence_after();
       float m = -INFINITY, den = 0.0f, num = 0.0f;
 #pragma unroll 1
