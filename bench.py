@@ -326,7 +326,7 @@ def run_sharded(args, ws, rank, local):
     while the local block is contracted, and each rank finishes its rows.  Eager launches (no
     graph); inputs per rank (>= 302 MB at N = 8) exceed L2, so no flush is needed."""
     from esmfold2_mlx_b200 import _lib, ops
-    from esmfold2_mlx_b200.sharded import DistExchange, LocalExchange, RowShardedTrimul
+    from esmfold2_mlx_b200.sharded import CopyEngineExchange, DistExchange, LocalExchange, RowShardedTrimul
     from esmfold2_mlx_b200.synthetic import CONFIGS, FoldingTrunk, pair_tensor
 
     device = torch.device("cuda", local)
@@ -337,7 +337,12 @@ def run_sharded(args, ws, rank, local):
     trunk = FoldingTrunk(1, C_Z, C, seed=cfg.seed)
     w = {d: ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + d), device) for d in ("out", "in")}
 
-    ex = DistExchange(None) if ws > 1 else LocalExchange()
+    if ws == 1:
+        ex = LocalExchange()
+    elif args.c5_nccl:
+        ex = DistExchange(None)
+    else:
+        ex = CopyEngineExchange(None)
     sh = RowShardedTrimul(L, device=device, exchange=ex)
     Lr = sh.Lr
     z_host = pair_tensor(1, L, C_Z, cfg.seed).half()[:, rank * Lr:(rank + 1) * Lr].contiguous()
@@ -405,11 +410,15 @@ def run_sharded(args, ws, rank, local):
                     "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": 6 * args.steps,
             "collectives": {"recv_bytes_per_rank_per_step": recv,
-                            "note": "all-to-all of z blocks (incoming form); asynchronous all-gather of b "
-                                    "overlapped with the contraction of the local block"},
+                            "b_transfer": "NCCL all-gather" if (ws > 1 and args.c5_nccl) else
+                                          ("copy engines (CUDA IPC, cudaMemcpyAsync)" if ws > 1 else "none"),
+                            "note": "all-to-all of z blocks (incoming form, NCCL); b's remote blocks arrive "
+                                    "while the local block is contracted"},
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    if hasattr(ex, "close"):
+        ex.close()
 
 
 def run_b200(args, ws, rank, local):
@@ -602,6 +611,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-trunk", action="store_true", help="skip the trunk-recycle (config 3) measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--c5-nccl", action="store_true",
+                    help="c5: move b with an NCCL all-gather instead of copy-engine peer copies")
     ap.add_argument("--workload", choices=WORKLOADS, default="c2",
                     help="c2 (default: the metric's configuration), c1, c4 (64 folds x L=146), L2048, "
                          "c5 (one L=3072 fold row-sharded over the N ranks), c2w / L2048w (c_z = c = 256)")

@@ -15,6 +15,7 @@ LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libtmu.so")
 
 TMU_STATUS_BYTES = 256
+TMU_IPC_HANDLE_BYTES = 64
 
 STATUS_NAMES = {
     0: "TMU_OK",
@@ -86,6 +87,10 @@ SIGNATURES = {
     "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_transition": (_i, [_vp, _vp, _TW, _i, _i, _i, _i, _i, _vp, _vp]),
     "tmu_disto_expected": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "tmu_ipc_export": (_i, [_vp, _vp, ctypes.POINTER(_ull)]),
+    "tmu_ipc_import": (_i, [_vp, _ull, ctypes.POINTER(_vp)]),
+    "tmu_ipc_close": (_i, [_vp]),
+    "tmu_copy_async": (_i, [_vp, _vp, _sz, _vp]),
     "tmu_selftest_wait_timeout": (_i, [_vp, _ull, _vp]),
 }
 

@@ -59,6 +59,25 @@ int get_encoder() {
   return st;
 }
 
+// Start address of the allocation that contains `ptr` (cuMemGetAddressRange through the runtime's
+// driver entry point, as for the tensor-map encoder: the library does not link libcuda).
+int allocation_base(const void* ptr, CUdeviceptr* base) {
+  static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 3020, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(f);
+  });
+  if (fn == nullptr) return fail(TMU_ERR_DRIVER, "cuMemGetAddressRange entry point not available");
+  size_t size = 0;
+  if (fn(base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+    return fail(TMU_ERR_INVALID_ARGUMENT, "pointer is not inside a device allocation");
+  return TMU_OK;
+}
+
 int encode_map(CUtensorMap* m, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
                const uint32_t* box, CUtensorMapSwizzle sw) {
   int st = get_encoder();
@@ -896,6 +915,46 @@ int tmu_disto_expected(const void* z, const void* w, const float* bias, const fl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return c_z == 128 ? launch_k5<128>(z, w, bias, centres, out, B, L, st, s)
                     : launch_k5<256>(z, w, bias, centres, out, B, L, st, s);
+}
+
+int tmu_ipc_export(const void* ptr, void* handle, unsigned long long* offset) {
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL argument");
+  CUdeviceptr base = 0;
+  int st = allocation_base(ptr, &base);
+  if (st) return st;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == TMU_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = reinterpret_cast<CUdeviceptr>(ptr) - base;
+  return TMU_OK;
+}
+
+int tmu_ipc_import(const void* handle, unsigned long long offset, void** ptr) {
+  if (handle == nullptr || ptr == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return TMU_OK;
+}
+
+int tmu_ipc_close(void* ptr) {
+  if (ptr == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL argument");
+  CUdeviceptr base = 0;
+  int st = allocation_base(ptr, &base);
+  if (st) return st;
+  cudaError_t e = cudaIpcCloseMemHandle(reinterpret_cast<void*>(base));
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int tmu_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (dst == nullptr || src == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL argument");
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "cudaMemcpyAsync");
 }
 
 int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream) {

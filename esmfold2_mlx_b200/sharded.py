@@ -41,15 +41,15 @@ class CudaStages:
         self.device = torch.device(device)
         self.status = ops.new_status(self.device)
 
-    def project_gate(self, z, layout, mask, w):
+    def project_gate(self, z, layout, mask, w, b_out=None):
         """z: storage holding a [B, rows, cols, c_z] view with element strides
         (stride_b, stride_row, stride_col); mask likewise with mask strides (or None).
-        Returns a, b: [B*c, rows, pitch(cols)]."""
+        Returns a, b: [B*c, rows, pitch(cols)] (b written into ``b_out`` when given)."""
         B, rows, cols, sb, sr, sc, msb, msr, msc = layout
         lib = _lib.load()
         g = _lib.TmuPairLayout(B, rows, cols, sb, sr, sc, msb, msr, msc)
         a = torch.empty(B * w.c, rows, ops.row_pitch(cols), dtype=torch.float16, device=self.device)
-        b = torch.empty_like(a)
+        b = torch.empty_like(a) if b_out is None else b_out
         _lib.check(lib.tmu_project_gate_ex(ops._ptr(z), ops._ptr(mask), ctypes.byref(g), ctypes.byref(w.struct),
                                            w.c_z, w.c, ops._ptr(a), ops._ptr(b), ops._ptr(self.status),
                                            ops._stream_ptr(self.device)), "tmu_project_gate_ex")
@@ -115,6 +115,115 @@ class DistExchange:
         handle.wait()
 
 
+class CopyEngineExchange(DistExchange):
+    """The b slabs moved by the GPUs' copy engines instead of NCCL kernels.
+
+    Each rank writes its b slab into one of two persistent buffers (alternating per call) that
+    every peer has mapped once through CUDA IPC (``tmu_ipc_export`` / ``tmu_ipc_import``).  Per
+    call: the owner records an interprocess "ready" event after K1; the ranks meet at a host
+    barrier (gloo), so every peer enqueues its wait after that record; each rank's copy stream
+    waits on the peers' ready events and pulls their slabs with ``cudaMemcpyAsync`` over NVLink
+    (``tmu_copy_async``) -- no SM time, so the local block's contraction runs at full speed
+    beside it -- and records a "read" event that the owner waits on before it rewrites the same
+    buffer two calls later.  No kernel reads another GPU's memory.  The incoming form's
+    all-to-all of z blocks stays on NCCL (``DistExchange``).
+    """
+
+    def __init__(self, group=None, host_group=None):
+        super().__init__(group)
+        self.host_group = host_group if host_group is not None else dist.new_group(backend="gloo")
+        self._shape = None
+        self.calls = 0
+
+    def _setup(self, shape, dtype, device):
+        lib = _lib.load()
+        P, r = self.size, self.rank
+        self.bufs = [torch.empty(shape, dtype=dtype, device=device) for _ in range(2)]
+        self.parts = torch.empty((P,) + tuple(shape), dtype=dtype, device=device)
+        self.copy_stream = torch.cuda.Stream(device)
+        self.ready = [torch.cuda.Event(interprocess=True) for _ in range(2)]
+        self.read = [torch.cuda.Event(interprocess=True) for _ in range(2)]
+        self.copied = torch.cuda.Event()
+        for e in self.ready + self.read:  # materialise the events on this device before export
+            e.record(torch.cuda.current_stream(device))
+        rec = bytearray()
+        for b in self.bufs:
+            h = ctypes.create_string_buffer(_lib.TMU_IPC_HANDLE_BYTES)
+            off = ctypes.c_ulonglong(0)
+            _lib.check(lib.tmu_ipc_export(ops._ptr(b), h, ctypes.byref(off)), "tmu_ipc_export")
+            rec += h.raw + off.value.to_bytes(8, "little")
+        for e in self.ready + self.read:
+            rec += bytes(e.ipc_handle())
+        mine = torch.frombuffer(bytearray(rec), dtype=torch.uint8).to(device)
+        every = torch.empty(P * mine.numel(), dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, mine, group=self.group)
+        every = every.view(P, -1).cpu().numpy().tobytes()
+        n = mine.numel()
+        self.peer_bufs, self.peer_ready, self.peer_read = {}, {}, {}
+        for q in range(P):
+            if q == r:
+                continue
+            blob = every[q * n:(q + 1) * n]
+            ptrs = []
+            for i in range(2):
+                h = blob[i * 72:i * 72 + 64]
+                off = int.from_bytes(blob[i * 72 + 64:i * 72 + 72], "little")
+                p = ctypes.c_void_p()
+                _lib.check(lib.tmu_ipc_import(h, off, ctypes.byref(p)), "tmu_ipc_import")
+                ptrs.append(p.value)
+            self.peer_bufs[q] = ptrs
+            ev = [blob[144 + 64 * i:144 + 64 * (i + 1)] for i in range(4)]
+            self.peer_ready[q] = [torch.cuda.Event.from_ipc_handle(device, ev[i]) for i in range(2)]
+            self.peer_read[q] = [torch.cuda.Event.from_ipc_handle(device, ev[2 + i]) for i in range(2)]
+        self.nbytes = self.bufs[0].numel() * self.bufs[0].element_size()
+        self._shape = tuple(shape)
+        dist.barrier(group=self.host_group)
+
+    def slab_for_write(self, shape, dtype, device):
+        """This call's persistent buffer for the local b slab (K1 writes into it)."""
+        if self._shape != tuple(shape):
+            self._setup(shape, dtype, device)
+        par = self.calls & 1
+        if self.calls >= 2:  # the peers finished copying this buffer's previous content
+            cur = torch.cuda.current_stream(device)
+            for q in self.peer_read:
+                cur.wait_event(self.peer_read[q][par])
+        return self.bufs[par]
+
+    def gather_start(self):
+        """Publish this call's slab and start pulling the peers' into ``parts``; returns
+        (parts [P, *shape], handle).  The local slot of ``parts`` is left unwritten."""
+        lib = _lib.load()
+        par = self.calls & 1
+        self.calls += 1
+        cur = torch.cuda.current_stream()
+        self.ready[par].record(cur)
+        dist.barrier(group=self.host_group)  # every rank has recorded: the waits below see it
+        cs = self.copy_stream
+        for q, ptrs in self.peer_bufs.items():
+            cs.wait_event(self.peer_ready[q][par])
+            _lib.check(lib.tmu_copy_async(ops._ptr(self.parts[q]), ptrs[par], self.nbytes, cs.cuda_stream),
+                       "tmu_copy_async")
+        self.read[par].record(cs)
+        self.copied.record(cs)
+        return self.parts, self.copied
+
+    def wait(self, handle):
+        torch.cuda.current_stream().wait_event(handle)
+
+    def close(self):
+        """Release the imported peer mappings (after every rank is done with them)."""
+        if self._shape is None:
+            return
+        lib = _lib.load()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.host_group)
+        for ptrs in self.peer_bufs.values():
+            for p in ptrs:
+                lib.tmu_ipc_close(ctypes.c_void_p(p))
+        self._shape = None
+
+
 class LocalExchange:
     """The exchange of a single rank (P = 1): the collectives are identities."""
 
@@ -177,16 +286,20 @@ class RowShardedTrimul:
             raise ValueError(f"z_local must be [1, {Lr}, {L}, {cz}], got {tuple(z_local.shape)}")
         z_local = z_local.contiguous()
         out = torch.empty_like(z_local) if out is None else out
+        b_out = None
+        if hasattr(self.exchange, "slab_for_write"):
+            b_out = self.exchange.slab_for_write((w.c, Lr, ops.row_pitch(L)), torch.float16, z_local.device)
         if outgoing:
             layout = (1, Lr, L, Lr * L * cz, L * cz, cz, Lr * L, L, 1)
-            a, b = self.stages.project_gate(z_local, layout, None if mask_local is None else mask_local.contiguous(), w)
+            a, b = self.stages.project_gate(z_local, layout, None if mask_local is None else mask_local.contiguous(), w,
+                                            b_out=b_out)
         else:
             zt = self._to_columns(z_local[0])  # [P, Lr(k within source), Lr(i), cz]: z[k, i] at k*Lr*cz + i*cz
             mt = None
             if mask_local is not None:
                 mt = self._to_columns(mask_local[0])  # [P, Lr(k), Lr(i)]: mask[k, i] at k*Lr + i
             layout = (1, Lr, L, L * Lr * cz, cz, Lr * cz, L * Lr, 1, Lr)
-            a, b = self.stages.project_gate(zt, layout, mt, w)
+            a, b = self.stages.project_gate(zt, layout, mt, w, b_out=b_out)
         x = self._contract_ring(a, b)
         return self.stages.emit_residual(x, z_local, w, mix_eps, out)
 
@@ -199,8 +312,13 @@ class RowShardedTrimul:
             return self.stages.contract(a, b_local.unsqueeze(0), Lr, L, L, Lr)
         Bc = a.shape[0]
         x = torch.empty(Bc, Lr, ops.row_pitch(L), dtype=a.dtype, device=a.device)
-        parts, handle = self.exchange.all_gather_start(b_local)  # [P, Bc, Lr, pitch(L)]
-        self.stages.contract(a, b_local.unsqueeze(0), Lr, Lr, L, Lr, x=x[:, :, r * Lr:], max_ctas=self.contract_ctas)
+        if hasattr(self.exchange, "gather_start"):  # copy engines: no SMs taken from the contraction
+            parts, handle = self.exchange.gather_start()
+            ctas = 0
+        else:
+            parts, handle = self.exchange.all_gather_start(b_local)  # [P, Bc, Lr, pitch(L)]
+            ctas = self.contract_ctas
+        self.stages.contract(a, b_local.unsqueeze(0), Lr, Lr, L, Lr, x=x[:, :, r * Lr:], max_ctas=ctas)
         self.exchange.wait(handle)
         for q0, q1 in ((0, r), (r + 1, P)):  # the remote blocks before and after this rank's
             if q1 > q0:

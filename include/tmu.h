@@ -204,6 +204,19 @@ int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, 
 int tmu_disto_expected(const void* z, const void* w, const float* bias, const float* centres, float* out, int B,
                        int L, int c_z, int n_bins, void* status, void* stream);
 
+/* ---- Copy-engine exchange for the row-sharded path (no counterpart in the reference).  A rank
+ * exports a device buffer with tmu_ipc_export (CUDA IPC handle of the allocation that contains
+ * `ptr`, plus ptr's byte offset inside it); a peer process imports it with tmu_ipc_import and
+ * copies from it with tmu_copy_async, a cudaMemcpyAsync that the copy engines carry over NVLink,
+ * so the transfer uses no SM and no kernel ever reads another GPU's memory.  tmu_ipc_close
+ * releases an imported mapping (pass the pointer tmu_ipc_import returned). */
+#define TMU_IPC_HANDLE_BYTES 64
+
+int tmu_ipc_export(const void* ptr, void* handle, unsigned long long* offset);
+int tmu_ipc_import(const void* handle, unsigned long long offset, void** ptr);
+int tmu_ipc_close(void* ptr);
+int tmu_copy_async(void* dst, const void* src, size_t bytes, void* stream);
+
 /* Self-test of the bounded-wait machinery: launches one CTA that waits on an mbarrier nothing
  * ever arrives at, with a limit of `timeout_ns`; the kernel must give up, record
  * TMU_ERR_DEVICE_TIMEOUT in `status` and exit.  Returns the launch status. */

@@ -30,7 +30,7 @@ class OracleStages:
     def __init__(self, p):
         self.p = p
 
-    def project_gate(self, z, layout, mask, w):
+    def project_gate(self, z, layout, mask, w, b_out=None):
         B, rows, cols, sb, sr, sc, msb, msr, msc = layout
         zv = torch.as_strided(z.reshape(-1).float(), (B, rows, cols, 128), (sb, sr, sc, 1))
         mv = None if mask is None else torch.as_strided(mask.reshape(-1).float(), (B, rows, cols), (msb, msr, msc))
@@ -42,7 +42,11 @@ class OracleStages:
             o[:, :, :cols] = t.reshape(B * 128, rows, cols).half()
             return o
 
-        return pack(a), pack(b)
+        pb = pack(b)
+        if b_out is not None:
+            b_out.copy_(pb)
+            pb = b_out
+        return pack(a), pb
 
     def contract(self, a, b_parts, M, N, K, rows_per_part, x=None, max_ctas=0):
         Pp, Bc, R, pitch = b_parts.shape

@@ -182,9 +182,9 @@ class _SerialStages(CudaStages):
 
     lock = threading.Lock()
 
-    def project_gate(self, *a):
+    def project_gate(self, *a, **kw):
         with self.lock:
-            return super().project_gate(*a)
+            return super().project_gate(*a, **kw)
 
     def contract(self, *a, **kw):
         with self.lock:
@@ -248,7 +248,7 @@ def test_row_sharded_emulated_ranks_match_oracle(P, L, n_pad, outgoing):
     assert float((got - full).abs().max()) <= 2 * _ulp16(float(full.abs().max()))
 
 
-def _nccl_worker(rank, port, q, L):
+def _nccl_worker(rank, port, q, L, copy_engines=False):
     import datetime
     import traceback
 
@@ -266,7 +266,13 @@ def _nccl_worker(rank, port, q, L):
             Lr = L // 2
             zl = z[:, rank * Lr:(rank + 1) * Lr].half().contiguous().cuda()
             ml = mask[:, rank * Lr:(rank + 1) * Lr].half().contiguous().cuda()
-            sh = RowShardedTrimul(L)
+            if copy_engines:
+                from esmfold2_mlx_b200.sharded import CopyEngineExchange
+                if direction == "out":
+                    ex = CopyEngineExchange()
+                sh = RowShardedTrimul(L, exchange=ex)
+            else:
+                sh = RowShardedTrimul(L)
             out = sh(zl, ml, w, outgoing)
             full = torch.empty(2, Lr, L, 128, dtype=torch.float16, device=out.device)
             dist.all_gather_into_tensor(full, out)
@@ -275,6 +281,8 @@ def _nccl_worker(rank, port, q, L):
                 got = full.reshape(1, L, L, 128).float().cpu()
                 ref16 = orc.trimul_fp16(p, z, mask, outgoing)
                 res[direction] = (float((got - ref16).abs().max()), _ulp16(float(ref16.abs().max())))
+        if copy_engines:
+            ex.close()
         q.put((rank, res))
     except Exception:  # noqa: BLE001 - reported to the parent instead of hanging the peer
         q.put((rank, {"error": traceback.format_exc()}))
@@ -284,13 +292,14 @@ def _nccl_worker(rank, port, q, L):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.timeout(600)
-def test_row_sharded_two_nccl_ranks_match_oracle():
+@pytest.mark.parametrize("copy_engines", [False, True])
+def test_row_sharded_two_nccl_ranks_match_oracle(copy_engines):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29800 + os.getpid() % 150
-    procs = [ctx.Process(target=_nccl_worker, args=(r, port, q, 512)) for r in range(2)]
+    port = 29800 + os.getpid() % 150 + (7 if copy_engines else 0)
+    procs = [ctx.Process(target=_nccl_worker, args=(r, port, q, 512, copy_engines)) for r in range(2)]
     for pr in procs:
         pr.start()
     out = dict(q.get(timeout=400) for _ in range(2))
