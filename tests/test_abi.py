@@ -65,3 +65,27 @@ def test_argument_checks_need_no_gpu(lib):
     assert lib.tmu_reset_status(None, None) == 1
     old = lib.tmu_set_wait_timeout_ns(123)
     assert lib.tmu_set_wait_timeout_ns(old) == 123
+
+
+def test_argument_checks_of_the_later_entry_points_need_no_gpu(lib):
+    """tmu_transition, tmu_disto_expected, the slab and IPC helpers reject bad arguments before
+    touching a device (codes: 1 invalid argument, 4 unsupported)."""
+    TW = ctypes.POINTER(_lib.TmuTransitionWeights)
+    tw = _lib.TmuTransitionWeights()
+    assert lib.tmu_transition(None, None, TW(), 1, 64, 256, 512, 0, None, None) == 4  # c_z 256 not fused
+    assert lib.tmu_transition(None, None, TW(), 1, 64, 128, 100, 0, None, None) == 4  # hidden % 64
+    assert lib.tmu_transition(None, None, TW(), 1, 64, 128, 512, 7, None, None) == 1  # activation
+    assert lib.tmu_transition(None, None, ctypes.byref(tw), 1, 64, 128, 512, 0, None, None) == 1  # no weights
+    assert lib.tmu_disto_expected(None, None, None, None, None, 1, 64, 128, 64, None, None) == 4  # 128 bins only
+    assert lib.tmu_disto_expected(None, None, None, None, None, 1, 64, 192, 128, None, None) == 4
+    assert lib.tmu_disto_expected(None, None, None, None, None, 1, 64, 128, 128, None, None) == 1
+    # a column block of x needs a row pitch >= N and a multiple of 8
+    assert lib.tmu_contract_ex(None, None, None, 1, 128, 256, 256, 128, 200, 0, None, None) == 1
+    assert lib.tmu_contract_ex(None, None, None, 1, 128, 256, 256, 128, 260, 0, None, None) == 1
+    assert lib.tmu_contract_ex(None, None, None, 1, 128, 256, 256, 128, 0, -1, None, None) == 1
+    off = ctypes.c_ulonglong(0)
+    assert lib.tmu_ipc_export(None, None, ctypes.byref(off)) == 1
+    p = ctypes.c_void_p()
+    assert lib.tmu_ipc_import(None, 0, ctypes.byref(p)) == 1
+    assert lib.tmu_ipc_close(None) == 1
+    assert lib.tmu_copy_async(None, None, 0, None) == 1
