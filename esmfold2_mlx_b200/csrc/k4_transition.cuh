@@ -1,5 +1,5 @@
 // K4: the pair transition of a PairUpdateBlock, z' = z + ffn(LN(z)), in one pass over the pair
-// grid (c_z = 128, hidden h a multiple of 64).
+// grid (c_z = 128 or 256, hidden h a multiple of 64).
 //
 // Reference (src/esmfold2_mlx/): mlx_trunk.py:96-99, fused path mlx_trunk_kernels.py:236-239
 // (module form fast_trunk.py:35-42), in the fp16 scheme:
@@ -10,16 +10,23 @@
 //   z' = fp16(z + s @ w3^T)                    w3 [c_z, h]; one rounding (mx.addmm)
 //
 // Tile = 128 positions (ih x jw block of the grid); TMEM lane = position.  The hidden dimension
-// is processed in chunks of 64: GEMM1 of chunk k (D1 = h W12_k^T, N = 64, or 2 x 64 for SwiGLU's
-// x1 and x2 halves) lands in one of two TMEM chunk buffers, the activation warps turn it into
-// the fp16 A operand s_k in shared memory, and GEMM2 accumulates D2 += s_k W3_k^T (N = c_z,
-// K = 64) in one of two per-tile TMEM accumulators.  The MMA thread issues G1(0), G1(1), G1(2),
-// G2(0), G1(3), G2(1), ... (GEMM1 two chunks ahead), so the tensor core computes the next chunks
-// while the current ones are being activated.  The weights (256-384 KB) do not fit beside the tiles, so they stream from L2
-// through a 4-stage ring of 16 KB items in exactly that order.
+// is processed in chunks of 64: GEMM1 of chunk k (D1 = h W12_k^T: N = 128 for SwiGLU, whose B
+// operand stacks the chunk's 64 x1 rows over its 64 x2 rows, N = 64 for ReLU) lands in one of
+// two TMEM chunk buffers, the activation warps turn it into the fp16 A operand s_k in shared
+// memory, and GEMM2 accumulates D2 += s_k W3_k^T (N = c_z as 128-column MMAs, K = 64) in a
+// per-tile TMEM accumulator.  The MMA thread issues G1(0), G1(1), G1(2), G2(0), G1(3), G2(1), ...
+// (GEMM1 two chunks ahead), so the tensor core computes the next chunks while the current ones
+// are being activated.  The weights (256 KB - 1.5 MB) do not fit beside the tiles, so they
+// stream from L2 through a 4-stage ring of 16 KB items in exactly that order.
+//
+// c_z = 128: z tiles (2 stages) and LayerNorm outputs h (2 stages) are separate buffers, and the
+// epilogue adds D2 to the z tile still in shared memory; two D2 accumulators (256 columns).
+// c_z = 256: a 64 KB tile leaves room for two tile buffers only, so each holds z, is normalised
+// in place into h, and after the tile's last GEMM1 is refilled with z (an L2 hit: the same CTA
+// read it microseconds before) for the epilogue; one 256-column D2 accumulator.
 // CTA = 19 warps, one per SM, persistent:
 //   warp 0      TMA: the weight ring
-//   warp 1      TMEM (512 columns: D2 x 2 at [0, 256), D1 x 2 at [256, 512)) + MMA thread
+//   warp 1      TMEM (512 columns: D2 at [0, 256), D1 x 2 at [256, 512)) + MMA thread
 //   warp 2      TMA: z tiles (2 stages)
 //   warps 3-6   LayerNorm z tile -> h (K-major swizzled A operand, 2 stages)
 //   warps 7-14  activation: D1 -> s, two groups of four (one TMEM lane quadrant per warp),
@@ -33,30 +40,37 @@
 namespace tmu {
 namespace k4 {
 
-constexpr int CZ = 128;
 constexpr int TILE = 128;
 constexpr int CHUNK = 64;                        // hidden units per chunk
 constexpr int ATOM_BYTES = TILE * 128;           // 128 rows x 128 B
-constexpr int TILE_BYTES = TILE * CZ * 2;        // 32 KB
 constexpr int S_BYTES = TILE * CHUNK * 2;        // 16 KB: one chunk of s
 constexpr int W_BYTES = 16384;                   // one ring item
 constexpr int NW = 4;
-constexpr int OFF_Z = 0;                         // 2 stages
-constexpr int OFF_H = OFF_Z + 2 * TILE_BYTES;    // 2 stages
-constexpr int OFF_S = OFF_H + 2 * TILE_BYTES;    // 2 buffers
-constexpr int OFF_W = OFF_S + 2 * S_BYTES;       // NW ring items
-constexpr int OFF_PAR = OFF_W + NW * W_BYTES;    // fp32 LN gamma[128], beta[128]
-constexpr int OFF_BAR = OFF_PAR + 2 * CZ * 4;
-constexpr int SMEM_BYTES = OFF_BAR + 512;
 constexpr int kThreads = 608;
 constexpr int TMEM_COLS = 512;
-static_assert(SMEM_BYTES <= 232448, "K4 shared memory exceeds the per-block limit");
+
+template <int CZ>
+struct Cfg {
+  static constexpr int KATOMS = CZ / 64;
+  static constexpr int TILE_BYTES = TILE * CZ * 2;                     // 32 or 64 KB
+  static constexpr bool INPLACE = CZ == 256;                           // h overwrites z in its stage
+  static constexpr int NACC = CZ == 128 ? 2 : 1;                       // D2 accumulators
+  static constexpr int OFF_Z = 0;                                      // 2 stages
+  static constexpr int OFF_H = INPLACE ? OFF_Z : OFF_Z + 2 * TILE_BYTES;  // 2 stages
+  static constexpr int OFF_S = OFF_H + 2 * TILE_BYTES;                 // 2 buffers
+  static constexpr int OFF_W = OFF_S + 2 * S_BYTES;                    // NW ring items
+  static constexpr int OFF_PAR = OFF_W + NW * W_BYTES;                 // fp32 LN gamma[c_z], beta[c_z]
+  static constexpr int OFF_BAR = OFF_PAR + 2 * CZ * 4;
+  static constexpr int SMEM_BYTES = OFF_BAR + 512;
+  static_assert(SMEM_BYTES <= 232448, "K4 shared memory exceeds the per-block limit");
+  static_assert(NACC * CZ + 2 * 128 <= TMEM_COLS, "K4 TMEM columns");
+};
 
 struct Params {
-  CUtensorMap tm_z;    // z [B, L, L, 128]: box {64, jw, ih, 1}, 128B swizzle (load)
+  CUtensorMap tm_z;    // z [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle (load)
   CUtensorMap tm_zo;   // z_out: box {64, min(jw,32), 32/min(jw,32), 1}, 128B swizzle (per-warp store)
-  CUtensorMap tm_w12;  // w12 [W, 128]: box {64, 64}, 128B swizzle
-  CUtensorMap tm_w3;   // w3 [128, h]: box {64, 128}, 128B swizzle
+  CUtensorMap tm_w12;  // w12 [W, c_z]: box {64, 64}, 128B swizzle
+  CUtensorMap tm_w3;   // w3 [c_z, h]: box {64, 128}, 128B swizzle
   const __half* ln_w;
   const __half* ln_b;
   int hidden;          // h
@@ -79,17 +93,22 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
-template <bool SWIGLU>
+template <int CZ, bool SWIGLU>
 __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_constant__ Params p) {
-  constexpr uint32_t IDESC1 = idesc_f16_f32(128, CHUNK, false, false);
-  constexpr uint32_t IDESC2 = idesc_f16_f32(128, CZ, false, false);
-  constexpr int W1_ITEMS = SWIGLU ? 2 : 1;  // ring items per GEMM1 chunk
+  using C = Cfg<CZ>;
+  constexpr uint32_t IDESC1 = idesc_f16_f32(128, SWIGLU ? 2 * CHUNK : CHUNK, false, false);
+  constexpr uint32_t IDESC2 = idesc_f16_f32(128, 128, false, false);
+  // Ring items per chunk.  GEMM1, SwiGLU: one per 64-channel K atom, holding that atom of the
+  // chunk's 64 x1 rows and then of its 64 x2 rows (one N = 128 B operand).  GEMM1, ReLU: one per
+  // two K atoms of the chunk's 64 rows (N = 64).  GEMM2: one per 128 output channels.
+  constexpr int G1_ITEMS = SWIGLU ? C::KATOMS : C::KATOMS / 2;
+  constexpr int G2_ITEMS = CZ / 128;
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x4ff;
     return;
   }
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* wfull = bars;           // [NW]
   uint64_t* wempty = bars + 4;      // [NW]
   uint64_t* zfull = bars + 8;       // [2]
@@ -106,7 +125,8 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
   uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 29);
   volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 29) + 4);
   volatile int* gflags = reinterpret_cast<volatile int*>(bars + 30);  // [4 groups][2] group_wait verdicts
-  float* par = reinterpret_cast<float*>(smem + OFF_PAR);
+  uint64_t* rfull = bars + 34;      // [2] c_z = 256: z reloaded for the epilogue
+  float* par = reinterpret_cast<float*>(smem + C::OFF_PAR);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtx ctx{p.status, &abort_sh, p.timeout_ns};
@@ -129,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
       mbar_init(&sempty[s], 1);
       mbar_init(&accfull[s], 1);
       mbar_init(&accempty[s], 4);  // the four epilogue warps
+      mbar_init(&rfull[s], 1);
     }
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
@@ -156,22 +177,27 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     if (lane == 0) {
       uint32_t r = 0;
       bool ok = true;
-      auto put = [&](const CUtensorMap* m, int c0, int c1, int nloads, int c0_step) -> bool {
+      // One ring item: two 64 x 64 boxes of w12 (at 0 and 8 KB), or one 64 x 128 box of w3.
+      auto put = [&](const CUtensorMap* m, int c0, int c1, int c0b, int c1b, bool two) -> bool {
         const uint32_t s = r % NW, ph = (r / NW) & 1;
         if (!mbar_wait(&wempty[s], ph ^ 1, ctx, kSiteProdW)) return false;
         mbar_arrive_expect_tx(&wfull[s], W_BYTES);
-        for (int q = 0; q < nloads; ++q)
-          tma_load_2d(smem + OFF_W + s * W_BYTES + q * (W_BYTES / nloads), m, &wfull[s], c0 + q * c0_step, c1);
+        uint8_t* dst = smem + C::OFF_W + s * W_BYTES;
+        tma_load_2d(dst, m, &wfull[s], c0, c1);
+        if (two) tma_load_2d(dst + W_BYTES / 2, m, &wfull[s], c0b, c1b);
         ++r;
         return true;
       };
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         for (int j = 0; ok && j <= n + 1; ++j) {
-          if (j < n) {  // w12 rows of chunk j (x1), and of x2 for SwiGLU: two 64 x 64 boxes each
-            ok = put(&p.tm_w12, 0, j * CHUNK, 2, 64);
-            if (ok && SWIGLU) ok = put(&p.tm_w12, 0, p.hidden + j * CHUNK, 2, 64);
+          for (int k = 0; ok && j < n && k < G1_ITEMS; ++k) {  // w12 rows of chunk j
+            if (SWIGLU)  // K atom k of the x1 rows over K atom k of the x2 rows
+              ok = put(&p.tm_w12, k * 64, j * CHUNK, k * 64, p.hidden + j * CHUNK, true);
+            else         // K atoms 2k and 2k + 1 of the chunk's rows
+              ok = put(&p.tm_w12, 2 * k * 64, j * CHUNK, (2 * k + 1) * 64, j * CHUNK, true);
           }
-          if (ok && j >= 2) ok = put(&p.tm_w3, (j - 2) * CHUNK, 0, 1, 0);  // w3[:, chunk j-2]
+          for (int m = 0; ok && j >= 2 && m < G2_ITEMS; ++m)  // w3[128 m .. 128 m + 127, chunk j-2]
+            ok = put(&p.tm_w3, (j - 2) * CHUNK, m * 128, 0, 0, false);
         }
       }
       if (abort_sh) {  // drain the loads still in flight before the CTA exits
@@ -190,9 +216,9 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
         decode_tile(p, tile, bb, i0, j0);
         const uint32_t s = it & 1, ph = (it >> 1) & 1;
         if (!mbar_wait(&zempty[s], ph ^ 1, ctx, kSiteProdZ)) break;
-        mbar_arrive_expect_tx(&zfull[s], TILE_BYTES);
-        for (int a = 0; a < 2; ++a)
-          tma_load_4d(smem + OFF_Z + s * TILE_BYTES + a * ATOM_BYTES, &p.tm_z, &zfull[s], a * 64, j0, i0, bb);
+        mbar_arrive_expect_tx(&zfull[s], C::TILE_BYTES);
+        for (int a = 0; a < C::KATOMS; ++a)
+          tma_load_4d(smem + C::OFF_Z + s * C::TILE_BYTES + a * ATOM_BYTES, &p.tm_z, &zfull[s], a * 64, j0, i0, bb);
       }
       if (abort_sh) {
         for (uint32_t s = 0; s < 2; ++s) {
@@ -208,9 +234,10 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t tb = it & 1, tph = (it >> 1) & 1;
+        const uint32_t ab = it % C::NACC, aph = (it / C::NACC) & 1;
         if (!(ok = mbar_wait(&hfull[tb], tph, ctx, kSiteMmaH))) break;
-        const uint32_t hbase = smem_u32(smem + OFF_H + tb * TILE_BYTES);
-        const uint32_t acc = tmem_base + tb * CZ;
+        const uint32_t hbase = smem_u32(smem + C::OFF_H + tb * C::TILE_BYTES);
+        const uint32_t acc = tmem_base + ab * CZ;
         // GEMM1 runs two chunks ahead of GEMM2: G1(j) needs only that its TMEM buffer has been
         // read (by the activation of chunk j-2), so the tensor core computes chunk j while
         // chunks j-1 and j-2 are still being activated.
@@ -218,17 +245,24 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
           if (j < n) {  // GEMM1 of chunk gc + j
             const uint32_t c = gc + j, b = c & 1, cph = (c >> 1) & 1;
             if (!(ok = mbar_wait(&d1empty[b], cph ^ 1, ctx, kSiteMmaD1))) break;
-            for (int half = 0; half < W1_ITEMS; ++half) {
+            const uint32_t d = tmem_base + 256 + b * 128;
+            for (int k = 0; k < G1_ITEMS; ++k) {
               const uint32_t s = r % NW, ph = (r / NW) & 1;
               if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
               tc_fence_after();
-              const uint32_t wb = smem_u32(smem + OFF_W + s * W_BYTES);
-              const uint32_t d = tmem_base + 256 + b * 128 + half * CHUNK;
+              const uint32_t wb = smem_u32(smem + C::OFF_W + s * W_BYTES);
+              if (SWIGLU) {  // K atom k: D1[:, 0:64] = x1, D1[:, 64:128] = x2
 #pragma unroll
-              for (int kk = 0; kk < CZ / 16; ++kk) {
-                const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
-                umma_f16(d, sdesc_sw128(hbase + ka * ATOM_BYTES + kb, 16, 1024),
-                         sdesc_sw128(wb + ka * (W_BYTES / 2) + kb, 16, 1024), IDESC1, kk > 0 ? 1u : 0u);
+                for (int kk = 0; kk < 4; ++kk)
+                  umma_f16(d, sdesc_sw128(hbase + k * ATOM_BYTES + kk * 32, 16, 1024),
+                           sdesc_sw128(wb + kk * 32, 16, 1024), IDESC1, (k > 0 || kk > 0) ? 1u : 0u);
+              } else {       // K atoms 2k, 2k + 1
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                  const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
+                  umma_f16(d, sdesc_sw128(hbase + (2 * k + ka) * ATOM_BYTES + kb, 16, 1024),
+                           sdesc_sw128(wb + ka * (W_BYTES / 2) + kb, 16, 1024), IDESC1, (k > 0 || kk > 0) ? 1u : 0u);
+                }
               }
               umma_commit(&wempty[s]);
               ++r;
@@ -239,24 +273,27 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
           }
           if (j >= 2) {  // GEMM2 of chunk gc + j - 2
             const uint32_t c = gc + j - 2, b = c & 1, cph = (c >> 1) & 1;
-            if (j == 2 && !(ok = mbar_wait(&accempty[tb], tph ^ 1, ctx, kSiteMmaAcc))) break;
+            if (j == 2 && !(ok = mbar_wait(&accempty[ab], aph ^ 1, ctx, kSiteMmaAcc))) break;
             if (!(ok = mbar_wait(&sfull[b], cph, ctx, kSiteMmaS))) break;
-            const uint32_t s = r % NW, ph = (r / NW) & 1;
-            if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
-            tc_fence_after();
-            const uint32_t sb = smem_u32(smem + OFF_S + b * S_BYTES);
-            const uint32_t wb = smem_u32(smem + OFF_W + s * W_BYTES);
+            const uint32_t sb = smem_u32(smem + C::OFF_S + b * S_BYTES);
+            for (int m = 0; m < G2_ITEMS; ++m) {  // output channels [128 m, 128 m + 128)
+              const uint32_t s = r % NW, ph = (r / NW) & 1;
+              if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
+              tc_fence_after();
+              const uint32_t wb = smem_u32(smem + C::OFF_W + s * W_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < CHUNK / 16; ++kk)
-              umma_f16(acc, sdesc_sw128(sb + kk * 32, 16, 1024), sdesc_sw128(wb + kk * 32, 16, 1024), IDESC2,
-                       (j > 2 || kk > 0) ? 1u : 0u);
-            umma_commit(&wempty[s]);
+              for (int kk = 0; kk < CHUNK / 16; ++kk)
+                umma_f16(acc + m * 128, sdesc_sw128(sb + kk * 32, 16, 1024), sdesc_sw128(wb + kk * 32, 16, 1024),
+                         IDESC2, (j > 2 || kk > 0) ? 1u : 0u);
+              umma_commit(&wempty[s]);
+              ++r;
+            }
+            if (!ok) break;
             umma_commit(&sempty[b]);
-            ++r;
           }
         }
         if (!ok) break;
-        umma_commit(&accfull[tb]);
+        umma_commit(&accfull[ab]);
         gc += n;
       }
       umma_commit(&drain_bar);
@@ -268,9 +305,19 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     uint32_t it = 0, gcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
-      if (!group_wait(&hempty[s], ph ^ 1, &zfull[s], ph, ctx, kSiteLn, row == 0, 4, 128, gflags + 6, gcount)) break;
-      ln_row128_sw128(smem + OFF_Z + s * TILE_BYTES, smem + OFF_H + s * TILE_BYTES, ATOM_BYTES, row, 1e-5f,
-                      LnParSmem{par, par + CZ});
+      if (C::INPLACE) {  // the stage is free once its z arrived (the previous tile there is done)
+        if (!group_wait(&zfull[s], ph, nullptr, 0, ctx, kSiteLn, row == 0, 4, 128, gflags + 6, gcount)) break;
+        uint8_t* X = smem + C::OFF_Z + s * C::TILE_BYTES;
+        const float k = ln_row_shift(X, row);
+        const float2 mr = ln256_moments(ln_half_sums(X, ATOM_BYTES, row, 0, k), ln_half_sums(X, ATOM_BYTES, row, 1, k),
+                                        k, 1e-5f);
+        ln_half_apply(X, X, ATOM_BYTES, row, 0, mr.x, mr.y, LnParSmem{par, par + CZ});
+        ln_half_apply(X, X, ATOM_BYTES, row, 1, mr.x, mr.y, LnParSmem{par, par + CZ});
+      } else {
+        if (!group_wait(&hempty[s], ph ^ 1, &zfull[s], ph, ctx, kSiteLn, row == 0, 4, 128, gflags + 6, gcount)) break;
+        ln_row128_sw128(smem + C::OFF_Z + s * C::TILE_BYTES, smem + C::OFF_H + s * C::TILE_BYTES, ATOM_BYTES, row,
+                        1e-5f, LnParSmem{par, par + CZ});
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&hfull[s]);
@@ -294,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
           break;
         tc_fence_after();
         const uint32_t d = tmem_base + tl + 256 + b * 128;
-        uint8_t* S = smem + OFF_S + b * S_BYTES;
+        uint8_t* S = smem + C::OFF_S + b * S_BYTES;
         if (!SWIGLU) {
           // ReLU: load and activate the whole chunk, and only then wait for the s buffer (GEMM2 of
           // chunk gc - 2 done reading it), so that wait overlaps this warp's own work.
@@ -358,26 +405,36 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     const int row = q * 32 + lane;
     const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
     const uint32_t tl = static_cast<uint32_t>(q * 32) << 16;
+    const bool leader = warp == 15 && lane == 0;
     uint32_t it = 0, gcount = 0;
+    int reload_armed = -1;  // c_z = 256: the stage whose reload is in flight (for the abort drain)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const uint32_t tb = it & 1, tph = (it >> 1) & 1;
-      if (!group_wait(&accfull[tb], tph, &zfull[tb], tph, ctx, kSiteEpi, warp == 15 && lane == 0, 3, 128, gflags + 4,
-                      gcount))
+      const uint32_t ab = it % C::NACC, aph = (it / C::NACC) & 1;
+      uint8_t* Z = smem + C::OFF_Z + tb * C::TILE_BYTES;
+      if (C::INPLACE && leader && mbar_wait(&hempty[tb], tph, ctx, kSiteEpi)) {
+        // The stage held h until the tile's last GEMM1: bring z back for the residual.
+        mbar_arrive_expect_tx(&rfull[tb], C::TILE_BYTES);
+        for (int a = 0; a < C::KATOMS; ++a) tma_load_4d(Z + a * ATOM_BYTES, &p.tm_z, &rfull[tb], a * 64, j0, i0, bb);
+        reload_armed = static_cast<int>(tb);
+      }
+      if (!group_wait(&accfull[ab], aph, C::INPLACE ? &rfull[tb] : &zfull[tb], tph, ctx, kSiteEpi, leader, 3, 128,
+                      gflags + 4, gcount))
         break;
+      reload_armed = -1;
       tc_fence_after();
-      uint8_t* Z = smem + OFF_Z + tb * TILE_BYTES;
 #pragma unroll 1
-      for (int a = 0; a < 2; ++a) {  // channels [64a, 64a + 64) = z atom a
+      for (int a = 0; a < C::KATOMS; ++a) {  // channels [64a, 64a + 64) = z atom a
         uint32_t v[32], u[32];
-        tmem_ld32(tmem_base + tl + tb * CZ + a * 64, v);
-        tmem_ld32(tmem_base + tl + tb * CZ + a * 64 + 32, u);
+        tmem_ld32(tmem_base + tl + ab * CZ + a * 64, v);
+        tmem_ld32(tmem_base + tl + ab * CZ + a * 64 + 32, u);
         tmem_wait_ld2(v, u);
-        if (a == 1) {
+        if (a == C::KATOMS - 1) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&accempty[tb]);
+          if (lane == 0) mbar_arrive(&accempty[ab]);
         }
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {  // 8-channel chunks of the z row
@@ -397,13 +454,18 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        for (int a = 0; a < 2; ++a) tma_store_4d(&p.tm_zo, Z + a * ATOM_BYTES + q * 32 * 128, a * 64, j0 + jo, i0 + io, bb);
+        for (int a = 0; a < C::KATOMS; ++a)
+          tma_store_4d(&p.tm_zo, Z + a * ATOM_BYTES + q * 32 * 128, a * 64, j0 + jo, i0 + io, bb);
         bulk_commit();
         bulk_wait_read<0>();
         mbar_arrive(&zempty[tb]);
       }
     }
     if (lane == 0) bulk_wait<0>();
+    if (reload_armed >= 0) {  // an abort left a reload in flight: let it land before the CTA exits
+      const uint32_t tb = static_cast<uint32_t>(reload_armed);
+      mbar_drain(&rfull[tb], ((it >> 1) & 1), 200000000ull);
+    }
   }
 
   tc_fence_before();

@@ -529,19 +529,22 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_w_kernel");
 }
 
+template <int CZ>
 int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int hidden, bool swiglu,
               DeviceStatus* status, cudaStream_t stream) {
-  void (*kern)(k4::Params) = swiglu ? k4::transition_kernel<true> : k4::transition_kernel<false>;
+  void (*kern)(k4::Params) = swiglu ? k4::transition_kernel<CZ, true> : k4::transition_kernel<CZ, false>;
+  constexpr int smem = k4::Cfg<CZ>::SMEM_BYTES;
   Dev dev;
-  int st = current_device(dev, 1u << (24 + (swiglu ? 1 : 0)), reinterpret_cast<const void*>(kern), k4::SMEM_BYTES);
+  int st = current_device(dev, 1u << ((CZ == 256 ? 28 : 24) + (swiglu ? 1 : 0)), reinterpret_cast<const void*>(kern),
+                          smem);
   if (st) return st;
   k4::Params p;
   memset(&p, 0, sizeof(p));
   int ih = 1, jw = 128;
   choose_tile(L, L, ih, jw, k4::TILE);
   {
-    const uint64_t dims[4] = {128, (uint64_t)L, (uint64_t)L, (uint64_t)B};
-    const uint64_t str[3] = {256, 256ull * L, 256ull * L * L};
+    const uint64_t dims[4] = {CZ, (uint64_t)L, (uint64_t)L, (uint64_t)B};
+    const uint64_t str[3] = {2ull * CZ, 2ull * CZ * L, 2ull * CZ * L * L};
     const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
     if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
     const uint32_t jwp = jw < 32 ? jw : 32;  // one epilogue warp's 32 positions
@@ -549,13 +552,13 @@ int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B
     if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, boxo, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
-    const uint64_t dims[2] = {128, (uint64_t)(swiglu ? 2 * hidden : hidden)};
-    const uint64_t str[1] = {256};
+    const uint64_t dims[2] = {CZ, (uint64_t)(swiglu ? 2 * hidden : hidden)};
+    const uint64_t str[1] = {2 * CZ};
     const uint32_t box[2] = {64, 64};
     if ((st = encode_map(&p.tm_w12, w->w12, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
-    const uint64_t dims[2] = {(uint64_t)hidden, 128};
+    const uint64_t dims[2] = {(uint64_t)hidden, CZ};
     const uint64_t str[1] = {2ull * hidden};
     const uint32_t box[2] = {64, 128};
     if ((st = encode_map(&p.tm_w3, w->w3, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
@@ -573,7 +576,7 @@ int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B
   p.status = status;
   p.timeout_ns = g_timeout_ns;
   const int grid = std::min(p.num_tiles, dev.sms);
-  cudaError_t e = launch_pdl(kern, grid, k4::kThreads, k4::SMEM_BYTES, stream, p);
+  cudaError_t e = launch_pdl(kern, grid, k4::kThreads, smem, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel");
 }
@@ -890,7 +893,7 @@ int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_t
 int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int c_z, int hidden,
                    int activation, void* status, void* stream) {
   if (B < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "B and L must be positive");
-  if (c_z != 128) return fail(TMU_ERR_UNSUPPORTED, "the fused transition is built for c_z = 128");
+  if (c_z != 128 && c_z != 256) return fail(TMU_ERR_UNSUPPORTED, "c_z must be 128 or 256");
   if (hidden < 64 || hidden > 4096 || hidden % 64) return fail(TMU_ERR_UNSUPPORTED, "hidden must be a multiple of 64 in [64, 4096]");
   if (L > 8192 || B > 65535) return fail(TMU_ERR_UNSUPPORTED, "L > 8192");
   if (activation != TMU_ACT_SWIGLU && activation != TMU_ACT_RELU) return fail(TMU_ERR_INVALID_ARGUMENT, "unknown activation");
@@ -899,8 +902,11 @@ int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, 
   const void* al[] = {z, z_out, w->ln_w, w->ln_b, w->w12, w->w3};
   for (const void* q : al)
     if (!aligned16(q)) return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");
-  return launch_k4(z, z_out, w, B, L, hidden, activation == TMU_ACT_SWIGLU, static_cast<DeviceStatus*>(status),
-                   static_cast<cudaStream_t>(stream));
+  const bool swiglu = activation == TMU_ACT_SWIGLU;
+  DeviceStatus* st = static_cast<DeviceStatus*>(status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return c_z == 128 ? launch_k4<128>(z, z_out, w, B, L, hidden, swiglu, st, s)
+                    : launch_k4<256>(z, z_out, w, B, L, hidden, swiglu, st, s);
 }
 
 int tmu_disto_expected(const void* z, const void* w, const float* bias, const float* centres, float* out, int B,

@@ -272,8 +272,8 @@ class TransitionWeights:
 
     @property
     def fused(self) -> bool:
-        """Whether ``tmu_transition`` covers this shape (c_z = 128, hidden a multiple of 64)."""
-        return self.c_z == 128 and self.hidden % 64 == 0 and 64 <= self.hidden <= 4096
+        """Whether ``tmu_transition`` covers this shape (c_z = 128 or 256, hidden a multiple of 64)."""
+        return self.c_z in (128, 256) and self.hidden % 64 == 0 and 64 <= self.hidden <= 4096
 
 
 def transition(z: torch.Tensor, w: TransitionWeights, out: torch.Tensor | None = None,

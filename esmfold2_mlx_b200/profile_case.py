@@ -8,7 +8,7 @@ Inputs are seeded synthetic tensors (``synthetic``); weights are random-init.  T
 is launched ``--reps`` times after one untimed launch of every stage (and one more of itself), then the script checks the
 device status word and prints the mean CUDA-event time per launch.  Use ``ncu -k regex:<name>``
 with ``project_gate``, ``contract``, ``emit_residual`` or ``transition`` to select a kernel
-(k4 is the fused pair transition, c_z = 128; k5 the distogram expected distance, ``disto``).
+(k4 is the fused pair transition; k5 the distogram expected distance, ``disto``).
 """
 
 from __future__ import annotations

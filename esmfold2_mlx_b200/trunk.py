@@ -62,7 +62,7 @@ def trunk_params(folding_trunk, dtype=torch.float16, device="cuda", biases: list
 def transition_(p: dict, z: torch.Tensor, workspace: ops.Workspace | None = None) -> torch.Tensor:
     """``z + ffn(LN(z))`` in place (``mlx_trunk_kernels.py:236-239``): fp16 LayerNorm output,
     fp16 GEMM output, three fp16 element-wise ops for SwiGLU, one-rounding ``addmm`` residual.
-    c_z = 128 runs the fused kernel K4 (``tmu_transition``); other widths run torch ops."""
+    c_z = 128 and 256 run the fused kernel K4 (``tmu_transition``); other shapes run torch ops."""
     if p["tw"].fused:
         status = workspace.aux_status(z.device) if workspace is not None else None
         return ops.transition(z, p["tw"], out=z, status=status)

@@ -72,7 +72,7 @@ def test_argument_checks_of_the_later_entry_points_need_no_gpu(lib):
     touching a device (codes: 1 invalid argument, 4 unsupported)."""
     TW = ctypes.POINTER(_lib.TmuTransitionWeights)
     tw = _lib.TmuTransitionWeights()
-    assert lib.tmu_transition(None, None, TW(), 1, 64, 256, 512, 0, None, None) == 4  # c_z 256 not fused
+    assert lib.tmu_transition(None, None, TW(), 1, 64, 192, 512, 0, None, None) == 4  # c_z 192 not built
     assert lib.tmu_transition(None, None, TW(), 1, 64, 128, 100, 0, None, None) == 4  # hidden % 64
     assert lib.tmu_transition(None, None, TW(), 1, 64, 128, 512, 7, None, None) == 1  # activation
     assert lib.tmu_transition(None, None, ctypes.byref(tw), 1, 64, 128, 512, 0, None, None) == 1  # no weights

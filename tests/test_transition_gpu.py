@@ -26,19 +26,21 @@ def _ulp16(x: float) -> float:
     return 2.0 ** (math.floor(math.log2(x)) - 10)
 
 
-def _case(L, B, hidden, activation, seed):
-    trunk = FoldingTrunk(1, 128, 128, hidden=hidden, seed=seed, activation=activation, ln_noise=0.1)
+def _case(L, B, hidden, activation, seed, cz=128):
+    trunk = FoldingTrunk(1, cz, cz, hidden=hidden, seed=seed, activation=activation, ln_noise=0.1)
     tr = trunk.blocks[0].pair_transition
-    z = (pair_tensor(B, L, 128, seed + 1) * 2).half().float()
+    z = (pair_tensor(B, L, cz, seed + 1) * 2).half().float()
     p = orc.trunk_params(trunk, True)[0]
     ref = orc.transition_fp16(p, z, activation)
     return tr, z, ref
 
 
 @pytest.mark.parametrize("activation", ["swiglu", "relu"])
-@pytest.mark.parametrize("L,B,hidden", [(37, 1, 512), (76, 2, 512), (130, 1, 256), (64, 1, 64)])
-def test_transition_matches_oracle(activation, L, B, hidden):
-    tr, z, ref = _case(L, B, hidden, activation, seed=L + hidden)
+@pytest.mark.parametrize("L,B,hidden,cz", [(37, 1, 512, 128), (76, 2, 512, 128), (130, 1, 256, 128), (64, 1, 64, 128),
+                                           (37, 1, 512, 256), (76, 2, 1024, 256), (130, 1, 256, 256),
+                                           (64, 1, 64, 256)])
+def test_transition_matches_oracle(activation, L, B, hidden, cz):
+    tr, z, ref = _case(L, B, hidden, activation, seed=L + hidden, cz=cz)
     w = ops.TransitionWeights.from_module(tr, DEV)
     assert w.fused
     st = ops.new_status(DEV)
@@ -52,8 +54,9 @@ def test_transition_matches_oracle(activation, L, B, hidden):
     assert float((diff > 0).float().mean()) < 0.05
 
 
-def test_transition_in_place_equals_out_of_place():
-    tr, z, _ = _case(96, 1, 512, "swiglu", seed=5)
+@pytest.mark.parametrize("cz", [128, 256])
+def test_transition_in_place_equals_out_of_place(cz):
+    tr, z, _ = _case(96, 1, 512, "swiglu", seed=5, cz=cz)
     w = ops.TransitionWeights.from_module(tr, DEV)
     zd = z.half().to(DEV)
     ref = ops.transition(zd, w).clone()
