@@ -63,6 +63,19 @@ class TmuTransitionWeights(ctypes.Structure):
 
 TMU_ACT_SWIGLU, TMU_ACT_RELU = 0, 1
 
+
+class TmuCondTransitionWeights(ctypes.Structure):
+    """Mirror of ``tmu_cond_transition_weights``."""
+
+    _fields_ = [("ln_w", _vp), ("ln_b", _vp), ("w12", _vp), ("w3", _vp)]
+
+
+class TmuPairCondWeights(ctypes.Structure):
+    """Mirror of ``tmu_pair_cond_weights``."""
+
+    _fields_ = [("ln_w", _vp), ("ln_b", _vp), ("proj", _vp), ("n_transitions", _i),
+                ("transitions", ctypes.POINTER(TmuCondTransitionWeights)), ("bias_w", _vp), ("bias_b", _vp)]
+
 _W = ctypes.POINTER(TmuTrimulWeights)
 _G = ctypes.POINTER(TmuPairLayout)
 _TW = ctypes.POINTER(TmuTransitionWeights)
@@ -87,6 +100,9 @@ SIGNATURES = {
     "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_transition": (_i, [_vp, _vp, _TW, _i, _i, _i, _i, _i, _vp, _vp]),
     "tmu_disto_expected": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "tmu_pair_cond_workspace_bytes": (_sz, [_i, _i, _i]),
+    "tmu_pair_cond": (_i, [_vp, _vp, ctypes.POINTER(TmuPairCondWeights), _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp,
+                           _sz, _vp, _vp]),
     "tmu_ipc_export": (_i, [_vp, _vp, ctypes.POINTER(_ull)]),
     "tmu_ipc_import": (_i, [_vp, _ull, ctypes.POINTER(_vp)]),
     "tmu_ipc_close": (_i, [_vp]),

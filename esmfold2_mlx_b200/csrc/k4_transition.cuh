@@ -33,9 +33,16 @@
 //               group g on the chunks that use buffer g
 //   warps 15-18 epilogue: D2 + z -> z' over the z tile, per-warp TMA store of 32 positions
 // Each tile is read and written by exactly one CTA, so z_out may alias z.
+//
+// Row mode (MODE != kModeTile): the transition layers of the diffusion head's pair conditioning
+// (mlx_diffusion16.py:64-67,83-84: z = z + fp32(fp16(silu(h@a) * (h@b)) @ out), h = fp16(LN(z)),
+// the residual stream fp32).  The LayerNorm warps read their rows straight from global memory
+// (fp16 z0 or fp32 z, one warp per row, fp32 gamma/beta), there is no z tile producer, and the
+// epilogue adds fp16(D2) to the fp32 row re-read from global memory and stores fp32.  The SwiGLU
+// arithmetic (w12 = [a; b] rows) is the trunk transition's.
 #pragma once
 
-#include "tmu_common.cuh"
+#include "ln_rows.cuh"
 
 namespace tmu {
 namespace k4 {
@@ -49,14 +56,17 @@ constexpr int NW = 4;
 constexpr int kThreads = 608;
 constexpr int TMEM_COLS = 512;
 
-template <int CZ>
+enum Mode : int { kModeTile = 0, kModeRows16 = 1, kModeRows32 = 2 };
+
+template <int CZ, int MODE = kModeTile>
 struct Cfg {
   static constexpr int KATOMS = CZ / 64;
   static constexpr int TILE_BYTES = TILE * CZ * 2;                     // 32 or 64 KB
-  static constexpr bool INPLACE = CZ == 256;                           // h overwrites z in its stage
+  static constexpr bool ROWS = MODE != kModeTile;                      // LN from global rows, fp32 residual
+  static constexpr bool INPLACE = !ROWS && CZ == 256;                  // h overwrites z in its stage
   static constexpr int NACC = CZ == 128 ? 2 : 1;                       // D2 accumulators
-  static constexpr int OFF_Z = 0;                                      // 2 stages
-  static constexpr int OFF_H = INPLACE ? OFF_Z : OFF_Z + 2 * TILE_BYTES;  // 2 stages
+  static constexpr int OFF_Z = 0;                                      // 2 stages (tile mode)
+  static constexpr int OFF_H = (INPLACE || ROWS) ? OFF_Z : OFF_Z + 2 * TILE_BYTES;  // 2 stages
   static constexpr int OFF_S = OFF_H + 2 * TILE_BYTES;                 // 2 buffers
   static constexpr int OFF_W = OFF_S + 2 * S_BYTES;                    // NW ring items
   static constexpr int OFF_PAR = OFF_W + NW * W_BYTES;                 // fp32 LN gamma[c_z], beta[c_z]
@@ -73,6 +83,10 @@ struct Params {
   CUtensorMap tm_w3;   // w3 [c_z, h]: box {64, 128}, 128B swizzle
   const __half* ln_w;
   const __half* ln_b;
+  const void* zin;     // row mode: z rows, fp16 (kModeRows16) or fp32 (kModeRows32) [cells, c_z]
+  float* zout;         // row mode: z' rows fp32 [cells, c_z] (may alias an fp32 zin)
+  const float* ln_g32; // row mode: LayerNorm gamma/beta fp32
+  const float* ln_b32;
   int hidden;          // h
   int nchunk;          // h / 64
   int L, ih, jw, tiles_i, tiles_j, num_tiles;
@@ -93,9 +107,9 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
-template <int CZ, bool SWIGLU>
+template <int CZ, bool SWIGLU, int MODE = kModeTile>
 __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_constant__ Params p) {
-  using C = Cfg<CZ>;
+  using C = Cfg<CZ, MODE>;
   constexpr uint32_t IDESC1 = idesc_f16_f32(128, SWIGLU ? 2 * CHUNK : CHUNK, false, false);
   constexpr uint32_t IDESC2 = idesc_f16_f32(128, 128, false, false);
   // Ring items per chunk.  GEMM1, SwiGLU: one per 64-channel K atom, holding that atom of the
@@ -154,10 +168,13 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < 2 * CZ; i += blockDim.x) par[i] = __half2float(i < CZ ? p.ln_w[i] : p.ln_b[i - CZ]);
+  if (!C::ROWS)
+    for (int i = threadIdx.x; i < 2 * CZ; i += blockDim.x) par[i] = __half2float(i < CZ ? p.ln_w[i] : p.ln_b[i - CZ]);
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&p.tm_z);
-    tma_prefetch_desc(&p.tm_zo);
+    if (!C::ROWS) {
+      tma_prefetch_desc(&p.tm_z);
+      tma_prefetch_desc(&p.tm_zo);
+    }
     tma_prefetch_desc(&p.tm_w12);
     tma_prefetch_desc(&p.tm_w3);
   }
@@ -208,8 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
       }
     }
   } else if (warp == 2) {
-    // ---------------- z tile producer ----------------
-    if (lane == 0) {
+    // ---------------- z tile producer (tile mode) ----------------
+    if (lane == 0 && !C::ROWS) {
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         int bb, i0, j0;
@@ -303,6 +320,45 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     // ---------------- LayerNorm: z tile -> h ----------------
     const int row = threadIdx.x - 96;
     uint32_t it = 0, gcount = 0;
+    if constexpr (C::ROWS) {
+      // Row mode: warp w normalises rows w, w + 4, .. of the tile, four rows in flight.
+      constexpr int NQ = CZ / 128;
+      constexpr int SRC = MODE == kModeRows16 ? kRowF16 : kRowF32;
+      const int w = warp - 3;
+      float4 gg[NQ], bb4[NQ];
+      load_ln_par<NQ>(p.ln_g32, p.ln_b32, lane, gg, bb4);
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+        int bb, i0, j0;
+        decode_tile(p, tile, bb, i0, j0);
+        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        if (!group_wait(&hempty[s], ph ^ 1, nullptr, 0, ctx, kSiteLn, row == 0, 4, 128, gflags + 6, gcount)) break;
+        uint8_t* H = smem + C::OFF_H + s * C::TILE_BYTES;
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 4) {
+          float4 v[4][NQ];
+          bool valid[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int rr = w + 4 * (r0 + u);
+            const int gi = i0 + rr / p.jw, gj = j0 + rr % p.jw;
+            valid[u] = gi < p.L && gj < p.L;
+            if (valid[u])
+              load_row<SRC, NQ>(p.zin, nullptr, (static_cast<size_t>(bb) * p.L + gi) * p.L + gj, CZ, 0, lane, v[u]);
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int rr = w + 4 * (r0 + u);
+            if (valid[u])
+              ln_row_store<NQ>(v[u], gg, bb4, true, 1e-5f, H, ATOM_BYTES, rr, lane);
+            else
+              zero_row_store<NQ>(H, ATOM_BYTES, rr, lane);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&hfull[s]);
+      }
+    } else
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
       if (C::INPLACE) {  // the stage is free once its z arrived (the previous tile there is done)
@@ -408,6 +464,46 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     const bool leader = warp == 15 && lane == 0;
     uint32_t it = 0, gcount = 0;
     int reload_armed = -1;  // c_z = 256: the stage whose reload is in flight (for the abort drain)
+    if constexpr (C::ROWS) {
+      // Row mode: z' = z + fp32(fp16(D2)), z re-read from global memory (an L2 hit), fp32 out.
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+        int bb, i0, j0;
+        decode_tile(p, tile, bb, i0, j0);
+        const uint32_t ab = it % C::NACC, aph = (it / C::NACC) & 1;
+        if (!group_wait(&accfull[ab], aph, nullptr, 0, ctx, kSiteEpi, leader, 3, 128, gflags + 4, gcount)) break;
+        tc_fence_after();
+        const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
+        const bool valid = gi < p.L && gj < p.L;
+        const size_t cell = (static_cast<size_t>(bb) * p.L + gi) * p.L + gj;
+#pragma unroll 1
+        for (int c0 = 0; c0 < CZ; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld32(tmem_base + tl + ab * CZ + c0, v);
+          tmem_wait_ld(v);
+          if (c0 + 32 == CZ) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&accempty[ab]);
+          }
+          if (!valid) continue;
+          float4* dst = reinterpret_cast<float4*>(p.zout + cell * CZ + c0);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float4 z;
+            if (MODE == kModeRows16) {
+              const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __half*>(p.zin) + cell * CZ + c0) + e);
+              const float2 a = unpack_half2(u.x), b = unpack_half2(u.y);
+              z = make_float4(a.x, a.y, b.x, b.y);
+            } else {
+              z = reinterpret_cast<const float4*>(static_cast<const float*>(p.zin) + cell * CZ + c0)[e];
+            }
+            dst[e] = make_float4(z.x + round_f16(__uint_as_float(v[4 * e])), z.y + round_f16(__uint_as_float(v[4 * e + 1])),
+                                 z.z + round_f16(__uint_as_float(v[4 * e + 2])),
+                                 z.w + round_f16(__uint_as_float(v[4 * e + 3])));
+          }
+        }
+      }
+    } else
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);

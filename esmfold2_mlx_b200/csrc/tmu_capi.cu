@@ -18,6 +18,7 @@
 #include "k3w_emit.cuh"
 #include "k4_transition.cuh"
 #include "k5_disto.cuh"
+#include "k6_ln_gemm.cuh"
 #include "tmu.h"
 
 using namespace tmu;
@@ -30,7 +31,7 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 constexpr int kMaxDevices = 64;
 int g_num_sms[kMaxDevices] = {0};
-unsigned g_attr_done[kMaxDevices] = {0};
+unsigned long long g_attr_done[kMaxDevices] = {0};
 
 int fail(int code, const char* what) {
   g_last_error = what;
@@ -127,7 +128,7 @@ struct Dev {
   int sms;
 };
 
-int current_device(Dev& d, unsigned attr_bit, const void* kernel, int smem) {
+int current_device(Dev& d, unsigned long long attr_bit, const void* kernel, int smem) {
   cudaError_t e = cudaGetDevice(&d.id);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (d.id < 0 || d.id >= kMaxDevices) return fail(TMU_ERR_INVALID_ARGUMENT, "device id out of range");
@@ -581,6 +582,98 @@ int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel");
 }
 
+// K4 in row mode (the diffusion pair conditioning's transitions): zin fp16 (MODE kModeRows16) or
+// fp32 (kModeRows32) rows, zout fp32 rows, SwiGLU.
+template <int CZ, int MODE>
+int launch_k4_rows(const void* zin, float* zout, const tmu_cond_transition_weights* w, int B, int L, int hidden,
+                   unsigned long long bit, DeviceStatus* status, cudaStream_t stream) {
+  void (*kern)(k4::Params) = k4::transition_kernel<CZ, true, MODE>;
+  constexpr int smem = k4::Cfg<CZ, MODE>::SMEM_BYTES;
+  Dev dev;
+  int st = current_device(dev, bit, reinterpret_cast<const void*>(kern), smem);
+  if (st) return st;
+  k4::Params p;
+  memset(&p, 0, sizeof(p));
+  int ih = 1, jw = 128;
+  choose_tile(L, L, ih, jw, k4::TILE);
+  {
+    const uint64_t dims[2] = {CZ, (uint64_t)(2 * hidden)};
+    const uint64_t str[1] = {2 * CZ};
+    const uint32_t box[2] = {64, 64};
+    if ((st = encode_map(&p.tm_w12, w->w12, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)hidden, CZ};
+    const uint64_t str[1] = {2ull * hidden};
+    const uint32_t box[2] = {64, 128};
+    if ((st = encode_map(&p.tm_w3, w->w3, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  p.zin = zin;
+  p.zout = zout;
+  p.ln_g32 = w->ln_w;
+  p.ln_b32 = w->ln_b;
+  p.hidden = hidden;
+  p.nchunk = hidden / k4::CHUNK;
+  p.L = L;
+  p.ih = ih;
+  p.jw = jw;
+  p.tiles_i = (L + ih - 1) / ih;
+  p.tiles_j = (L + jw - 1) / jw;
+  p.num_tiles = B * p.tiles_i * p.tiles_j;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms);
+  cudaError_t e = launch_pdl(kern, grid, k4::kThreads, smem, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel (rows)");
+}
+
+// K6: D = fp16(LN(rows)) @ W^T, W fp16 [n, K]; epilogue per EPI.
+template <int K, int SRC, int EPI>
+int launch_k6(const void* x1, const void* x2, int ld1, int ld2, const float* g, const float* b, const void* w,
+              int n, void* out, const void* bias, int heads, int B, int L, unsigned long long bit,
+              DeviceStatus* status, cudaStream_t stream) {
+  void (*kern)(k6::Params) = k6::ln_gemm_kernel<K, SRC, EPI>;
+  constexpr int smem = k6::Cfg<K>::SMEM_BYTES;
+  Dev dev;
+  int st = current_device(dev, bit, reinterpret_cast<const void*>(kern), smem);
+  if (st) return st;
+  k6::Params p;
+  memset(&p, 0, sizeof(p));
+  {
+    const uint64_t dims[2] = {K, (uint64_t)n};
+    const uint64_t str[1] = {2 * K};
+    const uint32_t box[2] = {64, (uint32_t)n};
+    if ((st = encode_map(&p.tm_w, w, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
+  int ih = 1, jw = 128;
+  choose_tile(L, L, ih, jw, k6::TILE);
+  p.x1 = x1;
+  p.x2 = x2;
+  p.ld1 = ld1;
+  p.ld2 = ld2;
+  p.ln_g = g;
+  p.ln_b = b;
+  p.out = out;
+  p.bias = static_cast<const __half*>(bias);
+  p.n = n;
+  p.heads = heads;
+  p.B = B;
+  p.L = L;
+  p.ih = ih;
+  p.jw = jw;
+  p.tiles_i = (L + ih - 1) / ih;
+  p.tiles_j = (L + jw - 1) / jw;
+  p.num_tiles = B * p.tiles_i * p.tiles_j;
+  p.eps = 1e-5f;
+  p.status = status;
+  p.timeout_ns = g_timeout_ns;
+  const int grid = std::min(p.num_tiles, dev.sms);
+  cudaError_t e = launch_pdl(kern, grid, k6::kThreads, smem, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch ln_gemm_kernel");
+}
+
 template <int CZ>
 int launch_k5(const void* z, const void* w, const float* bias, const float* centres, float* out, int B, int L,
               DeviceStatus* status, cudaStream_t stream) {
@@ -921,6 +1014,79 @@ int tmu_disto_expected(const void* z, const void* w, const float* bias, const fl
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return c_z == 128 ? launch_k5<128>(z, w, bias, centres, out, B, L, st, s)
                     : launch_k5<256>(z, w, bias, centres, out, B, L, st, s);
+}
+
+size_t tmu_pair_cond_workspace_bytes(int B, int L, int c_pair) {
+  if (B < 1 || L < 1 || c_pair < 1) return 0;
+  const size_t cells = static_cast<size_t>(B) * L * L;
+  const size_t z16 = (cells * c_pair * 2 + 255) / 256 * 256;
+  return z16 + cells * c_pair * 4;
+}
+
+int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_cond_weights* w, int B, int L,
+                  int c_trunk, int c_rel, int c_pair, int hidden, int n_bias, int heads, void* out,
+                  void* workspace, size_t workspace_bytes, void* status, void* stream) {
+  if (B < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "B and L must be positive");
+  if (L > 8192 || B > 65535) return fail(TMU_ERR_UNSUPPORTED, "L > 8192");
+  if (c_trunk != c_rel || (c_trunk + c_rel != 256 && c_trunk + c_rel != 512))
+    return fail(TMU_ERR_UNSUPPORTED, "c_trunk == c_rel with c_trunk + c_rel = 256 or 512 is built");
+  if (c_pair != 128 && c_pair != 256) return fail(TMU_ERR_UNSUPPORTED, "c_pair must be 128 or 256");
+  if (w == nullptr || !w->ln_w || !w->ln_b || !w->proj || !w->bias_w || !w->bias_b ||
+      w->n_transitions < 0 || (w->n_transitions > 0 && !w->transitions))
+    return fail(TMU_ERR_INVALID_ARGUMENT, "pair conditioning weights missing");
+  if (w->n_transitions > 0 && (hidden < 64 || hidden > 4096 || hidden % 64))
+    return fail(TMU_ERR_UNSUPPORTED, "hidden must be a multiple of 64 in [64, 4096]");
+  if (n_bias < 16 || n_bias > 256 || n_bias % 16 || heads < 1 || n_bias % heads)
+    return fail(TMU_ERR_UNSUPPORTED, "n_bias must be a multiple of 16 in [16, 256], divisible by heads");
+  if (!z_trunk || !rel_pos || !out || !workspace || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (workspace_bytes < tmu_pair_cond_workspace_bytes(B, L, c_pair))
+    return fail(TMU_ERR_INVALID_ARGUMENT, "workspace too small");
+  const void* al[] = {z_trunk, rel_pos, out, workspace, w->ln_w, w->ln_b, w->proj, w->bias_w};
+  for (const void* q : al)
+    if (!aligned16(q)) return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");
+  for (int t = 0; t < w->n_transitions; ++t) {
+    const tmu_cond_transition_weights& tw = w->transitions[t];
+    if (!tw.ln_w || !tw.ln_b || !tw.w12 || !tw.w3) return fail(TMU_ERR_INVALID_ARGUMENT, "transition weights missing");
+    if (!aligned16(tw.ln_w) || !aligned16(tw.ln_b) || !aligned16(tw.w12) || !aligned16(tw.w3))
+      return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");
+  }
+  DeviceStatus* st = static_cast<DeviceStatus*>(status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t cells = static_cast<size_t>(B) * L * L;
+  __half* z16 = static_cast<__half*>(workspace);
+  float* z32 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (cells * c_pair * 2 + 255) / 256 * 256);
+  // Stage A: z0 = fp16(fp16(LN(concat)) @ proj^T)
+  int r = c_trunk == 256
+              ? launch_k6<512, kRowCat32, k6::kEpiStore16>(z_trunk, rel_pos, c_trunk, c_rel, w->ln_w, w->ln_b,
+                                                           w->proj, c_pair, z16, nullptr, 1, B, L, 1ull << 32, st, s)
+              : launch_k6<256, kRowCat32, k6::kEpiStore16>(z_trunk, rel_pos, c_trunk, c_rel, w->ln_w, w->ln_b,
+                                                           w->proj, c_pair, z16, nullptr, 1, B, L, 1ull << 33, st, s);
+  if (r) return r;
+  // Transitions: z0 (fp16) -> z (fp32), then z in place
+  for (int t = 0; t < w->n_transitions && r == TMU_OK; ++t) {
+    const tmu_cond_transition_weights* tw = &w->transitions[t];
+    if (c_pair == 256)
+      r = t == 0 ? launch_k4_rows<256, k4::kModeRows16>(z16, z32, tw, B, L, hidden, 1ull << 34, st, s)
+                 : launch_k4_rows<256, k4::kModeRows32>(z32, z32, tw, B, L, hidden, 1ull << 35, st, s);
+    else
+      r = t == 0 ? launch_k4_rows<128, k4::kModeRows16>(z16, z32, tw, B, L, hidden, 1ull << 36, st, s)
+                 : launch_k4_rows<128, k4::kModeRows32>(z32, z32, tw, B, L, hidden, 1ull << 37, st, s);
+  }
+  if (r) return r;
+  // Stage D: bias = fp16(fp16(fp16(LN(z)) @ bias_w^T) + bias_b), transposed store
+  const bool f32 = w->n_transitions > 0;
+  const void* zsrc = f32 ? static_cast<const void*>(z32) : static_cast<const void*>(z16);
+  if (c_pair == 256)
+    r = f32 ? launch_k6<256, kRowF32, k6::kEpiBiasT>(zsrc, nullptr, 256, 0, nullptr, nullptr, w->bias_w, n_bias, out,
+                                                     w->bias_b, heads, B, L, 1ull << 38, st, s)
+            : launch_k6<256, kRowF16, k6::kEpiBiasT>(zsrc, nullptr, 256, 0, nullptr, nullptr, w->bias_w, n_bias, out,
+                                                     w->bias_b, heads, B, L, 1ull << 39, st, s);
+  else
+    r = f32 ? launch_k6<128, kRowF32, k6::kEpiBiasT>(zsrc, nullptr, 128, 0, nullptr, nullptr, w->bias_w, n_bias, out,
+                                                     w->bias_b, heads, B, L, 1ull << 40, st, s)
+            : launch_k6<128, kRowF16, k6::kEpiBiasT>(zsrc, nullptr, 128, 0, nullptr, nullptr, w->bias_w, n_bias, out,
+                                                     w->bias_b, heads, B, L, 1ull << 41, st, s);
+  return r;
 }
 
 int tmu_ipc_export(const void* ptr, void* handle, unsigned long long* offset) {

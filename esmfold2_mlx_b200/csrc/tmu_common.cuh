@@ -313,6 +313,15 @@ __device__ __forceinline__ void tmem_wait_ld16x2(uint32_t (&r)[16], uint32_t (&s
                : "memory");
 }
 
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
 // One thread of a warp waits (bounded) and the whole warp gets its verdict; the __syncwarp
 // orders the other lanes' later reads after lane 0's acquiring wait.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const WaitCtx& ctx, unsigned int site) {

@@ -8,7 +8,8 @@ Inputs are seeded synthetic tensors (``synthetic``); weights are random-init.  T
 is launched ``--reps`` times after one untimed launch of every stage (and one more of itself), then the script checks the
 device status word and prints the mean CUDA-event time per launch.  Use ``ncu -k regex:<name>``
 with ``project_gate``, ``contract``, ``emit_residual`` or ``transition`` to select a kernel
-(k4 is the fused pair transition; k5 the distogram expected distance, ``disto``).
+(k4 is the fused pair transition; k5 the distogram expected distance, ``disto``; pc the diffusion
+pair conditioning, ``ln_gemm`` and ``transition``).
 """
 
 from __future__ import annotations
@@ -26,7 +27,8 @@ def main():
     ap.add_argument("--L", type=int, default=1024)
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--direction", choices=["out", "in"], default="out")
-    ap.add_argument("--stage", choices=["all", "k1", "k2", "k3", "k4", "k5"], default="all")
+    ap.add_argument("--stage", choices=["all", "k1", "k2", "k3", "k4", "k5", "pc"], default="all",
+                    help="pc: the diffusion pair conditioning (tmu_pair_cond: K6, K4 rows x 2, K6)")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--mask-pad", type=int, default=0)
     ap.add_argument("--cz", type=int, choices=[128, 256], default=128, help="c_z = c")
@@ -64,6 +66,15 @@ def main():
     if args.stage == "k4":
         tw = ops.TransitionWeights.from_module(trunk.blocks[0].pair_transition, dev)
         stages["k4"] = lambda: ops.transition(z, tw, out=out, status=status)
+    if args.stage == "pc":
+        from . import pair_cond
+        from .synthetic import DiffusionHead
+        pw = pair_cond.PairCondWeights.from_head(DiffusionHead(), dev)
+        zt = pair_tensor(B, L, 256, 1).to(dev) * 20.0
+        rp = pair_tensor(B, L, 256, 2).to(dev)
+        ws = torch.empty(pair_cond.workspace_bytes(B, L, pw.c_pair), dtype=torch.uint8, device=dev)
+        pout = torch.empty(pw.n_bias // pw.heads, B, pw.heads, L, L, dtype=torch.float16, device=dev)
+        stages["pc"] = lambda: pair_cond.pair_biases(pw, zt, rp, out=pout, workspace=ws, status=status)
     fn = stages[args.stage]
     fn()  # warm-up: the stage's own output allocations happen here, outside the timed launches
     torch.cuda.synchronize()

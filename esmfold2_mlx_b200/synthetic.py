@@ -112,6 +112,52 @@ class FoldModel(nn.Module):
         self.folding_trunk = folding_trunk
 
 
+class _TransitionLayer(nn.Module):
+    """``TransitionLayer``: LN -> silu(h @ a) * (h @ b) -> out (``mlx_diffusion.py:51-52``)."""
+
+    def __init__(self, c: int, hidden: int, g: torch.Generator, ln_noise: float):
+        super().__init__()
+        self.norm = _ln(c, g, ln_noise)
+        self.a_proj = _linear(hidden, c, g)
+        self.b_proj = _linear(hidden, c, g)
+        self.out_proj = _linear(c, hidden, g)
+
+
+class _AttnPairBias(nn.Module):
+    """The pair-bias part of one token-transformer attention block (``mlx_diffusion.py:87-89``)."""
+
+    def __init__(self, c: int, heads: int, g: torch.Generator, ln_noise: float):
+        super().__init__()
+        self.num_heads = heads
+        self.pair_norm = _ln(c, g, ln_noise)
+        self.pair_bias_proj = _linear(heads, c, g)
+
+
+class DiffusionHead(nn.Module):
+    """The diffusion head's pair-conditioning weights under the names the reference reads
+    (``mlx_diffusion.py:61-64,85-92``): ``diffusion_module.conditioning.{z_input_norm, z_proj,
+    z_transitions[k].{norm, a_proj, b_proj, out_proj}}`` and
+    ``diffusion_module.token_transformer.attn_blocks[i].{pair_norm, pair_bias_proj, num_heads}``.
+    The checkpoint's sizes are not public here; the defaults take c_trunk = c_rel = 256 (the
+    reference's "[L, L, 512]" concat, ``mlx_diffusion.py:322``), c_pair = 256, two transitions of
+    width 2 c_pair and 12 blocks x 16 heads (its "12 token-attention pair biases", ``:5``)."""
+
+    def __init__(self, c_trunk: int = 256, c_rel: int = 256, c_pair: int = 256, hidden: int = 512,
+                 n_transitions: int = 2, n_blocks: int = 12, heads: int = 16, seed: int = 0,
+                 ln_noise: float = 0.1):
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        cond = nn.Module()
+        cond.z_input_norm = _ln(c_trunk + c_rel, g, ln_noise)
+        cond.z_proj = _linear(c_pair, c_trunk + c_rel, g)
+        cond.z_transitions = nn.ModuleList(_TransitionLayer(c_pair, hidden, g, ln_noise) for _ in range(n_transitions))
+        tt = nn.Module()
+        tt.attn_blocks = nn.ModuleList(_AttnPairBias(c_pair, heads, g, ln_noise) for _ in range(n_blocks))
+        self.diffusion_module = nn.Module()
+        self.diffusion_module.conditioning = cond
+        self.diffusion_module.token_transformer = tt
+
+
 def trimul_biases(c_z: int, c: int, seed: int, std: float = 0.02) -> dict:
     """Biases for one tri-mul: proj (4c, reference column order), emit (c_z), gate (c_z)."""
     g = torch.Generator().manual_seed(seed)

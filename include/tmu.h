@@ -192,7 +192,7 @@ typedef struct tmu_transition_weights {
   const void* w3;    /* fp16 [c_z, hidden]: ffn.w3.weight */
 } tmu_transition_weights;
 
-/* c_z = 128, hidden a multiple of 64 in [64, 4096]; z [B, L, L, c_z] fp16. */
+/* c_z = 128 or 256, hidden a multiple of 64 in [64, 4096]; z [B, L, L, c_z] fp16. */
 int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int c_z, int hidden,
                    int activation, void* status, void* stream);
 
@@ -203,6 +203,42 @@ int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, 
  * [B, L, L]; n_bins = 128. */
 int tmu_disto_expected(const void* z, const void* w, const float* bias, const float* centres, float* out, int B,
                        int L, int c_z, int n_bins, void* status, void* stream);
+
+/* ---- Diffusion pair conditioning (K6 + K4 row mode): the per-fold pair biases of the diffusion
+ * head's token transformer.  Replaces pair_biases (mlx_diffusion16.py:81-87 in the pair16
+ * precision of the adopted var_mlx_diffusion16 stack; fp32 form mlx_diffusion.py:252-259):
+ *   z    = fp16(fp16(LN(concat(z_trunk, rel_pos))) @ proj^T)                  (fp32 from here on)
+ *   z   += fp32(fp16(fp16(silu(x1) * x2) @ w3^T)), x = fp16(fp16(LN(z)) @ w12^T)   per transition
+ *   bias = fp16(fp16(fp16(LN(z)) @ bias_w^T) + bias_b)       (LN without affine)
+ * and out[k, b, h, i, j] = bias[b, i, j, k * heads + h]  ([n_bias / heads, B, heads, L, L]).
+ * z_trunk, rel_pos fp32 [B, L, L, c_trunk] and [B, L, L, c_rel]; LayerNorm parameters fp32, matrices fp16 in nn.Linear layout
+ * ([out, in]); bias_w [n_bias, c_pair] folds each token block's pair_norm affine into its
+ * pair_bias_proj (mlx_diffusion.py:85-89), bias_b fp16 [n_bias]. */
+typedef struct tmu_cond_transition_weights {
+  const float* ln_w;  /* fp32 [c_pair]: norm.weight */
+  const float* ln_b;  /* fp32 [c_pair]: norm.bias */
+  const void* w12;    /* fp16 [2*hidden, c_pair]: a_proj.weight rows, then b_proj.weight rows */
+  const void* w3;     /* fp16 [c_pair, hidden]: out_proj.weight */
+} tmu_cond_transition_weights;
+
+typedef struct tmu_pair_cond_weights {
+  const float* ln_w;  /* fp32 [c_trunk + c_rel]: z_input_norm.weight */
+  const float* ln_b;  /* fp32 [c_trunk + c_rel]: z_input_norm.bias */
+  const void* proj;   /* fp16 [c_pair, c_trunk + c_rel]: z_proj.weight */
+  int n_transitions;
+  const tmu_cond_transition_weights* transitions; /* [n_transitions] */
+  const void* bias_w; /* fp16 [n_bias, c_pair] */
+  const void* bias_b; /* fp16 [n_bias] */
+} tmu_pair_cond_weights;
+
+/* Bytes of scratch tmu_pair_cond needs: z fp16 and z fp32, [B, L, L, c_pair] each. */
+size_t tmu_pair_cond_workspace_bytes(int B, int L, int c_pair);
+
+/* Shapes: c_trunk == c_rel, c_trunk + c_rel in {256, 512}; c_pair in {128, 256}; hidden a
+ * multiple of 64 in [64, 4096]; n_bias a multiple of 16 in [16, 256], divisible by heads. */
+int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_cond_weights* w, int B, int L,
+                  int c_trunk, int c_rel, int c_pair, int hidden, int n_bias, int heads, void* out,
+                  void* workspace, size_t workspace_bytes, void* status, void* stream);
 
 /* ---- Copy-engine exchange for the row-sharded path (no counterpart in the reference).  A rank
  * exports a device buffer with tmu_ipc_export (CUDA IPC handle of the allocation that contains

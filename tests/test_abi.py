@@ -89,3 +89,18 @@ def test_argument_checks_of_the_later_entry_points_need_no_gpu(lib):
     assert lib.tmu_ipc_import(None, 0, ctypes.byref(p)) == 1
     assert lib.tmu_ipc_close(None) == 1
     assert lib.tmu_copy_async(None, None, 0, None) == 1
+
+
+def test_pair_cond_argument_checks_need_no_gpu(lib):
+    """tmu_pair_cond rejects unsupported widths and missing weights before touching a device."""
+    PW = ctypes.POINTER(_lib.TmuPairCondWeights)
+    pw = _lib.TmuPairCondWeights()
+    args = lambda ct, cr, cp, h, nb, H: (None, None, PW(), 1, 16, ct, cr, cp, h, nb, H, None, None, 0, None, None)  # noqa: E731
+    assert lib.tmu_pair_cond(*args(256, 128, 256, 512, 192, 16)) == 4  # c_trunk != c_rel
+    assert lib.tmu_pair_cond(*args(256, 256, 192, 512, 192, 16)) == 4  # c_pair
+    assert lib.tmu_pair_cond(*args(256, 256, 256, 512, 192, 16)) == 1  # no weights
+    a = list(args(256, 256, 256, 512, 192, 16))
+    a[2] = ctypes.byref(pw)
+    assert lib.tmu_pair_cond(*a) == 1  # empty weight struct
+    assert lib.tmu_pair_cond_workspace_bytes(1, 16, 256) == 16 * 16 * 256 * 6
+    assert lib.tmu_pair_cond_workspace_bytes(0, 16, 256) == 0

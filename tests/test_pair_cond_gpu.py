@@ -1,0 +1,118 @@
+"""GPU parity of the diffusion pair conditioning (``tmu_pair_cond``: K6 + K4 row mode + K6)
+against the CPU oracle (``oracle/pair_cond_oracle.py``, mlx_diffusion16.py:81-87 in pair16).
+
+Stage by stage, each GPU stage is compared with the oracle's stage fed the GPU's own input
+(the workspace holds z0 fp16 and the final fp32 z): fp32 summation order and the hardware
+sigmoid may flip a rare fp16 rounding, so a small fraction of elements differ, by at most one
+fp16 ulp at the tensor's scale (measured: 0.2-4 % of elements, 0.5-1 ulp; near-zero outputs of
+a cancelling dot product move by that absolute amount, many of their own ulps).  End to end the fp32 residual stream carries every such flip into the
+next LayerNorm, so the pipeline is sensitive to summation order as such: the oracle itself
+changes about a fifth of its outputs by one ulp when its GEMMs accumulate in fp64 instead of
+fp32.  The end-to-end bound is therefore relative to that sensitivity (measured: GPU 34 % vs
+the oracle's own 22 % on the default shape), with the maximum deviation held to 2 ulps at the
+output's scale (measured: 1).
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from esmfold2_mlx_b200 import _lib, pair_cond
+from esmfold2_mlx_b200.ops import new_status, read_status
+from esmfold2_mlx_b200.synthetic import DiffusionHead, pair_tensor
+from oracle import pair_cond_oracle as pco
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ulp16(x: float) -> float:
+    x = max(abs(x), 2.0**-14)
+    return 2.0 ** (math.floor(math.log2(x)) - 10)
+
+
+def _case(B, L, c_side, c_pair, hidden, n_trans, n_blocks, heads, seed):
+    head = DiffusionHead(c_side, c_side, c_pair, hidden, n_trans, n_blocks, heads, seed=seed)
+    zt = pair_tensor(B, L, c_side, seed + 1) * 20.0
+    rp = pair_tensor(B, L, c_side, seed + 2)
+    ref = pco.pair_biases_fp16(pco.pair_cond_params(head), zt, rp)
+    return head, zt, rp, ref
+
+
+def _frac(a, b) -> float:
+    return float((a != b).float().mean())
+
+
+@pytest.mark.parametrize("B,L,c_side,c_pair,hidden,n_trans,n_blocks,heads", [
+    (1, 37, 256, 256, 512, 2, 12, 16),   # the default stand-in shape, ragged L
+    (1, 37, 256, 256, 512, 1, 12, 16),   # one transition: its output is visible in the workspace
+    (2, 50, 256, 256, 512, 2, 12, 16),   # batched folds
+    (1, 130, 256, 256, 512, 1, 12, 16),  # L > 128: several tiles per row
+    (1, 64, 128, 128, 256, 1, 4, 8),     # narrow variant
+    (1, 40, 256, 256, 512, 0, 2, 16),    # no transitions: the bias GEMM reads fp16 z
+])
+def test_pair_biases_match_oracle(B, L, c_side, c_pair, hidden, n_trans, n_blocks, heads):
+    head, zt, rp, ref = _case(B, L, c_side, c_pair, hidden, n_trans, n_blocks, heads, seed=L + hidden)
+    p = pco.pair_cond_params(head)
+    w = pair_cond.PairCondWeights.from_head(head, DEV)
+    ws = torch.empty(pair_cond.workspace_bytes(B, L, c_pair), dtype=torch.uint8, device=DEV)
+    st = new_status(DEV)
+    out = pair_cond.pair_biases(w, zt.to(DEV), rp.to(DEV), workspace=ws, status=st)
+    torch.cuda.synchronize()
+    assert read_status(st)[0] == 0
+    assert out.shape == (n_blocks, B, heads, L, L) and out.dtype == torch.float16
+    got = out.float().cpu()
+    assert bool(torch.isfinite(got).all())
+
+    cells = B * L * L
+    off32 = (cells * c_pair * 2 + 255) // 256 * 256
+    z0 = ws[:cells * c_pair * 2].view(torch.float16).view(B, L, L, c_pair).float().cpu()
+    z32 = ws[off32:off32 + cells * c_pair * 4].view(torch.float32).view(B, L, L, c_pair).cpu()
+
+    # stage A: LN(concat) -> proj, fp16
+    z0_ref = pco.stage_project(p, zt, rp)
+    assert float((z0 - z0_ref).abs().max()) <= _ulp16(float(z0_ref.abs().max()))
+    assert _frac(z0, z0_ref) < 0.01
+    # one transition from the GPU's own z0: z1 = z0 + r16(t); a flip of r16(t) is one ulp of t
+    if n_trans == 1:
+        z1_ref = pco.stage_transition(p["transitions"][0], z0)
+        t_scale = float((z1_ref - z0).abs().max())
+        tol = 1.01 * _ulp16(t_scale) + float(z1_ref.abs().max()) * 2.0**-23  # + the fp32 add's own rounding
+        assert float((z32 - z1_ref).abs().max()) <= tol
+        assert _frac(z32, z1_ref) < 0.06
+    # the bias GEMM from the GPU's own final z
+    bias_ref = pco.stage_bias(p, z32 if n_trans else z0)
+    assert float((got - bias_ref).abs().max()) <= _ulp16(float(bias_ref.abs().max()))
+    assert _frac(got, bias_ref) < 0.01
+
+    # end to end against the all-CPU oracle
+    ref64 = pco.pair_biases_fp16(p, zt, rp, acc=torch.float64)
+    diff = (got - ref).abs()
+    assert float(diff.max()) <= 2 * _ulp16(float(ref.abs().max())), float(diff.max())
+    assert _frac(got, ref) <= 2 * _frac(ref, ref64) + 0.05
+
+
+def test_pair_biases_reuse_workspace_and_output():
+    head, zt, rp, ref = _case(1, 48, 256, 256, 512, 2, 12, 16, seed=9)
+    w = pair_cond.PairCondWeights.from_head(head, DEV)
+    ws = torch.empty(pair_cond.workspace_bytes(1, 48, 256), dtype=torch.uint8, device=DEV)
+    out = torch.empty(12, 1, 16, 48, 48, dtype=torch.float16, device=DEV)
+    a = pair_cond.pair_biases(w, zt.to(DEV), rp.to(DEV), out=out, workspace=ws).clone()
+    b = pair_cond.pair_biases(w, zt.to(DEV), rp.to(DEV), out=out, workspace=ws)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+
+
+def test_pair_biases_rejects_bad_shapes():
+    head, zt, rp, _ = _case(1, 16, 256, 256, 512, 1, 2, 16, seed=3)
+    w = pair_cond.PairCondWeights.from_head(head, DEV)
+    with pytest.raises(ValueError):
+        pair_cond.pair_biases(w, zt.to(DEV), rp[..., :128].contiguous().to(DEV))
+    w.heads = 5  # n_bias = 32 not divisible by 5
+    w._struct = None
+    with pytest.raises(_lib.TmuError):
+        pair_cond.pair_biases(w, zt.to(DEV), rp.to(DEV))
