@@ -100,7 +100,7 @@ SIGNATURES = {
     "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_transition": (_i, [_vp, _vp, _TW, _i, _i, _i, _i, _i, _vp, _vp]),
     "tmu_disto_expected": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
-    "tmu_pair_cond_workspace_bytes": (_sz, [_i, _i, _i]),
+    "tmu_pair_cond_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "tmu_pair_cond": (_i, [_vp, _vp, ctypes.POINTER(TmuPairCondWeights), _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp,
                            _sz, _vp, _vp]),
     "tmu_ipc_export": (_i, [_vp, _vp, ctypes.POINTER(_ull)]),

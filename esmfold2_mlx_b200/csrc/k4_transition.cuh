@@ -34,12 +34,12 @@
 //   warps 15-18 epilogue: D2 + z -> z' over the z tile, per-warp TMA store of 32 positions
 // Each tile is read and written by exactly one CTA, so z_out may alias z.
 //
-// Row mode (MODE != kModeTile): the transition layers of the diffusion head's pair conditioning
+// h mode (MODE == kModeH): the transition layers of the diffusion head's pair conditioning
 // (mlx_diffusion16.py:64-67,83-84: z = z + fp32(fp16(silu(h@a) * (h@b)) @ out), h = fp16(LN(z)),
-// the residual stream fp32).  The LayerNorm warps read their rows straight from global memory
-// (fp16 z0 or fp32 z, one warp per row, fp32 gamma/beta), there is no z tile producer, and the
-// epilogue adds fp16(D2) to the fp32 row re-read from global memory and stores fp32.  The SwiGLU
-// arithmetic (w12 = [a; b] rows) is the trunk transition's.
+// the residual stream fp32).  h comes precomputed from the row LayerNorm pass (which rebuilds
+// the fp32 z from its fp16 terms) and is loaded by TMA straight into the A-operand stages; the
+// epilogue stores only t = fp16(D2), the next term of z.  The SwiGLU arithmetic (w12 = [a; b]
+// rows) is the trunk transition's.
 #pragma once
 
 #include "ln_rows.cuh"
@@ -56,13 +56,16 @@ constexpr int NW = 4;
 constexpr int kThreads = 608;
 constexpr int TMEM_COLS = 512;
 
-enum Mode : int { kModeTile = 0, kModeRows16 = 1, kModeRows32 = 2 };
+// kModeTile: the trunk transition (z tiles by TMA, LayerNorm in the kernel, fp16 residual).
+// kModeH:    h = fp16(LN(z)) precomputed (a row LayerNorm pass), loaded by TMA straight into the
+//            A-operand stages; t = fp16(D2) out.
+enum Mode : int { kModeTile = 0, kModeH = 1 };
 
 template <int CZ, int MODE = kModeTile>
 struct Cfg {
   static constexpr int KATOMS = CZ / 64;
   static constexpr int TILE_BYTES = TILE * CZ * 2;                     // 32 or 64 KB
-  static constexpr bool ROWS = MODE != kModeTile;                      // LN from global rows, fp32 residual
+  static constexpr bool ROWS = MODE != kModeTile;                      // no z tile: h by TMA, t rows out
   static constexpr bool INPLACE = !ROWS && CZ == 256;                  // h overwrites z in its stage
   static constexpr int NACC = CZ == 128 ? 2 : 1;                       // D2 accumulators
   static constexpr int OFF_Z = 0;                                      // 2 stages (tile mode)
@@ -77,16 +80,13 @@ struct Cfg {
 };
 
 struct Params {
-  CUtensorMap tm_z;    // z [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle (load)
+  CUtensorMap tm_z;    // z (kModeH: h) [B, L, L, c_z]: box {64, jw, ih, 1}, 128B swizzle (load)
   CUtensorMap tm_zo;   // z_out: box {64, min(jw,32), 32/min(jw,32), 1}, 128B swizzle (per-warp store)
   CUtensorMap tm_w12;  // w12 [W, c_z]: box {64, 64}, 128B swizzle
   CUtensorMap tm_w3;   // w3 [c_z, h]: box {64, 128}, 128B swizzle
   const __half* ln_w;
   const __half* ln_b;
-  const void* zin;     // row mode: z rows, fp16 (kModeRows16) or fp32 (kModeRows32) [cells, c_z]
-  float* zout;         // row mode: z' rows fp32 [cells, c_z] (may alias an fp32 zin)
-  const float* ln_g32; // row mode: LayerNorm gamma/beta fp32
-  const float* ln_b32;
+  __half* tout;        // h mode: t = fp16(ffn(h)) [cells, c_z]
   int hidden;          // h
   int nchunk;          // h / 64
   int L, ih, jw, tiles_i, tiles_j, num_tiles;
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     for (int s = 0; s < 2; ++s) {
       mbar_init(&zfull[s], 1);
       mbar_init(&zempty[s], 4);    // the four epilogue warps, after their stores read the tile
-      mbar_init(&hfull[s], 4);     // the four LayerNorm warps
+      mbar_init(&hfull[s], MODE == kModeH ? 1 : 4);  // the four LayerNorm warps, or the h loads
       mbar_init(&hempty[s], 1);    // the MMA, after the tile's last GEMM1
       mbar_init(&d1full[s], 1);
       mbar_init(&d1empty[s], 4);   // the four activation warps
@@ -171,10 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
   if (!C::ROWS)
     for (int i = threadIdx.x; i < 2 * CZ; i += blockDim.x) par[i] = __half2float(i < CZ ? p.ln_w[i] : p.ln_b[i - CZ]);
   if (warp == 0 && lane == 0) {
-    if (!C::ROWS) {
-      tma_prefetch_desc(&p.tm_z);
-      tma_prefetch_desc(&p.tm_zo);
-    }
+    tma_prefetch_desc(&p.tm_z);
+    if (MODE == kModeTile) tma_prefetch_desc(&p.tm_zo);
     tma_prefetch_desc(&p.tm_w12);
     tma_prefetch_desc(&p.tm_w3);
   }
@@ -225,8 +223,27 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
       }
     }
   } else if (warp == 2) {
+    // ---------------- h tile producer (kModeH): the stage is free after the tile's last GEMM1 ----------------
+    if (lane == 0 && MODE == kModeH) {
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+        int bb, i0, j0;
+        decode_tile(p, tile, bb, i0, j0);
+        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        if (!mbar_wait(&hempty[s], ph ^ 1, ctx, kSiteProdZ)) break;
+        mbar_arrive_expect_tx(&hfull[s], C::TILE_BYTES);
+        for (int a = 0; a < C::KATOMS; ++a)
+          tma_load_4d(smem + C::OFF_H + s * C::TILE_BYTES + a * ATOM_BYTES, &p.tm_z, &hfull[s], a * 64, j0, i0, bb);
+      }
+      if (abort_sh) {
+        for (uint32_t s = 0; s < 2; ++s) {
+          const uint32_t armed = it > s ? (it - s + 1) / 2 : 0;
+          if (armed) mbar_drain(&hfull[s], (armed - 1) & 1, 200000000ull);
+        }
+      }
+    }
     // ---------------- z tile producer (tile mode) ----------------
-    if (lane == 0 && !C::ROWS) {
+    if (lane == 0 && MODE == kModeTile) {
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         int bb, i0, j0;
@@ -320,44 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     // ---------------- LayerNorm: z tile -> h ----------------
     const int row = threadIdx.x - 96;
     uint32_t it = 0, gcount = 0;
-    if constexpr (C::ROWS) {
-      // Row mode: warp w normalises rows w, w + 4, .. of the tile, four rows in flight.
-      constexpr int NQ = CZ / 128;
-      constexpr int SRC = MODE == kModeRows16 ? kRowF16 : kRowF32;
-      const int w = warp - 3;
-      float4 gg[NQ], bb4[NQ];
-      load_ln_par<NQ>(p.ln_g32, p.ln_b32, lane, gg, bb4);
-      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
-        int bb, i0, j0;
-        decode_tile(p, tile, bb, i0, j0);
-        const uint32_t s = it & 1, ph = (it >> 1) & 1;
-        if (!group_wait(&hempty[s], ph ^ 1, nullptr, 0, ctx, kSiteLn, row == 0, 4, 128, gflags + 6, gcount)) break;
-        uint8_t* H = smem + C::OFF_H + s * C::TILE_BYTES;
-#pragma unroll 1
-        for (int r0 = 0; r0 < 32; r0 += 4) {
-          float4 v[4][NQ];
-          bool valid[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int rr = w + 4 * (r0 + u);
-            const int gi = i0 + rr / p.jw, gj = j0 + rr % p.jw;
-            valid[u] = gi < p.L && gj < p.L;
-            if (valid[u])
-              load_row<SRC, NQ>(p.zin, nullptr, (static_cast<size_t>(bb) * p.L + gi) * p.L + gj, CZ, 0, lane, v[u]);
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int rr = w + 4 * (r0 + u);
-            if (valid[u])
-              ln_row_store<NQ>(v[u], gg, bb4, true, 1e-5f, H, ATOM_BYTES, rr, lane);
-            else
-              zero_row_store<NQ>(H, ATOM_BYTES, rr, lane);
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&hfull[s]);
-      }
+    if constexpr (MODE == kModeH) {
+      // h arrives by TMA: nothing to normalise
     } else
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
@@ -465,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
     uint32_t it = 0, gcount = 0;
     int reload_armed = -1;  // c_z = 256: the stage whose reload is in flight (for the abort drain)
     if constexpr (C::ROWS) {
-      // Row mode: z' = z + fp32(fp16(D2)), z re-read from global memory (an L2 hit), fp32 out.
+      // h mode: t = fp16(D2), stored straight from registers.
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         int bb, i0, j0;
         decode_tile(p, tile, bb, i0, j0);
@@ -474,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
         tc_fence_after();
         const int gi = i0 + row / p.jw, gj = j0 + row % p.jw;
         const bool valid = gi < p.L && gj < p.L;
-        const size_t cell = (static_cast<size_t>(bb) * p.L + gi) * p.L + gj;
+        uint4* dst = reinterpret_cast<uint4*>(p.tout + ((static_cast<size_t>(bb) * p.L + gi) * p.L + gj) * CZ);
 #pragma unroll 1
         for (int c0 = 0; c0 < CZ; c0 += 32) {
           uint32_t v[32];
@@ -486,21 +467,11 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
             if (lane == 0) mbar_arrive(&accempty[ab]);
           }
           if (!valid) continue;
-          float4* dst = reinterpret_cast<float4*>(p.zout + cell * CZ + c0);
+          uint32_t o[16];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float4 z;
-            if (MODE == kModeRows16) {
-              const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __half*>(p.zin) + cell * CZ + c0) + e);
-              const float2 a = unpack_half2(u.x), b = unpack_half2(u.y);
-              z = make_float4(a.x, a.y, b.x, b.y);
-            } else {
-              z = reinterpret_cast<const float4*>(static_cast<const float*>(p.zin) + cell * CZ + c0)[e];
-            }
-            dst[e] = make_float4(z.x + round_f16(__uint_as_float(v[4 * e])), z.y + round_f16(__uint_as_float(v[4 * e + 1])),
-                                 z.z + round_f16(__uint_as_float(v[4 * e + 2])),
-                                 z.w + round_f16(__uint_as_float(v[4 * e + 3])));
-          }
+          for (int e = 0; e < 16; ++e) o[e] = pack_half2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1]));
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dst[c0 / 8 + e] = make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
         }
       }
     } else

@@ -1,9 +1,9 @@
-// LayerNorm of pair-grid rows read straight from global memory by one warp per row, written as
-// fp16 into a K-major 128B-swizzled MMA operand tile (atoms of 128 rows x 64 channels).
+// Row LayerNorm pass over the pair grid: h[row] = fp16(LN(x[row])), written row-major for a TMA
+// tile map over [B, L, L, K] to read.  The GEMM kernels of the diffusion pair conditioning
+// (K6, K4 in h mode) take their A operand from it.
 //
-// Lane l holds channels 4(l + 32q) .. 4(l + 32q) + 3 for q < NQ = K / 128, so every load
-// instruction of the warp reads 32 x 16 B (fp32) or 32 x 8 B (fp16) contiguous bytes of the row.
-// Plain (coherent) loads: a kernel may write the rows it normalised later in the same launch.
+// One warp per row: lane l holds channels 4(l + 32q) .. 4(l + 32q) + 3 for q < NQ = K / 128, so
+// every load instruction of the warp reads 32 x 16 B (fp32) or 32 x 8 B (fp16) contiguous bytes.
 // Statistics are fp32 and two-pass over the registers: mean = sum(x) / K, then
 // var = sum((x - mean)^2) / K, each a warp all-reduce; y = (x - mean) * rstd * gamma + beta, rounded
 // once to fp16 (gamma/beta absent: y = (x - mean) * rstd).
@@ -20,8 +20,9 @@ __device__ __forceinline__ float warp_allsum(float x) {
 }
 
 // Where a row comes from: one fp32 or fp16 tensor, the concatenation of two fp32 tensors of K/2
-// channels each (channels [0, K/2) from x1, [K/2, K) from x2), or the sum of two fp32 tensors.
-enum RowSrc : int { kRowF32 = 0, kRowF16 = 1, kRowCat32 = 2, kRowSum32 = 3 };
+// channels each (channels [0, K/2) from x1, [K/2, K) from x2), the sum of two fp32 tensors, or
+// an fp32 sum of fp16 terms (RowTerms below).
+enum RowSrc : int { kRowF32 = 0, kRowF16 = 1, kRowCat32 = 2, kRowSum32 = 3, kRowTerms16 = 4 };
 
 template <int SRC, int NQ>
 __device__ __forceinline__ void load_row(const void* x1, const void* x2, size_t cell, int ld1, int ld2, int lane,
@@ -46,6 +47,17 @@ __device__ __forceinline__ void load_row(const void* x1, const void* x2, size_t 
   }
 }
 
+// A row held as an fp32 sum of fp16 terms, z = fl32(fl32(s0 + s1) + s2) ..., added in source
+// order: a residual stream kept as its fp16 increments (z0 and each transition's rounded output)
+// gives back exactly the fp32 value a running fp32 sum would hold.
+constexpr int kMaxTerms = 4;
+
+struct RowTerms {
+  const __half* src[kMaxTerms];
+  int n;   // 1 .. kMaxTerms
+  int ld;  // row pitch, elements (the same for every term)
+};
+
 // gamma/beta of this lane's channels (or identity when g == nullptr)
 template <int NQ>
 __device__ __forceinline__ void load_ln_par(const float* g, const float* b, int lane, float4 (&gg)[NQ],
@@ -57,50 +69,103 @@ __device__ __forceinline__ void load_ln_par(const float* g, const float* b, int 
   }
 }
 
-// Normalise the row held in v and write it to row `row` of the swizzled tile at `tile`.
-// affine == false skips gamma/beta (mx.fast.layer_norm(x, None, None, eps)).
-template <int NQ>
-__device__ __forceinline__ void ln_row_store(const float4 (&v)[NQ], const float4 (&gg)[NQ], const float4 (&bb)[NQ],
-                                             bool affine, float eps, uint8_t* tile, int atom_bytes, int row,
-                                             int lane) {
-  constexpr float inv_k = 1.0f / (128 * NQ);
-  float s = 0.f;
+namespace lnr {
+
+// h[row] = fp16(LN(x[row])) for `rows` rows of K channels.  RL rows in flight per warp and many
+// warps per SM, so the loads of this memory-bound pass overlap.
+constexpr int kThreads = 256;
+
+struct Params {
+  const void* x1;
+  const void* x2;
+  int ld1, ld2;
+  RowTerms terms;
+  const float* g;  // [K] or null
+  const float* b;
+  __half* out;     // [rows, K]
+  long long rows;
+  float eps;
+};
+
+template <int K, int SRC>
+__global__ void __launch_bounds__(kThreads) ln_rows_kernel(const __grid_constant__ Params p) {
+  constexpr int NQ = K / 128;
+  constexpr int RL = K <= 256 ? 4 : 2;
+  // fp16 terms: every load of the RL rows (all terms, kMaxTerms of them predicated by the count)
+  // is issued before the first add, so the rows' memory latencies overlap.
+  constexpr int NT = SRC == kRowTerms16 ? kMaxTerms : 1;
+  const int lane = threadIdx.x & 31;
+  const long long warp0 = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * kThreads) >> 5;
+  float4 gg[NQ], bb[NQ];
+  load_ln_par<NQ>(p.g, p.b, lane, gg, bb);
+  const bool affine = p.g != nullptr;
+  griddep_wait();  // the rows may be the previous kernel's output
+  for (long long r0 = warp0 * RL; r0 < p.rows; r0 += nwarps * RL) {
+    float4 v[RL][NQ];
+    if constexpr (SRC == kRowTerms16) {
+      uint2 raw[RL][NT][NQ];
 #pragma unroll
-  for (int q = 0; q < NQ; ++q) s += (v[q].x + v[q].y) + (v[q].z + v[q].w);
-  const float mean = warp_allsum(s) * inv_k;
-  float s2 = 0.f;
+      for (int u = 0; u < RL; ++u)
 #pragma unroll
-  for (int q = 0; q < NQ; ++q) {
-    const float a = v[q].x - mean, b = v[q].y - mean, c = v[q].z - mean, d = v[q].w - mean;
-    s2 = fmaf(a, a, s2);
-    s2 = fmaf(b, b, s2);
-    s2 = fmaf(c, c, s2);
-    s2 = fmaf(d, d, s2);
-  }
-  const float rstd = rsqrtf(warp_allsum(s2) * inv_k + eps);
+        for (int k = 0; k < NT; ++k)
 #pragma unroll
-  for (int q = 0; q < NQ; ++q) {
-    float2 lo = make_float2((v[q].x - mean) * rstd, (v[q].y - mean) * rstd);
-    float2 hi = make_float2((v[q].z - mean) * rstd, (v[q].w - mean) * rstd);
-    if (affine) {
-      lo = make_float2(fmaf(lo.x, gg[q].x, bb[q].x), fmaf(lo.y, gg[q].y, bb[q].y));
-      hi = make_float2(fmaf(hi.x, gg[q].z, bb[q].z), fmaf(hi.y, gg[q].w, bb[q].w));
+          for (int q = 0; q < NQ; ++q)
+            raw[u][k][q] = (r0 + u < p.rows && k < p.terms.n)
+                               ? reinterpret_cast<const uint2*>(p.terms.src[k] + static_cast<size_t>(r0 + u) * p.terms.ld)[lane + 32 * q]
+                               : make_uint2(0u, 0u);
+#pragma unroll
+      for (int u = 0; u < RL; ++u)
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          float2 a = unpack_half2(raw[u][0][q].x), b = unpack_half2(raw[u][0][q].y);
+          v[u][q] = make_float4(a.x, a.y, b.x, b.y);
+#pragma unroll
+          for (int k = 1; k < NT; ++k)
+            if (k < p.terms.n) {  // fl32(fl32(t0 + t1) + t2) ..., in term order
+              a = unpack_half2(raw[u][k][q].x);
+              b = unpack_half2(raw[u][k][q].y);
+              v[u][q] = make_float4(v[u][q].x + a.x, v[u][q].y + a.y, v[u][q].z + b.x, v[u][q].w + b.y);
+            }
+        }
+    } else {
+#pragma unroll
+      for (int u = 0; u < RL; ++u)
+        if (r0 + u < p.rows) load_row<SRC, NQ>(p.x1, p.x2, static_cast<size_t>(r0 + u), p.ld1, p.ld2, lane, v[u]);
     }
-    const int c0 = 4 * (lane + 32 * q);  // first channel of this lane's four
-    uint8_t* dst = tile + (c0 >> 6) * atom_bytes + sw128_off(row, (c0 & 63) >> 3) + (c0 & 4) * 2;
-    *reinterpret_cast<uint2*>(dst) = make_uint2(pack_half2(lo.x, lo.y), pack_half2(hi.x, hi.y));
-  }
-}
-
-// A row past the grid's edge (a tile overhanging L): zeros, so the MMA reads defined values.
-template <int NQ>
-__device__ __forceinline__ void zero_row_store(uint8_t* tile, int atom_bytes, int row, int lane) {
 #pragma unroll
-  for (int q = 0; q < NQ; ++q) {
-    const int c0 = 4 * (lane + 32 * q);
-    uint8_t* dst = tile + (c0 >> 6) * atom_bytes + sw128_off(row, (c0 & 63) >> 3) + (c0 & 4) * 2;
-    *reinterpret_cast<uint2*>(dst) = make_uint2(0u, 0u);
+    for (int u = 0; u < RL; ++u) {
+      const long long row = r0 + u;
+      if (row >= p.rows) break;
+      float s = 0.f;
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) s += (v[u][q].x + v[u][q].y) + (v[u][q].z + v[u][q].w);
+      const float mean = warp_allsum(s) * (1.0f / K);
+      float s2 = 0.f;
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const float a = v[u][q].x - mean, b = v[u][q].y - mean, c = v[u][q].z - mean, d = v[u][q].w - mean;
+        s2 = fmaf(a, a, s2);
+        s2 = fmaf(b, b, s2);
+        s2 = fmaf(c, c, s2);
+        s2 = fmaf(d, d, s2);
+      }
+      const float rstd = rsqrtf(warp_allsum(s2) * (1.0f / K) + p.eps);
+      uint2* dst = reinterpret_cast<uint2*>(p.out + static_cast<size_t>(row) * K);
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        float2 lo = make_float2((v[u][q].x - mean) * rstd, (v[u][q].y - mean) * rstd);
+        float2 hi = make_float2((v[u][q].z - mean) * rstd, (v[u][q].w - mean) * rstd);
+        if (affine) {
+          lo = make_float2(fmaf(lo.x, gg[q].x, bb[q].x), fmaf(lo.y, gg[q].y, bb[q].y));
+          hi = make_float2(fmaf(hi.x, gg[q].z, bb[q].z), fmaf(hi.y, gg[q].w, bb[q].w));
+        }
+        dst[lane + 32 * q] = make_uint2(pack_half2(lo.x, lo.y), pack_half2(hi.x, hi.y));
+      }
+    }
   }
+  griddep_trigger();
 }
 
+}  // namespace lnr
 }  // namespace tmu

@@ -18,7 +18,7 @@
 #include "k3w_emit.cuh"
 #include "k4_transition.cuh"
 #include "k5_disto.cuh"
-#include "k6_ln_gemm.cuh"
+#include "k6_gemm.cuh"
 #include "tmu.h"
 
 using namespace tmu;
@@ -139,7 +139,7 @@ int current_device(Dev& d, unsigned long long attr_bit, const void* kernel, int 
     g_num_sms[d.id] = n;
   }
   d.sms = g_num_sms[d.id];
-  if (!(g_attr_done[d.id] & attr_bit)) {
+  if (attr_bit != 0 && !(g_attr_done[d.id] & attr_bit)) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     g_attr_done[d.id] |= attr_bit;
@@ -582,11 +582,39 @@ int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel");
 }
 
-// K4 in row mode (the diffusion pair conditioning's transitions): zin fp16 (MODE kModeRows16) or
-// fp32 (kModeRows32) rows, zout fp32 rows, SwiGLU.
-template <int CZ, int MODE>
-int launch_k4_rows(const void* zin, float* zout, const tmu_cond_transition_weights* w, int B, int L, int hidden,
-                   unsigned long long bit, DeviceStatus* status, cudaStream_t stream) {
+// Row LayerNorm pass: h = fp16(LN(rows)) [rows, K].
+template <int K, int SRC>
+int launch_lnr(const void* x1, const void* x2, int ld1, int ld2, const RowTerms* terms, const float* g,
+               const float* b, __half* out, long long rows, cudaStream_t stream) {
+  void (*kern)(lnr::Params) = lnr::ln_rows_kernel<K, SRC>;
+  Dev dev;
+  int st = current_device(dev, 0, reinterpret_cast<const void*>(kern), 0);
+  if (st) return st;
+  lnr::Params p;
+  memset(&p, 0, sizeof(p));
+  p.x1 = x1;
+  p.x2 = x2;
+  p.ld1 = ld1;
+  p.ld2 = ld2;
+  if (terms) p.terms = *terms;
+  p.g = g;
+  p.b = b;
+  p.out = out;
+  p.rows = rows;
+  p.eps = 1e-5f;
+  constexpr int rows_per_cta = (lnr::kThreads / 32) * (K <= 256 ? 4 : 2);
+  const long long need = (rows + rows_per_cta - 1) / rows_per_cta;
+  const int grid = static_cast<int>(std::min<long long>(need, 8LL * dev.sms));
+  cudaError_t e = launch_pdl(kern, grid, lnr::kThreads, 0, stream, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch ln_rows_kernel");
+}
+
+// K4 in h mode: h = fp16(LN(z)) [B, L, L, CZ] by TMA, t = fp16(ffn) out, SwiGLU.
+template <int CZ>
+int launch_k4_h(const __half* h, __half* tout, const tmu_cond_transition_weights* w, int B, int L, int hidden,
+                unsigned long long bit, DeviceStatus* status, cudaStream_t stream) {
+  constexpr int MODE = k4::kModeH;
   void (*kern)(k4::Params) = k4::transition_kernel<CZ, true, MODE>;
   constexpr int smem = k4::Cfg<CZ, MODE>::SMEM_BYTES;
   Dev dev;
@@ -596,6 +624,12 @@ int launch_k4_rows(const void* zin, float* zout, const tmu_cond_transition_weigh
   memset(&p, 0, sizeof(p));
   int ih = 1, jw = 128;
   choose_tile(L, L, ih, jw, k4::TILE);
+  {
+    const uint64_t dims[4] = {CZ, (uint64_t)L, (uint64_t)L, (uint64_t)B};
+    const uint64_t str[3] = {2ull * CZ, 2ull * CZ * L, 2ull * CZ * L * L};
+    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    if ((st = encode_map(&p.tm_z, h, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
   {
     const uint64_t dims[2] = {CZ, (uint64_t)(2 * hidden)};
     const uint64_t str[1] = {2 * CZ};
@@ -608,10 +642,7 @@ int launch_k4_rows(const void* zin, float* zout, const tmu_cond_transition_weigh
     const uint32_t box[2] = {64, 128};
     if ((st = encode_map(&p.tm_w3, w->w3, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
-  p.zin = zin;
-  p.zout = zout;
-  p.ln_g32 = w->ln_w;
-  p.ln_b32 = w->ln_b;
+  p.tout = tout;
   p.hidden = hidden;
   p.nchunk = hidden / k4::CHUNK;
   p.L = L;
@@ -625,35 +656,33 @@ int launch_k4_rows(const void* zin, float* zout, const tmu_cond_transition_weigh
   const int grid = std::min(p.num_tiles, dev.sms);
   cudaError_t e = launch_pdl(kern, grid, k4::kThreads, smem, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
-  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel (rows)");
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel (h)");
 }
 
-// K6: D = fp16(LN(rows)) @ W^T, W fp16 [n, K]; epilogue per EPI.
-template <int K, int SRC, int EPI>
-int launch_k6(const void* x1, const void* x2, int ld1, int ld2, const float* g, const float* b, const void* w,
-              int n, void* out, const void* bias, int heads, int B, int L, unsigned long long bit,
-              DeviceStatus* status, cudaStream_t stream) {
-  void (*kern)(k6::Params) = k6::ln_gemm_kernel<K, SRC, EPI>;
-  constexpr int smem = k6::Cfg<K>::SMEM_BYTES;
+// K6 with the A operand by TMA: D = h @ W^T, h [B, L, L, K] fp16, W fp16 [n, K].
+template <int K, int EPI>
+int launch_k6g(const __half* h, const void* w, int n, void* out, const void* bias, int heads, int B, int L,
+               unsigned long long bit, DeviceStatus* status, cudaStream_t stream) {
+  void (*kern)(k6::Params) = k6::gemm_kernel<K, EPI>;
   Dev dev;
-  int st = current_device(dev, bit, reinterpret_cast<const void*>(kern), smem);
+  int st = current_device(dev, bit, reinterpret_cast<const void*>(kern), k6::SMEM_BYTES);
   if (st) return st;
   k6::Params p;
   memset(&p, 0, sizeof(p));
+  int ih = 1, jw = 128;
+  choose_tile(L, L, ih, jw, k6::TILE);
   {
     const uint64_t dims[2] = {K, (uint64_t)n};
     const uint64_t str[1] = {2 * K};
     const uint32_t box[2] = {64, (uint32_t)n};
     if ((st = encode_map(&p.tm_w, w, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
-  int ih = 1, jw = 128;
-  choose_tile(L, L, ih, jw, k6::TILE);
-  p.x1 = x1;
-  p.x2 = x2;
-  p.ld1 = ld1;
-  p.ld2 = ld2;
-  p.ln_g = g;
-  p.ln_b = b;
+  {
+    const uint64_t dims[4] = {K, (uint64_t)L, (uint64_t)L, (uint64_t)B};
+    const uint64_t str[3] = {2ull * K, 2ull * K * L, 2ull * K * L * L};
+    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    if ((st = encode_map(&p.tm_a, h, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+  }
   p.out = out;
   p.bias = static_cast<const __half*>(bias);
   p.n = n;
@@ -665,13 +694,12 @@ int launch_k6(const void* x1, const void* x2, int ld1, int ld2, const float* g, 
   p.tiles_i = (L + ih - 1) / ih;
   p.tiles_j = (L + jw - 1) / jw;
   p.num_tiles = B * p.tiles_i * p.tiles_j;
-  p.eps = 1e-5f;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
   const int grid = std::min(p.num_tiles, dev.sms);
-  cudaError_t e = launch_pdl(kern, grid, k6::kThreads, smem, stream, p);
+  cudaError_t e = launch_pdl(kern, grid, k6::kThreads, k6::SMEM_BYTES, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
-  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch ln_gemm_kernel");
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch gemm_kernel");
 }
 
 template <int CZ>
@@ -1016,11 +1044,13 @@ int tmu_disto_expected(const void* z, const void* w, const float* bias, const fl
                     : launch_k5<256>(z, w, bias, centres, out, B, L, st, s);
 }
 
-size_t tmu_pair_cond_workspace_bytes(int B, int L, int c_pair) {
-  if (B < 1 || L < 1 || c_pair < 1) return 0;
-  const size_t cells = static_cast<size_t>(B) * L * L;
-  const size_t z16 = (cells * c_pair * 2 + 255) / 256 * 256;
-  return z16 + cells * c_pair * 4;
+namespace {
+size_t pc_term_bytes(int B, int L, int c) { return (static_cast<size_t>(B) * L * L * c * 2 + 255) / 256 * 256; }
+}  // namespace
+
+size_t tmu_pair_cond_workspace_bytes(int B, int L, int c_in, int c_pair, int n_transitions) {
+  if (B < 1 || L < 1 || c_in < 1 || c_pair < 1 || n_transitions < 0) return 0;
+  return pc_term_bytes(B, L, c_pair) * (n_transitions + 1) + pc_term_bytes(B, L, std::max(c_in, c_pair));
 }
 
 int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_cond_weights* w, int B, int L,
@@ -1034,12 +1064,14 @@ int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_con
   if (w == nullptr || !w->ln_w || !w->ln_b || !w->proj || !w->bias_w || !w->bias_b ||
       w->n_transitions < 0 || (w->n_transitions > 0 && !w->transitions))
     return fail(TMU_ERR_INVALID_ARGUMENT, "pair conditioning weights missing");
+  if (w->n_transitions > kMaxTerms - 1) return fail(TMU_ERR_UNSUPPORTED, "at most 3 transitions");
   if (w->n_transitions > 0 && (hidden < 64 || hidden > 4096 || hidden % 64))
     return fail(TMU_ERR_UNSUPPORTED, "hidden must be a multiple of 64 in [64, 4096]");
   if (n_bias < 16 || n_bias > 256 || n_bias % 16 || heads < 1 || n_bias % heads)
     return fail(TMU_ERR_UNSUPPORTED, "n_bias must be a multiple of 16 in [16, 256], divisible by heads");
   if (!z_trunk || !rel_pos || !out || !workspace || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
-  if (workspace_bytes < tmu_pair_cond_workspace_bytes(B, L, c_pair))
+  const int c_in = c_trunk + c_rel;
+  if (workspace_bytes < tmu_pair_cond_workspace_bytes(B, L, c_in, c_pair, w->n_transitions))
     return fail(TMU_ERR_INVALID_ARGUMENT, "workspace too small");
   const void* al[] = {z_trunk, rel_pos, out, workspace, w->ln_w, w->ln_b, w->proj, w->bias_w};
   for (const void* q : al)
@@ -1052,41 +1084,43 @@ int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_con
   }
   DeviceStatus* st = static_cast<DeviceStatus*>(status);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t cells = static_cast<size_t>(B) * L * L;
-  __half* z16 = static_cast<__half*>(workspace);
-  float* z32 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + (cells * c_pair * 2 + 255) / 256 * 256);
-  // Stage A: z0 = fp16(fp16(LN(concat)) @ proj^T)
-  int r = c_trunk == 256
-              ? launch_k6<512, kRowCat32, k6::kEpiStore16>(z_trunk, rel_pos, c_trunk, c_rel, w->ln_w, w->ln_b,
-                                                           w->proj, c_pair, z16, nullptr, 1, B, L, 1ull << 32, st, s)
-              : launch_k6<256, kRowCat32, k6::kEpiStore16>(z_trunk, rel_pos, c_trunk, c_rel, w->ln_w, w->ln_b,
-                                                           w->proj, c_pair, z16, nullptr, 1, B, L, 1ull << 33, st, s);
+  const long long cells = static_cast<long long>(B) * L * L;
+  // Workspace: the fp32 residual stream as its fp16 terms (z0, then each transition's t_k), then
+  // one h buffer for the LayerNorm pass in front of each GEMM kernel.
+  const size_t term = pc_term_bytes(B, L, c_pair);
+  RowTerms terms;
+  memset(&terms, 0, sizeof(terms));
+  terms.ld = c_pair;
+  for (int k = 0; k <= w->n_transitions; ++k)
+    terms.src[k] = reinterpret_cast<const __half*>(static_cast<uint8_t*>(workspace) + k * term);
+  __half* z0 = static_cast<__half*>(workspace);
+  __half* h = reinterpret_cast<__half*>(static_cast<uint8_t*>(workspace) + (w->n_transitions + 1) * term);
+  const bool wide = c_pair == 256;
+  // Stage A: h = fp16(LN(concat)), z0 = fp16(h @ proj^T)
+  int r = c_in == 512 ? launch_lnr<512, kRowCat32>(z_trunk, rel_pos, c_trunk, c_rel, nullptr, w->ln_w, w->ln_b, h, cells, s)
+                      : launch_lnr<256, kRowCat32>(z_trunk, rel_pos, c_trunk, c_rel, nullptr, w->ln_w, w->ln_b, h, cells, s);
   if (r) return r;
-  // Transitions: z0 (fp16) -> z (fp32), then z in place
-  for (int t = 0; t < w->n_transitions && r == TMU_OK; ++t) {
-    const tmu_cond_transition_weights* tw = &w->transitions[t];
-    if (c_pair == 256)
-      r = t == 0 ? launch_k4_rows<256, k4::kModeRows16>(z16, z32, tw, B, L, hidden, 1ull << 34, st, s)
-                 : launch_k4_rows<256, k4::kModeRows32>(z32, z32, tw, B, L, hidden, 1ull << 35, st, s);
-    else
-      r = t == 0 ? launch_k4_rows<128, k4::kModeRows16>(z16, z32, tw, B, L, hidden, 1ull << 36, st, s)
-                 : launch_k4_rows<128, k4::kModeRows32>(z32, z32, tw, B, L, hidden, 1ull << 37, st, s);
+  r = c_in == 512 ? launch_k6g<512, k6::kEpiStore16>(h, w->proj, c_pair, z0, nullptr, 1, B, L, 1ull << 32, st, s)
+                  : launch_k6g<256, k6::kEpiStore16>(h, w->proj, c_pair, z0, nullptr, 1, B, L, 1ull << 33, st, s);
+  // Transition k: h = fp16(LN(z0 + t_1 + .. + t_{k-1})), t_k = fp16(ffn(h))
+  for (int k = 1; k <= w->n_transitions && r == TMU_OK; ++k) {
+    const tmu_cond_transition_weights* tw = &w->transitions[k - 1];
+    terms.n = k;
+    r = wide ? launch_lnr<256, kRowTerms16>(nullptr, nullptr, 0, 0, &terms, tw->ln_w, tw->ln_b, h, cells, s)
+             : launch_lnr<128, kRowTerms16>(nullptr, nullptr, 0, 0, &terms, tw->ln_w, tw->ln_b, h, cells, s);
+    if (r) break;
+    __half* tk = const_cast<__half*>(terms.src[k]);
+    r = wide ? launch_k4_h<256>(h, tk, tw, B, L, hidden, 1ull << 34, st, s)
+             : launch_k4_h<128>(h, tk, tw, B, L, hidden, 1ull << 35, st, s);
   }
   if (r) return r;
-  // Stage D: bias = fp16(fp16(fp16(LN(z)) @ bias_w^T) + bias_b), transposed store
-  const bool f32 = w->n_transitions > 0;
-  const void* zsrc = f32 ? static_cast<const void*>(z32) : static_cast<const void*>(z16);
-  if (c_pair == 256)
-    r = f32 ? launch_k6<256, kRowF32, k6::kEpiBiasT>(zsrc, nullptr, 256, 0, nullptr, nullptr, w->bias_w, n_bias, out,
-                                                     w->bias_b, heads, B, L, 1ull << 38, st, s)
-            : launch_k6<256, kRowF16, k6::kEpiBiasT>(zsrc, nullptr, 256, 0, nullptr, nullptr, w->bias_w, n_bias, out,
-                                                     w->bias_b, heads, B, L, 1ull << 39, st, s);
-  else
-    r = f32 ? launch_k6<128, kRowF32, k6::kEpiBiasT>(zsrc, nullptr, 128, 0, nullptr, nullptr, w->bias_w, n_bias, out,
-                                                     w->bias_b, heads, B, L, 1ull << 40, st, s)
-            : launch_k6<128, kRowF16, k6::kEpiBiasT>(zsrc, nullptr, 128, 0, nullptr, nullptr, w->bias_w, n_bias, out,
-                                                     w->bias_b, heads, B, L, 1ull << 41, st, s);
-  return r;
+  // Stage D: h = fp16(LN(z)) without affine, bias = fp16(fp16(h @ bias_w^T) + bias_b), transposed store
+  terms.n = w->n_transitions + 1;
+  r = wide ? launch_lnr<256, kRowTerms16>(nullptr, nullptr, 0, 0, &terms, nullptr, nullptr, h, cells, s)
+           : launch_lnr<128, kRowTerms16>(nullptr, nullptr, 0, 0, &terms, nullptr, nullptr, h, cells, s);
+  if (r) return r;
+  return wide ? launch_k6g<256, k6::kEpiBiasT>(h, w->bias_w, n_bias, out, w->bias_b, heads, B, L, 1ull << 36, st, s)
+              : launch_k6g<128, k6::kEpiBiasT>(h, w->bias_w, n_bias, out, w->bias_b, heads, B, L, 1ull << 37, st, s);
 }
 
 int tmu_ipc_export(const void* ptr, void* handle, unsigned long long* offset) {

@@ -1,6 +1,9 @@
 """Per-fold pair conditioning of the diffusion head on B200: ``pair_biases`` as one call of
-``tmu_pair_cond`` (K6 LayerNorm + projection, K4 in row mode for the transitions, K6 again for
-the folded pair-bias GEMM).
+``tmu_pair_cond`` (LayerNorm pass + K6 projection, LayerNorm pass + K4 for each transition,
+LayerNorm pass + K6 for the folded pair-bias GEMM).
+
+Each GEMM kernel reads its LayerNorm output from a row LayerNorm pass (many warps per SM,
+coalesced), and the fp32 residual stream between the transitions is kept as its fp16 terms.
 
 Reference (``src/esmfold2_mlx/``): ``mlx_diffusion16.pair_biases`` (``mlx_diffusion16.py:81-87``)
 in the pair16 precision of the adopted ``var_mlx_diffusion16`` stack, weights as
@@ -74,8 +77,10 @@ class PairCondWeights:
         return self._struct
 
 
-def workspace_bytes(B: int, L: int, c_pair: int) -> int:
-    return int(_lib.load().tmu_pair_cond_workspace_bytes(B, L, c_pair))
+def workspace_bytes(B: int, L: int, c_in: int, c_pair: int, n_transitions: int) -> int:
+    """Scratch for z0 and each transition's fp16 output (the fp32 residual stream's terms) and
+    the LayerNorm output buffer."""
+    return int(_lib.load().tmu_pair_cond_workspace_bytes(B, L, c_in, c_pair, n_transitions))
 
 
 def pair_biases(w: PairCondWeights, z_trunk: torch.Tensor, rel_pos: torch.Tensor, out: torch.Tensor | None = None,
@@ -94,7 +99,7 @@ def pair_biases(w: PairCondWeights, z_trunk: torch.Tensor, rel_pos: torch.Tensor
     dev = z_trunk.device
     nb = w.n_bias // w.heads
     out = torch.empty(nb, B, w.heads, L, L, dtype=torch.float16, device=dev) if out is None else out
-    need = workspace_bytes(B, L, w.c_pair)
+    need = workspace_bytes(B, L, w.c_in, w.c_pair, len(w.tensors["transitions"]))
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, dtype=torch.uint8, device=dev)
     status = new_status(dev) if status is None else status

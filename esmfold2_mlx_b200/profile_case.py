@@ -72,7 +72,7 @@ def main():
         pw = pair_cond.PairCondWeights.from_head(DiffusionHead(), dev)
         zt = pair_tensor(B, L, 256, 1).to(dev) * 20.0
         rp = pair_tensor(B, L, 256, 2).to(dev)
-        ws = torch.empty(pair_cond.workspace_bytes(B, L, pw.c_pair), dtype=torch.uint8, device=dev)
+        ws = torch.empty(pair_cond.workspace_bytes(B, L, pw.c_in, pw.c_pair, 2), dtype=torch.uint8, device=dev)
         pout = torch.empty(pw.n_bias // pw.heads, B, pw.heads, L, L, dtype=torch.float16, device=dev)
         stages["pc"] = lambda: pair_cond.pair_biases(pw, zt, rp, out=pout, workspace=ws, status=status)
     fn = stages[args.stage]

@@ -231,11 +231,15 @@ typedef struct tmu_pair_cond_weights {
   const void* bias_b; /* fp16 [n_bias] */
 } tmu_pair_cond_weights;
 
-/* Bytes of scratch tmu_pair_cond needs: z fp16 and z fp32, [B, L, L, c_pair] each. */
-size_t tmu_pair_cond_workspace_bytes(int B, int L, int c_pair);
+/* Bytes of scratch tmu_pair_cond needs: the fp32 residual stream kept as its fp16 terms (z0 and
+ * each transition's output: n_transitions + 1 tensors [B, L, L, c_pair]), then one fp16 buffer
+ * [B, L, L, max(c_in, c_pair)] for the LayerNorm output each GEMM kernel reads; every tensor
+ * starts on a 256-byte boundary.  c_in = c_trunk + c_rel. */
+size_t tmu_pair_cond_workspace_bytes(int B, int L, int c_in, int c_pair, int n_transitions);
 
-/* Shapes: c_trunk == c_rel, c_trunk + c_rel in {256, 512}; c_pair in {128, 256}; hidden a
- * multiple of 64 in [64, 4096]; n_bias a multiple of 16 in [16, 256], divisible by heads. */
+/* Shapes: c_trunk == c_rel, c_trunk + c_rel in {256, 512}; c_pair in {128, 256}; at most 3
+ * transitions; hidden a multiple of 64 in [64, 4096]; n_bias a multiple of 16 in [16, 256],
+ * divisible by heads. */
 int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_cond_weights* w, int B, int L,
                   int c_trunk, int c_rel, int c_pair, int hidden, int n_bias, int heads, void* out,
                   void* workspace, size_t workspace_bytes, void* status, void* stream);

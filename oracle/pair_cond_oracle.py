@@ -68,12 +68,17 @@ def stage_project(p: dict, z_trunk, rel_pos, acc=torch.float32) -> torch.Tensor:
     return r16(_mm(r16(layer_norm(x, p["ln_w"], p["ln_b"], LN_EPS)), p["proj"], acc))
 
 
-def stage_transition(t: dict, z: torch.Tensor, acc=torch.float32) -> torch.Tensor:
-    """z + r16(s @ out), s the fp16 SwiGLU of r16(LN(z)) (mlx_diffusion16.py:64-67,83-84)."""
+def stage_transition_delta(t: dict, z: torch.Tensor, acc=torch.float32) -> torch.Tensor:
+    """r16(s @ out), s the fp16 SwiGLU of r16(LN(z)) (mlx_diffusion16.py:64-67)."""
     hh = r16(layer_norm(z, t["ln_w"], t["ln_b"], LN_EPS))
     xa, xb = r16(_mm(hh, t["a"], acc)), r16(_mm(hh, t["b"], acc))
     s = r16(r16(xa * r16(sigmoid(xa))) * xb)
-    return z + r16(_mm(s, t["out"], acc))
+    return r16(_mm(s, t["out"], acc))
+
+
+def stage_transition(t: dict, z: torch.Tensor, acc=torch.float32) -> torch.Tensor:
+    """z + r16(s @ out): the fp32 residual update (mlx_diffusion16.py:83-84)."""
+    return z + stage_transition_delta(t, z, acc)
 
 
 def stage_bias(p: dict, z: torch.Tensor, acc=torch.float32) -> torch.Tensor:

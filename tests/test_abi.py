@@ -102,5 +102,6 @@ def test_pair_cond_argument_checks_need_no_gpu(lib):
     a = list(args(256, 256, 256, 512, 192, 16))
     a[2] = ctypes.byref(pw)
     assert lib.tmu_pair_cond(*a) == 1  # empty weight struct
-    assert lib.tmu_pair_cond_workspace_bytes(1, 16, 256) == 16 * 16 * 256 * 6
-    assert lib.tmu_pair_cond_workspace_bytes(0, 16, 256) == 0
+    assert lib.tmu_pair_cond_workspace_bytes(1, 16, 512, 256, 2) == 3 * 16 * 16 * 256 * 2 + 16 * 16 * 512 * 2
+    assert lib.tmu_pair_cond_workspace_bytes(1, 5, 256, 128, 0) == 6400 + 12800  # terms rounded up to 256 B
+    assert lib.tmu_pair_cond_workspace_bytes(0, 16, 512, 256, 2) == 0

@@ -2,7 +2,8 @@
 against the CPU oracle (``oracle/pair_cond_oracle.py``, mlx_diffusion16.py:81-87 in pair16).
 
 Stage by stage, each GPU stage is compared with the oracle's stage fed the GPU's own input
-(the workspace holds z0 fp16 and the final fp32 z): fp32 summation order and the hardware
+(the workspace holds the fp32 residual stream as its fp16 terms: z0 and each transition's
+output): fp32 summation order and the hardware
 sigmoid may flip a rare fp16 rounding, so a small fraction of elements differ, by at most one
 fp16 ulp at the tensor's scale (measured: 0.2-4 % of elements, 0.5-1 ulp; near-zero outputs of
 a cancelling dot product move by that absolute amount, many of their own ulps).  End to end the fp32 residual stream carries every such flip into the
@@ -49,7 +50,7 @@ def _frac(a, b) -> float:
 
 @pytest.mark.parametrize("B,L,c_side,c_pair,hidden,n_trans,n_blocks,heads", [
     (1, 37, 256, 256, 512, 2, 12, 16),   # the default stand-in shape, ragged L
-    (1, 37, 256, 256, 512, 1, 12, 16),   # one transition: its output is visible in the workspace
+    (1, 37, 256, 256, 512, 1, 12, 16),   # one transition
     (2, 50, 256, 256, 512, 2, 12, 16),   # batched folds
     (1, 130, 256, 256, 512, 1, 12, 16),  # L > 128: several tiles per row
     (1, 64, 128, 128, 256, 1, 4, 8),     # narrow variant
@@ -59,7 +60,7 @@ def test_pair_biases_match_oracle(B, L, c_side, c_pair, hidden, n_trans, n_block
     head, zt, rp, ref = _case(B, L, c_side, c_pair, hidden, n_trans, n_blocks, heads, seed=L + hidden)
     p = pco.pair_cond_params(head)
     w = pair_cond.PairCondWeights.from_head(head, DEV)
-    ws = torch.empty(pair_cond.workspace_bytes(B, L, c_pair), dtype=torch.uint8, device=DEV)
+    ws = torch.empty(pair_cond.workspace_bytes(B, L, 2 * c_side, c_pair, n_trans), dtype=torch.uint8, device=DEV)
     st = new_status(DEV)
     out = pair_cond.pair_biases(w, zt.to(DEV), rp.to(DEV), workspace=ws, status=st)
     torch.cuda.synchronize()
@@ -68,24 +69,24 @@ def test_pair_biases_match_oracle(B, L, c_side, c_pair, hidden, n_trans, n_block
     got = out.float().cpu()
     assert bool(torch.isfinite(got).all())
 
-    cells = B * L * L
-    off32 = (cells * c_pair * 2 + 255) // 256 * 256
-    z0 = ws[:cells * c_pair * 2].view(torch.float16).view(B, L, L, c_pair).float().cpu()
-    z32 = ws[off32:off32 + cells * c_pair * 4].view(torch.float32).view(B, L, L, c_pair).cpu()
+    # the workspace holds the fp32 residual stream's fp16 terms: z0, then each transition's t_k
+    term = (B * L * L * c_pair * 2 + 255) // 256 * 256
+    terms = [ws[k * term:k * term + B * L * L * c_pair * 2].view(torch.float16).view(B, L, L, c_pair).float().cpu()
+             for k in range(n_trans + 1)]
 
     # stage A: LN(concat) -> proj, fp16
     z0_ref = pco.stage_project(p, zt, rp)
-    assert float((z0 - z0_ref).abs().max()) <= _ulp16(float(z0_ref.abs().max()))
-    assert _frac(z0, z0_ref) < 0.01
-    # one transition from the GPU's own z0: z1 = z0 + r16(t); a flip of r16(t) is one ulp of t
-    if n_trans == 1:
-        z1_ref = pco.stage_transition(p["transitions"][0], z0)
-        t_scale = float((z1_ref - z0).abs().max())
-        tol = 1.01 * _ulp16(t_scale) + float(z1_ref.abs().max()) * 2.0**-23  # + the fp32 add's own rounding
-        assert float((z32 - z1_ref).abs().max()) <= tol
-        assert _frac(z32, z1_ref) < 0.06
+    assert float((terms[0] - z0_ref).abs().max()) <= _ulp16(float(z0_ref.abs().max()))
+    assert _frac(terms[0], z0_ref) < 0.01
+    # each transition from the GPU's own z = fl32(z0 + t1 + ..): t_k = r16(s @ out)
+    z = terms[0]
+    for k in range(1, n_trans + 1):
+        t_ref = pco.stage_transition_delta(p["transitions"][k - 1], z)
+        assert float((terms[k] - t_ref).abs().max()) <= _ulp16(float(t_ref.abs().max()))
+        assert _frac(terms[k], t_ref) < 0.06
+        z = z + terms[k]
     # the bias GEMM from the GPU's own final z
-    bias_ref = pco.stage_bias(p, z32 if n_trans else z0)
+    bias_ref = pco.stage_bias(p, z)
     assert float((got - bias_ref).abs().max()) <= _ulp16(float(bias_ref.abs().max()))
     assert _frac(got, bias_ref) < 0.01
 
@@ -99,7 +100,7 @@ def test_pair_biases_match_oracle(B, L, c_side, c_pair, hidden, n_trans, n_block
 def test_pair_biases_reuse_workspace_and_output():
     head, zt, rp, ref = _case(1, 48, 256, 256, 512, 2, 12, 16, seed=9)
     w = pair_cond.PairCondWeights.from_head(head, DEV)
-    ws = torch.empty(pair_cond.workspace_bytes(1, 48, 256), dtype=torch.uint8, device=DEV)
+    ws = torch.empty(pair_cond.workspace_bytes(1, 48, 512, 256, 2), dtype=torch.uint8, device=DEV)
     out = torch.empty(12, 1, 16, 48, 48, dtype=torch.float16, device=DEV)
     a = pair_cond.pair_biases(w, zt.to(DEV), rp.to(DEV), out=out, workspace=ws).clone()
     b = pair_cond.pair_biases(w, zt.to(DEV), rp.to(DEV), out=out, workspace=ws)
