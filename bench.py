@@ -147,7 +147,8 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-WORKLOADS = ("c2", "c1", "c4", "L2048", "c5", "c2w", "L2048w")
+WORKLOADS = ("c2", "c1", "c4", "L2048", "c5", "c2w", "L2048w", "pc", "pc476")
+PAIR_COND_L = {"pc": 238, "pc476": 476}  # diffusion pair conditioning, one fold of L residues
 SHARDED_WORKLOADS = ("c5",)
 
 
@@ -197,6 +198,9 @@ def run_reference(args, ws, rank, local):
         return
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
+    if args.workload in PAIR_COND_L:
+        _reference_pair_cond(args, threads)
+        return
     cfg, trunk, biases, _, z, mask = _workload(0, None, args.workload)
     L = cfg.L
     from oracle import trimul_oracle as orc
@@ -222,6 +226,33 @@ def run_reference(args, ws, rank, local):
                                    "oracle/trimul_oracle.py on torch CPU (fp32 math, fp16 rounding points)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    print(json.dumps(line), flush=True)
+
+
+def _reference_pair_cond(args, threads):
+    """Reference arm of the pair-conditioning workloads: the oracle port of pair_biases
+    (mlx_diffusion16.py:81-87) on the host cores, one fold per step."""
+    from esmfold2_mlx_b200.synthetic import DiffusionHead, pair_tensor
+    from oracle import pair_cond_oracle as pco
+
+    L = PAIR_COND_L[args.workload]
+    p = pco.pair_cond_params(DiffusionHead(seed=11))
+    zt, rp = pair_tensor(1, L, 256, 12) * 20.0, pair_tensor(1, L, 256, 13)
+    for _ in range(min(args.warmup, 1)):
+        pco.pair_biases_fp16(p, zt, rp)
+    steps = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        pco.pair_biases_fp16(p, zt, rp)
+    el = time.perf_counter() - t0
+    value = L * L * steps / el
+    line = {"impl": "reference", "metric": "pair_cond_cells_per_s", "value": value, "unit": "pair-cells/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": f"{args.workload}_pair_conditioning_L{L}", "B": 1, "L": L},
+            "cpu_baseline": {"value": value, "unit": "pair-cells/s", "cores": threads, "kind": "port",
+                             "sample": f"{steps} x pair_biases of one fold at L={L}; oracle/pair_cond_oracle.py"},
+            "e2e": {"value": value, "unit": "pair-cells/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -602,6 +633,123 @@ def run_b200(args, ws, rank, local):
     del g_step, g_kern
 
 
+def run_pair_cond(args, ws, rank, local):
+    """The diffusion head's per-fold pair conditioning (``tmu_pair_cond``: LayerNorm pass + K6,
+    2 x (LayerNorm pass + K4 in h mode), LayerNorm pass + K6) on the stand-in head's default shape
+    (c_trunk = c_rel = c_pair = 256, hidden 512, 12 blocks x 16 heads).  One step = one fold's
+    call; N > 1 runs independent replicas (weak scaling)."""
+    from esmfold2_mlx_b200 import _lib, ops, pair_cond
+    from esmfold2_mlx_b200.synthetic import DiffusionHead, pair_tensor
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
+    L, B = PAIR_COND_L[args.workload], 1
+    head = DiffusionHead(seed=11)
+    pw = pair_cond.PairCondWeights.from_head(head, device)
+    zt_h = (pair_tensor(B, L, 256, 12 + rank) * 20.0).contiguous()
+    rp_h = pair_tensor(B, L, 256, 13 + rank).contiguous()
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    zt, rp = zt_h.to(device), rp_h.to(device)
+    wbuf = torch.empty(pair_cond.workspace_bytes(B, L, 512, 256, 2), dtype=torch.uint8, device=device)
+    out = torch.empty(pw.n_bias // pw.heads, B, pw.heads, L, L, dtype=torch.float16, device=device)
+    status = ops.new_status(device)
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
+
+    def step():
+        pair_cond.pair_biases(pw, zt, rp, out=out, workspace=wbuf, status=status)
+
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    for _ in range(max(3, args.warmup)):
+        flush.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    sampler = ClockSampler(local)
+    sampler.start()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    _barrier(ws)
+    for e0, e1 in evs:
+        flush.zero_()
+        e0.record()
+        g.replay()
+        e1.record()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    clocks = sampler.stop()
+    ms_per_step = _max_over_ranks(sum(e0.elapsed_time(e1) for e0, e1 in evs), ws, device) / args.steps
+    code, site = ops.read_status(status)
+    if code != 0:
+        raise RuntimeError(f"device status {code} at site {site:#x}")
+    cells = B * L * L
+    value = ws * cells / (ms_per_step * 1e-3)
+    # algorithmic work per pair cell: proj 2*512*256, 2 transitions x (2*256*1024 + 2*512*256), bias 2*256*192
+    flops_cell = 2 * 512 * 256 + 2 * (2 * 256 * 1024 + 2 * 512 * 256) + 2 * 256 * 192
+    bytes_cell = 2 * 256 * 4 + pw.n_bias * 2  # fp32 inputs in, fp16 biases out
+    hbm, tflops, peak_kind = _peaks()
+    ach = flops_cell * cells / (ms_per_step * 1e-3) / 1e12
+    roofline = {"kernel": "tmu_pair_cond (8 launches: 4 LayerNorm passes, 2 x K6, 2 x K4 h mode)",
+                "bound": "tensor", "achieved": round(ach, 2), "peak": tflops, "unit": "TFLOP/s",
+                "frac": round(ach / tflops, 4), "traffic": None,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)" if peak_kind == "measured" else "fallback",
+                "algorithmic_per_cell": {"flops": flops_cell, "bytes": bytes_cell},
+                "note": "whole-call roofline: per-kernel shares in profiles/pair_cond_launches_L1024.md"}
+    # end to end through the public API: fp32 inputs from pinned host memory, biases back to host
+    zp, rpp = zt_h.pin_memory(), rp_h.pin_memory()
+    outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    e2e_ms = 0.0
+    for i in range(args.steps + 2):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        zt.copy_(zp, non_blocking=True)
+        rp.copy_(rpp, non_blocking=True)
+        pair_cond.pair_biases(pw, zt, rp, out=out, workspace=wbuf, status=status)
+        outh.copy_(out, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        if i >= 2:
+            e2e_ms += e0.elapsed_time(e1)
+    e2e_ms = _max_over_ranks(e2e_ms, ws, device) / args.steps
+    e2e = {"value": ws * cells / (e2e_ms * 1e-3), "unit": "pair-cells/s",
+           "h2d_bytes_per_step": 2 * cells * 256 * 4, "d2h_bytes_per_step": out.numel() * 2,
+           "ms_per_step": round(e2e_ms, 4)}
+    cpu = None
+    if ws == 1 and not args.no_cpu_baseline:
+        from oracle import pair_cond_oracle as pco
+
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        p = pco.pair_cond_params(head)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            pco.pair_biases_fp16(p, zt_h, rp_h)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= min(args.cpu_seconds, 5.0):
+                break
+        cpu = {"value": n * cells / el, "unit": "pair-cells/s", "cores": threads, "kind": "port",
+               "sample": f"{n} x pair_biases of one fold at L={L} in {el:.1f} s; oracle/pair_cond_oracle.py on "
+                         "torch CPU (fp32 math, fp16 rounding points)"}
+    if rank == 0:
+        line = {"metric": "pair_cond_cells_per_s", "value": value, "unit": "pair-cells/s", "n_gpus": ws,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+                "config": {"workload": f"{args.workload}_pair_conditioning_L{L}", "B": B, "L": L, "c_trunk": 256,
+                           "c_rel": 256, "c_pair": 256, "hidden": 512, "transitions": 2, "bias_heads": "12 x 16",
+                           "l2": "flushed between steps (256 MiB write)", "parallelism": f"replicas x{ws}"},
+                "e2e": e2e, "gpu_launches": 8 * args.steps, "roofline": roofline, "cpu_baseline": cpu,
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    del g
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -615,7 +763,8 @@ def main():
                     help="c5: move b with an NCCL all-gather instead of copy-engine peer copies")
     ap.add_argument("--workload", choices=WORKLOADS, default="c2",
                     help="c2 (default: the metric's configuration), c1, c4 (64 folds x L=146), L2048, "
-                         "c5 (one L=3072 fold row-sharded over the N ranks), c2w / L2048w (c_z = c = 256)")
+                         "c5 (one L=3072 fold row-sharded over the N ranks), c2w / L2048w (c_z = c = 256), "
+                         "pc / pc476 (diffusion pair conditioning of one fold, L = 238 / 476)")
     args = ap.parse_args()
     ws, rank, local = _dist()
     if args.impl == "reference":
@@ -625,6 +774,8 @@ def main():
     try:
         if args.workload in SHARDED_WORKLOADS:
             run_sharded(args, ws, rank, local)
+        elif args.workload in PAIR_COND_L:
+            run_pair_cond(args, ws, rank, local)
         else:
             run_b200(args, ws, rank, local)
     finally:
