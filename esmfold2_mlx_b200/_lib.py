@@ -70,6 +70,12 @@ class TmuCondTransitionWeights(ctypes.Structure):
     _fields_ = [("ln_w", _vp), ("ln_b", _vp), ("w12", _vp), ("w3", _vp)]
 
 
+class TmuParcaeWeights(ctypes.Structure):
+    """Mirror of ``tmu_parcae_weights``."""
+
+    _fields_ = [("ln_w", _vp), ("ln_b", _vp), ("a", _vp), ("b_split", _vp)]
+
+
 class TmuPairCondWeights(ctypes.Structure):
     """Mirror of ``tmu_pair_cond_weights``."""
 
@@ -103,6 +109,8 @@ SIGNATURES = {
     "tmu_pair_cond_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "tmu_pair_cond": (_i, [_vp, _vp, ctypes.POINTER(TmuPairCondWeights), _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp,
                            _sz, _vp, _vp]),
+    "tmu_parcae_workspace_bytes": (_sz, [_i, _i, _i]),
+    "tmu_parcae_step": (_i, [_vp, _vp, _vp, ctypes.POINTER(TmuParcaeWeights), _vp, _i, _i, _i, _vp, _sz, _vp, _vp]),
     "tmu_ipc_export": (_i, [_vp, _vp, ctypes.POINTER(_ull)]),
     "tmu_ipc_import": (_i, [_vp, _ull, ctypes.POINTER(_vp)]),
     "tmu_ipc_close": (_i, [_vp]),

@@ -6,7 +6,12 @@
 //   stage D  bias = fp16(fp16(h @ bias_w^T) + bias_b), h = fp16(LN(z)) without affine, stored as
 //            [nb, B, H, L, L]
 // (bias_w / bias_b fold every token block's pair_norm affine into its pair_bias_proj:
-// mlx_diffusion.py:85-89).
+// mlx_diffusion.py:85-89), and the parcae step of the 6B loop (var_6b_mlx_loop.py:67-71, fp32):
+//   z' = a * z + LN(z_init + refined) @ B^T
+// as an fp32-accurate bf16 GEMM: LN's output and B are each split into three bf16 parts
+// (x = x0 + x1 + x2 to 24 bits) and the six products x_i B_j with i + j <= 2 are accumulated in
+// fp32 TMEM, smallest first (truncation error ~2^-24 relative).  The K steps run from a
+// schedule: step s multiplies A channels [a_coord[s], +64) by W columns [w_coord[s], +64).
 //
 // Tile = 128 positions (ih x jw block); TMEM lane = position, column = output channel.
 // CTA = 12 warps, one per SM, persistent:
@@ -37,15 +42,22 @@ constexpr int OFF_BAR = OFF_PAR + NMAX * 4 + NMAX * 8;
 constexpr int SMEM_BYTES = OFF_BAR + 256;
 static_assert(SMEM_BYTES <= 232448, "K6 shared memory exceeds the per-block limit");
 
-enum Epi : int { kEpiStore16 = 0, kEpiBiasT = 1 };
+enum Epi : int { kEpiStore16 = 0, kEpiBiasT = 1, kEpiAxpy = 2 };
+constexpr int kMaxSteps = 32;
 
 struct Params {
   CUtensorMap tm_w;       // W [N, K] fp16 (nn.Linear layout): box {64, N}, 128B swizzle
   CUtensorMap tm_a;       // h [B, L, L, K] fp16: box {64, jw, ih, 1}, 128B swizzle
-  void* out;              // kEpiStore16: fp16 [cells, N]; kEpiBiasT: fp16 [N / heads, B, heads, L, L]
+  void* out;              // kEpiStore16: fp16 [cells, N]; kEpiBiasT: fp16 [N / heads, B, heads, L, L];
+                          // kEpiAxpy: fp32 [cells, N]
   const __half* bias;     // [N] (kEpiBiasT)
+  const float* zres;      // kEpiAxpy: z fp32 [cells, N] (may alias out)
+  const float* avec;      // kEpiAxpy: a [N]
   int n;                  // output channels N
   int heads;              // kEpiBiasT: H
+  int nsteps;             // K steps of 64 (<= kMaxSteps)
+  short a_coord[kMaxSteps];
+  short w_coord[kMaxSteps];
   int B, L, ih, jw, tiles_i, tiles_j, num_tiles;
   DeviceStatus* status;
   unsigned long long timeout_ns;
@@ -63,9 +75,9 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
-template <int K, int EPI>
+template <int EPI, bool BF16 = false>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Params p) {
-  constexpr int KATOMS = K / 64;
+  const int nsteps = p.nsteps;
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x6ff;
@@ -106,6 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
   }
+  if (EPI == kEpiAxpy)
+    for (int c = threadIdx.x; c < p.n; c += blockDim.x) bias_s[c] = p.avec[c];
   if (EPI == kEpiBiasT) {
     // channel c = blk * H + hh lives in plane (blk * B + b) * H + hh of [nb, B, H, L, L]: the
     // b-independent part of its element offset, and its bias, once per CTA
@@ -136,11 +150,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       uint32_t r = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
-        for (int k = 0; k < KATOMS; ++k, ++r) {
+        for (int k = 0; k < nsteps; ++k, ++r) {
           const uint32_t s = r % NW, ph = (r / NW) & 1;
           if (!(ok = mbar_wait(&wempty[s], ph ^ 1, ctx, kSiteProdW))) break;
           mbar_arrive_expect_tx(&wfull[s], w_bytes);
-          tma_load_2d(smem + OFF_W + s * NMAX * 128, &p.tm_w, &wfull[s], k * 64, 0);
+          tma_load_2d(smem + OFF_W + s * NMAX * 128, &p.tm_w, &wfull[s], p.w_coord[k], 0);
         }
       }
       if (abort_sh) {
@@ -157,11 +171,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x) {
         int bb, i0, j0;
         decode_tile(p, tile, bb, i0, j0);
-        for (int k = 0; k < KATOMS; ++k, ++a) {
+        for (int k = 0; k < nsteps; ++k, ++a) {
           const uint32_t s = a % NA, ph = (a / NA) & 1;
           if (!(ok = mbar_wait(&aempty[s], ph ^ 1, ctx, kSiteProdA))) break;
           mbar_arrive_expect_tx(&afull[s], ATOM_BYTES);
-          tma_load_4d(smem + OFF_A + s * ATOM_BYTES, &p.tm_a, &afull[s], k * 64, j0, i0, bb);
+          tma_load_4d(smem + OFF_A + s * ATOM_BYTES, &p.tm_a, &afull[s], p.a_coord[k], j0, i0, bb);
         }
       }
       if (abort_sh) {
@@ -173,13 +187,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16_f32(128, p.n, false, false);
+      const uint32_t idesc = BF16 ? idesc_bf16_f32(128, p.n, false, false) : idesc_f16_f32(128, p.n, false, false);
       uint32_t r = 0, a = 0, it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t ab = it & 1, aph = (it >> 1) & 1;
         if (!(ok = mbar_wait(&accempty[ab], aph ^ 1, ctx, kSiteMmaAcc))) break;
-        for (int k = 0; k < KATOMS; ++k, ++r, ++a) {
+        for (int k = 0; k < nsteps; ++k, ++r, ++a) {
           const uint32_t sa = a % NA, sw = r % NW;
           if (!(ok = mbar_wait(&afull[sa], (a / NA) & 1, ctx, kSiteMmaA))) break;
           if (!(ok = mbar_wait(&wfull[sw], (r / NW) & 1, ctx, kSiteMmaW))) break;
@@ -233,11 +247,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + cell * p.n + c0);
           dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
           dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
-        } else {  // fp16(fp16(D) + bias) at out[c / H, b, c % H, i, j]
+        } else if (EPI == kEpiBiasT) {  // fp16(fp16(D) + bias) at out[c / H, b, c % H, i, j]
           __half* out = static_cast<__half*>(p.out) + pos;
 #pragma unroll
           for (int k = 0; k < 16; ++k)
             out[plane_s[c0 + k]] = __float2half_rn(round_f16(__uint_as_float(v[k])) + bias_s[c0 + k]);
+        } else {  // a * z + D, fp32 (z read before its row is written: same thread, same columns)
+          const float4* zr = reinterpret_cast<const float4*>(p.zres + cell * p.n + c0);
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + cell * p.n + c0);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float4 z = zr[k];
+            const float* av = bias_s + c0 + 4 * k;
+            dst[k] = make_float4(fmaf(av[0], z.x, __uint_as_float(v[4 * k])), fmaf(av[1], z.y, __uint_as_float(v[4 * k + 1])),
+                                 fmaf(av[2], z.z, __uint_as_float(v[4 * k + 2])),
+                                 fmaf(av[3], z.w, __uint_as_float(v[4 * k + 3])));
+          }
         }
       }
       tc_fence_before();

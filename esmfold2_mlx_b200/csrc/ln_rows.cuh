@@ -9,6 +9,8 @@
 // once to fp16 (gamma/beta absent: y = (x - mean) * rstd).
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "tmu_common.cuh"
 
 namespace tmu {
@@ -82,12 +84,28 @@ struct Params {
   RowTerms terms;
   const float* g;  // [K] or null
   const float* b;
-  __half* out;     // [rows, K]
+  void* out;       // kOutF16: fp16 [rows, K]; kOutBf16x3: bf16 [rows, 3K]
   long long rows;
   float eps;
 };
 
-template <int K, int SRC>
+// kOutF16:    h = fp16(y), one rounding.
+// kOutBf16x3: y split exactly into three bf16 parts, y = y0 + y1 + y2 to 24 significant bits
+//             (y0 = bf16(y), y1 = bf16(y - y0), y2 = bf16(y - y0 - y1)), stored as channel blocks
+//             [y0 | y1 | y2] of a 3K-wide row: the A operand of an fp32-accurate tensor-core GEMM.
+enum Out : int { kOutF16 = 0, kOutBf16x3 = 1 };
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t u) {
+  const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&u);
+  return __bfloat1622float2(v);
+}
+
+template <int K, int SRC, int OUT = kOutF16>
 __global__ void __launch_bounds__(kThreads) ln_rows_kernel(const __grid_constant__ Params p) {
   constexpr int NQ = K / 128;
   constexpr int RL = K <= 256 ? 4 : 2;
@@ -151,7 +169,6 @@ __global__ void __launch_bounds__(kThreads) ln_rows_kernel(const __grid_constant
         s2 = fmaf(d, d, s2);
       }
       const float rstd = rsqrtf(warp_allsum(s2) * (1.0f / K) + p.eps);
-      uint2* dst = reinterpret_cast<uint2*>(p.out + static_cast<size_t>(row) * K);
 #pragma unroll
       for (int q = 0; q < NQ; ++q) {
         float2 lo = make_float2((v[u][q].x - mean) * rstd, (v[u][q].y - mean) * rstd);
@@ -160,7 +177,23 @@ __global__ void __launch_bounds__(kThreads) ln_rows_kernel(const __grid_constant
           lo = make_float2(fmaf(lo.x, gg[q].x, bb[q].x), fmaf(lo.y, gg[q].y, bb[q].y));
           hi = make_float2(fmaf(hi.x, gg[q].z, bb[q].z), fmaf(hi.y, gg[q].w, bb[q].w));
         }
-        dst[lane + 32 * q] = make_uint2(pack_half2(lo.x, lo.y), pack_half2(hi.x, hi.y));
+        if constexpr (OUT == kOutF16) {
+          uint2* dst = reinterpret_cast<uint2*>(static_cast<__half*>(p.out) + static_cast<size_t>(row) * K);
+          dst[lane + 32 * q] = make_uint2(pack_half2(lo.x, lo.y), pack_half2(hi.x, hi.y));
+        } else {
+          uint2* dst = reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(row) * 3 * K);
+          float y[4] = {lo.x, lo.y, hi.x, hi.y};
+#pragma unroll
+          for (int part = 0; part < 3; ++part) {
+            const uint32_t w0 = pack_bf16x2(y[0], y[1]), w1 = pack_bf16x2(y[2], y[3]);
+            dst[part * (K / 4) + lane + 32 * q] = make_uint2(w0, w1);
+            const float2 r0 = unpack_bf16x2(w0), r1 = unpack_bf16x2(w1);
+            y[0] -= r0.x;  // exact: the remainder of a bf16 rounding of an fp32 value
+            y[1] -= r0.y;
+            y[2] -= r1.x;
+            y[3] -= r1.y;
+          }
+        }
       }
     }
   }

@@ -583,10 +583,10 @@ int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B
 }
 
 // Row LayerNorm pass: h = fp16(LN(rows)) [rows, K].
-template <int K, int SRC>
+template <int K, int SRC, int OUT = lnr::kOutF16>
 int launch_lnr(const void* x1, const void* x2, int ld1, int ld2, const RowTerms* terms, const float* g,
-               const float* b, __half* out, long long rows, cudaStream_t stream) {
-  void (*kern)(lnr::Params) = lnr::ln_rows_kernel<K, SRC>;
+               const float* b, void* out, long long rows, cudaStream_t stream) {
+  void (*kern)(lnr::Params) = lnr::ln_rows_kernel<K, SRC, OUT>;
   Dev dev;
   int st = current_device(dev, 0, reinterpret_cast<const void*>(kern), 0);
   if (st) return st;
@@ -659,11 +659,26 @@ int launch_k4_h(const __half* h, __half* tout, const tmu_cond_transition_weights
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch transition_kernel (h)");
 }
 
-// K6 with the A operand by TMA: D = h @ W^T, h [B, L, L, K] fp16, W fp16 [n, K].
-template <int K, int EPI>
-int launch_k6g(const __half* h, const void* w, int n, void* out, const void* bias, int heads, int B, int L,
-               unsigned long long bit, DeviceStatus* status, cudaStream_t stream) {
-  void (*kern)(k6::Params) = k6::gemm_kernel<K, EPI>;
+// K6 with the A operand by TMA: D = h @ W^T over a K-step schedule (step s: A channels
+// [a_coord[s], +64) of the ka-wide h rows times W columns [w_coord[s], +64) of the kw-wide W rows).
+struct K6Sched {
+  int nsteps;
+  short a_coord[k6::kMaxSteps];
+  short w_coord[k6::kMaxSteps];
+};
+
+K6Sched plain_sched(int K) {
+  K6Sched sc;
+  sc.nsteps = K / 64;
+  for (int k = 0; k < sc.nsteps; ++k) sc.a_coord[k] = sc.w_coord[k] = static_cast<short>(64 * k);
+  return sc;
+}
+
+template <int EPI, bool BF16 = false>
+int launch_k6g(const void* h, int ka, const void* w, int kw, int n, const K6Sched& sc, void* out, const void* bias,
+               int heads, const float* zres, const float* avec, int B, int L, unsigned long long bit,
+               DeviceStatus* status, cudaStream_t stream) {
+  void (*kern)(k6::Params) = k6::gemm_kernel<EPI, BF16>;
   Dev dev;
   int st = current_device(dev, bit, reinterpret_cast<const void*>(kern), k6::SMEM_BYTES);
   if (st) return st;
@@ -672,21 +687,28 @@ int launch_k6g(const __half* h, const void* w, int n, void* out, const void* bia
   int ih = 1, jw = 128;
   choose_tile(L, L, ih, jw, k6::TILE);
   {
-    const uint64_t dims[2] = {K, (uint64_t)n};
-    const uint64_t str[1] = {2 * K};
+    const uint64_t dims[2] = {(uint64_t)kw, (uint64_t)n};
+    const uint64_t str[1] = {2ull * kw};
     const uint32_t box[2] = {64, (uint32_t)n};
     if ((st = encode_map(&p.tm_w, w, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
-    const uint64_t dims[4] = {K, (uint64_t)L, (uint64_t)L, (uint64_t)B};
-    const uint64_t str[3] = {2ull * K, 2ull * K * L, 2ull * K * L * L};
+    const uint64_t dims[4] = {(uint64_t)ka, (uint64_t)L, (uint64_t)L, (uint64_t)B};
+    const uint64_t str[3] = {2ull * ka, 2ull * ka * L, 2ull * ka * L * L};
     const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
     if ((st = encode_map(&p.tm_a, h, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   p.out = out;
   p.bias = static_cast<const __half*>(bias);
+  p.zres = zres;
+  p.avec = avec;
   p.n = n;
   p.heads = heads;
+  p.nsteps = sc.nsteps;
+  for (int k = 0; k < sc.nsteps; ++k) {
+    p.a_coord[k] = sc.a_coord[k];
+    p.w_coord[k] = sc.w_coord[k];
+  }
   p.B = B;
   p.L = L;
   p.ih = ih;
@@ -1100,8 +1122,8 @@ int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_con
   int r = c_in == 512 ? launch_lnr<512, kRowCat32>(z_trunk, rel_pos, c_trunk, c_rel, nullptr, w->ln_w, w->ln_b, h, cells, s)
                       : launch_lnr<256, kRowCat32>(z_trunk, rel_pos, c_trunk, c_rel, nullptr, w->ln_w, w->ln_b, h, cells, s);
   if (r) return r;
-  r = c_in == 512 ? launch_k6g<512, k6::kEpiStore16>(h, w->proj, c_pair, z0, nullptr, 1, B, L, 1ull << 32, st, s)
-                  : launch_k6g<256, k6::kEpiStore16>(h, w->proj, c_pair, z0, nullptr, 1, B, L, 1ull << 33, st, s);
+  r = launch_k6g<k6::kEpiStore16>(h, c_in, w->proj, c_in, c_pair, plain_sched(c_in), z0, nullptr, 1, nullptr, nullptr,
+                                  B, L, 1ull << 32, st, s);
   // Transition k: h = fp16(LN(z0 + t_1 + .. + t_{k-1})), t_k = fp16(ffn(h))
   for (int k = 1; k <= w->n_transitions && r == TMU_OK; ++k) {
     const tmu_cond_transition_weights* tw = &w->transitions[k - 1];
@@ -1119,8 +1141,49 @@ int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_con
   r = wide ? launch_lnr<256, kRowTerms16>(nullptr, nullptr, 0, 0, &terms, nullptr, nullptr, h, cells, s)
            : launch_lnr<128, kRowTerms16>(nullptr, nullptr, 0, 0, &terms, nullptr, nullptr, h, cells, s);
   if (r) return r;
-  return wide ? launch_k6g<256, k6::kEpiBiasT>(h, w->bias_w, n_bias, out, w->bias_b, heads, B, L, 1ull << 36, st, s)
-              : launch_k6g<128, k6::kEpiBiasT>(h, w->bias_w, n_bias, out, w->bias_b, heads, B, L, 1ull << 37, st, s);
+  return launch_k6g<k6::kEpiBiasT>(h, c_pair, w->bias_w, c_pair, n_bias, plain_sched(c_pair), out, w->bias_b, heads,
+                                   nullptr, nullptr, B, L, 1ull << 36, st, s);
+}
+
+size_t tmu_parcae_workspace_bytes(int B, int L, int c_z) {
+  if (B < 1 || L < 1 || c_z < 1) return 0;
+  return static_cast<size_t>(B) * L * L * 3 * c_z * 2;
+}
+
+int tmu_parcae_step(const float* z, const float* z_init, const float* refined, const tmu_parcae_weights* w,
+                    float* z_out, int B, int L, int c_z, void* workspace, size_t workspace_bytes, void* status,
+                    void* stream) {
+  if (B < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "B and L must be positive");
+  if (L > 8192 || B > 65535) return fail(TMU_ERR_UNSUPPORTED, "L > 8192");
+  if (c_z != 128 && c_z != 256) return fail(TMU_ERR_UNSUPPORTED, "c_z must be 128 or 256");
+  if (w == nullptr || !w->ln_w || !w->ln_b || !w->a || !w->b_split)
+    return fail(TMU_ERR_INVALID_ARGUMENT, "parcae weights missing");
+  if (!z || !z_init || !refined || !z_out || !workspace || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (workspace_bytes < tmu_parcae_workspace_bytes(B, L, c_z)) return fail(TMU_ERR_INVALID_ARGUMENT, "workspace too small");
+  const void* al[] = {z, z_init, refined, z_out, workspace, w->ln_w, w->ln_b, w->a, w->b_split};
+  for (const void* q : al)
+    if (!aligned16(q)) return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");
+  DeviceStatus* st = static_cast<DeviceStatus*>(status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long cells = static_cast<long long>(B) * L * L;
+  // LN(z_init + refined), split into three bf16 parts [x0 | x1 | x2]
+  int r = c_z == 256 ? launch_lnr<256, kRowSum32, lnr::kOutBf16x3>(z_init, refined, c_z, c_z, nullptr, w->ln_w, w->ln_b,
+                                                                  workspace, cells, s)
+                     : launch_lnr<128, kRowSum32, lnr::kOutBf16x3>(z_init, refined, c_z, c_z, nullptr, w->ln_w, w->ln_b,
+                                                                  workspace, cells, s);
+  if (r) return r;
+  // the six products x_i B_j with i + j <= 2, smallest first, each over the c_z / 64 K atoms
+  static const int pairs[6][2] = {{2, 0}, {1, 1}, {0, 2}, {1, 0}, {0, 1}, {0, 0}};
+  K6Sched sc;
+  sc.nsteps = 0;
+  for (const auto& pr : pairs)
+    for (int k = 0; k < c_z / 64; ++k) {
+      sc.a_coord[sc.nsteps] = static_cast<short>(pr[0] * c_z + 64 * k);
+      sc.w_coord[sc.nsteps] = static_cast<short>(pr[1] * c_z + 64 * k);
+      ++sc.nsteps;
+    }
+  return launch_k6g<k6::kEpiAxpy, true>(workspace, 3 * c_z, w->b_split, 3 * c_z, c_z, sc, z_out, nullptr, 0, z,
+                                        w->a, B, L, 1ull << 38, st, s);
 }
 
 int tmu_ipc_export(const void* ptr, void* handle, unsigned long long* offset) {

@@ -372,6 +372,11 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool a_mn_maj
          | (static_cast<uint32_t>(M >> 4) << 24);   // M / 16
 }
 
+// The same for bf16 A and B (kind::f16 takes both operands in one format: f16 or bf16).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_major, bool b_mn_major) {
+  return idesc_f16_f32(M, N, a_mn_major, b_mn_major) | (1u << 7) | (1u << 10);
+}
+
 // Byte offset of the 16-byte chunk `chunk` (0..7) of row `row` in a 128B-swizzled tile whose
 // rows are 128 bytes and whose base is 1024-byte aligned.
 __device__ __forceinline__ uint32_t sw128_off(uint32_t row, uint32_t chunk) {

@@ -27,8 +27,8 @@ def main():
     ap.add_argument("--L", type=int, default=1024)
     ap.add_argument("--B", type=int, default=1)
     ap.add_argument("--direction", choices=["out", "in"], default="out")
-    ap.add_argument("--stage", choices=["all", "k1", "k2", "k3", "k4", "k5", "pc"], default="all",
-                    help="pc: the diffusion pair conditioning (tmu_pair_cond: K6, K4 rows x 2, K6)")
+    ap.add_argument("--stage", choices=["all", "k1", "k2", "k3", "k4", "k5", "pc", "parcae"], default="all",
+                    help="pc: the diffusion pair conditioning (tmu_pair_cond); parcae: the 6B loop's parcae step")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--mask-pad", type=int, default=0)
     ap.add_argument("--cz", type=int, choices=[128, 256], default=128, help="c_z = c")
@@ -75,6 +75,18 @@ def main():
         ws = torch.empty(pair_cond.workspace_bytes(B, L, pw.c_in, pw.c_pair, 2), dtype=torch.uint8, device=dev)
         pout = torch.empty(pw.n_bias // pw.heads, B, pw.heads, L, L, dtype=torch.float16, device=dev)
         stages["pc"] = lambda: pair_cond.pair_biases(pw, zt, rp, out=pout, workspace=ws, status=status)
+    if args.stage == "parcae":
+        from torch import nn
+
+        from . import parcae
+        m = nn.Module()
+        m.parcae_input_norm = nn.LayerNorm(args.cz)
+        pwt = parcae.ParcaeWeights.from_model(m, torch.full((args.cz,), 0.5), torch.randn(args.cz, args.cz) / 16, dev)
+        zf = pair_tensor(B, L, args.cz, 3).to(dev)
+        zi, rf = pair_tensor(B, L, args.cz, 4).to(dev), pair_tensor(B, L, args.cz, 5).to(dev)
+        pws = torch.empty(_lib.load().tmu_parcae_workspace_bytes(B, L, args.cz), dtype=torch.uint8, device=dev)
+        pout = torch.empty_like(zf)
+        stages["parcae"] = lambda: parcae.parcae_step(zf, zi, rf, pwt, out=pout, workspace=pws, status=status)
     fn = stages[args.stage]
     fn()  # warm-up: the stage's own output allocations happen here, outside the timed launches
     torch.cuda.synchronize()

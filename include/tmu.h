@@ -244,6 +244,29 @@ int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_con
                   int c_trunk, int c_rel, int c_pair, int hidden, int n_bias, int heads, void* out,
                   void* workspace, size_t workspace_bytes, void* status, void* stream);
 
+/* ---- Parcae step of the 6B release model's recycling loop (var_6b_mlx_loop.py:67-71, fp32 in
+ * the reference):  z_out = a * z + LN(z_init + refined) @ B^T, with refined the lm_encoder
+ * trunk's output.  z, z_init, refined, z_out fp32 [B, L, L, c_z] (z_out may alias z); a fp32
+ * [c_z] (a scalar a is a constant vector); LayerNorm fp32 (parcae_input_norm, eps 1e-5).
+ * The GEMM runs on the tensor cores with fp32 accuracy: B is passed split into three bf16 parts,
+ * b_split = [B0 | B1 | B2] bf16 [c_z, 3 c_z] with B = B0 + B1 + B2 exactly (B0 = bf16(B),
+ * B1 = bf16(B - B0), B2 = bf16(B - B0 - B1)), LN's output is split the same way in the kernel,
+ * and the six products x_i B_j with i + j <= 2 accumulate in fp32. */
+typedef struct tmu_parcae_weights {
+  const float* ln_w;    /* fp32 [c_z]: parcae_input_norm.weight */
+  const float* ln_b;    /* fp32 [c_z]: parcae_input_norm.bias */
+  const float* a;       /* fp32 [c_z] */
+  const void* b_split;  /* bf16 [c_z, 3 c_z] */
+} tmu_parcae_weights;
+
+/* Scratch for the split LayerNorm output: bf16 [B, L, L, 3 c_z]. */
+size_t tmu_parcae_workspace_bytes(int B, int L, int c_z);
+
+/* c_z = 128 or 256. */
+int tmu_parcae_step(const float* z, const float* z_init, const float* refined, const tmu_parcae_weights* w,
+                    float* z_out, int B, int L, int c_z, void* workspace, size_t workspace_bytes, void* status,
+                    void* stream);
+
 /* ---- Copy-engine exchange for the row-sharded path (no counterpart in the reference).  A rank
  * exports a device buffer with tmu_ipc_export (CUDA IPC handle of the allocation that contains
  * `ptr`, plus ptr's byte offset inside it); a peer process imports it with tmu_ipc_import and
