@@ -126,10 +126,13 @@ def make_trunk(dtype=torch.float16):
 
 
 class _GraphEntry:
-    """One captured trunk pass: static input / mask / output buffers and the CUDA graph."""
+    """One captured trunk pass: static input / mask / output buffers, the CUDA graph, and the
+    trunk function whose workspace the captured kernels address.  The entry must own that
+    function: a later capture's ``torch.cuda.graph`` runs ``gc.collect()`` and ``empty_cache()``,
+    which would hand an orphaned workspace back to the driver while this graph still writes it."""
 
-    def __init__(self, graph, z_in, mask_in, out):
-        self.graph, self.z_in, self.mask_in, self.out = graph, z_in, mask_in, out
+    def __init__(self, graph, z_in, mask_in, out, fn):
+        self.graph, self.z_in, self.mask_in, self.out, self.fn = graph, z_in, mask_in, out, fn
 
 
 class CUDAFoldingTrunk(nn.Module):
@@ -175,7 +178,7 @@ class CUDAFoldingTrunk(nn.Module):
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
                 out = fn(self.params, z_in, mask_in)
-            entry = _GraphEntry(graph, z_in, mask_in, out)
+            entry = _GraphEntry(graph, z_in, mask_in, out, fn)
             while len(self._graph_cache) >= self.max_graphs:
                 self._graph_cache.pop(next(iter(self._graph_cache)))
         self._graph_cache[key] = entry  # most recently used last

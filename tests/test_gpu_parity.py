@@ -222,3 +222,18 @@ def test_trunk_graph_replay_equals_eager_and_is_cached():
     z = pair_tensor(1, 33, 128, 1).to(DEV)
     assert torch.equal(eager(z), graphed(z))
     assert len(graphed._graph_cache) == 2
+
+
+def test_trunk_graph_survives_a_later_capture_and_cache_release():
+    """A cached graph's kernels address the workspace of the trunk function it was captured
+    with; the cache entry owns that function, so a later capture (which runs gc.collect() and
+    empty_cache()) or an explicit empty_cache() cannot hand the workspace back to the driver."""
+    from esmfold2_mlx_b200.trunk import CUDAFoldingTrunk
+
+    first = CUDAFoldingTrunk(FoldingTrunk(1, 128, 128, hidden=256, seed=5, ln_noise=0.1))
+    second = CUDAFoldingTrunk(FoldingTrunk(2, 128, 128, hidden=256, seed=6, ln_noise=0.1))
+    z = pair_tensor(1, 40, 128, 7).to(DEV)
+    a = first(z)
+    second(z)  # a second capture
+    torch.cuda.empty_cache()
+    assert torch.equal(first(z), a)

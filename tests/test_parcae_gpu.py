@@ -72,3 +72,21 @@ def test_parcae_scalar_a_broadcasts():
     nw, nb = m.parcae_input_norm.weight.detach(), m.parcae_input_norm.bias.detach()
     ref = po.parcae_step(z, zi, rf, nw, nb, 0.5, b_mat, torch.float64)
     assert float((out - ref).abs().max()) <= float(ref.abs().max()) * 2.0**-19
+
+
+def test_loop_step_composes_lm_encoder_parcae_and_trunk():
+    """loop_step == folding_trunk(parcae(z, z_init, lm_encoder(lz))) (var_6b_mlx_loop.py:67-71)."""
+    from esmfold2_mlx_b200.synthetic import FoldingTrunk
+    from esmfold2_mlx_b200.trunk import CUDAFoldingTrunk
+
+    c, L = 128, 40
+    lm = CUDAFoldingTrunk(FoldingTrunk(1, c, c, hidden=256, seed=1, ln_noise=0.1), device=DEV)
+    tr = CUDAFoldingTrunk(FoldingTrunk(2, c, c, hidden=256, seed=2, ln_noise=0.1), device=DEV)
+    m = _Model(c, seed=3)
+    z, zi, rf, a, b_mat = _inputs(1, L, c, seed=4)
+    w = parcae.ParcaeWeights.from_model(m, a, b_mat, DEV)
+    lz, zd, zid = rf.to(DEV), (z / 10).to(DEV), zi.to(DEV)
+    got = parcae.loop_step(lm, tr, w, lz, zd, zid)
+    ref = tr(parcae.parcae_step(zd, zid, lm(lz).float().contiguous(), w))
+    torch.cuda.synchronize()
+    assert got.shape == (1, L, L, c) and torch.equal(got, ref)
