@@ -10,20 +10,25 @@
 // a, b stored [B*c, L, Lpad] (channel d, row i, column j).  The fp16 pre-scale of w_in[:, :c]
 // by 1/256 (mlx_trunk.py:47-48) lives in the packed weights.
 //
-// The projection is computed transposed, D = W n^T (M = 128 output channels, N = 64 positions,
+// The projection is computed transposed, D = W n^T (M = 128 output channels, N = 128 positions,
 // K = c_z), so TMEM lane = channel and column = position: an epilogue thread owns one channel
 // and reads 16 consecutive positions at a time, which are contiguous in the channel-major
-// output.  The signal and gate rows of the same channels go through two MMAs into the same
-// TMEM lanes (columns [0,64) and [64,128) of a slot), so the gate pairs up in registers.
+// output.  Each of the four 128-row weight blocks (signal a, gate a, signal b, gate b) is one
+// MMA chain over the whole tile into its own TMEM slot, so the tensor core reads every weight
+// block once per tile (N = 64 chains over position halves read each twice, and the operand
+// traffic through shared memory was the kernel's limiter); a signal and its gate share TMEM
+// lanes, so they pair up in registers.
 //
 // One tile = 128 pair positions, an ih x jw block of the L x L grid (ih * jw = 128), chosen by
 // the host to minimise padding at ragged L.  CTA = 26 warps, one per SM, persistent:
 //   warp 0      TMA: packed weights once (resident, 4c x c_z fp16), then z tiles (2 stages)
-//   warp 1      TMEM allocation (512 columns = 4 slots of 128: {a, b} x {positions 0-63,
-//               64-127}) and the MMA thread, which refills a slot as soon as it is drained
+//   warp 1      TMEM allocation (512 columns = 4 slots of 128 positions: signal a, gate a,
+//               signal b, gate b) and the MMA thread, which refills the a (or b) slot pair as
+//               soon as both epilogue groups of a (or b) have drained it
 //   warps 2-9   LayerNorm of the z tile in place (a lane pair per position, each lane one half of
 //               the channels, interleaved by 16-byte chunk) + the tile's mask as fp32
-//   warps 10-25 epilogue: four warps (one per TMEM lane quadrant) per slot; per 16 positions:
+//   warps 10-25 epilogue: four groups {a, b} x {positions 0-63, 64-127} of four warps (one per
+//               TMEM lane quadrant); per 16 positions:
 //               gate, mask, fp16, 32 B per thread into a 2 KB staging block; every 32 positions
 //               a per-warp TMA store of the 32-channel x 32-position box (64-byte rows when
 //               jw >= 32), staged with the swizzle that keeps a warp's 32 row writes free of
@@ -90,7 +95,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 
 template <bool HAS_BIAS, bool HAS_MASK>
 __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_constant__ Params p) {
-  constexpr uint32_t IDESC = idesc_f16_f32(128, 64, false, false);
+  constexpr uint32_t IDESC = idesc_f16_f32(128, 128, false, false);
   // All shared state lives in the dynamic buffer (no static __shared__), whose base the 128B
   // swizzle needs 1024-byte aligned; a misaligned base is reported, never computed on.
   extern __shared__ uint8_t smem[];
@@ -126,8 +131,8 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
       mbar_init(&lnfull[s], 8);  // one arrival per LayerNorm warp
     }
     for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 4);  // one arrival per epilogue warp draining the slot
+      mbar_init(&tfull[s], 1);   // [0]: slots a, [1]: slots b
+      mbar_init(&tempty[s], 8);  // the eight epilogue warps (two groups) draining a slot pair
     }
     for (int k = 0; k < NMASK; ++k) {
       mbar_init(&mfull[k], 8);      // LayerNorm warps wrote the tile's mask
@@ -199,21 +204,19 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
         if (!mbar_wait(&lnfull[s], ph, ctx, kSiteMmaLn)) { ok = false; break; }
         tc_fence_after();
         const uint32_t n_base = smem_u32(smem + OFF_A + s * A_BYTES);
-        for (int slot = 0; slot < NSLOT; ++slot) {  // slot = 2 * (a: 0, b: 1) + position half
-          const int x = slot >> 1, hpos = slot & 1;
-          if (!mbar_wait(&tempty[slot], (it & 1) ^ 1, ctx, kSiteMmaSlot)) { ok = false; break; }
+        for (int x = 0; x < 2; ++x) {  // x = 0: a (slots 0, 1), x = 1: b (slots 2, 3)
+          if (!mbar_wait(&tempty[x], (it & 1) ^ 1, ctx, kSiteMmaSlot)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t b_base = n_base + hpos * 64 * 128;  // positions [64 hpos, 64 hpos + 64)
-          for (int h = 0; h < 2; ++h) {  // h = 0 signal rows, h = 1 gate rows
+          for (int h = 0; h < 2; ++h) {  // h = 0 signal rows, h = 1 gate rows: slot 2x + h
             const uint32_t w_base = smem_u32(smem + OFF_W + (2 * x + h) * WBLOCK_BYTES);
 #pragma unroll
             for (int kk = 0; kk < CZ / 16; ++kk) {
               const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-              umma_f16(tmem_base + slot * 128 + h * 64, sdesc_sw128(w_base + off, 16, 1024),
-                       sdesc_sw128(b_base + off, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+              umma_f16(tmem_base + (2 * x + h) * 128, sdesc_sw128(w_base + off, 16, 1024),
+                       sdesc_sw128(n_base + off, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
             }
           }
-          umma_commit(&tfull[slot]);
+          umma_commit(&tfull[x]);
         }
         if (ok) umma_commit(&zempty[s]);  // the z/n tile may be refilled once these MMAs have read it
       }
@@ -251,8 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
     }
   } else {
     // ---------------- epilogue: gate, mask, channel-major store ----------------
-    const int slot = (warp - 10) >> 2;  // 2 * (a: 0, b: 1) + position half
-    const int x = slot >> 1, hpos = slot & 1;
+    const int grp = (warp - 10) >> 2;  // 2 * (a: 0, b: 1) + position half
+    const int x = grp >> 1, hpos = grp & 1;
     const int q = warp & 3;            // TMEM lane quadrant = channels [32q, 32q+32)
     const int ch = q * 32 + lane;      // this thread's output channel
     uint8_t* stg = smem + OFF_STG + (warp - 10) * WSTG_BYTES;
@@ -282,16 +285,17 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
       bg = __ldg(p.bias + (2 * x + 1) * 128 + ch);
     }
     const float2 bs2 = make_float2(bs, bs), bg2 = make_float2(bg, bg);
-    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 128;
+    // signal in slot 2x, gate in slot 2x + 1, this group's positions [64 hpos, 64 hpos + 64)
+    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + 2 * x * 128 + 64 * hpos;
     const CUtensorMap* tm = x == 0 ? &p.tm_a : &p.tm_b;
     uint32_t it = 0, gcount = 0;
     const bool leader = ((warp - 10) & 3) == 0 && lane == 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
-      // one thread of the slot's four warps waits, the others park on barrier 2 + slot
-      if (!group_wait(&tfull[slot], it & 1, HAS_MASK ? &mfull[it % NMASK] : nullptr, (it / NMASK) & 1, ctx,
-                      kSiteEpilogue, leader, 2 + slot, 128, gflags + 2 + 2 * slot, gcount))
+      // one thread of the group's four warps waits, the others park on barrier 2 + grp
+      if (!group_wait(&tfull[x], it & 1, HAS_MASK ? &mfull[it % NMASK] : nullptr, (it / NMASK) & 1, ctx,
+                      kSiteEpilogue, leader, 2 + grp, 128, gflags + 2 + 2 * grp, gcount))
         break;
       tc_fence_after();
       const float* mrow = maskf + (it % NMASK) * TILE + hpos * 64;
@@ -299,12 +303,12 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
       for (int pb = 0; pb < 64; pb += POS) {
         uint32_t sg[16], gt[16];
         tmem_ld16(taddr + pb, sg);
-        tmem_ld16(taddr + 64 + pb, gt);
+        tmem_ld16(taddr + 128 + pb, gt);
         tmem_wait_ld16x2(sg, gt);
-        if (pb == 64 - POS) {  // the whole slot has been read: hand it back to the MMA
+        if (pb == 64 - POS) {  // this group's part of the slot pair has been read
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[slot]);
+          if (lane == 0) mbar_arrive(&tempty[x]);
         }
         uint32_t o[8];
 #pragma unroll

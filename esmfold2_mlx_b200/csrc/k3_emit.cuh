@@ -12,7 +12,7 @@
 // The LayerNorm that the reference fuses after the residual (resgate_ln's second output) is
 // the next kernel's prologue (K1 of the next tri-mul normalises the z' it loads).
 //
-// One tile = 128 positions (ih x jw block).  CTA = 18 warps, one per SM, persistent:
+// One tile = 128 positions (ih x jw block).  CTA = 19 warps, one per SM, persistent:
 //   warp 0     TMA: w_emit and w_gate once (resident), then per tile the z tile and the x tile
 //              (2 stages each; z 128B-swizzled position-major, x channel-major unswizzled)
 //   warp 1     TMEM (2 x 256 columns) + MMA thread: emit (A1 x W_e) and gate (A2 x W_g)
@@ -22,6 +22,8 @@
 //   warps 10-17 epilogue, two groups of four warps (one per TMEM lane quadrant); group h owns
 //              output channels [64h, 64h+64): TMEM -> gate/residual in fp32 -> z' written over
 //              the z tile -> each warp TMA-stores its own 32 positions x 64 channels
+//   warp 18    TMA: the x tiles (warp 0 keeps the z tiles), so an x load never queues behind
+//              the z stage, which stays busy until the epilogue has stored z'
 #pragma once
 
 #include "tmu_common.cuh"
@@ -42,7 +44,7 @@ constexpr int OFF_A2 = OFF_X + 2 * TILE_BYTES;
 constexpr int OFF_PAR = OFF_A2 + TILE_BYTES;     // fp32 LN params: in gamma, in beta, mix gamma, mix beta
 constexpr int OFF_BAR = OFF_PAR + 4 * 128 * 4;   // mbarriers and flags
 constexpr int SMEM_BYTES = OFF_BAR + 256;        // no alignment slack: the kernel checks the base instead
-constexpr int kThreads = 576;
+constexpr int kThreads = 608;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
@@ -92,7 +94,8 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   uint64_t* zempty = bars + 3;
   uint64_t* xfull = bars + 5;
   uint64_t* xempty = bars + 7;
-  uint64_t& afull = bars[9];
+  uint64_t& a2full = bars[9];       // A2 written (the four LN_in warps)
+  uint64_t* a1full = bars + 21;     // [2] A1 written over x stage s (the four LN_mix warps)
   uint64_t& a2empty = bars[10];
   uint64_t* tfull = bars + 11;
   uint64_t* tempty = bars + 13;
@@ -119,7 +122,11 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       mbar_init(&xfull[s], 1);
       mbar_init(&xempty[s], 1);  // committed by the MMA that read A1 from this stage
     }
-    mbar_init(&afull, 8);  // one arrival per LN_mix / LN_in warp
+    // A1 and A2 have separate barriers: LN_mix may finish tile t+1 before LN_in finishes tile t
+    // (the x tiles have their own producer), and one shared count would then mix the two tiles
+    mbar_init(&a1full[0], 4);
+    mbar_init(&a1full[1], 4);
+    mbar_init(&a2full, 4);
     mbar_init(&a2empty, 1);
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
@@ -155,7 +162,9 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      uint32_t it = 0, nz = 0, nx = 0;
+      // z tiles; the x tiles have their own producer (warp 18), so an x load never waits
+      // behind the long-lived z stage (held until the epilogue has stored z')
+      uint32_t it = 0, nz = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         int bb, i0, j0;
         decode_tile(p, tile, bb, i0, j0);
@@ -165,16 +174,30 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
         for (int a = 0; a < CZ / 64; ++a)
           tma_load_4d(smem + OFF_Z + s * TILE_BYTES + a * ATOM_BYTES, &p.tm_z, &zfull[s], a * 64, j0, i0, bb);
         ++nz;
-        if (!mbar_wait(&xempty[s], ph ^ 1, ctx, kSiteProdX)) break;
-        mbar_arrive_expect_tx(&xfull[s], TILE * CC * 2);
-        tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
-        ++nx;
       }
       if (abort_sh) {
         mbar_drain(&w_bar, 0, 200000000ull);
         for (uint32_t s = 0; s < 2; ++s) {
           const uint32_t nza = nz > s ? (nz - s + 1) / 2 : 0;
           if (nza) mbar_drain(&zfull[s], (nza - 1) & 1, 200000000ull);
+        }
+      }
+    }
+  } else if (warp == 18) {
+    // ---------------- TMA producer: x tiles ----------------
+    if (lane == 0) {
+      uint32_t it = 0, nx = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
+        int bb, i0, j0;
+        decode_tile(p, tile, bb, i0, j0);
+        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        if (!mbar_wait(&xempty[s], ph ^ 1, ctx, kSiteProdX)) break;
+        mbar_arrive_expect_tx(&xfull[s], TILE * CC * 2);
+        tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
+        ++nx;
+      }
+      if (abort_sh) {
+        for (uint32_t s = 0; s < 2; ++s) {
           const uint32_t nxa = nx > s ? (nx - s + 1) / 2 : 0;
           if (nxa) mbar_drain(&xfull[s], (nxa - 1) & 1, 200000000ull);
         }
@@ -189,7 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       const uint32_t we = smem_u32(smem + OFF_WE), wg = smem_u32(smem + OFF_WG);
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t acc = it & 1, aph = (it >> 1) & 1;
-        if (!mbar_wait(&afull, it & 1, ctx, kSiteMmaA)) break;
+        if (!mbar_wait(&a1full[it & 1], (it >> 1) & 1, ctx, kSiteMmaA)) break;
+        if (!mbar_wait(&a2full, it & 1, ctx, kSiteMmaA)) break;
         if (!mbar_wait(&tempty[acc], aph ^ 1, ctx, kSiteMmaT)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * 256;
@@ -247,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       ln_row128_sw128(A1, A1, ATOM_BYTES, row, p.mix_eps, LnParSmem{par + 256, par + 384});
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&afull);
+      if (lane == 0) mbar_arrive(&a1full[s]);
     }
   } else if (warp < 10) {
     // ---------------- A2 = LN_in of each position's z row ----------------
@@ -260,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
                       LnParSmem{par, par + 128});
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&afull);
+      if (lane == 0) mbar_arrive(&a2full);
     }
   } else {
     // ---------------- epilogue ----------------
