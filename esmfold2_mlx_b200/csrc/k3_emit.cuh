@@ -12,17 +12,21 @@
 // The LayerNorm that the reference fuses after the residual (resgate_ln's second output) is
 // the next kernel's prologue (K1 of the next tri-mul normalises the z' it loads).
 //
-// One tile = 128 positions (ih x jw block).  CTA = 19 warps, one per SM, persistent:
-//   warp 0     TMA: w_emit and w_gate once (resident), then per tile the z tile and the x tile
-//              (2 stages each; z 128B-swizzled position-major, x channel-major unswizzled)
+// One tile = 128 positions (ih x jw block).  CTA = 23 warps, one per SM, persistent:
+//   warp 0     TMA: w_emit and w_gate once (resident), then per tile the z tile (3 stages,
+//              128B-swizzled position-major); warp 22 the x tile (2 stages, channel-major)
 //   warp 1     TMEM (2 x 256 columns) + MMA thread: emit (A1 x W_e) and gate (A2 x W_g)
-//   warps 2-5  A1 = fp16(LN_mix(x column)), written over the x tile it was gathered from once all
-//              four warps hold their columns in registers; warps 6-9  A2 = fp16(LN_in(z row));
-//              both concurrently, both K-major 128B-swizzled UMMA operands
-//   warps 10-17 epilogue, two groups of four warps (one per TMEM lane quadrant); group h owns
+//   warps 2-9  A1 = fp16(LN_mix(x column)), a lane pair per position, written over the x tile
+//              it was gathered from once every thread holds its half-column in registers;
+//   warps 10-13 A2 = fp16(LN_in(z row)), in place over the z stage; both concurrently, both
+//              K-major 128B-swizzled UMMA operands.  A2 in place (instead of one separate A2
+//              buffer) lets LN_in run ahead of the MMA, and its 32 KB pays for a third z stage;
+//              after the MMA has read A2, each epilogue half reloads its 64-channel z atom into
+//              the stage (an L2 hit) for the residual.
+//   warps 14-21 epilogue, two groups of four warps (one per TMEM lane quadrant); group h owns
 //              output channels [64h, 64h+64): TMEM -> gate/residual in fp32 -> z' written over
 //              the z tile -> each warp TMA-stores its own 32 positions x 64 channels
-//   warp 18    TMA: the x tiles (warp 0 keeps the z tiles), so an x load never queues behind
+//   warp 22    TMA: the x tiles (warp 0 keeps the z tiles), so an x load never queues behind
 //              the z stage, which stays busy until the epilogue has stored z'
 #pragma once
 
@@ -38,13 +42,14 @@ constexpr int ATOM_BYTES = TILE * 128;
 constexpr int TILE_BYTES = TILE * 128 * 2;  // 128 positions x 128 channels fp16
 constexpr int OFF_WE = 0;
 constexpr int OFF_WG = OFF_WE + CZ * CC * 2;
+constexpr int NZ = 3;                          // z stages: z, then A2 in place, then z again
 constexpr int OFF_Z = OFF_WG + CZ * CZ * 2;
-constexpr int OFF_X = OFF_Z + 2 * TILE_BYTES;  // 2 stages; stage s holds the x tile, then A1 in place
-constexpr int OFF_A2 = OFF_X + 2 * TILE_BYTES;
-constexpr int OFF_PAR = OFF_A2 + TILE_BYTES;     // fp32 LN params: in gamma, in beta, mix gamma, mix beta
+constexpr int OFF_X = OFF_Z + NZ * TILE_BYTES;   // 2 stages; stage s holds the x tile, then A1 in place
+constexpr int OFF_PAR = OFF_X + 2 * TILE_BYTES;  // fp32 LN params: in gamma, in beta, mix gamma, mix beta
 constexpr int OFF_BAR = OFF_PAR + 4 * 128 * 4;   // mbarriers and flags
-constexpr int SMEM_BYTES = OFF_BAR + 256;        // no alignment slack: the kernel checks the base instead
-constexpr int kThreads = 608;
+constexpr int SMEM_BYTES = OFF_BAR + 512;        // no alignment slack: the kernel checks the base instead
+static_assert(SMEM_BYTES <= 232448, "K3 shared memory exceeds the per-block limit");
+constexpr int kThreads = 736;
 constexpr int TMEM_COLS = 512;
 
 struct Params {
@@ -90,20 +95,21 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t& w_bar = bars[0];
-  uint64_t* zfull = bars + 1;
-  uint64_t* zempty = bars + 3;
-  uint64_t* xfull = bars + 5;
-  uint64_t* xempty = bars + 7;
-  uint64_t& a2full = bars[9];       // A2 written (the four LN_in warps)
-  uint64_t* a1full = bars + 21;     // [2] A1 written over x stage s (the four LN_mix warps)
-  uint64_t& a2empty = bars[10];
-  uint64_t* tfull = bars + 11;
-  uint64_t* tempty = bars + 13;
-  uint64_t& drain_bar = bars[15];
-  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 16) + 4);
-  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 18);  // [3 groups][2] group_wait verdicts
-  volatile int& x_ok_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 16) + 8);
+  uint64_t* zfull = bars + 1;       // [NZ] z loaded
+  uint64_t* zempty = bars + 4;      // [NZ] the epilogue's stores have read z'
+  uint64_t* xfull = bars + 7;       // [2]
+  uint64_t* xempty = bars + 9;      // [2] committed by the MMA that read A1 from this stage
+  uint64_t* a2full = bars + 11;     // [NZ] A2 written in place over z stage s (the four LN_in warps)
+  uint64_t* zread = bars + 14;      // [NZ] committed by the MMA that read A2 from z stage s
+  uint64_t* rfull = bars + 17;      // [NZ][2] z atom h reloaded into stage s for the epilogue
+  uint64_t* tfull = bars + 23;      // [2]
+  uint64_t* tempty = bars + 25;     // [2]
+  uint64_t* a1full = bars + 27;     // [2] A1 written over x stage s (the eight LN_mix warps)
+  uint64_t& drain_bar = bars[29];
+  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 30);
+  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 30) + 4);
+  volatile int& x_ok_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 31));
+  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 32);  // [3 groups][2] group_wait verdicts
   float* par = reinterpret_cast<float*>(smem + OFF_PAR);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -112,22 +118,22 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   if (threadIdx.x == 0) {
     abort_sh = 0;
     mbar_init(&w_bar, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NZ; ++s) {
       mbar_init(&zfull[s], 1);
       mbar_init(&zempty[s], 8);   // each epilogue warp, once its store has read the tile
-      mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 8);   // one arrival per epilogue warp
+      mbar_init(&a2full[s], 4);   // the four LN_in warps
+      mbar_init(&zread[s], 1);
+      mbar_init(&rfull[2 * s], 1);
+      mbar_init(&rfull[2 * s + 1], 1);
     }
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 8);   // one arrival per epilogue warp
       mbar_init(&xfull[s], 1);
-      mbar_init(&xempty[s], 1);  // committed by the MMA that read A1 from this stage
+      mbar_init(&xempty[s], 1);
+      // A1 and A2 have separate barriers: LN_mix may finish tile t+1 before LN_in finishes tile t
+      mbar_init(&a1full[s], 8);   // the eight LN_mix warps
     }
-    // A1 and A2 have separate barriers: LN_mix may finish tile t+1 before LN_in finishes tile t
-    // (the x tiles have their own producer), and one shared count would then mix the two tiles
-    mbar_init(&a1full[0], 4);
-    mbar_init(&a1full[1], 4);
-    mbar_init(&a2full, 4);
-    mbar_init(&a2empty, 1);
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
   }
@@ -162,13 +168,13 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      // z tiles; the x tiles have their own producer (warp 18), so an x load never waits
+      // z tiles; the x tiles have their own producer (warp 22), so an x load never waits
       // behind the long-lived z stage (held until the epilogue has stored z')
       uint32_t it = 0, nz = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         int bb, i0, j0;
         decode_tile(p, tile, bb, i0, j0);
-        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        const uint32_t s = it % NZ, ph = (it / NZ) & 1;
         if (!mbar_wait(&zempty[s], ph ^ 1, ctx, kSiteProdZ)) break;
         mbar_arrive_expect_tx(&zfull[s], TILE_BYTES);
         for (int a = 0; a < CZ / 64; ++a)
@@ -177,13 +183,13 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       }
       if (abort_sh) {
         mbar_drain(&w_bar, 0, 200000000ull);
-        for (uint32_t s = 0; s < 2; ++s) {
-          const uint32_t nza = nz > s ? (nz - s + 1) / 2 : 0;
+        for (uint32_t s = 0; s < NZ; ++s) {
+          const uint32_t nza = nz > s ? (nz - s + NZ - 1) / NZ : 0;
           if (nza) mbar_drain(&zfull[s], (nza - 1) & 1, 200000000ull);
         }
       }
     }
-  } else if (warp == 18) {
+  } else if (warp == 22) {
     // ---------------- TMA producer: x tiles ----------------
     if (lane == 0) {
       uint32_t it = 0, nx = 0;
@@ -208,12 +214,13 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     if (lane == 0) {
       bool ok = mbar_wait(&w_bar, 0, ctx, kSiteMmaW);
       uint32_t it = 0;
-      const uint32_t a2 = smem_u32(smem + OFF_A2);
       const uint32_t we = smem_u32(smem + OFF_WE), wg = smem_u32(smem + OFF_WG);
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t acc = it & 1, aph = (it >> 1) & 1;
+        const uint32_t zs = it % NZ, zph = (it / NZ) & 1;
         if (!mbar_wait(&a1full[it & 1], (it >> 1) & 1, ctx, kSiteMmaA)) break;
-        if (!mbar_wait(&a2full, it & 1, ctx, kSiteMmaA)) break;
+        if (!mbar_wait(&a2full[zs], zph, ctx, kSiteMmaA)) break;
+        const uint32_t a2 = smem_u32(smem + OFF_Z + zs * TILE_BYTES);
         if (!mbar_wait(&tempty[acc], aph ^ 1, ctx, kSiteMmaT)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + acc * 256;
@@ -229,83 +236,122 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
           umma_f16(d + CZ, sdesc_sw128(a2 + off, 16, 1024), sdesc_sw128(wg + off, 16, 1024), IDESC,
                    kk > 0 ? 1u : 0u);
         }
-        umma_commit(&xempty[it & 1]);  // A1 (over the x tile) and A2 have been read
-        umma_commit(&a2empty);
+        umma_commit(&xempty[it & 1]);  // A1 (over the x tile) and A2 (over the z tile) have been read
+        umma_commit(&zread[zs]);
         umma_commit(&tfull[acc]);
       }
       umma_commit(&drain_bar);
       mbar_drain(&drain_bar, 0, 200000000ull);
     }
-  } else if (warp < 6) {
-    // ---------------- A1 = LN_mix of each position's x column ----------------
-    const int row = threadIdx.x - 64;
+  } else if (warp < 10) {
+    // ---------------- A1 = LN_mix of each position's x column (a lane pair per position) ----------------
+    const int row = (threadIdx.x - 64) >> 1, half = threadIdx.x & 1;
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
-      // one thread waits (bounded) and shares the verdict, so the four warps always meet at
+      // one thread waits (bounded) and shares the verdict, so the eight warps always meet at
       // the named barriers below together
-      if (row == 0) x_ok_sh = mbar_wait(&xfull[s], ph, ctx, kSiteTrX) ? 1 : 0;
-      named_bar_sync(1, 128);
+      if (threadIdx.x == 64) x_ok_sh = mbar_wait(&xfull[s], ph, ctx, kSiteTrX) ? 1 : 0;
+      named_bar_sync(1, 256);
       if (!x_ok_sh) break;
       // The x tile is [channel][position] (256 B per channel).  A1's 64-channel atom h occupies
-      // exactly the bytes of x channels [64h, 64h+64), so each half of this position's column
-      // is gathered into registers, the 128 threads meet, and the half is written back as row
-      // `row` of atom h of the K-major swizzled A1 operand; then the row is normalised in place.
+      // exactly the bytes of x channels [64h, 64h+64): each thread gathers its half of this
+      // position's column into registers, the pair computes the row's statistics, the 256
+      // threads meet, and each writes its normalised half as row `row` of atom `half` of the
+      // K-major swizzled A1 operand.
       const __half* X = reinterpret_cast<const __half*>(smem + OFF_X + s * TILE_BYTES);
       uint8_t* A1 = smem + OFF_X + s * TILE_BYTES;
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        uint32_t u[32];
+      uint32_t u[32];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const int ch = 64 * h + 2 * k;
-          __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
-          u[k] = *reinterpret_cast<uint32_t*>(&h2);
-        }
-        named_bar_sync(1, 128);  // these 64 channels are in registers everywhere: overwrite them
-#pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16)
-          *reinterpret_cast<uint4*>(A1 + h * ATOM_BYTES + sw128_off(row, c16)) =
-              make_uint4(u[4 * c16], u[4 * c16 + 1], u[4 * c16 + 2], u[4 * c16 + 3]);
+      for (int k = 0; k < 32; ++k) {
+        const int ch = 64 * half + 2 * k;
+        __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
+        u[k] = *reinterpret_cast<uint32_t*>(&h2);
       }
-      ln_row128_sw128(A1, A1, ATOM_BYTES, row, p.mix_eps, LnParSmem{par + 256, par + 384});
+      // LayerNorm of the row straight from the two lanes' registers: statistics as shifted sums
+      // around the row's channel 0 (held by the half-0 lane), combined with one shuffle, then the
+      // normalised half written once, over the x bytes every thread has finished reading.
+      const float kshift = __shfl_sync(0xffffffffu, __low2float(*reinterpret_cast<const __half2*>(&u[0])), lane & ~1);
+      float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        unsigned short lo, hi;
+        split_half2(u[k], lo, hi);
+        const float2 d = make_float2(add_f16_f32(lo, -kshift), add_f16_f32(hi, -kshift));
+        s1 = __fadd2_rn(s1, d);
+        s2 = __ffma2_rn(d, d, s2);
+      }
+      float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+      t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
+      t2 += __shfl_xor_sync(0xffffffffu, t2, 1);
+      const float m1 = t1 * (1.0f / 128);
+      const float var = fmaxf(t2 * (1.0f / 128) - m1 * m1, 0.0f);
+      const float mean = kshift + m1;
+      const float rs = rsqrtf(var + p.mix_eps);
+      const float2 r2 = make_float2(rs, rs);
+      const LnParSmem mpar{par + 256, par + 384};
+      named_bar_sync(1, 256);  // every column half is in registers: overwrite the tile
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 8 channels 64 half + 8c .. at a time
+        float g[8], b[8];
+        mpar(8 * half + c, g, b);
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          unsigned short lo, hi;
+          split_half2(u[4 * c + e], lo, hi);
+          const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
+          const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
+          o[e] = pack_half2(y.x, y.y);
+        }
+        *reinterpret_cast<uint4*>(A1 + half * ATOM_BYTES + sw128_off(row, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a1full[s]);
     }
-  } else if (warp < 10) {
+  } else if (warp < 14) {
     // ---------------- A2 = LN_in of each position's z row ----------------
-    const int row = threadIdx.x - 192;
+    const int row = threadIdx.x - 320;
     uint32_t it = 0, gcount = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
-      const uint32_t s = it & 1, ph = (it >> 1) & 1;
-      if (!group_wait(&a2empty, (it & 1) ^ 1, &zfull[s], ph, ctx, kSiteTrZ, row == 0, 2, 128, gflags, gcount)) break;
-      ln_row128_sw128(smem + OFF_Z + s * TILE_BYTES, smem + OFF_A2, ATOM_BYTES, row, 1e-5f,
-                      LnParSmem{par, par + 128});
+      const uint32_t s = it % NZ, ph = (it / NZ) & 1;
+      if (!group_wait(&zfull[s], ph, nullptr, 0, ctx, kSiteTrZ, row == 0, 2, 128, gflags, gcount)) break;
+      uint8_t* Z = smem + OFF_Z + s * TILE_BYTES;
+      ln_row128_sw128(Z, Z, ATOM_BYTES, row, 1e-5f, LnParSmem{par, par + 128});  // A2 in place
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&a2full);
+      if (lane == 0) mbar_arrive(&a2full[s]);
     }
   } else {
     // ---------------- epilogue ----------------
     const int q = warp & 3;          // TMEM lane quadrant
-    const int h = (warp - 10) >> 2;  // output channels [64h, 64h+64)
+    const int h = (warp - 14) >> 2;  // output channels [64h, 64h+64)
     const int row = q * 32 + lane;
     const int jo = (q * 32) % p.jw, io = (q * 32) / p.jw;  // this warp's 32 positions in the tile
     constexpr bool has_be = HAS_BIAS, has_bg = HAS_BIAS;
     uint32_t it = 0, gcount = 0;
-    const bool leader = ((warp - 10) & 3) == 0 && lane == 0;
+    const bool leader = ((warp - 14) & 3) == 0 && lane == 0;
+    int reload_armed = -1;  // the stage whose z reload is in flight (for the abort drain)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
-      const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      const uint32_t s = it % NZ, ph = (it / NZ) & 1;
       const uint32_t acc = it & 1, aph = (it >> 1) & 1;
-      // one thread of each channel half's four warps waits, the others park on barrier 3 + h
-      if (!group_wait(&tfull[acc], aph, &zfull[s], ph, ctx, kSiteEpilogue, leader, 3 + h, 128, gflags + 2 + 2 * h,
-                      gcount))
-        break;
-      tc_fence_after();
       uint8_t* Zh = smem + OFF_Z + s * TILE_BYTES + h * ATOM_BYTES;
+      if (leader && mbar_wait(&zread[s], ph, ctx, kSiteEpilogue)) {
+        // The stage held A2 until the MMA read it: bring this half's z atom back for the residual
+        // (an L2 hit, read by this CTA microseconds before).
+        mbar_arrive_expect_tx(&rfull[2 * s + h], ATOM_BYTES);
+        tma_load_4d(Zh, &p.tm_z, &rfull[2 * s + h], h * 64, j0, i0, bb);
+        reload_armed = static_cast<int>(s);
+      }
+      // one thread of each channel half's four warps waits, the others park on barrier 3 + h
+      if (!group_wait(&tfull[acc], aph, &rfull[2 * s + h], ph, ctx, kSiteEpilogue, leader, 3 + h, 128,
+                      gflags + 2 + 2 * h, gcount))
+        break;
+      reload_armed = -1;
+      tc_fence_after();
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256 + h * 64;
 #pragma unroll 1
       for (int cc = 0; cc < 4; ++cc) {  // 16 output channels at a time
@@ -349,6 +395,9 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       }
     }
     if (lane == 0) bulk_wait<0>();
+    if (reload_armed >= 0) {  // an abort left a reload in flight: let it land before the CTA exits
+      mbar_drain(&rfull[2 * reload_armed + h], (it / NZ) & 1, 200000000ull);
+    }
   }
 
   tc_fence_before();
