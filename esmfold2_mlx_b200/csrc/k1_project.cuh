@@ -247,7 +247,55 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
         if (lane == 0) mbar_arrive(&mfull[k]);
       }
       uint8_t* A = smem + OFF_A + s * A_BYTES;
-      ln_row128_pair_sw128(A, A, ATOM_BYTES, row, half, 1e-5f, LnParSmem{par, par + CZ});
+      // LayerNorm of the row by the lane pair, each lane's half (16-byte chunks c = 2i + half of
+      // both atoms) read once into registers: shifted sums around the row's channel 0, one
+      // shuffle to combine, then the normalised values written back in place.
+      uint32_t u[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c16 = 2 * i + half;
+        const uint4 v = *reinterpret_cast<const uint4*>(A + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7));
+        u[4 * i] = v.x;
+        u[4 * i + 1] = v.y;
+        u[4 * i + 2] = v.z;
+        u[4 * i + 3] = v.w;
+      }
+      const float kshift = __shfl_sync(0xffffffffu, __low2float(*reinterpret_cast<const __half2*>(&u[0])), lane & ~1);
+      float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        unsigned short lo, hi;
+        split_half2(u[k], lo, hi);
+        const float2 d = make_float2(add_f16_f32(lo, -kshift), add_f16_f32(hi, -kshift));
+        s1 = __fadd2_rn(s1, d);
+        s2 = __ffma2_rn(d, d, s2);
+      }
+      float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+      t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
+      t2 += __shfl_xor_sync(0xffffffffu, t2, 1);
+      const float m1 = t1 * (1.0f / 128);
+      const float var = fmaxf(t2 * (1.0f / 128) - m1 * m1, 0.0f);
+      const float mean = kshift + m1;
+      const float rs = rsqrtf(var + 1e-5f);
+      const float2 r2 = make_float2(rs, rs);
+      const LnParSmem lpar{par, par + CZ};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int c16 = 2 * i + half;
+        float g[8], b[8];
+        lpar(c16, g, b);
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          unsigned short lo, hi;
+          split_half2(u[4 * i + e], lo, hi);
+          const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
+          const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
+          o[e] = pack_half2(y.x, y.y);
+        }
+        *reinterpret_cast<uint4*>(A + (c16 >> 3) * ATOM_BYTES + sw128_off(row, c16 & 7)) =
+            make_uint4(o[0], o[1], o[2], o[3]);
+      }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core's reads
       __syncwarp();
       if (lane == 0) mbar_arrive(&lnfull[s]);
