@@ -16,8 +16,11 @@
 //   warp 0     TMA: w_emit and w_gate once (resident), then per tile the z tile (3 stages,
 //              128B-swizzled position-major); warp 22 the x tile (2 stages, channel-major)
 //   warp 1     TMEM (2 x 256 columns) + MMA thread: emit (A1 x W_e) and gate (A2 x W_g)
-//   warps 2-9  A1 = fp16(LN_mix(x column)), a lane pair per position, written over the x tile
-//              it was gathered from once every thread holds its half-column in registers;
+//   warps 2-9  A1 = fp16(LN_mix(x column)), written over the x tile it was gathered from once
+//              every thread holds its part of the columns in registers.  With jw >= 64 (XSW)
+//              the x tile arrives as two 128B-swizzled [channel][64 positions] halves and is
+//              transposed by ldmatrix.trans (four lanes per position, conflict-free), A1
+//              written by stmatrix; otherwise a lane pair per position gathers 2-byte values;
 //   warps 10-13 A2 = fp16(LN_in(z row)), in place over the z stage; both concurrently, both
 //              K-major 128B-swizzled UMMA operands.  A2 in place (instead of one separate A2
 //              buffer) lets LN_in run ahead of the MMA, and its 32 KB pays for a third z stage;
@@ -55,7 +58,7 @@ constexpr int TMEM_COLS = 512;
 struct Params {
   CUtensorMap tm_z;   // z [B, rows, cols, c_z]: box {64, jw, ih, 1}, 128B swizzle (load)
   CUtensorMap tm_zo;  // z_out: box {64, min(jw,32), 32/min(jw,32), 1}, 128B swizzle (per-warp store)
-  CUtensorMap tm_x;   // x [B*c, L, Lpad]: box {jw, ih, c}, no swizzle (load)
+  CUtensorMap tm_x;   // x [B*c, L, Lpad]: box {jw, ih, c}, no swizzle; XSW: box {64, 1, c}, 128B swizzle
   CUtensorMap tm_we;  // w_emit [c_z, c]: box {64, 128}
   CUtensorMap tm_wg;  // w_gate [c_z, c_z]: box {64, 128}
   const __half* ln_in_w;
@@ -83,7 +86,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
-template <bool HAS_BIAS>
+template <bool HAS_BIAS, bool XSW>
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid_constant__ Params p) {
   constexpr uint32_t IDESC = idesc_f16_f32(128, CZ, false, false);
   // All shared state lives in the dynamic buffer (no static __shared__), whose base the 128B
@@ -145,8 +148,13 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     tma_prefetch_desc(&p.tm_wg);
   }
   for (int i = threadIdx.x; i < 4 * 128; i += blockDim.x) {
-    const __half* src = i < 128 ? p.ln_in_w : i < 256 ? p.ln_in_b : i < 384 ? p.ln_mix_w : p.ln_mix_b;
-    par[i] = __half2float(src[i & 127]);
+    if (XSW && i >= 256) {  // mix parameters interleaved per channel pair: {g[2k], g[2k+1], b[2k], b[2k+1]}
+      const int k = (i - 256) >> 2, e = i & 3;
+      par[i] = __half2float(e < 2 ? p.ln_mix_w[2 * k + e] : p.ln_mix_b[2 * k + e - 2]);
+    } else {
+      const __half* src = i < 128 ? p.ln_in_w : i < 256 ? p.ln_in_b : i < 384 ? p.ln_mix_w : p.ln_mix_b;
+      par[i] = __half2float(src[i & 127]);
+    }
   }
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, TMEM_COLS);
@@ -199,7 +207,13 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
         const uint32_t s = it & 1, ph = (it >> 1) & 1;
         if (!mbar_wait(&xempty[s], ph ^ 1, ctx, kSiteProdX)) break;
         mbar_arrive_expect_tx(&xfull[s], TILE * CC * 2);
-        tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
+        if (XSW) {  // positions 0-63, then 64-127 (the tile's second half-row, or its second row)
+          tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
+          tma_load_3d(smem + OFF_X + s * TILE_BYTES + TILE_BYTES / 2, &p.tm_x, &xfull[s], p.jw == 128 ? j0 + 64 : j0,
+                      p.jw == 128 ? i0 : i0 + 1, bb * CC);
+        } else {
+          tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
+        }
         ++nx;
       }
       if (abort_sh) {
@@ -254,57 +268,130 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       if (threadIdx.x == 64) x_ok_sh = mbar_wait(&xfull[s], ph, ctx, kSiteTrX) ? 1 : 0;
       named_bar_sync(1, 256);
       if (!x_ok_sh) break;
-      // The x tile is [channel][position] (256 B per channel).  A1's 64-channel atom h occupies
-      // exactly the bytes of x channels [64h, 64h+64): each thread gathers its half of this
-      // position's column into registers, the pair computes the row's statistics, the 256
-      // threads meet, and each writes its normalised half as row `row` of atom `half` of the
-      // K-major swizzled A1 operand.
-      const __half* X = reinterpret_cast<const __half*>(smem + OFF_X + s * TILE_BYTES);
-      uint8_t* A1 = smem + OFF_X + s * TILE_BYTES;
-      uint32_t u[32];
+      if constexpr (XSW) {
+        // The x stage holds two halves of 64 tile positions, each [channel][64 positions] with
+        // 128 B per channel and the 16-byte chunk m (positions 8m..8m+7) at chunk m ^ (channel
+        // & 7).  Warp wl owns tile positions [16 wl, 16 wl + 16) = chunks m0, m0 + 1 of half
+        // wl / 4.  ldmatrix.trans of the 8 x 8 block (channels 8cb.., positions 8m..) gives lane
+        // t channels 8cb + 2(t%4), +1 of position 8m + t/4: four lanes per position, 32
+        // channels each; lane t supplies the row address of channel 32q + t.
+        const int wl = warp - 2;
+        const uint32_t xs = smem_u32(smem + OFF_X + s * TILE_BYTES);
+        const uint32_t xh = xs + (wl >> 2) * (TILE_BYTES / 2);
+        const int m0 = 2 * (wl & 3);
+        uint32_t u[2][16];  // u[mi][4q + j]: channels 32q + 8j + 2(t%4), +1 of position 16 wl + 8 mi + t/4
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        const int ch = 64 * half + 2 * k;
-        __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
-        u[k] = *reinterpret_cast<uint32_t*>(&h2);
-      }
-      // LayerNorm of the row straight from the two lanes' registers: statistics as shifted sums
-      // around the row's channel 0 (held by the half-0 lane), combined with one shuffle, then the
-      // normalised half written once, over the x bytes every thread has finished reading.
-      const float kshift = __shfl_sync(0xffffffffu, __low2float(*reinterpret_cast<const __half2*>(&u[0])), lane & ~1);
-      float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+        for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        unsigned short lo, hi;
-        split_half2(u[k], lo, hi);
-        const float2 d = make_float2(add_f16_f32(lo, -kshift), add_f16_f32(hi, -kshift));
-        s1 = __fadd2_rn(s1, d);
-        s2 = __ffma2_rn(d, d, s2);
-      }
-      float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
-      t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
-      t2 += __shfl_xor_sync(0xffffffffu, t2, 1);
-      const float m1 = t1 * (1.0f / 128);
-      const float var = fmaxf(t2 * (1.0f / 128) - m1 * m1, 0.0f);
-      const float mean = kshift + m1;
-      const float rs = rsqrtf(var + p.mix_eps);
-      const float2 r2 = make_float2(rs, rs);
-      const LnParSmem mpar{par + 256, par + 384};
-      named_bar_sync(1, 256);  // every column half is in registers: overwrite the tile
+          for (int q = 0; q < 4; ++q)
+            ldsm_x4_trans(xh + (32 * q + lane) * 128 + 16 * ((m0 + mi) ^ (lane & 7)), u[mi][4 * q], u[mi][4 * q + 1],
+                          u[mi][4 * q + 2], u[mi][4 * q + 3]);
+        // statistics of each position over its four lanes: shifted sums around its channel 0
+        // (the low half of u[mi][0] on lane t with t%4 == 0), two shuffle steps
+        float mean[2], rs[2];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 8 channels 64 half + 8c .. at a time
-        float g[8], b[8];
-        mpar(8 * half + c, g, b);
-        uint32_t o[4];
+        for (int mi = 0; mi < 2; ++mi) {
+          const float kshift =
+              __shfl_sync(0xffffffffu, __low2float(*reinterpret_cast<const __half2*>(&u[mi][0])), lane & ~3);
+          float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          unsigned short lo, hi;
-          split_half2(u[4 * c + e], lo, hi);
-          const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
-          const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
-          o[e] = pack_half2(y.x, y.y);
+          for (int k = 0; k < 16; ++k) {
+            unsigned short lo, hi;
+            split_half2(u[mi][k], lo, hi);
+            const float2 d = make_float2(add_f16_f32(lo, -kshift), add_f16_f32(hi, -kshift));
+            s1 = __fadd2_rn(s1, d);
+            s2 = __ffma2_rn(d, d, s2);
+          }
+          float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+          t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
+          t2 += __shfl_xor_sync(0xffffffffu, t2, 1);
+          t1 += __shfl_xor_sync(0xffffffffu, t1, 2);
+          t2 += __shfl_xor_sync(0xffffffffu, t2, 2);
+          const float m1 = t1 * (1.0f / 128);
+          const float var = fmaxf(t2 * (1.0f / 128) - m1 * m1, 0.0f);
+          mean[mi] = kshift + m1;
+          rs[mi] = rsqrtf(var + p.mix_eps);
         }
-        *reinterpret_cast<uint4*>(A1 + half * ATOM_BYTES + sw128_off(row, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+        named_bar_sync(1, 256);  // every x value is in registers: overwrite the tile with A1
+        // A1 (K-major, 128B-swizzled atoms of 64 channels): stmatrix of the same 8 x 8 blocks,
+        // rows = positions; lane t supplies the row address of position 16 wl + 8 mi + t%8 in
+        // chunk 4(q%2) + t/8 of atom q/2.
+        const float4* mp = reinterpret_cast<const float4*>(par + 256);  // interleaved per channel pair
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float4 gb[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) gb[j] = mp[16 * q + 4 * j + (lane & 3)];
+#pragma unroll
+          for (int mi = 0; mi < 2; ++mi) {
+            const float2 r2 = make_float2(rs[mi], rs[mi]);
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              unsigned short lo, hi;
+              split_half2(u[mi][4 * q + j], lo, hi);
+              const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean[mi]), add_f16_f32(hi, -mean[mi])), r2);
+              const float2 y = __ffma2_rn(d, make_float2(gb[j].x, gb[j].y), make_float2(gb[j].z, gb[j].w));
+              o[j] = pack_half2(y.x, y.y);
+            }
+            const uint32_t pos = 16 * wl + 8 * mi + (lane & 7);
+            stsm_x4(xs + (q >> 1) * ATOM_BYTES + pos * 128 + 16 * ((4 * (q & 1) + (lane >> 3)) ^ (lane & 7)), o[0], o[1],
+                    o[2], o[3]);
+          }
+        }
+      } else {
+        // The x tile is [channel][position] (256 B per channel).  A1's 64-channel atom h occupies
+        // exactly the bytes of x channels [64h, 64h+64): each thread gathers its half of this
+        // position's column into registers, the pair computes the row's statistics, the 256
+        // threads meet, and each writes its normalised half as row `row` of atom `half` of the
+        // K-major swizzled A1 operand.
+        const __half* X = reinterpret_cast<const __half*>(smem + OFF_X + s * TILE_BYTES);
+        uint8_t* A1 = smem + OFF_X + s * TILE_BYTES;
+        uint32_t u[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int ch = 64 * half + 2 * k;
+          __half2 h2 = __halves2half2(X[ch * TILE + row], X[(ch + 1) * TILE + row]);
+          u[k] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        // LayerNorm of the row straight from the two lanes' registers: statistics as shifted sums
+        // around the row's channel 0 (held by the half-0 lane), combined with one shuffle, then the
+        // normalised half written once, over the x bytes every thread has finished reading.
+        const float kshift = __shfl_sync(0xffffffffu, __low2float(*reinterpret_cast<const __half2*>(&u[0])), lane & ~1);
+        float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          unsigned short lo, hi;
+          split_half2(u[k], lo, hi);
+          const float2 d = make_float2(add_f16_f32(lo, -kshift), add_f16_f32(hi, -kshift));
+          s1 = __fadd2_rn(s1, d);
+          s2 = __ffma2_rn(d, d, s2);
+        }
+        float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+        t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
+        t2 += __shfl_xor_sync(0xffffffffu, t2, 1);
+        const float m1 = t1 * (1.0f / 128);
+        const float var = fmaxf(t2 * (1.0f / 128) - m1 * m1, 0.0f);
+        const float mean = kshift + m1;
+        const float rs = rsqrtf(var + p.mix_eps);
+        const float2 r2 = make_float2(rs, rs);
+        const LnParSmem mpar{par + 256, par + 384};
+        named_bar_sync(1, 256);  // every column half is in registers: overwrite the tile
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {  // 8 channels 64 half + 8c .. at a time
+          float g[8], b[8];
+          mpar(8 * half + c, g, b);
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            unsigned short lo, hi;
+            split_half2(u[4 * c + e], lo, hi);
+            const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
+            const float2 y = __ffma2_rn(d, make_float2(g[2 * e], g[2 * e + 1]), make_float2(b[2 * e], b[2 * e + 1]));
+            o[e] = pack_half2(y.x, y.y);
+          }
+          *reinterpret_cast<uint4*>(A1 + half * ATOM_BYTES + sw128_off(row, c)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
       }
       fence_proxy_async_smem();
       __syncwarp();

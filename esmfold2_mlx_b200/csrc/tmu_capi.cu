@@ -357,14 +357,19 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
     return fail(TMU_ERR_INVALID_ARGUMENT, "b_emit and b_gate must both be set or both be NULL");
   if (cz == 256) return launch_k3w(x, z, z_out, w, B, rows, cols, mix_eps, status, stream);
   const bool hb = w->b_emit != nullptr;
-  void (*kern)(k3::Params) = hb ? k3::emit_residual_kernel<true> : k3::emit_residual_kernel<false>;
+  int ih = 1, jw = 128;
+  choose_tile(rows, cols, ih, jw);
+  // jw >= 64: the x tile is loaded as two 128B-swizzled halves of 64 positions (one 128-byte
+  // row per channel each) and transposed by ldmatrix
+  const bool xsw = jw >= 64;
+  void (*kern)(k3::Params) = hb ? (xsw ? k3::emit_residual_kernel<true, true> : k3::emit_residual_kernel<true, false>)
+                                : (xsw ? k3::emit_residual_kernel<false, true> : k3::emit_residual_kernel<false, false>);
   Dev dev;
-  int st = current_device(dev, 1u << (12 + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern), k3::SMEM_BYTES);
+  int st = current_device(dev, 1ull << ((xsw ? 40 : 12) + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern),
+                          k3::SMEM_BYTES);
   if (st) return st;
   k3::Params p;
   memset(&p, 0, sizeof(p));
-  int ih = 1, jw = 128;
-  choose_tile(rows, cols, ih, jw);
   const uint64_t cp = row_pitch(cols);
   {
     const uint64_t dims[4] = {128, (uint64_t)cols, (uint64_t)rows, (uint64_t)B};
@@ -378,8 +383,9 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   {
     const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, (uint64_t)B * 128};
     const uint64_t str[2] = {cp * 2, cp * 2 * rows};
-    const uint32_t box[3] = {(uint32_t)jw, (uint32_t)ih, 128};
-    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+    const uint32_t box[3] = {xsw ? 64u : (uint32_t)jw, xsw ? 1u : (uint32_t)ih, 128};
+    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, xsw ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return st;
   }
   {
     const uint64_t dims[2] = {128, 128};

@@ -413,6 +413,23 @@ __device__ __forceinline__ float2 sigmoid_f32x2(float2 x) {
   return make_float2(rcp_approx(d.x), rcp_approx(d.y));
 }
 
+// Four 8x8 b16 matrices between shared memory and registers (lanes 8j..8j+7 give the row
+// addresses of matrix j, 16 contiguous bytes each; register j holds matrix j).  Without .trans
+// lane t holds row t/4, columns 2(t%4) and 2(t%4)+1 (the lower column in the low half); with
+// .trans it holds column t/4, rows 2(t%4) and 2(t%4)+1.
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t saddr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(saddr)
+               : "memory");
+}
+
+__device__ __forceinline__ void stsm_x4(uint32_t saddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(saddr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
+}
+
 // cvt(h) + c with one rounding (the fp16 -> fp32 conversion is exact): sm_100's mixed-precision
 // add, which saves the separate conversion instruction.
 __device__ __forceinline__ float add_f16_f32(unsigned short h, float c) {

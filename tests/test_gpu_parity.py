@@ -111,7 +111,9 @@ def test_project_gate_matches_oracle(L, B, n_pad, biases):
             assert float(got.permute(0, 2, 3, 1)[~m].abs().max()) == 0.0
 
 
-@pytest.mark.parametrize("L,B", [(76, 1), (238, 1), (146, 2)])
+# tile shapes: 76, 238 -> 8 x 16; 146 -> 4 x 32; 120 -> 1 x 128 (ragged columns); 59 -> 2 x 64
+# (ragged rows and columns); 128 -> 1 x 128 (jw >= 64 loads x as two swizzled halves)
+@pytest.mark.parametrize("L,B", [(76, 1), (238, 1), (146, 2), (120, 1), (59, 2), (128, 1)])
 @pytest.mark.parametrize("outgoing", [True, False])
 def test_emit_residual_matches_oracle(L, B, outgoing):
     trunk, z, mask, bias = _setup(L, B, seed=L + 1, biases=True)
@@ -138,7 +140,8 @@ def _exact_update(trunk, direction, bias, z, mask, outgoing):
 
 
 @pytest.mark.parametrize("L,B,n_pad,biases", [(76, 1, 0, False), (238, 1, 24, True), (146, 2, 0, False),
-                                              (33, 3, 5, True), (200, 1, 0, False)])
+                                              (33, 3, 5, True), (200, 1, 0, False), (120, 1, 8, True),
+                                              (59, 2, 3, False)])
 @pytest.mark.parametrize("outgoing", [True, False])
 def test_trimul_matches_oracle(L, B, n_pad, biases, outgoing):
     trunk, z, mask, bias = _setup(L, B, seed=L + 2, n_pad=n_pad, biases=biases)
