@@ -123,6 +123,24 @@ void choose_tile(int rows, int cols, int& ih, int& jw, int tile = 128) {
   }
 }
 
+// K3's tile: as choose_tile, but a shape with jw >= 64 (whose x tile is transposed by ldmatrix)
+// is charged 10 % less per position than the narrower shapes (2-byte gather), the measured
+// difference in K3's time per tile, so a little padding buys the faster path.
+void choose_tile_k3(int rows, int cols, int& ih, int& jw) {
+  static const int widths[5] = {128, 64, 32, 16, 8};
+  long long best = -1;
+  for (int wi : widths) {
+    const int hi = 128 / wi;
+    const long long area = static_cast<long long>((rows + hi - 1) / hi) * hi * ((cols + wi - 1) / wi) * wi;
+    const long long cost = area * (wi >= 64 ? 10 : 11);
+    if (best < 0 || cost < best) {
+      best = cost;
+      ih = hi;
+      jw = wi;
+    }
+  }
+}
+
 struct Dev {
   int id;
   int sms;
@@ -358,9 +376,11 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   if (cz == 256) return launch_k3w(x, z, z_out, w, B, rows, cols, mix_eps, status, stream);
   const bool hb = w->b_emit != nullptr;
   int ih = 1, jw = 128;
-  choose_tile(rows, cols, ih, jw);
+  choose_tile_k3(rows, cols, ih, jw);
   // jw >= 64: the x tile is loaded as two 128B-swizzled halves of 64 positions (one 128-byte
-  // row per channel each) and transposed by ldmatrix
+  // row per channel each) and transposed by ldmatrix.  (A narrower box cannot take this form:
+  // with the 128-byte swizzle, TMA pads every inner row shorter than 128 bytes to 128 bytes in
+  // shared memory, which would quadruple the x tile's footprint at jw = 16.)
   const bool xsw = jw >= 64;
   void (*kern)(k3::Params) = hb ? (xsw ? k3::emit_residual_kernel<true, true> : k3::emit_residual_kernel<true, false>)
                                 : (xsw ? k3::emit_residual_kernel<false, true> : k3::emit_residual_kernel<false, false>);
