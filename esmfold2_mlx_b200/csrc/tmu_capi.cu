@@ -123,6 +123,27 @@ void choose_tile(int rows, int cols, int& ih, int& jw, int tile = 128) {
   }
 }
 
+// K1's tile: measured per position, K1 is fastest on 1 x 128 tiles (3.1-3.7 TB/s at L = 1024-
+// 2048) and slower the narrower the tile (L = 1032: 8 x 16 tiles 1.39x the 1 x 128 cost per
+// position, 4 x 32 1.1x; L = 1544 and 2056: 8 x 16 and 4 x 32 tiles 1.4-1.8x), the channel-major
+// stores covering fewer positions per row.  Each shape is charged its relative cost per
+// position, so some padding buys the wide tiles.
+void choose_tile_k1(int rows, int cols, int& ih, int& jw) {
+  static const int widths[5] = {128, 64, 32, 16, 8};
+  static const int weight[5] = {20, 22, 25, 28, 32};  // relative cost per position, x 20
+  long long best = -1;
+  for (int w = 0; w < 5; ++w) {
+    const int wi = widths[w], hi = 128 / wi;
+    const long long area = static_cast<long long>((rows + hi - 1) / hi) * hi * ((cols + wi - 1) / wi) * wi;
+    const long long cost = area * weight[w];
+    if (best < 0 || cost < best) {
+      best = cost;
+      ih = hi;
+      jw = wi;
+    }
+  }
+}
+
 // K3's tile: as choose_tile, but a shape with jw >= 64 (whose x tile is transposed by ldmatrix)
 // is charged 10 % less per position than the narrower shapes (2-byte gather), the measured
 // difference in K3's time per tile, so a little padding buys the faster path.
@@ -242,7 +263,7 @@ int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, cons
   k1::Params p;
   memset(&p, 0, sizeof(p));
   int ih = 1, jw = 128;
-  choose_tile(g.rows, g.cols, ih, jw);
+  choose_tile_k1(g.rows, g.cols, ih, jw);
   const uint64_t cp = row_pitch(g.cols);
   {
     const uint64_t dims[4] = {128, (uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B};

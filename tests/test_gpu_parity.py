@@ -141,7 +141,7 @@ def _exact_update(trunk, direction, bias, z, mask, outgoing):
 
 @pytest.mark.parametrize("L,B,n_pad,biases", [(76, 1, 0, False), (238, 1, 24, True), (146, 2, 0, False),
                                               (33, 3, 5, True), (200, 1, 0, False), (120, 1, 8, True),
-                                              (59, 2, 3, False)])
+                                              (59, 2, 3, False), (12, 2, 3, True)])
 @pytest.mark.parametrize("outgoing", [True, False])
 def test_trimul_matches_oracle(L, B, n_pad, biases, outgoing):
     trunk, z, mask, bias = _setup(L, B, seed=L + 2, n_pad=n_pad, biases=biases)
