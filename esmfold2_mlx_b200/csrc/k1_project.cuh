@@ -203,17 +203,17 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
         const uint32_t s = it & 1, ph = (it >> 1) & 1;
         if (!mbar_wait(&lnfull[s], ph, ctx, kSiteMmaLn)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t n_base = smem_u32(smem + OFF_A + s * A_BYTES);
+        const uint64_t n_desc = sdesc_sw128(smem_u32(smem + OFF_A + s * A_BYTES), 16, 1024);
         for (int x = 0; x < 2; ++x) {  // x = 0: a (slots 0, 1), x = 1: b (slots 2, 3)
           if (!mbar_wait(&tempty[x], (it & 1) ^ 1, ctx, kSiteMmaSlot)) { ok = false; break; }
           tc_fence_after();
           for (int h = 0; h < 2; ++h) {  // h = 0 signal rows, h = 1 gate rows: slot 2x + h
-            const uint32_t w_base = smem_u32(smem + OFF_W + (2 * x + h) * WBLOCK_BYTES);
+            const uint64_t w_desc = sdesc_sw128(smem_u32(smem + OFF_W + (2 * x + h) * WBLOCK_BYTES), 16, 1024);
 #pragma unroll
             for (int kk = 0; kk < CZ / 16; ++kk) {
               const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-              umma_f16(tmem_base + (2 * x + h) * 128, sdesc_sw128(w_base + off, 16, 1024),
-                       sdesc_sw128(n_base + off, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+              umma_f16(tmem_base + (2 * x + h) * 128, sdesc_add(w_desc, off), sdesc_add(n_desc, off), IDESC,
+                       kk > 0 ? 1u : 0u);
             }
           }
           umma_commit(&tfull[x]);

@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     if (lane == 0) {
       bool ok = mbar_wait(&w_bar, 0, ctx, kSiteMmaW);
       uint32_t it = 0;
-      const uint32_t we = smem_u32(smem + OFF_WE), wg = smem_u32(smem + OFF_WG);
+      const uint64_t wed = sdesc_sw128(smem_u32(smem + OFF_WE), 16, 1024), wgd = sdesc_sw128(smem_u32(smem + OFF_WG), 16, 1024);
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t acc = it & 1, aph = (it >> 1) & 1;
         const uint32_t zs = it % NZ, zph = (it / NZ) & 1;
@@ -239,16 +239,16 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
         tc_fence_after();
         const uint32_t d = tmem_base + acc * 256;
         const uint32_t a1 = smem_u32(smem + OFF_X + (it & 1) * TILE_BYTES);
+        const uint64_t a1d = sdesc_sw128(a1, 16, 1024), a2d = sdesc_sw128(a2, 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < CC / 16; ++kk) {
           const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-          umma_f16(d, sdesc_sw128(a1 + off, 16, 1024), sdesc_sw128(we + off, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+          umma_f16(d, sdesc_add(a1d, off), sdesc_add(wed, off), IDESC, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < CZ / 16; ++kk) {
           const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-          umma_f16(d + CZ, sdesc_sw128(a2 + off, 16, 1024), sdesc_sw128(wg + off, 16, 1024), IDESC,
-                   kk > 0 ? 1u : 0u);
+          umma_f16(d + CZ, sdesc_add(a2d, off), sdesc_add(wgd, off), IDESC, kk > 0 ? 1u : 0u);
         }
         umma_commit(&xempty[it & 1]);  // A1 (over the x tile) and A2 (over the z tile) have been read
         umma_commit(&zread[zs]);

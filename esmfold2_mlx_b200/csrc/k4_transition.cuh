@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
         const uint32_t tb = it & 1, tph = (it >> 1) & 1;
         const uint32_t ab = it % C::NACC, aph = (it / C::NACC) & 1;
         if (!(ok = mbar_wait(&hfull[tb], tph, ctx, kSiteMmaH))) break;
-        const uint32_t hbase = smem_u32(smem + C::OFF_H + tb * C::TILE_BYTES);
+        const uint64_t hdesc = sdesc_sw128(smem_u32(smem + C::OFF_H + tb * C::TILE_BYTES), 16, 1024);
         const uint32_t acc = tmem_base + ab * CZ;
         // GEMM1 runs two chunks ahead of GEMM2: G1(j) needs only that its TMEM buffer has been
         // read (by the activation of chunk j-2), so the tensor core computes chunk j while
@@ -284,18 +284,18 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
               const uint32_t s = r % NW, ph = (r / NW) & 1;
               if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
               tc_fence_after();
-              const uint32_t wb = smem_u32(smem + C::OFF_W + s * W_BYTES);
+              const uint64_t wdesc = sdesc_sw128(smem_u32(smem + C::OFF_W + s * W_BYTES), 16, 1024);
               if (SWIGLU) {  // K atom k: D1[:, 0:64] = x1, D1[:, 64:128] = x2
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
-                  umma_f16(d, sdesc_sw128(hbase + k * ATOM_BYTES + kk * 32, 16, 1024),
-                           sdesc_sw128(wb + kk * 32, 16, 1024), IDESC1, (k > 0 || kk > 0) ? 1u : 0u);
+                  umma_f16(d, sdesc_add(hdesc, k * ATOM_BYTES + kk * 32), sdesc_add(wdesc, kk * 32), IDESC1,
+                           (k > 0 || kk > 0) ? 1u : 0u);
               } else {       // K atoms 2k, 2k + 1
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                   const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
-                  umma_f16(d, sdesc_sw128(hbase + (2 * k + ka) * ATOM_BYTES + kb, 16, 1024),
-                           sdesc_sw128(wb + ka * (W_BYTES / 2) + kb, 16, 1024), IDESC1, (k > 0 || kk > 0) ? 1u : 0u);
+                  umma_f16(d, sdesc_add(hdesc, (2 * k + ka) * ATOM_BYTES + kb), sdesc_add(wdesc, ka * (W_BYTES / 2) + kb),
+                           IDESC1, (k > 0 || kk > 0) ? 1u : 0u);
                 }
               }
               umma_commit(&wempty[s]);
@@ -309,16 +309,16 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
             const uint32_t c = gc + j - 2, b = c & 1, cph = (c >> 1) & 1;
             if (j == 2 && !(ok = mbar_wait(&accempty[ab], aph ^ 1, ctx, kSiteMmaAcc))) break;
             if (!(ok = mbar_wait(&sfull[b], cph, ctx, kSiteMmaS))) break;
-            const uint32_t sb = smem_u32(smem + C::OFF_S + b * S_BYTES);
+            const uint64_t sdesc = sdesc_sw128(smem_u32(smem + C::OFF_S + b * S_BYTES), 16, 1024);
             for (int m = 0; m < G2_ITEMS; ++m) {  // output channels [128 m, 128 m + 128)
               const uint32_t s = r % NW, ph = (r / NW) & 1;
               if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
               tc_fence_after();
-              const uint32_t wb = smem_u32(smem + C::OFF_W + s * W_BYTES);
+              const uint64_t wdesc = sdesc_sw128(smem_u32(smem + C::OFF_W + s * W_BYTES), 16, 1024);
 #pragma unroll
               for (int kk = 0; kk < CHUNK / 16; ++kk)
-                umma_f16(acc + m * 128, sdesc_sw128(sb + kk * 32, 16, 1024), sdesc_sw128(wb + kk * 32, 16, 1024),
-                         IDESC2, (j > 2 || kk > 0) ? 1u : 0u);
+                umma_f16(acc + m * 128, sdesc_add(sdesc, kk * 32), sdesc_add(wdesc, kk * 32), IDESC2,
+                         (j > 2 || kk > 0) ? 1u : 0u);
               umma_commit(&wempty[s]);
               ++r;
             }
