@@ -421,11 +421,14 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
             uint32_t o[8];
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float2 a = round_f16x2(make_float2(__uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1])));
-              const float2 c = round_f16x2(make_float2(__uint_as_float(y[2 * e]), __uint_as_float(y[2 * e + 1])));
-              const float2 sg = round_f16x2(sigmoid_f32x2(a));
-              const float2 r = __fmul2_rn(round_f16x2(__fmul2_rn(a, sg)), c);
-              o[e] = pack_half2(r.x, r.y);
+              // a = fp16(x1), c = fp16(x2), sg = fp16(sigmoid(a)); the product of two fp16 values
+              // is exact in fp32, so fp16(a * sg) and fp16(t * c) are single correctly rounded
+              // fp16 multiplies, bit-identical to rounding the fp32 products
+              const __half2 a = __floats2half2_rn(__uint_as_float(x[2 * e]), __uint_as_float(x[2 * e + 1]));
+              const __half2 c = __floats2half2_rn(__uint_as_float(y[2 * e]), __uint_as_float(y[2 * e + 1]));
+              const float2 sf = sigmoid_f32x2(__half22float2(a));
+              const __half2 r = __hmul2_rn(__hmul2_rn(a, __floats2half2_rn(sf.x, sf.y)), c);
+              o[e] = *reinterpret_cast<const uint32_t*>(&r);
             }
             *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * hq)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * hq + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
