@@ -127,15 +127,17 @@ void choose_tile(int rows, int cols, int& ih, int& jw, int tile = 128) {
 // 2048) and slower the narrower the tile (L = 1032: 8 x 16 tiles 1.39x the 1 x 128 cost per
 // position, 4 x 32 1.1x; L = 1544 and 2056: 8 x 16 and 4 x 32 tiles 1.4-1.8x), the channel-major
 // stores covering fewer positions per row.  Each shape is charged its relative cost per
-// position, so some padding buys the wide tiles.
+// position, so some padding buys the wide tiles.  Below 512 x 512 positions the outputs stay in
+// L2 and the least padding measured best (L = 238: 8 x 16 tiles 2 % faster than 1 x 128).
 void choose_tile_k1(int rows, int cols, int& ih, int& jw) {
   static const int widths[5] = {128, 64, 32, 16, 8};
   static const int weight[5] = {20, 22, 25, 28, 32};  // relative cost per position, x 20
+  const bool dram = static_cast<long long>(rows) * cols >= 512ll * 512;
   long long best = -1;
   for (int w = 0; w < 5; ++w) {
     const int wi = widths[w], hi = 128 / wi;
     const long long area = static_cast<long long>((rows + hi - 1) / hi) * hi * ((cols + wi - 1) / wi) * wi;
-    const long long cost = area * weight[w];
+    const long long cost = area * (dram ? weight[w] : 1);
     if (best < 0 || cost < best) {
       best = cost;
       ih = hi;
@@ -146,15 +148,17 @@ void choose_tile_k1(int rows, int cols, int& ih, int& jw) {
 
 // K1W's tile (64 positions): the same effect, measured: 8 x 8 tiles cost 1.21x the 1 x 64 cost
 // per position at L = 1032 (c_z = 256).  Charged 1, 1.1, 1.25, 1.4 per position from the widest
-// shape (1 x 64) to the narrowest (8 x 8).
+// shape (1 x 64) to the narrowest (8 x 8), from 512 x 512 positions up (as K1; L = 238: the
+// least padding 3 % faster).
 void choose_tile_k1w(int rows, int cols, int& ih, int& jw) {
   static const int widths[4] = {64, 32, 16, 8};
   static const int weight[4] = {20, 22, 25, 28};  // relative cost per position, x 20
+  const bool dram = static_cast<long long>(rows) * cols >= 512ll * 512;
   long long best = -1;
   for (int w = 0; w < 4; ++w) {
     const int wi = widths[w], hi = 64 / wi;
     const long long area = static_cast<long long>((rows + hi - 1) / hi) * hi * ((cols + wi - 1) / wi) * wi;
-    const long long cost = area * weight[w];
+    const long long cost = area * (dram ? weight[w] : 1);
     if (best < 0 || cost < best) {
       best = cost;
       ih = hi;

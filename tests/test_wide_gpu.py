@@ -43,9 +43,10 @@ def _w(trunk, direction, bias, fp16=True):
     return ops.TrimulWeights.from_module(tri, DEV, b), orc.trimul_params(tri, fp16, b)
 
 
-# K1W tile shapes: 64, 100 -> 1 x 64; 146 -> 2 x 32; 12 -> 4 x 16; 37 -> 8 x 8
+# K1W tile shapes (least padding below 512 x 512): 64 -> 1 x 64; 96 -> 2 x 32; 12 -> 4 x 16;
+# 100, 146, 37 -> 8 x 8
 @pytest.mark.parametrize("L,B,n_pad,biases", [(64, 1, 0, False), (100, 1, 9, True), (146, 2, 0, False),
-                                              (37, 3, 5, True), (12, 2, 3, False)])
+                                              (37, 3, 5, True), (12, 2, 3, False), (96, 1, 0, True)])
 def test_wide_project_gate_matches_oracle(L, B, n_pad, biases):
     trunk, z, mask, bias = _setup(L, B, seed=L, n_pad=n_pad, biases=biases)
     w, p = _w(trunk, "out", bias)
