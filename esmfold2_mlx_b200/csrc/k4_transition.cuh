@@ -10,11 +10,14 @@
 //   z' = fp16(z + s @ w3^T)                    w3 [c_z, h]; one rounding (mx.addmm)
 //
 // Tile = 128 positions (ih x jw block of the grid); TMEM lane = position.  The hidden dimension
-// is processed in chunks of 64: GEMM1 of chunk k (D1 = h W12_k^T: N = 128 for SwiGLU, whose B
-// operand stacks the chunk's 64 x1 rows over its 64 x2 rows, N = 64 for ReLU) lands in one of
-// two TMEM chunk buffers, the activation warps turn it into the fp16 A operand s_k in shared
-// memory, and GEMM2 accumulates D2 += s_k W3_k^T (N = c_z as 128-column MMAs, K = 64) in a
-// per-tile TMEM accumulator.  The MMA thread issues G1(0), G1(1), G1(2), G2(0), G1(3), G2(1), ...
+// is processed in chunks: GEMM1 of chunk k (D1 = h W12_k^T, N = 128: for SwiGLU a chunk is 64
+// hidden units, the B operand stacking its 64 x1 rows over its 64 x2 rows; for ReLU a chunk is
+// 128 hidden units, its first 64 rows over its next 64, so GEMM1 is N = 128 MMAs, which one
+// issuing thread drives at the tensor core's rate where N = 64 MMAs reach about two thirds of
+// it) lands in one of two TMEM chunk buffers, the activation warps turn it into the fp16 A
+// operand s in shared memory (SwiGLU: one 64-wide s per chunk; ReLU: two, one per s buffer),
+// and GEMM2 accumulates D2 += s W3^T (N = c_z as 128-column MMAs, K = 64 per s) in a per-tile
+// TMEM accumulator.  The MMA thread issues G1(0), G1(1), G1(2), G2(0), G1(3), G2(1), ...
 // (GEMM1 two chunks ahead), so the tensor core computes the next chunks while the current ones
 // are being activated.  The weights (256 KB - 1.5 MB) do not fit beside the tiles, so they
 // stream from L2 through a 4-stage ring of 16 KB items in exactly that order.
@@ -48,7 +51,7 @@ namespace tmu {
 namespace k4 {
 
 constexpr int TILE = 128;
-constexpr int CHUNK = 64;                        // hidden units per chunk
+constexpr int CHUNK = 64;                        // hidden units per s buffer (a SwiGLU chunk; half a ReLU chunk)
 constexpr int ATOM_BYTES = TILE * 128;           // 128 rows x 128 B
 constexpr int S_BYTES = TILE * CHUNK * 2;        // 16 KB: one chunk of s
 constexpr int W_BYTES = 16384;                   // one ring item
@@ -110,13 +113,15 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 template <int CZ, bool SWIGLU, int MODE = kModeTile>
 __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_constant__ Params p) {
   using C = Cfg<CZ, MODE>;
-  constexpr uint32_t IDESC1 = idesc_f16_f32(128, SWIGLU ? 2 * CHUNK : CHUNK, false, false);
+  constexpr uint32_t IDESC1 = idesc_f16_f32(128, 2 * CHUNK, false, false);
   constexpr uint32_t IDESC2 = idesc_f16_f32(128, 128, false, false);
-  // Ring items per chunk.  GEMM1, SwiGLU: one per 64-channel K atom, holding that atom of the
-  // chunk's 64 x1 rows and then of its 64 x2 rows (one N = 128 B operand).  GEMM1, ReLU: one per
-  // two K atoms of the chunk's 64 rows (N = 64).  GEMM2: one per 128 output channels.
-  constexpr int G1_ITEMS = SWIGLU ? C::KATOMS : C::KATOMS / 2;
+  // Ring items per chunk.  GEMM1: one per 64-channel K atom, holding that atom of the chunk's
+  // first 64 B rows and then of its next 64 (SwiGLU: x1 rows, x2 rows; ReLU: hidden units
+  // 128k .. 128k+63, 128k+64 .. 128k+127): one N = 128 B operand.  GEMM2: one per 128 output
+  // channels and s (NQ s per chunk).
+  constexpr int G1_ITEMS = C::KATOMS;
   constexpr int G2_ITEMS = CZ / 128;
+  constexpr int NQ = SWIGLU ? 1 : 2;
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x4ff;
@@ -140,6 +145,11 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
   volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 29) + 4);
   volatile int* gflags = reinterpret_cast<volatile int*>(bars + 30);  // [4 groups][2] group_wait verdicts
   uint64_t* rfull = bars + 34;      // [2] c_z = 256: z reloaded for the epilogue
+  // ReLU: GEMM2 of chunk c releases s buffer q on semptyq[2q + (c & 1)].  Every ReLU chunk uses
+  // both s buffers, and the activation of chunk c may start while GEMM2 of chunk c - 2 still
+  // runs, so one barrier per buffer would let its parity wait see a phase two back as done;
+  // split by chunk parity, each barrier advances once per two chunks.
+  uint64_t* semptyq = bars + 36;    // [4]
   float* par = reinterpret_cast<float*>(smem + C::OFF_PAR);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -165,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
       mbar_init(&accempty[s], 4);  // the four epilogue warps
       mbar_init(&rfull[s], 1);
     }
+    for (int s = 0; s < 4; ++s) mbar_init(&semptyq[s], 1);
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
   }
@@ -208,11 +219,11 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
           for (int k = 0; ok && j < n && k < G1_ITEMS; ++k) {  // w12 rows of chunk j
             if (SWIGLU)  // K atom k of the x1 rows over K atom k of the x2 rows
               ok = put(&p.tm_w12, k * 64, j * CHUNK, k * 64, p.hidden + j * CHUNK, true);
-            else         // K atoms 2k and 2k + 1 of the chunk's rows
-              ok = put(&p.tm_w12, 2 * k * 64, j * CHUNK, (2 * k + 1) * 64, j * CHUNK, true);
+            else         // K atom k of rows 128j .. 128j+63 over rows 128j+64 .. (zero past h)
+              ok = put(&p.tm_w12, k * 64, 2 * j * CHUNK, k * 64, (2 * j + 1) * CHUNK, true);
           }
-          for (int m = 0; ok && j >= 2 && m < G2_ITEMS; ++m)  // w3[128 m .. 128 m + 127, chunk j-2]
-            ok = put(&p.tm_w3, (j - 2) * CHUNK, m * 128, 0, 0, false);
+          for (int q = 0; ok && j >= 2 && q < NQ; ++q)  // w3[128 m .. 128 m + 127, s q of chunk j-2]
+            for (int m = 0; ok && m < G2_ITEMS; ++m) ok = put(&p.tm_w3, (NQ * (j - 2) + q) * CHUNK, m * 128, 0, 0, false);
         }
       }
       if (abort_sh) {  // drain the loads still in flight before the CTA exits
@@ -285,19 +296,11 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
               if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
               tc_fence_after();
               const uint64_t wdesc = sdesc_sw128(smem_u32(smem + C::OFF_W + s * W_BYTES), 16, 1024);
-              if (SWIGLU) {  // K atom k: D1[:, 0:64] = x1, D1[:, 64:128] = x2
+              // K atom k: D1[:, 0:64] = x1 (ReLU: the chunk's first 64), D1[:, 64:128] = x2 (its next 64)
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                  umma_f16(d, sdesc_add(hdesc, k * ATOM_BYTES + kk * 32), sdesc_add(wdesc, kk * 32), IDESC1,
-                           (k > 0 || kk > 0) ? 1u : 0u);
-              } else {       // K atoms 2k, 2k + 1
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                  const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
-                  umma_f16(d, sdesc_add(hdesc, (2 * k + ka) * ATOM_BYTES + kb), sdesc_add(wdesc, ka * (W_BYTES / 2) + kb),
-                           IDESC1, (k > 0 || kk > 0) ? 1u : 0u);
-                }
-              }
+              for (int kk = 0; kk < 4; ++kk)
+                umma_f16(d, sdesc_add(hdesc, k * ATOM_BYTES + kk * 32), sdesc_add(wdesc, kk * 32), IDESC1,
+                         (k > 0 || kk > 0) ? 1u : 0u);
               umma_commit(&wempty[s]);
               ++r;
             }
@@ -308,22 +311,28 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
           if (j >= 2) {  // GEMM2 of chunk gc + j - 2
             const uint32_t c = gc + j - 2, b = c & 1, cph = (c >> 1) & 1;
             if (j == 2 && !(ok = mbar_wait(&accempty[ab], aph ^ 1, ctx, kSiteMmaAcc))) break;
-            if (!(ok = mbar_wait(&sfull[b], cph, ctx, kSiteMmaS))) break;
-            const uint64_t sdesc = sdesc_sw128(smem_u32(smem + C::OFF_S + b * S_BYTES), 16, 1024);
-            for (int m = 0; m < G2_ITEMS; ++m) {  // output channels [128 m, 128 m + 128)
-              const uint32_t s = r % NW, ph = (r / NW) & 1;
-              if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
-              tc_fence_after();
-              const uint64_t wdesc = sdesc_sw128(smem_u32(smem + C::OFF_W + s * W_BYTES), 16, 1024);
+            for (int q = 0; ok && q < NQ; ++q) {
+              // SwiGLU: the chunk's s is in buffer c & 1; ReLU: its half q is in buffer q (every
+              // chunk uses both)
+              const uint32_t sb = SWIGLU ? b : q, sph = SWIGLU ? cph : (c & 1);
+              if (!(ok = mbar_wait(&sfull[sb], sph, ctx, kSiteMmaS))) break;
+              const uint64_t sdesc = sdesc_sw128(smem_u32(smem + C::OFF_S + sb * S_BYTES), 16, 1024);
+              for (int m = 0; m < G2_ITEMS; ++m) {  // output channels [128 m, 128 m + 128)
+                const uint32_t s = r % NW, ph = (r / NW) & 1;
+                if (!(ok = mbar_wait(&wfull[s], ph, ctx, kSiteMmaW))) break;
+                tc_fence_after();
+                const uint64_t wdesc = sdesc_sw128(smem_u32(smem + C::OFF_W + s * W_BYTES), 16, 1024);
 #pragma unroll
-              for (int kk = 0; kk < CHUNK / 16; ++kk)
-                umma_f16(acc + m * 128, sdesc_add(sdesc, kk * 32), sdesc_add(wdesc, kk * 32), IDESC2,
-                         (j > 2 || kk > 0) ? 1u : 0u);
-              umma_commit(&wempty[s]);
-              ++r;
+                for (int kk = 0; kk < CHUNK / 16; ++kk)
+                  umma_f16(acc + m * 128, sdesc_add(sdesc, kk * 32), sdesc_add(wdesc, kk * 32), IDESC2,
+                           (j > 2 || q > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&wempty[s]);
+                ++r;
+              }
+              if (!ok) break;
+              umma_commit(SWIGLU ? &sempty[sb] : &semptyq[2 * q + (c & 1)]);
             }
             if (!ok) break;
-            umma_commit(&sempty[b]);
           }
         }
         if (!ok) break;
@@ -380,27 +389,40 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
         const uint32_t d = tmem_base + tl + 256 + b * 128;
         uint8_t* S = smem + C::OFF_S + b * S_BYTES;
         if (!SWIGLU) {
-          // ReLU: load and activate the whole chunk, and only then wait for the s buffer (GEMM2 of
-          // chunk gc - 2 done reading it), so that wait overlaps this warp's own work.
-          uint32_t x[32], y[32];  // hidden units [0, 32) and [32, 64) of the chunk
-          tmem_ld32(d, x);
-          tmem_ld32(d + 32, y);
-          tmem_wait_ld2(x, y);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&d1empty[b]);
-          uint32_t o[32];
+          // ReLU: the chunk's 128 hidden units in two halves of 64, half q into s buffer q.  Each
+          // half is loaded and activated before waiting for its s buffer (GEMM2 of the previous
+          // chunk done reading it), so the wait overlaps this warp's own work.
+          for (int q = 0; q < 2; ++q) {
+            uint32_t x[32], y[32];  // hidden units [64q, 64q + 32) and [64q + 32, 64q + 64) of the chunk
+            tmem_ld32(d + 64 * q, x);
+            tmem_ld32(d + 64 * q + 32, y);
+            tmem_wait_ld2(x, y);
+            if (q == 1) {  // the chunk buffer has been read: hand it back
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&d1empty[b]);
+            }
+            uint32_t o[32];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {  // relu(fp16(v)) == fp16(relu(v)): one rounding
-            o[e] = pack_half2(fmaxf(__uint_as_float(x[2 * e]), 0.0f), fmaxf(__uint_as_float(x[2 * e + 1]), 0.0f));
-            o[16 + e] = pack_half2(fmaxf(__uint_as_float(y[2 * e]), 0.0f), fmaxf(__uint_as_float(y[2 * e + 1]), 0.0f));
+            for (int e = 0; e < 16; ++e) {  // relu(fp16(v)) == fp16(relu(v)): one rounding
+              o[e] = pack_half2(fmaxf(__uint_as_float(x[2 * e]), 0.0f), fmaxf(__uint_as_float(x[2 * e + 1]), 0.0f));
+              o[16 + e] = pack_half2(fmaxf(__uint_as_float(y[2 * e]), 0.0f), fmaxf(__uint_as_float(y[2 * e + 1]), 0.0f));
+            }
+            // buffer q is used by every chunk: wait for the previous chunk's GEMM2 of it (phase
+            // (gc - 1) / 2 of its barrier for chunk parity (gc - 1) & 1)
+            if (gc > 0 && !(ok = group_wait(&semptyq[2 * q + ((gc - 1) & 1)], ((gc - 1) >> 1) & 1, nullptr, 0, ctx,
+                                            kSiteAct, leader, 1 + g, 128, gflags + 2 * g, gcount)))
+              break;
+            uint8_t* Sq = smem + C::OFF_S + q * S_BYTES;
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8)
+              *reinterpret_cast<uint4*>(Sq + sw128_off(row, c8)) =
+                  make_uint4(o[4 * c8], o[4 * c8 + 1], o[4 * c8 + 2], o[4 * c8 + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sfull[q]);
           }
-          if (!(ok = group_wait(&sempty[b], cph ^ 1, nullptr, 0, ctx, kSiteAct, leader, 1 + g, 128, gflags + 2 * g,
-                                gcount)))
-            break;
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8)
-            *reinterpret_cast<uint4*>(S + sw128_off(row, c8)) = make_uint4(o[4 * c8], o[4 * c8 + 1], o[4 * c8 + 2], o[4 * c8 + 3]);
+          if (!ok) break;
         } else {
           // SwiGLU: the sigmoid makes this the longer computation; holding all 64 results would
           // spill, so wait for the s buffer first and store 16 hidden units at a time.
@@ -433,10 +455,10 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
             *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * hq)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4*>(S + sw128_off(row, 2 * hq + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
           }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sfull[b]);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sfull[b]);
       }
     }
   } else {

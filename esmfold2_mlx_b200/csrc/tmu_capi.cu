@@ -637,7 +637,9 @@ int launch_k4(const void* z, void* z_out, const tmu_transition_weights* w, int B
   p.ln_w = static_cast<const __half*>(w->ln_w);
   p.ln_b = static_cast<const __half*>(w->ln_b);
   p.hidden = hidden;
-  p.nchunk = hidden / k4::CHUNK;
+  // SwiGLU chunks are 64 hidden units, ReLU chunks 128 (a last chunk past h reads zero rows
+  // and zero w3 columns, which add exact zeros)
+  p.nchunk = swiglu ? hidden / k4::CHUNK : (hidden + 2 * k4::CHUNK - 1) / (2 * k4::CHUNK);
   p.L = L;
   p.ih = ih;
   p.jw = jw;
