@@ -149,17 +149,14 @@ __global__ void __launch_bounds__(kThreads, 1) contract_kernel(const __grid_cons
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + s * C::STAGE_BYTES);
           const uint32_t b_base = a_base + C::A_BYTES;
+          // K-major: 16-element K steps 32 B apart (LBO unused); MN-major: 2 KB apart, 8 KB between
+          // 64-wide M/N groups
+          const uint64_t a0 = MN_MAJOR ? sdesc_sw128(a_base, 8192, 1024) : sdesc_sw128(a_base, 16, 1024);
+          const uint64_t b0 = MN_MAJOR ? sdesc_sw128(b_base, 8192, 1024) : sdesc_sw128(b_base, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
-            uint64_t adesc, bdesc;
-            if (!MN_MAJOR) {
-              adesc = sdesc_sw128(a_base + kk * 32, 16, 1024);
-              bdesc = sdesc_sw128(b_base + kk * 32, 16, 1024);
-            } else {
-              adesc = sdesc_sw128(a_base + kk * 2048, 8192, 1024);
-              bdesc = sdesc_sw128(b_base + kk * 2048, 8192, 1024);
-            }
-            umma_f16(dtm, adesc, bdesc, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            const uint32_t step = MN_MAJOR ? kk * 2048 : kk * 32;
+            umma_f16(dtm, sdesc_add(a0, step), sdesc_add(b0, step), IDESC, (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit(&empty_bar[s]);  // the stage is free once these MMAs have read it
         }

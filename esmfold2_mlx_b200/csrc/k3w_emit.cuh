@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
     if (lane == 0) {
       bool ok = mbar_wait(&w_bar, 0, ctx, kSiteMmaW);
       uint32_t it = 0;
-      const uint32_t we = smem_u32(smem + OFF_WE), wg = smem_u32(smem + OFF_WG);
+      const uint64_t wed = sdesc_sw128(smem_u32(smem + OFF_WE), 16, 1024), wgd = sdesc_sw128(smem_u32(smem + OFF_WG), 16, 1024);
       for (int tile = blockIdx.x; ok && tile < p.num_tiles; tile += gridDim.x, ++it) {
         const uint32_t s = it & 1, ph = (it >> 1) & 1;
         const uint32_t slot = it & 3, sph = (it >> 2) & 1;
@@ -196,19 +196,19 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
         if (!mbar_wait(&tempty[slot], sph ^ 1, ctx, kSiteMmaT)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + slot * 64;
-        const uint32_t a1 = smem_u32(smem + OFF_X + s * TILE_BYTES);
-        const uint32_t a2 = smem_u32(smem + OFF_A2 + s * TILE_BYTES);
+        const uint64_t a1d = sdesc_sw128(smem_u32(smem + OFF_X + s * TILE_BYTES), 16, 1024);
+        const uint64_t a2d = sdesc_sw128(smem_u32(smem + OFF_A2 + s * TILE_BYTES), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
           const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
-          umma_f16(d, sdesc_sw128(we + ka * WATOM_BYTES + kb, 16, 1024),
-                   sdesc_sw128(a1 + ka * ATOM_BYTES + kb, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+          umma_f16(d, sdesc_add(wed, ka * WATOM_BYTES + kb), sdesc_add(a1d, ka * ATOM_BYTES + kb), IDESC,
+                   kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
           const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
-          umma_f16(d + TILE, sdesc_sw128(wg + ka * WATOM_BYTES + kb, 16, 1024),
-                   sdesc_sw128(a2 + ka * ATOM_BYTES + kb, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+          umma_f16(d + TILE, sdesc_add(wgd, ka * WATOM_BYTES + kb), sdesc_add(a2d, ka * ATOM_BYTES + kb), IDESC,
+                   kk > 0 ? 1u : 0u);
         }
         umma_commit(&xempty[s]);   // A1 has been read
         umma_commit(&a2empty[s]);  // A2 has been read

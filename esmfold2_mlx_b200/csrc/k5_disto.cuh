@@ -160,14 +160,15 @@ __global__ void __launch_bounds__(kThreads, 1) disto_kernel(const __grid_constan
         if (!(ok = mbar_wait(&zfull[s], ph, ctx, kSiteMmaZ))) break;
         if (!(ok = mbar_wait(&accempty[b], bph ^ 1, ctx, kSiteMmaAcc))) break;
         tc_fence_after();
-        const uint32_t zb = smem_u32(smem + C::OFF_Z + s * C::STAGE_BYTES);
+        const uint64_t zd = sdesc_sw128(smem_u32(smem + C::OFF_Z + s * C::STAGE_BYTES), 16, 1024);
+        const uint64_t wd = sdesc_sw128(wb, 16, 1024);
 #pragma unroll
         for (int half = 0; half < 2; ++half)
 #pragma unroll
           for (int kk = 0; kk < CZ / 16; ++kk) {
             const uint32_t off = (kk >> 2) * ATOM_BYTES + (kk & 3) * 32;
-            umma_f16(tmem_base + b * NBINS, sdesc_sw128(zb + half * C::HALF_BYTES + off, 16, 1024),
-                     sdesc_sw128(wb + off, 16, 1024), IDESC, (half > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(tmem_base + b * NBINS, sdesc_add(zd, half * C::HALF_BYTES + off), sdesc_add(wd, off), IDESC,
+                     (half > 0 || kk > 0) ? 1u : 0u);
           }
         umma_commit(&zempty[s]);
         umma_commit(&accfull[b]);

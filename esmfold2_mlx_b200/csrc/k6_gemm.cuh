@@ -198,12 +198,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           if (!(ok = mbar_wait(&afull[sa], (a / NA) & 1, ctx, kSiteMmaA))) break;
           if (!(ok = mbar_wait(&wfull[sw], (r / NW) & 1, ctx, kSiteMmaW))) break;
           tc_fence_after();
-          const uint32_t ha = smem_u32(smem + OFF_A + sa * ATOM_BYTES);
-          const uint32_t wb = smem_u32(smem + OFF_W + sw * NMAX * 128);
+          const uint64_t had = sdesc_sw128(smem_u32(smem + OFF_A + sa * ATOM_BYTES), 16, 1024);
+          const uint64_t wbd = sdesc_sw128(smem_u32(smem + OFF_W + sw * NMAX * 128), 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16(tmem_base + ab * NMAX, sdesc_sw128(ha + kk * 32, 16, 1024), sdesc_sw128(wb + kk * 32, 16, 1024),
-                     idesc, (k > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(tmem_base + ab * NMAX, sdesc_add(had, kk * 32), sdesc_add(wbd, kk * 32), idesc,
+                     (k > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&aempty[sa]);
           umma_commit(&wempty[sw]);
         }
