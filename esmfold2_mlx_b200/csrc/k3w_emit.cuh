@@ -18,7 +18,11 @@
 //   warp 1      TMEM (4 slots x 64 columns) + MMA thread
 //   warps 2-5   A1 = fp16(LN_mix(x column)) over the x tile, one 64-channel atom per warp:
 //               each thread gathers its row's 64 channels, the group meets, the rows are written
-//               back K-major swizzled, the four partial sums are combined through shared memory
+//               back K-major swizzled, the four partial sums are combined through shared memory.
+//               With 1 x 32 tiles (XSW) the x tile arrives 64B-swizzled and each warp transposes
+//               its atom with ldmatrix.trans (four lanes per position), combines the four atoms'
+//               mean and M2 (parallel-variance formula) after one meeting, and writes A1 with
+//               stmatrix: two group barriers per tile instead of four
 //   warps 6-9   A2 = fp16(LN_in(z row)) into its own 2-stage buffer (z stays for the residual)
 //   warps 10-13 epilogue, TMEM lane quadrant warp mod 4 (32 channels each): z' = z + m*sigmoid(g)
 //               computed over the z tile's half-h atoms in shared memory, then TMA-stored.
@@ -52,7 +56,7 @@ static_assert(SMEM_BYTES <= 232448, "K3W shared memory exceeds the per-block lim
 struct Params {
   CUtensorMap tm_z;   // z [B, rows, cols, 256]: box {64, jw, ih, 1}, 128B swizzle (load)
   CUtensorMap tm_zo;  // z_out, same geometry (store)
-  CUtensorMap tm_x;   // x [B*256, rows, pitch]: box {jw, ih, 256}, no swizzle (load)
+  CUtensorMap tm_x;   // x [B*256, rows, pitch]: box {jw, ih, 256}, no swizzle; XSW: box {32, 1, 256}, 64B swizzle
   CUtensorMap tm_we;  // w_emit [256, 256]: box {64, 128}
   CUtensorMap tm_wg;  // w_gate [256, 256]: box {64, 128}
   const __half* ln_in_w;
@@ -81,7 +85,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
-template <bool HAS_BIAS>
+template <bool HAS_BIAS, bool XSW>
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __grid_constant__ Params p) {
   constexpr uint32_t IDESC = idesc_f16_f32(128, TILE, false, false);
   extern __shared__ uint8_t smem[];
@@ -227,6 +231,16 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
     float2* rd = red + grp * 4 * TILE;
     const LnParHalf par = mix ? LnParHalf{p.ln_mix_w, p.ln_mix_b} : LnParHalf{p.ln_in_w, p.ln_in_b};
     const float eps = mix ? p.mix_eps : 1e-5f;
+    // XSW: this lane's LN_mix parameters, channel pairs 64 part + 32g + 8j + 2(t%4) (g < 2, j < 4)
+    uint32_t gmw[8], bmw[8];
+    if (XSW && mix) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = 64 * part + 32 * (e >> 2) + 8 * (e & 3) + 2 * (lane & 3);
+        gmw[e] = __ldg(reinterpret_cast<const unsigned int*>(p.ln_mix_w + c));
+        bmw[e] = __ldg(reinterpret_cast<const unsigned int*>(p.ln_mix_b + c));
+      }
+    }
     uint32_t it = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       const uint32_t s = it & 1, ph = (it >> 1) & 1;
@@ -243,6 +257,79 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
       }
       named_bar_sync(bar_id, 128);
       if (!ok_sh[grp]) break;
+      if (XSW && mix) {
+        // The x tile: [channel][32 positions], 64 B per channel, the 16-byte chunk m (positions
+        // 8m..8m+7) of channel ch at chunk m ^ ((ch >> 1) & 3).  ldmatrix.trans of the 8 x 8 block
+        // (channels 8cb.., positions 8m..) gives lane t channels 8cb + 2(t%4), +1 of position
+        // 8m + t/4 (lane t addresses channel 32g + t of this warp's atom; eight channel rows fall
+        // in eight bank groups).
+        const uint32_t xs = smem_u32(smem + OFF_X + s * TILE_BYTES);
+        uint32_t u[4][8];  // u[m][4g + j]: channels 64 part + 32g + 8j + 2(t%4), +1 of position 8m + t/4
+#pragma unroll
+        for (int m = 0; m < 4; ++m)
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            const uint32_t ch = 64 * part + 32 * g + lane;
+            ldsm_x4_trans(xs + ch * 64 + 16 * (m ^ ((ch >> 1) & 3)), u[m][4 * g], u[m][4 * g + 1], u[m][4 * g + 2],
+                          u[m][4 * g + 3]);
+          }
+        // per position, this atom's mean and M2 (sum of squared deviations) around its own first
+        // channel, from the four lanes that hold it
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const float k = __shfl_sync(0xffffffffu, __low2float(*reinterpret_cast<const __half2*>(&u[m][0])), lane & ~3);
+          float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            unsigned short lo, hi;
+            split_half2(u[m][e], lo, hi);
+            const float2 d = make_float2(add_f16_f32(lo, -k), add_f16_f32(hi, -k));
+            s1 = __fadd2_rn(s1, d);
+            s2 = __ffma2_rn(d, d, s2);
+          }
+          float t1 = s1.x + s1.y, t2 = s2.x + s2.y;
+          t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
+          t2 += __shfl_xor_sync(0xffffffffu, t2, 1);
+          t1 += __shfl_xor_sync(0xffffffffu, t1, 2);
+          t2 += __shfl_xor_sync(0xffffffffu, t2, 2);
+          if ((lane & 3) == 0) rd[part * TILE + 8 * m + (lane >> 2)] = make_float2(k + t1 * (1.0f / 64), t2 - t1 * t1 * (1.0f / 64));
+        }
+        named_bar_sync(bar_id, 128);  // every atom's partials are written; every x value is in registers
+        uint8_t* A1 = smem + OFF_X + s * TILE_BYTES;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          // the four atoms combined (Chan et al.): mean of the means, M2 = sum M2_a + 64 sum (mean_a - mean)^2
+          const int pos = 8 * m + (lane >> 2);
+          const float2 a0 = rd[pos], a1 = rd[TILE + pos], a2 = rd[2 * TILE + pos], a3 = rd[3 * TILE + pos];
+          const float mean = 0.25f * ((a0.x + a1.x) + (a2.x + a3.x));
+          const float d0 = a0.x - mean, d1 = a1.x - mean, d2 = a2.x - mean, d3 = a3.x - mean;
+          const float m2 = (a0.y + a1.y) + (a2.y + a3.y) + 64.0f * ((d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3));
+          const float rs = rsqrtf(fmaxf(m2 * (1.0f / 256), 0.0f) + eps);
+          const float2 r2 = make_float2(rs, rs);
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              unsigned short lo, hi;
+              split_half2(u[m][4 * g + j], lo, hi);
+              const float2 d = __fmul2_rn(make_float2(add_f16_f32(lo, -mean), add_f16_f32(hi, -mean)), r2);
+              const float2 gv = unpack_half2(gmw[4 * g + j]), bv = unpack_half2(bmw[4 * g + j]);
+              const float2 y = __ffma2_rn(d, gv, bv);
+              o[j] = pack_half2(y.x, y.y);
+            }
+            // A1 atom `part` (32 rows x 128 B, K-major 128B-swizzled): lane l gives the row of
+            // position 8m + l%8 in chunk 4g + l/8
+            const uint32_t row8 = lane & 7;
+            stsm_x4(smem_u32(A1) + part * ATOM_BYTES + (8 * m + row8) * 128 + 16 * ((4 * g + (lane >> 3)) ^ row8), o[0], o[1],
+                    o[2], o[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a1full[s]);
+        continue;
+      }
       uint8_t* src;
       uint8_t* dst;
       if (mix) {

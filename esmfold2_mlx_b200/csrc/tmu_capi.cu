@@ -548,15 +548,20 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
   if (zi < zo + bytes && zo < zi + bytes)
     return fail(TMU_ERR_INVALID_ARGUMENT, "c_z = 256: z_out must not overlap z (two CTAs share each tile's z)");
   const bool hb = w->b_emit != nullptr;
-  void (*kern)(k3w::Params) = hb ? k3w::emit_residual_w_kernel<true> : k3w::emit_residual_w_kernel<false>;
+  int ih = 1, jw = 32;
+  choose_tile(rows, cols, ih, jw, k3w::TILE);
+  // 1 x 32 tiles: each channel's 32 positions are one 64-byte row, loaded 64B-swizzled and
+  // transposed by ldmatrix (a narrower box cannot take a swizzle without TMA padding its rows)
+  const bool xsw = jw == 32;
+  void (*kern)(k3w::Params) = hb ? (xsw ? k3w::emit_residual_w_kernel<true, true> : k3w::emit_residual_w_kernel<true, false>)
+                                 : (xsw ? k3w::emit_residual_w_kernel<false, true> : k3w::emit_residual_w_kernel<false, false>);
   Dev dev;
-  int st = current_device(dev, 1u << (20 + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern), k3w::SMEM_BYTES);
+  int st = current_device(dev, 1ull << ((xsw ? 42 : 20) + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern),
+                          k3w::SMEM_BYTES);
   if (st) return st;
   if (dev.sms < 2) return fail(TMU_ERR_UNSUPPORTED, "fewer than 2 SMs");
   k3w::Params p;
   memset(&p, 0, sizeof(p));
-  int ih = 1, jw = 32;
-  choose_tile(rows, cols, ih, jw, k3w::TILE);
   const uint64_t cp = row_pitch(cols);
   {
     const uint64_t dims[4] = {256, (uint64_t)cols, (uint64_t)rows, (uint64_t)B};
@@ -569,7 +574,8 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
     const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, (uint64_t)B * 256};
     const uint64_t str[2] = {cp * 2, cp * 2 * rows};
     const uint32_t box[3] = {(uint32_t)jw, (uint32_t)ih, 256};
-    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))) return st;
+    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, xsw ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return st;
   }
   {
     const uint64_t dims[2] = {256, 256};
