@@ -20,7 +20,8 @@
 // lanes, so they pair up in registers.
 //
 // One tile = 128 pair positions, an ih x jw block of the L x L grid (ih * jw = 128), chosen by
-// the host to minimise padding at ragged L.  CTA = 26 warps, one per SM, persistent:
+// the host by padded positions x a measured cost per position (wide tiles preferred from
+// 512 x 512 positions up, the least padding below).  CTA = 26 warps, one per SM, persistent:
 //   warp 0      TMA: packed weights once (resident, 4c x c_z fp16), then z tiles (2 stages)
 //   warp 1      TMEM allocation (512 columns = 4 slots of 128 positions: signal a, gate a,
 //               signal b, gate b) and the MMA thread, which refills the a (or b) slot pair as
