@@ -17,8 +17,9 @@
 //              128B-swizzled position-major); warp 22 the x tile (2 stages, channel-major)
 //   warp 1     TMEM (2 x 256 columns) + MMA thread: emit (A1 x W_e) and gate (A2 x W_g)
 //   warps 2-9  A1 = fp16(LN_mix(x column)), written over the x tile it was gathered from once
-//              every thread holds its part of the columns in registers.  With jw >= 64 (XSW)
-//              the x tile arrives as two 128B-swizzled [channel][64 positions] halves and is
+//              every thread holds its part of the columns in registers.  With jw >= 64 (XMODE
+//              1) the x tile arrives as two 128B-swizzled [channel][64 positions] halves, with
+//              jw == 32 (XMODE 2) as four 64B-swizzled [channel][32 positions] quarters, and is
 //              transposed by ldmatrix.trans (four lanes per position, conflict-free), A1
 //              written by stmatrix; otherwise a lane pair per position gathers 2-byte values;
 //   warps 10-13 A2 = fp16(LN_in(z row)), in place over the z stage; both concurrently, both
@@ -58,7 +59,8 @@ constexpr int TMEM_COLS = 512;
 struct Params {
   CUtensorMap tm_z;   // z [B, rows, cols, c_z]: box {64, jw, ih, 1}, 128B swizzle (load)
   CUtensorMap tm_zo;  // z_out: box {64, min(jw,32), 32/min(jw,32), 1}, 128B swizzle (per-warp store)
-  CUtensorMap tm_x;   // x [B*c, L, Lpad]: box {jw, ih, c}, no swizzle; XSW: box {64, 1, c}, 128B swizzle
+  CUtensorMap tm_x;   // x [B*c, L, Lpad]: box {jw, ih, c}, no swizzle; XMODE 1: box {64, 1, c}, 128B
+                      // swizzle; XMODE 2: box {32, 1, c}, 64B swizzle
   CUtensorMap tm_we;  // w_emit [c_z, c]: box {64, 128}
   CUtensorMap tm_wg;  // w_gate [c_z, c_z]: box {64, 128}
   const __half* ln_in_w;
@@ -86,7 +88,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
-template <bool HAS_BIAS, bool XSW>
+template <bool HAS_BIAS, int XMODE>
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid_constant__ Params p) {
   constexpr uint32_t IDESC = idesc_f16_f32(128, CZ, false, false);
   // All shared state lives in the dynamic buffer (no static __shared__), whose base the 128B
@@ -148,7 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     tma_prefetch_desc(&p.tm_wg);
   }
   for (int i = threadIdx.x; i < 4 * 128; i += blockDim.x) {
-    if (XSW && i >= 256) {  // mix parameters interleaved per channel pair: {g[2k], g[2k+1], b[2k], b[2k+1]}
+    if (XMODE != 0 && i >= 256) {  // mix parameters interleaved per channel pair: {g[2k], g[2k+1], b[2k], b[2k+1]}
       const int k = (i - 256) >> 2, e = i & 3;
       par[i] = __half2float(e < 2 ? p.ln_mix_w[2 * k + e] : p.ln_mix_b[2 * k + e - 2]);
     } else {
@@ -207,10 +209,13 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
         const uint32_t s = it & 1, ph = (it >> 1) & 1;
         if (!mbar_wait(&xempty[s], ph ^ 1, ctx, kSiteProdX)) break;
         mbar_arrive_expect_tx(&xfull[s], TILE * CC * 2);
-        if (XSW) {  // positions 0-63, then 64-127 (the tile's second half-row, or its second row)
+        if (XMODE == 1) {  // positions 0-63, then 64-127 (the tile's second half-row, or its second row)
           tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
           tma_load_3d(smem + OFF_X + s * TILE_BYTES + TILE_BYTES / 2, &p.tm_x, &xfull[s], p.jw == 128 ? j0 + 64 : j0,
                       p.jw == 128 ? i0 : i0 + 1, bb * CC);
+        } else if (XMODE == 2) {  // the tile's four rows of 32 positions
+          for (int r = 0; r < 4; ++r)
+            tma_load_3d(smem + OFF_X + s * TILE_BYTES + r * (TILE_BYTES / 4), &p.tm_x, &xfull[s], j0, i0 + r, bb * CC);
         } else {
           tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
         }
@@ -268,24 +273,29 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       if (threadIdx.x == 64) x_ok_sh = mbar_wait(&xfull[s], ph, ctx, kSiteTrX) ? 1 : 0;
       named_bar_sync(1, 256);
       if (!x_ok_sh) break;
-      if constexpr (XSW) {
+      if constexpr (XMODE != 0) {
         // The x stage holds two halves of 64 tile positions, each [channel][64 positions] with
         // 128 B per channel and the 16-byte chunk m (positions 8m..8m+7) at chunk m ^ (channel
         // & 7).  Warp wl owns tile positions [16 wl, 16 wl + 16) = chunks m0, m0 + 1 of half
         // wl / 4.  ldmatrix.trans of the 8 x 8 block (channels 8cb.., positions 8m..) gives lane
         // t channels 8cb + 2(t%4), +1 of position 8m + t/4: four lanes per position, 32
         // channels each; lane t supplies the row address of channel 32q + t.
+        // XMODE 2: four quarters [channel][32 positions], 64 B per channel, chunk m of channel ch
+        // at chunk m ^ ((ch >> 1) & 3); warp wl's positions are chunks m0, m0 + 1 of quarter wl / 2.
         const int wl = warp - 2;
         const uint32_t xs = smem_u32(smem + OFF_X + s * TILE_BYTES);
-        const uint32_t xh = xs + (wl >> 2) * (TILE_BYTES / 2);
-        const int m0 = 2 * (wl & 3);
+        const uint32_t xh = XMODE == 1 ? xs + (wl >> 2) * (TILE_BYTES / 2) : xs + (wl >> 1) * (TILE_BYTES / 4);
+        const int m0 = XMODE == 1 ? 2 * (wl & 3) : 2 * (wl & 1);
         uint32_t u[2][16];  // u[mi][4q + j]: channels 32q + 8j + 2(t%4), +1 of position 16 wl + 8 mi + t/4
 #pragma unroll
         for (int mi = 0; mi < 2; ++mi)
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            ldsm_x4_trans(xh + (32 * q + lane) * 128 + 16 * ((m0 + mi) ^ (lane & 7)), u[mi][4 * q], u[mi][4 * q + 1],
-                          u[mi][4 * q + 2], u[mi][4 * q + 3]);
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t ch = 32 * q + lane;
+            const uint32_t addr = XMODE == 1 ? xh + ch * 128 + 16 * ((m0 + mi) ^ (lane & 7))
+                                             : xh + ch * 64 + 16 * ((m0 + mi) ^ ((ch >> 1) & 3));
+            ldsm_x4_trans(addr, u[mi][4 * q], u[mi][4 * q + 1], u[mi][4 * q + 2], u[mi][4 * q + 3]);
+          }
         // statistics of each position over its four lanes: shifted sums around its channel 0
         // (the low half of u[mi][0] on lane t with t%4 == 0), two shuffle steps
         float mean[2], rs[2];

@@ -167,7 +167,7 @@ void choose_tile_k1w(int rows, int cols, int& ih, int& jw) {
   }
 }
 
-// K3's tile: as choose_tile, but a shape with jw >= 64 (whose x tile is transposed by ldmatrix)
+// K3's tile: as choose_tile, but a shape with jw >= 32 (whose x tile is transposed by ldmatrix)
 // is charged 10 % less per position than the narrower shapes (2-byte gather), the measured
 // difference in K3's time per tile, so a little padding buys the faster path.
 void choose_tile_k3(int rows, int cols, int& ih, int& jw) {
@@ -176,7 +176,7 @@ void choose_tile_k3(int rows, int cols, int& ih, int& jw) {
   for (int wi : widths) {
     const int hi = 128 / wi;
     const long long area = static_cast<long long>((rows + hi - 1) / hi) * hi * ((cols + wi - 1) / wi) * wi;
-    const long long cost = area * (wi >= 64 ? 10 : 11);
+    const long long cost = area * (wi >= 32 ? 10 : 11);
     if (best < 0 || cost < best) {
       best = cost;
       ih = hi;
@@ -422,15 +422,19 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   int ih = 1, jw = 128;
   choose_tile_k3(rows, cols, ih, jw);
   // jw >= 64: the x tile is loaded as two 128B-swizzled halves of 64 positions (one 128-byte
-  // row per channel each) and transposed by ldmatrix.  (A narrower box cannot take this form:
-  // with the 128-byte swizzle, TMA pads every inner row shorter than 128 bytes to 128 bytes in
-  // shared memory, which would quadruple the x tile's footprint at jw = 16.)
-  const bool xsw = jw >= 64;
-  void (*kern)(k3::Params) = hb ? (xsw ? k3::emit_residual_kernel<true, true> : k3::emit_residual_kernel<true, false>)
-                                : (xsw ? k3::emit_residual_kernel<false, true> : k3::emit_residual_kernel<false, false>);
+  // row per channel each), jw == 32 as four 64B-swizzled quarters (64-byte rows), and
+  // transposed by ldmatrix.  (A box whose inner rows are shorter than the swizzle span cannot
+  // take this form: TMA pads every such row to the span in shared memory, which would
+  // quadruple the x tile's footprint at jw = 16 with the 128-byte swizzle.)
+  const int xmode = jw >= 64 ? 1 : jw == 32 ? 2 : 0;
+  void (*kern)(k3::Params) =
+      hb ? (xmode == 1 ? k3::emit_residual_kernel<true, 1> : xmode == 2 ? k3::emit_residual_kernel<true, 2>
+                                                                        : k3::emit_residual_kernel<true, 0>)
+         : (xmode == 1 ? k3::emit_residual_kernel<false, 1> : xmode == 2 ? k3::emit_residual_kernel<false, 2>
+                                                                         : k3::emit_residual_kernel<false, 0>);
   Dev dev;
-  int st = current_device(dev, 1ull << ((xsw ? 40 : 12) + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern),
-                          k3::SMEM_BYTES);
+  int st = current_device(dev, 1ull << ((xmode == 1 ? 40 : xmode == 2 ? 44 : 12) + (hb ? 1 : 0)),
+                          reinterpret_cast<const void*>(kern), k3::SMEM_BYTES);
   if (st) return st;
   k3::Params p;
   memset(&p, 0, sizeof(p));
@@ -447,9 +451,10 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   {
     const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, (uint64_t)B * 128};
     const uint64_t str[2] = {cp * 2, cp * 2 * rows};
-    const uint32_t box[3] = {xsw ? 64u : (uint32_t)jw, xsw ? 1u : (uint32_t)ih, 128};
-    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, xsw ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return st;
+    const uint32_t box[3] = {xmode == 1 ? 64u : (uint32_t)jw, xmode != 0 ? 1u : (uint32_t)ih, 128};
+    const CUtensorMapSwizzle sw =
+        xmode == 1 ? CU_TENSOR_MAP_SWIZZLE_128B : xmode == 2 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, sw))) return st;
   }
   {
     const uint64_t dims[2] = {128, 128};
