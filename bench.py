@@ -16,8 +16,9 @@ weights N(0, 1/fan_in) plus N(0, 0.02) biases, z ~ N(0, 1).  One step = tri-mul 
              copied from pinned host memory and the result copied back, inside the interval.
 * roofline   the kernel with the largest time share, from per-kernel CUDA events captured in a
              second graph (K1 project+gate, K2 contraction, K3 emit+residual, each launched
-             through its own C-ABI entry point); algorithmic bytes / FLOPs per launch as stated
-             in DESIGN.md; peaks from MEASURED_PEAKS.json.
+             through its own C-ABI entry point); algorithmic bytes / FLOPs per launch are
+             the per-cell figures in ``_kernel_costs`` times the cells a launch processes;
+             peaks from MEASURED_PEAKS.json.
 * N > 1      one process per GPU (torchrun), each rank runs its own fold (seed + rank): weak
              scaling, no collective on the data path; times are the max over ranks.
 * --impl reference   the reference's CPU path (the PyTorch restatement in oracle/, all host

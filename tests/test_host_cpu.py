@@ -1,0 +1,193 @@
+"""Host logic with no GPU: the variant registry (``src/esmfold2_mlx/variants.py:74-86``) and the
+adaptive-recycling state machine (``src/esmfold2_mlx/var_adaptive_loops.py:79-156``).
+
+The adaptive tests replace the K5 distogram kernel with the reference's own formula on the CPU
+(``var_adaptive_loops.py:43-46``: ``softmax(head(z + z^T)) @ centres``) and the trunk with a
+scripted module, so only the pass / convergence / extra-pass bookkeeping is under test.
+"""
+
+from __future__ import annotations
+
+import sys
+import types
+
+import pytest
+import torch
+from torch import nn
+
+from esmfold2_mlx_b200 import adaptive, variants
+
+
+# ---------------------------------------------------------------- registry
+
+def test_unknown_variant_raises_value_error():
+    with pytest.raises(ValueError, match="unknown speed variant 'no_such_stack'"):
+        variants.apply_variants(object(), ["no_such_stack"])
+
+
+def test_variants_apply_in_order_from_a_comma_string(monkeypatch):
+    calls = []
+    for name in ("fake_a", "fake_b"):
+        mod = types.ModuleType(f"esmfold2_mlx_b200.var_{name}")
+        mod.apply = lambda model, _n=name: calls.append((_n, model))
+        monkeypatch.setitem(sys.modules, mod.__name__, mod)
+    model = object()
+    assert variants.apply_variants(model, "fake_b,,fake_a") is model
+    assert calls == [("fake_b", model), ("fake_a", model)]
+    calls.clear()
+    variants.apply_variants(model, [])
+    variants.apply_variants(model, "")
+    assert calls == []
+
+
+def test_a_broken_import_inside_a_variant_is_not_reported_as_unknown(monkeypatch):
+    """Only a missing ``var_<name>`` module means "unknown"; an import error inside it surfaces."""
+    import importlib
+
+    real = importlib.import_module
+
+    def fake_import(name, *a, **k):
+        if name.endswith("var_broken"):
+            raise ModuleNotFoundError("No module named 'dependency_x'", name="dependency_x")
+        return real(name, *a, **k)
+
+    monkeypatch.setattr(importlib, "import_module", fake_import)
+    with pytest.raises(ModuleNotFoundError, match="dependency_x"):
+        variants.apply_variants(object(), "broken")
+
+
+# ---------------------------------------------------------------- adaptive recycling
+
+C_Z, L = 8, 6
+
+
+class _ScriptedTrunk(nn.Module):
+    """Returns ``base * s`` for the next scale ``s`` of its script; records every call."""
+
+    def __init__(self, scales):
+        super().__init__()
+        self.scales = list(scales)
+        self.inputs = []
+        self.base = torch.randn(1, L, L, C_Z, generator=torch.Generator().manual_seed(0))
+
+    def forward(self, pair, pair_attention_mask=None):
+        self.inputs.append(pair.clone())
+        return self.base * self.scales[len(self.inputs) - 1]
+
+    def set_chunk_size(self, n):
+        self.chunk = n
+
+    def set_kernel_backend(self, b):
+        self.backend = b
+
+
+@torch.no_grad()
+def _reference_expected_distance(z, head):
+    logits = head(z.float() + z.float().transpose(-2, -3))
+    return logits.softmax(-1) @ adaptive.CENTRES
+
+
+def _model(proj=None):
+    m = nn.Module()
+    m.distogram_head = nn.Linear(C_Z, 128)
+    torch.nn.init.normal_(m.distogram_head.weight, std=2.0, generator=torch.Generator().manual_seed(1))
+    if proj is not None:
+        m.pair_loop_proj = proj
+    return m
+
+
+@pytest.fixture
+def cpu_head(monkeypatch):
+    monkeypatch.setattr(adaptive, "DistoHead", lambda head, device: head)
+    monkeypatch.setattr(adaptive, "expected_distance", _reference_expected_distance)
+
+
+def _p95(trunk_a, trunk_b, head):
+    ea = _reference_expected_distance(trunk_a.to(torch.float16), head)
+    eb = _reference_expected_distance(trunk_b.to(torch.float16), head)
+    return float((eb - ea).abs().flatten().quantile(0.95))
+
+
+def test_converges_then_returns_the_converged_output_without_running_the_trunk(cpu_head):
+    scripted = _ScriptedTrunk([1.0, -1.0, -1.0, 9.0, 9.0])
+    model = _model()
+    t = adaptive.CUDAAdaptiveTrunk(scripted, model)
+    t.reset(5)
+    pair = torch.zeros(1, L, L, C_Z)
+    outs = [t(pair) for _ in range(5)]
+    # pass 2 (the sign flipped) moves the distogram (p95 well above 0.6 A), pass 3 repeats it
+    assert _p95(scripted.base, -scripted.base, model.distogram_head) > adaptive.THRESHOLD
+    assert t.converged and t.passes == 3 and len(scripted.inputs) == 3
+    assert [h["disto_p95"] for h in t.history][1] == 0.0
+    assert outs[3] is outs[2] and outs[4] is outs[2]
+
+
+def test_min_passes_holds_back_an_early_convergence(cpu_head):
+    scripted = _ScriptedTrunk([2.0, 2.0, 2.0, 2.0])
+    t = adaptive.CUDAAdaptiveTrunk(scripted, _model(), min_passes=3)
+    t.reset(4)
+    pair = torch.zeros(1, L, L, C_Z)
+    t(pair)
+    t(pair)
+    assert not t.converged and t.passes == 2  # converged by the metric, but only two passes ran
+    t(pair)
+    assert t.converged and t.passes == 3
+    t(pair)
+    assert len(scripted.inputs) == 3
+
+
+def test_reset_starts_a_new_fold(cpu_head):
+    scripted = _ScriptedTrunk([1.0, 1.0, 1.0, -1.0])
+    t = adaptive.CUDAAdaptiveTrunk(scripted, _model())
+    pair = torch.zeros(1, L, L, C_Z)
+    t.reset(2)
+    t(pair)
+    t(pair)
+    assert t.converged
+    t.reset(2)
+    assert not t.converged and t.passes == 0 and t.history == [] and t.prev is None
+    t(pair)
+    t(pair)
+    assert t.passes == 2 and not t.converged  # the sign flip moves the distogram
+    assert len(scripted.inputs) == 4
+
+
+def test_extra_passes_after_the_scheduled_ones(cpu_head):
+    """With ``max_extra``, the last scheduled call runs up to ``max_extra`` more passes on
+    ``z_init + proj(out)`` (``var_adaptive_loops.py:127-142``), stopping at the extra threshold."""
+    proj = nn.Linear(C_Z, C_Z)
+    scripted = _ScriptedTrunk([1.0, -1.0, 1.0, -1.0, -1.0, 1.0])
+    t = adaptive.CUDAAdaptiveTrunk(scripted, _model(proj), max_extra=3)
+    t.reset(3)
+    pair = torch.randn(1, L, L, C_Z, generator=torch.Generator().manual_seed(2))
+    z_init = pair - proj(torch.zeros_like(pair))
+    t(pair)
+    t(pair)
+    out = t(pair)  # scheduled call 3: pass 3, then extra passes 4 (moves) and 5 (repeats: stop)
+    assert t.passes == 5 and not t.converged
+    assert torch.equal(out, -scripted.base)
+    # extra pass inputs are z_init + proj(previous output)
+    assert torch.allclose(scripted.inputs[3], z_init + proj(scripted.base))
+    assert torch.allclose(scripted.inputs[4], z_init + proj(-scripted.base))
+    assert t.history[-1]["disto_p95"] == 0.0
+
+
+def test_wrapper_forwards_chunk_and_backend_setters(cpu_head):
+    scripted = _ScriptedTrunk([1.0])
+    t = adaptive.CUDAAdaptiveTrunk(scripted, _model())
+    t.set_chunk_size(64)
+    t.set_kernel_backend("cuda")
+    assert scripted.chunk == 64 and scripted.backend == "cuda"
+
+
+def test_apply_resets_per_fold_with_num_loops_plus_one(cpu_head):
+    model = _model()
+    model.folding_trunk = _ScriptedTrunk([1.0] * 8)
+    model.config = types.SimpleNamespace(num_loops=3)
+    seen = []
+    model.forward = lambda *a, num_loops=None, **k: seen.append(model.folding_trunk.scheduled)
+    trunk = adaptive.apply(model)
+    assert model.folding_trunk is trunk
+    model.forward()
+    model.forward(num_loops=5)
+    assert seen == [4, 6]
