@@ -191,3 +191,50 @@ def test_apply_resets_per_fold_with_num_loops_plus_one(cpu_head):
     model.forward()
     model.forward(num_loops=5)
     assert seen == [4, 6]
+
+
+# ---------------------------------------------------------------- weight copies (mlx_trunk.py:40-69)
+
+@pytest.mark.parametrize("c_z", [128, 256])
+def test_trunk_weight_copy_matches_the_reference_orientation(c_z):
+    """``trunk_params`` (the kernels' layouts, built on the CPU here) holds exactly the oracle's
+    reference-orientation fp16 weights: the packed projection is ``w_in^T`` with rows in the
+    order [signal a | gate a | signal b | gate b] and the 1/256 pre-scale on signal a
+    (``mlx_trunk.py:44-48``); emit / gate / transition matrices are the ``nn.Linear`` layouts,
+    i.e. the transposes of ``w_emit`` / ``w_out_gate`` / ``w12`` / ``w3`` (``:49-66``)."""
+    from esmfold2_mlx_b200 import ops
+    from esmfold2_mlx_b200.synthetic import FoldingTrunk, trimul_biases
+    from esmfold2_mlx_b200.trunk import trunk_params
+    from oracle import trimul_oracle as orc
+
+    ft = FoldingTrunk(2, c_z, c_z, hidden=2 * c_z, seed=3)
+    biases = [{"out": trimul_biases(c_z, c_z, seed=10 + i), "in": trimul_biases(c_z, c_z, seed=20 + i)} for i in range(2)]
+    got = trunk_params(ft, device="cpu", biases=biases)
+    ref = orc.trunk_params(ft)
+    order = torch.tensor(ops.proj_row_order_py(c_z))
+    for g, r, blk, bb in zip(got, ref, ft.blocks, biases):
+        for d in ("out", "in"):
+            w, p = g[d], r[d]
+            assert (w.c, w.c_z) == (c_z, c_z)
+            assert torch.equal(w.w_proj.float(), p["w_in"].T[order])
+            assert torch.equal(w.w_emit.float(), p["w_emit"].T)
+            assert torch.equal(w.w_gate.float(), p["w_out_gate"].T)
+            for k in ("ln_in_w", "ln_in_b", "ln_mix_w", "ln_mix_b"):
+                assert torch.equal(getattr(w, k).float(), p[k])
+            b_in = bb[d]["b_in"].detach().float().clone()
+            b_in[:c_z] /= ops.CONTRACT_SCALE
+            assert torch.equal(w.b_proj, b_in[order])
+            assert torch.equal(w.b_emit, bb[d]["b_emit"].float())
+            assert w.w_proj.dtype == torch.float16 and w.b_proj.dtype == torch.float32
+        tw = g["tw"]
+        assert tw.fused and tw.activation == "swiglu" and tw.hidden == 2 * c_z
+        assert torch.equal(tw.w12.float(), r["w12"].T) and torch.equal(tw.w3.float(), r["w3"].T)
+        assert torch.equal(tw.ln_w.float(), r["ln_w"]) and torch.equal(tw.ln_b.float(), r["ln_b"])
+
+
+def test_trunk_params_refuses_other_dtypes():
+    from esmfold2_mlx_b200.synthetic import FoldingTrunk
+    from esmfold2_mlx_b200.trunk import trunk_params
+
+    with pytest.raises(ValueError, match="fp16"):
+        trunk_params(FoldingTrunk(1, 128, 128, hidden=256, seed=0), dtype=torch.bfloat16, device="cpu")
