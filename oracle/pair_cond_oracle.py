@@ -22,9 +22,12 @@ Rounding points (``r16`` = one fp16 rounding): ``h = r16(LN(cat(z_trunk, rel_pos
 ``xb = r16(hh @ b)``, ``s = r16(r16(xa * r16(sigmoid(xa))) * xb)``, ``z = z + r16(s @ out)``
 (fp32 residual); ``bias = r16(r16(r16(LN(z)) @ bias_w) + bias_b)`` with an affine-free LN.
 
-Parity pin: the reference's own tests cover this path only through end-to-end atom coordinates
-that need the esm package, the checkpoint and MLX (all absent), so this restatement is checked
-against the code it cites line by line and is otherwise unpinned.
+Parity pin: ``tests/golden/conditioning_golden.npz``, made by
+``tests/golden/make_golden_conditioning.py`` running the reference's ``pair_biases``
+(``mlx_diffusion16.py:81-87``) unmodified over a numpy stand-in for MLX 0.32.3; checked by
+``tests/test_oracle_golden_conditioning.py`` (<= 2 fp16 ulps at the tensor's scale, rel-L2 <= 1e-3).
+The reference's own tests cover this path only through end-to-end atom coordinates that need the
+esm package, the checkpoint and MLX (all absent).
 """
 
 from __future__ import annotations

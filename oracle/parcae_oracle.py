@@ -3,8 +3,11 @@
 Restates ``_step``'s recurrence (abhi0raj/esmfold2-mlx ``src/esmfold2_mlx/var_6b_mlx_loop.py:67-71``,
 fp32 MLX in the reference):  z' = a * z + LN(z_init + refined; parcae_input_norm, eps 1e-5) @ B^T,
 with ``bT = b_mat.T`` (``:169``).  ``dtype`` float32 follows the reference's arithmetic; float64
-is the exact value both are measured against.  Parity pin: none beyond the cited code (the
-reference's tests need the 6B checkpoint, esm and MLX, all absent).
+is the exact value both are measured against.  Parity pin: ``tests/golden/conditioning_golden.npz``
+(``tests/golden/make_golden_conditioning.py`` runs the reference's ``_step`` unmodified over a
+numpy stand-in for MLX, with identity lm_encoder and trunk), checked by
+``tests/test_oracle_golden_conditioning.py`` to a few fp32 ulps; the reference's own tests need the
+6B checkpoint, esm and MLX, all absent.
 """
 
 from __future__ import annotations

@@ -1,12 +1,15 @@
 """``mlx.core`` restated over numpy, for running the reference trunk on the CPU (fixtures only).
 
-Only what ``src/esmfold2_mlx/mlx_trunk.py`` and ``mlx_trunk_kernels.py`` call is provided.
+Only what ``src/esmfold2_mlx/mlx_trunk.py``, ``mlx_trunk_kernels.py``, ``mlx_diffusion16.pair_biases``
+and ``var_6b_mlx_loop._step`` call is provided.
 Semantics follow MLX 0.32.3's documented behaviour for these primitives:
 
-* arrays carry a dtype (float16 or float32); every op returns its inputs' dtype;
+* arrays carry a dtype (float16 or float32); an op on float16 and float32 arrays returns float32,
+  an op of an array with a Python scalar returns the array's dtype;
 * fp16 element-wise ops (``+ - *``, ``sigmoid``) compute in fp32 and round once to fp16;
 * ``matmul`` / ``addmm`` accumulate in fp32 and round once to the output dtype;
 * ``fast.layer_norm`` computes fp32 statistics (mean, then centred variance) and rounds once;
+  a ``None`` weight or bias means no scale or no shift;
 * ``compile`` returns the function unchanged (it does not alter arithmetic), ``eval`` is a no-op.
 
 ``fast.metal_kernel`` returns an evaluator keyed by the kernel's ``name`` that restates the three
@@ -30,10 +33,10 @@ def _np(x):
 
 
 def _dtype_of(*xs):
-    for x in xs:
-        if isinstance(x, array):
-            return x.dtype
-    return float32
+    dts = [x.dtype for x in xs if isinstance(x, array)]
+    if not dts or float32 in dts:
+        return float32
+    return float16
 
 
 class array:
@@ -149,6 +152,15 @@ def split(x, n, axis=-1):
     return [array(p, x.dtype) for p in np.split(_np(x), n, axis=axis)]
 
 
+def concatenate(xs, axis=0):
+    dt = _dtype_of(*xs)
+    return array(np.concatenate([_np(x).astype(dt) for x in xs], axis=axis), dt)
+
+
+def linspace(start, stop, num=50, dtype=float32):
+    return array(np.linspace(start, stop, num, dtype=np.float64).astype(np.float32).astype(dtype), dtype)
+
+
 def zeros(shape, dtype=float32):
     return array(np.zeros(shape, dtype), dtype)
 
@@ -167,11 +179,18 @@ def _ln32(x, w, b, eps):
     v = x - mean
     var = (v * v).mean(-1, keepdims=True, dtype=np.float32)
     inv = (1.0 / np.sqrt(var + np.float32(eps))).astype(np.float32)
-    return v * inv * w.astype(np.float32) + b.astype(np.float32)
+    y = v * inv
+    if w is not None:
+        y = y * w.astype(np.float32)
+    if b is not None:
+        y = y + b.astype(np.float32)
+    return y
 
 
 def _layer_norm(x, w, b, eps):
-    return array(_ln32(_np(x), _np(w), _np(b), eps).astype(x.dtype), x.dtype)
+    w = None if w is None else _np(w)
+    b = None if b is None else _np(b)
+    return array(_ln32(_np(x), w, b, eps).astype(x.dtype), x.dtype)
 
 
 # --------------------------------------------------------------------------------------
