@@ -18,6 +18,10 @@ Stored cases (c_z = c = 128, one PairUpdateBlock, transition hidden 128):
   * ``trunk16_{nomask,mask}``: ``mlx_trunk_kernels.make_trunk(float16)`` (default stack path).
   * ``trunk16_unfused_mask``: ``make_trunk(float16, use=())`` (plain MLX ops, no Metal kernels).
   * ``trunk32_mask``: ``mlx_trunk.make_trunk(float32)`` (the exact fp32 trunk).
+
+``--c-z 256`` writes ``trimul_golden_cz256.npz`` instead: the same cases at c_z = c = 256 (the
+released trunk's width, ``mlx_trunk.py:4``) for (B, L) = (1, 12) and (2, 7), the trunk cases on
+the first.
 """
 
 from __future__ import annotations
@@ -40,8 +44,13 @@ HIDDEN = 128
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of abhi0raj/esmfold2-mlx")
-    ap.add_argument("--out", default=os.path.join(HERE, "trimul_golden.npz"))
+    ap.add_argument("--out", default=None)
+    ap.add_argument("--c-z", type=int, default=C_Z, choices=(128, 256))
     args = ap.parse_args()
+    c_z = c = args.c_z
+    cases = ((1, 20), (2, 13)) if c_z == 128 else ((1, 12), (2, 7))
+    if args.out is None:
+        args.out = os.path.join(HERE, "trimul_golden.npz" if c_z == 128 else f"trimul_golden_cz{c_z}.npz")
 
     sys.path.insert(0, os.path.join(HERE, "mlx_standin"))
     sys.path.insert(0, os.path.join(args.reference, "src"))
@@ -52,7 +61,7 @@ def main():
 
     from esmfold2_mlx_b200.synthetic import FoldingTrunk, pair_mask
 
-    trunk = FoldingTrunk(1, C_Z, C, hidden=HIDDEN, seed=SEED_WEIGHTS, ln_noise=0.1)
+    trunk = FoldingTrunk(1, c_z, c, hidden=HIDDEN, seed=SEED_WEIGHTS, ln_noise=0.1)
     out = {}
     sd = {k: v.detach().numpy().astype(np.float32) for k, v in trunk.state_dict().items()}
     for k, v in sd.items():
@@ -66,9 +75,9 @@ def main():
     p32 = mt.trunk_params(trunk, mx.float32)
     mix_eps16 = mt.EPS / mt.CONTRACT_SCALE**2
 
-    for (B, L) in ((1, 20), (2, 13)):
+    for (B, L) in cases:
         g = torch.Generator().manual_seed(1000 + L)
-        z = torch.randn(B, L, L, C_Z, generator=g).to(torch.float16)
+        z = torch.randn(B, L, L, c_z, generator=g).to(torch.float16)
         msk = pair_mask(B, L, n_pad=3).to(torch.float16)
         tag = f"B{B}L{L}"
         out[f"z/{tag}"] = z.numpy()
@@ -84,7 +93,7 @@ def main():
                 z2, n2 = mk._trimul(pt, zm, n, mask, outgoing, mix_eps16, nxt, mk.ALL)
                 out[f"tm_{direction}_{mname}/{tag}/z"] = np.asarray(z2).astype(np.float16)
                 out[f"tm_{direction}_{mname}/{tag}/n_next"] = np.asarray(n2).astype(np.float16)
-        if (B, L) == (1, 20):
+        if (B, L) == cases[0]:
             for mname, mask in (("nomask", None), ("mask", mm)):
                 r = mk.make_trunk(mx.float16)(p16, mx.array(z.float().numpy()), mask)
                 out[f"trunk16_{mname}/{tag}"] = np.asarray(r).astype(np.float32)
@@ -93,7 +102,7 @@ def main():
             r = mt.make_trunk(mx.float32)(p32, mx.array(z.float().numpy()), mx.array(msk.float().numpy()))
             out[f"trunk32_mask/{tag}"] = np.asarray(r).astype(np.float32)
 
-    meta = {"seed_weights": SEED_WEIGHTS, "c_z": C_Z, "c": C, "hidden": HIDDEN, "ln_noise": 0.1,
+    meta = {"seed_weights": SEED_WEIGHTS, "c_z": c_z, "c": c, "hidden": HIDDEN, "ln_noise": 0.1,
             "mix_eps16": mix_eps16}
     out["meta"] = np.frombuffer(repr(meta).encode(), dtype=np.uint8)
     np.savez_compressed(args.out, **out)

@@ -20,17 +20,21 @@ import torch
 from esmfold2_mlx_b200.synthetic import FoldingTrunk
 from oracle import trimul_oracle as orc
 
-GOLD = os.path.join(os.path.dirname(__file__), "golden", "trimul_golden.npz")
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+# c_z = c = 128 (the BASELINE configurations) and 256 (the released trunk, mlx_trunk.py:4)
+FILES = {128: ("trimul_golden.npz", ("B1L20", "B2L13")), 256: ("trimul_golden_cz256.npz", ("B1L12", "B2L7"))}
 
 
-@pytest.fixture(scope="module")
-def gold():
-    d = np.load(GOLD)
+@pytest.fixture(scope="module", params=sorted(FILES), ids=lambda w: f"cz{w}")
+def gold(request):
+    name, tags = FILES[request.param]
+    d = np.load(os.path.join(GOLDEN, name))
     meta = ast.literal_eval(bytes(d["meta"]).decode())
+    assert meta["c_z"] == request.param
     trunk = FoldingTrunk(1, meta["c_z"], meta["c"], hidden=meta["hidden"], seed=0)
     sd = {k[2:]: torch.from_numpy(d[k].astype(np.float32)) for k in d.files if k.startswith("w/")}
     trunk.load_state_dict(sd)
-    return d, trunk, meta
+    return d, trunk, {**meta, "tags": tags}
 
 
 def _ulp16(x: torch.Tensor) -> torch.Tensor:
@@ -56,11 +60,12 @@ def _close16(ref: np.ndarray, test: torch.Tensor, max_ulps: float, frac_off: flo
     assert err <= rel_l2, f"rel L2 {err:.3g}"
 
 
-@pytest.mark.parametrize("tag", ["B1L20", "B2L13"])
+@pytest.mark.parametrize("case", [0, 1])
 @pytest.mark.parametrize("direction", ["out", "in"])
 @pytest.mark.parametrize("mname", ["nomask", "mask"])
-def test_trimul_matches_reference_code(gold, tag, direction, mname):
+def test_trimul_matches_reference_code(gold, case, direction, mname):
     d, trunk, meta = gold
+    tag = meta["tags"][case]
     blk = trunk.blocks[0]
     p = orc.trimul_params(getattr(blk, "tri_mul_" + direction), fp16=True)
     z = torch.from_numpy(d[f"z/{tag}"].astype(np.float32))
@@ -77,10 +82,10 @@ def test_trimul_matches_reference_code(gold, tag, direction, mname):
 def test_trunk16_matches_reference_code(gold, mname):
     d, trunk, meta = gold
     params = orc.trunk_params(trunk, fp16=True)
-    z = torch.from_numpy(d["z/B1L20"].astype(np.float32))
-    mask = torch.from_numpy(d["mask/B1L20"].astype(np.float32)) if mname == "mask" else None
+    z = torch.from_numpy(d[f"z/{meta['tags'][0]}"].astype(np.float32))
+    mask = torch.from_numpy(d[f"mask/{meta['tags'][0]}"].astype(np.float32)) if mname == "mask" else None
     out = orc.trunk_fp16(params, z, mask, meta["mix_eps16"])
-    _close16(d[f"trunk16_{mname}/B1L20"], out, max_ulps=4, rel_l2=1e-3)
+    _close16(d[f"trunk16_{mname}/{meta['tags'][0]}"], out, max_ulps=4, rel_l2=1e-3)
 
 
 def test_unfused_trunk_is_close_to_fused(gold):
@@ -88,10 +93,10 @@ def test_unfused_trunk_is_close_to_fused(gold):
     one; the oracle follows the fused path and stays within fp16 noise of the unfused one."""
     d, trunk, meta = gold
     params = orc.trunk_params(trunk, fp16=True)
-    z = torch.from_numpy(d["z/B1L20"].astype(np.float32))
-    mask = torch.from_numpy(d["mask/B1L20"].astype(np.float32))
+    z = torch.from_numpy(d[f"z/{meta['tags'][0]}"].astype(np.float32))
+    mask = torch.from_numpy(d[f"mask/{meta['tags'][0]}"].astype(np.float32))
     out = orc.trunk_fp16(params, z, mask, meta["mix_eps16"])
-    ref = torch.from_numpy(d["trunk16_unfused_mask/B1L20"])
+    ref = torch.from_numpy(d[f"trunk16_unfused_mask/{meta['tags'][0]}"])
     st = orc.error_stats(ref, out)
     assert st["rel_l2"] < 5e-3 and st["max_abs"] < 0.1, st
 
@@ -99,8 +104,8 @@ def test_unfused_trunk_is_close_to_fused(gold):
 def test_trunk32_matches_reference_code(gold):
     d, trunk, meta = gold
     blk = trunk.blocks[0]
-    z = torch.from_numpy(d["z/B1L20"].astype(np.float32))
-    mask = torch.from_numpy(d["mask/B1L20"].astype(np.float32))
+    z = torch.from_numpy(d[f"z/{meta['tags'][0]}"].astype(np.float32))
+    mask = torch.from_numpy(d[f"mask/{meta['tags'][0]}"].astype(np.float32))
     p32o = orc.trimul_params(blk.tri_mul_out, fp16=False)
     p32i = orc.trimul_params(blk.tri_mul_in, fp16=False)
     zz = orc.trimul_fp32(p32o, z, mask, True)
@@ -110,16 +115,16 @@ def test_trunk32_matches_reference_code(gold):
     x = h @ tp["w12"]
     x1, x2 = x.chunk(2, -1)
     zz = zz + (x1 * torch.sigmoid(x1) * x2) @ tp["w3"]
-    st = orc.error_stats(torch.from_numpy(d["trunk32_mask/B1L20"]), zz)
+    st = orc.error_stats(torch.from_numpy(d[f"trunk32_mask/{meta['tags'][0]}"]), zz)
     assert st["rel_l2"] < 1e-5, st
 
 
 def test_fp16_scheme_tracks_fp32(gold):
     """The 1/256 pre-scale keeps the fp16 path within fp16 noise of the exact fp32 trunk."""
     d, trunk, meta = gold
-    z = torch.from_numpy(d["z/B1L20"].astype(np.float32))
-    ref32 = torch.from_numpy(d["trunk32_mask/B1L20"])
-    ref16 = torch.from_numpy(d["trunk16_mask/B1L20"])
+    z = torch.from_numpy(d[f"z/{meta['tags'][0]}"].astype(np.float32))
+    ref32 = torch.from_numpy(d[f"trunk32_mask/{meta['tags'][0]}"])
+    ref16 = torch.from_numpy(d[f"trunk16_mask/{meta['tags'][0]}"])
     st = orc.error_stats(ref32, ref16)
     assert st["rel_l2"] < 5e-3, st
     assert z.shape == ref32.shape
