@@ -105,6 +105,8 @@ SIGNATURES = {
     "tmu_trimul": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp]),
     "tmu_trimul_noalloc": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _i, _f, _vp, _vp]),
     "tmu_transition": (_i, [_vp, _vp, _TW, _i, _i, _i, _i, _i, _vp, _vp]),
+    "tmu_pair_block_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "tmu_pair_block": (_i, [_vp, _vp, _vp, _W, _W, _TW, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp]),
     "tmu_disto_expected": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
     "tmu_pair_cond_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "tmu_pair_cond": (_i, [_vp, _vp, ctypes.POINTER(TmuPairCondWeights), _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp,

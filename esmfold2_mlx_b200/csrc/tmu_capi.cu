@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <string>
 
@@ -1116,23 +1117,78 @@ int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_t
   return launch_k3(x, z, z_out, w, B, L, L, mix_eps, dstat, s, c_z);
 }
 
-int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int c_z, int hidden,
-                   int activation, void* status, void* stream) {
+// Host-side checks of a transition call (shared by tmu_transition and tmu_pair_block).
+static int check_transition(const void* z, const void* z_out, const tmu_transition_weights* w, int B, int L, int c_z,
+                            int hidden, int activation) {
   if (B < 1 || L < 1) return fail(TMU_ERR_INVALID_ARGUMENT, "B and L must be positive");
   if (c_z != 128 && c_z != 256) return fail(TMU_ERR_UNSUPPORTED, "c_z must be 128 or 256");
   if (hidden < 64 || hidden > 4096 || hidden % 64) return fail(TMU_ERR_UNSUPPORTED, "hidden must be a multiple of 64 in [64, 4096]");
   if (L > 8192 || B > 65535) return fail(TMU_ERR_UNSUPPORTED, "L > 8192");
   if (activation != TMU_ACT_SWIGLU && activation != TMU_ACT_RELU) return fail(TMU_ERR_INVALID_ARGUMENT, "unknown activation");
   if (w == nullptr || !w->ln_w || !w->ln_b || !w->w12 || !w->w3) return fail(TMU_ERR_INVALID_ARGUMENT, "transition weights missing");
-  if (!z || !z_out || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if (!z || !z_out) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   const void* al[] = {z, z_out, w->ln_w, w->ln_b, w->w12, w->w3};
   for (const void* q : al)
     if (!aligned16(q)) return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");
+  return TMU_OK;
+}
+
+int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int c_z, int hidden,
+                   int activation, void* status, void* stream) {
+  int rc = check_transition(z, z_out, w, B, L, c_z, hidden, activation);
+  if (rc) return rc;
+  if (!status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   const bool swiglu = activation == TMU_ACT_SWIGLU;
   DeviceStatus* st = static_cast<DeviceStatus*>(status);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return c_z == 128 ? launch_k4<128>(z, z_out, w, B, L, hidden, swiglu, st, s)
                     : launch_k4<256>(z, z_out, w, B, L, hidden, swiglu, st, s);
+}
+
+size_t tmu_pair_block_workspace_bytes(int B, int L, int c_z, int c) {
+  const size_t tm = tmu_workspace_bytes(B, L, c_z, c);
+  if (tm == 0 || c_z < 1) return 0;
+  const size_t pair = c_z == 256 ? (static_cast<size_t>(B) * L * L * c_z * 2 + 255) / 256 * 256 : 0;
+  return tm + pair;
+}
+
+int tmu_pair_block(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w_out,
+                   const tmu_trimul_weights* w_in, const tmu_transition_weights* w_tr, int B, int L, int c_z, int c,
+                   int hidden, int activation, float mix_eps, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_sizes(B, L, c_z, c);
+  if (st) return st;
+  if ((st = check_weights(w_out, true, true))) return st;
+  if ((st = check_weights(w_in, true, true))) return st;
+  if ((st = check_transition(z, z_out, w_tr, B, L, c_z, hidden, activation))) return st;
+  // checked here as well as in each launch, so that a bad argument launches nothing
+  for (const tmu_trimul_weights* w : {w_out, w_in})
+    if ((w->b_emit == nullptr) != (w->b_gate == nullptr))
+      return fail(TMU_ERR_INVALID_ARGUMENT, "b_emit and b_gate must both be set or both be NULL");
+  if (!workspace) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return fail(TMU_ERR_MISALIGNED, "workspace not 256-byte aligned");
+  if (workspace_bytes < tmu_pair_block_workspace_bytes(B, L, c_z, c))
+    return fail(TMU_ERR_WORKSPACE_TOO_SMALL, "workspace too small");
+  if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  DeviceStatus* status = reinterpret_cast<DeviceStatus*>(ws);
+  const size_t cm = cm_bytes(B, L, c);
+  void* a = ws + TMU_STATUS_BYTES;
+  void* b = ws + TMU_STATUS_BYTES + cm;
+  void* x = ws + TMU_STATUS_BYTES + 2 * cm;
+  // c_z = 128 updates in place; the wide kernels write the outgoing result to the pair buffer
+  void* mid = c_z == 256 ? static_cast<void*>(ws + tmu_workspace_bytes(B, L, c_z, c)) : z_out;
+  const PairGeom g = square_geom(B, L, c_z);
+  // the first kernel zeroes the shared status word; the six after it only record errors
+  if ((st = launch_k1(z, mask, w_out, g, a, b, status, s, true))) return st;
+  if ((st = launch_k2(a, b, x, B * c, L, L, L, L, true, status, s))) return st;
+  if ((st = launch_k3(x, z, mid, w_out, B, L, L, mix_eps, status, s, c_z))) return st;
+  if ((st = launch_k1(mid, mask, w_in, g, a, b, status, s))) return st;
+  if ((st = launch_k2(a, b, x, B * c, L, L, L, L, false, status, s))) return st;
+  if ((st = launch_k3(x, mid, z_out, w_in, B, L, L, mix_eps, status, s, c_z))) return st;
+  const bool swiglu = activation == TMU_ACT_SWIGLU;
+  return c_z == 128 ? launch_k4<128>(z_out, z_out, w_tr, B, L, hidden, swiglu, status, s)
+                    : launch_k4<256>(z_out, z_out, w_tr, B, L, hidden, swiglu, status, s);
 }
 
 int tmu_disto_expected(const void* z, const void* w, const float* bias, const float* centres, float* out, int B,

@@ -193,7 +193,10 @@ class Workspace:
         self.pair: torch.Tensor | None = None
 
     def get(self, B: int, L: int, c_z: int, c: int, device) -> torch.Tensor:
-        need = int(_lib.load().tmu_workspace_bytes(B, L, c_z, c))
+        return self.get_bytes(int(_lib.load().tmu_workspace_bytes(B, L, c_z, c)), device)
+
+    def get_bytes(self, need: int, device) -> torch.Tensor:
+        """The buffer, grown to at least ``need`` bytes on ``device``."""
         if self.buf is None or self.buf.numel() < need or self.buf.device != torch.device(device):
             self.buf = torch.empty(need + 256, dtype=torch.uint8, device=device)
         return self.buf
@@ -286,4 +289,24 @@ def transition(z: torch.Tensor, w: TransitionWeights, out: torch.Tensor | None =
     act = _lib.TMU_ACT_SWIGLU if w.activation == "swiglu" else _lib.TMU_ACT_RELU
     _lib.check(lib.tmu_transition(_ptr(z), _ptr(out), ctypes.byref(w.struct), B, L, w.c_z, w.hidden, act,
                                   _ptr(status), _stream_ptr(z.device)), "tmu_transition")
+    return out
+
+
+def pair_block(z: torch.Tensor, mask: torch.Tensor | None, w_out: TrimulWeights, w_in: TrimulWeights,
+               tw: TransitionWeights, mix_eps: float = MIX_EPS_FP16, out: torch.Tensor | None = None,
+               workspace: Workspace | None = None) -> torch.Tensor:
+    """One PairUpdateBlock (tri-mul out, tri-mul in, transition) in one C-ABI call
+    (``tmu_pair_block``; the reference's ``block_forward``, ``mlx_trunk_kernels.py:232-239``).
+    ``out`` may be ``z``; the status word is the workspace's (``workspace.status``)."""
+    lib = _lib.load()
+    B, L = _check_pair(z, w_out.c_z)
+    mask = _check_mask(mask, B, L)
+    out = torch.empty_like(z) if out is None else out
+    workspace = workspace if workspace is not None else Workspace()
+    need = int(lib.tmu_pair_block_workspace_bytes(B, L, w_out.c_z, w_out.c))
+    ws = workspace.get_bytes(need, z.device)
+    act = _lib.TMU_ACT_SWIGLU if tw.activation == "swiglu" else _lib.TMU_ACT_RELU
+    _lib.check(lib.tmu_pair_block(_ptr(z), _ptr(out), _ptr(mask), ctypes.byref(w_out.struct), ctypes.byref(w_in.struct),
+                                  ctypes.byref(tw.struct), B, L, w_out.c_z, w_out.c, tw.hidden, act, float(mix_eps),
+                                  _ptr(ws), ws.numel(), _stream_ptr(z.device)), "tmu_pair_block")
     return out

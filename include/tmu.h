@@ -196,6 +196,20 @@ typedef struct tmu_transition_weights {
 int tmu_transition(const void* z, void* z_out, const tmu_transition_weights* w, int B, int L, int c_z, int hidden,
                    int activation, void* status, void* stream);
 
+/* ---- One PairUpdateBlock in one call: tri-mul outgoing, tri-mul incoming, then the pair
+ * transition, on fp16 z [B, L, L, c_z] (the reference's block_forward, mlx_trunk_kernels.py:232-239;
+ * unfused order mlx_trunk.py:93-99).  Seven launches on `stream`, chained with programmatic
+ * dependent launch: K1 K2 K3 outgoing, K1 K2 K3 incoming, K4.  z_out may equal z.  At c_z = 128
+ * both updates run in place on z_out; at c_z = 256 (whose kernels cannot write over their input)
+ * the outgoing update goes to a pair buffer at the end of the workspace.  The workspace
+ * (tmu_pair_block_workspace_bytes bytes, 256-byte aligned) starts with the status word, zeroed by
+ * the first kernel and shared by all seven (tmu_read_status).  Constraints: those of tmu_trimul
+ * and tmu_transition. */
+size_t tmu_pair_block_workspace_bytes(int B, int L, int c_z, int c);
+int tmu_pair_block(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w_out,
+                   const tmu_trimul_weights* w_in, const tmu_transition_weights* w_tr, int B, int L, int c_z, int c,
+                   int hidden, int activation, float mix_eps, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Distogram expected distance (K5), the convergence signal of adaptive recycling
  * (var_adaptive_loops.py:43-46): out[b,i,j] = sum_k softmax((z[b,i,j] + z[b,j,i]) @ w^T + bias)_k
  * * centres[k].  z [B, L, L, c_z] fp16 (c_z = 128 or 256), w fp16 [n_bins, c_z] (the head's

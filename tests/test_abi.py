@@ -105,3 +105,35 @@ def test_pair_cond_argument_checks_need_no_gpu(lib):
     assert lib.tmu_pair_cond_workspace_bytes(1, 16, 512, 256, 2) == 3 * 16 * 16 * 256 * 2 + 16 * 16 * 512 * 2
     assert lib.tmu_pair_cond_workspace_bytes(1, 5, 256, 128, 0) == 6400 + 12800  # terms rounded up to 256 B
     assert lib.tmu_pair_cond_workspace_bytes(0, 16, 512, 256, 2) == 0
+
+
+def test_pair_block_workspace_and_argument_checks_need_no_gpu(lib):
+    """tmu_pair_block: the workspace is the tri-mul's plus, at c_z = 256, one pair buffer; bad
+    arguments are rejected before anything is launched (codes: 1 invalid argument, 2 misaligned,
+    3 workspace too small, 4 unsupported).  The pointers below are never dereferenced."""
+    for B, L in ((1, 76), (2, 146)):
+        assert lib.tmu_pair_block_workspace_bytes(B, L, 128, 128) == lib.tmu_workspace_bytes(B, L, 128, 128)
+        pair = (B * L * L * 256 * 2 + 255) // 256 * 256
+        assert lib.tmu_pair_block_workspace_bytes(B, L, 256, 256) == lib.tmu_workspace_bytes(B, L, 256, 256) + pair
+    assert lib.tmu_pair_block_workspace_bytes(0, 10, 128, 128) == 0
+
+    fake = lambda i: ctypes.c_void_p(0x100000 + 0x1000 * i)  # noqa: E731  16- and 256-byte aligned
+    w = _lib.TmuTrimulWeights(*(fake(i) if i not in (3, 7, 9) else None for i in range(10)))  # no biases
+    tw = _lib.TmuTransitionWeights(fake(20), fake(21), fake(22), fake(23))
+    need = lib.tmu_pair_block_workspace_bytes(1, 64, 128, 128)
+
+    def call(c=128, hidden=256, act=0, w_in=w, tw_=tw, ws=fake(30), nbytes=need, eps=1e-5):
+        return lib.tmu_pair_block(fake(40), fake(41), None, ctypes.byref(w), ctypes.byref(w_in), ctypes.byref(tw_),
+                                  1, 64, c, c, hidden, act, eps, ws, nbytes, None)
+
+    assert call(c=192) == 4
+    assert call(hidden=100) == 4
+    assert call(act=5) == 1
+    assert call(tw_=_lib.TmuTransitionWeights()) == 1
+    assert call(w_in=_lib.TmuTrimulWeights()) == 1
+    one_bias = _lib.TmuTrimulWeights(*(fake(i) if i not in (3, 9) else None for i in range(10)))  # b_emit only
+    assert call(w_in=one_bias) == 1
+    assert call(ws=None) == 1
+    assert call(ws=ctypes.c_void_p(0x100010)) == 2
+    assert call(nbytes=need - 1) == 3
+    assert call(eps=0.0) == 1
