@@ -238,3 +238,59 @@ def test_trunk_params_refuses_other_dtypes():
 
     with pytest.raises(ValueError, match="fp16"):
         trunk_params(FoldingTrunk(1, 128, 128, hidden=256, seed=0), dtype=torch.bfloat16, device="cpu")
+
+
+# ---------------------------------------------------------------- drop-in module surface (var_mlx_trunk.py:24-46)
+
+def _tiny_trunk(seed):
+    from esmfold2_mlx_b200.synthetic import FoldingTrunk
+
+    return FoldingTrunk(1, 128, 128, hidden=256, seed=seed)
+
+
+def test_trunk_module_surface_and_no_cpu_fallback():
+    """``CUDAFoldingTrunk`` keeps the reference module's surface (``params``, ``_fn``, no-op
+    ``set_chunk_size`` / ``set_kernel_backend``, an ``nn.Module`` whose forward hooks see the pair
+    tensor, as ``tools/regression_check.py:73-77`` reads it), and its compute path refuses tensors
+    that are not on a CUDA device instead of falling back to another implementation."""
+    from esmfold2_mlx_b200.trunk import CUDAFoldingTrunk, make_trunk
+
+    t = CUDAFoldingTrunk(_tiny_trunk(1), device="cpu")
+    assert isinstance(t, nn.Module) and callable(t._fn) and len(t.params) == 1
+    assert set(t.params[0]) >= {"out", "in", "tw"}
+    assert t.set_chunk_size(64) is None and t.set_kernel_backend("triton") is None
+    seen = []
+    t.register_forward_pre_hook(lambda mod, args, kwargs: seen.append(args[0] if args else kwargs["pair"]),
+                                with_kwargs=True)
+    pair = torch.zeros(1, 8, 8, 128)
+    with pytest.raises(TypeError, match="CUDA"):
+        t(pair)
+    assert len(seen) == 1 and seen[0] is pair
+    with pytest.raises(ValueError, match="fp16"):
+        make_trunk(torch.float32)
+
+
+def test_6b_variant_wraps_all_four_trunk_stacks():
+    """``var_6b_mlx_trunks16k.py:19-32``: folding trunk, lm_encoder (when present), parcae coda and
+    the confidence head's trunk each become the B200 module; applying twice keeps them."""
+    from esmfold2_mlx_b200 import var_6b_cuda_trunks16 as v6
+    from esmfold2_mlx_b200.trunk import CUDAFoldingTrunk
+
+    def model(with_lm):
+        m = nn.Module()
+        m.folding_trunk, m.parcae_coda = _tiny_trunk(1), _tiny_trunk(2)
+        m.lm_encoder = _tiny_trunk(3) if with_lm else None
+        m.confidence_head = nn.Module()
+        m.confidence_head.folding_trunk = _tiny_trunk(4)
+        return m
+
+    m = model(True)
+    v6.apply(m, device="cpu")
+    stacks = (m.folding_trunk, m.lm_encoder, m.parcae_coda, m.confidence_head.folding_trunk)
+    assert all(isinstance(s, CUDAFoldingTrunk) for s in stacks)
+    v6.apply(m, device="cpu")
+    assert all(a is b for a, b in zip(stacks, (m.folding_trunk, m.lm_encoder, m.parcae_coda,
+                                                 m.confidence_head.folding_trunk)))
+    m = model(False)
+    v6.apply(m, device="cpu")
+    assert m.lm_encoder is None and isinstance(m.parcae_coda, CUDAFoldingTrunk)
