@@ -39,25 +39,26 @@ def _ulp16(x: torch.Tensor) -> torch.Tensor:
     return 2.0 ** (torch.floor(torch.log2(ax)) - 10)
 
 
-@pytest.mark.parametrize("tag", ["B1L12", "B2L7"])
-def test_pair_cond_matches_reference_code(gold, tag):
+@pytest.mark.parametrize("name,tag", [("pc", "B1L12"), ("pc", "B2L7"), ("pc2", "B1L64")])
+def test_pair_cond_matches_reference_code(gold, name, tag):
     d, meta = gold
-    head = DiffusionHead(**meta["pc"])
-    head.load_state_dict({k[5:]: torch.from_numpy(d[k]) for k in d.files if k.startswith("pc_w/")})
+    head = DiffusionHead(**meta[name])
+    pre = f"{name}_w/"
+    head.load_state_dict({k[len(pre):]: torch.from_numpy(d[k]) for k in d.files if k.startswith(pre)})
     p = pco.pair_cond_params(head)
-    zt = torch.from_numpy(d[f"pc/{tag}/z_trunk"])
-    rp = torch.from_numpy(d[f"pc/{tag}/rel_pos"])
+    zt = torch.from_numpy(d[f"{name}/{tag}/z_trunk"]).float()
+    rp = torch.from_numpy(d[f"{name}/{tag}/rel_pos"]).float()
     got = pco.pair_biases_fp16(p, zt, rp)
-    ref = torch.from_numpy(d[f"pc/{tag}/bias"].astype(np.float32))
+    ref = torch.from_numpy(d[f"{name}/{tag}/bias"].astype(np.float32))
     B, L = zt.shape[:2]
-    assert got.shape == ref.shape == (meta["pc"]["n_blocks"], B, meta["pc"]["heads"], L, L)
+    assert got.shape == ref.shape == (meta[name]["n_blocks"], B, meta[name]["heads"], L, L)
     diff = (got - ref).abs()
     scale = float(_ulp16(ref.abs().max()))
     assert float(diff.max()) <= 2 * scale, f"max diff {float(diff.max()):.3g} > 2 x {scale:.3g}"
     assert float(diff.norm() / ref.norm()) <= 1e-3
 
 
-@pytest.mark.parametrize("tag", ["B1L9", "B2L5"])
+@pytest.mark.parametrize("tag", ["B1L9", "B2L5", "B1L20c128"])
 def test_parcae_step_matches_reference_code(gold, tag):
     d, _ = gold
     t = {k: torch.from_numpy(d[f"parcae/{tag}/{k}"]) for k in
