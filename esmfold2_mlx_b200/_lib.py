@@ -96,6 +96,7 @@ SIGNATURES = {
     "tmu_set_wait_timeout_ns": (_ull, [_ull]),
     "tmu_reset_status": (_i, [_vp, _vp]),
     "tmu_read_status": (_i, [_vp, _vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "tmu_read_first_error": (_i, [_vp, _vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "tmu_project_gate": (_i, [_vp, _vp, _W, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tmu_contract": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "tmu_emit_residual": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _f, _vp, _vp]),

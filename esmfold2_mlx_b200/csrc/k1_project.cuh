@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   // swizzle needs 1024-byte aligned; a misaligned base is reported, never computed on.
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
-    if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x1ff;
+    if (threadIdx.x == 0) record_status(p.status, kStatusLayout, 0x1ff);
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
@@ -168,6 +168,9 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   }
   griddep_trigger();
   griddep_wait();
+  // Block 0 clears this call's error fields once the previous kernel (which may share the word)
+  // has finished.  Another CTA of this grid that gave up on a wait before block 0 got here
+  // would have its per-call record cleared; its since-reset record (first_code) survives.
   if (p.reset_status && blockIdx.x == 0 && threadIdx.x == 0) {
     p.status->code = 0;
     p.status->site = 0;

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   // swizzle needs 1024-byte aligned; a misaligned base is reported, never computed on.
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
-    if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x3ff;
+    if (threadIdx.x == 0) record_status(p.status, kStatusLayout, 0x3ff);
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);

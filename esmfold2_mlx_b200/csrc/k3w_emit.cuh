@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
   constexpr uint32_t IDESC = idesc_f16_f32(128, TILE, false, false);
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
-    if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x31f;
+    if (threadIdx.x == 0) record_status(p.status, kStatusLayout, 0x31f);
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);

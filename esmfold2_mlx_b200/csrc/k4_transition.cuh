@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
   constexpr int NQ = SWIGLU ? 1 : 2;
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
-    if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x4ff;
+    if (threadIdx.x == 0) record_status(p.status, kStatusLayout, 0x4ff);
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);

@@ -67,7 +67,7 @@ __global__ void __launch_bounds__(kThreads, 1) disto_kernel(const __grid_constan
   constexpr uint32_t IDESC = idesc_f16_f32(128, NBINS, false, false);
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
-    if (threadIdx.x == 0 && atomicCAS(&p.status->code, 0u, kStatusLayout) == 0u) p.status->site = 0x5ff;
+    if (threadIdx.x == 0) record_status(p.status, kStatusLayout, 0x5ff);
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);

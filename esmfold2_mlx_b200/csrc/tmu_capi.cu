@@ -984,6 +984,18 @@ int tmu_read_status(const void* status, void* stream, int* code, int* site) {
   return TMU_OK;
 }
 
+int tmu_read_first_error(const void* status, void* stream, int* code, int* site) {
+  if (status == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "status is NULL");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  DeviceStatus h;
+  e = cudaMemcpy(&h, status, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  if (code) *code = static_cast<int>(h.first_code);
+  if (site) *site = static_cast<int>(h.first_site);
+  return TMU_OK;
+}
+
 int tmu_project_gate(const void* z, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z, int c,
                      void* a, void* b, void* status, void* stream) {
   int st = check_sizes(B, L, c_z, c);
@@ -1091,6 +1103,7 @@ int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_t
   if ((st = check_weights(w, true, true))) return st;
   if (!z || !z_out) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   if (!aligned16(z) || !aligned16(z_out)) return fail(TMU_ERR_MISALIGNED, "z not 16-byte aligned");
+  if (status != nullptr && !aligned16(status)) return fail(TMU_ERR_MISALIGNED, "status not 16-byte aligned");
   if (!(mix_eps > 0.f)) return fail(TMU_ERR_INVALID_ARGUMENT, "mix_eps must be positive");
   if ((st = check_wide_alias(z, z_out, B, L, c_z))) return st;
   const size_t cm = cm_bytes(B, L, c);
@@ -1233,7 +1246,7 @@ int tmu_pair_cond(const float* z_trunk, const float* rel_pos, const tmu_pair_con
   if (!z_trunk || !rel_pos || !out || !workspace || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
   const int c_in = c_trunk + c_rel;
   if (workspace_bytes < tmu_pair_cond_workspace_bytes(B, L, c_in, c_pair, w->n_transitions))
-    return fail(TMU_ERR_INVALID_ARGUMENT, "workspace too small");
+    return fail(TMU_ERR_WORKSPACE_TOO_SMALL, "workspace too small");
   const void* al[] = {z_trunk, rel_pos, out, workspace, w->ln_w, w->ln_b, w->proj, w->bias_w};
   for (const void* q : al)
     if (!aligned16(q)) return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");
@@ -1298,7 +1311,8 @@ int tmu_parcae_step(const float* z, const float* z_init, const float* refined, c
   if (w == nullptr || !w->ln_w || !w->ln_b || !w->a || !w->b_split)
     return fail(TMU_ERR_INVALID_ARGUMENT, "parcae weights missing");
   if (!z || !z_init || !refined || !z_out || !workspace || !status) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL tensor");
-  if (workspace_bytes < tmu_parcae_workspace_bytes(B, L, c_z)) return fail(TMU_ERR_INVALID_ARGUMENT, "workspace too small");
+  if (workspace_bytes < tmu_parcae_workspace_bytes(B, L, c_z))
+    return fail(TMU_ERR_WORKSPACE_TOO_SMALL, "workspace too small");
   const void* al[] = {z, z_init, refined, z_out, workspace, w->ln_w, w->ln_b, w->a, w->b_split};
   for (const void* q : al)
     if (!aligned16(q)) return fail(TMU_ERR_MISALIGNED, "pointer not 16-byte aligned");

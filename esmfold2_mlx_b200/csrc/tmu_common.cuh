@@ -22,12 +22,27 @@ namespace tmu {
 // ------------------------------------------------------------------------------------------
 // status word (first bytes of the caller's workspace)
 // ------------------------------------------------------------------------------------------
+// The device status word (the first bytes of a TMU_STATUS_BYTES block).  code/site/block hold the
+// first error of the current call: the first kernel of tmu_trimul / tmu_pair_block clears them.
+// first_code/first_site hold the first error since the block was last cleared by
+// tmu_reset_status, which no kernel clears, so one read covers a whole sequence of calls.
 struct DeviceStatus {
   unsigned int code;   // 0 ok, else a TMU_STATUS_* value (tmu.h)
   unsigned int site;   // kernel-specific id of the wait that gave up
   unsigned int block;  // blockIdx.x of the first CTA that gave up
   unsigned int pad;
+  unsigned int first_code;  // first error since tmu_reset_status
+  unsigned int first_site;
 };
+
+// Record an error: the first one wins in both the per-call and the since-reset fields.
+__device__ __forceinline__ void record_status(DeviceStatus* s, unsigned int code, unsigned int site) {
+  if (atomicCAS(&s->code, 0u, code) == 0u) {
+    s->site = site;
+    s->block = blockIdx.x;
+  }
+  if (atomicCAS(&s->first_code, 0u, code) == 0u) s->first_site = site;
+}
 
 constexpr unsigned int kStatusDeviceTimeout = 6;  // TMU_ERR_DEVICE_TIMEOUT in tmu.h
 constexpr unsigned int kStatusLayout = 9;         // TMU_ERR_SMEM_LAYOUT in tmu.h
@@ -50,10 +65,7 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __device__ __forceinline__ void raise_abort(const WaitCtx& ctx, unsigned int site) {
   *ctx.abort = 1;
-  if (atomicCAS(&ctx.status->code, 0u, kStatusDeviceTimeout) == 0u) {
-    ctx.status->site = site;
-    ctx.status->block = blockIdx.x;
-  }
+  record_status(ctx.status, kStatusDeviceTimeout, site);
   __threadfence();
 }
 

@@ -142,6 +142,33 @@ def read_status(status: torch.Tensor) -> tuple[int, int]:
     return code.value, site.value
 
 
+def reset_status(status: torch.Tensor) -> None:
+    """Zero a status block on the current stream (both its per-call and since-reset records)."""
+    _lib.check(_lib.load().tmu_reset_status(_ptr(status), _stream_ptr(status.device)), "tmu_reset_status")
+
+
+def read_first_error(status: torch.Tensor) -> tuple[int, int]:
+    """Synchronise the current stream and return (code, site) of the first error recorded in
+    ``status`` since :func:`reset_status`, by any call."""
+    lib = _lib.load()
+    code, site = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(lib.tmu_read_first_error(_ptr(status), _stream_ptr(status.device), ctypes.byref(code),
+                                        ctypes.byref(site)), "tmu_read_first_error")
+    return code.value, site.value
+
+
+def raise_for_status(code: int, site: int, where: str) -> None:
+    """Raise :class:`TmuError` for a non-zero device status (a bounded wait that gave up, or a
+    kernel that found its shared memory misaligned), naming the kernel site that recorded it."""
+    if code != 0:
+        raise _lib.TmuError(code, where, f"device status recorded at kernel site {site:#x}; the output is invalid")
+
+
+def check_status(status: torch.Tensor, where: str) -> None:
+    """Synchronise, read the call's status and raise if a kernel recorded an error."""
+    raise_for_status(*read_status(status), where)
+
+
 def project_gate(z: torch.Tensor, mask: torch.Tensor | None, w: TrimulWeights, status: torch.Tensor | None = None):
     """K1: returns channel-major (a, b), each [B*c, L, row_pitch(L)] fp16 (pad columns unset)."""
     lib = _lib.load()

@@ -22,6 +22,7 @@ import torch
 
 from . import _lib
 from .ops import _ptr, _stream_ptr, new_status
+from .ops import check_status as check_status_fn
 
 
 @dataclass
@@ -84,9 +85,13 @@ def workspace_bytes(B: int, L: int, c_in: int, c_pair: int, n_transitions: int) 
 
 
 def pair_biases(w: PairCondWeights, z_trunk: torch.Tensor, rel_pos: torch.Tensor, out: torch.Tensor | None = None,
-                workspace: torch.Tensor | None = None, status: torch.Tensor | None = None) -> torch.Tensor:
+                workspace: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                check_status: bool = False) -> torch.Tensor:
     """The token transformer's pair biases ``[nb, B, H, L, L]`` fp16 from fp32 ``z_trunk``
-    [B, L, L, c_trunk] and ``rel_pos`` [B, L, L, c_rel] (``mlx_diffusion16.py:81-87``)."""
+    [B, L, L, c_trunk] and ``rel_pos`` [B, L, L, c_rel] (``mlx_diffusion16.py:81-87``).
+
+    A device-side error (a bounded wait that gave up) lands in ``status``; with ``check_status``
+    the call synchronises and raises ``TmuError`` if one was recorded."""
     for name, t in (("z_trunk", z_trunk), ("rel_pos", rel_pos)):
         if not t.is_cuda or t.dtype != torch.float32 or t.dim() != 4 or not t.is_contiguous():
             raise ValueError(f"{name} must be a contiguous CUDA fp32 [B, L, L, C] tensor")
@@ -106,4 +111,6 @@ def pair_biases(w: PairCondWeights, z_trunk: torch.Tensor, rel_pos: torch.Tensor
     _lib.check(lib.tmu_pair_cond(_ptr(z_trunk), _ptr(rel_pos), ctypes.byref(w.struct), B, L, z_trunk.shape[3],
                                  rel_pos.shape[3], w.c_pair, w.hidden, w.n_bias, w.heads, _ptr(out), _ptr(workspace),
                                  workspace.numel(), _ptr(status), _stream_ptr(dev)), "tmu_pair_cond")
+    if check_status:
+        check_status_fn(status, "tmu_pair_cond")
     return out

@@ -18,7 +18,7 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib
-from .ops import _ptr, _stream_ptr, new_status
+from .ops import _ptr, _stream_ptr, check_status as _check_status, new_status
 
 
 def split_bf16x3(m: torch.Tensor) -> torch.Tensor:
@@ -68,8 +68,12 @@ class ParcaeWeights:
 
 def parcae_step(z: torch.Tensor, z_init: torch.Tensor, refined: torch.Tensor, w: ParcaeWeights,
                 out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
-                status: torch.Tensor | None = None) -> torch.Tensor:
-    """``a * z + LN(z_init + refined) @ B^T`` for fp32 [B, L, L, c_z] tensors (``out`` may be ``z``)."""
+                status: torch.Tensor | None = None, check_status: bool = False) -> torch.Tensor:
+    """``a * z + LN(z_init + refined) @ B^T`` for fp32 [B, L, L, c_z] tensors (``out`` may be ``z``).
+
+    The kernels record a device-side error (a bounded wait that gave up) in ``status``; with
+    ``check_status`` the call synchronises and raises ``TmuError`` if one was recorded, otherwise
+    the caller reads ``status`` (``ops.read_status``) when it next synchronises."""
     for name, t in (("z", z), ("z_init", z_init), ("refined", refined)):
         if not t.is_cuda or t.dtype != torch.float32 or t.dim() != 4 or not t.is_contiguous() or t.shape != z.shape:
             raise ValueError(f"{name} must be a contiguous CUDA fp32 tensor shaped like z")
@@ -85,14 +89,17 @@ def parcae_step(z: torch.Tensor, z_init: torch.Tensor, refined: torch.Tensor, w:
     _lib.check(lib.tmu_parcae_step(_ptr(z), _ptr(z_init), _ptr(refined), ctypes.byref(w.struct), _ptr(out), B, L, c,
                                    _ptr(workspace), workspace.numel(), _ptr(status), _stream_ptr(z.device)),
                "tmu_parcae_step")
+    if check_status:
+        _check_status(status, "tmu_parcae_step")
     return out
 
 
 def loop_step(lm_encoder, folding_trunk, w: ParcaeWeights, lz: torch.Tensor, z: torch.Tensor, z_init: torch.Tensor,
-              mask=None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+              mask=None, workspace: torch.Tensor | None = None, check_status: bool = False) -> torch.Tensor:
     """One step of the 6B recycling loop as ``_step`` composes it (``var_6b_mlx_loop.py:67-71``):
     ``refined = lm_encoder(lz)``, the parcae recurrence, then the folding trunk.  Both trunks are
     modules with the reference trunk call (``CUDAFoldingTrunk``); every tensor stays on the GPU."""
     refined = lm_encoder(lz, pair_attention_mask=mask).float().contiguous()
-    zn = parcae_step(z.float().contiguous(), z_init.float().contiguous(), refined, w, workspace=workspace)
+    zn = parcae_step(z.float().contiguous(), z_init.float().contiguous(), refined, w, workspace=workspace,
+                     check_status=check_status)
     return folding_trunk(zn, pair_attention_mask=mask)

@@ -64,7 +64,8 @@ def transition_(p: dict, z: torch.Tensor, workspace: ops.Workspace | None = None
     fp16 GEMM output, three fp16 element-wise ops for SwiGLU, one-rounding ``addmm`` residual.
     c_z = 128 and 256 run the fused kernel K4 (``tmu_transition``); other shapes run torch ops."""
     if p["tw"].fused:
-        status = workspace.aux_status(z.device) if workspace is not None else None
+        # the tri-mul workspace's status word, so one read after the pass covers every kernel
+        status = workspace.status if workspace is not None and workspace.status is not None else None
         return ops.transition(z, p["tw"], out=z, status=status)
     c_z = z.shape[-1]
     h = F.layer_norm(z, (c_z,), p["ln_w"], p["ln_b"], EPS)
@@ -98,10 +99,16 @@ def trunk_forward(params: list, z: torch.Tensor, mask=None, mix_eps: float = ops
     """z in any float dtype on any device; computed in fp16 on the params' device; returns fp32
     there (``mlx_trunk_kernels.py:242-249``)."""
     device = params[0]["out"].device
+    if device.type != "cuda":
+        raise TypeError(f"the B200 trunk runs on a CUDA device; its weights are on {device}")
     z = z.to(device=device, dtype=torch.float16).contiguous().clone()
     if mask is not None:
         mask = mask.to(device=device, dtype=torch.float16).contiguous()
     ws = workspace if workspace is not None else ops.Workspace()
+    # Size the workspace before zeroing its status word, so the word stays put for the pass: the
+    # kernels of all blocks record into it and its since-reset record is read once afterwards.
+    ws.get(z.shape[0], z.shape[1], params[0]["out"].c_z, params[0]["out"].c, device)
+    ops.reset_status(ws.status)
     for p in params:
         block_forward(p, z, mask, mix_eps, ws)
     return z.float()
@@ -142,15 +149,50 @@ class CUDAFoldingTrunk(nn.Module):
     once per (B, L, mask present, device) -- the reference recompiles its MLX trunk per new L in
     the same way (``var_mlx_trunk.py:28-30``) -- so a 24-block pass is one launch instead of
     ~170; up to ``max_graphs`` shapes are kept (least recently used evicted), each holding its
-    own static buffers.  The graph's output buffer is reused, so the returned tensor is a copy."""
+    own static buffers.  The graph's output buffer is reused, so the returned tensor is a copy.
+
+    Device-side errors (a bounded wait in a kernel that gave up, which leaves the output invalid)
+    are reported per pass through the pass's status word, copied to the host after the pass:
+    ``check_status="deferred"`` (default) raises ``TmuError`` at the start of the next call (or
+    at :meth:`check_status`), which costs no synchronisation; ``"sync"`` waits for the pass and
+    raises before returning; ``"off"`` leaves the word unread.  Passes run inside the caller's
+    own stream capture are not checked (the caller reads the status word after its replay)."""
 
     def __init__(self, folding_trunk, dtype=torch.float16, device="cuda", biases: list | None = None,
-                 graphs: bool = True, max_graphs: int = 4):
+                 graphs: bool = True, max_graphs: int = 4, check_status: str = "deferred"):
         super().__init__()
+        if check_status not in ("deferred", "sync", "off"):
+            raise ValueError("check_status must be 'deferred', 'sync' or 'off'")
         self.params = trunk_params(folding_trunk, dtype, device, biases)
         self._fn = make_trunk(dtype)
         self.graphs, self.max_graphs = graphs, max_graphs
         self._graph_cache: dict = {}
+        self.check_mode = check_status
+        self._pending = None  # (event, pinned host copy of the status word) of the last pass
+        self._status_host = None
+
+    def _note_status(self, status):
+        """Copy the pass's status word to pinned host memory behind the pass (no sync)."""
+        if self.check_mode == "off" or status is None:
+            return
+        if self._status_host is None:
+            self._status_host = torch.zeros(8, dtype=torch.int32).pin_memory()
+        self._status_host.copy_(status[:32].view(torch.int32), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._pending = ev
+        if self.check_mode == "sync":
+            self.check_status()
+
+    def check_status(self):
+        """Raise ``TmuError`` if the last unchecked pass recorded a device-side error (waits for
+        that pass to finish)."""
+        ev, self._pending = self._pending, None
+        if ev is None:
+            return
+        ev.synchronize()
+        h = self._status_host
+        ops.raise_for_status(int(h[4]), int(h[5]), "CUDAFoldingTrunk pass")
 
     # FoldingTrunk API the model calls on its trunk; the fused kernels ignore both.
     def set_chunk_size(self, chunk_size):
@@ -186,15 +228,21 @@ class CUDAFoldingTrunk(nn.Module):
         if entry.mask_in is not None:
             entry.mask_in.copy_(mask)
         entry.graph.replay()
+        self._note_status(entry.fn.workspace.status)
         return entry.out.clone()
 
     def forward(self, pair, pair_attention_mask=None):
+        capturing = pair.is_cuda and torch.cuda.is_current_stream_capturing()
+        if not capturing:
+            self.check_status()  # the previous pass's device status (deferred mode)
         # A single-chain fold has an all-ones mask; skipping it saves a multiply per tri-mul.
         mask = None
         if pair_attention_mask is not None and not bool(pair_attention_mask.all()):
             mask = pair_attention_mask
-        if self.graphs and pair.is_cuda and not torch.cuda.is_current_stream_capturing():
+        if self.graphs and pair.is_cuda and not capturing:
             out = self._graph_pass(pair, mask)
         else:
             out = self._fn(self.params, pair, mask)
+            if not capturing:
+                self._note_status(getattr(getattr(self._fn, "workspace", None), "status", None))
         return out.to(pair.device)

@@ -9,6 +9,8 @@ import torch
 
 from .trunk import CUDAFoldingTrunk
 
+DEVICE = "cuda"  # where the weights live when apply() is given no device (the current CUDA device)
+
 
 def _wrap(trunk, device):
     if not isinstance(trunk, CUDAFoldingTrunk):
@@ -16,7 +18,8 @@ def _wrap(trunk, device):
     return trunk
 
 
-def apply(model, device="cuda"):
+def apply(model, device=None):
+    device = DEVICE if device is None else device
     model.folding_trunk = _wrap(model.folding_trunk, device)
     if getattr(model, "lm_encoder", None) is not None:
         model.lm_encoder = _wrap(model.lm_encoder, device)

@@ -9,6 +9,9 @@ import torch
 
 from .trunk import CUDAFoldingTrunk
 
+DEVICE = "cuda"  # where the weights live when apply() is given no device (the current CUDA device)
 
-def apply(model, device="cuda"):
-    model.folding_trunk = CUDAFoldingTrunk(model.folding_trunk, dtype=torch.float16, device=device)
+
+def apply(model, device=None):
+    model.folding_trunk = CUDAFoldingTrunk(model.folding_trunk, dtype=torch.float16,
+                                           device=DEVICE if device is None else device)

@@ -20,10 +20,14 @@
  *   - a, b, x: [B*c, L, Lpad] channel-major, Lpad = tmu_row_pitch(L) (= L rounded up to 8);
  *     the pad columns are never read.
  *   - stream: a cudaStream_t passed as void*; every launch goes on it, nothing synchronises.
- *   - status: device memory of at least TMU_STATUS_BYTES holding the device-side status word;
- *     kernels record a bounded-wait timeout there (read it with tmu_read_status).
- *   - Supported now: c_z == c == 128, 1 <= L <= 8192, B*c <= 65535.  Other sizes return
- *     TMU_ERR_UNSUPPORTED.
+ *   - status: device memory of at least TMU_STATUS_BYTES (16-byte aligned) holding the device-side
+ *     status word; kernels record a bounded-wait timeout there.  It keeps two records: the
+ *     current call's first error (tmu_read_status; cleared by the first kernel of tmu_trimul and
+ *     tmu_pair_block) and the first error since the block was last zeroed by tmu_reset_status
+ *     (tmu_read_first_error; no kernel clears it, so one read covers a whole sequence of calls).
+ *   - Widths: c_z == c, 128 or 256 (the released ESMFold2 trunk's width, mlx_trunk.py:4);
+ *     1 <= L <= 8192, B*c <= 65535.  Other sizes return TMU_ERR_UNSUPPORTED.  At c_z = 256,
+ *     z_out must not overlap z (two CTAs share each tile's z): TMU_ERR_INVALID_ARGUMENT.
  *   - Return value: TMU_OK or a TMU_ERR_* code (never aborts the process).  Device-side
  *     conditions (TMU_ERR_DEVICE_TIMEOUT, TMU_ERR_SMEM_LAYOUT) land in the status word.
  */
@@ -99,6 +103,11 @@ int tmu_reset_status(void* status, void* stream);
  * TMU_ERR_DEVICE_TIMEOUT; *site identifies the wait that gave up (0 if none). */
 int tmu_read_status(const void* status, void* stream, int* code, int* site);
 
+/* Like tmu_read_status, but returns the first error recorded in `status` since it was last zeroed
+ * by tmu_reset_status, whichever call recorded it: a caller that runs many calls on one status
+ * word (a 24-block trunk pass) zeroes it once, runs the calls and reads it once. */
+int tmu_read_first_error(const void* status, void* stream, int* code, int* site);
+
 /* K1: n = LN(z); a, b = gated projections of n, channel-major.  outputs a, b: [B*c, L, Lpad]. */
 int tmu_project_gate(const void* z, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z,
                      int c, void* a, void* b, void* status, void* stream);
@@ -150,7 +159,8 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
                int c, int outgoing, float mix_eps, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Size cap of tmu_trimul_noalloc: each of its three channel-major buffers (a, b, x) must fit in
- * this many bytes, i.e. B * c * L * tmu_row_pitch(L) * 2 <= 8 MiB (B = 1, c = 128: L <= 178). */
+ * this many bytes, i.e. B * c * L * tmu_row_pitch(L) * 2 <= 8 MiB: one fold up to L = 178 at
+ * c = 128 and up to L = 126 at c = 256. */
 #define TMU_NOALLOC_MAX_BUFFER_BYTES (8u << 20)
 
 /* One triangle update, z_out = z + tri-mul(z), like tmu_trimul but without a workspace argument
@@ -166,14 +176,18 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
  * (tmu_last_error); use tmu_trimul for them.  The call itself issues no cudaMalloc or cudaFree.
  *
  * - The first call on each device looks up that device's address of the scratch array
- *   (cudaGetSymbolAddress, with the device current) and caches it: make that first call before
- *   any stream capture on the device.
+ *   (cudaGetSymbolAddress, with the device current) and caches it for the life of the process:
+ *   make that first call before any stream capture on the device, and do not keep using this
+ *   entry point after cudaDeviceReset (the cached address would point into the destroyed
+ *   context).
+ * - At c_z = 256, z_out must not overlap z (TMU_ERR_INVALID_ARGUMENT), as for tmu_trimul.
  * - All calls on a device share the one scratch array, which keeps the previous call's
  *   contents.  The call clears the status word it uses; everything else is rewritten before it
  *   is read.  Calls that can overlap on the GPU (different streams without ordering, or several
  *   host threads) race on the scratch and give wrong results: serialise them.
- * - `status`: device memory of TMU_STATUS_BYTES for the bounded-wait status word (read it with
- *   tmu_read_status), or NULL to use the scratch's own word, which the caller cannot read. */
+ * - `status`: device memory of TMU_STATUS_BYTES, 16-byte aligned, for the bounded-wait status word
+ *   (read it with tmu_read_status), or NULL to use the scratch's own word, which the caller
+ *   cannot read.  The call zeroes the whole status block before its first kernel. */
 int tmu_trimul_noalloc(const void* z, void* z_out, const void* mask, const tmu_trimul_weights* w, int B, int L,
                        int c_z, int c, int outgoing, float mix_eps, void* status, void* stream);
 

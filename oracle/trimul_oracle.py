@@ -243,6 +243,106 @@ def _ln(x, w, b, eps, dtype):
 
 
 # --------------------------------------------------------------------------------------
+# a slab of rows of one update, for lengths whose full update is too slow on the CPU
+# --------------------------------------------------------------------------------------
+
+
+def _gated_half(p: dict, z: torch.Tensor, mask, half: int, exact: bool) -> torch.Tensor:
+    """One gated operand (half 0: a, half 1: b) on a [B, rows, cols, c_z] grid, channel-major
+    [B, c, rows, cols]: only the projection columns of that operand (its signal and gate
+    columns), with the same arithmetic as :func:`project_gate_fp16` (``exact``: float64 and no
+    rounding, as :func:`trimul_fp32`)."""
+    c = p["c"]
+    cols = list(range(half * c, half * c + c)) + list(range(2 * c + half * c, 3 * c + half * c))
+    if exact:
+        dt = torch.float64
+        n = _ln(z, p["ln_in_w"], p["ln_in_b"], EPS, dt)
+        proj = n @ p["w_in"][:, cols].to(dt)
+        if p.get("b_in") is not None:
+            proj = proj + p["b_in"][cols].to(dt)
+        v = proj[..., :c] * torch.sigmoid(proj[..., c:])
+        if mask is not None:
+            v = v * mask.to(dt)[..., None]
+        return v.permute(0, 3, 1, 2).contiguous()
+    z = r16(z.float())
+    n = r16(layer_norm(z, p["ln_in_w"], p["ln_in_b"], EPS))
+    proj = n @ p["w_in"][:, cols]
+    if p.get("b_in") is not None:
+        proj = proj + p["b_in"][cols]
+    proj = r16(proj)
+    v = proj[..., :c] / (1.0 + torch.exp(-proj[..., c:]))
+    if mask is not None:
+        v = v * r16(mask.float())[..., None]
+    return r16(v).permute(0, 3, 1, 2).contiguous()
+
+
+def trimul_rows(p: dict, z: torch.Tensor, mask, outgoing: bool, rows, exact: bool = False,
+                mix_eps: float | None = None, chunk: int = 64) -> torch.Tensor:
+    """Rows ``rows`` (a range of i) of ``z + trimul(z)`` without forming the whole update.
+
+    Outgoing, row i needs a[:, i, :] (the projection of z's row i) and all of b; incoming,
+    ``x[d, i, j] = sum_k a[d, k, i] b[d, k, j]`` needs a[:, :, i] (the projection of z's column
+    i) and all of b.  b is projected in chunks of ``chunk`` rows and kept in fp16 (exact: its
+    values are fp16 roundings) or, with ``exact``, in fp32 (float64 arithmetic otherwise; the
+    fp32 storage of b is 2^13 times finer than the fp16 errors this reference measures).
+    With ``exact``, ``p`` comes from ``trimul_params(..., fp16=False)``.  Returns
+    [B, len(rows), L, c_z] in fp32 (fp16 values unless ``exact``) or float64 (``exact``)."""
+    rows = range(rows.start, rows.stop) if isinstance(rows, range) else rows
+    r0, r1 = rows[0], rows[-1] + 1
+    B, L = z.shape[0], z.shape[1]
+    c = p["c"]
+    store = torch.float32 if exact else torch.float16
+    b_all = torch.empty(B, c, L, L, dtype=store)
+    for s in range(0, L, chunk):
+        e = min(L, s + chunk)
+        b_all[:, :, s:e] = _gated_half(p, z[:, s:e], None if mask is None else mask[:, s:e], 1, exact).to(store)
+    if outgoing:
+        a_r = _gated_half(p, z[:, r0:r1], None if mask is None else mask[:, r0:r1], 0, exact)  # [B, c, R, L]
+    else:
+        a_r = _gated_half(p, z[:, :, r0:r1], None if mask is None else mask[:, :, r0:r1], 0, exact)  # [B, c, L, R]
+        a_r = a_r.transpose(2, 3)  # [B, c, R, L]: a[d, k, i] as rows i
+    dt = torch.float64 if exact else torch.float32
+    x = torch.empty(B, c, r1 - r0, L, dtype=dt)
+    for d0 in range(0, c, 16):
+        d1 = min(c, d0 + 16)
+        bb = b_all[:, d0:d1].to(dt).reshape(B * (d1 - d0), L, L)
+        ar = a_r[:, d0:d1].to(dt).reshape(B * (d1 - d0), r1 - r0, L)
+        xr = torch.bmm(ar, bb.transpose(1, 2)) if outgoing else torch.bmm(ar, bb)
+        x[:, d0:d1] = xr.reshape(B, d1 - d0, r1 - r0, L)
+    zr = z[:, r0:r1]
+    if exact:
+        n = _ln(zr, p["ln_in_w"], p["ln_in_b"], EPS, dt)
+        mixn = _ln(x.permute(0, 2, 3, 1), p["ln_mix_w"], p["ln_mix_b"], EPS if mix_eps is None else mix_eps, dt)
+        mixed = mixn @ p["w_emit"].to(dt)
+        if p.get("b_emit") is not None:
+            mixed = mixed + p["b_emit"].to(dt)
+        g = n @ p["w_out_gate"].to(dt)
+        if p.get("b_gate") is not None:
+            g = g + p["b_gate"].to(dt)
+        return zr.to(dt) + mixed * torch.sigmoid(g)
+    out, _ = emit_residual_fp16(p, zr, r16(x), MIX_EPS_FP16 if mix_eps is None else mix_eps)
+    return out
+
+
+def ulps16(ref: torch.Tensor, test: torch.Tensor) -> float:
+    """Largest |test - ref| in fp16 ulps at the reference tensor's scale (the ulp of max |ref|)."""
+    scale = max(float(ref.abs().max()), 2.0**-14)
+    ulp = 2.0 ** (math.floor(math.log2(scale)) - 10)
+    return float((test.double() - ref.double()).abs().max()) / ulp
+
+
+def parity(exact: torch.Tensor, ref16: torch.Tensor, test: torch.Tensor) -> dict:
+    """The parity figures of a CUDA result ``test``: its error against the exact (float64)
+    update, the fp16 oracle's own error against the same (e_ref), and its distance from the
+    oracle in fp16 ulps.  The acceptance rule is e_cuda <= 2 * e_ref + 1e-3 (max-abs and rel-L2)."""
+    e = error_stats(exact, test)
+    er = error_stats(exact, ref16)
+    ok = (e["finite"] and e["max_abs"] <= 2 * er["max_abs"] + 1e-3 and e["rel_l2"] <= 2 * er["rel_l2"] + 1e-3)
+    return {"max_abs": e["max_abs"], "rel_l2": e["rel_l2"], "e_ref_max_abs": er["max_abs"],
+            "e_ref_rel_l2": er["rel_l2"], "max_ulps": ulps16(ref16, test), "within_tolerance": bool(ok)}
+
+
+# --------------------------------------------------------------------------------------
 # transition, block, trunk (mlx_trunk.py:93-109, mlx_trunk_kernels.py:232-249)
 # --------------------------------------------------------------------------------------
 

@@ -1,5 +1,6 @@
-"""K5 (distogram expected distance) against the oracle, and the adaptive-recycling wrapper's
-control flow (var_adaptive_loops.py:76-142) with K5 as its convergence signal."""
+"""K5 (distogram expected distance) against the oracle, the reference-signature hook
+``expected_distance(z, disto_head)``, and the adaptive-recycling wrapper (behaviour of
+var_adaptive_loops.py:76-142) with K5 as its settle signal."""
 
 from __future__ import annotations
 
@@ -32,8 +33,8 @@ def _head(c_z, seed, bias=True):
 def test_expected_distance_matches_oracle(c_z, L, B, bias):
     head = _head(c_z, seed=L, bias=bias)
     z = (pair_tensor(B, L, c_z, L + 1) * 0.5).half()
-    dh = adaptive.DistoHead(head, DEV)
-    got = adaptive.expected_distance(z.to(DEV), dh).cpu()
+    dh = adaptive.ExpectedDistance(head, DEV)
+    got = dh(z.to(DEV)).cpu()
     torch.cuda.synchronize()
     assert ops.read_status(dh.status)[0] == 0
     # the kernel uses the head's weight rounded to fp16; compare with the oracle on that weight
@@ -46,6 +47,19 @@ def test_expected_distance_matches_oracle(c_z, L, B, bias):
     assert float((got - ref32).abs().max()) < 5e-2  # the fp16 weight's own effect, far below 0.6 Å
     # symmetric by construction (z + z^T)
     assert float((got - got.transpose(1, 2)).abs().max()) < 1e-4
+
+
+def test_reference_signature_hook_takes_fp32_output_and_head_module():
+    """``expected_distance(z, disto_head)`` as the reference's wrapper calls it: the trunk's fp32
+    output and the model's head module; equal to K5 on the fp16 values, one device copy per head."""
+    head = _head(128, seed=9).to(DEV)
+    z32 = pair_tensor(1, 40, 128, 8).half().float().to(DEV)
+    e1 = adaptive.expected_distance(z32, head)
+    e2 = adaptive.expected_distance(z32, head)
+    ref = adaptive.ExpectedDistance(head, DEV)(z32.half())
+    torch.cuda.synchronize()
+    assert torch.equal(e1, ref) and torch.equal(e2, ref)
+    assert len(adaptive._evaluators[head]) == 1
 
 
 class _Trunk(nn.Module):
@@ -75,13 +89,13 @@ def test_adaptive_wrapper_stops_when_converged(step, expect_converged):
     inner = _Trunk(step)
     model.folding_trunk = inner
     trunk = adaptive.CUDAAdaptiveTrunk(inner, model)
-    trunk.reset(4)
+    trunk.start_fold(4)
     z = pair_tensor(1, L, 128, 5).half().float().to(DEV)
     outs = [trunk(z) for _ in range(4)]  # the model's recycling loop: 4 trunk calls
     if expect_converged:
         assert trunk.converged and inner.calls == 2 and trunk.passes == 2
-        assert trunk.history[0]["disto_p95"] < adaptive.THRESHOLD
+        assert trunk.fold.changes[0] < adaptive.SETTLE_A
         assert outs[3] is outs[1]  # the converged output is returned without running the trunk
     else:
         assert not trunk.converged and inner.calls == 4
-        assert all(h["disto_p95"] >= adaptive.THRESHOLD for h in trunk.history)
+        assert all(ch >= adaptive.SETTLE_A for ch in trunk.fold.changes)

@@ -1,9 +1,9 @@
 """Host logic with no GPU: the variant registry (``src/esmfold2_mlx/variants.py:74-86``) and the
 adaptive-recycling state machine (``src/esmfold2_mlx/var_adaptive_loops.py:79-156``).
 
-The adaptive tests replace the K5 distogram kernel with the reference's own formula on the CPU
+The adaptive tests replace the K5 distogram kernel with the reference's formula on the CPU
 (``var_adaptive_loops.py:43-46``: ``softmax(head(z + z^T)) @ centres``) and the trunk with a
-scripted module, so only the pass / convergence / extra-pass bookkeeping is under test.
+scripted module, so only the pass / settle / extra-pass bookkeeping is under test.
 """
 
 from __future__ import annotations
@@ -82,7 +82,8 @@ class _ScriptedTrunk(nn.Module):
 
 
 @torch.no_grad()
-def _reference_expected_distance(z, head):
+def _formula_expected_distance(z, head):
+    """The reference's formula on the CPU (var_adaptive_loops.py:43-46)."""
     logits = head(z.float() + z.float().transpose(-2, -3))
     return logits.softmax(-1) @ adaptive.CENTRES
 
@@ -98,34 +99,43 @@ def _model(proj=None):
 
 @pytest.fixture
 def cpu_head(monkeypatch):
-    monkeypatch.setattr(adaptive, "DistoHead", lambda head, device: head)
-    monkeypatch.setattr(adaptive, "expected_distance", _reference_expected_distance)
+    """K5 replaced by the formula on the CPU: the wrapper's evaluator calls the head module."""
+    monkeypatch.setattr(adaptive, "ExpectedDistance", lambda head, device: (lambda z: _formula_expected_distance(z, head)))
 
 
 def _p95(trunk_a, trunk_b, head):
-    ea = _reference_expected_distance(trunk_a.to(torch.float16), head)
-    eb = _reference_expected_distance(trunk_b.to(torch.float16), head)
+    ea = _formula_expected_distance(trunk_a.to(torch.float16), head)
+    eb = _formula_expected_distance(trunk_b.to(torch.float16), head)
     return float((eb - ea).abs().flatten().quantile(0.95))
+
+
+def test_bin_centres_follow_the_reference_edges():
+    """128 centres: 127 edges evenly over 2-52 A, open-ended bins 0.2 A outside (var_adaptive_loops.py:38-40)."""
+    c = adaptive.CENTRES
+    step = 50.0 / 126
+    assert c.shape == (128,)
+    assert abs(float(c[0]) - 1.8) < 1e-6 and abs(float(c[-1]) - 52.2) < 1e-5
+    assert torch.allclose(c[1:-1], 2.0 + step * (torch.arange(126) + 0.5), atol=1e-5)
 
 
 def test_converges_then_returns_the_converged_output_without_running_the_trunk(cpu_head):
     scripted = _ScriptedTrunk([1.0, -1.0, -1.0, 9.0, 9.0])
     model = _model()
     t = adaptive.CUDAAdaptiveTrunk(scripted, model)
-    t.reset(5)
+    t.start_fold(5)
     pair = torch.zeros(1, L, L, C_Z)
     outs = [t(pair) for _ in range(5)]
     # pass 2 (the sign flipped) moves the distogram (p95 well above 0.6 A), pass 3 repeats it
-    assert _p95(scripted.base, -scripted.base, model.distogram_head) > adaptive.THRESHOLD
+    assert _p95(scripted.base, -scripted.base, model.distogram_head) > adaptive.SETTLE_A
     assert t.converged and t.passes == 3 and len(scripted.inputs) == 3
-    assert [h["disto_p95"] for h in t.history][1] == 0.0
+    assert t.fold.changes[1] == 0.0
     assert outs[3] is outs[2] and outs[4] is outs[2]
 
 
 def test_min_passes_holds_back_an_early_convergence(cpu_head):
     scripted = _ScriptedTrunk([2.0, 2.0, 2.0, 2.0])
     t = adaptive.CUDAAdaptiveTrunk(scripted, _model(), min_passes=3)
-    t.reset(4)
+    t.start_fold(4)
     pair = torch.zeros(1, L, L, C_Z)
     t(pair)
     t(pair)
@@ -136,19 +146,21 @@ def test_min_passes_holds_back_an_early_convergence(cpu_head):
     assert len(scripted.inputs) == 3
 
 
-def test_reset_starts_a_new_fold(cpu_head):
+def test_start_fold_begins_a_new_fold(cpu_head):
     scripted = _ScriptedTrunk([1.0, 1.0, 1.0, -1.0])
     t = adaptive.CUDAAdaptiveTrunk(scripted, _model())
     pair = torch.zeros(1, L, L, C_Z)
-    t.reset(2)
+    t.start_fold(2)
     t(pair)
     t(pair)
     assert t.converged
-    t.reset(2)
-    assert not t.converged and t.passes == 0 and t.history == [] and t.prev is None
+    t.start_fold(2)
+    assert not t.converged and t.passes == 0 and t.fold.changes == [] and t.fold.latest is None
     t(pair)
     t(pair)
-    assert t.passes == 2 and not t.converged  # the sign flip moves the distogram
+    # the first pass of the new fold has nothing to compare with (no carry-over from the last
+    # fold), and the second (sign flip) moves the distogram
+    assert t.passes == 2 and not t.converged and len(t.fold.changes) == 1
     assert len(scripted.inputs) == 4
 
 
@@ -158,7 +170,7 @@ def test_extra_passes_after_the_scheduled_ones(cpu_head):
     proj = nn.Linear(C_Z, C_Z)
     scripted = _ScriptedTrunk([1.0, -1.0, 1.0, -1.0, -1.0, 1.0])
     t = adaptive.CUDAAdaptiveTrunk(scripted, _model(proj), max_extra=3)
-    t.reset(3)
+    t.start_fold(3)
     pair = torch.randn(1, L, L, C_Z, generator=torch.Generator().manual_seed(2))
     z_init = pair - proj(torch.zeros_like(pair))
     t(pair)
@@ -169,7 +181,7 @@ def test_extra_passes_after_the_scheduled_ones(cpu_head):
     # extra pass inputs are z_init + proj(previous output)
     assert torch.allclose(scripted.inputs[3], z_init + proj(scripted.base))
     assert torch.allclose(scripted.inputs[4], z_init + proj(-scripted.base))
-    assert t.history[-1]["disto_p95"] == 0.0
+    assert t.fold.changes[-1] == 0.0
 
 
 def test_wrapper_forwards_chunk_and_backend_setters(cpu_head):
@@ -180,17 +192,27 @@ def test_wrapper_forwards_chunk_and_backend_setters(cpu_head):
     assert scripted.chunk == 64 and scripted.backend == "cuda"
 
 
-def test_apply_resets_per_fold_with_num_loops_plus_one(cpu_head):
+def test_apply_starts_a_fold_per_forward_with_num_loops_plus_one(cpu_head):
     model = _model()
     model.folding_trunk = _ScriptedTrunk([1.0] * 8)
     model.config = types.SimpleNamespace(num_loops=3)
     seen = []
-    model.forward = lambda *a, num_loops=None, **k: seen.append(model.folding_trunk.scheduled)
+    model.forward = lambda *a, num_loops=None, **k: seen.append(model.folding_trunk.fold.scheduled)
     trunk = adaptive.apply(model)
     assert model.folding_trunk is trunk
     model.forward()
     model.forward(num_loops=5)
     assert seen == [4, 6]
+
+
+def test_wrapper_keeps_the_model_state_dict_unchanged(cpu_head):
+    proj = nn.Linear(C_Z, C_Z)
+    model = _model(proj)
+    model.folding_trunk = _ScriptedTrunk([1.0])
+    before = set(model.state_dict())
+    adaptive.apply(model)
+    after = {k for k in model.state_dict() if not k.startswith("folding_trunk.")}
+    assert after == before - {k for k in before if k.startswith("folding_trunk.")}
 
 
 # ---------------------------------------------------------------- weight copies (mlx_trunk.py:40-69)
