@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -154,23 +155,19 @@ SHARDED_WORKLOADS = ("c5",)
 
 
 def _workload(rank: int, device, name: str = "c2"):
-    """Seeded weights and one step's input for a named configuration (``synthetic.CONFIGS``);
-    ``device=None`` keeps everything on the CPU (reference arm)."""
-    from esmfold2_mlx_b200.synthetic import CONFIGS, FoldingTrunk, pair_mask, pair_tensor, trimul_biases
+    """Seeded weights and one step's input for a named configuration (``synthetic.workload``,
+    the same inputs the parity tests check); ``device=None`` keeps everything on the CPU
+    (reference arm)."""
+    from esmfold2_mlx_b200.synthetic import workload
 
-    cfg = CONFIGS[name]
-    trunk = FoldingTrunk(1, cfg.c_z, cfg.c, seed=cfg.seed)
-    biases = {d: (trimul_biases(cfg.c_z, cfg.c, cfg.seed + 31 + i) if cfg.biases else None)
-              for i, d in enumerate(("out", "in"))}
+    wl = workload(name, rank)
     w = None
     if device is not None:
         from esmfold2_mlx_b200 import ops
 
-        w = {d: ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + d), device, biases[d])
+        w = {d: ops.TrimulWeights.from_module(getattr(wl.trunk.blocks[0], "tri_mul_" + d), device, wl.biases[d])
              for d in ("out", "in")}
-    z = pair_tensor(cfg.B, cfg.L, cfg.c_z, cfg.seed + rank).half()
-    mask = pair_mask(cfg.B, cfg.L, cfg.n_pad).half() if cfg.n_pad else None
-    return cfg, trunk, biases, w, z, mask
+    return wl.cfg, wl.trunk, wl.biases, w, wl.z, wl.mask
 
 
 def _cpu_sample(trunk, biases, z, mask, min_seconds: float):
@@ -280,13 +277,12 @@ def _trunk_recycle(device, flush, reps: int = 3):
     ReLU transition 128 -> 512 -> 128), L = 384, run for 3 recycles with z fed back; random
     N(0, 1/fan_in) weights (seed 2), z0 ~ N(0, 1).  The whole 3-recycle forward is one CUDA graph
     through the public module (CUDAFoldingTrunk); L2 flushed before each timed replay."""
-    from esmfold2_mlx_b200.synthetic import CONFIGS, FoldingTrunk, pair_tensor
+    from esmfold2_mlx_b200.synthetic import recycle_workload
     from esmfold2_mlx_b200.trunk import CUDAFoldingTrunk
 
-    cfg = CONFIGS["c3"]
-    trunk = FoldingTrunk(cfg.blocks, C_Z, C, hidden=512, seed=cfg.seed, activation="relu")
+    cfg, trunk, z0 = recycle_workload("c3")
     mod = CUDAFoldingTrunk(trunk, device=device)
-    z0 = pair_tensor(1, cfg.L, C_Z, cfg.seed).to(device)
+    z0 = z0.to(device)
 
     def forward():
         z = z0
@@ -453,121 +449,285 @@ def run_sharded(args, ws, rank, local):
         ex.close()
 
 
+class TrimulCase:
+    """One configuration's out+in tri-mul step on the GPU: inputs resident in HBM, the step as a
+    CUDA graph of the two ``tmu_trimul`` calls (the timed form), and the same six kernels launched
+    through the per-kernel entry points, each with its own armed trace block (the traced form:
+    the same programmatic-dependent-launch chain, timed kernel by kernel on the device)."""
+
+    NAMES = ("K1_project_gate", "K2_contract", "K3_emit_residual")
+
+    def __init__(self, name: str, rank: int, device, stream):
+        from esmfold2_mlx_b200 import _lib, ops
+
+        self.ops, self.lib = ops, _lib.load()
+        self.cfg, self.trunk, self.biases, self.w, self.z_host, self.mask_host = _workload(rank, device, name)
+        cfg = self.cfg
+        self.device, self.stream = device, stream
+        self.z0 = self.z_host.to(device)
+        self.mask = None if self.mask_host is None else self.mask_host.to(device)
+        self.z1, self.z2 = torch.empty_like(self.z0), torch.empty_like(self.z0)
+        self.wsp = ops.Workspace()
+        self.wsp.get(cfg.B, cfg.L, cfg.c_z, cfg.c, device)
+        Lp = ops.row_pitch(cfg.L)
+        self.a = torch.empty(cfg.B * cfg.c, cfg.L, Lp, dtype=torch.float16, device=device)
+        self.b, self.x = torch.empty_like(self.a), torch.empty_like(self.a)
+        self.trace_st = torch.zeros(6, 256, dtype=torch.uint8, device=device)
+        self.cells = 2 * cfg.B * cfg.L * cfg.L  # pair-cells per step (out + in)
+        self.step()
+        self.step_traced()
+        torch.cuda.synchronize()
+        self.g_step, self.g_trace = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g_step, stream=stream):
+            self.step()
+        with torch.cuda.graph(self.g_trace, stream=stream):
+            self.step_traced()
+        torch.cuda.synchronize()
+
+    def step(self):
+        ops = self.ops
+        ops.trimul(self.z0, self.mask, self.w["out"], True, out=self.z1, workspace=self.wsp)
+        ops.trimul(self.z1, self.mask, self.w["in"], False, out=self.z2, workspace=self.wsp)
+
+    def step_traced(self):
+        ops, lib, cfg = self.ops, self.lib, self.cfg
+        sp = ops._stream_ptr(self.device)
+        zin = self.z0
+        for k, (d, outgoing, zout) in enumerate((("out", True, self.z1), ("in", False, self.z2))):
+            wt = self.w[d]
+            st = [self.trace_st[3 * k + j] for j in range(3)]
+            _check(lib.tmu_project_gate(ops._ptr(zin), ops._ptr(self.mask), ops.ctypes.byref(wt.struct), cfg.B, cfg.L,
+                                        cfg.c_z, cfg.c, ops._ptr(self.a), ops._ptr(self.b), ops._ptr(st[0]), sp), "K1")
+            _check(lib.tmu_contract(ops._ptr(self.a), ops._ptr(self.b), ops._ptr(self.x), cfg.B * cfg.c, cfg.L,
+                                    1 if outgoing else 0, ops._ptr(st[1]), sp), "K2")
+            _check(lib.tmu_emit_residual(ops._ptr(self.x), ops._ptr(zin), ops._ptr(zout), ops.ctypes.byref(wt.struct),
+                                         cfg.B, cfg.L, cfg.c_z, cfg.c, ops.MIX_EPS_FP16, ops._ptr(st[2]), sp), "K3")
+            zin = zout
+
+    def time_steps(self, flush, steps: int) -> float:
+        """Milliseconds of ``steps`` graph replays, each bracketed by events, L2 flushed between."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record()
+            self.g_step.replay()
+            e1.record()
+        torch.cuda.synchronize()
+        return sum(e0.elapsed_time(e1) for e0, e1 in evs)
+
+    def trace(self, flush, reps: int) -> dict:
+        """Replays of the traced form: per launch, the span from its first CTA past the dependency
+        wait to its last CTA's exit (%globaltimer), averaged over ``reps`` L2-flushed replays."""
+        spans = [[0.0] * 6 for _ in range(reps)]
+        gaps = [[0.0] * 6 for _ in range(reps)]
+        step_ms = []
+        for r in range(reps):
+            flush.zero_()
+            for i in range(6):
+                self.ops.trace_arm(self.trace_st[i])
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            self.g_trace.replay()
+            e1.record()
+            e1.synchronize()
+            step_ms.append(e0.elapsed_time(e1))
+            marks = [self.ops.trace_read(self.trace_st[i]) for i in range(6)]
+            for i, (t0, t1) in enumerate(marks):
+                spans[r][i] = (t1 - t0) * 1e-3
+                if i:
+                    gaps[r][i] = (t0 - marks[i - 1][1]) * 1e-3
+        mean = lambda rows, i: statistics.fmean(row[i] for row in rows)  # noqa: E731
+        return {"spans_us": [round(mean(spans, i), 3) for i in range(6)],
+                "gaps_us": [round(mean(gaps, i), 3) for i in range(6)],
+                "traced_step_ms": round(statistics.fmean(step_ms), 5)}
+
+    def kernel_table(self, tr: dict) -> tuple[str, dict]:
+        """Per kernel: its in-step time (mean span of its two launches), the share of the summed
+        spans, and the fraction of the roofline its algorithmic bytes or FLOPs reach in that time."""
+        hbm, tflops, _ = _peaks()
+        cfg = self.cfg
+        costs = _kernel_costs(cfg.L, cfg.B, self.mask is not None, cfg.c_z, cfg.c)
+        total = sum(tr["spans_us"])
+        kernels = {}
+        for j, n in enumerate(self.NAMES):
+            us = 0.5 * (tr["spans_us"][j] + tr["spans_us"][3 + j])
+            t = us * 1e-6
+            byt, fl = costs[n]["bytes"], costs[n]["flops"]
+            bound = "tensor" if fl / (tflops * 1e12) > byt / (hbm * 1e9) else "hbm"
+            ach = (fl / t / 1e12) if bound == "tensor" else (byt / t / 1e9)
+            pk = tflops if bound == "tensor" else hbm
+            kernels[n] = {"us_in_step": round(us, 3), "share": round(2 * us / total, 4), "bound": bound,
+                          "achieved": round(ach, 2), "frac": round(ach / pk, 4),
+                          "algorithmic_per_launch": costs[n]}
+        dom = max(self.NAMES, key=lambda n: kernels[n]["us_in_step"])
+        return dom, kernels
+
+    def parity(self, slab_rows: int | None = None) -> dict:
+        """The step's outputs (left by the last replay) against the CPU oracle, used as the checker:
+        e_cuda vs e_ref (exact float64 update) and the distance in fp16 ulps, per direction, each
+        on the same input (in: the CUDA out result).  Large L: rows [124, 124 + slab_rows) only."""
+        from oracle import trimul_oracle as orc
+
+        torch.cuda.synchronize()
+        cfg = self.cfg
+        z1h, z2h = self.z1.cpu(), self.z2.cpu()
+        m = None if self.mask_host is None else self.mask_host.float()
+        res = {}
+        steps = (("out", True, self.z_host, z1h), ("in", False, z1h, z2h))
+        if slab_rows is not None:
+            steps = steps[:1]  # the outgoing update; both directions are checked in the test suite
+        for d, outgoing, zin, got in steps:
+            tri = getattr(self.trunk.blocks[0], "tri_mul_" + d)
+            p16 = orc.trimul_params(tri, True, self.biases[d])
+            pex = orc.trimul_params(tri, False, self.biases[d])
+            if slab_rows is None:
+                ref16 = orc.trimul_fp16(p16, zin.float(), m, outgoing)
+                exact = orc.trimul_fp32(pex, zin.double(), m, outgoing, dtype=torch.float64)
+                res[d] = orc.parity(exact, ref16, got.float())
+            else:
+                rows = range(124, 124 + slab_rows)
+                ref16 = orc.trimul_rows(p16, zin, m, outgoing, rows)
+                exact = orc.trimul_rows(pex, zin, m, outgoing, rows, exact=True)
+                res[d] = orc.parity(exact, ref16, got[:, rows.start:rows.stop].float())
+                res[d]["rows"] = [rows.start, rows.stop]
+        res["checker"] = "oracle/trimul_oracle.py (CPU), after the timed region"
+        res["tolerance"] = "e_cuda <= 2 e_ref + 1e-3 (max-abs, rel-L2); max_ulps <= 4"
+        res["within_tolerance"] = all(v["within_tolerance"] and v["max_ulps"] <= 4
+                                      for k, v in res.items() if isinstance(v, dict))
+        return res
+
+
+def _check(code, where):
+    if code != 0:
+        from esmfold2_mlx_b200 import _lib
+
+        _lib.check(code, where)
+
+
+def _case_summary(case, flush, steps, warmup, with_parity=True, slab_rows=None) -> dict:
+    """A sub-measurement of the default line: another configuration's step (value, ms/step,
+    in-step kernel table and parity), one GPU."""
+    for _ in range(max(3, warmup)):
+        flush.zero_()
+        case.g_step.replay()
+    torch.cuda.synchronize()
+    ms = case.time_steps(flush, steps) / steps
+    tr = case.trace(flush, max(3, min(steps, 10)))
+    dom, kernels = case.kernel_table(tr)
+    out = {"workload": case.cfg.name, "L": case.cfg.L, "B": case.cfg.B, "c_z": case.cfg.c_z,
+           "value": case.cells / (ms * 1e-3), "unit": UNIT, "ms_per_step": round(ms, 5), "steps": steps,
+           "dominant_kernel": dom, "kernels": kernels, "trace": tr}
+    code, site = case.ops.read_status(case.wsp.status)
+    if code != 0:
+        raise RuntimeError(f"device status {code} at site {site:#x}")
+    if with_parity:
+        out["parity"] = case.parity(slab_rows)
+    return out
+
+
+def _host_link(device, nbytes: int, reps: int = 10) -> dict:
+    """Host-link figures for the e2e leg: pinned H2D and D2H of one step's bytes alone and both
+    directions at once, the GPU's NUMA node and this process's CPU affinity."""
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    hd = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    d2 = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    s1, s2 = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    timed(lambda: d.copy_(h, non_blocking=True))
+
+    def both():
+        cur = torch.cuda.current_stream(device)
+        s1.wait_stream(cur)
+        s2.wait_stream(cur)
+        with torch.cuda.stream(s1):
+            d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(s2):
+            hd.copy_(d2, non_blocking=True)
+        cur.wait_stream(s1)
+        cur.wait_stream(s2)
+
+    t_h2d = timed(lambda: d.copy_(h, non_blocking=True))
+    t_d2h = timed(lambda: hd.copy_(d2, non_blocking=True))
+    t_both = timed(both)
+    numa = None
+    try:
+        pr = torch.cuda.get_device_properties(device)
+        path = f"/sys/bus/pci/devices/{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0/numa_node"
+        with open(path) as f:
+            numa = int(f.read().strip())
+    except (OSError, ValueError, AttributeError):
+        numa = None
+    aff = sorted(os.sched_getaffinity(0))
+    return {"bytes": nbytes, "h2d_gbs": round(nbytes / (t_h2d * 1e-3) / 1e9, 2),
+            "d2h_gbs": round(nbytes / (t_d2h * 1e-3) / 1e9, 2),
+            "both_directions_gbs_each": round(nbytes / (t_both * 1e-3) / 1e9, 2),
+            "gpu_numa_node": numa, "cpu_affinity": f"{aff[0]}-{aff[-1]} ({len(aff)} cpus)" if aff else None}
+
+
 def run_b200(args, ws, rank, local):
     from esmfold2_mlx_b200 import _lib, ops
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
-    cfg, trunk, biases, w, z_host, mask_host = _workload(rank, device, args.workload)
-    L, B = cfg.L, cfg.B
-    C_Z, C = cfg.c_z, cfg.c  # noqa: N806 - the pair and latent widths of this workload
-    cells_per_step = 2 * B * L * L
     stream = torch.cuda.Stream(device)
     torch.cuda.set_stream(stream)
-
-    z0 = z_host.to(device)
-    mask = None if mask_host is None else mask_host.to(device)
-    z1 = torch.empty_like(z0)
-    z2 = torch.empty_like(z0)
-    wsp = ops.Workspace()
-    wsp.get(B, L, C_Z, C, device)
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
-
-    def step():
-        ops.trimul(z0, mask, w["out"], True, out=z1, workspace=wsp)
-        ops.trimul(z1, mask, w["in"], False, out=z2, workspace=wsp)
-
-    # per-kernel instrumented step: the same work through the per-kernel entry points
-    Lp = ops.row_pitch(L)
-    a = torch.empty(B * C, L, Lp, dtype=torch.float16, device=device)
-    b = torch.empty_like(a)
-    x = torch.empty_like(a)
-    status = ops.new_status(device)
-    lib = _lib.load()
-    sp = ops._stream_ptr(device)
-    kev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(7)]
-
-    def step_kernels():
-        zin = z0
-        for k, (d, outgoing, zout) in enumerate((("out", True, z1), ("in", False, z2))):
-            wt = w[d]
-            kev[3 * k].record()
-            _lib.check(lib.tmu_project_gate(ops._ptr(zin), ops._ptr(mask), ops.ctypes.byref(wt.struct), B, L, C_Z, C,
-                                            ops._ptr(a), ops._ptr(b), ops._ptr(status), sp), "K1")
-            kev[3 * k + 1].record()
-            _lib.check(lib.tmu_contract(ops._ptr(a), ops._ptr(b), ops._ptr(x), B * C, L, 1 if outgoing else 0,
-                                        ops._ptr(status), sp), "K2")
-            kev[3 * k + 2].record()
-            _lib.check(lib.tmu_emit_residual(ops._ptr(x), ops._ptr(zin), ops._ptr(zout), ops.ctypes.byref(wt.struct),
-                                             B, L, C_Z, C, ops.MIX_EPS_FP16, ops._ptr(status), sp), "K3")
-            zin = zout
-        kev[6].record()
-
-    # eager warm-up (first-call host setup), then capture both steps as CUDA graphs
-    step()
-    step_kernels()
-    torch.cuda.synchronize()
-    g_step, g_kern = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_step, stream=stream):
-        step()
-    with torch.cuda.graph(g_kern, stream=stream):
-        step_kernels()
-    torch.cuda.synchronize()
+    case = TrimulCase(args.workload, rank, device, stream)
+    cfg, w = case.cfg, case.w
+    L, B = cfg.L, cfg.B
+    C_Z, C = cfg.c_z, cfg.c  # noqa: N806 - the pair and latent widths of this workload
+    mask, z_host, mask_host = case.mask, case.z_host, case.mask_host
+    trunk, biases = case.trunk, case.biases
+    cells_per_step = case.cells
 
     for _ in range(max(3, args.warmup)):
         flush.zero_()
-        g_step.replay()
+        case.g_step.replay()
     torch.cuda.synchronize()
     _barrier(ws)
 
     # ---------------- timed region: K steps ----------------
     sampler = ClockSampler(local)
     sampler.start()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     torch.cuda.synchronize()
     _barrier(ws)
-    for e0, e1 in evs:
-        flush.zero_()
-        e0.record()
-        g_step.replay()
-        e1.record()
-    torch.cuda.synchronize()
+    step_ms = case.time_steps(flush, args.steps)
     _barrier(ws)
-    step_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
     clocks = sampler.stop()
     step_ms_max = _max_over_ranks(step_ms, ws, device)
     ms_per_step = step_ms_max / args.steps
     value = ws * cells_per_step / (ms_per_step * 1e-3)
-    code, site = ops.read_status(wsp.status)
+    code, site = ops.read_status(case.wsp.status)
     if code != 0:
         raise RuntimeError(f"device status {code} at site {site:#x}")
+    z2_timed = case.z2.clone()
 
-    # ---------------- per-kernel times (instrumented graph) ----------------
-    names = ["K1_project_gate", "K2_contract", "K3_emit_residual"]
-    ktime = {n: 0.0 for n in names}
-    for _ in range(args.steps):
-        flush.zero_()
-        g_kern.replay()
-        torch.cuda.synchronize()
-        for k in range(2):
-            for j, n in enumerate(names):
-                ktime[n] += kev[3 * k + j].elapsed_time(kev[3 * k + j + 1])
-    n_launch = 2 * args.steps
-    kavg = {n: ktime[n] / n_launch for n in names}  # ms per launch
-    share = {n: ktime[n] / sum(ktime.values()) for n in names}
-    dom = max(names, key=lambda n: ktime[n])
+    # ---------------- sustained run (clocks under load for >= 0.5 s) ----------------
+    n_sus = max(args.steps, int(math.ceil(args.sustain_seconds * 1e3 / max(ms_per_step + 0.05, 1e-3))))
+    sampler2 = ClockSampler(local)
+    sampler2.start()
+    time.sleep(0.25)
+    sus_ms = case.time_steps(flush, n_sus)
+    clocks_sus = sampler2.stop()
+    sustained = {"steps": n_sus, "ms_per_step": round(sus_ms / n_sus, 5), "device_seconds": round(sus_ms * 1e-3, 3),
+                 "value": cells_per_step / (sus_ms / n_sus * 1e-3), "clocks": clocks_sus}
+
+    # ---------------- per-kernel in-step times (traced form of the same chain) ----------------
+    tr = case.trace(flush, max(3, min(args.steps, 20)))
+    dom, kernels = case.kernel_table(tr)
     hbm, tflops, peak_kind = _peaks()
-    costs = _kernel_costs(L, B, mask is not None, C_Z, C)
-    kernels = {}
-    for n in names:
-        t = kavg[n] * 1e-3
-        byt, fl = costs[n]["bytes"], costs[n]["flops"]
-        bound = "tensor" if fl / (tflops * 1e12) > byt / (hbm * 1e9) else "hbm"
-        ach = (fl / t / 1e12) if bound == "tensor" else (byt / t / 1e9)
-        pk = tflops if bound == "tensor" else hbm
-        kernels[n] = {"us_per_launch": round(kavg[n] * 1e3, 3), "share": round(share[n], 4), "bound": bound,
-                      "achieved": round(ach, 2), "frac": round(ach / pk, 4)}
     traffic = None  # DRAM bytes per launch of the dominant kernel, from a committed ncu capture
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -577,7 +737,12 @@ def run_b200(args, ws, rank, local):
                 "peak": tflops if d["bound"] == "tensor" else hbm,
                 "unit": "TFLOP/s" if d["bound"] == "tensor" else "GB/s", "frac": d["frac"], "traffic": traffic,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)" if peak_kind == "measured" else "fallback",
-                "algorithmic_per_launch": costs[dom], "kernels": kernels}
+                "algorithmic_per_launch": d["algorithmic_per_launch"],
+                "timing": "in-step: per launch, first CTA past its dependency wait to last CTA exit (%globaltimer), "
+                          "in the same PDL-chained launch sequence as the timed step; mean over L2-flushed replays",
+                "kernels": kernels, "trace": tr,
+                "step_vs_trace": {"timed_ms_per_step": round(ms_per_step, 5),
+                                  "sum_of_spans_ms": round(sum(tr["spans_us"]) * 1e-3, 5)}}
 
     # ---------------- end to end through the public API, host buffers ----------------
     # Every step copies its own input from pinned host memory and reads its result back.  Serial:
@@ -588,11 +753,11 @@ def run_b200(args, ws, rank, local):
     zh = z_host.pin_memory()
     mh = None if mask_host is None else mask_host.pin_memory()
     outh = [torch.empty_like(z_host).pin_memory() for _ in range(2)]
-    z_in = [torch.empty_like(z0) for _ in range(2)]
+    z_in = [torch.empty_like(case.z0) for _ in range(2)]
     m_in = [None if mask is None else torch.empty_like(mask) for _ in range(2)]
-    z_mid = [torch.empty_like(z0) for _ in range(2)]
-    z_out = [torch.empty_like(z0) for _ in range(2)]
-    wsp2 = [wsp, ops.Workspace()]
+    z_mid = [torch.empty_like(case.z0) for _ in range(2)]
+    z_out = [torch.empty_like(case.z0) for _ in range(2)]
+    wsp2 = [case.wsp, ops.Workspace()]
     wsp2[1].get(B, L, C_Z, C, device)
 
     def e2e_step(i, s_in, s_out):
@@ -653,15 +818,30 @@ def run_b200(args, ws, rank, local):
     e2e_ms = _max_over_ranks(p0.elapsed_time(p1), ws, device) / n_pipe
     h2d = zh.numel() * zh.element_size() + (0 if mh is None else mh.numel() * mh.element_size())
     d2h = outh[0].numel() * outh[0].element_size()
+    e2e_matches = bool(torch.equal(outh[(n_pipe - 1) % 2].to(device), z2_timed))
+    link = _host_link(device, h2d)
     e2e = {"value": ws * cells_per_step / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
            "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
            "mode": "pipelined: step k+1's H2D and step k-1's D2H overlap step k (3 streams, events)",
-           "serial": {"value": ws * cells_per_step / (e2e_serial * 1e-3), "ms_per_step": round(e2e_serial, 4)}}
+           "serial": {"value": ws * cells_per_step / (e2e_serial * 1e-3), "ms_per_step": round(e2e_serial, 4)},
+           "host_link": link, "output_equals_timed_step": e2e_matches,
+           "host_link_bound_ms": round(max(h2d / (link["both_directions_gbs_each"] * 1e9),
+                                           d2h / (link["both_directions_gbs_each"] * 1e9)) * 1e3, 4)}
 
-    # ---------------- trunk recycle, N = 1 only ----------------
+    # ---------------- parity of the timed step (oracle as the checker, after timing) ----------------
+    case.z2.copy_(z2_timed)
+    parity = case.parity() if not args.no_parity else None
+
+    # ---------------- other configurations, N = 1 only ----------------
     recycle = None
+    extra = {}
     if ws == 1 and not args.no_trunk:
         recycle = _trunk_recycle(device, flush)
+    if ws == 1 and not args.no_extra and args.workload == "c2":
+        for name, slab in (("L2048", 8), ("c2w", None)):
+            sub = TrimulCase(name, 0, device, stream)
+            extra[name] = _case_summary(sub, flush, min(args.steps, 20), args.warmup, not args.no_parity, slab)
+            del sub
 
     # ---------------- CPU baseline (rank 0, N = 1) ----------------
     cpu = None
@@ -680,10 +860,9 @@ def run_b200(args, ws, rank, local):
             "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
             "config": _config_dict(cfg, ws),
             "e2e": e2e, "gpu_launches": 6 * args.steps, "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
-            "trunk_recycle": recycle,
+            "sustained": sustained, "parity": parity, "trunk_recycle": recycle, **extra,
         }
         print(json.dumps(line), flush=True)
-    del g_step, g_kern
 
 
 def run_pair_cond(args, ws, rank, local):
@@ -803,6 +982,81 @@ def run_pair_cond(args, ws, rank, local):
     del g
 
 
+def run_stage(args):
+    """``--stage``: one kernel (or one whole update) at a chosen size, for profilers.  Every stage
+    runs once untimed, then ``--reps`` more times; the device status word is checked and the mean
+    CUDA-event time per launch is printed.  Select kernels in ncu with ``-k regex:`` and
+    ``project_gate``, ``contract``, ``emit_residual``, ``transition`` (k4), ``disto`` (k5), ``ln_rows``
+    / ``gemm_kernel`` (pc: the diffusion pair conditioning; parcae: the 6B loop's parcae step)."""
+    from torch import nn
+
+    from esmfold2_mlx_b200 import _lib, ops
+    from esmfold2_mlx_b200.synthetic import FoldingTrunk, pair_mask, pair_tensor
+
+    dev = torch.device("cuda", 0)
+    _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
+    L, B, cz = args.L, args.B, args.cz
+    trunk = FoldingTrunk(1, cz, cz, hidden=args.hidden, seed=0, activation=args.activation)
+    w = ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + args.direction), dev)
+    z = pair_tensor(B, L, cz, 0).half().to(dev)
+    mask = pair_mask(B, L, args.mask_pad).half().to(dev) if args.mask_pad else None
+    outgoing = args.direction == "out"
+    status = ops.new_status(dev)
+    a, b = ops.project_gate(z, mask, w, status)
+    x = ops.contract(a, b, L, outgoing, status)
+    out = ops.emit_residual(x, z, w, out=torch.empty_like(z), status=status)
+    torch.cuda.synchronize()
+    stages = {
+        "k1": lambda: ops.project_gate(z, mask, w, status),
+        "k2": lambda: ops.contract(a, b, L, outgoing, status),
+        "k3": lambda: ops.emit_residual(x, z, w, out=out, status=status),
+        "all": lambda: ops.trimul(z, mask, w, outgoing, out=out),
+    }
+    if args.stage == "k5":
+        from esmfold2_mlx_b200.adaptive import ExpectedDistance
+
+        ev = ExpectedDistance(nn.Linear(cz, 128), dev)
+        stages["k5"] = lambda: ev(z)
+    if args.stage == "k4":
+        tw = ops.TransitionWeights.from_module(trunk.blocks[0].pair_transition, dev)
+        stages["k4"] = lambda: ops.transition(z, tw, out=out, status=status)
+    if args.stage == "pc":
+        from esmfold2_mlx_b200 import pair_cond
+        from esmfold2_mlx_b200.synthetic import DiffusionHead
+
+        pw = pair_cond.PairCondWeights.from_head(DiffusionHead(), dev)
+        zt = pair_tensor(B, L, 256, 1).to(dev) * 20.0
+        rp = pair_tensor(B, L, 256, 2).to(dev)
+        ws = torch.empty(pair_cond.workspace_bytes(B, L, pw.c_in, pw.c_pair, 2), dtype=torch.uint8, device=dev)
+        pout = torch.empty(pw.n_bias // pw.heads, B, pw.heads, L, L, dtype=torch.float16, device=dev)
+        stages["pc"] = lambda: pair_cond.pair_biases(pw, zt, rp, out=pout, workspace=ws, status=status)
+    if args.stage == "parcae":
+        from esmfold2_mlx_b200 import parcae
+
+        m = nn.Module()
+        m.parcae_input_norm = nn.LayerNorm(cz)
+        pwt = parcae.ParcaeWeights.from_model(m, torch.full((cz,), 0.5), torch.randn(cz, cz) / 16, dev)
+        zf = pair_tensor(B, L, cz, 3).to(dev)
+        zi, rf = pair_tensor(B, L, cz, 4).to(dev), pair_tensor(B, L, cz, 5).to(dev)
+        pws = torch.empty(_lib.load().tmu_parcae_workspace_bytes(B, L, cz), dtype=torch.uint8, device=dev)
+        pout = torch.empty_like(zf)
+        stages["parcae"] = lambda: parcae.parcae_step(zf, zi, rf, pwt, out=pout, workspace=pws, status=status)
+    fn = stages[args.stage]
+    fn()  # the stage's own output allocations happen here, outside the timed launches
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    code, site = ops.read_status(status)
+    if code != 0:
+        raise SystemExit(f"device status {code} at site {site:#x}")
+    ms = e0.elapsed_time(e1) / max(1, args.reps)
+    print(f"L={L} B={B} c_z={cz} {args.direction} stage={args.stage}: {ms * 1e3:.1f} us per launch")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -812,13 +1066,30 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-trunk", action="store_true", help="skip the trunk-recycle (config 3) measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--sustain-seconds", type=float, default=0.6,
+                    help="device seconds of the sustained replay that records clocks under load")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed step's output")
+    ap.add_argument("--no-extra", action="store_true", help="skip the L2048 and c2w sub-measurements")
     ap.add_argument("--c5-nccl", action="store_true",
                     help="c5: move b with an NCCL all-gather instead of copy-engine peer copies")
     ap.add_argument("--workload", choices=WORKLOADS, default="c2",
                     help="c2 (default: the metric's configuration), c1, c4 (64 folds x L=146), L2048, "
                          "c5 (one L=3072 fold row-sharded over the N ranks), c2w / L2048w (c_z = c = 256), "
                          "pc / pc476 (diffusion pair conditioning of one fold, L = 238 / 476)")
+    prof = ap.add_argument_group("profiling (--stage): one kernel at a chosen size, for ncu")
+    prof.add_argument("--stage", choices=["all", "k1", "k2", "k3", "k4", "k5", "pc", "parcae"], default=None)
+    prof.add_argument("--L", type=int, default=1024)
+    prof.add_argument("--B", type=int, default=1)
+    prof.add_argument("--direction", choices=["out", "in"], default="out")
+    prof.add_argument("--reps", type=int, default=3)
+    prof.add_argument("--mask-pad", type=int, default=0)
+    prof.add_argument("--cz", type=int, choices=[128, 256], default=128, help="c_z = c")
+    prof.add_argument("--hidden", type=int, default=512, help="transition hidden width (k4)")
+    prof.add_argument("--activation", choices=["swiglu", "relu"], default="swiglu", help="transition activation (k4)")
     args = ap.parse_args()
+    if args.stage is not None:
+        run_stage(args)
+        return
     ws, rank, local = _dist()
     if args.impl == "reference":
         run_reference(args, ws, rank, local)

@@ -97,6 +97,8 @@ SIGNATURES = {
     "tmu_reset_status": (_i, [_vp, _vp]),
     "tmu_read_status": (_i, [_vp, _vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     "tmu_read_first_error": (_i, [_vp, _vp, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    "tmu_trace_arm": (_i, [_vp, _vp]),
+    "tmu_trace_read": (_i, [_vp, _vp, ctypes.POINTER(_ull), ctypes.POINTER(_ull)]),
     "tmu_project_gate": (_i, [_vp, _vp, _W, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "tmu_contract": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _vp]),
     "tmu_emit_residual": (_i, [_vp, _vp, _vp, _W, _i, _i, _i, _i, _f, _vp, _vp]),

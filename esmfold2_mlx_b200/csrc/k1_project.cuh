@@ -96,6 +96,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 
 template <bool HAS_BIAS, bool HAS_MASK>
 __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_constant__ Params p) {
+  const bool trace_on = trace_enabled(p.status);
   constexpr uint32_t IDESC = idesc_f16_f32(128, 128, false, false);
   // All shared state lives in the dynamic buffer (no static __shared__), whose base the 128B
   // swizzle needs 1024-byte aligned; a misaligned base is reported, never computed on.
@@ -168,6 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
   }
   griddep_trigger();
   griddep_wait();
+  trace_mark_start(p.status, trace_on);
   // Block 0 clears this call's error fields once the previous kernel (which may share the word)
   // has finished.  Another CTA of this grid that gave up on a wait before block 0 got here
   // would have its per-call record cleared; its since-reset record (first_code) survives.
@@ -405,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_kernel(const __grid_
 
   tc_fence_before();
   __syncthreads();
+  trace_mark_end(p.status, trace_on);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);

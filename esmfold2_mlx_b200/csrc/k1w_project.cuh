@@ -85,6 +85,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 
 template <bool HAS_BIAS, bool HAS_MASK>
 __global__ void __launch_bounds__(kThreads, 1) project_gate_w_kernel(const __grid_constant__ Params p) {
+  const bool trace_on = trace_enabled(p.status);
   constexpr uint32_t IDESC = idesc_f16_f32(128, 64, false, false);
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
@@ -156,6 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_w_kernel(const __gri
   }
   griddep_trigger();
   griddep_wait();
+  trace_mark_start(p.status, trace_on);
   // Block 0 clears (as in K1) this call's error fields once the previous kernel (which may share the word)
   // has finished.  Another CTA of this grid that gave up on a wait before block 0 got here
   // would have its per-call record cleared; its since-reset record (first_code) survives.
@@ -349,6 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_w_kernel(const __gri
 
   tc_fence_before();
   __syncthreads();
+  trace_mark_end(p.status, trace_on);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);

@@ -51,6 +51,7 @@ enum Site : unsigned int { kSiteProducer = 0x201, kSiteMmaTmem = 0x202, kSiteMma
 
 template <int BN, bool MN_MAJOR>
 __global__ void __launch_bounds__(kThreads, 1) contract_kernel(const __grid_constant__ Params p) {
+  const bool trace_on = trace_enabled(p.status);
   using C = Cfg<BN>;
   constexpr uint32_t IDESC = idesc_f16_f32(BM, BN, MN_MAJOR, MN_MAJOR);
 
@@ -97,6 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1) contract_kernel(const __grid_cons
   const int tiles_per_d = p.tiles_m * p.tiles_n;
   griddep_trigger();
   griddep_wait();  // a, b come from the previous kernel; x may still be read by it
+  trace_mark_start(p.status, trace_on);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -219,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1) contract_kernel(const __grid_cons
 
   tc_fence_before();
   __syncthreads();
+  trace_mark_end(p.status, trace_on);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);

@@ -90,6 +90,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 
 template <bool HAS_BIAS, int XMODE>
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid_constant__ Params p) {
+  const bool trace_on = trace_enabled(p.status);
   constexpr uint32_t IDESC = idesc_f16_f32(128, CZ, false, false);
   // All shared state lives in the dynamic buffer (no static __shared__), whose base the 128B
   // swizzle needs 1024-byte aligned; a misaligned base is reported, never computed on.
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
   }
   griddep_trigger();
   griddep_wait();  // x, z come from previous kernels; z_out may alias what they read
+  trace_mark_start(p.status, trace_on);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -499,6 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
 
   tc_fence_before();
   __syncthreads();
+  trace_mark_end(p.status, trace_on);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);

@@ -87,6 +87,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 
 template <bool HAS_BIAS, bool XSW>
 __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __grid_constant__ Params p) {
+  const bool trace_on = trace_enabled(p.status);
   constexpr uint32_t IDESC = idesc_f16_f32(128, TILE, false, false);
   extern __shared__ uint8_t smem[];
   if (smem_u32(smem) & 1023) {
@@ -157,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
   }
   griddep_trigger();
   griddep_wait();
+  trace_mark_start(p.status, trace_on);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -440,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_w_kernel(const __gr
 
   tc_fence_before();
   __syncthreads();
+  trace_mark_end(p.status, trace_on);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);

@@ -112,6 +112,7 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
 
 template <int CZ, bool SWIGLU, int MODE = kModeTile>
 __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_constant__ Params p) {
+  const bool trace_on = trace_enabled(p.status);
   using C = Cfg<CZ, MODE>;
   constexpr uint32_t IDESC1 = idesc_f16_f32(128, 2 * CHUNK, false, false);
   constexpr uint32_t IDESC2 = idesc_f16_f32(128, 128, false, false);
@@ -197,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
   const uint32_t tmem_base = tmem_base_sh;
   griddep_trigger();
   griddep_wait();
+  trace_mark_start(p.status, trace_on);
 
   if (warp == 0) {
     // ---------------- weight ring producer, in the MMA's order: G1(j), then G2(j-2) ----------------
@@ -562,6 +564,7 @@ __global__ void __launch_bounds__(kThreads, 1) transition_kernel(const __grid_co
 
   tc_fence_before();
   __syncthreads();
+  trace_mark_end(p.status, trace_on);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);

@@ -6,6 +6,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <initializer_list>
@@ -981,6 +982,28 @@ int tmu_read_status(const void* status, void* stream, int* code, int* site) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
   if (code) *code = static_cast<int>(h.code);
   if (site) *site = static_cast<int>(h.site);
+  return TMU_OK;
+}
+
+int tmu_trace_arm(void* status, void* stream) {
+  if (status == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "status is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* b = static_cast<uint8_t*>(status);
+  cudaError_t e = cudaMemsetAsync(b, 0, sizeof(DeviceStatus), s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b + offsetof(DeviceStatus, trace_flag), 1, 1, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b + offsetof(DeviceStatus, t_start), 0xff, sizeof(unsigned long long), s);
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "cudaMemsetAsync(trace)");
+}
+
+int tmu_trace_read(const void* status, void* stream, unsigned long long* t_start, unsigned long long* t_end) {
+  if (status == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "status is NULL");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  DeviceStatus h;
+  e = cudaMemcpy(&h, status, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  if (t_start) *t_start = h.t_start;
+  if (t_end) *t_end = h.t_end;
   return TMU_OK;
 }
 

@@ -33,6 +33,10 @@ struct DeviceStatus {
   unsigned int pad;
   unsigned int first_code;  // first error since tmu_reset_status
   unsigned int first_site;
+  unsigned int trace_flag;  // set by the host to record this launch's span (below)
+  unsigned int pad2;
+  unsigned long long t_start;  // min over CTAs of the %globaltimer value after the dependency wait
+  unsigned long long t_end;    // max over CTAs of the %globaltimer value at exit
 };
 
 // Record an error: the first one wins in both the per-call and the since-reset fields.
@@ -67,6 +71,24 @@ __device__ __forceinline__ void raise_abort(const WaitCtx& ctx, unsigned int sit
   *ctx.abort = 1;
   record_status(ctx.status, kStatusDeviceTimeout, site);
   __threadfence();
+}
+
+// Launch-span trace, a measurement aid.  When the host sets trace_flag in a status block, every
+// CTA of a kernel given that block records when it passes its dependency wait (min over CTAs)
+// and when it finishes (max), so a chain of kernels launched with programmatic dependent launch
+// can be timed kernel by kernel inside the chain (an event between two launches would break the
+// chain).  One thread per CTA, the last one, takes the marks: it belongs to a warp that has no
+// work at the start, so the flag's load never delays a producer.
+__device__ __forceinline__ bool trace_enabled(const DeviceStatus* s) {
+  return threadIdx.x == blockDim.x - 1 && *reinterpret_cast<const volatile unsigned int*>(&s->trace_flag) != 0u;
+}
+
+__device__ __forceinline__ void trace_mark_start(DeviceStatus* s, bool on) {
+  if (on) atomicMin(&s->t_start, static_cast<unsigned long long>(globaltimer_ns()));
+}
+
+__device__ __forceinline__ void trace_mark_end(DeviceStatus* s, bool on) {
+  if (on) atomicMax(&s->t_end, static_cast<unsigned long long>(globaltimer_ns()));
 }
 
 // ------------------------------------------------------------------------------------------

@@ -157,6 +157,20 @@ def read_first_error(status: torch.Tensor) -> tuple[int, int]:
     return code.value, site.value
 
 
+def trace_arm(status: torch.Tensor) -> None:
+    """Zero a status block and switch on its launch-span trace (``tmu_trace_arm``)."""
+    _lib.check(_lib.load().tmu_trace_arm(_ptr(status), _stream_ptr(status.device)), "tmu_trace_arm")
+
+
+def trace_read(status: torch.Tensor) -> tuple[int, int]:
+    """(t_start, t_end) in %globaltimer ns of the kernel launched with this armed block."""
+    lib = _lib.load()
+    t0, t1 = ctypes.c_ulonglong(0), ctypes.c_ulonglong(0)
+    _lib.check(lib.tmu_trace_read(_ptr(status), _stream_ptr(status.device), ctypes.byref(t0), ctypes.byref(t1)),
+               "tmu_trace_read")
+    return t0.value, t1.value
+
+
 def raise_for_status(code: int, site: int, where: str) -> None:
     """Raise :class:`TmuError` for a non-zero device status (a bounded wait that gave up, or a
     kernel that found its shared memory misaligned), naming the kernel site that recorded it."""

@@ -218,3 +218,36 @@ CONFIGS = {
                   directions=("out", "in")),
     "L2048w": Config("L2048w_cz256_out_in", L=2048, c_z=256, c=256, seed=4, directions=("out", "in")),
 }
+
+
+@dataclass(frozen=True)
+class Workload:
+    """One configuration's seeded inputs, all on the CPU: the trunk-shaped module tree holding
+    its tri-mul weights, the optional per-direction biases, the step's input ``z`` (fp16) and
+    the pair mask (fp16, or None for an all-ones mask)."""
+
+    cfg: Config
+    trunk: FoldingTrunk
+    biases: dict
+    z: torch.Tensor
+    mask: torch.Tensor | None
+
+
+def workload(name: str, rank: int = 0) -> Workload:
+    """The inputs the benchmark times for configuration ``name`` (rank ``rank`` of a multi-GPU
+    run draws its own fold, seed + rank); the parity tests use exactly these."""
+    cfg = CONFIGS[name]
+    trunk = FoldingTrunk(1, cfg.c_z, cfg.c, seed=cfg.seed)
+    biases = {d: (trimul_biases(cfg.c_z, cfg.c, cfg.seed + 31 + i) if cfg.biases else None)
+              for i, d in enumerate(("out", "in"))}
+    z = pair_tensor(cfg.B, cfg.L, cfg.c_z, cfg.seed + rank).half()
+    mask = pair_mask(cfg.B, cfg.L, cfg.n_pad).half() if cfg.n_pad else None
+    return Workload(cfg, trunk, biases, z, mask)
+
+
+def recycle_workload(name: str = "c3"):
+    """The trunk-recycle configuration's inputs (CPU): the stack (``cfg.blocks`` blocks with the
+    configuration's transition, hidden 4 c_z) and its z0 ~ N(0, 1) fp32."""
+    cfg = CONFIGS[name]
+    trunk = FoldingTrunk(cfg.blocks, cfg.c_z, cfg.c, hidden=4 * cfg.c_z, seed=cfg.seed, activation=cfg.transition)
+    return cfg, trunk, pair_tensor(1, cfg.L, cfg.c_z, cfg.seed)

@@ -108,6 +108,18 @@ int tmu_read_status(const void* status, void* stream, int* code, int* site);
  * word (a 24-block trunk pass) zeroes it once, runs the calls and reads it once. */
 int tmu_read_first_error(const void* status, void* stream, int* code, int* site);
 
+/* Launch-span trace, a measurement aid (no counterpart in the reference).  tmu_trace_arm zeroes a
+ * status block and switches its trace on (async on `stream`); every kernel launched with that
+ * block as its status word then records, in %globaltimer nanoseconds, the earliest time one of its
+ * CTAs passed its dependency wait and the latest time one finished.  Giving each launch of a
+ * chain its own armed block times the kernels inside a programmatic-dependent-launch chain,
+ * which events between the launches would break.  tmu_trace_read synchronises `stream` and
+ * returns the two times (t_start = UINT64_MAX if no kernel ran with the block).  Traced: the
+ * tri-mul kernels (tmu_project_gate, tmu_contract, tmu_emit_residual and their _ex forms) and
+ * tmu_transition. */
+int tmu_trace_arm(void* status, void* stream);
+int tmu_trace_read(const void* status, void* stream, unsigned long long* t_start, unsigned long long* t_end);
+
 /* K1: n = LN(z); a, b = gated projections of n, channel-major.  outputs a, b: [B*c, L, Lpad]. */
 int tmu_project_gate(const void* z, const void* mask, const tmu_trimul_weights* w, int B, int L, int c_z,
                      int c, void* a, void* b, void* status, void* stream);

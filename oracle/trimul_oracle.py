@@ -277,18 +277,19 @@ def _gated_half(p: dict, z: torch.Tensor, mask, half: int, exact: bool) -> torch
 
 
 def trimul_rows(p: dict, z: torch.Tensor, mask, outgoing: bool, rows, exact: bool = False,
-                mix_eps: float | None = None, chunk: int = 64) -> torch.Tensor:
-    """Rows ``rows`` (a range of i) of ``z + trimul(z)`` without forming the whole update.
+                mix_eps: float | None = None, chunk: int = 64):
+    """Rows of ``z + trimul(z)`` without forming the whole update: ``rows`` is a range of i, or a
+    list of ranges (slabs) that share one projection of b.
 
     Outgoing, row i needs a[:, i, :] (the projection of z's row i) and all of b; incoming,
     ``x[d, i, j] = sum_k a[d, k, i] b[d, k, j]`` needs a[:, :, i] (the projection of z's column
     i) and all of b.  b is projected in chunks of ``chunk`` rows and kept in fp16 (exact: its
     values are fp16 roundings) or, with ``exact``, in fp32 (float64 arithmetic otherwise; the
     fp32 storage of b is 2^13 times finer than the fp16 errors this reference measures).
-    With ``exact``, ``p`` comes from ``trimul_params(..., fp16=False)``.  Returns
-    [B, len(rows), L, c_z] in fp32 (fp16 values unless ``exact``) or float64 (``exact``)."""
-    rows = range(rows.start, rows.stop) if isinstance(rows, range) else rows
-    r0, r1 = rows[0], rows[-1] + 1
+    ``z`` may be fp16 or fp32.  With ``exact``, ``p`` comes from ``trimul_params(..., fp16=False)``.
+    Returns [B, len(rows), L, c_z] per slab, fp32 holding fp16 values, or float64 (``exact``)."""
+    single = isinstance(rows, range)
+    slabs = [rows] if single else list(rows)
     B, L = z.shape[0], z.shape[1]
     c = p["c"]
     store = torch.float32 if exact else torch.float16
@@ -296,32 +297,37 @@ def trimul_rows(p: dict, z: torch.Tensor, mask, outgoing: bool, rows, exact: boo
     for s in range(0, L, chunk):
         e = min(L, s + chunk)
         b_all[:, :, s:e] = _gated_half(p, z[:, s:e], None if mask is None else mask[:, s:e], 1, exact).to(store)
-    if outgoing:
-        a_r = _gated_half(p, z[:, r0:r1], None if mask is None else mask[:, r0:r1], 0, exact)  # [B, c, R, L]
-    else:
-        a_r = _gated_half(p, z[:, :, r0:r1], None if mask is None else mask[:, :, r0:r1], 0, exact)  # [B, c, L, R]
-        a_r = a_r.transpose(2, 3)  # [B, c, R, L]: a[d, k, i] as rows i
     dt = torch.float64 if exact else torch.float32
-    x = torch.empty(B, c, r1 - r0, L, dtype=dt)
-    for d0 in range(0, c, 16):
-        d1 = min(c, d0 + 16)
-        bb = b_all[:, d0:d1].to(dt).reshape(B * (d1 - d0), L, L)
-        ar = a_r[:, d0:d1].to(dt).reshape(B * (d1 - d0), r1 - r0, L)
-        xr = torch.bmm(ar, bb.transpose(1, 2)) if outgoing else torch.bmm(ar, bb)
-        x[:, d0:d1] = xr.reshape(B, d1 - d0, r1 - r0, L)
-    zr = z[:, r0:r1]
-    if exact:
-        n = _ln(zr, p["ln_in_w"], p["ln_in_b"], EPS, dt)
-        mixn = _ln(x.permute(0, 2, 3, 1), p["ln_mix_w"], p["ln_mix_b"], EPS if mix_eps is None else mix_eps, dt)
-        mixed = mixn @ p["w_emit"].to(dt)
-        if p.get("b_emit") is not None:
-            mixed = mixed + p["b_emit"].to(dt)
-        g = n @ p["w_out_gate"].to(dt)
-        if p.get("b_gate") is not None:
-            g = g + p["b_gate"].to(dt)
-        return zr.to(dt) + mixed * torch.sigmoid(g)
-    out, _ = emit_residual_fp16(p, zr, r16(x), MIX_EPS_FP16 if mix_eps is None else mix_eps)
-    return out
+    outs = []
+    for sl in slabs:
+        r0, r1 = sl[0], sl[-1] + 1
+        if outgoing:
+            a_r = _gated_half(p, z[:, r0:r1], None if mask is None else mask[:, r0:r1], 0, exact)  # [B, c, R, L]
+        else:
+            a_r = _gated_half(p, z[:, :, r0:r1], None if mask is None else mask[:, :, r0:r1], 0, exact)
+            a_r = a_r.transpose(2, 3)  # [B, c, R, L]: a[d, k, i] as rows i
+        x = torch.empty(B, c, r1 - r0, L, dtype=dt)
+        for d0 in range(0, c, 16):
+            d1 = min(c, d0 + 16)
+            bb = b_all[:, d0:d1].to(dt).reshape(B * (d1 - d0), L, L)
+            ar = a_r[:, d0:d1].to(dt).reshape(B * (d1 - d0), r1 - r0, L)
+            xr = torch.bmm(ar, bb.transpose(1, 2)) if outgoing else torch.bmm(ar, bb)
+            x[:, d0:d1] = xr.reshape(B, d1 - d0, r1 - r0, L)
+        zr = z[:, r0:r1]
+        if exact:
+            n = _ln(zr, p["ln_in_w"], p["ln_in_b"], EPS, dt)
+            mixn = _ln(x.permute(0, 2, 3, 1), p["ln_mix_w"], p["ln_mix_b"], EPS if mix_eps is None else mix_eps, dt)
+            mixed = mixn @ p["w_emit"].to(dt)
+            if p.get("b_emit") is not None:
+                mixed = mixed + p["b_emit"].to(dt)
+            g = n @ p["w_out_gate"].to(dt)
+            if p.get("b_gate") is not None:
+                g = g + p["b_gate"].to(dt)
+            outs.append(zr.to(dt) + mixed * torch.sigmoid(g))
+        else:
+            out, _ = emit_residual_fp16(p, zr, r16(x), MIX_EPS_FP16 if mix_eps is None else mix_eps)
+            outs.append(out)
+    return outs[0] if single else outs
 
 
 def ulps16(ref: torch.Tensor, test: torch.Tensor) -> float:
