@@ -2,8 +2,10 @@
 
     python -m esmfold2_mlx_b200.build [--force]
 
-One translation unit (``csrc/tmu_capi.cu``) includes the three kernels; the result is a plain
-C-ABI shared library (``include/tmu.h``) with the CUDA runtime linked statically.
+One translation unit (``csrc/tmu_capi.cu``) includes every kernel header in ``csrc/`` (the tri-mul
+kernels K1-K3 and their c_z = 256 forms, the transition K4, the distogram K5, the GEMM K6 and the
+row LayerNorm pass); the result is a plain C-ABI shared library (``include/tmu.h``) with the CUDA
+runtime linked statically.
 """
 
 from __future__ import annotations

@@ -172,7 +172,7 @@ int tmu_trimul(const void* z, void* z_out, const void* mask, const tmu_trimul_we
 
 /* Size cap of tmu_trimul_noalloc: each of its three channel-major buffers (a, b, x) must fit in
  * this many bytes, i.e. B * c * L * tmu_row_pitch(L) * 2 <= 8 MiB: one fold up to L = 178 at
- * c = 128 and up to L = 126 at c = 256. */
+ * c = 128 and up to L = 128 at c = 256. */
 #define TMU_NOALLOC_MAX_BUFFER_BYTES (8u << 20)
 
 /* One triangle update, z_out = z + tri-mul(z), like tmu_trimul but without a workspace argument

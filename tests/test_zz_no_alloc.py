@@ -7,6 +7,8 @@ through the C ABI, that two calls in a row -- different shapes, directions and m
 second call reuses scratch the first one left behind -- give the same fp16 output as tmu_trimul
 on the same inputs, within the parity tests' tolerance (4 fp16 ulps at the tensor's scale; the
 kernels are the same, so equality is expected), and that sizes beyond the cap are refused.
+At the released model's width (c_z = c = 256) the cap allows one fold up to L = 128, and the
+wide kernels cannot write over their input, so an in-place call is refused.
 It is collected last so that a failure here does not stop the rest of the suite.
 """
 
@@ -32,8 +34,8 @@ def _ulp16(x: float) -> float:
 
 def _noalloc(lib, z, out, mask, w, outgoing, status):
     B, L = z.shape[0], z.shape[1]
-    return lib.tmu_trimul_noalloc(ops._ptr(z), ops._ptr(out), ops._ptr(mask), ctypes.byref(w.struct), B, L, 128, 128,
-                                  1 if outgoing else 0, ops.MIX_EPS_FP16, ops._ptr(status),
+    return lib.tmu_trimul_noalloc(ops._ptr(z), ops._ptr(out), ops._ptr(mask), ctypes.byref(w.struct), B, L, w.c_z,
+                                  w.c, 1 if outgoing else 0, ops.MIX_EPS_FP16, ops._ptr(status),
                                   ops._stream_ptr(z.device))
 
 
@@ -72,3 +74,30 @@ def test_noalloc_refuses_sizes_beyond_its_scratch():
     rc = _noalloc(lib, z, out, None, w, True, None)
     assert _lib.STATUS_NAMES[rc] == "TMU_ERR_UNSUPPORTED"
     assert b"static scratch" in lib.tmu_last_error()
+
+
+def test_noalloc_wide_cz256_matches_and_refuses_in_place():
+    """c_z = c = 256: two calls in a row against tmu_trimul, then an in-place call (z_out == z),
+    which the wide kernels cannot do, refused with TMU_ERR_INVALID_ARGUMENT before any launch."""
+    lib = _lib.load()
+    trunk = FoldingTrunk(1, 256, 256, hidden=512, seed=23, ln_noise=0.1)
+    status = ops.new_status(DEV)
+    for k, (L, direction, n_pad) in enumerate(((60, "out", 5), (128, "in", 0))):
+        w = ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + direction), DEV)
+        z = pair_tensor(1, L, 256, 50 + k).half().to(DEV)
+        mask = pair_mask(1, L, n_pad).half().to(DEV) if n_pad else None
+        ref = ops.trimul(z, mask, w, direction == "out")
+        out = torch.full_like(z, float("nan"))
+        rc = _noalloc(lib, z, out, mask, w, direction == "out", status)
+        assert rc == 0, (_lib.STATUS_NAMES.get(rc), lib.tmu_last_error())
+        code, site = ops.read_status(status)
+        assert code == 0, f"device status {code} at {site:#x}"
+        got, want = out.float().cpu(), ref.float().cpu()
+        assert torch.isfinite(got).all()
+        diff = float((got - want).abs().max())
+        assert diff <= 4 * _ulp16(float(want.abs().max())), f"call {k}: max diff {diff}"
+    rc = _noalloc(lib, z, z, None, w, False, status)
+    assert _lib.STATUS_NAMES[rc] == "TMU_ERR_INVALID_ARGUMENT"
+    z129 = torch.zeros(1, 129, 129, 256, dtype=torch.float16, device=DEV)  # 256 * 129 * 136 * 2 > 8 MiB
+    rc = _noalloc(lib, z129, torch.empty_like(z129), None, w, True, None)
+    assert _lib.STATUS_NAMES[rc] == "TMU_ERR_UNSUPPORTED"
