@@ -154,13 +154,13 @@ PAIR_COND_L = {"pc": 238, "pc476": 476}  # diffusion pair conditioning, one fold
 SHARDED_WORKLOADS = ("c5",)
 
 
-def _workload(rank: int, device, name: str = "c2"):
+def _workload(rank: int, device, name: str = "c2", world: int = 1):
     """Seeded weights and one step's input for a named configuration (``synthetic.workload``,
     the same inputs the parity tests check); ``device=None`` keeps everything on the CPU
     (reference arm)."""
     from esmfold2_mlx_b200.synthetic import workload
 
-    wl = workload(name, rank)
+    wl = workload(name, rank, world)
     w = None
     if device is not None:
         from esmfold2_mlx_b200 import ops
@@ -347,33 +347,27 @@ def _trunk_recycle(device, flush, reps: int = 3):
             "output_finite": finite}
 
 
-def run_sharded(args, ws, rank, local):
+def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True) -> dict:
     """one fold of L = 3072, outgoing then incoming tri-mul, its rows split over
     the N ranks (strong scaling: the total work is fixed).  Each rank projects its rows (for the
-    incoming form after an all-to-all of z's column blocks), b is all-gathered asynchronously
-    while the local block is contracted, and each rank finishes its rows.  Eager launches (no
-    graph); inputs per rank (>= 302 MB at N = 8) exceed L2, so no flush is needed."""
-    from esmfold2_mlx_b200 import _lib, ops
+    incoming form from its columns, which the copy engines pull from every rank's rows with one
+    pitched copy per peer), b is exchanged while the local block is contracted (copy engines over
+    NVLink by default, ``nccl``: an NCCL all-gather), and each rank finishes its rows.  Eager
+    launches; the inputs per rank (>= 302 MB at N = 8) exceed L2, so no flush is needed."""
+    from esmfold2_mlx_b200 import ops
     from esmfold2_mlx_b200.sharded import CopyEngineExchange, DistExchange, LocalExchange, RowShardedTrimul
-    from esmfold2_mlx_b200.synthetic import CONFIGS, FoldingTrunk, pair_tensor
 
     device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
-    cfg = CONFIGS[args.workload]
+    cfg, trunk, _, w, z_host, _ = _workload(rank, device, "c5", ws)
     L = cfg.L
-    trunk = FoldingTrunk(1, C_Z, C, seed=cfg.seed)
-    w = {d: ops.TrimulWeights.from_module(getattr(trunk.blocks[0], "tri_mul_" + d), device) for d in ("out", "in")}
-
     if ws == 1:
         ex = LocalExchange()
-    elif args.c5_nccl:
+    elif nccl:
         ex = DistExchange(None)
     else:
         ex = CopyEngineExchange(None)
     sh = RowShardedTrimul(L, device=device, exchange=ex)
     Lr = sh.Lr
-    z_host = pair_tensor(1, L, C_Z, cfg.seed).half()[:, rank * Lr:(rank + 1) * Lr].contiguous()
     z0 = z_host.to(device)
     z1 = torch.empty_like(z0)
     z2 = torch.empty_like(z0)
@@ -382,13 +376,13 @@ def run_sharded(args, ws, rank, local):
         sh(zin, None, w["out"], True, out=z1)
         return sh(z1, None, w["in"], False, out=z2)
 
-    for _ in range(max(3, args.warmup)):
+    for _ in range(max(3, warmup)):
         step(z0)
     torch.cuda.synchronize()
     _barrier(ws)
     sampler = ClockSampler(local)
     sampler.start()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     torch.cuda.synchronize()
     _barrier(ws)
     for e0, e1 in evs:
@@ -399,8 +393,7 @@ def run_sharded(args, ws, rank, local):
     _barrier(ws)
     clocks = sampler.stop()
     step_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
-    step_ms_max = _max_over_ranks(step_ms, ws, device)
-    ms_per_step = step_ms_max / args.steps
+    ms_per_step = _max_over_ranks(step_ms, ws, device) / steps
     cells = 2 * L * L
     code, site = ops.read_status(sh.stages.status)
     if code != 0:
@@ -411,7 +404,7 @@ def run_sharded(args, ws, rank, local):
     outh = torch.empty_like(z_host).pin_memory()
     z_in = torch.empty_like(z0)
     e2e_ms = 0.0
-    for i in range(args.steps + 1):
+    for i in range(steps + 1):
         _barrier(ws)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -421,32 +414,107 @@ def run_sharded(args, ws, rank, local):
         e1.synchronize()
         if i >= 1:
             e2e_ms += e0.elapsed_time(e1)
-    e2e_ms = _max_over_ranks(e2e_ms, ws, device) / args.steps
+    e2e_ms = _max_over_ranks(e2e_ms, ws, device) / steps
     pitch = ops.row_pitch(L)
     # bytes each rank receives per step: (P-1)/P of b for both directions, plus z's column blocks
-    recv = (ws - 1) * (2 * C * Lr * pitch * 2 + Lr * Lr * C_Z * 2)
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": cells / (ms_per_step * 1e-3), "unit": UNIT, "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": cfg.name, "L": L, "B": 1, "c_z": C_Z, "c": C, "directions": ["out", "in"],
-                       "parallelism": f"rows x{ws} (row-sharded fold; NCCL all-gather of b, all-to-all of z blocks)",
-                       "l2": "inputs larger than L2 (no flush)", "launch": "eager"},
-            "e2e": {"value": cells / (e2e_ms * 1e-3), "unit": UNIT,
-                    "h2d_bytes_per_step": zh.numel() * 2, "d2h_bytes_per_step": outh.numel() * 2,
-                    "ms_per_step": round(e2e_ms, 4)},
-            "gpu_launches": 6 * args.steps,
-            "collectives": {"recv_bytes_per_rank_per_step": recv,
-                            "b_transfer": "NCCL all-gather" if (ws > 1 and args.c5_nccl) else
-                                          ("copy engines (CUDA IPC, cudaMemcpyAsync)" if ws > 1 else "none"),
-                            "note": "all-to-all of z blocks (incoming form, NCCL); b's remote blocks arrive "
-                                    "while the local block is contracted"},
-            "clocks": clocks,
-        }
-        print(json.dumps(line), flush=True)
+    recv = (ws - 1) * (2 * cfg.c * Lr * pitch * 2 + Lr * Lr * cfg.c_z * 2)
+    link_gbs = 770.0  # measured peer copy per direction on this pool's NVLink (bytes / s / 1e9)
+    comm_ms = recv / (link_gbs * 1e9) * 1e3
+    flops = 2 * (2 * cfg.c * L) * Lr * L  # the contraction's FLOPs per rank per step (both directions)
+    hbm, tflops, peak_kind = _peaks()
+    tensor_ms = flops / (tflops * 1e12) * 1e3
+    bound_ms = max(comm_ms, tensor_ms)
+    res = {"workload": cfg.name, "L": L, "B": 1, "c_z": cfg.c_z, "n_gpus": ws, "scaling": "strong",
+           "value": cells / (ms_per_step * 1e-3), "unit": UNIT, "ms_per_step": round(ms_per_step, 4),
+           "steps": steps,
+           "parallelism": f"rows x{ws} (row-sharded fold)",
+           "exchange": ("none" if ws == 1 else "NCCL all-gather of b" if nccl else
+                        "copy engines over NVLink (CUDA IPC): b slabs by cudaMemcpyAsync, z column blocks "
+                        "(incoming all-to-all + transpose) by one cudaMemcpy2DAsync per peer"),
+           "roofline": {"bound": "nvlink" if comm_ms > tensor_ms else "tensor",
+                        "recv_bytes_per_rank_per_step": recv, "nvlink_gbs_per_direction": link_gbs,
+                        "comm_floor_ms": round(comm_ms, 4), "contraction_floor_ms": round(tensor_ms, 4),
+                        "frac": round(bound_ms / ms_per_step, 4),
+                        "note": "floor = max(received bytes / measured 770 GB/s peer copy, contraction FLOPs / "
+                                f"{tflops} TFLOP/s {peak_kind} peak); frac = floor / measured step"},
+           "e2e": {"value": cells / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": zh.numel() * 2,
+                   "d2h_bytes_per_step": outh.numel() * 2, "ms_per_step": round(e2e_ms, 4)},
+           "gpu_launches": 6 * steps, "clocks": clocks}
+    if parity:
+        res["parity"] = _c5_parity(cfg, trunk, z2 if ws > 1 else z2, z1, rank, ws)
     if hasattr(ex, "close"):
         ex.close()
+    return res
+
+
+def _c5_parity(cfg, trunk, z2, z1, rank, ws) -> dict | None:
+    """Rows [124, 128) of the row-sharded step's outgoing result (rank 0 holds them) against the
+    oracle's row slab; the exact reference here is float32 arithmetic without the fp16 rounding
+    points (2^13 finer than the fp16 errors it measures; the test suite uses float64)."""
+    if rank != 0:
+        _barrier(ws)
+        return None
+    from esmfold2_mlx_b200.synthetic import pair_rows
+    from oracle import trimul_oracle as orc
+
+    z = pair_rows(cfg.L, cfg.c_z, cfg.seed, 0, cfg.L).half()
+    rows = range(124, 128)
+    tri = trunk.blocks[0].tri_mul_out
+    ref16 = orc.trimul_rows(orc.trimul_params(tri, True), z, None, True, rows)
+    exact = orc.trimul_rows(orc.trimul_params(tri, False), z, None, True, rows, exact=True,
+                            exact_dtype=torch.float32)
+    res = orc.parity(exact, ref16, z1[:, rows.start:rows.stop].float().cpu())
+    res.update({"rows": [rows.start, rows.stop], "direction": "out",
+                "exact": "float32 arithmetic (no fp16 rounding points)"})
+    _barrier(ws)
+    return res
+
+
+def run_sharded(args, ws, rank, local):
+    """``--workload c5``: the row-sharded long fold as the line's own metric."""
+    from esmfold2_mlx_b200 import _lib
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
+    res = _c5_measure(ws, rank, local, args.steps, args.warmup, args.c5_nccl, not args.no_parity)
+    if rank == 0:
+        line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+                "config": {"workload": res["workload"], "L": res["L"], "B": 1, "c_z": res["c_z"],
+                           "directions": ["out", "in"], "parallelism": res["parallelism"],
+                           "exchange": res["exchange"], "l2": "inputs larger than L2 (no flush)", "launch": "eager"},
+                "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "roofline": res["roofline"],
+                "parity": res.get("parity"), "clocks": res["clocks"]}
+        print(json.dumps(line), flush=True)
+
+
+def _c4_measure(ws, rank, local, steps, warmup, flush, stream, parity=True) -> dict:
+    """BASELINE config 4 as a fixed batch: 64 folds of L = 146 split 64 / N per rank (strong
+    scaling, no collective on the data path), out + in per fold; max over ranks."""
+    device = torch.device("cuda", local)
+    case = TrimulCase("c4", rank, device, stream, world=ws)
+    for _ in range(max(3, warmup)):
+        flush.zero_()
+        case.g_step.replay()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    ms = _max_over_ranks(case.time_steps(flush, steps), ws, device) / steps
+    code, site = case.ops.read_status(case.wsp.status)
+    if code != 0:
+        raise RuntimeError(f"device status {code} at site {site:#x}")
+    total_cells = 2 * case.cfg.B * case.cfg.L * case.cfg.L  # all 64 folds, out + in
+    tr = case.trace(flush, 5)
+    dom, kernels = case.kernel_table(tr)
+    res = {"workload": case.cfg.name, "L": case.cfg.L, "folds": case.cfg.B, "folds_per_gpu": case.cfg.B // ws,
+           "n_gpus": ws, "scaling": "strong", "value": total_cells / (ms * 1e-3), "unit": UNIT,
+           "ms_per_step": round(ms, 5), "steps": steps, "dominant_kernel": dom, "kernels": kernels,
+           "parallelism": f"folds x{ws} (64 / {ws} folds per GPU, no collective)"}
+    if parity and rank == 0:
+        res["parity"] = case.parity(folds=[0, case.z0.shape[0] - 1])
+    _barrier(ws)
+    return res
 
 
 class TrimulCase:
@@ -457,23 +525,24 @@ class TrimulCase:
 
     NAMES = ("K1_project_gate", "K2_contract", "K3_emit_residual")
 
-    def __init__(self, name: str, rank: int, device, stream):
+    def __init__(self, name: str, rank: int, device, stream, world: int = 1):
         from esmfold2_mlx_b200 import _lib, ops
 
         self.ops, self.lib = ops, _lib.load()
-        self.cfg, self.trunk, self.biases, self.w, self.z_host, self.mask_host = _workload(rank, device, name)
+        self.cfg, self.trunk, self.biases, self.w, self.z_host, self.mask_host = _workload(rank, device, name, world)
         cfg = self.cfg
+        self.B = self.z_host.shape[0]  # folds on this rank
         self.device, self.stream = device, stream
         self.z0 = self.z_host.to(device)
         self.mask = None if self.mask_host is None else self.mask_host.to(device)
         self.z1, self.z2 = torch.empty_like(self.z0), torch.empty_like(self.z0)
         self.wsp = ops.Workspace()
-        self.wsp.get(cfg.B, cfg.L, cfg.c_z, cfg.c, device)
+        self.wsp.get(self.B, cfg.L, cfg.c_z, cfg.c, device)
         Lp = ops.row_pitch(cfg.L)
-        self.a = torch.empty(cfg.B * cfg.c, cfg.L, Lp, dtype=torch.float16, device=device)
+        self.a = torch.empty(self.B * cfg.c, cfg.L, Lp, dtype=torch.float16, device=device)
         self.b, self.x = torch.empty_like(self.a), torch.empty_like(self.a)
         self.trace_st = torch.zeros(6, 256, dtype=torch.uint8, device=device)
-        self.cells = 2 * cfg.B * cfg.L * cfg.L  # pair-cells per step (out + in)
+        self.cells = 2 * self.B * cfg.L * cfg.L  # pair-cells per step on this rank (out + in)
         self.step()
         self.step_traced()
         torch.cuda.synchronize()
@@ -496,12 +565,12 @@ class TrimulCase:
         for k, (d, outgoing, zout) in enumerate((("out", True, self.z1), ("in", False, self.z2))):
             wt = self.w[d]
             st = [self.trace_st[3 * k + j] for j in range(3)]
-            _check(lib.tmu_project_gate(ops._ptr(zin), ops._ptr(self.mask), ops.ctypes.byref(wt.struct), cfg.B, cfg.L,
+            _check(lib.tmu_project_gate(ops._ptr(zin), ops._ptr(self.mask), ops.ctypes.byref(wt.struct), self.B, cfg.L,
                                         cfg.c_z, cfg.c, ops._ptr(self.a), ops._ptr(self.b), ops._ptr(st[0]), sp), "K1")
-            _check(lib.tmu_contract(ops._ptr(self.a), ops._ptr(self.b), ops._ptr(self.x), cfg.B * cfg.c, cfg.L,
+            _check(lib.tmu_contract(ops._ptr(self.a), ops._ptr(self.b), ops._ptr(self.x), self.B * cfg.c, cfg.L,
                                     1 if outgoing else 0, ops._ptr(st[1]), sp), "K2")
             _check(lib.tmu_emit_residual(ops._ptr(self.x), ops._ptr(zin), ops._ptr(zout), ops.ctypes.byref(wt.struct),
-                                         cfg.B, cfg.L, cfg.c_z, cfg.c, ops.MIX_EPS_FP16, ops._ptr(st[2]), sp), "K3")
+                                         self.B, cfg.L, cfg.c_z, cfg.c, ops.MIX_EPS_FP16, ops._ptr(st[2]), sp), "K3")
             zin = zout
 
     def time_steps(self, flush, steps: int) -> float:
@@ -546,7 +615,7 @@ class TrimulCase:
         spans, and the fraction of the roofline its algorithmic bytes or FLOPs reach in that time."""
         hbm, tflops, _ = _peaks()
         cfg = self.cfg
-        costs = _kernel_costs(cfg.L, cfg.B, self.mask is not None, cfg.c_z, cfg.c)
+        costs = _kernel_costs(cfg.L, self.B, self.mask is not None, cfg.c_z, cfg.c)
         total = sum(tr["spans_us"])
         kernels = {}
         for j, n in enumerate(self.NAMES):
@@ -562,18 +631,19 @@ class TrimulCase:
         dom = max(self.NAMES, key=lambda n: kernels[n]["us_in_step"])
         return dom, kernels
 
-    def parity(self, slab_rows: int | None = None) -> dict:
+    def parity(self, slab_rows: int | None = None, folds=None) -> dict:
         """The step's outputs (left by the last replay) against the CPU oracle, used as the checker:
         e_cuda vs e_ref (exact float64 update) and the distance in fp16 ulps, per direction, each
-        on the same input (in: the CUDA out result).  Large L: rows [124, 124 + slab_rows) only."""
+        on the same input (in: the CUDA out result).  Large L: rows [124, 124 + slab_rows) only;
+        ``folds``: those folds only."""
         from oracle import trimul_oracle as orc
 
         torch.cuda.synchronize()
-        cfg = self.cfg
-        z1h, z2h = self.z1.cpu(), self.z2.cpu()
-        m = None if self.mask_host is None else self.mask_host.float()
+        sel = slice(None) if folds is None else list(folds)
+        z1h, z2h = self.z1.cpu()[sel], self.z2.cpu()[sel]
+        m = None if self.mask_host is None else self.mask_host.float()[sel]
         res = {}
-        steps = (("out", True, self.z_host, z1h), ("in", False, z1h, z2h))
+        steps = (("out", True, self.z_host[sel], z1h), ("in", False, z1h, z2h))
         if slab_rows is not None:
             steps = steps[:1]  # the outgoing update; both directions are checked in the test suite
         for d, outgoing, zin, got in steps:
@@ -686,7 +756,7 @@ def run_b200(args, ws, rank, local):
     flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
     case = TrimulCase(args.workload, rank, device, stream)
     cfg, w = case.cfg, case.w
-    L, B = cfg.L, cfg.B
+    L, B = cfg.L, case.B
     C_Z, C = cfg.c_z, cfg.c  # noqa: N806 - the pair and latent widths of this workload
     mask, z_host, mask_host = case.mask, case.z_host, case.mask_host
     trunk, biases = case.trunk, case.biases
@@ -842,6 +912,13 @@ def run_b200(args, ws, rank, local):
             sub = TrimulCase(name, 0, device, stream)
             extra[name] = _case_summary(sub, flush, min(args.steps, 20), args.warmup, not args.no_parity, slab)
             del sub
+    if not args.no_extra and args.workload == "c2":
+        # the two multi-GPU configurations, at every N (N = 1 is their scaling baseline)
+        extra["c4"] = _c4_measure(ws, rank, local, min(args.steps, 20), args.warmup, flush, stream,
+                                  not args.no_parity)
+        torch.cuda.empty_cache()
+        extra["c5"] = _c5_measure(ws, rank, local, min(args.steps, 10), args.warmup, False, not args.no_parity)
+        torch.cuda.empty_cache()
 
     # ---------------- CPU baseline (rank 0, N = 1) ----------------
     cpu = None

@@ -120,6 +120,7 @@ SIGNATURES = {
     "tmu_ipc_import": (_i, [_vp, _ull, ctypes.POINTER(_vp)]),
     "tmu_ipc_close": (_i, [_vp]),
     "tmu_copy_async": (_i, [_vp, _vp, _sz, _vp]),
+    "tmu_copy2d_async": (_i, [_vp, _sz, _vp, _sz, _sz, _sz, _vp]),
     "tmu_selftest_wait_timeout": (_i, [_vp, _ull, _vp]),
 }
 

@@ -1402,6 +1402,15 @@ int tmu_copy_async(void* dst, const void* src, size_t bytes, void* stream) {
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "cudaMemcpyAsync");
 }
 
+int tmu_copy2d_async(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width, size_t height,
+                     void* stream) {
+  if (dst == nullptr || src == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "NULL argument");
+  if (width > dst_pitch || width > src_pitch) return fail(TMU_ERR_INVALID_ARGUMENT, "width exceeds a pitch");
+  cudaError_t e = cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width, height, cudaMemcpyDeviceToDevice,
+                                    static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "cudaMemcpy2DAsync");
+}
+
 int tmu_selftest_wait_timeout(void* status, unsigned long long timeout_ns, void* stream) {
   if (status == nullptr) return fail(TMU_ERR_INVALID_ARGUMENT, "status is NULL");
   wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<DeviceStatus*>(status),

@@ -115,35 +115,19 @@ class DistExchange:
         handle.wait()
 
 
-class CopyEngineExchange(DistExchange):
-    """The b slabs moved by the GPUs' copy engines instead of NCCL kernels.
+class _SharedPair:
+    """Two persistent device buffers of one shape that every peer maps once through CUDA IPC
+    (``tmu_ipc_export`` / ``tmu_ipc_import``), used alternately by successive calls, with an
+    interprocess "ready" event (the owner recorded it after writing the buffer) and "read" event
+    (a rank recorded it after pulling every peer's buffer of that parity) per buffer."""
 
-    Each rank writes its b slab into one of two persistent buffers (alternating per call) that
-    every peer has mapped once through CUDA IPC (``tmu_ipc_export`` / ``tmu_ipc_import``).  Per
-    call: the owner records an interprocess "ready" event after K1; the ranks meet at a host
-    barrier (gloo), so every peer enqueues its wait after that record; each rank's copy stream
-    waits on the peers' ready events and pulls their slabs with ``cudaMemcpyAsync`` over NVLink
-    (``tmu_copy_async``) -- no SM time, so the local block's contraction runs at full speed
-    beside it -- and records a "read" event that the owner waits on before it rewrites the same
-    buffer two calls later.  No kernel reads another GPU's memory.  The incoming form's
-    all-to-all of z blocks stays on NCCL (``DistExchange``).
-    """
-
-    def __init__(self, group=None, host_group=None):
-        super().__init__(group)
-        self.host_group = host_group if host_group is not None else dist.new_group(backend="gloo")
-        self._shape = None
-        self.calls = 0
-
-    def _setup(self, shape, dtype, device):
+    def __init__(self, ex, shape, dtype, device):
         lib = _lib.load()
-        P, r = self.size, self.rank
+        P, r = ex.size, ex.rank
+        self.ex, self.shape = ex, tuple(shape)
         self.bufs = [torch.empty(shape, dtype=dtype, device=device) for _ in range(2)]
-        self.parts = torch.empty((P,) + tuple(shape), dtype=dtype, device=device)
-        self.copy_stream = torch.cuda.Stream(device)
         self.ready = [torch.cuda.Event(interprocess=True) for _ in range(2)]
         self.read = [torch.cuda.Event(interprocess=True) for _ in range(2)]
-        self.copied = torch.cuda.Event()
         for e in self.ready + self.read:  # materialise the events on this device before export
             e.record(torch.cuda.current_stream(device))
         rec = bytearray()
@@ -156,7 +140,7 @@ class CopyEngineExchange(DistExchange):
             rec += bytes(e.ipc_handle())
         mine = torch.frombuffer(bytearray(rec), dtype=torch.uint8).to(device)
         every = torch.empty(P * mine.numel(), dtype=torch.uint8, device=device)
-        dist.all_gather_into_tensor(every, mine, group=self.group)
+        dist.all_gather_into_tensor(every, mine, group=ex.group)
         every = every.view(P, -1).cpu().numpy().tobytes()
         n = mine.numel()
         self.peer_bufs, self.peer_ready, self.peer_read = {}, {}, {}
@@ -168,60 +152,154 @@ class CopyEngineExchange(DistExchange):
             for i in range(2):
                 h = blob[i * 72:i * 72 + 64]
                 off = int.from_bytes(blob[i * 72 + 64:i * 72 + 72], "little")
-                p = ctypes.c_void_p()
-                _lib.check(lib.tmu_ipc_import(h, off, ctypes.byref(p)), "tmu_ipc_import")
-                ptrs.append(p.value)
+                ptr = ctypes.c_void_p()
+                _lib.check(lib.tmu_ipc_import(h, off, ctypes.byref(ptr)), "tmu_ipc_import")
+                ptrs.append(ptr.value)
             self.peer_bufs[q] = ptrs
             ev = [blob[144 + 64 * i:144 + 64 * (i + 1)] for i in range(4)]
             self.peer_ready[q] = [torch.cuda.Event.from_ipc_handle(device, ev[i]) for i in range(2)]
             self.peer_read[q] = [torch.cuda.Event.from_ipc_handle(device, ev[2 + i]) for i in range(2)]
         self.nbytes = self.bufs[0].numel() * self.bufs[0].element_size()
-        self._shape = tuple(shape)
-        dist.barrier(group=self.host_group)
+        self.calls = 0
 
-    def slab_for_write(self, shape, dtype, device):
-        """This call's persistent buffer for the local b slab (K1 writes into it)."""
-        if self._shape != tuple(shape):
-            self._setup(shape, dtype, device)
+    def for_write(self, device):
+        """This call's buffer; the current stream first waits until every peer has finished
+        copying what it held two calls ago."""
         par = self.calls & 1
-        if self.calls >= 2:  # the peers finished copying this buffer's previous content
+        if self.calls >= 2:
             cur = torch.cuda.current_stream(device)
             for q in self.peer_read:
                 cur.wait_event(self.peer_read[q][par])
         return self.bufs[par]
 
+    def publish(self):
+        """Mark this call's buffer written (on the current stream) and meet the peers at a host
+        barrier, so every wait they enqueue next sees this record.  Returns the parity."""
+        par = self.calls & 1
+        self.calls += 1
+        self.ready[par].record(torch.cuda.current_stream())
+        dist.barrier(group=self.ex.host_group)
+        return par
+
+    def close(self):
+        lib = _lib.load()
+        for ptrs in self.peer_bufs.values():
+            for p in ptrs:
+                lib.tmu_ipc_close(ctypes.c_void_p(p))
+        self.peer_bufs = {}
+
+
+class CopyEngineExchange(DistExchange):
+    """The slabs moved by the GPUs' copy engines instead of NCCL kernels.
+
+    Outgoing b: each rank's K1 writes its b slab into one of two persistent buffers
+    (alternating per call) that every peer mapped once through CUDA IPC.  Per call the owner
+    records an interprocess "ready" event; the ranks meet at a host barrier (gloo), so every
+    peer enqueues its wait after that record; each rank's copy stream waits on the peers' ready
+    events and pulls their slabs with ``cudaMemcpyAsync`` over NVLink (``tmu_copy_async``) -- no
+    SM time, so the local block's contraction runs at full speed beside it -- and records a
+    "read" event that the owner waits on before it rewrites the same buffer two calls later.
+
+    Incoming z: the all-to-all and the transpose into column blocks are one pitched copy per
+    peer (``tmu_copy2d_async``): rank r pulls, from each peer q's exported row slab
+    z_q [Lr, L, c_z], the block of its own columns (Lr rows of Lr * c_z contiguous elements,
+    L * c_z apart) straight into slot q of its [P, Lr, Lr, c_z] buffer, with the same
+    ready / read protocol.  No kernel reads another GPU's memory.  A mask, when present, still
+    travels by NCCL (2 bytes per position against z's 2 c_z)."""
+
+    def __init__(self, group=None, host_group=None):
+        super().__init__(group)
+        self.host_group = host_group if host_group is not None else dist.new_group(backend="gloo")
+        self._b = None
+        self._z = None
+        self.copy_stream = None
+
+    def _stream(self, device):
+        if self.copy_stream is None:
+            self.copy_stream = torch.cuda.Stream(device)
+            self.copied = torch.cuda.Event()
+        return self.copy_stream
+
+    # ---- outgoing b slabs
+    def slab_for_write(self, shape, dtype, device):
+        """This call's persistent buffer for the local b slab (K1 writes into it)."""
+        if self._b is None or self._b.shape != tuple(shape):
+            if self._b is not None:
+                self._b.close()
+            self._b = _SharedPair(self, shape, dtype, device)
+            self.parts = torch.empty((self.size,) + tuple(shape), dtype=dtype, device=device)
+            dist.barrier(group=self.host_group)
+        return self._b.for_write(device)
+
     def gather_start(self):
         """Publish this call's slab and start pulling the peers' into ``parts``; returns
         (parts [P, *shape], handle).  The local slot of ``parts`` is left unwritten."""
         lib = _lib.load()
-        par = self.calls & 1
-        self.calls += 1
-        cur = torch.cuda.current_stream()
-        self.ready[par].record(cur)
-        dist.barrier(group=self.host_group)  # every rank has recorded: the waits below see it
-        cs = self.copy_stream
-        for q, ptrs in self.peer_bufs.items():
-            cs.wait_event(self.peer_ready[q][par])
-            _lib.check(lib.tmu_copy_async(ops._ptr(self.parts[q]), ptrs[par], self.nbytes, cs.cuda_stream),
+        sp = self._b
+        par = sp.publish()
+        cs = self._stream(sp.bufs[0].device)
+        # ``parts`` is rewritten below: the previous call's contractions, which read it on the
+        # current stream, must be done first
+        cs.wait_stream(torch.cuda.current_stream(sp.bufs[0].device))
+        for q, ptrs in sp.peer_bufs.items():
+            cs.wait_event(sp.peer_ready[q][par])
+            _lib.check(lib.tmu_copy_async(ops._ptr(self.parts[q]), ptrs[par], sp.nbytes, cs.cuda_stream),
                        "tmu_copy_async")
-        self.read[par].record(cs)
+        sp.read[par].record(cs)
         self.copied.record(cs)
         return self.parts, self.copied
+
+    # ---- incoming z column blocks
+    def columns(self, z_rows: torch.Tensor, Lr: int) -> torch.Tensor:
+        """z_rows [Lr, L, c] (this rank's rows) -> [P, Lr, Lr, c] with slot q = z[q's rows, my
+        columns], pulled by the copy engines; the current stream waits for the result."""
+        lib = _lib.load()
+        device = z_rows.device
+        shape = tuple(z_rows.shape)
+        if self._z is None or self._z.shape != shape:
+            if self._z is not None:
+                self._z.close()
+            self._z = _SharedPair(self, shape, z_rows.dtype, device)
+            self.zt = torch.empty((self.size, Lr, Lr) + shape[2:], dtype=z_rows.dtype, device=device)
+            dist.barrier(group=self.host_group)
+        sp = self._z
+        buf = sp.for_write(device)
+        if buf.data_ptr() != z_rows.data_ptr():
+            buf.copy_(z_rows)
+        par = sp.publish()
+        cs = self._stream(device)
+        cs.wait_stream(torch.cuda.current_stream(device))
+        row_bytes = shape[1] * shape[2] * z_rows.element_size()  # one row of z: L positions x c
+        blk = Lr * shape[2] * z_rows.element_size()               # this rank's Lr columns of it
+        col0 = self.rank * blk
+        for q in range(self.size):
+            dst = self.zt[q]
+            if q == self.rank:
+                src = buf.data_ptr() + col0
+            else:
+                cs.wait_event(sp.peer_ready[q][par])
+                src = sp.peer_bufs[q][par] + col0
+            _lib.check(lib.tmu_copy2d_async(ops._ptr(dst), blk, ctypes.c_void_p(src), row_bytes, blk, Lr,
+                                            cs.cuda_stream), "tmu_copy2d_async")
+        sp.read[par].record(cs)
+        done = torch.cuda.Event()
+        done.record(cs)
+        torch.cuda.current_stream(device).wait_event(done)
+        return self.zt
 
     def wait(self, handle):
         torch.cuda.current_stream().wait_event(handle)
 
     def close(self):
         """Release the imported peer mappings (after every rank is done with them)."""
-        if self._shape is None:
+        if self._b is None and self._z is None:
             return
-        lib = _lib.load()
         torch.cuda.synchronize()
         dist.barrier(group=self.host_group)
-        for ptrs in self.peer_bufs.values():
-            for p in ptrs:
-                lib.tmu_ipc_close(ctypes.c_void_p(p))
-        self._shape = None
+        for sp in (self._b, self._z):
+            if sp is not None:
+                sp.close()
+        self._b = self._z = None
 
 
 class LocalExchange:
@@ -273,6 +351,8 @@ class RowShardedTrimul:
     def _to_columns(self, t):
         """[Lr(my rows), L, ...] -> [P(source), Lr(source rows), Lr(my columns), ...]."""
         P, Lr = self.P, self.Lr
+        if hasattr(self.exchange, "columns") and t.dim() == 3:  # z: one pitched copy per peer
+            return self.exchange.columns(t, Lr)
         # [Lr, P, Lr, ...] -> [P(dest), Lr, Lr, ...]: one copy with Lr*c contiguous elements per run
         send = t.reshape((Lr, P, Lr) + tuple(t.shape[2:])).transpose(0, 1).contiguous()
         return self.exchange.all_to_all(send)

@@ -233,16 +233,49 @@ class Workload:
     mask: torch.Tensor | None
 
 
-def workload(name: str, rank: int = 0) -> Workload:
-    """The inputs the benchmark times for configuration ``name`` (rank ``rank`` of a multi-GPU
-    run draws its own fold, seed + rank); the parity tests use exactly these."""
+def pair_rows(L: int, c_z: int, seed: int, r0: int, r1: int, block: int = 128) -> torch.Tensor:
+    """Rows [r0, r1) of one fold's z ~ N(0, 1) [1, L, L, c_z] fp32 generated in blocks of ``block``
+    rows, block k from its own generator (seed * 1000 + k), so that each rank of a row-sharded
+    run draws only its own rows and every rank's rows agree with the whole tensor's."""
+    out = torch.empty(1, r1 - r0, L, c_z)
+    for k in range(r0 // block, (r1 + block - 1) // block):
+        b0, b1 = k * block, min(L, (k + 1) * block)
+        g = torch.Generator().manual_seed(seed * 1000 + k)
+        blk = torch.randn(1, b1 - b0, L, c_z, generator=g)
+        s0, s1 = max(b0, r0), min(b1, r1)
+        out[:, s0 - r0:s1 - r0] = blk[:, s0 - b0:s1 - b0]
+    return out
+
+
+def workload(name: str, rank: int = 0, world: int = 1) -> Workload:
+    """The inputs the benchmark times for configuration ``name`` on rank ``rank`` of ``world``;
+    the parity tests use exactly these.
+
+    * ``c4`` (64 folds, strong scaling): the rank's share of the folds, fold ``idx`` drawn with
+      seed 100 + idx (the configuration's per-fold seeds);
+    * ``c5`` (one long fold, row-sharded): the rank's rows, drawn block by block (``pair_rows``);
+    * the others: one fold group per rank, drawn with seed + rank (weak scaling)."""
     cfg = CONFIGS[name]
     trunk = FoldingTrunk(1, cfg.c_z, cfg.c, seed=cfg.seed)
     biases = {d: (trimul_biases(cfg.c_z, cfg.c, cfg.seed + 31 + i) if cfg.biases else None)
               for i, d in enumerate(("out", "in"))}
-    z = pair_tensor(cfg.B, cfg.L, cfg.c_z, cfg.seed + rank).half()
-    mask = pair_mask(cfg.B, cfg.L, cfg.n_pad).half() if cfg.n_pad else None
-    return Workload(cfg, trunk, biases, z, mask)
+    if name == "c4":
+        if cfg.B % world:
+            raise ValueError(f"{cfg.B} folds do not split over {world} ranks")
+        per = cfg.B // world
+        z = torch.cat([pair_tensor(1, cfg.L, cfg.c_z, cfg.seed + idx) for idx in range(rank * per, (rank + 1) * per)])
+        B = per
+    elif name == "c5":
+        Lr = cfg.L // world
+        z = pair_rows(cfg.L, cfg.c_z, cfg.seed, rank * Lr, (rank + 1) * Lr)
+        B = cfg.B
+    else:
+        z = pair_tensor(cfg.B, cfg.L, cfg.c_z, cfg.seed + rank)
+        B = cfg.B
+    mask = pair_mask(B, cfg.L, cfg.n_pad).half() if cfg.n_pad else None
+    if name == "c5" and mask is not None:
+        mask = mask[:, rank * Lr:(rank + 1) * Lr].contiguous()
+    return Workload(cfg, trunk, biases, z.half(), mask)
 
 
 def recycle_workload(name: str = "c3"):

@@ -320,6 +320,13 @@ int tmu_ipc_import(const void* handle, unsigned long long offset, void** ptr);
 int tmu_ipc_close(void* ptr);
 int tmu_copy_async(void* dst, const void* src, size_t bytes, void* stream);
 
+/* A pitched copy by the copy engines (cudaMemcpy2DAsync): `height` rows of `width` bytes from
+ * `src` (rows `src_pitch` bytes apart) to `dst` (rows `dst_pitch` bytes apart).  The row-sharded
+ * incoming update pulls each peer's block of z rows x this rank's columns with one such copy,
+ * which is the all-to-all and its transpose in one transfer. */
+int tmu_copy2d_async(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width, size_t height,
+                     void* stream);
+
 /* Self-test of the bounded-wait machinery: launches one CTA that waits on an mbarrier nothing
  * ever arrives at, with a limit of `timeout_ns`; the kernel must give up, record
  * TMU_ERR_DEVICE_TIMEOUT in `status` and exit.  Returns the launch status. */

@@ -247,7 +247,7 @@ def _ln(x, w, b, eps, dtype):
 # --------------------------------------------------------------------------------------
 
 
-def _gated_half(p: dict, z: torch.Tensor, mask, half: int, exact: bool) -> torch.Tensor:
+def _gated_half(p: dict, z: torch.Tensor, mask, half: int, exact: bool, exact_dtype=torch.float64) -> torch.Tensor:
     """One gated operand (half 0: a, half 1: b) on a [B, rows, cols, c_z] grid, channel-major
     [B, c, rows, cols]: only the projection columns of that operand (its signal and gate
     columns), with the same arithmetic as :func:`project_gate_fp16` (``exact``: float64 and no
@@ -255,7 +255,7 @@ def _gated_half(p: dict, z: torch.Tensor, mask, half: int, exact: bool) -> torch
     c = p["c"]
     cols = list(range(half * c, half * c + c)) + list(range(2 * c + half * c, 3 * c + half * c))
     if exact:
-        dt = torch.float64
+        dt = exact_dtype
         n = _ln(z, p["ln_in_w"], p["ln_in_b"], EPS, dt)
         proj = n @ p["w_in"][:, cols].to(dt)
         if p.get("b_in") is not None:
@@ -277,7 +277,7 @@ def _gated_half(p: dict, z: torch.Tensor, mask, half: int, exact: bool) -> torch
 
 
 def trimul_rows(p: dict, z: torch.Tensor, mask, outgoing: bool, rows, exact: bool = False,
-                mix_eps: float | None = None, chunk: int = 64):
+                mix_eps: float | None = None, chunk: int = 64, exact_dtype=torch.float64):
     """Rows of ``z + trimul(z)`` without forming the whole update: ``rows`` is a range of i, or a
     list of ranges (slabs) that share one projection of b.
 
@@ -286,8 +286,10 @@ def trimul_rows(p: dict, z: torch.Tensor, mask, outgoing: bool, rows, exact: boo
     i) and all of b.  b is projected in chunks of ``chunk`` rows and kept in fp16 (exact: its
     values are fp16 roundings) or, with ``exact``, in fp32 (float64 arithmetic otherwise; the
     fp32 storage of b is 2^13 times finer than the fp16 errors this reference measures).
-    ``z`` may be fp16 or fp32.  With ``exact``, ``p`` comes from ``trimul_params(..., fp16=False)``.
-    Returns [B, len(rows), L, c_z] per slab, fp32 holding fp16 values, or float64 (``exact``)."""
+    ``z`` may be fp16 or fp32.  With ``exact``, ``p`` comes from ``trimul_params(..., fp16=False)``
+    and the arithmetic is ``exact_dtype`` (float64 by default; float32 is 2^13 times finer than
+    the fp16 errors it measures, and much faster for L in the thousands).
+    Returns [B, len(rows), L, c_z] per slab, fp32 holding fp16 values, or ``exact_dtype``."""
     single = isinstance(rows, range)
     slabs = [rows] if single else list(rows)
     B, L = z.shape[0], z.shape[1]
@@ -296,15 +298,18 @@ def trimul_rows(p: dict, z: torch.Tensor, mask, outgoing: bool, rows, exact: boo
     b_all = torch.empty(B, c, L, L, dtype=store)
     for s in range(0, L, chunk):
         e = min(L, s + chunk)
-        b_all[:, :, s:e] = _gated_half(p, z[:, s:e], None if mask is None else mask[:, s:e], 1, exact).to(store)
-    dt = torch.float64 if exact else torch.float32
+        b_all[:, :, s:e] = _gated_half(p, z[:, s:e], None if mask is None else mask[:, s:e], 1, exact,
+                                       exact_dtype).to(store)
+    dt = exact_dtype if exact else torch.float32
     outs = []
     for sl in slabs:
         r0, r1 = sl[0], sl[-1] + 1
         if outgoing:
-            a_r = _gated_half(p, z[:, r0:r1], None if mask is None else mask[:, r0:r1], 0, exact)  # [B, c, R, L]
+            a_r = _gated_half(p, z[:, r0:r1], None if mask is None else mask[:, r0:r1], 0, exact,
+                              exact_dtype)  # [B, c, R, L]
         else:
-            a_r = _gated_half(p, z[:, :, r0:r1], None if mask is None else mask[:, :, r0:r1], 0, exact)
+            a_r = _gated_half(p, z[:, :, r0:r1], None if mask is None else mask[:, :, r0:r1], 0, exact,
+                              exact_dtype)
             a_r = a_r.transpose(2, 3)  # [B, c, R, L]: a[d, k, i] as rows i
         x = torch.empty(B, c, r1 - r0, L, dtype=dt)
         for d0 in range(0, c, 16):
