@@ -423,7 +423,11 @@ def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True) -> dict
     flops = 2 * (2 * cfg.c * L) * Lr * L  # the contraction's FLOPs per rank per step (both directions)
     hbm, tflops, peak_kind = _peaks()
     tensor_ms = flops / (tflops * 1e12) * 1e3
-    bound_ms = max(comm_ms, tensor_ms)
+    # K1 and K3 of both directions on this rank's Lr x L cells, at the HBM peak (algorithmic bytes)
+    costs = _kernel_costs(L, 1, False, cfg.c_z, cfg.c)
+    k13_ms = 2 * (costs["K1_project_gate"]["bytes"] + costs["K3_emit_residual"]["bytes"]) * (Lr / L) / (hbm * 1e9) * 1e3
+    # the exchange overlaps the contraction, not the position-wise kernels before and after it
+    bound_ms = k13_ms + max(comm_ms, tensor_ms)
     res = {"workload": cfg.name, "L": L, "B": 1, "c_z": cfg.c_z, "n_gpus": ws, "scaling": "strong",
            "value": cells / (ms_per_step * 1e-3), "unit": UNIT, "ms_per_step": round(ms_per_step, 4),
            "steps": steps,
@@ -434,8 +438,10 @@ def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True) -> dict
            "roofline": {"bound": "nvlink" if comm_ms > tensor_ms else "tensor",
                         "recv_bytes_per_rank_per_step": recv, "nvlink_gbs_per_direction": link_gbs,
                         "comm_floor_ms": round(comm_ms, 4), "contraction_floor_ms": round(tensor_ms, 4),
+                        "k1_k3_hbm_floor_ms": round(k13_ms, 4), "step_floor_ms": round(bound_ms, 4),
                         "frac": round(bound_ms / ms_per_step, 4),
-                        "note": "floor = max(received bytes / measured 770 GB/s peer copy, contraction FLOPs / "
+                        "note": "floor = K1 + K3 algorithmic bytes / measured HBM peak + max(received bytes / "
+                                "measured 770 GB/s peer copy, contraction FLOPs / "
                                 f"{tflops} TFLOP/s {peak_kind} peak); frac = floor / measured step"},
            "e2e": {"value": cells / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": zh.numel() * 2,
                    "d2h_bytes_per_step": outh.numel() * 2, "ms_per_step": round(e2e_ms, 4)},
@@ -457,6 +463,8 @@ def _c5_parity(cfg, trunk, z2, z1, rank, ws) -> dict | None:
     from esmfold2_mlx_b200.synthetic import pair_rows
     from oracle import trimul_oracle as orc
 
+    threads = torch.get_num_threads()
+    torch.set_num_threads(len(os.sched_getaffinity(0)))  # the other ranks wait at the barrier below
     z = pair_rows(cfg.L, cfg.c_z, cfg.seed, 0, cfg.L).half()
     rows = range(124, 128)
     tri = trunk.blocks[0].tri_mul_out
@@ -466,6 +474,7 @@ def _c5_parity(cfg, trunk, z2, z1, rank, ws) -> dict | None:
     res = orc.parity(exact, ref16, z1[:, rows.start:rows.stop].float().cpu())
     res.update({"rows": [rows.start, rows.stop], "direction": "out",
                 "exact": "float32 arithmetic (no fp16 rounding points)"})
+    torch.set_num_threads(threads)
     _barrier(ws)
     return res
 
