@@ -14,7 +14,8 @@
 // channels, N = 64 positions, K = 256 (signal rows into TMEM columns [0, 64) of a slot, gate
 // rows into [64, 128)).  CTA = 22 warps, one per SM, persistent:
 //   warp 0      TMA: this CTA's weight set once, then z tiles (2 stages of 32 KB, 128B swizzle)
-//   warp 1      TMEM (4 slots x 128 columns; tile t uses slot t mod 4) and the MMA thread
+//   warp 1      TMEM (4 slots x 128 columns; tile t uses slot t mod 4) and the MMA thread, whose
+//               operand descriptors are built once per stage and advanced by constants
 //   warps 2-5   LayerNorm in place: row = position, each row split over two warps (channel
 //               halves) that exchange their partial sums through shared memory; + the mask
 //   warps 6-21  epilogue: four groups of four warps (one per TMEM lane quadrant), group g drains
@@ -199,14 +200,14 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_w_kernel(const __gri
         if (!mbar_wait(&lnfull[s], ph, ctx, kSiteMmaLn)) break;
         if (!mbar_wait(&tempty[slot], sph ^ 1, ctx, kSiteMmaSlot)) break;
         tc_fence_after();
-        const uint32_t n_base = smem_u32(smem + OFF_A + s * A_BYTES);
+        const uint64_t n_desc = sdesc_sw128(smem_u32(smem + OFF_A + s * A_BYTES), 16, 1024);
         for (int h = 0; h < 2; ++h) {  // h = 0 signal rows, h = 1 gate rows
-          const uint32_t w_base = smem_u32(smem + OFF_W + h * WBLOCK_BYTES);
+          const uint64_t w_desc = sdesc_sw128(smem_u32(smem + OFF_W + h * WBLOCK_BYTES), 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < CZ / 16; ++kk) {
             const uint32_t ka = (kk >> 2), kb = (kk & 3) * 32;
-            umma_f16(tmem_base + slot * 128 + h * 64, sdesc_sw128(w_base + ka * WATOM_BYTES + kb, 16, 1024),
-                     sdesc_sw128(n_base + ka * ZATOM_BYTES + kb, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+            umma_f16(tmem_base + slot * 128 + h * 64, sdesc_add(w_desc, ka * WATOM_BYTES + kb),
+                     sdesc_add(n_desc, ka * ZATOM_BYTES + kb), IDESC, kk > 0 ? 1u : 0u);
           }
         }
         umma_commit(&tfull[slot]);
