@@ -14,10 +14,10 @@
 #include <string>
 
 #include "k1_project.cuh"
+#include "k3p_emit.cuh"
 #include "k1w_project.cuh"
 #include "k2_contract.cuh"
 #include "k3_emit.cuh"
-#include "k3w_emit.cuh"
 #include "k4_transition.cuh"
 #include "k5_disto.cuh"
 #include "k6_gemm.cuh"
@@ -259,6 +259,49 @@ cudaError_t launch_pdl(void (*kern)(P), int grid, int block, int smem, cudaStrea
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
+// A launch of clusters of two CTAs (CTA pairs), chained like launch_pdl.
+template <typename P>
+cudaError_t launch_pdl_pair(void (*kern)(P), int grid, int block, int smem, cudaStream_t stream, const P& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, p);
+}
+
+// How many CTA pairs of `kern` can be resident at once on the current device (cached per device
+// and kernel by the caller): pairs need two SMs of one GPC, so this can be below SMs / 2.
+template <typename P>
+int max_resident_pairs(void (*kern)(P), int block, int smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+    cudaGetLastError();  // clear the error: fall back to one pair per two SMs
+    return 0;
+  }
+  return n;
+}
+
 // A pair tensor [B, rows, cols, cz] with contiguous channels and arbitrary element strides
 // (z, or a transposed view of a received slab), plus the element strides of its mask.
 struct PairGeom {
@@ -411,7 +454,7 @@ int launch_k2(const void* a, const void* b, void* x, int Bc, int M, int N, int K
   return fail(TMU_ERR_UNSUPPORTED, "rows_per_part of a gathered operand must be a multiple of 128");
 }
 
-int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
+int launch_k3p(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
                float mix_eps, DeviceStatus* status, cudaStream_t stream);
 
 int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
@@ -419,7 +462,7 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   // the emit and gate biases come together (both present, or neither: the reference's form)
   if ((w->b_emit == nullptr) != (w->b_gate == nullptr))
     return fail(TMU_ERR_INVALID_ARGUMENT, "b_emit and b_gate must both be set or both be NULL");
-  if (cz == 256) return launch_k3w(x, z, z_out, w, B, rows, cols, mix_eps, status, stream);
+  if (cz == 256) return launch_k3p(x, z, z_out, w, B, rows, cols, mix_eps, status, stream);
   const bool hb = w->b_emit != nullptr;
   int ih = 1, jw = 128;
   choose_tile_k3(rows, cols, ih, jw);
@@ -548,41 +591,47 @@ int launch_k1w(const void* z, const void* mask, const tmu_trimul_weights* w, con
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch project_gate_w_kernel");
 }
 
-int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
+int g_pairs_k3p[kMaxDevices][2] = {{0}};
+
+// K3 at c_z = 256 on CTA pairs (k3p_emit.cuh): tiles of 64 positions, 2 x 32 or 1 x 64, whichever
+// pads less (the pair's CTAs take one row of 32 positions each).
+int launch_k3p(const void* x, const void* z, void* z_out, const tmu_trimul_weights* w, int B, int rows, int cols,
                float mix_eps, DeviceStatus* status, cudaStream_t stream) {
   const uintptr_t bytes = static_cast<uintptr_t>(B) * rows * cols * 256 * 2;
   const uintptr_t zi = reinterpret_cast<uintptr_t>(z), zo = reinterpret_cast<uintptr_t>(z_out);
   if (zi < zo + bytes && zo < zi + bytes)
     return fail(TMU_ERR_INVALID_ARGUMENT, "c_z = 256: z_out must not overlap z (two CTAs share each tile's z)");
   const bool hb = w->b_emit != nullptr;
-  int ih = 1, jw = 32;
-  choose_tile(rows, cols, ih, jw, k3w::TILE);
-  // 1 x 32 tiles: each channel's 32 positions are one 64-byte row, loaded 64B-swizzled and
-  // transposed by ldmatrix (a narrower box cannot take a swizzle without TMA padding its rows)
-  const bool xsw = jw == 32;
-  void (*kern)(k3w::Params) = hb ? (xsw ? k3w::emit_residual_w_kernel<true, true> : k3w::emit_residual_w_kernel<true, false>)
-                                 : (xsw ? k3w::emit_residual_w_kernel<false, true> : k3w::emit_residual_w_kernel<false, false>);
+  const long long area2 = static_cast<long long>((rows + 1) / 2) * 2 * ((cols + 31) / 32) * 32;
+  const long long area1 = static_cast<long long>(rows) * ((cols + 63) / 64) * 64;
+  const int ih = area2 <= area1 ? 2 : 1, jw = 64 / ih;
+  void (*kern)(k3p::Params) = hb ? k3p::emit_residual_pair_kernel<true> : k3p::emit_residual_pair_kernel<false>;
   Dev dev;
-  int st = current_device(dev, 1ull << ((xsw ? 42 : 20) + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern),
-                          k3w::SMEM_BYTES);
+  int st = current_device(dev, 1ull << (46 + (hb ? 1 : 0)), reinterpret_cast<const void*>(kern), k3p::SMEM_BYTES);
   if (st) return st;
   if (dev.sms < 2) return fail(TMU_ERR_UNSUPPORTED, "fewer than 2 SMs");
-  k3w::Params p;
+  int& pairs = g_pairs_k3p[dev.id][hb ? 1 : 0];
+  if (pairs == 0) {
+    pairs = max_resident_pairs(kern, k3p::kThreads, k3p::SMEM_BYTES);
+    if (pairs == 0) pairs = dev.sms / 2;
+  }
+  k3p::Params p;
   memset(&p, 0, sizeof(p));
   const uint64_t cp = row_pitch(cols);
   {
     const uint64_t dims[4] = {256, (uint64_t)cols, (uint64_t)rows, (uint64_t)B};
     const uint64_t str[3] = {512, 512ull * cols, 512ull * cols * rows};
-    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
-    if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
-    if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    const uint32_t boxp[4] = {64, 32, 1, 1};
+    if ((st = encode_map(&p.tm_z, z, 4, dims, str, boxp, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    const uint32_t boxt[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    if ((st = encode_map(&p.tm_r, z, 4, dims, str, boxt, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    if ((st = encode_map(&p.tm_zo, z_out, 4, dims, str, boxt, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
     const uint64_t dims[3] = {(uint64_t)cols, (uint64_t)rows, (uint64_t)B * 256};
     const uint64_t str[2] = {cp * 2, cp * 2 * rows};
-    const uint32_t box[3] = {(uint32_t)jw, (uint32_t)ih, 256};
-    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, xsw ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE)))
-      return st;
+    const uint32_t box[3] = {32, 1, 256};
+    if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
   }
   {
     const uint64_t dims[2] = {256, 256};
@@ -604,13 +653,13 @@ int launch_k3w(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
   p.jw = jw;
   p.tiles_i = (rows + ih - 1) / ih;
   p.tiles_j = (cols + jw - 1) / jw;
-  p.num_tiles = 2 * B * p.tiles_i * p.tiles_j;
+  p.num_tiles = B * p.tiles_i * p.tiles_j;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
-  const int grid = std::min(p.num_tiles, dev.sms & ~1);  // even: a CTA keeps one output half
-  cudaError_t e = launch_pdl(kern, grid, k3w::kThreads, k3w::SMEM_BYTES, stream, p);
+  const int grid = 2 * std::min(p.num_tiles, pairs);
+  cudaError_t e = launch_pdl_pair(kern, grid, k3p::kThreads, k3p::SMEM_BYTES, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
-  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_w_kernel");
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_pair_kernel");
 }
 
 template <int CZ>

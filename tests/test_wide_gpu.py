@@ -1,6 +1,6 @@
 """GPU parity at c_z = c = 256, the pair width of ESMFold2's released trunk (mlx_trunk.py:4).
 
-The wide kernels (K1W, K3W; K2 is width-agnostic) against the CPU oracle, with the same bounds
+The wide kernels (K1W, the CTA-pair K3P; K2 is width-agnostic) against the CPU oracle, with the same bounds
 as the c_z = 128 tests: kernel outputs within 2 fp16 ulps of the oracle's intermediates (a few %
 of elements may differ), whole updates with e_cuda <= 2 e_ref + 1e-3 against the exact float64
 update and within 4 ulps of the fp16 oracle.
