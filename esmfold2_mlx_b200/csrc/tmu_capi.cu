@@ -14,8 +14,8 @@
 #include <string>
 
 #include "k1_project.cuh"
+#include "k1p_project.cuh"
 #include "k3p_emit.cuh"
-#include "k1w_project.cuh"
 #include "k2_contract.cuh"
 #include "k3_emit.cuh"
 #include "k4_transition.cuh"
@@ -138,27 +138,6 @@ void choose_tile_k1(int rows, int cols, int& ih, int& jw) {
   long long best = -1;
   for (int w = 0; w < 5; ++w) {
     const int wi = widths[w], hi = 128 / wi;
-    const long long area = static_cast<long long>((rows + hi - 1) / hi) * hi * ((cols + wi - 1) / wi) * wi;
-    const long long cost = area * (dram ? weight[w] : 1);
-    if (best < 0 || cost < best) {
-      best = cost;
-      ih = hi;
-      jw = wi;
-    }
-  }
-}
-
-// K1W's tile (64 positions): the same effect, measured: 8 x 8 tiles cost 1.21x the 1 x 64 cost
-// per position at L = 1032 (c_z = 256).  Charged 1, 1.1, 1.25, 1.4 per position from the widest
-// shape (1 x 64) to the narrowest (8 x 8), from 512 x 512 positions up (as K1; L = 238: the
-// least padding 3 % faster).
-void choose_tile_k1w(int rows, int cols, int& ih, int& jw) {
-  static const int widths[4] = {64, 32, 16, 8};
-  static const int weight[4] = {20, 22, 25, 28};  // relative cost per position, x 20
-  const bool dram = static_cast<long long>(rows) * cols >= 512ll * 512;
-  long long best = -1;
-  for (int w = 0; w < 4; ++w) {
-    const int wi = widths[w], hi = 64 / wi;
     const long long area = static_cast<long long>((rows + hi - 1) / hi) * hi * ((cols + wi - 1) / wi) * wi;
     const long long cost = area * (dram ? weight[w] : 1);
     if (best < 0 || cost < best) {
@@ -315,12 +294,12 @@ PairGeom square_geom(int B, int L, int cz) {
   return PairGeom{B, L, L, 1LL * cz * L * L, 1LL * cz * L, cz, 1LL * L * L, L, 1, cz};
 }
 
-int launch_k1w(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
+int launch_k1p(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
                DeviceStatus* status, cudaStream_t stream, bool reset_status);
 
 int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
               DeviceStatus* status, cudaStream_t stream, bool reset_status = false) {
-  if (g.cz == 256) return launch_k1w(z, mask, w, g, a, b, status, stream, reset_status);
+  if (g.cz == 256) return launch_k1p(z, mask, w, g, a, b, status, stream, reset_status);
   const bool hb = w->b_proj != nullptr, hm = mask != nullptr;
   void (*kern)(k1::Params) = hb ? (hm ? k1::project_gate_kernel<true, true> : k1::project_gate_kernel<true, false>)
                                 : (hm ? k1::project_gate_kernel<false, true> : k1::project_gate_kernel<false, false>);
@@ -530,25 +509,36 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_kernel");
 }
 
-int launch_k1w(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
+int g_pairs_k1p[kMaxDevices][4] = {{0}};
+
+// K1 at c_z = 256 on CTA pairs (k1p_project.cuh): tiles of 128 positions, shape chosen as K1's
+// (the wide tiles from 512 x 512 positions up, the least padding below); pairs alternate between
+// the operands a and b, so the pair count is even.
+int launch_k1p(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
                DeviceStatus* status, cudaStream_t stream, bool reset_status) {
   const bool hb = w->b_proj != nullptr, hm = mask != nullptr;
-  void (*kern)(k1w::Params) = hb ? (hm ? k1w::project_gate_w_kernel<true, true> : k1w::project_gate_w_kernel<true, false>)
-                                 : (hm ? k1w::project_gate_w_kernel<false, true> : k1w::project_gate_w_kernel<false, false>);
+  void (*kern)(k1p::Params) = hb ? (hm ? k1p::project_gate_pair_kernel<true, true> : k1p::project_gate_pair_kernel<true, false>)
+                                 : (hm ? k1p::project_gate_pair_kernel<false, true> : k1p::project_gate_pair_kernel<false, false>);
   Dev dev;
-  int st = current_device(dev, 1u << (16 + (hb ? 2 : 0) + (hm ? 1 : 0)), reinterpret_cast<const void*>(kern),
-                          k1w::SMEM_BYTES);
+  int st = current_device(dev, 1ull << (48 + (hb ? 2 : 0) + (hm ? 1 : 0)), reinterpret_cast<const void*>(kern),
+                          k1p::SMEM_BYTES);
   if (st) return st;
   if (dev.sms < 4) return fail(TMU_ERR_UNSUPPORTED, "fewer than 4 SMs");
-  k1w::Params p;
+  int& pairs = g_pairs_k1p[dev.id][(hb ? 2 : 0) + (hm ? 1 : 0)];
+  if (pairs == 0) {
+    pairs = max_resident_pairs(kern, k1p::kThreads, k1p::SMEM_BYTES);
+    if (pairs == 0) pairs = dev.sms / 2;
+  }
+  k1p::Params p;
   memset(&p, 0, sizeof(p));
-  int ih = 1, jw = 64;
-  choose_tile_k1w(g.rows, g.cols, ih, jw);
+  int ih = 1, jw = 128;
+  choose_tile_k1(g.rows, g.cols, ih, jw);
   const uint64_t cp = row_pitch(g.cols);
   {
     const uint64_t dims[4] = {256, (uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B};
     const uint64_t str[3] = {2ull * g.sc, 2ull * g.sr, 2ull * g.sb};
-    const uint32_t box[4] = {64, (uint32_t)jw, (uint32_t)ih, 1};
+    // a CTA's piece: rows [ih/2 r, ..) of the tile, or (ih = 1) columns [64 r, 64 r + 64)
+    const uint32_t box[4] = {64, ih >= 2 ? (uint32_t)jw : 64u, ih >= 2 ? (uint32_t)(ih / 2) : 1u, 1};
     if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
@@ -560,8 +550,8 @@ int launch_k1w(const void* z, const void* mask, const tmu_trimul_weights* w, con
   {
     const uint64_t dims[3] = {(uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B * 256};
     const uint64_t str[2] = {cp * 2, cp * 2 * g.rows};
-    const uint32_t w32 = jw < k1w::SPOS ? jw : k1w::SPOS;
-    const uint32_t box[3] = {w32, k1w::SPOS / w32, 32};
+    const uint32_t w32 = jw < k1p::SPOS ? jw : k1p::SPOS;
+    const uint32_t box[3] = {w32, k1p::SPOS / w32, 32};
     const CUtensorMapSwizzle sw = w32 == 32 ? CU_TENSOR_MAP_SWIZZLE_64B
                                             : w32 == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
     if ((st = encode_map(&p.tm_a, a, 3, dims, str, box, sw))) return st;
@@ -581,14 +571,14 @@ int launch_k1w(const void* z, const void* mask, const tmu_trimul_weights* w, con
   p.log2_jw = 31 - __builtin_clz(static_cast<unsigned>(jw));
   p.tiles_i = (g.rows + ih - 1) / ih;
   p.tiles_j = (g.cols + jw - 1) / jw;
-  p.num_tiles = 4 * g.B * p.tiles_i * p.tiles_j;
+  p.num_tiles = 2 * g.B * p.tiles_i * p.tiles_j;
   p.reset_status = reset_status ? 1 : 0;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
-  const int grid = std::min(p.num_tiles, dev.sms & ~3);  // a multiple of 4: a CTA keeps one weight set
-  cudaError_t e = launch_pdl(kern, grid, k1w::kThreads, k1w::SMEM_BYTES, stream, p);
+  const int npairs = std::min(p.num_tiles, pairs & ~1);  // even: a pair keeps one operand
+  cudaError_t e = launch_pdl_pair(kern, 2 * npairs, k1p::kThreads, k1p::SMEM_BYTES, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
-  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch project_gate_w_kernel");
+  return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch project_gate_pair_kernel");
 }
 
 int g_pairs_k3p[kMaxDevices][2] = {{0}};

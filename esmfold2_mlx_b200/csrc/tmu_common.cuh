@@ -356,6 +356,21 @@ __device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, con
   }
 }
 
+// group_wait whose first barrier the other CTA of the pair completes (cluster-scope acquire).
+__device__ __forceinline__ bool group_wait_cl(uint64_t* bar, uint32_t parity, uint64_t* bar2, uint32_t parity2,
+                                              const WaitCtx& ctx, unsigned int site, bool leader, uint32_t bar_id,
+                                              uint32_t nthreads, volatile int* flags, uint32_t& count) {
+  volatile int* flag = flags + (count & 1);
+  ++count;
+  if (leader) {
+    bool ok = mbar_wait_cl(bar, parity, ctx, site);
+    if (ok && bar2 != nullptr) ok = mbar_wait(bar2, parity2, ctx, site);
+    *flag = ok ? 1 : 0;
+  }
+  named_bar_sync(bar_id, nthreads);
+  return *flag != 0;
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {  // same warp in both CTAs
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
                "r"(ncols)
