@@ -1,22 +1,31 @@
-// K1P: K1 for c_z = c = 256 (mlx_trunk.py:4) on CTA pairs.  Same arithmetic as K1
-// (mlx_trunk.py:72-76,81-83; mlx_trunk_kernels.py:47-80,214-216):
+// K1P: K1 on CTA pairs, for c_z = c = 128 and 256.  Same arithmetic as K1 (mlx_trunk.py:72-76,
+// 81-83; mlx_trunk_kernels.py:47-80,214-216):
 //   n = fp16(LN(z)), proj = fp16(n @ w_in [+ b]), a/b = fp16(signal * sigmoid(gate) * mask).
 //
-// The packed projection weights are 4c x c_z fp16 = 512 KB.  A cluster of two CTAs on two SMs
-// computes one operand (a or b: its 256 signal rows and 256 gate rows) for a tile of 128
-// positions through MMAs that span both SMs (tcgen05 .cta_group::2, M = 256 output channels,
-// N = 128 positions, K = 256): CTA r keeps the signal and gate rows of channels
-// [128 r, 128 r + 128) resident (128 KB, the A operand's half), normalises ITS 64 of the tile's
-// 128 positions (the B operand's half), and receives in its TMEM the projections of its 128
-// channels for all 128 positions.  Pairs alternate between the operands (pair p computes a for
-// even p, b for odd p; the pair count is even), so every LayerNorm is computed twice (once per
-// operand) and one MMA instruction covers 256 x 128 outputs.
+// A cluster of two CTAs on two SMs projects a tile of 128 positions through MMAs that span both
+// SMs (tcgen05 .cta_group::2, M = 256 output rows, N = 128 positions, K = c_z).  CTA r holds the
+// A operand's rows [128 r, 128 r + 128) of two MMA chains (signal, gate) resident, normalises ITS
+// 64 of the tile's 128 positions (the B operand's half), and receives in its TMEM the signal and
+// gate projections of its 128 output channels for all 128 positions, so an epilogue thread has a
+// channel's signal and gate side by side:
+//   c_z = 256: the packed weights are 4c x c_z fp16 = 512 KB, so a pair computes one operand (a
+//              or b: signal chain = its 256 signal rows, gate chain = its 256 gate rows; CTA r
+//              takes channels [128 r, 128 r + 128)).  Pairs alternate between the operands (the
+//              pair count is even): every LayerNorm is computed twice, once per operand.
+//   c_z = 128: a pair computes both operands (signal chain = [signal a; signal b], gate chain
+//              = [gate a; gate b]: CTA 0 produces a, CTA 1 produces b) from 64 KB of weights per
+//              CTA, which leaves room for four z stages; every LayerNorm is computed once.
+// One MMA instruction covers 256 x 128 outputs (the single-CTA K1: 128 x 128), and the two TMEM
+// slots double-buffer the accumulators (the single-CTA K1 fills all of TMEM with one tile).
+// The library launches the c_z = 256 form.  The c_z = 128 form passes the same parity tests but
+// measured slower than the single-CTA K1 (L = 1024: 309 vs 219 us; L = 238: 26.0 vs 24.2 us), so
+// K1 keeps c_z = 128.
 //
 // Tile = 128 positions as an ih x jw block (ih * jw = 128); CTA r's piece is rows
 // [ih/2 r, ih/2 r + ih/2) of it (ih >= 2) or columns [64 r, 64 r + 64) (ih = 1), so the
 // accumulator's columns are the tile's positions in row-major order.  Per CTA, 26 warps:
-//   warp 0      TMA: the weight halves once; per tile its piece of z (64 positions x 256
-//               channels, [4 atoms][64 rows][128 B], 128B swizzle), 2 stages
+//   warp 0      TMA: the weight halves once; per tile its piece of z (64 positions x c_z
+//               channels, [c_z/64 atoms][64 rows][128 B], 128B swizzle), NSTAGE stages
 //   warp 1      TMEM (2 slots x 256 columns: signal [0, 128), gate [128, 256), allocated for the
 //               pair) and, in the even CTA, the MMA thread
 //   warps 2-9   LayerNorm of the piece in place: a row on four adjacent lanes, lane k holding the
@@ -35,43 +44,46 @@
 namespace tmu {
 namespace k1p {
 
-constexpr int CZ = 256;
-constexpr int CC = 256;
 constexpr int TILE = 128;                        // positions per pair tile
 constexpr int PT = 64;                           // positions per CTA
-constexpr int KATOMS = CZ / 64;                  // 64-channel swizzle atoms along K
 constexpr int ZATOM_BYTES = PT * 128;            // 64 rows x 128 B
 constexpr int WATOM_BYTES = 128 * 128;           // 128 weight rows x 128 B
-constexpr int WBLOCK_BYTES = 128 * CZ * 2;       // 128 weight rows x 256 channels
-constexpr int PIECE_BYTES = PT * CZ * 2;         // 64 positions x 256 channels
 constexpr int POS = 16;                          // positions per TMEM load
 constexpr int SPOS = 32;                         // positions per TMA store
 constexpr int WSTG_BYTES = 32 * SPOS * 2;
 constexpr int NEPI = 16;
 constexpr int NMASK = 3;                         // mask ring (a tile's mask outlives its z stage)
-constexpr int OFF_W = 0;                         // [signal rows | gate rows] of the CTA's channels
-constexpr int OFF_A = OFF_W + 2 * WBLOCK_BYTES;  // 2 stages: the z piece, then n in place
-constexpr int OFF_STG = OFF_A + 2 * PIECE_BYTES;
-constexpr int OFF_PAR = OFF_STG + NEPI * WSTG_BYTES;  // fp16 LN gamma[256], beta[256]
-constexpr int OFF_MASK = OFF_PAR + 2 * CZ * 2;        // fp16 mask [NMASK][TILE]
-constexpr int OFF_BAR = OFF_MASK + NMASK * TILE * 2;
-constexpr int SMEM_BYTES = OFF_BAR + 256;
 constexpr int kThreads = 832;
 constexpr int EPI_WARP0 = 10;
 constexpr int TMEM_COLS = 512;
-static_assert(SMEM_BYTES <= 232448, "K1P shared memory exceeds the per-block limit");
+
+template <int CZ>
+struct Cfg {
+  static constexpr int KATOMS = CZ / 64;                  // 64-channel swizzle atoms along K
+  static constexpr int WBLOCK_BYTES = 128 * CZ * 2;       // 128 weight rows x c_z channels
+  static constexpr int PIECE_BYTES = PT * CZ * 2;         // 64 positions x c_z channels
+  static constexpr int NSTAGE = CZ == 256 ? 2 : 4;        // z stages beside the resident weights
+  static constexpr int OFF_W = 0;                         // [signal rows | gate rows]
+  static constexpr int OFF_A = OFF_W + 2 * WBLOCK_BYTES;  // NSTAGE stages: the z piece, then n in place
+  static constexpr int OFF_STG = OFF_A + NSTAGE * PIECE_BYTES;
+  static constexpr int OFF_PAR = OFF_STG + NEPI * WSTG_BYTES;  // fp16 LN gamma[c_z], beta[c_z]
+  static constexpr int OFF_MASK = OFF_PAR + 2 * CZ * 2;        // fp16 mask [NMASK][TILE]
+  static constexpr int OFF_BAR = OFF_MASK + NMASK * TILE * 2;
+  static constexpr int SMEM_BYTES = OFF_BAR + 256;
+  static_assert(SMEM_BYTES <= 232448, "K1P shared memory exceeds the per-block limit");
+};
 
 struct Params {
-  CUtensorMap tm_z;  // z [B, rows, cols, 256] (any element strides): box {64, pjw, pih, 1}, 128B swizzle
-  CUtensorMap tm_w;  // packed proj weights [1024, 256]: box {64, 128}, 128B swizzle
-  CUtensorMap tm_a;  // a [B*256, rows, pitch]: box {min(jw,32), 32/min(jw,32), 32} (store)
+  CUtensorMap tm_z;  // z [B, rows, cols, c_z] (any element strides): box {64, piece cols, piece rows, 1}, 128B swizzle
+  CUtensorMap tm_w;  // packed proj weights [4 c, c_z]: box {64, 128}, 128B swizzle
+  CUtensorMap tm_a;  // a [B*c, rows, pitch]: box {min(jw,32), 32/min(jw,32), 32} (store)
   CUtensorMap tm_b;
   const __half* ln_w;
   const __half* ln_b;
   const float* bias;   // [4c] in packed-row order, or null
   const __half* mask;  // [B, rows, cols] with element strides mask_s*, or null
   long long mask_sb, mask_si, mask_sj;
-  int rows, cols, ih, jw, log2_jw, tiles_i, tiles_j, num_tiles;  // num_tiles = 2 x position tiles
+  int rows, cols, ih, jw, log2_jw, tiles_i, tiles_j, num_tiles;  // c_z = 256: num_tiles = 2 x position tiles
   int reset_status;
   DeviceStatus* status;
   unsigned long long timeout_ns;
@@ -82,8 +94,9 @@ enum Site : unsigned int {
   kSiteEpilogue = 0x136
 };
 
+template <int CZ>
 __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, int& i0, int& j0) {
-  const int pt = tile >> 1;
+  const int pt = CZ == 256 ? tile >> 1 : tile;  // c_z = 256: tile = (position tile, operand)
   const int per_b = p.tiles_i * p.tiles_j;
   bb = pt / per_b;
   const int r = pt - bb * per_b;
@@ -91,8 +104,13 @@ __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, 
   j0 = (r % p.tiles_j) * p.jw;
 }
 
-template <bool HAS_BIAS, bool HAS_MASK>
+template <int CZ, bool HAS_BIAS, bool HAS_MASK>
 __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __grid_constant__ Params p) {
+  using C = Cfg<CZ>;
+  constexpr int CC = CZ;  // c == c_z
+  constexpr int KATOMS = C::KATOMS, NSTAGE = C::NSTAGE, PIECE_BYTES = C::PIECE_BYTES, WBLOCK_BYTES = C::WBLOCK_BYTES;
+  constexpr int OFF_W = C::OFF_W, OFF_A = C::OFF_A, OFF_STG = C::OFF_STG, OFF_PAR = C::OFF_PAR, OFF_MASK = C::OFF_MASK,
+                OFF_BAR = C::OFF_BAR;
   const bool trace_on = trace_enabled(p.status);
   constexpr uint32_t IDESC = idesc_f16_f32(256, TILE, false, false);
   extern __shared__ uint8_t smem[];
@@ -105,35 +123,41 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t& w_bar = bars[0];
   uint64_t& wpair = bars[1];     // even CTA: both weight halves resident (2 arrivals)
-  uint64_t* zfull = bars + 2;
-  uint64_t* zempty = bars + 4;   // the paired MMAs have read n (multicast commit)
-  uint64_t* lnfull = bars + 6;   // even CTA: both CTAs' LayerNorm warps (16 arrivals)
-  uint64_t* tfull = bars + 8;    // the accumulator slot is complete (multicast commit)
-  uint64_t* tempty = bars + 10;  // even CTA: both CTAs' epilogue warps have read it (32 arrivals)
-  uint64_t* mfull = bars + 12;   // [NMASK]: the LayerNorm warps wrote the tile's mask
-  uint64_t* mempty = bars + 15;  // [NMASK]: every epilogue warp is done with it
-  uint64_t& drain_bar = bars[18];
-  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 19);
-  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 19) + 4);
-  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 20);  // [5 groups][2] group_wait verdicts
-  __half* par = reinterpret_cast<__half*>(smem + OFF_PAR);     // [gamma 256 | beta 256]
+  uint64_t* zfull = bars + 2;    // [NSTAGE]
+  uint64_t* zempty = bars + 6;   // [NSTAGE]: the paired MMAs have read n (multicast commit)
+  uint64_t* lnfull = bars + 10;  // [NSTAGE], even CTA: both CTAs' LayerNorm warps (16 arrivals)
+  uint64_t* tfull = bars + 14;   // [2 slots]: the accumulator slot is complete (multicast commit)
+  uint64_t* tempty = bars + 16;  // [2 slots], even CTA: both CTAs' epilogue warps have read it (32 arrivals)
+  uint64_t* mfull = bars + 18;   // [NMASK]: the LayerNorm warps wrote the tile's mask
+  uint64_t* mempty = bars + 21;  // [NMASK]: every epilogue warp is done with it
+  uint64_t& drain_bar = bars[24];
+  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 25);
+  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 25) + 4);
+  volatile int* gflags = reinterpret_cast<volatile int*>(bars + 26);  // [5 groups][2] group_wait verdicts
+  __half* par = reinterpret_cast<__half*>(smem + OFF_PAR);     // [gamma c_z | beta c_z]
   __half* maskh = reinterpret_cast<__half*>(smem + OFF_MASK);  // [NMASK][128]
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const WaitCtx ctx{p.status, &abort_sh, p.timeout_ns};
   const uint32_t rank = cluster_ctarank();  // 0: the even CTA (issues the MMAs), 1: its pair
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int xsel = pair & 1;                // operand a (0) or b (1): constant, npairs is even
+  // the operand this CTA's output channels belong to (c_z = 256: the pair's, constant because the
+  // pair count is even; c_z = 128: the CTA's) and the packed weight row of its first signal row
+  const int xsel = CZ == 256 ? (pair & 1) : static_cast<int>(rank);
+  const int sig_row = CZ == 256 ? 2 * xsel * CC + static_cast<int>(rank) * 128 : 2 * xsel * CC;
+  const int ch0 = CZ == 256 ? static_cast<int>(rank) * 128 : 0;  // first output channel of the operand
   const int pih = p.ih >= 2 ? p.ih / 2 : 1;  // this CTA's piece: rows of it (ih >= 2) or one row of 64
 
   if (threadIdx.x == 0) {
     abort_sh = 0;
     mbar_init(&w_bar, 1);
     mbar_init(&wpair, 2);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NSTAGE; ++s) {
       mbar_init(&zfull[s], 1);
       mbar_init(&zempty[s], 1);
       mbar_init(&lnfull[s], 16);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull[s], 1);
       mbar_init(&tempty[s], 2 * NEPI);
     }
@@ -162,8 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
   const uint32_t tmem_base = tmem_base_sh;
   if (warp == 0 && lane == 0) {  // weights are never written by this library: load before the wait
     mbar_arrive_expect_tx(&w_bar, 2 * WBLOCK_BYTES);
-    for (int h = 0; h < 2; ++h) {  // h = 0: signal rows, 1: gate rows of operand xsel, channels [128 r, +128)
-      const int row0 = (2 * xsel + h) * CC + static_cast<int>(rank) * 128;
+    for (int h = 0; h < 2; ++h) {  // h = 0: this CTA's 128 signal rows, 1: its 128 gate rows
+      const int row0 = sig_row + h * CC;
       for (int a = 0; a < KATOMS; ++a)
         tma_load_2d(smem + OFF_W + h * WBLOCK_BYTES + a * WATOM_BYTES, &p.tm_w, &w_bar, a * 64, row0);
     }
@@ -186,10 +210,10 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
       uint32_t it = 0;
       for (int tile = pair; tile < p.num_tiles; tile += npairs, ++it) {
         int bb, i0, j0;
-        decode_tile(p, tile, bb, i0, j0);
+        decode_tile<CZ>(p, tile, bb, i0, j0);
         const int pi = i0 + (p.ih >= 2 ? pih * static_cast<int>(rank) : 0);
         const int pj = j0 + (p.ih >= 2 ? 0 : PT * static_cast<int>(rank));
-        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        const uint32_t s = it % NSTAGE, ph = (it / NSTAGE) & 1;
         if (!mbar_wait(&zempty[s], ph ^ 1, ctx, kSiteProducer)) break;
         mbar_arrive_expect_tx(&zfull[s], PIECE_BYTES);
         for (int a = 0; a < KATOMS; ++a)
@@ -197,8 +221,8 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
       }
       if (abort_sh) {
         mbar_drain(&w_bar, 0, 200000000ull);
-        for (uint32_t s = 0; s < 2; ++s) {
-          const uint32_t n_armed = it > s ? (it - s + 1) / 2 : 0;
+        for (uint32_t s = 0; s < NSTAGE; ++s) {
+          const uint32_t n_armed = it > s ? (it - s + NSTAGE - 1) / NSTAGE : 0;
           if (n_armed) mbar_drain(&zfull[s], (n_armed - 1) & 1, 200000000ull);
         }
       }
@@ -211,12 +235,13 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
       const uint64_t wsd = sdesc_sw128(smem_u32(smem + OFF_W), 16, 1024);
       const uint64_t wgd = sdesc_sw128(smem_u32(smem + OFF_W + WBLOCK_BYTES), 16, 1024);
       for (int tile = pair; ok && tile < p.num_tiles; tile += npairs, ++it) {
-        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        const uint32_t s = it % NSTAGE, ph = (it / NSTAGE) & 1;
+        const uint32_t slot = it & 1, sph = (it >> 1) & 1;
         if (!mbar_wait_cl(&lnfull[s], ph, ctx, kSiteMmaLn)) break;
-        if (!mbar_wait_cl(&tempty[s], ph ^ 1, ctx, kSiteMmaSlot)) break;
+        if (!mbar_wait_cl(&tempty[slot], sph ^ 1, ctx, kSiteMmaSlot)) break;
         tc_fence_after();
         const uint64_t nd = sdesc_sw128(smem_u32(smem + OFF_A + s * PIECE_BYTES), 16, 1024);
-        const uint32_t d = tmem_base + s * 256;
+        const uint32_t d = tmem_base + slot * 256;
 #pragma unroll
         for (int kk = 0; kk < CZ / 16; ++kk) {
           const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
@@ -229,8 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
           umma_f16_pair(d + TILE, sdesc_add(wgd, ka * WATOM_BYTES + kb), sdesc_add(nd, ka * ZATOM_BYTES + kb), IDESC,
                         kk > 0 ? 1u : 0u);
         }
-        umma_commit_pair(&zempty[s], 0x3);  // both CTAs' n pieces have been read
-        umma_commit_pair(&tfull[s], 0x3);   // both CTAs' accumulators are complete
+        umma_commit_pair(&zempty[s], 0x3);    // both CTAs' n pieces have been read
+        umma_commit_pair(&tfull[slot], 0x3);  // both CTAs' accumulators are complete
       }
       umma_commit_pair(&drain_bar, 0x1);
       mbar_drain(&drain_bar, 0, 200000000ull);
@@ -241,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
     const int row = t >> 2, qtr = t & 3;  // lane qtr of the row: its chunks qtr, qtr + 4 of every atom
     uint32_t it = 0, gcount = 0;
     for (int tile = pair; tile < p.num_tiles; tile += npairs, ++it) {
-      const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      const uint32_t s = it % NSTAGE, ph = (it / NSTAGE) & 1;
       const uint32_t k = it % NMASK, mph = (it / NMASK) & 1;
       // one thread waits for the piece (and the mask slot), the other LayerNorm warps park on barrier 1
       if (!group_wait(&zfull[s], ph, HAS_MASK ? &mempty[k] : nullptr, mph ^ 1, ctx, kSiteLn, t == 0, 1, 256,
@@ -250,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
       if (HAS_MASK) {
         if (t < TILE) {  // the tile's 128 positions, in the accumulator's (row-major) order
           int bb, i0, j0;
-          decode_tile(p, tile, bb, i0, j0);
+          decode_tile<CZ>(p, tile, bb, i0, j0);
           const int gi = i0 + (t >> p.log2_jw), gj = j0 + (t & (p.jw - 1));
           __half m = __float2half(0.0f);
           if (gi < p.rows && gj < p.cols) m = p.mask[bb * p.mask_sb + gi * p.mask_si + gj * p.mask_sj];
@@ -264,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
       // row starts with the other half of its chunks, so the two rows that share a shared-memory
       // phase (8 lanes) read 8 different 16-byte bank groups.
       const int odd = row & 1;
-      uint32_t u[32];
+      uint32_t u[8 * KATOMS];
 #pragma unroll
       for (int a = 0; a < KATOMS; ++a)
 #pragma unroll
@@ -282,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
       const float kshift = __shfl_sync(0xffffffffu, __low2float(*reinterpret_cast<const __half2*>(&c0)), lane & ~3);
       float2 s1 = make_float2(0.f, 0.f), s2 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
+      for (int e = 0; e < 8 * KATOMS; ++e) {
         unsigned short lo, hi;
         split_half2(u[e], lo, hi);
         const float2 dd = make_float2(add_f16_f32(lo, -kshift), add_f16_f32(hi, -kshift));
@@ -328,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
     const int grp = (warp - EPI_WARP0) >> 2;  // positions [32 grp, 32 grp + 32) of the tile
     const int q = warp & 3;                   // TMEM lane quadrant = channels [32q, 32q+32) of the CTA's half
     const int chl = q * 32 + lane;
-    const int ch = static_cast<int>(rank) * 128 + chl;  // channel of the operand
+    const int ch = ch0 + chl;  // channel of the operand
     uint8_t* stg = smem + OFF_STG + (warp - EPI_WARP0) * WSTG_BYTES;
     // byte offsets in the staging block of this thread's two 16-byte chunks c of compute step
     // st (positions 16 st + 8 c ..), matching the store box and its swizzle (as in K1)
@@ -348,9 +373,9 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
         }
       }
     float bs = 0.0f, bgt = 0.0f;
-    if (HAS_BIAS) {
-      bs = __ldg(p.bias + (2 * xsel) * CC + ch);
-      bgt = __ldg(p.bias + (2 * xsel + 1) * CC + ch);
+    if (HAS_BIAS) {  // packed order: this CTA's signal rows start at sig_row, its gate rows c later
+      bs = __ldg(p.bias + sig_row + chl);
+      bgt = __ldg(p.bias + sig_row + CC + chl);
     }
     const float2 bs2 = make_float2(bs, bs), bg2 = make_float2(bgt, bgt);
     const CUtensorMap* tm = xsel == 0 ? &p.tm_a : &p.tm_b;
@@ -358,15 +383,15 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
     const bool leader = ((warp - EPI_WARP0) & 3) == 0 && lane == 0;
     for (int tile = pair; tile < p.num_tiles; tile += npairs, ++it) {
       int bb, i0, j0;
-      decode_tile(p, tile, bb, i0, j0);
-      const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      decode_tile<CZ>(p, tile, bb, i0, j0);
+      const uint32_t slot = it & 1, sph = (it >> 1) & 1;
       const uint32_t k = it % NMASK, mph = (it / NMASK) & 1;
       // one thread of the group waits, the other warps park on barrier 2 + grp
-      if (!group_wait_cl(&tfull[s], ph, HAS_MASK ? &mfull[k] : nullptr, mph, ctx, kSiteEpilogue, leader, 2 + grp, 128,
-                         gflags + 2 * grp, gcount))
+      if (!group_wait_cl(&tfull[slot], sph, HAS_MASK ? &mfull[k] : nullptr, mph, ctx, kSiteEpilogue, leader, 2 + grp,
+                         128, gflags + 2 * grp, gcount))
         break;
       tc_fence_after();
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + s * 256 + 32 * grp;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + slot * 256 + 32 * grp;
       const __half* mrow = maskh + k * TILE + 32 * grp;
 #pragma unroll 1
       for (int pb = 0; pb < SPOS; pb += POS) {
@@ -377,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
         if (pb == SPOS - POS) {  // this group's columns of the slot have been read
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[s], 0));
+          if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[slot], 0));
         }
         uint32_t o[8];
 #pragma unroll

@@ -294,12 +294,13 @@ PairGeom square_geom(int B, int L, int cz) {
   return PairGeom{B, L, L, 1LL * cz * L * L, 1LL * cz * L, cz, 1LL * L * L, L, 1, cz};
 }
 
+template <int CZ>
 int launch_k1p(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
                DeviceStatus* status, cudaStream_t stream, bool reset_status);
 
 int launch_k1(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
               DeviceStatus* status, cudaStream_t stream, bool reset_status = false) {
-  if (g.cz == 256) return launch_k1p(z, mask, w, g, a, b, status, stream, reset_status);
+  if (g.cz == 256) return launch_k1p<256>(z, mask, w, g, a, b, status, stream, reset_status);
   const bool hb = w->b_proj != nullptr, hm = mask != nullptr;
   void (*kern)(k1::Params) = hb ? (hm ? k1::project_gate_kernel<true, true> : k1::project_gate_kernel<true, false>)
                                 : (hm ? k1::project_gate_kernel<false, true> : k1::project_gate_kernel<false, false>);
@@ -509,24 +510,27 @@ int launch_k3(const void* x, const void* z, void* z_out, const tmu_trimul_weight
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch emit_residual_kernel");
 }
 
-int g_pairs_k1p[kMaxDevices][4] = {{0}};
+int g_pairs_k1p[kMaxDevices][8] = {{0}};
 
-// K1 at c_z = 256 on CTA pairs (k1p_project.cuh): tiles of 128 positions, shape chosen as K1's
-// (the wide tiles from 512 x 512 positions up, the least padding below); pairs alternate between
-// the operands a and b, so the pair count is even.
+// K1 on CTA pairs (k1p_project.cuh), c_z = 128 or 256: tiles of 128 positions, shape chosen as
+// K1's (the wide tiles from 512 x 512 positions up, the least padding below).  At c_z = 256 the
+// pairs alternate between the operands a and b, so the pair count is even.
+template <int CZ>
 int launch_k1p(const void* z, const void* mask, const tmu_trimul_weights* w, const PairGeom& g, void* a, void* b,
                DeviceStatus* status, cudaStream_t stream, bool reset_status) {
+  using C = k1p::Cfg<CZ>;
   const bool hb = w->b_proj != nullptr, hm = mask != nullptr;
-  void (*kern)(k1p::Params) = hb ? (hm ? k1p::project_gate_pair_kernel<true, true> : k1p::project_gate_pair_kernel<true, false>)
-                                 : (hm ? k1p::project_gate_pair_kernel<false, true> : k1p::project_gate_pair_kernel<false, false>);
+  void (*kern)(k1p::Params) =
+      hb ? (hm ? k1p::project_gate_pair_kernel<CZ, true, true> : k1p::project_gate_pair_kernel<CZ, true, false>)
+         : (hm ? k1p::project_gate_pair_kernel<CZ, false, true> : k1p::project_gate_pair_kernel<CZ, false, false>);
+  const int variant = (CZ == 256 ? 4 : 0) + (hb ? 2 : 0) + (hm ? 1 : 0);
   Dev dev;
-  int st = current_device(dev, 1ull << (48 + (hb ? 2 : 0) + (hm ? 1 : 0)), reinterpret_cast<const void*>(kern),
-                          k1p::SMEM_BYTES);
+  int st = current_device(dev, 1ull << (48 + variant), reinterpret_cast<const void*>(kern), C::SMEM_BYTES);
   if (st) return st;
   if (dev.sms < 4) return fail(TMU_ERR_UNSUPPORTED, "fewer than 4 SMs");
-  int& pairs = g_pairs_k1p[dev.id][(hb ? 2 : 0) + (hm ? 1 : 0)];
+  int& pairs = g_pairs_k1p[dev.id][variant];
   if (pairs == 0) {
-    pairs = max_resident_pairs(kern, k1p::kThreads, k1p::SMEM_BYTES);
+    pairs = max_resident_pairs(kern, k1p::kThreads, C::SMEM_BYTES);
     if (pairs == 0) pairs = dev.sms / 2;
   }
   k1p::Params p;
@@ -535,20 +539,20 @@ int launch_k1p(const void* z, const void* mask, const tmu_trimul_weights* w, con
   choose_tile_k1(g.rows, g.cols, ih, jw);
   const uint64_t cp = row_pitch(g.cols);
   {
-    const uint64_t dims[4] = {256, (uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B};
+    const uint64_t dims[4] = {(uint64_t)CZ, (uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B};
     const uint64_t str[3] = {2ull * g.sc, 2ull * g.sr, 2ull * g.sb};
     // a CTA's piece: rows [ih/2 r, ..) of the tile, or (ih = 1) columns [64 r, 64 r + 64)
     const uint32_t box[4] = {64, ih >= 2 ? (uint32_t)jw : 64u, ih >= 2 ? (uint32_t)(ih / 2) : 1u, 1};
     if ((st = encode_map(&p.tm_z, z, 4, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
-    const uint64_t dims[2] = {256, 1024};
-    const uint64_t str[1] = {512};
+    const uint64_t dims[2] = {(uint64_t)CZ, 4ull * CZ};
+    const uint64_t str[1] = {2ull * CZ};
     const uint32_t box[2] = {64, 128};
     if ((st = encode_map(&p.tm_w, w->w_proj, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
   }
   {
-    const uint64_t dims[3] = {(uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B * 256};
+    const uint64_t dims[3] = {(uint64_t)g.cols, (uint64_t)g.rows, (uint64_t)g.B * CZ};
     const uint64_t str[2] = {cp * 2, cp * 2 * g.rows};
     const uint32_t w32 = jw < k1p::SPOS ? jw : k1p::SPOS;
     const uint32_t box[3] = {w32, k1p::SPOS / w32, 32};
@@ -571,12 +575,13 @@ int launch_k1p(const void* z, const void* mask, const tmu_trimul_weights* w, con
   p.log2_jw = 31 - __builtin_clz(static_cast<unsigned>(jw));
   p.tiles_i = (g.rows + ih - 1) / ih;
   p.tiles_j = (g.cols + jw - 1) / jw;
-  p.num_tiles = 2 * g.B * p.tiles_i * p.tiles_j;
+  p.num_tiles = (CZ == 256 ? 2 : 1) * g.B * p.tiles_i * p.tiles_j;
   p.reset_status = reset_status ? 1 : 0;
   p.status = status;
   p.timeout_ns = g_timeout_ns;
-  const int npairs = std::min(p.num_tiles, pairs & ~1);  // even: a pair keeps one operand
-  cudaError_t e = launch_pdl_pair(kern, 2 * npairs, k1p::kThreads, k1p::SMEM_BYTES, stream, p);
+  // c_z = 256: an even pair count, so that a pair keeps one operand
+  const int npairs = std::min(p.num_tiles, CZ == 256 ? (pairs & ~1) : pairs);
+  cudaError_t e = launch_pdl_pair(kern, 2 * npairs, k1p::kThreads, C::SMEM_BYTES, stream, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? TMU_OK : cuda_fail(e, "launch project_gate_pair_kernel");
 }
