@@ -690,12 +690,16 @@ def _case_summary(case, flush, steps, warmup, with_parity=True, slab_rows=None) 
         flush.zero_()
         case.g_step.replay()
     torch.cuda.synchronize()
+    sampler = ClockSampler(torch.cuda.current_device())
+    sampler.start()
+    time.sleep(0.2)
     ms = case.time_steps(flush, steps) / steps
+    clocks = sampler.stop()
     tr = case.trace(flush, max(3, min(steps, 10)))
     dom, kernels = case.kernel_table(tr)
     out = {"workload": case.cfg.name, "L": case.cfg.L, "B": case.cfg.B, "c_z": case.cfg.c_z,
            "value": case.cells / (ms * 1e-3), "unit": UNIT, "ms_per_step": round(ms, 5), "steps": steps,
-           "dominant_kernel": dom, "kernels": kernels, "trace": tr}
+           "dominant_kernel": dom, "kernels": kernels, "trace": tr, "clocks": clocks}
     code, site = case.ops.read_status(case.wsp.status)
     if code != 0:
         raise RuntimeError(f"device status {code} at site {site:#x}")
