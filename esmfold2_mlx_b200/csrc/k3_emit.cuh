@@ -25,13 +25,14 @@
 //   warps 10-13 A2 = fp16(LN_in(z row)), in place over the z stage; both concurrently, both
 //              K-major 128B-swizzled UMMA operands.  A2 in place (instead of one separate A2
 //              buffer) lets LN_in run ahead of the MMA, and its 32 KB pays for a third z stage;
-//              after the MMA has read A2, each epilogue half reloads its 64-channel z atom into
-//              the stage (an L2 hit) for the residual.
+//              after the MMA has read A2, warp 22 reloads the tile's z into the stage (an L2
+//              hit) for the residual, ahead of the epilogue.
 //   warps 14-21 epilogue, two groups of four warps (one per TMEM lane quadrant); group h owns
 //              output channels [64h, 64h+64): TMEM -> gate/residual in fp32 -> z' written over
 //              the z tile -> each warp TMA-stores its own 32 positions x 64 channels
 //   warp 22    TMA: the x tiles (warp 0 keeps the z tiles), so an x load never queues behind
-//              the z stage, which stays busy until the epilogue has stored z'
+//              the z stage, which stays busy until the epilogue has stored z'; and the residual
+//              reloads, one tile behind the x loads
 #pragma once
 
 #include "tmu_common.cuh"
@@ -77,7 +78,7 @@ struct Params {
 
 enum Site : unsigned int {
   kSiteProdZ = 0x301, kSiteProdX = 0x302, kSiteTrA = 0x303, kSiteTrX = 0x304, kSiteTrZ = 0x305,
-  kSiteMmaW = 0x306, kSiteMmaA = 0x307, kSiteMmaT = 0x308, kSiteEpilogue = 0x309
+  kSiteMmaW = 0x306, kSiteMmaA = 0x307, kSiteMmaT = 0x308, kSiteEpilogue = 0x309, kSiteProdR = 0x30a
 };
 
 __device__ __forceinline__ void decode_tile(const Params& p, int tile, int& bb, int& i0, int& j0) {
@@ -202,14 +203,34 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       }
     }
   } else if (warp == 22) {
-    // ---------------- TMA producer: x tiles ----------------
+    // ---------------- TMA producer: x tiles and the residual reloads ----------------
+    // After the MMA has read A2 from a z stage (zread), the stage is refilled with that tile's z
+    // (an L2 hit) for the epilogue's residual.  The reload of tile t is issued here, right after
+    // the x load of tile t + 1: both wait for the same MMA commits (xempty of the stage x(t + 1)
+    // reuses and zread of t come from the MMAs of t - 1 and t), so neither waits on the other,
+    // and the reload is in flight while the epilogue is still busy with tile t - 1.
     if (lane == 0) {
-      uint32_t it = 0, nx = 0;
+      uint32_t it = 0, nx = 0, nr = 0;
+      int pb = 0, pi = 0, pj = 0;  // the previous tile, whose reload is due
+      auto reload = [&](uint32_t k, int bb, int i0, int j0) -> bool {
+        const uint32_t s = k % NZ, ph = (k / NZ) & 1;
+        if (!mbar_wait(&zread[s], ph, ctx, kSiteProdR)) return false;
+        for (int h = 0; h < 2; ++h) {
+          mbar_arrive_expect_tx(&rfull[2 * s + h], ATOM_BYTES);
+          tma_load_4d(smem + OFF_Z + s * TILE_BYTES + h * ATOM_BYTES, &p.tm_z, &rfull[2 * s + h], h * 64, j0, i0, bb);
+        }
+        ++nr;
+        return true;
+      };
+      bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
         int bb, i0, j0;
         decode_tile(p, tile, bb, i0, j0);
         const uint32_t s = it & 1, ph = (it >> 1) & 1;
-        if (!mbar_wait(&xempty[s], ph ^ 1, ctx, kSiteProdX)) break;
+        if (!mbar_wait(&xempty[s], ph ^ 1, ctx, kSiteProdX)) {
+          ok = false;
+          break;
+        }
         mbar_arrive_expect_tx(&xfull[s], TILE * CC * 2);
         if (XMODE == 1) {  // positions 0-63, then 64-127 (the tile's second half-row, or its second row)
           tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
@@ -222,11 +243,24 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
           tma_load_3d(smem + OFF_X + s * TILE_BYTES, &p.tm_x, &xfull[s], j0, i0, bb * CC);
         }
         ++nx;
+        if (it > 0 && !reload(it - 1, pb, pi, pj)) {
+          ok = false;
+          break;
+        }
+        pb = bb, pi = i0, pj = j0;
       }
+      if (ok && it > 0) reload(it - 1, pb, pi, pj);
       if (abort_sh) {
         for (uint32_t s = 0; s < 2; ++s) {
           const uint32_t nxa = nx > s ? (nx - s + 1) / 2 : 0;
           if (nxa) mbar_drain(&xfull[s], (nxa - 1) & 1, 200000000ull);
+        }
+        for (uint32_t s = 0; s < NZ; ++s) {  // reloads in flight land before the CTA exits
+          const uint32_t nra = nr > s ? (nr - s + NZ - 1) / NZ : 0;
+          if (nra) {
+            mbar_drain(&rfull[2 * s], (nra - 1) & 1, 200000000ull);
+            mbar_drain(&rfull[2 * s + 1], (nra - 1) & 1, 200000000ull);
+          }
         }
       }
     }
@@ -431,25 +465,17 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
     constexpr bool has_be = HAS_BIAS, has_bg = HAS_BIAS;
     uint32_t it = 0, gcount = 0;
     const bool leader = ((warp - 14) & 3) == 0 && lane == 0;
-    int reload_armed = -1;  // the stage whose z reload is in flight (for the abort drain)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
       const uint32_t s = it % NZ, ph = (it / NZ) & 1;
       const uint32_t acc = it & 1, aph = (it >> 1) & 1;
       uint8_t* Zh = smem + OFF_Z + s * TILE_BYTES + h * ATOM_BYTES;
-      if (leader && mbar_wait(&zread[s], ph, ctx, kSiteEpilogue)) {
-        // The stage held A2 until the MMA read it: bring this half's z atom back for the residual
-        // (an L2 hit, read by this CTA microseconds before).
-        mbar_arrive_expect_tx(&rfull[2 * s + h], ATOM_BYTES);
-        tma_load_4d(Zh, &p.tm_z, &rfull[2 * s + h], h * 64, j0, i0, bb);
-        reload_armed = static_cast<int>(s);
-      }
-      // one thread of each channel half's four warps waits, the others park on barrier 3 + h
+      // the accumulators and this half's z atom, reloaded for the residual by warp 22; one thread
+      // of each channel half's four warps waits, the others park on barrier 3 + h
       if (!group_wait(&tfull[acc], aph, &rfull[2 * s + h], ph, ctx, kSiteEpilogue, leader, 3 + h, 128,
                       gflags + 2 + 2 * h, gcount))
         break;
-      reload_armed = -1;
       tc_fence_after();
       const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * 256 + h * 64;
 #pragma unroll 1
@@ -494,9 +520,6 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_kernel(const __grid
       }
     }
     if (lane == 0) bulk_wait<0>();
-    if (reload_armed >= 0) {  // an abort left a reload in flight: let it land before the CTA exits
-      mbar_drain(&rfull[2 * reload_armed + h], (it / NZ) & 1, 200000000ull);
-    }
   }
 
   tc_fence_before();
