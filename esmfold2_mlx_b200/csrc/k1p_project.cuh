@@ -344,9 +344,9 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
           }
           *reinterpret_cast<uint4*>(A + a * ZATOM_BYTES + sw128_off(row, c16)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
-      fence_proxy_async_all();  // n (generic-proxy writes) -> visible to the paired MMA
+      fence_proxy_async_smem();  // generic-proxy writes to this CTA's shared memory -> the paired MMA's reads
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(cluster_addr(&lnfull[s], 0));
+      if (lane == 0) mbar_arrive_cluster_smem(cluster_addr(&lnfull[s], 0));
     }
   } else {
     // ---------------- epilogue: gate, mask, channel-major store ----------------
@@ -402,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) project_gate_pair_kernel(const __
         if (pb == SPOS - POS) {  // this group's columns of the slot have been read
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[slot], 0));
+          if (lane == 0) mbar_arrive_cluster_smem(cluster_addr(&tempty[slot], 0));
         }
         uint32_t o[8];
 #pragma unroll

@@ -354,9 +354,9 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
                                         shift, 1e-5f);
         ln_atom_apply(Zp, Zp, ATOM_BYTES, row, part, mr.x, mr.y, par);
       }
-      fence_proxy_async_all();  // A1 / A2 (generic-proxy writes) -> visible to the paired MMA
+      fence_proxy_async_smem();  // generic-proxy writes to this CTA's shared memory -> the paired MMA's reads
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(cluster_addr(&afull[s], 0));
+      if (lane == 0) mbar_arrive_cluster_smem(cluster_addr(&afull[s], 0));
     }
   } else {
     // ---------------- epilogue ----------------
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
         if (pb == TILE - 16) {  // the slot has been read: hand it back to the MMA thread
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[s], 0));
+          if (lane == 0) mbar_arrive_cluster_smem(cluster_addr(&tempty[s], 0));
         }
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
