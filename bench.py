@@ -347,15 +347,21 @@ def _trunk_recycle(device, flush, reps: int = 3):
             "output_finite": finite}
 
 
-def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True) -> dict:
+def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True, partition="rows") -> dict:
     """one fold of L = 3072, outgoing then incoming tri-mul, its rows split over
-    the N ranks (strong scaling: the total work is fixed).  Each rank projects its rows (for the
+    the N ranks (strong scaling: the total work is fixed).
+
+    ``partition="rows"`` (the configuration's own scheme): each rank projects its rows (for the
     incoming form from its columns, which the copy engines pull from every rank's rows with one
     pitched copy per peer), b is exchanged while the local block is contracted (copy engines over
-    NVLink by default, ``nccl``: an NCCL all-gather), and each rank finishes its rows.  Eager
-    launches; the inputs per rank (>= 302 MB at N = 8) exceed L2, so no flush is needed."""
+    NVLink by default, ``nccl``: an NCCL all-gather), and each rank finishes its rows.
+    ``partition="channels"``: each rank projects its rows, two all-to-alls move a and b to channel
+    ownership and x back (copy engines, or NCCL with ``nccl``), and the contraction of c/N
+    channels over the whole grid runs between them.  Eager launches; the inputs per rank
+    (>= 302 MB at N = 8) exceed L2, so no flush is needed."""
     from esmfold2_mlx_b200 import ops
-    from esmfold2_mlx_b200.sharded import CopyEngineExchange, DistExchange, LocalExchange, RowShardedTrimul
+    from esmfold2_mlx_b200.sharded import (ChannelShardedTrimul, CopyEngineExchange, DistExchange, LocalExchange,
+                                           RowShardedTrimul)
 
     device = torch.device("cuda", local)
     cfg, trunk, _, w, z_host, _ = _workload(rank, device, "c5", ws)
@@ -366,7 +372,7 @@ def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True) -> dict
         ex = DistExchange(None)
     else:
         ex = CopyEngineExchange(None)
-    sh = RowShardedTrimul(L, device=device, exchange=ex)
+    sh = (RowShardedTrimul if partition == "rows" else ChannelShardedTrimul)(L, device=device, exchange=ex)
     Lr = sh.Lr
     z0 = z_host.to(device)
     z1 = torch.empty_like(z0)
@@ -416,8 +422,13 @@ def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True) -> dict
             e2e_ms += e0.elapsed_time(e1)
     e2e_ms = _max_over_ranks(e2e_ms, ws, device) / steps
     pitch = ops.row_pitch(L)
-    # bytes each rank receives per step: (P-1)/P of b for both directions, plus z's column blocks
-    recv = (ws - 1) * (2 * cfg.c * Lr * pitch * 2 + Lr * Lr * cfg.c_z * 2)
+    if partition == "rows":
+        # bytes each rank receives per step: (P-1)/P of b for both directions, plus z's column blocks
+        recv = (ws - 1) * (2 * cfg.c * Lr * pitch * 2 + Lr * Lr * cfg.c_z * 2)
+    else:
+        # per direction, from each peer: its rows of this rank's c/P channels of a and b, and this
+        # rank's rows of the peer's channels of x
+        recv = 2 * 3 * (ws - 1) * (cfg.c // ws) * Lr * pitch * 2
     link_gbs = 770.0  # measured peer copy per direction on this pool's NVLink (bytes / s / 1e9)
     comm_ms = recv / (link_gbs * 1e9) * 1e3
     flops = 2 * (2 * cfg.c * L) * Lr * L  # the contraction's FLOPs per rank per step (both directions)
@@ -431,10 +442,16 @@ def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True) -> dict
     res = {"workload": cfg.name, "L": L, "B": 1, "c_z": cfg.c_z, "n_gpus": ws, "scaling": "strong",
            "value": cells / (ms_per_step * 1e-3), "unit": UNIT, "ms_per_step": round(ms_per_step, 4),
            "steps": steps,
-           "parallelism": f"rows x{ws} (row-sharded fold)",
-           "exchange": ("none" if ws == 1 else "NCCL all-gather of b" if nccl else
-                        "copy engines over NVLink (CUDA IPC): b slabs by cudaMemcpyAsync, z column blocks "
-                        "(incoming all-to-all + transpose) by one cudaMemcpy2DAsync per peer"),
+           "parallelism": (f"rows x{ws} (row-sharded fold)" if partition == "rows" else
+                           f"rows x{ws} (row-sharded fold), contraction over c/{ws} channels per rank"),
+           "exchange": ("none" if ws == 1 else
+                        ("NCCL all-gather of b" if nccl else
+                         "copy engines over NVLink (CUDA IPC): b slabs by cudaMemcpyAsync, z column blocks "
+                         "(incoming all-to-all + transpose) by one cudaMemcpy2DAsync per peer")
+                        if partition == "rows" else
+                        ("NCCL all-to-all of a, b and x" if nccl else
+                         "copy engines over NVLink (CUDA IPC): a, b to channel ownership and x back to rows, "
+                         "one cudaMemcpy2DAsync per peer and tensor")),
            "roofline": {"bound": "nvlink" if comm_ms > tensor_ms else "tensor",
                         "recv_bytes_per_rank_per_step": recv, "nvlink_gbs_per_direction": link_gbs,
                         "comm_floor_ms": round(comm_ms, 4), "contraction_floor_ms": round(tensor_ms, 4),
@@ -486,7 +503,8 @@ def run_sharded(args, ws, rank, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
-    res = _c5_measure(ws, rank, local, args.steps, args.warmup, args.c5_nccl, not args.no_parity)
+    res = _c5_measure(ws, rank, local, args.steps, args.warmup, args.c5_nccl, not args.no_parity,
+                      args.c5_partition)
     if rank == 0:
         line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
@@ -952,6 +970,9 @@ def run_b200(args, ws, rank, local):
                                   not args.no_parity)
         torch.cuda.empty_cache()
         extra["c5"] = _c5_measure(ws, rank, local, min(args.steps, 10), args.warmup, False, not args.no_parity)
+        if ws > 1:  # at N = 1 both partitions run the same three kernels on the whole fold
+            extra["c5_channels"] = _c5_measure(ws, rank, local, min(args.steps, 10), args.warmup, False,
+                                               not args.no_parity, partition="channels")
         torch.cuda.empty_cache()
 
     # ---------------- CPU baseline (rank 0, N = 1) ----------------
@@ -1183,6 +1204,9 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the L2048 and c2w sub-measurements")
     ap.add_argument("--c5-nccl", action="store_true",
                     help="c5: move b with an NCCL all-gather instead of copy-engine peer copies")
+    ap.add_argument("--c5-partition", choices=["rows", "channels"], default="rows",
+                    help="c5: contraction partition (rows: all-gather of b, the configuration's scheme; "
+                         "channels: all-to-alls of a, b and x)")
     ap.add_argument("--workload", choices=WORKLOADS, default="c2",
                     help="c2 (default: the metric's configuration), c1, c4 (64 folds x L=146), L2048, "
                          "c5 (one L=3072 fold row-sharded over the N ranks), c2w / L2048w (c_z = c = 256), "

@@ -1,5 +1,10 @@
 """One long sequence's triangle update row-sharded over the GPUs of a process group.
 
+Two partitions of the contraction share the row-sharded pair tensor: :class:`RowShardedTrimul`
+(below: an all-gather of b, an all-to-all transpose of z for the incoming form) and
+:class:`ChannelShardedTrimul` (the contraction split over channels by two all-to-alls, at the
+end of this file).
+
 The reference runs one fold on one device; this path (L = 3072 over 2/4/8
 B200s) has no counterpart there.  Rank r holds rows [r*Lr, (r+1)*Lr) of the pair tensor
 z [1, L, L, c_z] (Lr = L / P) and returns the same rows of z + update.
@@ -41,14 +46,15 @@ class CudaStages:
         self.device = torch.device(device)
         self.status = ops.new_status(self.device)
 
-    def project_gate(self, z, layout, mask, w, b_out=None):
+    def project_gate(self, z, layout, mask, w, b_out=None, a_out=None):
         """z: storage holding a [B, rows, cols, c_z] view with element strides
         (stride_b, stride_row, stride_col); mask likewise with mask strides (or None).
-        Returns a, b: [B*c, rows, pitch(cols)] (b written into ``b_out`` when given)."""
+        Returns a, b: [B*c, rows, pitch(cols)] (written into ``a_out`` / ``b_out`` when given)."""
         B, rows, cols, sb, sr, sc, msb, msr, msc = layout
         lib = _lib.load()
         g = _lib.TmuPairLayout(B, rows, cols, sb, sr, sc, msb, msr, msc)
-        a = torch.empty(B * w.c, rows, ops.row_pitch(cols), dtype=torch.float16, device=self.device)
+        a = a_out if a_out is not None else torch.empty(B * w.c, rows, ops.row_pitch(cols), dtype=torch.float16,
+                                                        device=self.device)
         b = torch.empty_like(a) if b_out is None else b_out
         _lib.check(lib.tmu_project_gate_ex(ops._ptr(z), ops._ptr(mask), ctypes.byref(g), ctypes.byref(w.struct),
                                            w.c_z, w.c, ops._ptr(a), ops._ptr(b), ops._ptr(self.status),
@@ -69,6 +75,15 @@ class CudaStages:
                                        x.stride(1), int(max_ctas), ops._ptr(self.status),
                                        ops._stream_ptr(self.device)),
                    "tmu_contract_ex")
+        return x
+
+    def contract_full(self, a, b, L, outgoing, x=None):
+        """K2 over whole channels: a, b [Bc, L, pitch(L)] -> x[d] = a[d] b[d]^T (outgoing) or
+        a[d]^T b[d] (incoming), written into ``x`` ([Bc, L, pitch(L)], contiguous) when given."""
+        lib = _lib.load()
+        x = torch.empty_like(a) if x is None else x
+        _lib.check(lib.tmu_contract(ops._ptr(a), ops._ptr(b), ops._ptr(x), a.shape[0], L, 1 if outgoing else 0,
+                                    ops._ptr(self.status), ops._stream_ptr(self.device)), "tmu_contract")
         return x
 
     def emit_residual(self, x, z, w, mix_eps, out):
@@ -212,6 +227,8 @@ class CopyEngineExchange(DistExchange):
         self.host_group = host_group if host_group is not None else dist.new_group(backend="gloo")
         self._b = None
         self._z = None
+        self._ab = None  # channel partition: the local a and b row slabs [2, c, Lr, pitch]
+        self._xc = None  # channel partition: this rank's channels of x over the grid [c/P, L, pitch]
         self.copy_stream = None
 
     def _stream(self, device):
@@ -287,19 +304,87 @@ class CopyEngineExchange(DistExchange):
         torch.cuda.current_stream(device).wait_event(done)
         return self.zt
 
+    # ---- channel partition (ChannelShardedTrimul)
+    def _pull_blocks(self, sp, jobs):
+        """Publish this call's buffer of ``sp`` and, for each job (dst, dst_pitch, src_off,
+        src_pitch, width, height, dst_step), pull from every rank q (this one included) ``height``
+        rows of ``width`` bytes at byte offset ``src_off`` of q's buffer (rows ``src_pitch`` apart)
+        to ``dst + q * dst_step`` (rows ``dst_pitch`` apart): one pitched copy per rank and job on
+        the copy stream.  The current stream waits for the result."""
+        lib = _lib.load()
+        device = sp.bufs[0].device
+        par = sp.publish()
+        cs = self._stream(device)
+        cs.wait_stream(torch.cuda.current_stream(device))  # the destinations may still be read by the last call
+        for q in range(self.size):
+            if q == self.rank:
+                base = sp.bufs[par].data_ptr()
+            else:
+                cs.wait_event(sp.peer_ready[q][par])
+                base = sp.peer_bufs[q][par]
+            for dst, dst_pitch, src_off, src_pitch, width, height, dst_step in jobs:
+                _lib.check(lib.tmu_copy2d_async(ctypes.c_void_p(dst + q * dst_step), dst_pitch,
+                                                ctypes.c_void_p(base + src_off), src_pitch, width, height,
+                                                cs.cuda_stream), "tmu_copy2d_async")
+        sp.read[par].record(cs)
+        done = torch.cuda.Event()
+        done.record(cs)
+        torch.cuda.current_stream(device).wait_event(done)
+
+    def row_slabs(self, c: int, Lr: int, pitch: int, device) -> torch.Tensor:
+        """This call's persistent [2, c, Lr, pitch] buffer for the local a and b (K1 writes them)."""
+        shape = (2, c, Lr, pitch)
+        if self._ab is None or self._ab.shape != shape:
+            if self._ab is not None:
+                self._ab.close()
+            self._ab = _SharedPair(self, shape, torch.float16, device)
+            self.ab_ch = torch.empty((2, c // self.size, self.size * Lr, pitch), dtype=torch.float16, device=device)
+            dist.barrier(group=self.host_group)
+        return self._ab.for_write(device)
+
+    def to_channels(self):
+        """a, b of this rank's c/P channels over the whole grid, [c/P, L, pitch] each: from every
+        rank q its rows of those channels (c/P runs of Lr * pitch contiguous elements)."""
+        _, c, Lr, pitch = self._ab.shape
+        cp, blk = c // self.size, Lr * pitch * 2
+        self._pull_blocks(self._ab, [(self.ab_ch[t].data_ptr(), self.size * blk, (t * c + self.rank * cp) * blk, blk,
+                                      blk, cp, blk) for t in range(2)])
+        return self.ab_ch[0], self.ab_ch[1]
+
+    def channel_slab(self, cp: int, L: int, pitch: int, device) -> torch.Tensor:
+        """This call's persistent [c/P, L, pitch] buffer for this rank's channels of x (K2 writes it)."""
+        shape = (cp, L, pitch)
+        if self._xc is None or self._xc.shape != shape:
+            if self._xc is not None:
+                self._xc.close()
+            self._xc = _SharedPair(self, shape, torch.float16, device)
+            self.x_rows = torch.empty((self.size * cp, L // self.size, pitch), dtype=torch.float16, device=device)
+            dist.barrier(group=self.host_group)
+        return self._xc.for_write(device)
+
+    def to_rows(self):
+        """x of this rank's rows over all channels, [c, Lr, pitch]: from every rank q its channels
+        of those rows (c/P runs of Lr * pitch contiguous elements, L * pitch apart)."""
+        cp, L, pitch = self._xc.shape
+        Lr = L // self.size
+        blk = Lr * pitch * 2
+        self._pull_blocks(self._xc, [(self.x_rows.data_ptr(), blk, self.rank * blk, L * pitch * 2, blk, cp, cp * blk)])
+        return self.x_rows
+
     def wait(self, handle):
         torch.cuda.current_stream().wait_event(handle)
 
     def close(self):
         """Release the imported peer mappings (after every rank is done with them)."""
-        if self._b is None and self._z is None:
+        pairs = (self._b, self._z, self._ab, self._xc)
+        if all(sp is None for sp in pairs):
             return
         torch.cuda.synchronize()
         dist.barrier(group=self.host_group)
-        for sp in (self._b, self._z):
+        for sp in pairs:
             if sp is not None:
                 sp.close()
-        self._b = self._z = None
+        self._b = self._z = self._ab = self._xc = None
 
 
 class LocalExchange:
@@ -404,3 +489,80 @@ class RowShardedTrimul:
             if q1 > q0:
                 self.stages.contract(a, parts[q0:q1], Lr, (q1 - q0) * Lr, L, Lr, x=x[:, :, q0 * Lr:])
         return x
+
+
+class ChannelShardedTrimul:
+    """Triangle update of a row-sharded pair tensor, the contraction sharded over channels (B = 1).
+
+    Rank r holds rows [r*Lr, (r+1)*Lr) of z, as for :class:`RowShardedTrimul`, and returns the
+    same rows of z + update.  The row partition must bring every rank all of b, so the bytes a
+    rank receives grow towards b's size as P grows while its share of the contraction falls as
+    1/P.  The contraction is independent per channel (mlx_trunk.py:84-88: one L x L x L product
+    per channel d), so this driver moves channels instead:
+
+      K1 on the local rows, all c channels -> a, b [c, Lr, pitch]
+      all-to-all: rank r receives every rank's rows of its channels [rc, (r+1)c) / P
+                                           -> a, b [c/P, L, pitch] over the whole grid
+      K2 on those channels, the single-GPU kernel (outgoing or incoming form: the incoming
+         update needs no transposed z)      -> x [c/P, L, pitch]
+      all-to-all back to row ownership     -> x [c, Lr, pitch]
+      K3 on the local rows.
+
+    A rank receives (P-1)/P^2 of a, b and x per update: falling as 1/P.  With the copy-engine
+    exchange each all-to-all is one pitched copy per rank and tensor from the peers' exported
+    buffers (K1 and K2 write straight into them); any other exchange (NCCL, gloo, threads) runs
+    ``all_to_all`` on [P, c/P, Lr, pitch] blocks.  Needs c % P == 0.
+    """
+
+    def __init__(self, L: int, group=None, device=None, stages=None, exchange=None):
+        self.exchange = exchange if exchange is not None else DistExchange(group)
+        self.P = self.exchange.size
+        self.rank = self.exchange.rank
+        if L % self.P:
+            raise ValueError(f"L={L} is not divisible by the {self.P} ranks")
+        self.L, self.Lr = L, L // self.P
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.stages = stages if stages is not None else CudaStages(self.device)
+
+    def _to_channels(self, t):
+        """[c, Lr, pitch] (my rows) -> [c/P, L, pitch] (my channels) through ``all_to_all``."""
+        P, Lr = self.P, self.Lr
+        c, pitch = t.shape[0], t.shape[2]
+        recv = self.exchange.all_to_all(t.reshape(P, c // P, Lr, pitch))  # [P(source rows), c/P, Lr, pitch]
+        return recv.permute(1, 0, 2, 3).reshape(c // P, P * Lr, pitch)
+
+    def _to_rows(self, x):
+        """[c/P, L, pitch] (my channels) -> [c, Lr, pitch] (my rows) through ``all_to_all``."""
+        P, Lr = self.P, self.Lr
+        cp, pitch = x.shape[0], x.shape[2]
+        send = x.reshape(cp, P, Lr, pitch).permute(1, 0, 2, 3).contiguous()  # send[q] = q's rows
+        return self.exchange.all_to_all(send).reshape(P * cp, Lr, pitch)  # [P(source channels) * c/P, ...]
+
+    def __call__(self, z_local: torch.Tensor, mask_local, w: ops.TrimulWeights, outgoing: bool,
+                 mix_eps: float = ops.MIX_EPS_FP16, out: torch.Tensor | None = None) -> torch.Tensor:
+        """z_local: [1, Lr, L, c_z] fp16 (this rank's rows); mask_local: [1, Lr, L] fp16 or None."""
+        L, Lr, P = self.L, self.Lr, self.P
+        cz, c = w.c_z, w.c
+        if c % P:
+            raise ValueError(f"c={c} channels do not split over {P} ranks")
+        if tuple(z_local.shape) != (1, Lr, L, cz):
+            raise ValueError(f"z_local must be [1, {Lr}, {L}, {cz}], got {tuple(z_local.shape)}")
+        z_local = z_local.contiguous()
+        out = torch.empty_like(z_local) if out is None else out
+        pitch = ops.row_pitch(L)
+        ex = self.exchange
+        engines = P > 1 and hasattr(ex, "row_slabs")
+        layout = (1, Lr, L, Lr * L * cz, L * cz, cz, Lr * L, L, 1)
+        mask = None if mask_local is None else mask_local.contiguous()
+        if engines:
+            ab = ex.row_slabs(c, Lr, pitch, z_local.device)
+            self.stages.project_gate(z_local, layout, mask, w, b_out=ab[1], a_out=ab[0])
+            a_ch, b_ch = ex.to_channels()
+            x_ch = self.stages.contract_full(a_ch, b_ch, L, outgoing, x=ex.channel_slab(c // P, L, pitch,
+                                                                                       z_local.device))
+            x = ex.to_rows()
+        else:
+            a, b = self.stages.project_gate(z_local, layout, mask, w)
+            x_ch = self.stages.contract_full(self._to_channels(a), self._to_channels(b), L, outgoing)
+            x = self._to_rows(x_ch)
+        return self.stages.emit_residual(x, z_local, w, mix_eps, out)

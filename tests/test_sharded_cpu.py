@@ -1,7 +1,8 @@
 """Row-sharded tri-mul data movement on CPU ranks (gloo, world_size 2).
 
 ``RowShardedTrimul`` drives the exchange (all-to-all into columns for the incoming form, an
-asynchronous all-gather of b) and hands slabs to three stages.  Here the stages are the CPU oracle applied to
+asynchronous all-gather of b) and hands slabs to three stages; ``ChannelShardedTrimul`` moves
+a and b to channel ownership and x back by two all-to-alls.  Here the stages are the CPU oracle applied to
 exactly the buffers the CUDA kernels would see -- the strided (possibly transposed) z view, the
 [B*c, rows, pitch] projections, b blocks contracted into column blocks of x -- so the test checks
 the layouts and the collectives; the kernels themselves are checked on the GPU.
@@ -18,7 +19,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from esmfold2_mlx_b200 import ops
-from esmfold2_mlx_b200.sharded import RowShardedTrimul
+from esmfold2_mlx_b200.sharded import ChannelShardedTrimul, RowShardedTrimul
 from esmfold2_mlx_b200.synthetic import FoldingTrunk, pair_mask, pair_tensor
 from oracle import trimul_oracle as orc
 
@@ -30,7 +31,7 @@ class OracleStages:
     def __init__(self, p):
         self.p = p
 
-    def project_gate(self, z, layout, mask, w, b_out=None):
+    def project_gate(self, z, layout, mask, w, b_out=None, a_out=None):
         B, rows, cols, sb, sr, sc, msb, msr, msc = layout
         zv = torch.as_strided(z.reshape(-1).float(), (B, rows, cols, 128), (sb, sr, sc, 1))
         mv = None if mask is None else torch.as_strided(mask.reshape(-1).float(), (B, rows, cols), (msb, msr, msc))
@@ -56,6 +57,14 @@ class OracleStages:
         if x is None:
             x = torch.full((Bc, M, ops.row_pitch(N)), float("nan"), dtype=torch.float16)
         x[:, :, :N] = xv.half()
+        return x
+
+    def contract_full(self, a, b, L, outgoing, x=None):
+        A, Bm = a[:, :, :L].float(), b[:, :, :L].float()
+        xv = orc.r16(A @ Bm.transpose(1, 2) if outgoing else A.transpose(1, 2) @ Bm)
+        if x is None:
+            x = torch.full(a.shape, float("nan"), dtype=torch.float16)
+        x[:, :, :L] = xv.half()
         return x
 
     def emit_residual(self, x, z, w, mix_eps, out):
@@ -88,9 +97,10 @@ def _run(rank, q):
         Lr = L // P
         w = types.SimpleNamespace(c_z=128, c=128)
         res = {}
-        for direction, outgoing in (("out", True), ("in", False)):
+        for (direction, outgoing), Driver in ((d, D) for D in (RowShardedTrimul, ChannelShardedTrimul)
+                                              for d in (("out", True), ("in", False))):
             p = orc.trimul_params(getattr(trunk.blocks[0], "tri_mul_" + direction), True)
-            st = RowShardedTrimul(L, device="cpu", stages=OracleStages(p))
+            st = Driver(L, device="cpu", stages=OracleStages(p))
             z_loc = z[:, rank * Lr:(rank + 1) * Lr].contiguous()
             m_loc = mask[:, rank * Lr:(rank + 1) * Lr].contiguous()
             out = st(z_loc, m_loc, w, outgoing)
@@ -99,12 +109,12 @@ def _run(rank, q):
             got = full.reshape(1, L, L, 128).float()
             if rank == 0:
                 ref = orc.trimul_fp16(p, z.float(), mask.float(), outgoing)
-                res[direction] = float((got - ref).abs().max())
+                res[f"{Driver.__name__}/{direction}"] = float((got - ref).abs().max())
         q.put((rank, res))
 
 
 @pytest.mark.timeout(600)
-def test_row_sharded_matches_unsharded_oracle():
+def test_row_and_channel_sharded_match_unsharded_oracle():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29600 + os.getpid() % 200
@@ -119,6 +129,6 @@ def test_row_sharded_matches_unsharded_oracle():
     for pr in procs:
         assert pr.exitcode == 0
     res = out[0]
-    assert set(res) == {"out", "in"}
+    assert set(res) == {f"{n}/{d}" for n in ("RowShardedTrimul", "ChannelShardedTrimul") for d in ("out", "in")}
     for d, err in res.items():
         assert err <= 4e-3, f"{d}: sharded vs unsharded max |diff| {err}"

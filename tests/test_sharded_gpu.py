@@ -5,9 +5,10 @@
   differs); on a rectangular slab it is checked against the oracle's projections.
 * ``tmu_contract_ex`` with a B operand made of gathered row blocks is checked against float64.
 * ``tmu_emit_residual_ex`` on a rectangular slab is checked against the oracle.
-* ``RowShardedTrimul`` is run for P ranks emulated by threads on one GPU (the collectives become
-  stacks of the ranks' buffers) and, where two GPUs exist, for two NCCL ranks; both are compared
-  with the unsharded oracle under the same error bounds as the unsharded kernels.
+* ``RowShardedTrimul`` and ``ChannelShardedTrimul`` are run for P ranks emulated by threads on
+  one GPU (the collectives become stacks of the ranks' buffers) and, where two GPUs exist, for
+  two NCCL ranks (NCCL collectives, or the copy engines over CUDA IPC); all are compared with the
+  unsharded oracle under the same error bounds as the unsharded kernels.
 """
 
 from __future__ import annotations
@@ -20,7 +21,7 @@ import pytest
 import torch
 
 from esmfold2_mlx_b200 import _lib, ops
-from esmfold2_mlx_b200.sharded import CudaStages, RowShardedTrimul
+from esmfold2_mlx_b200.sharded import ChannelShardedTrimul, CudaStages, RowShardedTrimul
 from esmfold2_mlx_b200.synthetic import FoldingTrunk, pair_mask, pair_tensor, trimul_biases
 from oracle import trimul_oracle as orc
 
@@ -190,12 +191,16 @@ class _SerialStages(CudaStages):
         with self.lock:
             return super().contract(*a, **kw)
 
+    def contract_full(self, *a, **kw):
+        with self.lock:
+            return super().contract_full(*a, **kw)
+
     def emit_residual(self, *a):
         with self.lock:
             return super().emit_residual(*a)
 
 
-def _emulate(P, L, z, mask, w, outgoing):
+def _emulate(P, L, z, mask, w, outgoing, driver=RowShardedTrimul):
     hub = {"P": P, "slots": [None] * P, "barrier": threading.Barrier(P, timeout=120)}
     Lr = L // P
     outs, errs, stages = [None] * P, [], []
@@ -204,7 +209,7 @@ def _emulate(P, L, z, mask, w, outgoing):
         try:
             st = _SerialStages(DEV)
             stages.append(st)
-            sh = RowShardedTrimul(L, device=DEV, stages=st, exchange=_ThreadExchange(hub, r))
+            sh = driver(L, device=DEV, stages=st, exchange=_ThreadExchange(hub, r))
             zl = z[:, r * Lr:(r + 1) * Lr].contiguous()
             ml = None if mask is None else mask[:, r * Lr:(r + 1) * Lr].contiguous()
             outs[r] = sh(zl, ml, w, outgoing)
@@ -248,7 +253,23 @@ def test_row_sharded_emulated_ranks_match_oracle(P, L, n_pad, outgoing):
     assert float((got - full).abs().max()) <= 2 * _ulp16(float(full.abs().max()))
 
 
-def _nccl_worker(rank, port, q, L, copy_engines=False):
+@pytest.mark.parametrize("P,L,n_pad", [(2, 256, 0), (4, 512, 30), (8, 512, 0)])
+@pytest.mark.parametrize("outgoing", [True, False])
+def test_channel_sharded_emulated_ranks_match_oracle(P, L, n_pad, outgoing):
+    direction = "out" if outgoing else "in"
+    trunk, z, mask, bias = _trunk_and_pair(L, seed=L + P + 5, n_pad=n_pad, biases=bool(n_pad))
+    w, p = _weights(trunk, direction, bias)
+    zd = z.half().to(DEV)
+    md = None if mask is None else mask.half().to(DEV)
+    got = _emulate(P, L, zd, md, w, outgoing, ChannelShardedTrimul).float().cpu()
+    ref16 = orc.trimul_fp16(p, z, mask, outgoing)
+    assert float((got - ref16).abs().max()) <= 4 * _ulp16(float(ref16.abs().max()))
+    # the same kernels on the same values: the unsharded update, bit for bit
+    full = ops.trimul(zd, md, w, outgoing).float().cpu()
+    assert torch.equal(got, full)
+
+
+def _nccl_worker(rank, port, q, L, copy_engines=False, driver="rows"):
     import datetime
     import traceback
 
@@ -266,13 +287,14 @@ def _nccl_worker(rank, port, q, L, copy_engines=False):
             Lr = L // 2
             zl = z[:, rank * Lr:(rank + 1) * Lr].half().contiguous().cuda()
             ml = mask[:, rank * Lr:(rank + 1) * Lr].half().contiguous().cuda()
+            Driver = RowShardedTrimul if driver == "rows" else ChannelShardedTrimul
             if copy_engines:
                 from esmfold2_mlx_b200.sharded import CopyEngineExchange
                 if direction == "out":
                     ex = CopyEngineExchange()
-                sh = RowShardedTrimul(L, exchange=ex)
+                sh = Driver(L, exchange=ex)
             else:
-                sh = RowShardedTrimul(L)
+                sh = Driver(L)
             out = sh(zl, ml, w, outgoing)
             full = torch.empty(2, Lr, L, 128, dtype=torch.float16, device=out.device)
             dist.all_gather_into_tensor(full, out)
@@ -293,13 +315,14 @@ def _nccl_worker(rank, port, q, L, copy_engines=False):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.timeout(600)
 @pytest.mark.parametrize("copy_engines", [False, True])
-def test_row_sharded_two_nccl_ranks_match_oracle(copy_engines):
+@pytest.mark.parametrize("driver", ["rows", "channels"])
+def test_sharded_two_nccl_ranks_match_oracle(copy_engines, driver):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29800 + os.getpid() % 150 + (7 if copy_engines else 0)
-    procs = [ctx.Process(target=_nccl_worker, args=(r, port, q, 512, copy_engines)) for r in range(2)]
+    port = 29800 + os.getpid() % 150 + (7 if copy_engines else 0) + (3 if driver == "channels" else 0)
+    procs = [ctx.Process(target=_nccl_worker, args=(r, port, q, 512, copy_engines, driver)) for r in range(2)]
     for pr in procs:
         pr.start()
     out = dict(q.get(timeout=400) for _ in range(2))
@@ -311,9 +334,10 @@ def test_row_sharded_two_nccl_ranks_match_oracle(copy_engines):
         assert err <= 4 * ulp, f"{d}: {err} vs ulp {ulp}"
 
 
+@pytest.mark.parametrize("driver", [RowShardedTrimul, ChannelShardedTrimul])
 @pytest.mark.parametrize("outgoing", [True, False])
-def test_row_sharded_emulated_ranks_wide_pair(outgoing):
-    """c_z = c = 256 through the same sharded driver (P = 2, L = 256)."""
+def test_sharded_emulated_ranks_wide_pair(outgoing, driver):
+    """c_z = c = 256 through the same sharded drivers (P = 2, L = 256)."""
     P, L, cz = 2, 256, 256
     direction = "out" if outgoing else "in"
     trunk = FoldingTrunk(1, cz, cz, hidden=512, seed=41, ln_noise=0.1)
@@ -322,6 +346,6 @@ def test_row_sharded_emulated_ranks_wide_pair(outgoing):
     tri = getattr(trunk.blocks[0], "tri_mul_" + direction)
     w, p = ops.TrimulWeights.from_module(tri, DEV), orc.trimul_params(tri, True)
     zd, md = z.half().to(DEV), mask.half().to(DEV)
-    got = _emulate(P, L, zd, md, w, outgoing).float().cpu()
+    got = _emulate(P, L, zd, md, w, outgoing, driver).float().cpu()
     ref16 = orc.trimul_fp16(p, z, mask, outgoing)
     assert float((got - ref16).abs().max()) <= 4 * _ulp16(float(ref16.abs().max()))
