@@ -347,7 +347,7 @@ def _trunk_recycle(device, flush, reps: int = 3):
             "output_finite": finite}
 
 
-def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True, partition="rows") -> dict:
+def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True, partition="rows", groups=4) -> dict:
     """one fold of L = 3072, outgoing then incoming tri-mul, its rows split over
     the N ranks (strong scaling: the total work is fixed).
 
@@ -372,7 +372,10 @@ def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True, partiti
         ex = DistExchange(None)
     else:
         ex = CopyEngineExchange(None)
-    sh = (RowShardedTrimul if partition == "rows" else ChannelShardedTrimul)(L, device=device, exchange=ex)
+    if partition == "rows":
+        sh = RowShardedTrimul(L, device=device, exchange=ex)
+    else:
+        sh = ChannelShardedTrimul(L, device=device, exchange=ex, groups=groups)
     Lr = sh.Lr
     z0 = z_host.to(device)
     z1 = torch.empty_like(z0)
@@ -451,7 +454,8 @@ def _c5_measure(ws, rank, local, steps, warmup, nccl=False, parity=True, partiti
                         if partition == "rows" else
                         ("NCCL all-to-all of a, b and x" if nccl else
                          "copy engines over NVLink (CUDA IPC): a, b to channel ownership and x back to rows, "
-                         "one cudaMemcpy2DAsync per peer and tensor")),
+                         f"one cudaMemcpy2DAsync per peer, tensor and channel group ({groups} groups, each "
+                         "group's copies overlapping another group's contraction)")),
            "roofline": {"bound": "nvlink" if comm_ms > tensor_ms else "tensor",
                         "recv_bytes_per_rank_per_step": recv, "nvlink_gbs_per_direction": link_gbs,
                         "comm_floor_ms": round(comm_ms, 4), "contraction_floor_ms": round(tensor_ms, 4),
@@ -504,7 +508,7 @@ def run_sharded(args, ws, rank, local):
     torch.cuda.set_device(device)
     _lib.check(_lib.load().tmu_device_check(), "tmu_device_check")
     res = _c5_measure(ws, rank, local, args.steps, args.warmup, args.c5_nccl, not args.no_parity,
-                      args.c5_partition)
+                      args.c5_partition, args.c5_groups)
     if rank == 0:
         line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
@@ -1204,6 +1208,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the L2048 and c2w sub-measurements")
     ap.add_argument("--c5-nccl", action="store_true",
                     help="c5: move b with an NCCL all-gather instead of copy-engine peer copies")
+    ap.add_argument("--c5-groups", type=int, default=4,
+                    help="c5 channel partition: channel groups pipelined through the copy engines")
     ap.add_argument("--c5-partition", choices=["rows", "channels"], default="rows",
                     help="c5: contraction partition (rows: all-gather of b, the configuration's scheme; "
                          "channels: all-to-alls of a, b and x)")

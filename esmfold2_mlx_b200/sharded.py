@@ -305,31 +305,36 @@ class CopyEngineExchange(DistExchange):
         return self.zt
 
     # ---- channel partition (ChannelShardedTrimul)
-    def _pull_blocks(self, sp, jobs):
+    def _pull_blocks(self, sp, jobs, wait=True):
         """Publish this call's buffer of ``sp`` and, for each job (dst, dst_pitch, src_off,
         src_pitch, width, height, dst_step), pull from every rank q (this one included) ``height``
         rows of ``width`` bytes at byte offset ``src_off`` of q's buffer (rows ``src_pitch`` apart)
         to ``dst + q * dst_step`` (rows ``dst_pitch`` apart): one pitched copy per rank and job on
-        the copy stream.  The current stream waits for the result."""
+        the copy stream.  Returns one event per job, recorded after that job's copies; with
+        ``wait`` the current stream waits for the last."""
         lib = _lib.load()
         device = sp.bufs[0].device
         par = sp.publish()
         cs = self._stream(device)
-        cs.wait_stream(torch.cuda.current_stream(device))  # the destinations may still be read by the last call
+        # the destinations may still be read by earlier work; this rank's own block is written there
+        cs.wait_stream(torch.cuda.current_stream(device))
         for q in range(self.size):
-            if q == self.rank:
-                base = sp.bufs[par].data_ptr()
-            else:
+            if q != self.rank:
                 cs.wait_event(sp.peer_ready[q][par])
-                base = sp.peer_bufs[q][par]
-            for dst, dst_pitch, src_off, src_pitch, width, height, dst_step in jobs:
+        events = []
+        for dst, dst_pitch, src_off, src_pitch, width, height, dst_step in jobs:
+            for q in range(self.size):
+                base = sp.bufs[par].data_ptr() if q == self.rank else sp.peer_bufs[q][par]
                 _lib.check(lib.tmu_copy2d_async(ctypes.c_void_p(dst + q * dst_step), dst_pitch,
                                                 ctypes.c_void_p(base + src_off), src_pitch, width, height,
                                                 cs.cuda_stream), "tmu_copy2d_async")
+            ev = torch.cuda.Event()
+            ev.record(cs)
+            events.append(ev)
         sp.read[par].record(cs)
-        done = torch.cuda.Event()
-        done.record(cs)
-        torch.cuda.current_stream(device).wait_event(done)
+        if wait:
+            torch.cuda.current_stream(device).wait_event(events[-1])
+        return events
 
     def row_slabs(self, c: int, Lr: int, pitch: int, device) -> torch.Tensor:
         """This call's persistent [2, c, Lr, pitch] buffer for the local a and b (K1 writes them)."""
@@ -342,33 +347,46 @@ class CopyEngineExchange(DistExchange):
             dist.barrier(group=self.host_group)
         return self._ab.for_write(device)
 
-    def to_channels(self):
+    def to_channels(self, groups: int = 1):
         """a, b of this rank's c/P channels over the whole grid, [c/P, L, pitch] each: from every
-        rank q its rows of those channels (c/P runs of Lr * pitch contiguous elements)."""
+        rank q its rows of those channels (runs of Lr * pitch contiguous elements), pulled in
+        ``groups`` consecutive channel groups.  Returns (a, b, events): event g completes when
+        group g has landed; the caller orders its readers after them."""
         _, c, Lr, pitch = self._ab.shape
         cp, blk = c // self.size, Lr * pitch * 2
-        self._pull_blocks(self._ab, [(self.ab_ch[t].data_ptr(), self.size * blk, (t * c + self.rank * cp) * blk, blk,
-                                      blk, cp, blk) for t in range(2)])
-        return self.ab_ch[0], self.ab_ch[1]
+        cg = cp // groups
+        jobs = []
+        for g in range(groups):
+            for t in range(2):  # a then b of channel group g
+                jobs.append((self.ab_ch[t, g * cg].data_ptr(), self.size * blk, (t * c + self.rank * cp + g * cg) * blk,
+                             blk, blk, cg, blk))
+        events = self._pull_blocks(self._ab, jobs, wait=False)
+        return self.ab_ch[0], self.ab_ch[1], events[1::2]
 
-    def channel_slab(self, cp: int, L: int, pitch: int, device) -> torch.Tensor:
-        """This call's persistent [c/P, L, pitch] buffer for this rank's channels of x (K2 writes it)."""
-        shape = (cp, L, pitch)
-        if self._xc is None or self._xc.shape != shape:
-            if self._xc is not None:
-                self._xc.close()
-            self._xc = _SharedPair(self, shape, torch.float16, device)
+    def channel_slabs(self, cp: int, L: int, pitch: int, device, groups: int = 1) -> list:
+        """This call's persistent buffers for this rank's channels of x, one [c/P / groups, L, pitch]
+        buffer per channel group (K2 writes them group by group)."""
+        cg = cp // groups
+        shape = (cg, L, pitch)
+        if self._xc is None or len(self._xc) != groups or self._xc[0].shape != shape:
+            for sp in self._xc or []:
+                sp.close()
+            self._xc = [_SharedPair(self, shape, torch.float16, device) for _ in range(groups)]
             self.x_rows = torch.empty((self.size * cp, L // self.size, pitch), dtype=torch.float16, device=device)
             dist.barrier(group=self.host_group)
-        return self._xc.for_write(device)
+        return [sp.for_write(device) for sp in self._xc]
 
-    def to_rows(self):
-        """x of this rank's rows over all channels, [c, Lr, pitch]: from every rank q its channels
-        of those rows (c/P runs of Lr * pitch contiguous elements, L * pitch apart)."""
-        cp, L, pitch = self._xc.shape
-        Lr = L // self.size
-        blk = Lr * pitch * 2
-        self._pull_blocks(self._xc, [(self.x_rows.data_ptr(), blk, self.rank * blk, L * pitch * 2, blk, cp, cp * blk)])
+    def to_rows(self, g: int = 0):
+        """Publish channel group g of x and pull from every rank q its group-g channels of this
+        rank's rows (runs of Lr * pitch contiguous elements, L * pitch apart) into [c, Lr, pitch];
+        after the last group the current stream waits for all of them.  Returns that buffer."""
+        groups = len(self._xc)
+        sp = self._xc[g]
+        cg, L, pitch = sp.shape
+        cp = cg * groups
+        blk = (L // self.size) * pitch * 2
+        self._pull_blocks(sp, [(self.x_rows.data_ptr() + g * cg * blk, blk, self.rank * blk, L * pitch * 2, blk, cg,
+                                cp * blk)], wait=g == groups - 1)
         return self.x_rows
 
     def wait(self, handle):
@@ -376,7 +394,7 @@ class CopyEngineExchange(DistExchange):
 
     def close(self):
         """Release the imported peer mappings (after every rank is done with them)."""
-        pairs = (self._b, self._z, self._ab, self._xc)
+        pairs = (self._b, self._z, self._ab, *(self._xc or []))
         if all(sp is None for sp in pairs):
             return
         torch.cuda.synchronize()
@@ -509,18 +527,21 @@ class ChannelShardedTrimul:
       K3 on the local rows.
 
     A rank receives (P-1)/P^2 of a, b and x per update: falling as 1/P.  With the copy-engine
-    exchange each all-to-all is one pitched copy per rank and tensor from the peers' exported
-    buffers (K1 and K2 write straight into them); any other exchange (NCCL, gloo, threads) runs
-    ``all_to_all`` on [P, c/P, Lr, pitch] blocks.  Needs c % P == 0.
+    exchange each all-to-all is one pitched copy per rank, tensor and channel group from the
+    peers' exported buffers (K1 and K2 write straight into them), and the c/P channels go through
+    in ``groups`` groups so that the copies of one group overlap the contraction of another; any
+    other exchange (NCCL, gloo, threads) runs ``all_to_all`` on [P, c/P, Lr, pitch] blocks.
+    Needs c % P == 0.
     """
 
-    def __init__(self, L: int, group=None, device=None, stages=None, exchange=None):
+    def __init__(self, L: int, group=None, device=None, stages=None, exchange=None, groups: int = 4):
         self.exchange = exchange if exchange is not None else DistExchange(group)
         self.P = self.exchange.size
         self.rank = self.exchange.rank
         if L % self.P:
             raise ValueError(f"L={L} is not divisible by the {self.P} ranks")
         self.L, self.Lr = L, L // self.P
+        self.groups = groups  # channel groups pipelined through the copy-engine exchange
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.stages = stages if stages is not None else CudaStages(self.device)
 
@@ -555,12 +576,21 @@ class ChannelShardedTrimul:
         layout = (1, Lr, L, Lr * L * cz, L * cz, cz, Lr * L, L, 1)
         mask = None if mask_local is None else mask_local.contiguous()
         if engines:
+            # K1 into the exported row slabs; then per channel group: its a, b land (copy stream),
+            # K2 contracts it (this stream) while the next group lands, and its x goes back to
+            # the rows' owners while the next group is contracted
+            cp = c // P
+            groups = self.groups if cp % self.groups == 0 else 1
+            cg = cp // groups
             ab = ex.row_slabs(c, Lr, pitch, z_local.device)
             self.stages.project_gate(z_local, layout, mask, w, b_out=ab[1], a_out=ab[0])
-            a_ch, b_ch = ex.to_channels()
-            x_ch = self.stages.contract_full(a_ch, b_ch, L, outgoing, x=ex.channel_slab(c // P, L, pitch,
-                                                                                       z_local.device))
-            x = ex.to_rows()
+            a_ch, b_ch, landed = ex.to_channels(groups)
+            xs = ex.channel_slabs(cp, L, pitch, z_local.device, groups)
+            cur = torch.cuda.current_stream(z_local.device)
+            for g in range(groups):
+                cur.wait_event(landed[g])
+                self.stages.contract_full(a_ch[g * cg:(g + 1) * cg], b_ch[g * cg:(g + 1) * cg], L, outgoing, x=xs[g])
+                x = ex.to_rows(g)
         else:
             a, b = self.stages.project_gate(z_local, layout, mask, w)
             x_ch = self.stages.contract_full(self._to_channels(a), self._to_channels(b), L, outgoing)
