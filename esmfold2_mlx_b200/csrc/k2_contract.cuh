@@ -23,16 +23,19 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 
+// BN = 128, 192 or 256 columns per tile (the host picks the least padding for N: 192 serves
+// 129-192 and 257-384, e.g. L = 146 and 384, where a 256-wide tile computes 43 % / 25 % padding)
 template <int BN>
 struct Cfg {
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static_assert(BN == 128 || BN == 192 || BN == 256, "K2 tile width");
+  static constexpr int STAGES = (BN >= 192) ? 4 : 6;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STG_BYTES = BM * 64 * 2;  // one 64-column fp16 output chunk
   static constexpr int NSTG = 2;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + NSTG * STG_BYTES + 1024;  // + alignment slack
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int TMEM_COLS = BN == 192 ? 512 : 2 * BN;  // two accumulators; allocations are powers of 2
 };
 
 struct Params {

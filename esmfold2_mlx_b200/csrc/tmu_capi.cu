@@ -415,18 +415,36 @@ int launch_k2_t(const void* a, const void* b, void* x, int Bc, int M, int N, int
 
 // ldx: row pitch of x in elements (0: row_pitch(N)); x may be a column block of a wider matrix.
 // max_ctas > 0 caps the persistent grid (leaving SMs to kernels that run alongside, e.g. NCCL's).
+// The tile width for N columns: the least padding ceil(N / BN) * BN over BN in {128, 192, 256},
+// ties to the wider tile (fewer tiles).
+int choose_bn_k2(int N) {
+  int best = 256;
+  long long pad = static_cast<long long>((N + 255) / 256) * 256;
+  for (int bn : {192, 128}) {
+    const long long pb = static_cast<long long>((N + bn - 1) / bn) * bn;
+    if (pb < pad) {
+      pad = pb;
+      best = bn;
+    }
+  }
+  return best;
+}
+
 int launch_k2(const void* a, const void* b, void* x, int Bc, int M, int N, int K, int rows_per_part, bool outgoing,
               DeviceStatus* status, cudaStream_t stream, int ldx = 0, int max_ctas = 0) {
+  const int bn = choose_bn_k2(N);
   if (!outgoing) {
     if (M != N || M != K || rows_per_part != N) return fail(TMU_ERR_UNSUPPORTED, "incoming form is square only");
-    return N <= 128 ? launch_k2_t<128, true>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 2, max_ctas)
-                    : launch_k2_t<256, true>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 4, max_ctas);
+    return bn == 128 ? launch_k2_t<128, true>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 2, max_ctas)
+         : bn == 192 ? launch_k2_t<192, true>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 6, max_ctas)
+                     : launch_k2_t<256, true>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 4, max_ctas);
   }
   const int parts = N / rows_per_part;
   if (parts * rows_per_part != N) return fail(TMU_ERR_INVALID_ARGUMENT, "N must be a multiple of rows_per_part");
   if (parts == 1) {
-    return N <= 128 ? launch_k2_t<128, false>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 1, max_ctas)
-                    : launch_k2_t<256, false>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 3, max_ctas);
+    return bn == 128 ? launch_k2_t<128, false>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 1, max_ctas)
+         : bn == 192 ? launch_k2_t<192, false>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 5, max_ctas)
+                     : launch_k2_t<256, false>(a, b, x, Bc, M, N, K, N, ldx, status, stream, 1u << 3, max_ctas);
   }
   // a gathered B operand: a tile of BN rows must not straddle two parts
   if (rows_per_part % 256 == 0) return launch_k2_t<256, false>(a, b, x, Bc, M, N, K, rows_per_part, ldx, status, stream, 1u << 3, max_ctas);

@@ -67,7 +67,7 @@ def test_bounded_wait_reports_timeout():
     assert float(x.sum()) == 16.0
 
 
-@pytest.mark.parametrize("L", [64, 76, 130, 238, 256, 300])
+@pytest.mark.parametrize("L", [64, 76, 130, 146, 238, 256, 300, 384])  # tile widths 128, 192, 256
 @pytest.mark.parametrize("outgoing", [True, False])
 def test_contract_matches_fp32_bmm(L, outgoing):
     g = torch.Generator().manual_seed(L)
