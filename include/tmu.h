@@ -323,7 +323,9 @@ int tmu_copy_async(void* dst, const void* src, size_t bytes, void* stream);
 /* A pitched copy by the copy engines (cudaMemcpy2DAsync): `height` rows of `width` bytes from
  * `src` (rows `src_pitch` bytes apart) to `dst` (rows `dst_pitch` bytes apart).  The row-sharded
  * incoming update pulls each peer's block of z rows x this rank's columns with one such copy,
- * which is the all-to-all and its transpose in one transfer. */
+ * which is the all-to-all and its transpose in one transfer; the channel partition pulls each
+ * peer's rows of this rank's channels of a and b (and this rank's rows of the peer's channels
+ * of x) the same way, one run of rows x pitch elements per channel. */
 int tmu_copy2d_async(void* dst, size_t dst_pitch, const void* src, size_t src_pitch, size_t width, size_t height,
                      void* stream);
 
