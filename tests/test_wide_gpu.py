@@ -1,6 +1,6 @@
 """GPU parity at c_z = c = 256, the pair width of ESMFold2's released trunk (mlx_trunk.py:4).
 
-The wide kernels (K1W, the CTA-pair K3P; K2 is width-agnostic) against the CPU oracle, with the same bounds
+The wide kernels (the CTA-pair K1P and K3P; K2 is width-agnostic) against the CPU oracle, with the same bounds
 as the c_z = 128 tests: kernel outputs within 2 fp16 ulps of the oracle's intermediates (a few %
 of elements may differ), whole updates with e_cuda <= 2 e_ref + 1e-3 against the exact float64
 update and within 4 ulps of the fp16 oracle.
@@ -43,8 +43,8 @@ def _w(trunk, direction, bias, fp16=True):
     return ops.TrimulWeights.from_module(tri, DEV, b), orc.trimul_params(tri, fp16, b)
 
 
-# K1W tile shapes (least padding below 512 x 512): 64 -> 1 x 64; 96 -> 2 x 32; 12 -> 4 x 16;
-# 100, 146, 37 -> 8 x 8
+# K1P takes K1's 128-position tile shapes (the least padding below 512 x 512 positions): these
+# sizes reach the wide (1 x 128, 2 x 64), square-ish (8 x 16, 16 x 8) and sub-tile (L = 12) cases
 @pytest.mark.parametrize("L,B,n_pad,biases", [(64, 1, 0, False), (100, 1, 9, True), (146, 2, 0, False),
                                               (37, 3, 5, True), (12, 2, 3, False), (96, 1, 0, True)])
 def test_wide_project_gate_matches_oracle(L, B, n_pad, biases):
