@@ -975,8 +975,11 @@ def run_b200(args, ws, rank, local):
         torch.cuda.empty_cache()
         extra["c5"] = _c5_measure(ws, rank, local, min(args.steps, 10), args.warmup, False, not args.no_parity)
         if ws > 1:  # at N = 1 both partitions run the same three kernels on the whole fold
-            extra["c5_channels"] = _c5_measure(ws, rank, local, min(args.steps, 10), args.warmup, False,
-                                               not args.no_parity, partition="channels")
+            try:  # the alternative partition: a failure is reported in its sub-object, not the line
+                extra["c5_channels"] = _c5_measure(ws, rank, local, min(args.steps, 10), args.warmup, False,
+                                                   not args.no_parity, partition="channels")
+            except Exception as e:  # noqa: BLE001
+                extra["c5_channels"] = {"error": f"{type(e).__name__}: {e}"[:300]}
         torch.cuda.empty_cache()
 
     # ---------------- CPU baseline (rank 0, N = 1) ----------------
