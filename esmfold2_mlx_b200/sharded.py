@@ -204,6 +204,37 @@ class _SharedPair:
         self.peer_bufs = {}
 
 
+def channel_pull_jobs(rank: int, P: int, c: int, Lr: int, pitch: int, groups: int, dst_base: int,
+                      esize: int = 2) -> list:
+    """The pitched copies that bring rank ``rank`` its c/P channels of a and b over the whole grid.
+
+    Source: every rank's [2, c, Lr, pitch] row slab (a, then b); destination: this rank's
+    [2, c/P, P * Lr, pitch] buffer at address ``dst_base``.  One job per channel group g and
+    tensor t, as (dst, dst_pitch, src_off, src_pitch, width, height, dst_step): from rank q, the
+    group's c/P/groups channels (runs of Lr * pitch elements) into rows [q Lr, (q + 1) Lr) of each
+    destination channel (dst + q * dst_step).  Jobs are ordered by group, a before b."""
+    cp = c // P
+    cg = cp // groups
+    blk = Lr * pitch * esize
+    jobs = []
+    for g in range(groups):
+        for t in range(2):
+            dst = dst_base + (t * cp + g * cg) * P * blk
+            jobs.append((dst, P * blk, (t * c + rank * cp + g * cg) * blk, blk, blk, cg, blk))
+    return jobs
+
+
+def row_pull_job(rank: int, P: int, cp: int, L: int, pitch: int, groups: int, g: int, dst_base: int,
+                 esize: int = 2) -> tuple:
+    """The pitched copy that brings rank ``rank`` channel group g of x for its rows: from every rank
+    q's [c/P / groups, L, pitch] buffer of that group, rows [rank Lr, (rank + 1) Lr) of each channel
+    (one run of Lr * pitch elements, L * pitch apart) into channels q c/P + g c/P/groups .. of
+    this rank's [c, Lr, pitch] buffer at ``dst_base`` (dst + q * dst_step)."""
+    cg = cp // groups
+    blk = (L // P) * pitch * esize
+    return (dst_base + g * cg * blk, blk, rank * blk, L * pitch * esize, blk, cg, cp * blk)
+
+
 class CopyEngineExchange(DistExchange):
     """The slabs moved by the GPUs' copy engines instead of NCCL kernels.
 
@@ -353,13 +384,7 @@ class CopyEngineExchange(DistExchange):
         ``groups`` consecutive channel groups.  Returns (a, b, events): event g completes when
         group g has landed; the caller orders its readers after them."""
         _, c, Lr, pitch = self._ab.shape
-        cp, blk = c // self.size, Lr * pitch * 2
-        cg = cp // groups
-        jobs = []
-        for g in range(groups):
-            for t in range(2):  # a then b of channel group g
-                jobs.append((self.ab_ch[t, g * cg].data_ptr(), self.size * blk, (t * c + self.rank * cp + g * cg) * blk,
-                             blk, blk, cg, blk))
+        jobs = channel_pull_jobs(self.rank, self.size, c, Lr, pitch, groups, self.ab_ch.data_ptr())
         events = self._pull_blocks(self._ab, jobs, wait=False)
         return self.ab_ch[0], self.ab_ch[1], events[1::2]
 
@@ -383,10 +408,8 @@ class CopyEngineExchange(DistExchange):
         groups = len(self._xc)
         sp = self._xc[g]
         cg, L, pitch = sp.shape
-        cp = cg * groups
-        blk = (L // self.size) * pitch * 2
-        self._pull_blocks(sp, [(self.x_rows.data_ptr() + g * cg * blk, blk, self.rank * blk, L * pitch * 2, blk, cg,
-                                cp * blk)], wait=g == groups - 1)
+        self._pull_blocks(sp, [row_pull_job(self.rank, self.size, cg * groups, L, pitch, groups, g,
+                                            self.x_rows.data_ptr())], wait=g == groups - 1)
         return self.x_rows
 
     def wait(self, handle):

@@ -2,7 +2,9 @@
 
 ``RowShardedTrimul`` drives the exchange (all-to-all into columns for the incoming form, an
 asynchronous all-gather of b) and hands slabs to three stages; ``ChannelShardedTrimul`` moves
-a and b to channel ownership and x back by two all-to-alls.  Here the stages are the CPU oracle applied to
+a and b to channel ownership and x back by two all-to-alls.  The copy-engine form of those
+all-to-alls is a list of pitched copies per rank; their addresses are checked here for 2, 4 and
+8 emulated ranks on host buffers.  Here the stages are the CPU oracle applied to
 exactly the buffers the CUDA kernels would see -- the strided (possibly transposed) z view, the
 [B*c, rows, pitch] projections, b blocks contracted into column blocks of x -- so the test checks
 the layouts and the collectives; the kernels themselves are checked on the GPU.
@@ -132,3 +134,43 @@ def test_row_and_channel_sharded_match_unsharded_oracle():
     assert set(res) == {f"{n}/{d}" for n in ("RowShardedTrimul", "ChannelShardedTrimul") for d in ("out", "in")}
     for d, err in res.items():
         assert err <= 4e-3, f"{d}: sharded vs unsharded max |diff| {err}"
+
+
+def _copy2d(dst, dst_pitch, src, src_pitch, width, height):
+    """cudaMemcpy2D's semantics on host addresses."""
+    import ctypes
+
+    for r in range(height):
+        ctypes.memmove(dst + r * dst_pitch, src + r * src_pitch, width)
+
+
+@pytest.mark.parametrize("P,groups", [(2, 1), (2, 4), (4, 2), (4, 4), (8, 4)])
+def test_channel_exchange_copy_jobs_move_the_right_blocks(P, groups):
+    """The copy-engine channel partition's pitched copies (``channel_pull_jobs``,
+    ``row_pull_job``), applied to host buffers of P emulated ranks, give every rank exactly the
+    all-to-all results of the generic path: a, b of its channels over the grid, then x of its rows."""
+    from esmfold2_mlx_b200.sharded import channel_pull_jobs, row_pull_job
+
+    c, Lr, pitch = 32, 6, 16
+    L, cp = P * Lr, c // P
+    g = torch.Generator().manual_seed(P * 10 + groups)
+    ab = [torch.randn(2, c, Lr, pitch, generator=g).half() for _ in range(P)]  # each rank's row slabs
+    full = torch.cat(ab, dim=2)  # [2, c, L, pitch]: the whole grid
+    for r in range(P):
+        dst = torch.zeros(2, cp, L, pitch, dtype=torch.float16)
+        for job in channel_pull_jobs(r, P, c, Lr, pitch, groups, dst.data_ptr()):
+            d, dp, off, sp_, w, h, step = job
+            for q in range(P):
+                _copy2d(d + q * step, dp, ab[q].data_ptr() + off, sp_, w, h)
+        assert torch.equal(dst, full[:, r * cp:(r + 1) * cp])
+    # x: rank q holds channels [q cp, (q + 1) cp) of the grid, split into `groups` buffers
+    x = torch.randn(c, L, pitch, generator=g).half()
+    cg = cp // groups
+    xbufs = [[x[q * cp + k * cg:q * cp + (k + 1) * cg].clone() for k in range(groups)] for q in range(P)]
+    for r in range(P):
+        dst = torch.zeros(c, Lr, pitch, dtype=torch.float16)
+        for k in range(groups):
+            d, dp, off, sp_, w, h, step = row_pull_job(r, P, cp, L, pitch, groups, k, dst.data_ptr())
+            for q in range(P):
+                _copy2d(d + q * step, dp, xbufs[q][k].data_ptr() + off, sp_, w, h)
+        assert torch.equal(dst, x[:, r * Lr:(r + 1) * Lr])
