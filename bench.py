@@ -662,7 +662,7 @@ class TrimulCase:
         dom = max(self.NAMES, key=lambda n: kernels[n]["us_in_step"])
         return dom, kernels
 
-    def parity(self, slab_rows: int | None = None, folds=None) -> dict:
+    def parity(self, slab_rows: int | None = None, folds=None, exact_dtype=torch.float64) -> dict:
         """The step's outputs (left by the last replay) against the CPU oracle, used as the checker:
         e_cuda vs e_ref (exact float64 update) and the distance in fp16 ulps, per direction, each
         on the same input (in: the CUDA out result).  Large L: rows [124, 124 + slab_rows) only;
@@ -688,9 +688,11 @@ class TrimulCase:
             else:
                 rows = range(124, 124 + slab_rows)
                 ref16 = orc.trimul_rows(p16, zin, m, outgoing, rows)
-                exact = orc.trimul_rows(pex, zin, m, outgoing, rows, exact=True)
+                exact = orc.trimul_rows(pex, zin, m, outgoing, rows, exact=True, exact_dtype=exact_dtype)
                 res[d] = orc.parity(exact, ref16, got[:, rows.start:rows.stop].float())
                 res[d]["rows"] = [rows.start, rows.stop]
+                if exact_dtype != torch.float64:
+                    res[d]["exact"] = "float32 arithmetic (no fp16 rounding points)"
         res["checker"] = "oracle/trimul_oracle.py (CPU), after the timed region"
         res["tolerance"] = "e_cuda <= 2 e_ref + 1e-3 (max-abs, rel-L2); max_ulps <= 4"
         res["within_tolerance"] = all(v["within_tolerance"] and v["max_ulps"] <= 4
@@ -705,7 +707,7 @@ def _check(code, where):
         _lib.check(code, where)
 
 
-def _case_summary(case, flush, steps, warmup, with_parity=True, slab_rows=None) -> dict:
+def _case_summary(case, flush, steps, warmup, with_parity=True, slab_rows=None, exact_dtype=torch.float64) -> dict:
     """A sub-measurement of the default line: another configuration's step (value, ms/step,
     in-step kernel table and parity), one GPU."""
     for _ in range(max(3, warmup)):
@@ -726,7 +728,7 @@ def _case_summary(case, flush, steps, warmup, with_parity=True, slab_rows=None) 
     if code != 0:
         raise RuntimeError(f"device status {code} at site {site:#x}")
     if with_parity:
-        out["parity"] = case.parity(slab_rows)
+        out["parity"] = case.parity(slab_rows, exact_dtype=exact_dtype)
     return out
 
 
@@ -964,10 +966,14 @@ def run_b200(args, ws, rank, local):
     if ws == 1 and not args.no_trunk:
         recycle = _trunk_recycle(device, flush)
     if ws == 1 and not args.no_extra and args.workload == "c2":
-        for name, slab in (("L2048", 8), ("c2w", None)):
+        # L2048w: the released model's width at the metric's second anchor (parity on a row slab in
+        # float32, the whole-grid float64 projection being the slow part on the host)
+        for name, slab, edt in (("L2048", 8, torch.float64), ("c2w", None, torch.float64),
+                                ("L2048w", 8, torch.float32)):
             sub = TrimulCase(name, 0, device, stream)
-            extra[name] = _case_summary(sub, flush, min(args.steps, 20), args.warmup, not args.no_parity, slab)
+            extra[name] = _case_summary(sub, flush, min(args.steps, 20), args.warmup, not args.no_parity, slab, edt)
             del sub
+            torch.cuda.empty_cache()
     if not args.no_extra and args.workload == "c2":
         # the two multi-GPU configurations, at every N (N = 1 is their scaling baseline)
         extra["c4"] = _c4_measure(ws, rank, local, min(args.steps, 20), args.warmup, flush, stream,
@@ -1208,7 +1214,7 @@ def main():
     ap.add_argument("--sustain-seconds", type=float, default=0.6,
                     help="device seconds of the sustained replay that records clocks under load")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed step's output")
-    ap.add_argument("--no-extra", action="store_true", help="skip the L2048 and c2w sub-measurements")
+    ap.add_argument("--no-extra", action="store_true", help="skip the L2048, c2w and L2048w sub-measurements")
     ap.add_argument("--c5-nccl", action="store_true",
                     help="c5: move b with an NCCL all-gather instead of copy-engine peer copies")
     ap.add_argument("--c5-groups", type=int, default=4,
