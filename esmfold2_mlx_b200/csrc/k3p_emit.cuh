@@ -6,8 +6,10 @@
 // w_emit and w_out_gate are 2 x 256 x 256 fp16 = 256 KB, more than one SM's shared memory.  A
 // cluster of two CTAs on two SMs shares each tile instead, through MMAs that span both SMs
 // (tcgen05 .cta_group::2, M = 256 output channels): CTA r keeps rows [128 r, 128 r + 128) of
-// both matrices resident (the A operand's half), normalises ITS 32 of the tile's 64 positions
-// (the B operand's half), and receives in its TMEM the accumulators of its 128 output channels
+// both matrices resident in its tensor memory (the A operand's half, which the MMA reads from
+// TMEM, so the MMAs take only the activations from shared memory), normalises ITS 32 of the
+// tile's 64 positions (the B operand's half), and receives in its TMEM the accumulators of its
+// 128 output channels
 // for all 64 positions.  So every LayerNorm is computed once (a design that splits the output
 // channels over two independent CTAs computes each twice), and one MMA instruction covers
 // 256 x 64 outputs.
@@ -15,22 +17,29 @@
 // Tile = 64 positions of the pair grid as a 2 x 32 block (CTA r: row i0 + r) or a 1 x 64 block
 // (CTA r: columns j0 + 32 r ..), so each CTA's piece is one row of 32 positions.  Per CTA and
 // tile (14 warps, 448 threads):
-//   warp 0      TMA: the weight halves once; per tile its piece of x (channel-major [256][32],
-//               64B-swizzled, 16 KB) and of z ([4 atoms][32 positions][128 B], 16 KB), and the
-//               residual block z[64 positions][its 128 channels] (16 KB), 2 stages each
-//   warp 1      TMEM (2 slots x 128 columns, allocated for the pair) and, in the even CTA, the
-//               MMA thread: emit and gate chains, M = 256, N = 64, K = 256
+//   warp 0      TMA: per tile its piece of x (channel-major [256][32], 64B-swizzled, 16 KB) and
+//               of z ([4 atoms][32 positions][128 B], 16 KB), 4 stages, and the residual block
+//               z[64 positions][its 128 channels] (16 KB), 4 stages
+//   warp 1      TMEM (512 columns for the pair: 2 accumulator slots x 128, then w_emit's and
+//               w_gate's rows) and, in the even CTA, the MMA thread: emit and gate chains,
+//               M = 256, N = 64, K = 256, A from TMEM
 //   warps 2-5   A1 = fp16(LN_mix(x column)) in place over the x piece (ldmatrix.trans
 //               transpose, four 64-channel atoms combined by the parallel-variance formula)
 //   warps 6-9   A2 = fp16(LN_in(z row)) in place over the z piece
-//   warps 10-13 epilogue, TMEM lane quadrant warp mod 4: z' = z + m * sigmoid(g) over the
-//               residual block in shared memory, then one TMA store of the block.
+//   warps 10-13 first the weights into TMEM (a thread per output-channel row, from global
+//               memory, before the dependency wait); then the epilogue, TMEM lane quadrant warp
+//               mod 4: z' = z + m * sigmoid(g) over the residual block in shared memory, then
+//               one TMA store of the block.
 // Cross-CTA traffic is mbarrier signals only: the LayerNorm warps of both CTAs arrive on the
 // even CTA's operand barrier, the epilogue warps of both on its accumulator-free barrier, and the
 // MMA thread's commits arrive in both CTAs (multicast).  A2 in place frees a buffer that the
 // residual block reuses: the residual is reloaded from z (an L2 hit) for all 64 positions of
 // this CTA's channels.  z_out must not alias z (the pair's other CTA still reads z's channels
 // that this CTA writes).
+//
+// With the weights in shared memory (an earlier form), every M = 256, N = 64 MMA re-read 4 KB
+// of weights per CTA against 1 KB of activations: shared-memory bandwidth kept the paired MMAs
+// well below the tensor rate, and the 128 KB left room for only two operand and residual stages.
 #pragma once
 
 #include "tmu_common.cuh"
@@ -43,22 +52,24 @@ constexpr int CC = 256;
 constexpr int TILE = 64;                        // positions per pair tile
 constexpr int PT = 32;                          // positions per CTA
 constexpr int ATOM_BYTES = PT * 128;            // activation atoms: 32 rows x 128 B
-constexpr int WATOM_BYTES = 128 * 128;          // weight atoms: 128 rows x 128 B
-constexpr int WBLOCK_BYTES = 128 * 256 * 2;     // 128 rows x K = 256
 constexpr int PIECE_BYTES = PT * 256 * 2;       // 32 positions x 256 channels
 constexpr int RATOM_BYTES = TILE * 128;         // residual atoms: 64 rows x 128 B
 constexpr int RES_BYTES = 2 * RATOM_BYTES;      // 64 positions x 128 channels
-constexpr int OFF_WE = 0;
-constexpr int OFF_WG = OFF_WE + WBLOCK_BYTES;
-constexpr int OFF_X = OFF_WG + WBLOCK_BYTES;     // 2 stages: the x piece, then A1 in place
-constexpr int OFF_Z = OFF_X + 2 * PIECE_BYTES;   // 2 stages: the z piece, then A2 in place
-constexpr int OFF_R = OFF_Z + 2 * PIECE_BYTES;   // 2 stages: residual z, then z' in place
-constexpr int OFF_RED = OFF_R + 2 * RES_BYTES;   // float2 [4 parts][32 positions]: LN_mix partials
-constexpr int OFF_REDI = OFF_RED + 4 * PT * 8;   // the same for LN_in
+constexpr int NS = 4;                           // operand stages (x and z pieces)
+constexpr int NR = 4;                           // residual stages
+constexpr int OFF_X = 0;                           // NS stages: the x piece, then A1 in place
+constexpr int OFF_Z = OFF_X + NS * PIECE_BYTES;    // NS stages: the z piece, then A2 in place
+constexpr int OFF_R = OFF_Z + NS * PIECE_BYTES;    // NR stages: residual z, then z' in place
+constexpr int OFF_RED = OFF_R + NR * RES_BYTES;    // float2 [4 parts][32 positions]: LN_mix partials
+constexpr int OFF_REDI = OFF_RED + 4 * PT * 8;     // the same for LN_in
 constexpr int OFF_BAR = OFF_REDI + 4 * PT * 8;
-constexpr int SMEM_BYTES = OFF_BAR + 256;
+constexpr int SMEM_BYTES = OFF_BAR + 512;
 constexpr int kThreads = 448;
-constexpr int TMEM_COLS = 256;
+// TMEM: columns [0, 256) two accumulator slots (emit and gate, 64 positions each), [256, 384)
+// this CTA's 128 rows of w_emit and [384, 512) of w_gate as the MMA's A operand (K = 256 at two
+// fp16 per column)
+constexpr int TMEM_COLS = 512;
+constexpr int TM_WE = 256, TM_WG = 384;
 static_assert(SMEM_BYTES <= 232448, "K3P shared memory exceeds the per-block limit");
 
 struct Params {
@@ -66,8 +77,8 @@ struct Params {
   CUtensorMap tm_r;   // z, box {64, jw, ih, 1} (the tile's 64 positions, per atom)
   CUtensorMap tm_zo;  // z_out, box {64, jw, ih, 1} (store)
   CUtensorMap tm_x;   // x [B*256, rows, pitch]: box {32, 1, 256}, 64B swizzle
-  CUtensorMap tm_we;  // w_emit [256, 256]: box {64, 128}
-  CUtensorMap tm_wg;  // w_gate [256, 256]: box {64, 128}
+  const __half* w_emit;  // [256 out][256 in] (nn.Linear): row r = output channel r
+  const __half* w_gate;
   const __half* ln_in_w;
   const __half* ln_in_b;
   const __half* ln_mix_w;
@@ -105,20 +116,19 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t& w_bar = bars[0];
-  uint64_t& wpair = bars[1];     // even CTA: both CTAs' weight halves are resident (2 arrivals)
-  uint64_t* xfull = bars + 2;
-  uint64_t* zfull = bars + 4;
-  uint64_t* rfull = bars + 6;
-  uint64_t* rempty = bars + 8;   // the epilogue's store has read the residual stage
-  uint64_t* afull = bars + 10;   // even CTA: A1 and A2 of both CTAs (16 arrivals)
-  uint64_t* aempty = bars + 12;  // the paired MMAs have read A1 and A2 (multicast commit)
-  uint64_t* tfull = bars + 14;   // the accumulator slot is complete (multicast commit)
-  uint64_t* tempty = bars + 16;  // even CTA: both CTAs' epilogues have read the slot (8 arrivals)
-  uint64_t& drain_bar = bars[18];
-  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 19);
-  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 19) + 4);
-  volatile int* ok_sh = reinterpret_cast<volatile int*>(bars + 20);  // [3]
+  uint64_t& wpair = bars[1];     // even CTA: both CTAs' weight rows are in TMEM (8 arrivals)
+  uint64_t* xfull = bars + 2;    // [NS]
+  uint64_t* zfull = bars + 6;    // [NS]
+  uint64_t* rfull = bars + 10;   // [NR]
+  uint64_t* rempty = bars + 14;  // [NR] the epilogue's store has read the residual stage
+  uint64_t* afull = bars + 18;   // [NS] even CTA: A1 and A2 of both CTAs (16 arrivals)
+  uint64_t* aempty = bars + 22;  // [NS] the paired MMAs have read A1 and A2 (multicast commit)
+  uint64_t* tfull = bars + 26;   // [2] the accumulator slot is complete (multicast commit)
+  uint64_t* tempty = bars + 28;  // [2] even CTA: both CTAs' epilogues have read the slot (8 arrivals)
+  uint64_t& drain_bar = bars[30];
+  uint32_t& tmem_base_sh = *reinterpret_cast<uint32_t*>(bars + 31);
+  volatile int& abort_sh = *reinterpret_cast<volatile int*>(reinterpret_cast<uint8_t*>(bars + 31) + 4);
+  volatile int* ok_sh = reinterpret_cast<volatile int*>(bars + 32);  // [3][2]
   float2* rd = reinterpret_cast<float2*>(smem + OFF_RED);
   float2* rdi = reinterpret_cast<float2*>(smem + OFF_REDI);
   const int warp = threadIdx.x >> 5;
@@ -129,15 +139,18 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
 
   if (threadIdx.x == 0) {
     abort_sh = 0;
-    mbar_init(&w_bar, 1);
-    mbar_init(&wpair, 2);
-    for (int s = 0; s < 2; ++s) {
+    mbar_init(&wpair, 8);
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&xfull[s], 1);
       mbar_init(&zfull[s], 1);
-      mbar_init(&rfull[s], 1);
-      mbar_init(&rempty[s], 1);
       mbar_init(&afull[s], 16);
       mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < NR; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull[s], 1);
       mbar_init(&tempty[s], 8);
     }
@@ -149,8 +162,6 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
     tma_prefetch_desc(&p.tm_r);
     tma_prefetch_desc(&p.tm_zo);
     tma_prefetch_desc(&p.tm_x);
-    tma_prefetch_desc(&p.tm_we);
-    tma_prefetch_desc(&p.tm_wg);
   }
   if (warp == 1) {
     tmem_alloc_pair(&tmem_base_sh, TMEM_COLS);
@@ -161,13 +172,32 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
   cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA arrive
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
-  const uint32_t lead_wpair = cluster_addr(&wpair, 0);
-  if (warp == 0 && lane == 0) {  // weights are never written by this library: load before the wait
-    mbar_arrive_expect_tx(&w_bar, 2 * WBLOCK_BYTES);
-    for (int a = 0; a < 4; ++a) {
-      tma_load_2d(smem + OFF_WE + a * WATOM_BYTES, &p.tm_we, &w_bar, a * 64, rank * 128);
-      tma_load_2d(smem + OFF_WG + a * WATOM_BYTES, &p.tm_wg, &w_bar, a * 64, rank * 128);
+  if (warp >= 10) {
+    // The weights (never written by this library: loaded before the dependency wait) go to TMEM
+    // as the MMA's A operand: each epilogue warp writes its lane quadrant, thread = one output
+    // channel row, 512 B of w_emit and of w_gate straight from global memory.  Resident for the
+    // kernel, so the MMAs read only the activations from shared memory.
+    const int q = warp & 3;
+    const size_t row = static_cast<size_t>(rank) * 128 + q * 32 + lane;
+    const uint32_t tq = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+    for (int m = 0; m < 2; ++m) {
+      const uint4* src = reinterpret_cast<const uint4*>((m == 0 ? p.w_emit : p.w_gate) + row * CZ);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {  // 32 columns (64 K elements) at a time
+        uint32_t r[32];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint4 v = __ldg(src + 8 * c + e);
+          r[4 * e] = v.x, r[4 * e + 1] = v.y, r[4 * e + 2] = v.z, r[4 * e + 3] = v.w;
+        }
+        tmem_st32(tq + (m == 0 ? TM_WE : TM_WG) + 32 * c, r);
+      }
     }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(cluster_addr(&wpair, 0));  // once per kernel
   }
   griddep_trigger();
   griddep_wait();
@@ -176,15 +206,14 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      // this CTA's weight half is resident: tell the MMA thread (in the even CTA)
-      if (mbar_wait(&w_bar, 0, ctx, kSiteProd)) mbar_arrive_cluster(lead_wpair);
       uint32_t it = 0, nxz = 0, nr = 0;
       for (int tile = pair; tile < p.num_tiles; tile += npairs, ++it) {
         int bb, i0, j0;
         decode_tile(p, tile, bb, i0, j0);
         const int pi = i0 + (p.ih == 2 ? static_cast<int>(rank) : 0);
         const int pj = j0 + (p.ih == 2 ? 0 : PT * static_cast<int>(rank));
-        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        const uint32_t s = it % NS, ph = (it / NS) & 1;
+        const uint32_t rs = it % NR, rph = (it / NR) & 1;
         // the paired MMAs of this stage's previous tile have read A1 and A2 (both in place)
         if (!mbar_wait(&aempty[s], ph ^ 1, ctx, kSiteProd)) break;
         mbar_arrive_expect_tx(&xfull[s], PIECE_BYTES);
@@ -193,22 +222,23 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
         for (int a = 0; a < 4; ++a)
           tma_load_4d(smem + OFF_Z + s * PIECE_BYTES + a * ATOM_BYTES, &p.tm_z, &zfull[s], a * 64, pj, pi, bb);
         ++nxz;
-        if (!mbar_wait(&rempty[s], ph ^ 1, ctx, kSiteProdR)) break;
-        mbar_arrive_expect_tx(&rfull[s], RES_BYTES);
+        if (!mbar_wait(&rempty[rs], rph ^ 1, ctx, kSiteProdR)) break;
+        mbar_arrive_expect_tx(&rfull[rs], RES_BYTES);
         for (int k = 0; k < 2; ++k)
-          tma_load_4d(smem + OFF_R + s * RES_BYTES + k * RATOM_BYTES, &p.tm_r, &rfull[s], (2 * rank + k) * 64, j0,
+          tma_load_4d(smem + OFF_R + rs * RES_BYTES + k * RATOM_BYTES, &p.tm_r, &rfull[rs], (2 * rank + k) * 64, j0,
                       i0, bb);
         ++nr;
       }
       if (abort_sh) {
-        mbar_drain(&w_bar, 0, 200000000ull);
-        for (uint32_t s = 0; s < 2; ++s) {
-          const uint32_t na = nxz > s ? (nxz - s + 1) / 2 : 0;
+        for (uint32_t s = 0; s < NS; ++s) {
+          const uint32_t na = nxz > s ? (nxz - s + NS - 1) / NS : 0;
           if (na) {
             mbar_drain(&xfull[s], (na - 1) & 1, 200000000ull);
             mbar_drain(&zfull[s], (na - 1) & 1, 200000000ull);
           }
-          const uint32_t nra = nr > s ? (nr - s + 1) / 2 : 0;
+        }
+        for (uint32_t s = 0; s < NR; ++s) {
+          const uint32_t nra = nr > s ? (nr - s + NR - 1) / NR : 0;
           if (nra) mbar_drain(&rfull[s], (nra - 1) & 1, 200000000ull);
         }
       }
@@ -216,32 +246,32 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
   } else if (warp == 1) {
     // ---------------- MMA issuer (even CTA): emit and gate chains for both CTAs ----------------
     if (lane == 0 && rank == 0) {
-      bool ok = mbar_wait_cl(&wpair, 0, ctx, kSiteMmaW);
+      bool ok = mbar_wait_cl(&wpair, 0, ctx, kSiteMmaW);  // both CTAs' weight rows are in TMEM
+      tc_fence_after();
       uint32_t it = 0;
-      const uint64_t wed = sdesc_sw128(smem_u32(smem + OFF_WE), 16, 1024);
-      const uint64_t wgd = sdesc_sw128(smem_u32(smem + OFF_WG), 16, 1024);
       for (int tile = pair; ok && tile < p.num_tiles; tile += npairs, ++it) {
-        const uint32_t s = it & 1, ph = (it >> 1) & 1;
+        const uint32_t s = it % NS, ph = (it / NS) & 1;  // operand stage
+        const uint32_t a = it & 1, aph = (it >> 1) & 1;  // accumulator slot
         if (!mbar_wait_cl(&afull[s], ph, ctx, kSiteMmaA)) break;
-        if (!mbar_wait_cl(&tempty[s], ph ^ 1, ctx, kSiteMmaT)) break;
+        if (!mbar_wait_cl(&tempty[a], aph ^ 1, ctx, kSiteMmaT)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + s * 128;
+        const uint32_t d = tmem_base + a * 128;
         const uint64_t a1d = sdesc_sw128(smem_u32(smem + OFF_X + s * PIECE_BYTES), 16, 1024);
         const uint64_t a2d = sdesc_sw128(smem_u32(smem + OFF_Z + s * PIECE_BYTES), 16, 1024);
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) {
+        for (int kk = 0; kk < 16; ++kk) {  // K step kk: 8 TMEM columns of the weights
           const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
-          umma_f16_pair(d, sdesc_add(wed, ka * WATOM_BYTES + kb), sdesc_add(a1d, ka * ATOM_BYTES + kb), IDESC,
-                        kk > 0 ? 1u : 0u);
+          umma_f16_pair_ts(d, tmem_base + TM_WE + 8 * kk, sdesc_add(a1d, ka * ATOM_BYTES + kb), IDESC,
+                           kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < 16; ++kk) {
           const uint32_t ka = kk >> 2, kb = (kk & 3) * 32;
-          umma_f16_pair(d + TILE, sdesc_add(wgd, ka * WATOM_BYTES + kb), sdesc_add(a2d, ka * ATOM_BYTES + kb), IDESC,
-                        kk > 0 ? 1u : 0u);
+          umma_f16_pair_ts(d + TILE, tmem_base + TM_WG + 8 * kk, sdesc_add(a2d, ka * ATOM_BYTES + kb), IDESC,
+                           kk > 0 ? 1u : 0u);
         }
         umma_commit_pair(&aempty[s], 0x3);  // A1 and A2 of both CTAs have been read
-        umma_commit_pair(&tfull[s], 0x3);   // both CTAs' accumulators are complete
+        umma_commit_pair(&tfull[a], 0x3);   // both CTAs' accumulators are complete
       }
       umma_commit_pair(&drain_bar, 0x1);
       mbar_drain(&drain_bar, 0, 200000000ull);
@@ -266,14 +296,14 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
     }
     uint32_t it = 0;
     for (int tile = pair; tile < p.num_tiles; tile += npairs, ++it) {
-      const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      const uint32_t s = it % NS, ph = (it / NS) & 1;
       // one thread waits (bounded) and shares the verdict, so the group meets at every barrier
       if (t == 0) {
         const bool ok = mbar_wait(mix ? &xfull[s] : &zfull[s], ph, ctx, mix ? kSiteMix : kSiteIn);
-        ok_sh[grp] = ok ? 1 : 0;
+        ok_sh[2 * grp + (it & 1)] = ok ? 1 : 0;
       }
       named_bar_sync(bar_id, 128);
-      if (!ok_sh[grp]) break;
+      if (!ok_sh[2 * grp + (it & 1)]) break;
       if (mix) {
         // The x piece: [channel][32 positions], 64 B per channel, the 16-byte chunk m (positions
         // 8m..8m+7) of channel ch at chunk m ^ ((ch >> 1) & 3).  ldmatrix.trans of the 8 x 8 block
@@ -375,17 +405,18 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
     for (int tile = pair; tile < p.num_tiles; tile += npairs, ++it) {
       int bb, i0, j0;
       decode_tile(p, tile, bb, i0, j0);
-      const uint32_t s = it & 1, ph = (it >> 1) & 1;
+      const uint32_t a = it & 1, aph = (it >> 1) & 1;    // accumulator slot
+      const uint32_t rs = it % NR, rph = (it / NR) & 1;  // residual stage
       if (warp == 10 && lane == 0) {
-        bool ok = mbar_wait_cl(&tfull[s], ph, ctx, kSiteEpilogue);
-        ok = ok && mbar_wait(&rfull[s], ph, ctx, kSiteEpilogue);
-        ok_sh[2] = ok ? 1 : 0;
+        bool ok = mbar_wait_cl(&tfull[a], aph, ctx, kSiteEpilogue);
+        ok = ok && mbar_wait(&rfull[rs], rph, ctx, kSiteEpilogue);
+        ok_sh[4 + (it & 1)] = ok ? 1 : 0;
       }
       named_bar_sync(3, 128);
-      if (!ok_sh[2]) break;
+      if (!ok_sh[4 + (it & 1)]) break;
       tc_fence_after();
-      uint8_t* Rs = smem + OFF_R + s * RES_BYTES;
-      const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + s * 128;
+      uint8_t* Rs = smem + OFF_R + rs * RES_BYTES;
+      const uint32_t trow = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + a * 128;
 #pragma unroll 1
       for (int pb = 0; pb < TILE; pb += 16) {
         uint32_t em[16], gt[16];
@@ -395,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
         if (pb == TILE - 16) {  // the slot has been read: hand it back to the MMA thread
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster_smem(cluster_addr(&tempty[s], 0));
+          if (lane == 0) mbar_arrive_cluster_smem(cluster_addr(&tempty[a], 0));
         }
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
@@ -420,8 +451,12 @@ __global__ void __launch_bounds__(kThreads, 1) emit_residual_pair_kernel(const _
         for (int k = 0; k < 2; ++k)
           tma_store_4d(&p.tm_zo, Rs + k * RATOM_BYTES, (2 * rank + k) * 64, j0, i0, bb);
         bulk_commit();
-        bulk_wait_read<0>();
-        mbar_arrive(&rempty[s]);
+        // release the PREVIOUS tile's residual stage once its store has read it (long done): the
+        // group does not wait for this tile's store to read its block (0.45 us a tile when it did)
+        if (it > 0) {
+          bulk_wait_read<1>();
+          mbar_arrive(&rempty[(it - 1) % NR]);
+        }
       }
     }
     if (warp == 10 && lane == 0) bulk_wait<0>();

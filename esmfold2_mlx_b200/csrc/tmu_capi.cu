@@ -646,13 +646,8 @@ int launch_k3p(const void* x, const void* z, void* z_out, const tmu_trimul_weigh
     const uint32_t box[3] = {32, 1, 256};
     if ((st = encode_map(&p.tm_x, x, 3, dims, str, box, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
   }
-  {
-    const uint64_t dims[2] = {256, 256};
-    const uint64_t str[1] = {512};
-    const uint32_t box[2] = {64, 128};
-    if ((st = encode_map(&p.tm_we, w->w_emit, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
-    if ((st = encode_map(&p.tm_wg, w->w_gate, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
-  }
+  p.w_emit = static_cast<const __half*>(w->w_emit);
+  p.w_gate = static_cast<const __half*>(w->w_gate);
   p.ln_in_w = static_cast<const __half*>(w->ln_in_w);
   p.ln_in_b = static_cast<const __half*>(w->ln_in_b);
   p.ln_mix_w = static_cast<const __half*>(w->ln_mix_w);
