@@ -1076,7 +1076,7 @@ def run_pair_cond(args, ws, rank, local):
                 "frac": round(ach / tflops, 4), "traffic": None,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json burst)" if peak_kind == "measured" else "fallback",
                 "algorithmic_per_cell": {"flops": flops_cell, "bytes": bytes_cell},
-                "note": "whole-call roofline: per-kernel shares in profiles/pair_cond_launches_L1024.md"}
+                "note": "whole-call roofline over the eight launches of one call"}
     # end to end through the public API: fp32 inputs from pinned host memory, biases back to host
     zp, rpp = zt_h.pin_memory(), rp_h.pin_memory()
     outh = torch.empty(out.shape, dtype=out.dtype).pin_memory()

@@ -8,7 +8,7 @@ directory beside this repository; the tests skip without one), with:
 * the two Biohub ``esm`` classes its modules import (``fast_trunk.py:16``, ``variants.py:10``)
   registered as this repository's stand-in module tree (``synthetic.py``), since ``esm`` is not
   installed;
-* the shim files that INTEGRATION.md asks a maintainer to add (``var_cuda_trunk16.py`` and the
+* the shim files a maintainer of the reference adds to its package (``var_cuda_trunk16.py`` and the
   others, one ``import`` line each) written to a temporary directory that is appended to the
   ``esmfold2_mlx`` package's search path.
 
@@ -41,7 +41,7 @@ REF_SRC = os.path.join(REF, "src")
 pytestmark = pytest.mark.skipif(not os.path.exists(os.path.join(REF_SRC, "esmfold2_mlx", "variants.py")),
                                 reason="no checkout of the reference (set ESMFOLD2_MLX_REFERENCE)")
 
-# The shims a maintainer adds beside the reference's variants.
+# The shims a maintainer adds beside the reference's variants, one import line each.
 SHIMS = {
     "var_cuda_trunk16.py": "from esmfold2_mlx_b200.var_cuda_trunk16 import apply  # noqa: F401\n",
     "var_6b_cuda_trunks16.py": "from esmfold2_mlx_b200.var_6b_cuda_trunks16 import apply  # noqa: F401\n",
